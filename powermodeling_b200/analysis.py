@@ -1,0 +1,815 @@
+"""B200 analysis of sustained-power trials, with the reference's Python interface.
+
+``analyze_trial``/``analyze_trials``/``summarize``/``median_ci`` take the same
+arguments and return the same keys as powermodeling.analysis (analysis.py:597,
+1400, 1096) for the numeric core of a trial and a group: phase integrals over
+aligned completion epochs, idle-delta and paired-reference contrasts, pJ per
+FLOP/bit/op, group medians and bootstrap intervals.  Every number comes from
+libpmb200's kernels (pm_analyze_trials, pm_group_bootstrap); this module only
+packs records, turns issue bits into the reference's strings and builds the
+group keys whose sha256 prefix seeds each group's resampling.
+
+Outside this module's scope, and absent from its dicts: Nsight Compute
+evidence assessment (validation.py), memory-coalescing geometry, evaluation,
+selections and optima (analysis.py:1122-1398), and measurement diagnostics.
+``target_verified`` is therefore always False, as the reference reports for
+a trial without profiler evidence.
+"""
+from __future__ import annotations
+
+import hashlib
+import json
+import math
+import statistics
+from dataclasses import asdict, dataclass, replace
+from typing import Any, Iterable, Mapping
+
+import numpy as np
+
+from . import _native as N
+from . import contracts
+from .pack import (MEMORY_WORKLOADS, NONLINEAR_WORKLOADS, ROW_WORKLOADS, SFU_WORKLOADS, TENSOR_WORKLOADS,
+                   finite, pack_trials, phase_records, trials_struct)
+from .profiles import ARCHITECTURES
+
+ENERGY_WORKLOADS = TENSOR_WORKLOADS | MEMORY_WORKLOADS | SFU_WORKLOADS | NONLINEAR_WORKLOADS
+DEFAULT_RESAMPLES = 1000
+
+METRICS = ("board_power_w", "idle_power_w", "incremental_power_w", "throughput_ops_s", "throughput_bytes_s",
+           "pj_per_op", "pj_per_logical_byte", "total_pj_per_op", "total_pj_per_logical_byte",
+           "memory_rail_power_w", "memory_rail_incremental_power_w", "graphics_clock_mhz", "sm_clock_mhz", "memory_clock_mhz",
+           "temperature_c", "idle_fraction_of_measured_power", "idle_fraction_of_power_limit", "power_limit_utilization",
+           "tensor_peak_tflops_at_achieved_clock", "tensor_utilization_vs_dense_clock_peak",
+           "total_pj_per_flop", "total_pj_per_logical_bit",
+           "operational_idle_increment_power_w", "operational_idle_increment_energy_j",
+           "operational_idle_increment_pj_per_flop", "operational_idle_increment_pj_per_logical_bit",
+           "paired_active_reference_power_w", "paired_active_reference_energy_j",
+           "paired_active_reference_pj_per_flop", "paired_active_reference_pj_per_logical_bit",
+           "throughput_elements_s", "throughput_rows_s", "total_pj_per_element", "total_pj_per_row",
+           "operational_idle_increment_pj_per_element", "operational_idle_increment_pj_per_row",
+           "paired_active_reference_pj_per_element", "paired_active_reference_pj_per_row",
+           "throughput_sfu_instructions_s", "total_pj_per_instruction", "operational_idle_increment_pj_per_instruction",
+           "paired_active_reference_pj_per_instruction", "sfu_reference_delta_pj_per_instruction", "sfu_reference_delta_power_w",
+           "active_reference_duration_s", "active_reference_counted_loop_slots", "active_reference_loop_slots_s")
+"""The reference's _METRICS tuple (analysis.py:1059-1074); libpmb200 writes its rows in this order."""
+
+REPEAT_KEYS = {"repeat", "repeat_id", "repeat_index", "trial_id", "output_dir", "output_path"}
+
+
+@dataclass(frozen=True)
+class AnalysisPolicy:
+    """Same fields, defaults and validation as the reference's (analysis.py:42-67)."""
+    trim_s: float = 2.0
+    idle_trim_s: float = 1.0
+    min_measure_s: float = 5.0
+    min_idle_s: float = 4.0
+    min_samples: int = 4
+    max_sample_gap_s: float = 2.5
+    clock_tolerance_fraction: float = 0.03
+    max_clock_drift_fraction: float = 0.03
+    max_temperature_drift_c: float = 5.0
+    max_idle_drift_fraction: float = 0.10
+    counter_disagreement_fraction: float = 0.10
+    near_optimum_fraction: float = 0.05
+    min_geometries: int = 2
+
+    def __post_init__(self):
+        for name, value in asdict(self).items():
+            if isinstance(value, bool) or not isinstance(value, (int, float)) or not math.isfinite(value) or value < 0:
+                raise ValueError(f"Analysis policy {name} must be finite and nonnegative")
+        if type(self.min_samples) is not int or self.min_samples < 2:
+            raise ValueError("min_samples must be an integer >=2")
+        if type(self.min_geometries) is not int or self.min_geometries < 2:
+            raise ValueError("min_geometries must be an integer >=2; one geometry cannot qualify utilization")
+        if self.min_measure_s <= 0 or self.min_idle_s <= 0 or self.max_sample_gap_s <= 0:
+            raise ValueError("Measurement, idle and sample-gap durations must be positive")
+
+    def native(self) -> N.Policy:
+        return N.Policy(self.trim_s, self.idle_trim_s, self.min_measure_s, self.min_idle_s, self.min_samples,
+                        self.max_sample_gap_s, self.clock_tolerance_fraction, self.max_clock_drift_fraction,
+                        self.max_temperature_drift_c, self.max_idle_drift_fraction, self.counter_disagreement_fraction)
+
+
+def _policy(policy) -> AnalysisPolicy:
+    return policy if isinstance(policy, AnalysisPolicy) else AnalysisPolicy(**(policy or {}))
+
+
+def _none(x) -> float | None:
+    """NaN (the ABI's None) -> None; Python floats otherwise."""
+    x = float(x)
+    return None if math.isnan(x) else x
+
+
+# --- issue strings for each bit word ----------------------------------------
+_PHASE_ISSUES = ("missing_phase", "invalid_phase_window", "short_plateau", "too_few_samples", "telemetry_gap",
+                 "negative_power", "missing_power_coverage", "energy_counter_disagreement")
+_EPOCH_ISSUES = ("invalid_measure_epochs_phase_window", "invalid_measure_epoch_boundaries",
+                 "invalid_measure_epoch_count:operations", "invalid_measure_epoch_count:logical_bytes",
+                 "overlapping_measure_epochs", "insufficient_complete_measure_epochs",
+                 "measure_epoch_total_disagreement:operations", "measure_epoch_total_disagreement:logical_bytes",
+                 "invalid_measure_epoch")
+_CLOCKS = ("graphics_clock_mhz", "memory_clock_mhz", "sm_clock_mhz")
+
+
+def _treatment_strings() -> list[str | None]:
+    out = [f"{i}:measure" for i in _PHASE_ISSUES] + list(_EPOCH_ISSUES)
+    out += [f"missing_clock_telemetry:{c}" for c in _CLOCKS] + [f"clock_mismatch:{c}" for c in _CLOCKS]
+    out += [f"clock_drift:{c}" for c in _CLOCKS]
+    out += ["temperature_drift", "missing_temperature_telemetry", "missing_throttling_telemetry", "active_throttling",
+            "missing_process_inventory:compute_processes", "missing_process_inventory:graphics_processes",
+            "missing_measurement_pid", "other_gpu_processes", "mps_active", "host_device_duration_disagreement",
+            "missing_benchmark_duration", "missing_operation_count", "missing_logical_byte_count",
+            "nonlinear_requires_matching_work_energy_epochs", "sfu_requires_matching_work_energy_epochs"]
+    return out
+
+
+def _baseline_strings() -> list[str]:
+    out = [f"{i}:idle_pre" for i in _PHASE_ISSUES] + [f"{i}:idle_post" for i in _PHASE_ISSUES]
+    out += ["idle_baseline_drift", "missing_idle_baseline", "negative_incremental_energy",
+            "missing_process_inventory:compute_processes", "missing_process_inventory:graphics_processes",
+            "missing_measurement_pid", "baseline_other_gpu_processes", "mps_active",
+            "idle_state_mismatch_or_unverified:idle_pre:enforced_power_limit_w",
+            "idle_state_mismatch_or_unverified:idle_pre:pstate",
+            "idle_state_mismatch_or_unverified:idle_post:enforced_power_limit_w",
+            "idle_state_mismatch_or_unverified:idle_post:pstate"]
+    return out
+
+
+def _paired_strings() -> list[str]:
+    out = [f"{i}:active_reference" for i in _PHASE_ISSUES] + list(_EPOCH_ISSUES)
+    out += ["reference_work_energy_window_unverified"]
+    out += [f"paired_state_mismatch:{c}" for c in _CLOCKS] + ["paired_state_mismatch:temperature_c"]
+    out += ["reference_throttle_unverified_or_active", "reference_process_inventory_unverified:compute_processes",
+            "reference_process_inventory_unverified:graphics_processes", "reference_foreign_gpu_process",
+            "paired_power_cap_unverified", "paired_power_cap_changed",
+            "paired_state_mismatch:enforced_power_limit_w", "paired_state_mismatch:pstate",
+            "paired_power_unavailable",
+            "nonpositive_paired_contrast; signed observation retained but cannot minimize an energy objective",
+            "missing_paired_active_reference_phase"]
+    return out
+
+
+_WARNINGS = ("energy_counter_reset:idle_pre", "energy_counter_reset:measure", "energy_counter_reset:idle_post",
+             "energy_counter_reset:active_control", "uncontrolled_clock:graphics_clock_mhz",
+             "uncontrolled_clock:memory_clock_mhz",
+             "throughput_time_alignment_unverified; energy per work is a rate estimate assuming stationary throughput",
+             "memory_rail_source_changed; rail incremental energy withheld",
+             "tensor_peak_uses_graphics_clock_proxy; measured SM clock unavailable",
+             "tensor_theoretical_peak_unavailable",
+             "idle_active_pstate_or_enforced_cap_mismatch_or_unavailable; operational idle contrast is withheld from optimization",
+             "idle_active_power_cap_mismatch_or_unavailable; idle contrast is withheld from optimization",
+             "idle_active_clock_mismatch_or_unavailable; incremental power includes activation and frequency-state differences",
+             "idle_active_temperature_mismatch_or_unavailable; leakage/thermal drift can confound subtraction")
+
+_WORD_STRINGS = None
+
+
+def _word_strings():
+    global _WORD_STRINGS
+    if _WORD_STRINGS is None:
+        words = (_treatment_strings(), _baseline_strings(), _paired_strings(), list(_WARNINGS))
+        counts = [N.layout(name) for name in ("PM_IT_COUNT", "PM_IB_COUNT", "PM_IP_COUNT", "PM_W_COUNT")]
+        for strings, count in zip(words, counts):
+            if len(strings) != count:
+                raise N.NativeError(f"issue table mismatch: {len(strings)} strings for {count} bits")
+        _WORD_STRINGS = words
+    return _WORD_STRINGS
+
+
+def _bits(word: int, strings) -> list[str]:
+    out = []
+    while word:
+        low = word & -word
+        out.append(strings[low.bit_length() - 1])
+        word ^= low
+    return out
+
+
+# --- record-level (host) checks -------------------------------------------------
+def _host_treatment_issues(record, bench, config, device, epoch_status) -> list[str]:
+    """analyze_trial's checks on record metadata alone (analysis.py:620-629, 666-697, 753-757)."""
+    issues = []
+    if epoch_status == N.EP_INVALID_LIST:
+        issues.append("invalid_measure_epochs")
+    if not record.get("trial_id"):
+        issues.append("missing_trial_id")
+    quality = record.get("quality") or {}
+    if quality.get("valid") is False:
+        issues.append("runner_quality_invalid")
+    for key in ("interference_detected", "mig_active", "mps_active", "unsafe_short_duration"):
+        if quality.get(key) or config.get(key):
+            issues.append(key)
+    if quality.get("other_compute_processes", record.get("other_compute_processes")):
+        issues.append("other_compute_processes")
+    mig_mode = device.get("mig_mode") or {}
+    if isinstance(mig_mode, dict) and mig_mode.get("current"):
+        issues.append("mig_active")
+    if (record.get("provenance") or {}).get("mps_environment"):
+        issues.append("mps_environment")
+    if record.get("status") != "complete" or bench.get("error"):
+        issues.append("benchmark_failed")
+    sanity = bench.get("sanity") or {}
+    if isinstance(sanity, Mapping) and sanity.get("finite_output_sample") is False:
+        issues.append("benchmark_output_sanity_failed")
+    read_validation = bench.get("memory_read_validation") or {}
+    if ((isinstance(sanity, Mapping) and sanity.get("memory_read_sample_matches_reference") is False)
+            or (isinstance(read_validation, Mapping) and
+                (read_validation.get("status") == "fail" or (finite(read_validation.get("mismatched_values")) or 0) > 0))):
+        issues.append("memory_read_reference_mismatch")
+    workload = record.get("workload")
+    issues.extend(contracts.nonlinear_count_issues(bench, workload))
+    issues.extend(contracts.memory_count_issues(bench, workload))
+    issues.extend(contracts.sfu_count_issues(bench, workload))
+    return issues
+
+
+def _host_paired_issues(record, phases, epoch_status) -> list[str]:
+    """_paired_reference_contrast's checks on record metadata (analysis.py:310-333, 370-371)."""
+    protocol = record.get("treatment_protocol") or (record.get("benchmark") or {}).get("treatment_protocol") or {}
+    reference = record.get("active_reference") or {}
+    reference_phase = phases.get("active_reference")
+    if not reference_phase:
+        return []
+    sfu = record.get("workload") in SFU_WORKLOADS
+    issues = []
+    if epoch_status == N.EP_INVALID_LIST:
+        issues.append("invalid_measure_epochs")
+    for name in ("same_process", "same_allocations", "same_clock_policy", "launch_geometry_matched"):
+        if protocol.get(name) is not True:
+            issues.append("paired_protocol_unverified:" + name)
+    if (protocol.get("kind") != "paired_active_reference"
+            or protocol.get("reference_kind") != (contracts.SFU_REFERENCE_KIND if sfu else "issue_loop")
+            or protocol.get("reference_workload") != "control"):
+        issues.append("paired_reference_definition_unverified")
+    order = protocol.get("order")
+    if order not in ("AB", "BA"):
+        issues.append("paired_protocol_order_unverified")
+    measure = phases.get("measure") or {}
+    if order == "AB" and (finite(reference_phase.get("end_s")) or 0) > (finite(measure.get("start_s")) or 0):
+        issues.append("paired_arm_order_or_overlap_invalid")
+    if order == "BA" and (finite(measure.get("end_s")) or 0) > (finite(reference_phase.get("start_s")) or 0):
+        issues.append("paired_arm_order_or_overlap_invalid")
+    treatment = record.get("benchmark") or {}
+    for name in ("blocks", "threads", "batch_launches", "iterations_per_launch"):
+        if reference.get(name) is None or treatment.get(name) is None or reference[name] != treatment[name]:
+            issues.append("paired_geometry_mismatch:" + name)
+    if sfu:
+        issues.extend(contracts.sfu_count_issues(reference, record.get("workload"), reference=True))
+        for name in ("sfu_lanes", "sfu_chains", "sfu_primitive", "sfu_input_policy", "grid_mode",
+                     "math_implementation", "sfu_ptx_opcode"):
+            if reference.get(name) != treatment.get(name):
+                issues.append("paired_sfu_contract_mismatch:" + name)
+    if (reference.get("sanity") or {}).get("requested_sm_coverage_complete") is not True:
+        issues.append("reference_sm_coverage_unverified")
+    return issues
+
+
+def _experiment_contract(workload, benchmark, config):
+    """evaluation.experiment_contract (evaluation.py:32-58): part of the group key."""
+    def get(key, default=None):
+        return benchmark.get(key, config.get(key, default))
+    if workload in MEMORY_WORKLOADS or workload == "l2_latency":
+        size = get("working_set_bytes")
+        if workload == "l1":
+            blocks = get("blocks")
+            size = get("l1_bytes_per_block", size / blocks if finite(size) is not None and finite(blocks) and blocks > 0 else None)
+        contract = {"access": get("access", "read"),
+                    "kernel_implementation_version": get("kernel_implementation_version"),
+                    "read_cache_policy": get("read_cache_policy", "ca" if workload == "l1" else "cg"),
+                    "memory_read_index_math": get("memory_read_index_math", "uint64"),
+                    "memory_accesses_per_thread_iteration": get("memory_accesses_per_thread_iteration"),
+                    ("l1_bytes_per_block" if workload == "l1" else "working_set_bytes"): size,
+                    "stride_elements": get("stride_elements", 1)}
+        if workload == "l2_latency":
+            contract.update(blocks=get("blocks"), threads=get("threads"),
+                            iterations_per_launch=get("iterations_per_launch", config.get("iterations")),
+                            sm_filter_size=len(config.get("sm_ids") or []))
+        else:
+            contract.update(offset_bytes=get("offset_bytes", 0), sm_ids=config.get("sm_ids", []))
+        return contract
+    if workload in NONLINEAR_WORKLOADS:
+        return {key: get(key) for key in ("working_set_bytes", "row_width", "input_precision", "math_implementation",
+                                          "rms_epsilon", "affine_gamma", "nonlinear_input_distribution",
+                                          "input_elements", "grid_mode", "kernel_implementation_version",
+                                          "block_completion_count_source")}
+    if workload in SFU_WORKLOADS:
+        return {key: get(key) for key in contracts.SFU_CONTRACT_FIELDS}
+    return ({"definition": "dense FP16 input / FP32 accumulation", "implementation": workload}
+            if workload in TENSOR_WORKLOADS else {"definition": "active integer issue control"})
+
+
+# --- result assembly -------------------------------------------------------------
+class _Views:
+    def __init__(self, n):
+        self.PO = N.layout("PM_PO_COUNT")
+        self.TO = N.layout("PM_TO_COUNT")
+        self.phase_out = np.empty(n * N.PM_PHASES * self.PO)
+        self.phase_flags = np.empty(n * N.PM_PHASES, dtype=np.uint32)
+        self.trial_out = np.empty(n * self.TO)
+        self.issue_bits = np.empty(n * 4, dtype=np.uint64)
+        self.metrics = np.empty(n * len(METRICS))
+        self.valid = np.empty(n, dtype=np.uint8)
+
+    def struct(self) -> N.TrialResults:
+        r = N.TrialResults()
+        for name in ("phase_out", "phase_flags", "trial_out", "issue_bits", "metrics", "valid"):
+            setattr(r, name, getattr(self, name).ctypes.data)
+        return r
+
+
+_PO_NAMES = None
+
+
+def _po_names():
+    global _PO_NAMES
+    if _PO_NAMES is None:
+        names = {}
+        for key in ("START_S", "END_S", "DURATION_S", "MIDPOINT_S", "SAMPLES", "GAP_MEDIAN_S", "GAP_MAX_S", "ENERGY_J",
+                    "INTEGRATED_POWER_W", "POWER_W", "MEMORY_ENERGY_J", "MEMORY_POWER_W", "COUNTER_J", "DISAGREEMENT",
+                    "DISTINCT_POWER", "CHANGE_MEDIAN_S"):
+            names[key] = N.layout("PM_PO_" + key)
+        for prefix, field in (("GFX", "graphics_clock_mhz"), ("SM", "sm_clock_mhz"), ("MEM", "memory_clock_mhz"),
+                              ("TEMP", "temperature_c")):
+            names[field] = tuple(N.layout(f"PM_PO_{prefix}_{s}") for s in ("MED", "MIN", "MAX"))
+        _PO_NAMES = names
+    return _PO_NAMES
+
+
+def _phase_dict(name: str, po: np.ndarray, flags: int, policy: AnalysisPolicy) -> dict:
+    """The reference's _phase_stats dict without its private _selected list."""
+    L = _po_names()
+    out: dict[str, Any] = {"name": name, "issues": [], "warnings": []}
+    pf = {k: N.layout("PM_PF_" + k) for k in ("MISSING", "INVALID_WINDOW", "COUNTER_RESET", "COMPUTED")}
+    if flags >> pf["MISSING"] & 1:
+        out["issues"].append(f"missing_phase:{name}")
+        return out
+    if flags >> pf["INVALID_WINDOW"] & 1:
+        out["issues"].append(f"invalid_phase_window:{name}")
+        return out
+    samples = int(po[L["SAMPLES"]])
+    out.update(start_s=_none(po[L["START_S"]]), end_s=_none(po[L["END_S"]]), duration_s=_none(po[L["DURATION_S"]]),
+               midpoint_s=_none(po[L["MIDPOINT_S"]]), samples=samples,
+               sample_interval_median_s=_none(po[L["GAP_MEDIAN_S"]]), max_sample_gap_s=_none(po[L["GAP_MAX_S"]]))
+    issue_bits = {"SHORT_PLATEAU": "short_plateau", "TOO_FEW_SAMPLES": "too_few_samples", "TELEMETRY_GAP": "telemetry_gap",
+                  "NEGATIVE_POWER": "negative_power", "MISSING_POWER_COVERAGE": "missing_power_coverage",
+                  "COUNTER_DISAGREEMENT": "energy_counter_disagreement"}
+    order = ("SHORT_PLATEAU", "TOO_FEW_SAMPLES", "TELEMETRY_GAP", "NEGATIVE_POWER", "MISSING_POWER_COVERAGE",
+             "COUNTER_DISAGREEMENT")
+    for key in order:
+        if flags >> N.layout("PM_PF_" + key) & 1:
+            out["issues"].append(f"{issue_bits[key]}:{name}")
+    energy = _none(po[L["ENERGY_J"]])
+    out["integrated_power_energy_j"] = energy
+    out["integrated_power_w"] = _none(po[L["INTEGRATED_POWER_W"]])
+    out["power_w"] = _none(po[L["POWER_W"]])
+    memory_energy = _none(po[L["MEMORY_ENERGY_J"]])
+    out["memory_rail_energy_j"] = memory_energy
+    out["memory_power_w"] = _none(po[L["MEMORY_POWER_W"]])
+    if flags >> pf["COUNTER_RESET"] & 1:
+        out["warnings"].append(f"energy_counter_reset:{name}")
+    out["energy_counter_j"] = _none(po[L["COUNTER_J"]])
+    disagreement = _none(po[L["DISAGREEMENT"]])
+    if disagreement is not None:
+        out["counter_power_disagreement_fraction"] = disagreement
+    out["distinct_power_values"] = int(po[L["DISTINCT_POWER"]])
+    out["observed_power_change_interval_median_s"] = _none(po[L["CHANGE_MEDIAN_S"]])
+    out["power_update_cadence_note"] = "Changes are not proof of sensor refresh cadence; unchanged values may be steady power."
+    for field in ("graphics_clock_mhz", "sm_clock_mhz", "memory_clock_mhz", "temperature_c"):
+        med, lo, hi = L[field]
+        out[field] = _none(po[med])
+        out[f"{field}_min"] = _none(po[lo])
+        out[f"{field}_max"] = _none(po[hi])
+    return out
+
+
+def _gpu_uuid(record):
+    config = dict(record.get("config") or {})
+    device = record.get("device") or {}
+    return config.get("gpu_uuid") or device.get("uuid") or record.get("gpu_uuid")
+
+
+def _treatment_design_stratum(record, benchmark):
+    protocol = record.get("treatment_protocol") or benchmark.get("treatment_protocol") or {}
+    return {"kind": protocol.get("kind", "unspecified_legacy_protocol"),
+            "reference_kind": protocol.get("reference_kind"),
+            "paired_reference_context_allocated": benchmark.get("paired_reference_context_allocated",
+                                                                protocol.get("paired_reference_context_allocated"))}
+
+
+def prepare(records: list) -> tuple:
+    """Record-level checks and the packed batch: (Packed, host issues, host paired issues)."""
+    host_issues, host_paired, host_flags = [], [], []
+    for record in records:
+        bench = record.get("benchmark") or record.get("result") or {}
+        config = dict(record.get("config") or {})
+        device = record.get("device") or {}
+        phases = phase_records(record)
+        source = bench.get("measure_epochs", bench.get("work_epochs"))
+        status = N.EP_NONE if source is None else (N.EP_INVALID_LIST if not isinstance(source, list) or not source else N.EP_OK)
+        ref = record.get("active_reference") or {}
+        rsource = ref.get("measure_epochs", ref.get("work_epochs"))
+        rstatus = N.EP_NONE if rsource is None else (N.EP_INVALID_LIST if not isinstance(rsource, list) or not rsource else N.EP_OK)
+        hi = _host_treatment_issues(record, bench, config, device, status)
+        hp = _host_paired_issues(record, phases, rstatus)
+        host_issues.append(hi)
+        host_paired.append(hp)
+        flags = (N.T_HOST_ISSUES if hi else 0) | (N.T_HOST_PAIRED if hp else 0)
+        workload = record.get("workload")
+        if workload in SFU_WORKLOADS and not contracts.sfu_count_issues(bench, workload):
+            flags |= N.T_SFU_CONTRACT_OK
+        if workload in NONLINEAR_WORKLOADS and not contracts.nonlinear_count_issues(bench, workload):
+            flags |= N.T_NONLINEAR_OK
+        host_flags.append(flags)
+    return pack_trials(records, host_flags, ARCHITECTURES), host_issues, host_paired
+
+
+def analyze_trials(records: Iterable[Mapping[str, Any]], policy: AnalysisPolicy | Mapping[str, Any] | None = None,
+                   hbm_bandwidth_fraction: float = 0.80, _metrics_out: list | None = None) -> list[dict[str, Any]]:
+    """analyze_trial over a batch, in one kernel launch."""
+    from .hbm import trial_bandwidth, validate_fraction
+    hbm_bandwidth_fraction = validate_fraction(hbm_bandwidth_fraction)
+    policy = _policy(policy)
+    records = list(records)
+    if not records:
+        return []
+    words = _word_strings()
+    packed, host_issues, host_paired = prepare(records)
+    trials = trials_struct(packed)
+    views = _Views(len(records))
+    results = views.struct()
+    N.check(N.library().pm_analyze_trials(trials, policy.native(), results), "pm_analyze_trials")
+    if _metrics_out is not None:
+        _metrics_out.append((views.metrics.reshape(len(records), len(METRICS)).copy(), views.valid.copy()))
+    TO = {name: N.layout("PM_TO_" + name) for name in _TO_NAMES}
+    out = []
+    for i, record in enumerate(records):
+        bench = record.get("benchmark") or record.get("result") or {}
+        config = dict(record.get("config") or {})
+        device = record.get("device") or {}
+        phases_rec = phase_records(record)
+        to = views.trial_out[i * views.TO:(i + 1) * views.TO]
+        g = lambda name: _none(to[TO[name]])  # noqa: E731
+        ib = [int(x) for x in views.issue_bits[i * 4:(i + 1) * 4]]
+        issues = host_issues[i] + _bits(ib[0], words[0])
+        baseline_issues = _bits(ib[1], words[1])
+        paired_issues = host_paired[i] + _bits(ib[2], words[2])
+        warnings = _bits(ib[3], words[3])
+        phase_dicts = {}
+        for p, name in enumerate(N.PHASE_NAMES):
+            po = views.phase_out[(i * N.PM_PHASES + p) * views.PO:(i * N.PM_PHASES + p + 1) * views.PO]
+            phase_dicts[name] = _phase_dict(name, po, int(views.phase_flags[i * N.PM_PHASES + p]), policy)
+        other_pids = set()
+        measure_slot = i * N.PM_PHASES + 1
+        mpo = views.phase_out[measure_slot * views.PO:(measure_slot + 1) * views.PO]
+        lo, hi_ = mpo[N.layout("PM_PO_SEL_LO")], mpo[N.layout("PM_PO_SEL_HI")]
+        if not math.isnan(lo):
+            for index, pids in packed.foreign_pids[measure_slot]:
+                if lo <= index < hi_:
+                    other_pids.update(pids)
+        workload = record.get("workload")
+        duration = g("DURATION_S")
+        power_limit = g("POWER_LIMIT_W")
+        result: dict[str, Any] = {
+            "trial_id": record.get("trial_id"), "condition_id": record.get("condition_id"), "workload": workload,
+            "gpu_uuid": _gpu_uuid(record), "experiment_role": record.get("experiment_role", "legacy_unspecified"),
+            "experiment_contract": _experiment_contract(workload, bench, config),
+            "repeat_index": record.get("repeat", config.get("repeat", config.get("repeat_index"))),
+            "gpu_name": device.get("name", record.get("gpu_name")), "config": config,
+            "valid": not issues, "issues": sorted(set(issues)), "warnings": sorted(set(warnings)),
+            "baseline_valid": not baseline_issues, "baseline_issues": sorted(set(baseline_issues)),
+            "target_verified": False,
+            "benchmark_sha256": (record.get("provenance") or {}).get("benchmark_sha256"),
+            "treatment_design_stratum": _treatment_design_stratum(record, bench),
+            "resource_geometry": {f: bench.get(f, config.get(f)) for f in (
+                ("gemm_m", "gemm_n", "gemm_k") if workload == "gemm" else
+                ("blocks", "threads", "tensor_accumulators") if workload in TENSOR_WORKLOADS else
+                ("blocks", "threads", "sfu_chains") if workload in SFU_WORKLOADS else ("blocks", "threads"))},
+            "sfu_contract": {f: bench.get(f) for f in contracts.SFU_CONTRACT_FIELDS} if workload in SFU_WORKLOADS else None,
+            "nonlinear_contract": {f: bench.get(f) for f in (
+                "row_width", "working_set_bytes", "input_elements", "grid_mode", "input_precision", "math_implementation",
+                "kernel_implementation_version", "block_completion_count_source", "rms_epsilon", "affine_gamma",
+                "nonlinear_input_distribution")} if workload in NONLINEAR_WORKLOADS else None,
+            "measurement_stratum": {"ecc_mode": device.get("ecc_mode"), "mig_mode": device.get("mig_mode"),
+                                    "driver_version": device.get("driver_version"), "nvml_version": device.get("nvml_version"),
+                                    "runtime_versions": {k: (record.get("cuda_device") or {}).get(k) for k in (
+                                        "cuda_runtime_version", "cuda_driver_version", "cuda_compile_version", "cublas_version")},
+                                    "power_limit_w": power_limit,
+                                    "power_scope": (record.get("telemetry") or {}).get("power_scope", device.get("power_scope_note")),
+                                    "power_usage_semantics": device.get("power_usage_semantics"),
+                                    "kernel_implementation_version": bench.get("kernel_implementation_version"),
+                                    "block_completion_count_source": bench.get("block_completion_count_source"),
+                                    "memory_accesses_per_thread_iteration": bench.get("memory_accesses_per_thread_iteration")},
+            "kernel_implementation_version": bench.get("kernel_implementation_version"),
+            "duration_s": duration, "benchmark_duration_s": g("BENCH_MEASURED_DURATION_S"),
+            "benchmark_device_duration_s": g("BENCH_DEVICE_DURATION_S"),
+            "count_energy_time_alignment_exact": bool(to[TO["EXACT"]]),
+            "counted_measure_operations": g("COUNTED_OPS"), "counted_measure_logical_bytes": g("COUNTED_BYTES"),
+            "complete_measure_epochs": int(to[TO["EPOCHS"]]),
+            "energy_per_work_kind": "counted matching-window energy per work" if to[TO["EXACT"]] else "stationary whole-run-rate estimate",
+            "diagnostic_only": workload not in ENERGY_WORKLOADS,
+            "clock_comparison_controlled": all((finite(config.get(f)) or 0) > 0 for f in ("graphics_clock_mhz", "memory_clock_mhz")),
+            "throughput_ops_s": g("OPS_RATE"), "throughput_bytes_s": g("BYTE_RATE"),
+            "device_event_throughput_ops_s": g("DEVICE_OPS_RATE"), "device_event_throughput_bytes_s": g("DEVICE_BYTE_RATE"),
+            "tensor_peak_tflops_at_achieved_clock": g("TENSOR_PEAK_TFLOPS"),
+            "tensor_peak_clock_source": (("sm_clock_mhz" if to[TO["PEAK_CLOCK_IS_SM"]] else "graphics_clock_mhz")
+                                         if g("TENSOR_PEAK_TFLOPS") is not None else None),
+            "tensor_utilization_vs_dense_clock_peak": g("TENSOR_UTILIZATION"),
+            "board_power_w": g("BOARD_POWER_W"), "idle_power_w": g("IDLE_POWER_W"), "incremental_power_w": g("INCREMENTAL_POWER_W"),
+            "operational_idle_increment_power_w": g("INCREMENTAL_POWER_W"),
+            "operational_idle_increment_energy_j": g("INCREMENTAL_ENERGY_J"),
+            "operational_idle_increment_eligible": bool(to[TO["IDLE_INC_ELIGIBLE"]]) and not issues,
+            "total_energy_j": g("TOTAL_ENERGY_J"), "idle_energy_j": g("IDLE_ENERGY_J"), "incremental_energy_j": g("INCREMENTAL_ENERGY_J"),
+            "integrated_power_energy_j": phase_dicts["measure"].get("integrated_power_energy_j"),
+            "energy_counter_j": phase_dicts["measure"].get("energy_counter_j"),
+            "energy_source": "power_trapezoid" if to[TO["ENERGY_SOURCE_TRAPEZOID"]] else "energy_counter_delta",
+            "pj_per_op": g("PJ_PER_OP"), "pj_per_logical_byte": g("PJ_PER_LOGICAL_BYTE"),
+            "total_pj_per_op": g("TOTAL_PJ_PER_OP"), "total_pj_per_logical_byte": g("TOTAL_PJ_PER_LOGICAL_BYTE"),
+            "memory_rail_power_w": phase_dicts["measure"].get("memory_power_w"), "memory_rail_idle_power_w": g("IDLE_MEMORY_POWER_W"),
+            "memory_rail_energy_j": g("RAIL_ENERGY_J"), "memory_rail_incremental_energy_j": g("RAIL_INCREMENTAL_J"),
+            "memory_rail_incremental_power_w": g("RAIL_INCREMENTAL_W"),
+            "graphics_clock_mhz": phase_dicts["measure"].get("graphics_clock_mhz"),
+            "sm_clock_mhz": phase_dicts["measure"].get("sm_clock_mhz"),
+            "memory_clock_mhz": phase_dicts["measure"].get("memory_clock_mhz"),
+            "temperature_c": phase_dicts["measure"].get("temperature_c"),
+            "throttle_reasons_mask": int(to[TO["THROTTLE_MASK"]]) if not math.isnan(to[TO["THROTTLE_MASK"]]) else 0,
+            "other_gpu_process_pids": sorted(other_pids),
+            "power_limit_w": power_limit,
+            "idle_fraction_of_measured_power": g("IDLE_FRAC_MEASURED"), "idle_fraction_of_power_limit": g("IDLE_FRAC_LIMIT"),
+            "power_limit_utilization": g("LIMIT_UTILIZATION"),
+            "baseline_clock_matched": bool(to[TO["BASE_CLOCK_MATCHED"]]),
+            "baseline_temperature_matched": bool(to[TO["BASE_TEMP_MATCHED"]]),
+            "baseline_power_cap_matched": bool(to[TO["BASE_CAP_MATCHED"]]),
+            "baseline_state_matched": bool(to[TO["BASE_STATE_MATCHED"]]),
+            "baseline_state_issues": sorted(s for s in baseline_issues if s.startswith("idle_state_mismatch_or_unverified")),
+            "baseline_clock_domains_compared": ["graphics_clock_mhz", "memory_clock_mhz"] + (["sm_clock_mhz"] if to[TO["BASE_SM_COMPARED"]] else []),
+            "baseline_sm_clock_uses_graphics_proxy": not bool(to[TO["BASE_SM_COMPARED"]]),
+            "baseline_state_domains_compared": sorted(([ "enforced_power_limit_w"] if to[TO["BASE_ENF_COMPARED"]] else [])
+                                                      + (["pstate"] if to[TO["BASE_PSTATE_COMPARED"]] else [])),
+            "policy": asdict(policy), "phases": {},
+        }
+        result["baseline_state_issues"] = [s for s in sorted(set(baseline_issues)) if s.startswith("idle_state_mismatch_or_unverified")]
+        result["active_minus_idle_state_deltas"] = _state_deltas(to, TO)
+        tensor, memory = workload in TENSOR_WORKLOADS, workload in MEMORY_WORKLOADS
+        result["total_pj_per_flop"] = g("TOTAL_PJ_PER_FLOP")
+        result["total_pj_per_logical_bit"] = g("TOTAL_PJ_PER_BIT")
+        result["operational_idle_increment_pj_per_flop"] = g("INC_PJ_PER_FLOP")
+        result["operational_idle_increment_pj_per_logical_bit"] = g("INC_PJ_PER_BIT")
+        result["flop_count_convention"] = "multiply-add=2 FLOPs; reported dense FP16 tensor operations" if tensor else None
+        result["logical_bit_count_convention"] = "8 bits per logical byte; copy counts both read and write payload" if memory else None
+        for name in ("idle_pre", "measure", "idle_post"):
+            result["phases"][name] = phase_dicts[name]
+        if phases_rec.get("active_control"):
+            result["phases"]["active_control"] = phase_dicts["active_control"]
+            result["active_control_incremental_power_w"] = g("CONTROL_INC_POWER_W")
+            result["control_subtracted_power_w"] = None
+        # paired reference
+        result.update(paired_active_reference_eligible=bool(to[TO["PAIRED_ELIGIBLE"]]) and not paired_issues,
+                      paired_active_reference_power_w=None, paired_active_reference_energy_j=None,
+                      paired_active_reference_pj_per_flop=None, paired_active_reference_pj_per_logical_bit=None,
+                      paired_active_reference_issues=sorted(set(paired_issues)),
+                      paired_active_reference_protocol=record.get("treatment_protocol") or bench.get("treatment_protocol") or {})
+        if phases_rec.get("active_reference"):
+            result["paired_active_reference_eligible"] = (result["paired_active_reference_eligible"] and result["valid"])
+            result.update(paired_active_reference_power_w=g("PAIRED_POWER_W"),
+                          paired_active_reference_energy_j=g("PAIRED_ENERGY_J"),
+                          paired_active_reference_pj_per_flop=g("PAIRED_PJ_PER_FLOP"),
+                          paired_active_reference_pj_per_logical_bit=g("PAIRED_PJ_PER_BIT"),
+                          paired_active_reference_drift_adjusted_power_w=g("PAIRED_DRIFT_ADJUSTED_W"),
+                          active_reference_power_w=g("REF_POWER_W"), active_reference_duration_s=g("REF_DURATION_S"),
+                          active_reference_total_energy_j=g("REF_TOTAL_ENERGY_J"),
+                          paired_active_reference_state_deltas=_paired_deltas(to, TO))
+            result["phases"]["active_reference"] = phase_dicts["active_reference"]
+            result["paired_reference_clock_domains_compared"] = (["graphics_clock_mhz", "memory_clock_mhz"]
+                                                                 + (["sm_clock_mhz"] if to[TO["PAIRED_SM_COMPARED"]] else []))
+            result["paired_reference_sm_clock_uses_graphics_proxy"] = not bool(to[TO["PAIRED_SM_COMPARED"]])
+        else:
+            result["paired_active_reference_issues"] = ["missing_paired_active_reference_phase"]
+            result["paired_active_reference_eligible"] = False
+        if workload in SFU_WORKLOADS:
+            rate = g("SFU_RATE")
+            result.update(throughput_sfu_instructions_s=rate, counted_measure_sfu_instructions=g("SFU_COUNTED"),
+                          pj_per_op=None, total_pj_per_op=None,
+                          total_pj_per_instruction=g("SFU_TOTAL_PJ"),
+                          operational_idle_increment_pj_per_instruction=g("SFU_INC_PJ"),
+                          paired_active_reference_pj_per_instruction=g("SFU_PAIRED_PJ"),
+                          sfu_reference_delta_pj_per_instruction=g("SFU_PAIRED_PJ"),
+                          sfu_reference_delta_power_w=result.get("paired_active_reference_power_w"),
+                          sfu_reference_delta_measurement_valid=result["paired_active_reference_eligible"],
+                          sfu_reference_delta_issues=sorted(set(result["paired_active_reference_issues"]
+                                                                + ["treatment:" + s for s in result["issues"]])))
+            if phases_rec.get("active_reference"):
+                result["active_reference_counted_loop_slots"] = g("REF_SLOTS")
+                result["active_reference_loop_slots_s"] = g("REF_SLOTS_RATE")
+        nonlinear = workload in NONLINEAR_WORKLOADS
+        result.update(throughput_elements_s=g("ELEMENT_RATE"), throughput_rows_s=g("ROW_RATE"),
+                      row_width=bench.get("row_width") if nonlinear else None,
+                      counted_measure_elements=g("COUNTED_ELEMENTS"),
+                      total_pj_per_element=g("PJ_ELEMENT_TOTAL"), operational_idle_increment_pj_per_element=g("PJ_ELEMENT_INC"),
+                      paired_active_reference_pj_per_element=g("PJ_ELEMENT_PAIRED"),
+                      total_pj_per_row=g("PJ_ROW_TOTAL"), operational_idle_increment_pj_per_row=g("PJ_ROW_INC"),
+                      paired_active_reference_pj_per_row=g("PJ_ROW_PAIRED"))
+        if nonlinear and g("ELEMENT_RATE") is None:
+            result["pj_per_op"] = result["total_pj_per_op"] = None
+        selected = _selected(packed, i, 1, views)
+        result["hbm_bandwidth"] = trial_bandwidth(record, result, selected, hbm_bandwidth_fraction)
+        out.append(result)
+    return out
+
+
+def _selected(packed, trial, phase, views):
+    slot = trial * N.PM_PHASES + phase
+    po = views.phase_out[slot * views.PO:(slot + 1) * views.PO]
+    lo, hi = po[N.layout("PM_PO_SEL_LO")], po[N.layout("PM_PO_SEL_HI")]
+    if math.isnan(lo):
+        return []
+    return packed.samples[slot][int(lo):int(hi)]
+
+
+_TO_NAMES = ("DURATION_S", "BENCH_MEASURED_DURATION_S", "BENCH_DEVICE_DURATION_S", "IDLE_POWER_W", "IDLE_MEMORY_POWER_W",
+             "TOTAL_ENERGY_J", "ENERGY_SOURCE_TRAPEZOID", "BOARD_POWER_W", "IDLE_ENERGY_J", "INCREMENTAL_ENERGY_J",
+             "INCREMENTAL_POWER_W", "OPS_RATE", "BYTE_RATE", "DEVICE_OPS_RATE", "DEVICE_BYTE_RATE", "COUNTED_OPS",
+             "COUNTED_BYTES", "EPOCHS", "EXACT", "RAIL_ENERGY_J", "RAIL_INCREMENTAL_J", "RAIL_INCREMENTAL_W",
+             "POWER_LIMIT_W", "TENSOR_PEAK_TFLOPS", "PEAK_CLOCK_IS_SM", "TENSOR_UTILIZATION", "IDLE_FRAC_MEASURED",
+             "IDLE_FRAC_LIMIT", "LIMIT_UTILIZATION", "PJ_PER_OP", "PJ_PER_LOGICAL_BYTE", "TOTAL_PJ_PER_OP",
+             "TOTAL_PJ_PER_LOGICAL_BYTE", "TOTAL_PJ_PER_FLOP", "TOTAL_PJ_PER_BIT", "INC_PJ_PER_FLOP", "INC_PJ_PER_BIT",
+             "BASE_CLOCK_MATCHED", "BASE_TEMP_MATCHED", "BASE_CAP_MATCHED", "BASE_STATE_MATCHED", "BASE_SM_COMPARED",
+             "BASE_ENF_COMPARED", "BASE_PSTATE_COMPARED", "DPRE_GFX", "DPRE_MEM", "DPRE_SM", "DPRE_TEMP", "DPRE_ENF",
+             "DPRE_PSTATE", "DPOST_GFX", "DPOST_MEM", "DPOST_SM", "DPOST_TEMP", "DPOST_ENF", "DPOST_PSTATE",
+             "PAIRED_POWER_W", "PAIRED_ENERGY_J", "PAIRED_ELIGIBLE", "REF_POWER_W", "REF_DURATION_S", "REF_TOTAL_ENERGY_J",
+             "PAIRED_PJ_PER_FLOP", "PAIRED_PJ_PER_BIT", "PAIRED_DRIFT_ADJUSTED_W", "PAIRED_D_GFX", "PAIRED_D_MEM",
+             "PAIRED_D_SM", "PAIRED_D_TEMP", "PAIRED_SM_COMPARED", "REF_SLOTS", "REF_SLOTS_RATE", "SFU_RATE",
+             "SFU_COUNTED", "SFU_TOTAL_PJ", "SFU_INC_PJ", "SFU_PAIRED_PJ", "ELEMENT_RATE", "ROW_RATE", "COUNTED_ELEMENTS",
+             "PJ_ELEMENT_TOTAL", "PJ_ELEMENT_INC", "PJ_ELEMENT_PAIRED", "PJ_ROW_TOTAL", "PJ_ROW_INC", "PJ_ROW_PAIRED",
+             "CONTROL_INC_POWER_W", "VALID", "BASELINE_VALID", "IDLE_INC_ELIGIBLE", "THROTTLE_MASK")
+
+
+def _state_deltas(to, TO):
+    out = {}
+    sm = bool(to[TO["BASE_SM_COMPARED"]])
+    for name, prefix in (("idle_pre", "DPRE"), ("idle_post", "DPOST")):
+        d = {"graphics_clock_mhz": _none(to[TO[prefix + "_GFX"]]), "memory_clock_mhz": _none(to[TO[prefix + "_MEM"]])}
+        if sm:
+            d["sm_clock_mhz"] = _none(to[TO[prefix + "_SM"]])
+        d["temperature_c"] = _none(to[TO[prefix + "_TEMP"]])
+        if to[TO["BASE_ENF_COMPARED"]]:
+            d["enforced_power_limit_w"] = _none(to[TO[prefix + "_ENF"]])
+        if to[TO["BASE_PSTATE_COMPARED"]]:
+            d["pstate"] = _none(to[TO[prefix + "_PSTATE"]])
+        out[name] = d
+    return out
+
+
+def _paired_deltas(to, TO):
+    d = {"graphics_clock_mhz": _none(to[TO["PAIRED_D_GFX"]]), "memory_clock_mhz": _none(to[TO["PAIRED_D_MEM"]])}
+    if to[TO["PAIRED_SM_COMPARED"]]:
+        d["sm_clock_mhz"] = _none(to[TO["PAIRED_D_SM"]])
+    d["temperature_c"] = _none(to[TO["PAIRED_D_TEMP"]])
+    return d
+
+
+def analyze_trial(record: Mapping[str, Any], policy: AnalysisPolicy | Mapping[str, Any] | None = None,
+                  hbm_bandwidth_fraction: float = 0.80) -> dict[str, Any]:
+    """One trial through the batched kernel (analysis.py:597 interface)."""
+    return analyze_trials([record], policy, hbm_bandwidth_fraction)[0]
+
+
+def group_key(trial: Mapping[str, Any]) -> str:
+    """The reference's _group_key (analysis.py:1078-1093): its sha256 seeds the group's resampling."""
+    config = {k: v for k, v in trial.get("config", {}).items() if k not in REPEAT_KEYS}
+    achieved = None if trial.get("clock_comparison_controlled") else {
+        f: trial.get(f) for f in ("graphics_clock_mhz", "memory_clock_mhz")}
+    return json.dumps({"gpu_uuid": trial.get("gpu_uuid"), "workload": trial.get("workload"),
+                       "experiment_role": trial.get("experiment_role", "legacy_unspecified"),
+                       "config": config, "uncontrolled_achieved_clocks": achieved,
+                       "benchmark_sha256": trial.get("benchmark_sha256"),
+                       "measurement_stratum": trial.get("measurement_stratum"),
+                       "experiment_contract": trial.get("experiment_contract"),
+                       "nonlinear_contract": trial.get("nonlinear_contract"),
+                       "sfu_contract": trial.get("sfu_contract"),
+                       "treatment_design_stratum": trial.get("treatment_design_stratum"),
+                       "resource_geometry": trial.get("resource_geometry")}, sort_keys=True, separators=(",", ":"))
+
+
+def group_seed(key: str) -> int:
+    return int(hashlib.sha256(key.encode()).hexdigest()[:16], 16)
+
+
+def bootstrap_groups(values: np.ndarray, members: list[list[int]], seeds: list[int],
+                     resamples: int = DEFAULT_RESAMPLES) -> tuple[np.ndarray, np.ndarray, np.ndarray]:
+    """Medians and CIs of ``values[rows, metrics]`` for each group's member rows, on the GPU."""
+    values = np.ascontiguousarray(values, dtype=np.float64)
+    n_rows, n_metrics = values.shape
+    offsets = np.zeros(len(members) + 1, dtype=np.int32)
+    np.cumsum([len(m) for m in members], out=offsets[1:])
+    rows = np.ascontiguousarray(np.concatenate([np.asarray(m, dtype=np.int32) for m in members]) if members else np.zeros(0, np.int32))
+    seeds_a = np.asarray(seeds, dtype=np.uint64)
+    G = len(members)
+    med, lo, hi = (np.empty((G, n_metrics)) for _ in range(3))
+    job = N.BootstrapJob(G, n_metrics, int(rows.size), n_rows, resamples, max((len(m) for m in members), default=0),
+                         values.ctypes.data, offsets.ctypes.data, rows.ctypes.data if rows.size else None, None,
+                         seeds_a.ctypes.data if G else None, med.ctypes.data, lo.ctypes.data, hi.ctypes.data)
+    N.check(N.library().pm_group_bootstrap(job), "pm_group_bootstrap")
+    return med, lo, hi
+
+
+def median_ci(values: list[float], seed: int, resamples: int = DEFAULT_RESAMPLES) -> list[float] | None:
+    """_median_ci (analysis.py:1096-1101) for one value list, on the GPU."""
+    if len(values) < 3:
+        return None
+    _, lo, hi = bootstrap_groups(np.asarray(values, dtype=np.float64).reshape(-1, 1), [list(range(len(values)))], [seed], resamples)
+    return [float(lo[0, 0]), float(hi[0, 0])]
+
+
+def summarize(records: Iterable[Mapping[str, Any]], throughput_fraction: float = 0.95,
+              policy: AnalysisPolicy | Mapping[str, Any] | None = None, min_repeats: int = 3,
+              plan: Mapping[str, Any] | None = None, evaluation_policy=None,
+              hbm_bandwidth_fraction: float = 0.80, resamples: int = DEFAULT_RESAMPLES) -> dict[str, Any]:
+    """summarize's trial and group sections (analysis.py:1400-1519); ``resamples`` generalises the 1000 draws."""
+    if not 0 < throughput_fraction <= 1 or min_repeats < 1:
+        raise ValueError("throughput_fraction must be in (0, 1], min_repeats must be positive")
+    from .hbm import group_bandwidth, validate_fraction
+    hbm_bandwidth_fraction = validate_fraction(hbm_bandwidth_fraction)
+    policy = _policy(policy)
+    records = list(records)
+    seen, duplicates, kept = set(), [], []
+    for record in records:
+        trial_id = record.get("trial_id")
+        if trial_id is not None and trial_id in seen:
+            duplicates.append(trial_id)
+            continue
+        if trial_id is not None:
+            seen.add(trial_id)
+        kept.append(record)
+    metrics_out: list = []
+    trials = analyze_trials(kept, policy, hbm_bandwidth_fraction, _metrics_out=metrics_out)
+    metric_rows = metrics_out[0][0] if metrics_out else np.zeros((0, len(METRICS)))
+    buckets: dict[str, list[int]] = {}
+    for index, trial in enumerate(trials):
+        buckets.setdefault(group_key(trial), []).append(index)
+    ordered = sorted(buckets.items())
+    members, seeds, groups = [], [], []
+    for key, indices in ordered:
+        valid, seen_repeats, dup_repeats = [], set(), []
+        for index in indices:
+            trial = trials[index]
+            if not trial["valid"]:
+                continue
+            repeat = trial.get("repeat_index")
+            if repeat is not None and repeat in seen_repeats:
+                dup_repeats.append(repeat)
+                continue
+            if repeat is not None:
+                seen_repeats.add(repeat)
+            valid.append(index)
+        digest = hashlib.sha256(key.encode()).hexdigest()[:16]
+        members.append(valid)
+        seeds.append(int(digest, 16))
+        first = trials[indices[0]]
+        vt = [trials[i] for i in valid]
+        group = {"group_id": digest, "gpu_uuid": first["gpu_uuid"], "workload": first["workload"],
+                 "experiment_role": first.get("experiment_role", "legacy_unspecified"),
+                 "experiment_contract": first.get("experiment_contract"),
+                 "nonlinear_contract": first.get("nonlinear_contract"), "sfu_contract": first.get("sfu_contract"),
+                 "config": {k: v for k, v in first["config"].items() if k not in REPEAT_KEYS},
+                 "benchmark_sha256": first["benchmark_sha256"], "measurement_stratum": first["measurement_stratum"],
+                 "kernel_implementation_version": first.get("kernel_implementation_version"),
+                 "treatment_design_stratum": first["treatment_design_stratum"],
+                 "resource_geometry": first["resource_geometry"],
+                 "repeats": len(indices), "valid_repeats": len(valid), "trial_ids": [trials[i]["trial_id"] for i in indices],
+                 "duplicate_repeat_indices_ignored": dup_repeats,
+                 "target_verified": False, "verified_selection_eligible": False,
+                 "count_energy_time_alignment_exact": bool(vt) and all(t["count_energy_time_alignment_exact"] for t in vt),
+                 "clock_comparison_controlled": bool(vt) and all(t["clock_comparison_controlled"] for t in vt),
+                 "diagnostic_only": first["diagnostic_only"], "gpu_name": first["gpu_name"],
+                 "baseline_valid": bool(vt) and all(t["baseline_valid"] for t in vt),
+                 "operational_idle_increment_eligible": bool(vt) and all(t["operational_idle_increment_eligible"] for t in vt),
+                 "paired_active_reference_eligible": bool(vt) and all(t["paired_active_reference_eligible"] for t in vt),
+                 "paired_reference_order_counts": {o: sum((t.get("paired_active_reference_protocol") or {}).get("order") == o for t in vt)
+                                                   for o in ("AB", "BA")},
+                 "confidence": "repeat_median" if len(valid) >= min_repeats else "insufficient_valid_repeats", "ci95": {}}
+        groups.append(group)
+    med, lo, hi = bootstrap_groups(metric_rows, members, seeds, resamples) if groups else (None, None, None)
+    for g, group in enumerate(groups):
+        for m, metric in enumerate(METRICS):
+            group[metric] = _none(med[g, m])
+            a, b = _none(lo[g, m]), _none(hi[g, m])
+            group["ci95"][metric] = [a, b] if a is not None else None
+        vt = [trials[i] for i in members[g]]
+        group["hbm_bandwidth"] = group_bandwidth(vt, group["workload"], hbm_bandwidth_fraction)
+        counts = group["paired_reference_order_counts"]
+        group["paired_reference_both_orders_observed"] = all(counts.values())
+        group["paired_reference_counterbalanced"] = group["paired_reference_both_orders_observed"] and counts["AB"] == counts["BA"]
+        group["paired_reference_order_count_imbalance"] = counts["AB"] - counts["BA"]
+        group["paired_active_reference_eligible"] = group["paired_active_reference_eligible"] and group["paired_reference_counterbalanced"]
+        arm = {}
+        for order in ("AB", "BA"):
+            vals = [v for t in vt if (t.get("paired_active_reference_protocol") or {}).get("order") == order
+                    and (v := finite(t.get("paired_active_reference_power_w"))) is not None]
+            arm[order] = statistics.median(vals) if vals else None
+        group["paired_reference_order_medians_power_w"] = arm
+        group["paired_reference_order_effect_power_w"] = arm["AB"] - arm["BA"] if None not in arm.values() else None
+    return {"schema_version": 2, "trials": trials, "groups": groups, "duplicate_trial_ids_ignored": duplicates,
+            "selection_policy": {"throughput_fraction": throughput_fraction, "hbm_bandwidth_fraction": hbm_bandwidth_fraction,
+                                 "min_repeats": min_repeats, "resamples": resamples,
+                                 "ci_method": f"deterministic percentile bootstrap of repeat medians ({resamples} draws)"}}
+

@@ -1,0 +1,933 @@
+// Batched trial analysis on sm_100a: one CTA per trial.
+//
+// Restates, in data-parallel form, the numeric core of the reference's
+// powermodeling/analysis.py:
+//   _interpolate / _integrate            analysis.py:94-124
+//   _phase_stats                         analysis.py:127-207
+//   _idle_at                             analysis.py:210-216
+//   _measure_epochs                      analysis.py:228-276
+//   analyze_trial (numeric body, gates)  analysis.py:597-1056
+//   _paired_reference_contrast           analysis.py:292-423
+// Samples arrive sorted and de-duplicated per (trial, phase) slot, so the
+// selection window, the covering neighbours and every interpolation bracket
+// are binary searches; medians come from a CTA-wide bitonic sort of up to ten
+// columns at once; the trapezoid and counter sums run sequentially on single
+// lanes in the reference's order (CPython's compensated float sum), so the
+// energies agree bit for bit with the reference's.
+#include "pmb200.h"
+#include "pm_layout.h"
+#include "pm_device.cuh"
+#include "pm_capi.h"
+
+namespace pm {
+
+constexpr int kThreads = 256;
+constexpr int kMaxEpochs = 256;        // per arm; the host rejects longer lists
+enum Col { C_GAP = 0, C_CHANGE, C_POWER, C_GFX, C_SM, C_MEM, C_TEMP, C_PLIMIT, C_ENF, C_PSTATE, C_COUNT };
+static_assert(C_COUNT == kSortColumns, "sort column count");
+
+struct EpochResult {
+  int32_t n_inner;            // complete epochs kept (0 = none)
+  int32_t issue;              // -1 none, else offset from PM_IT_EP_PHASE_WINDOW
+  double start_s, end_s;      // aligned window
+  double ops, bytes, slots;   // sums over kept epochs (NaN slots if any missing)
+  int32_t exact;              // every kept epoch counts_exact
+};
+
+struct Shared {
+  double po[PM_PHASES][PM_PO_COUNT];
+  uint32_t pf[PM_PHASES];
+  EpochResult ep[2];
+  int16_t order[2][kMaxEpochs];
+  // per-phase broadcast scratch
+  int64_t sel_lo, sel_hi, cov_lo, cov_hi;
+  double wstart, wend;
+  int32_t nchange;
+  int32_t nfin[C_COUNT];
+};
+
+__device__ __forceinline__ double col_value(const pm_trials& T, int c, int64_t i) {
+  switch (c) {
+    case C_POWER: return T.power_w[i];
+    case C_GFX: return T.graphics_clock_mhz[i];
+    case C_SM: return T.sm_clock_mhz[i];
+    case C_MEM: return T.memory_clock_mhz[i];
+    case C_TEMP: return T.temperature_c[i];
+    case C_PLIMIT: return T.power_limit_w[i];
+    case C_ENF: return T.enforced_power_limit_w[i];
+    default: return T.pstate[i];
+  }
+}
+
+// Value of the reference's _interpolate(samples, field, x) over covering
+// samples [cb, ce) whose values come from `val`.
+template <class V>
+__device__ double interpolate(const double* t, int64_t cb, int64_t ce, double x, V val) {
+  if (ce <= cb || x < t[cb] || x > t[ce - 1]) return dnan();
+  const int64_t i = lower_bound(t, cb, ce, x);
+  if (t[i] == x) return val(i);
+  const double a = val(i - 1), b = val(i);
+  if (none(a) || none(b)) return dnan();
+  const double ratio = (x - t[i - 1]) / (t[i] - t[i - 1]);
+  return a + ratio * (b - a);
+}
+
+// The reference's _integrate(covering, field, start, end).
+template <class V>
+__device__ double integrate(const double* t, int64_t cb, int64_t ce, double start, double end, V val) {
+  const double first = interpolate(t, cb, ce, start, val);
+  const double last = interpolate(t, cb, ce, end, val);
+  if (none(first) || none(last) || end <= start) return dnan();
+  NeumaierSum s;
+  double pt = start, pv = first;
+  for (int64_t i = upper_bound(t, cb, ce, start); i < ce && t[i] < end; ++i) {
+    const double v = val(i);
+    if (none(v)) return dnan();
+    s.add((t[i] - pt) * (pv + v) * 0.5);
+    pt = t[i]; pv = v;
+  }
+  s.add((end - pt) * (pv + last) * 0.5);
+  return s.result();
+}
+
+// ---------------------------------------------------------------------------
+// _measure_epochs for one arm (single thread).
+__device__ void measure_epochs(const pm_trials& T, const pm_policy& P, int trial, int arm,
+                               double phase_start, double phase_end, double whole_ops, double whole_bytes,
+                               EpochResult& r, int16_t* order) {
+  r.n_inner = 0; r.issue = -1; r.start_s = r.end_s = dnan();
+  r.ops = r.bytes = r.slots = dnan(); r.exact = 0;
+  const int status = T.epoch_status[trial * 2 + arm];
+  if (status == PM_EP_NONE || status == PM_EP_INVALID_LIST) return;
+  if (none(phase_start) || none(phase_end)) { r.issue = 0; return; }
+  const int32_t b = T.epoch_offsets[trial * 2 + arm], e = T.epoch_offsets[trial * 2 + arm + 1];
+  const int n = e - b;
+  for (int k = 0; k < n; ++k) {
+    const double a = T.epoch_start_s[b + k], z = T.epoch_end_s[b + k];
+    if (none(a) || none(z) || z <= a || a < phase_start - 1e-6 || z > phase_end + 1e-6) { r.issue = 1; return; }
+    const double ops = T.epoch_operations[b + k];
+    if (none(ops) || ops < 0) { r.issue = 2; return; }
+    const double bytes = T.epoch_logical_bytes[b + k];
+    if (none(bytes) || bytes < 0) { r.issue = 3; return; }
+  }
+  if (status == PM_EP_NON_DICT_AFTER) { r.issue = 8; return; }
+  // Stable insertion sort by start (Python's list.sort is stable).
+  for (int k = 0; k < n; ++k) {
+    const double key = T.epoch_start_s[b + k];
+    int j = k - 1;
+    while (j >= 0 && T.epoch_start_s[b + order[j]] > key) { order[j + 1] = order[j]; --j; }
+    order[j + 1] = (int16_t)k;
+  }
+  for (int k = 1; k < n; ++k)
+    if (T.epoch_start_s[b + order[k]] < T.epoch_end_s[b + order[k - 1]] - 1e-6) { r.issue = 4; return; }
+  int first = -1, last = -1, kept = 0;
+  for (int k = 0; k < n; ++k) {
+    const int i = b + order[k];
+    if (T.epoch_start_s[i] >= phase_start + P.trim_s - 1e-6 && T.epoch_end_s[i] <= phase_end - P.trim_s + 1e-6) {
+      if (first < 0) first = k;
+      last = k; ++kept;
+    }
+  }
+  if (kept == 0 || T.epoch_end_s[b + order[last]] - T.epoch_start_s[b + order[first]] < P.min_measure_s - 1e-6) {
+    r.issue = 5; return;
+  }
+  NeumaierSum so, sb;
+  for (int k = 0; k < n; ++k) { so.add(T.epoch_operations[b + order[k]]); sb.add(T.epoch_logical_bytes[b + order[k]]); }
+  const double counted_ops = so.result(), counted_bytes = sb.result();
+  if (!none(whole_ops) && fabs(counted_ops - whole_ops) > fmax(fabs(whole_ops) * 1e-6, 1.0)) { r.issue = 6; return; }
+  if (!none(whole_bytes) && fabs(counted_bytes - whole_bytes) > fmax(fabs(whole_bytes) * 1e-6, 1.0)) { r.issue = 7; return; }
+  // Inner epochs keep sorted order; they need not be contiguous in it.
+  NeumaierSum io, ib, is;
+  bool exact = true, slots_ok = true;
+  double s0 = dnan(), s1 = dnan();
+  int m = 0;
+  for (int k = 0; k < n; ++k) {
+    const int i = b + order[k];
+    if (!(T.epoch_start_s[i] >= phase_start + P.trim_s - 1e-6 && T.epoch_end_s[i] <= phase_end - P.trim_s + 1e-6)) continue;
+    if (m == 0) s0 = T.epoch_start_s[i];
+    s1 = T.epoch_end_s[i];
+    io.add(T.epoch_operations[i]); ib.add(T.epoch_logical_bytes[i]);
+    const double sl = T.epoch_loop_slots[i];
+    if (none(sl)) slots_ok = false; else is.add(sl);
+    exact = exact && T.epoch_counts_exact[i] != 0;
+    order[m++] = order[k];   // compact kept indices in place (m <= k)
+  }
+  r.n_inner = m; r.start_s = s0; r.end_s = s1;
+  r.ops = io.result(); r.bytes = ib.result();
+  r.slots = slots_ok ? is.result() : dnan();
+  r.exact = exact ? 1 : 0;
+}
+
+// ---------------------------------------------------------------------------
+// _phase_stats for slot (trial, p) on window [start, end] after `trim`.
+// Writes Shared::po[p] / pf[p].  All threads call it.
+__device__ void phase_stats(const pm_trials& T, const pm_policy& P, Shared& S, double* sortbuf, int SP,
+                            int trial, int p, double start, double end, double trim, bool idle, bool aligned) {
+  double* po = S.po[p];
+  const int slot = trial * PM_PHASES + p;
+  const int64_t seg_b = T.phase_offsets[slot], seg_e = T.phase_offsets[slot + 1];
+  if (threadIdx.x == 0) {
+    for (int f = 0; f < PM_PO_COUNT; ++f) po[f] = dnan();
+    S.pf[p] = aligned ? (1u << PM_PF_ALIGNED) : 0u;
+  }
+  __syncthreads();
+  if (!T.phase_present[slot]) {
+    if (threadIdx.x == 0) S.pf[p] |= 1u << PM_PF_MISSING;
+    __syncthreads();
+    return;
+  }
+  if (none(start) || none(end) || end <= start || end - start <= trim * 2) {
+    if (threadIdx.x == 0) S.pf[p] |= 1u << PM_PF_INVALID_WINDOW;
+    __syncthreads();
+    return;
+  }
+  start = start + trim; end = end - trim;
+  const double duration = end - start;
+  const double* t = T.t_s;
+  if (threadIdx.x == 0) {
+    const int64_t lo = lower_bound(t, seg_b, seg_e, start);
+    const int64_t hi = upper_bound(t, seg_b, seg_e, end);
+    S.sel_lo = lo; S.sel_hi = hi;
+    S.cov_lo = lo > seg_b ? lo - 1 : lo;
+    S.cov_hi = hi < seg_e ? hi + 1 : hi;
+    S.nchange = 0;
+    for (int c = 0; c < C_COUNT; ++c) S.nfin[c] = 0;
+  }
+  __syncthreads();
+  const int64_t lo = S.sel_lo, hi = S.sel_hi, cb = S.cov_lo, ce = S.cov_hi;
+  const int nsel = (int)(hi - lo), ncov = (int)(ce - cb);
+  // ---- columns to sort: +inf marks "not a value" so finite values lead.
+  const double inf = dinf();
+  for (int q = threadIdx.x; q < SP; q += blockDim.x) {
+    double* col = sortbuf;
+    col[C_GAP * SP + q] = (q < ncov - 1) ? t[cb + q + 1] - t[cb + q] : inf;
+    col[C_CHANGE * SP + q] = inf;
+    for (int c = C_POWER; c < C_COUNT; ++c) {
+      double v = inf;
+      if (q < nsel) { const double x = col_value(T, c, lo + q); if (!none(x)) v = x; }
+      col[c * SP + q] = v;
+    }
+  }
+  __syncthreads();
+  // ---- change instants: selected pairs whose _finite(power) differ.
+  // The list is ordered; compact with a CTA prefix count.
+  {
+    __shared__ int warp_counts[kThreads / 32];
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    int base = 0;
+    for (int q0 = 0; q0 < nsel - 1; q0 += blockDim.x) {
+      const int q = q0 + threadIdx.x;
+      bool change = false;
+      if (q < nsel - 1) {
+        const double a = T.power_w[lo + q], b = T.power_w[lo + q + 1];
+        change = none(a) != none(b) || (!none(a) && a != b);
+      }
+      const unsigned ballot = __ballot_sync(0xffffffffu, change);
+      if (lane == 0) warp_counts[warp] = __popc(ballot);
+      __syncthreads();
+      int before = base;
+      for (int w = 0; w < warp; ++w) before += warp_counts[w];
+      int total = 0;
+      for (int w = 0; w < (int)(blockDim.x >> 5); ++w) total += warp_counts[w];
+      if (change) {
+        const int pos = before + __popc(ballot & ((1u << lane) - 1u));
+        // store the change instant temporarily in the CHANGE column
+        sortbuf[C_CHANGE * SP + pos] = t[lo + q + 1];
+      }
+      base += total;
+      __syncthreads();
+    }
+    if (threadIdx.x == 0) S.nchange = base;
+    __syncthreads();
+    // Gaps between consecutive change instants, in place: each chunk of
+    // blockDim.x slots reads its two neighbours before any slot is rewritten.
+    const int nch = S.nchange;
+    double* ch = sortbuf + C_CHANGE * SP;
+    for (int q0 = 0; q0 < SP; q0 += blockDim.x) {
+      const int q = q0 + threadIdx.x;
+      double g = inf;
+      if (q + 1 < nch) g = ch[q + 1] - ch[q];
+      __syncthreads();
+      if (q < SP) ch[q] = g;
+      __syncthreads();
+    }
+  }
+  // ---- flag reductions over selected samples.
+  uint32_t flags = 0;
+  unsigned long long thr_or = 0ull;
+  unsigned src_mask = 0;
+  bool neg_power = false;
+  int plim_none = 0, enf_none = 0, pst_none = 0;
+  for (int64_t i = lo + threadIdx.x; i < hi; i += blockDim.x) {
+    const uint16_t sf = T.sample_flags[i];
+    if (!none(T.sm_clock_mhz[i])) flags |= 1u << PM_PF_ANY_SM_FINITE;
+    if (none(T.temperature_c[i])) flags |= 1u << PM_PF_TEMP_MISSING;
+    { const double v = T.graphics_clock_mhz[i]; if (none(v) || v <= 0) flags |= 1u << PM_PF_GFX_NONPOS; }
+    { const double v = T.memory_clock_mhz[i]; if (none(v) || v <= 0) flags |= 1u << PM_PF_MEM_NONPOS; }
+    { const double v = T.sm_clock_mhz[i]; if (none(v) || v <= 0) flags |= 1u << PM_PF_SM_NONPOS; }
+    if (!(sf & PM_S_THROTTLE_VALID)) flags |= 1u << PM_PF_THROTTLE_MISSING;
+    else thr_or |= (unsigned long long)T.throttle_reasons[i] & ~3ull;
+    if (sf & PM_S_FOREIGN_PID) flags |= 1u << PM_PF_FOREIGN_PID;
+    if (sf & PM_S_NO_COMPUTE_INV) flags |= 1u << PM_PF_NO_COMPUTE_INV;
+    if (sf & PM_S_NO_GRAPHICS_INV) flags |= 1u << PM_PF_NO_GRAPHICS_INV;
+    if (sf & PM_S_MPS) flags |= 1u << PM_PF_MPS;
+    if (sf & PM_S_PID_UNKNOWN) flags |= 1u << PM_PF_PID_UNKNOWN;
+    if (sf & PM_S_REF_FOREIGN) flags |= 1u << PM_PF_REF_FOREIGN;
+    if ((sf & PM_S_MEMORY_POWER_SET) && T.memory_power_source[i]) src_mask |= 1u << (T.memory_power_source[i] & 15);
+    plim_none += none(T.power_limit_w[i]);
+    enf_none += none(T.enforced_power_limit_w[i]);
+    pst_none += none(T.pstate[i]);
+  }
+  // negative power is checked over the covering samples
+  for (int64_t i = cb + threadIdx.x; i < ce; i += blockDim.x) {
+    const double v = T.power_w[i];
+    if (!none(v) && v < 0) neg_power = true;
+  }
+  // per-column finite counts (selected columns; gaps counted from ncov)
+  int fin[C_COUNT];
+  for (int c = 0; c < C_COUNT; ++c) fin[c] = 0;
+  for (int64_t i = lo + threadIdx.x; i < hi; i += blockDim.x)
+    for (int c = C_POWER; c < C_COUNT; ++c) fin[c] += !none(col_value(T, c, i));
+  // CTA reductions
+  {
+    __shared__ uint32_t red_flags; __shared__ unsigned long long red_thr; __shared__ unsigned red_src;
+    __shared__ int red_neg, red_pn, red_en, red_sn;
+    if (threadIdx.x == 0) { red_flags = 0; red_thr = 0; red_src = 0; red_neg = 0; red_pn = red_en = red_sn = 0; }
+    __syncthreads();
+    if (flags) atomicOr(&red_flags, flags);
+    if (thr_or) atomicOr(&red_thr, thr_or);
+    if (src_mask) atomicOr(&red_src, src_mask);
+    if (neg_power) atomicOr(&red_neg, 1);
+    if (plim_none) atomicAdd(&red_pn, plim_none);
+    if (enf_none) atomicAdd(&red_en, enf_none);
+    if (pst_none) atomicAdd(&red_sn, pst_none);
+    for (int c = C_POWER; c < C_COUNT; ++c) if (fin[c]) atomicAdd(&S.nfin[c], fin[c]);
+    __syncthreads();
+    if (threadIdx.x == 0) {
+      uint32_t f = red_flags;
+      if (red_thr) f |= 1u << PM_PF_THROTTLE_ACTIVE;
+      if (red_neg) f |= 1u << PM_PF_NEGATIVE_POWER;
+      S.pf[p] |= f | (1u << PM_PF_COMPUTED);
+      po[PM_PO_THROTTLE_OR] = (double)red_thr;
+      po[PM_PO_MEM_SOURCES] = (double)red_src;
+      po[PM_PO_PLIMIT_NONE] = red_pn; po[PM_PO_ENF_NONE] = red_en; po[PM_PO_PSTATE_NONE] = red_sn;
+      S.nfin[C_GAP] = ncov > 1 ? ncov - 1 : 0;
+      S.nfin[C_CHANGE] = S.nchange > 1 ? S.nchange - 1 : 0;
+    }
+  }
+  __syncthreads();
+  // ---- sort the columns (medians, minima, maxima, distinct values)
+  bitonic_sort_arrays(sortbuf, C_COUNT, SP);
+  // ---- sequential integrals on three lanes of three different warps
+  const int lane_id = threadIdx.x;
+  if (lane_id == 0) {
+    const double energy = integrate(t, cb, ce, start, end, [&](int64_t i) { return T.power_w[i]; });
+    po[PM_PO_ENERGY_J] = energy;
+    po[PM_PO_INTEGRATED_POWER_W] = none(energy) ? dnan() : energy / duration;
+  } else if (lane_id == 32) {
+    const double me = integrate(t, cb, ce, start, end, [&](int64_t i) { return T.memory_power_w[i]; });
+    po[PM_PO_MEMORY_ENERGY_J] = me;
+    po[PM_PO_MEMORY_POWER_W] = none(me) ? dnan() : me / duration;
+  } else if (lane_id == 64) {
+    // Energy counter relative to the first exact-int reading in covering.
+    int64_t anchor = 0;
+    for (int64_t i = cb; i < ce; ++i) if (T.sample_flags[i] & PM_S_ENERGY_ANCHOR) { anchor = T.energy_int[i]; break; }
+    auto rel = [&](int64_t i) -> double {
+      const uint16_t sf = T.sample_flags[i];
+      double v;
+      if (sf & PM_S_ENERGY_INT) v = (double)(long long)((unsigned long long)T.energy_int[i] - (unsigned long long)anchor);
+      else if (sf & PM_S_ENERGY_FLOAT) v = T.energy_float[i] - (double)anchor;
+      else return dnan();
+      return isfinite(v) ? v : dnan();
+    };
+    const double c0 = interpolate(t, cb, ce, start, rel);
+    const double c1 = interpolate(t, cb, ce, end, rel);
+    bool reset = false, have = false;
+    double prev = 0.0;
+    for (int64_t i = cb; i < ce; ++i) {
+      const double v = rel(i);
+      if (none(v)) continue;
+      if (have && v < prev) reset = true;
+      prev = v; have = true;
+    }
+    double counter = dnan();
+    if (!none(c0) && !none(c1)) {
+      if (reset || c1 < c0) S.pf[p] |= 1u << PM_PF_COUNTER_RESET;  // only lane 64 writes here now
+      else counter = (c1 - c0) / 1000.0;
+    }
+    po[PM_PO_COUNTER_J] = counter;
+  }
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    po[PM_PO_START_S] = start; po[PM_PO_END_S] = end; po[PM_PO_DURATION_S] = duration;
+    po[PM_PO_MIDPOINT_S] = (start + end) / 2;
+    po[PM_PO_SAMPLES] = nsel;
+    po[PM_PO_SEL_LO] = (double)(lo - seg_b); po[PM_PO_SEL_HI] = (double)(hi - seg_b);
+    po[PM_PO_COV_LO] = (double)(cb - seg_b); po[PM_PO_COV_HI] = (double)(ce - seg_b);
+    const double* gap = sortbuf + C_GAP * SP;
+    const int ngap = S.nfin[C_GAP];
+    po[PM_PO_GAP_MEDIAN_S] = sorted_median(gap, ngap);
+    po[PM_PO_GAP_MAX_S] = ngap ? gap[ngap - 1] : dnan();
+    po[PM_PO_CHANGE_MEDIAN_S] = sorted_median(sortbuf + C_CHANGE * SP, S.nfin[C_CHANGE]);
+    {
+      const double* pw = sortbuf + C_POWER * SP;
+      const int n = S.nfin[C_POWER];
+      int distinct = 0;
+      for (int i = 0; i < n; ++i) distinct += (i == 0 || pw[i] != pw[i - 1]);
+      po[PM_PO_DISTINCT_POWER] = distinct;
+    }
+    const int stat_cols[7] = {C_GFX, C_SM, C_MEM, C_TEMP, C_PLIMIT, C_ENF, C_PSTATE};
+    const int med_slot[7] = {PM_PO_GFX_MED, PM_PO_SM_MED, PM_PO_MEM_MED, PM_PO_TEMP_MED, PM_PO_PLIMIT_MED, PM_PO_ENF_MED, PM_PO_PSTATE_MED};
+    const int min_slot[7] = {PM_PO_GFX_MIN, PM_PO_SM_MIN, PM_PO_MEM_MIN, PM_PO_TEMP_MIN, PM_PO_PLIMIT_MIN, PM_PO_ENF_MIN, PM_PO_PSTATE_MIN};
+    const int max_slot[7] = {PM_PO_GFX_MAX, PM_PO_SM_MAX, PM_PO_MEM_MAX, PM_PO_TEMP_MAX, PM_PO_PLIMIT_MAX, PM_PO_ENF_MAX, PM_PO_PSTATE_MAX};
+    for (int k = 0; k < 7; ++k) {
+      const double* v = sortbuf + stat_cols[k] * SP;
+      const int n = S.nfin[stat_cols[k]];
+      po[med_slot[k]] = sorted_median(v, n);
+      po[min_slot[k]] = n ? v[0] : dnan();
+      po[max_slot[k]] = n ? v[n - 1] : dnan();
+    }
+    po[PM_PO_PLIMIT_FIN] = S.nfin[C_PLIMIT]; po[PM_PO_ENF_FIN] = S.nfin[C_ENF]; po[PM_PO_PSTATE_FIN] = S.nfin[C_PSTATE];
+    // power_w: counter rate if present else trapezoid rate
+    const double energy = po[PM_PO_ENERGY_J], counter = po[PM_PO_COUNTER_J];
+    po[PM_PO_POWER_W] = !none(counter) ? counter / duration : po[PM_PO_INTEGRATED_POWER_W];
+    uint32_t f = S.pf[p];
+    const double minimum = idle ? P.min_idle_s : P.min_measure_s;
+    if (duration + 1e-9 < minimum) f |= 1u << PM_PF_SHORT_PLATEAU;
+    if (nsel < P.min_samples) f |= 1u << PM_PF_TOO_FEW_SAMPLES;
+    if (ngap && gap[ngap - 1] > P.max_sample_gap_s) f |= 1u << PM_PF_TELEMETRY_GAP;
+    if (none(energy)) f |= 1u << PM_PF_MISSING_POWER_COVERAGE;
+    if (!none(counter) && !none(energy) && energy > 0) {
+      const double d = fabs(counter - energy) / energy;
+      po[PM_PO_DISAGREEMENT] = d;
+      if (d > P.counter_disagreement_fraction) f |= 1u << PM_PF_COUNTER_DISAGREEMENT;
+    }
+    S.pf[p] = f;
+  }
+  __syncthreads();
+}
+
+// CTA-wide: does any selected sample of phase p violate |v - center| <= tol
+// (relative: |v - center| / center <= tol), or miss the value?
+__device__ bool any_outside(const pm_trials& T, const Shared& S, int trial, int p, int column,
+                            double center, double tol, bool relative) {
+  const int slot = trial * PM_PHASES + p;
+  const int64_t b = T.phase_offsets[slot];
+  bool bad = false;
+  if (S.pf[p] & (1u << PM_PF_COMPUTED)) {
+    const int64_t lo = b + (int64_t)S.po[p][PM_PO_SEL_LO], hi = b + (int64_t)S.po[p][PM_PO_SEL_HI];
+    for (int64_t i = lo + threadIdx.x; i < hi; i += blockDim.x) {
+      const double v = col_value(T, column, i);
+      if (none(v)) { bad = true; break; }
+      const double d = fabs(v - center);
+      if (relative ? (d / center > tol) : (d > tol)) { bad = true; break; }
+    }
+  }
+  return __syncthreads_or(bad) != 0;
+}
+
+__device__ __forceinline__ double fin(double x) { return x; }   // NaN already means None
+__device__ __forceinline__ bool truthy(double x) { return !none(x) && x != 0.0; }
+
+// _idle_at(pre, post, active, field) on phase outputs.
+__device__ double idle_at(const double* pre, const double* post, const double* act, int field) {
+  const double a = pre[field], b = post[field];
+  const double t0 = pre[PM_PO_MIDPOINT_S], t1 = post[PM_PO_MIDPOINT_S], t = act[PM_PO_MIDPOINT_S];
+  if (none(a) || none(b) || none(t0) || none(t1) || none(t) || t1 <= t0 || !(t0 <= t && t <= t1)) return dnan();
+  return a + (b - a) * (t - t0) / (t1 - t0);
+}
+
+__global__ void __launch_bounds__(kThreads)
+analyze_kernel(pm_trials T, pm_policy P, pm_trial_results R, int SP, double* gscratch) {
+  __shared__ Shared S;
+  extern __shared__ double dyn[];
+  const int trial = blockIdx.x;
+  double* sortbuf = gscratch ? gscratch + (size_t)blockIdx.x * C_COUNT * SP : dyn;
+  const double* ts = T.trial_scalars + (size_t)trial * PM_TS_COUNT;
+  const uint32_t tflags = T.trial_flags[trial];
+  const int wl = tflags & PM_T_WORKLOAD_MASK;
+  const bool tensor = wl == PM_WL_TENSOR, memory = wl == PM_WL_MEMORY, sfu = wl == PM_WL_SFU, nonlinear = wl == PM_WL_NONLINEAR;
+  const bool energy_wl = wl != PM_WL_OTHER;
+  const int ms = trial * PM_PHASES;
+
+  if (threadIdx.x == 0) {
+    measure_epochs(T, P, trial, 0, T.phase_present[ms + PM_MEASURE] ? T.phase_start_s[ms + PM_MEASURE] : dnan(),
+                   T.phase_present[ms + PM_MEASURE] ? T.phase_end_s[ms + PM_MEASURE] : dnan(),
+                   ts[PM_TS_BENCH_OPERATIONS], ts[PM_TS_BENCH_LOGICAL_BYTES], S.ep[0], S.order[0]);
+    if (T.phase_present[ms + PM_REFERENCE])
+      measure_epochs(T, P, trial, 1, T.phase_start_s[ms + PM_REFERENCE], T.phase_end_s[ms + PM_REFERENCE],
+                     ts[PM_TS_REF_OPERATIONS], ts[PM_TS_REF_LOGICAL_BYTES], S.ep[1], S.order[1]);
+    else { S.ep[1].n_inner = 0; S.ep[1].issue = -1; S.ep[1].exact = 0; }
+  }
+  __syncthreads();
+  phase_stats(T, P, S, sortbuf, SP, trial, PM_IDLE_PRE, T.phase_start_s[ms + PM_IDLE_PRE], T.phase_end_s[ms + PM_IDLE_PRE], P.idle_trim_s, true, false);
+  phase_stats(T, P, S, sortbuf, SP, trial, PM_IDLE_POST, T.phase_start_s[ms + PM_IDLE_POST], T.phase_end_s[ms + PM_IDLE_POST], P.idle_trim_s, true, false);
+  if (S.ep[0].n_inner > 0)
+    phase_stats(T, P, S, sortbuf, SP, trial, PM_MEASURE, S.ep[0].start_s, S.ep[0].end_s, 0.0, false, true);
+  else
+    phase_stats(T, P, S, sortbuf, SP, trial, PM_MEASURE, T.phase_start_s[ms + PM_MEASURE], T.phase_end_s[ms + PM_MEASURE], P.trim_s, false, false);
+  const bool has_ref = T.phase_present[ms + PM_REFERENCE] != 0;
+  if (has_ref) {
+    if (S.ep[1].n_inner > 0)
+      phase_stats(T, P, S, sortbuf, SP, trial, PM_REFERENCE, S.ep[1].start_s, S.ep[1].end_s, 0.0, false, true);
+    else
+      phase_stats(T, P, S, sortbuf, SP, trial, PM_REFERENCE, T.phase_start_s[ms + PM_REFERENCE], T.phase_end_s[ms + PM_REFERENCE], P.trim_s, false, false);
+  } else if (threadIdx.x == 0) {
+    for (int f = 0; f < PM_PO_COUNT; ++f) S.po[PM_REFERENCE][f] = dnan();
+    S.pf[PM_REFERENCE] = 1u << PM_PF_MISSING;
+  }
+  const bool has_control = T.phase_present[ms + PM_CONTROL] != 0;
+  if (has_control) {
+    phase_stats(T, P, S, sortbuf, SP, trial, PM_CONTROL, T.phase_start_s[ms + PM_CONTROL], T.phase_end_s[ms + PM_CONTROL], P.trim_s, false, false);
+  } else if (threadIdx.x == 0) {
+    for (int f = 0; f < PM_PO_COUNT; ++f) S.po[PM_CONTROL][f] = dnan();
+    S.pf[PM_CONTROL] = 1u << PM_PF_MISSING;
+  }
+  __syncthreads();
+  const double* pre = S.po[PM_IDLE_PRE];
+  const double* post = S.po[PM_IDLE_POST];
+  const double* mea = S.po[PM_MEASURE];
+  const double* ref = S.po[PM_REFERENCE];
+  const uint32_t mf = S.pf[PM_MEASURE];
+
+  // ---- per-sample baseline and paired state scans (all threads) -------------
+  // analyze_trial:780-805: each idle phase's selected samples vs the active median.
+  const bool base_sm = ((mf | S.pf[PM_IDLE_PRE] | S.pf[PM_IDLE_POST]) >> PM_PF_ANY_SM_FINITE) & 1u;
+  const int clock_cols[3] = {C_GFX, C_MEM, C_SM};
+  const int med_slot[3] = {PM_PO_GFX_MED, PM_PO_MEM_MED, PM_PO_SM_MED};
+  bool scan_idle_clock[2] = {false, false}, scan_idle_temp[2] = {false, false};
+  for (int side = 0; side < 2; ++side) {
+    const int ph = side ? PM_IDLE_POST : PM_IDLE_PRE;
+    for (int k = 0; k < (base_sm ? 3 : 2); ++k) {
+      const double active = mea[med_slot[k]];
+      if (!none(active) && active > 0 && any_outside(T, S, trial, ph, clock_cols[k], active, P.clock_tolerance_fraction, true))
+        scan_idle_clock[side] = true;
+    }
+    const double at = mea[PM_PO_TEMP_MED];
+    if (!none(at) && any_outside(T, S, trial, ph, C_TEMP, at, P.max_temperature_drift_c, false)) scan_idle_temp[side] = true;
+  }
+  // _paired_reference_contrast:335-342: reference selected samples vs the treatment median.
+  const bool paired_sm = ((mf | S.pf[PM_REFERENCE]) >> PM_PF_ANY_SM_FINITE) & 1u;
+  bool scan_ref[4] = {false, false, false, false};
+  if (has_ref) {
+    for (int k = 0; k < (paired_sm ? 3 : 2); ++k) {
+      const double active = mea[med_slot[k]];
+      const double tol = (none(active) ? 0.0 : active) * P.clock_tolerance_fraction;
+      scan_ref[k] = any_outside(T, S, trial, PM_REFERENCE, clock_cols[k], none(active) ? 0.0 : active, tol, false);
+    }
+    const double at = mea[PM_PO_TEMP_MED];
+    scan_ref[3] = any_outside(T, S, trial, PM_REFERENCE, C_TEMP, none(at) ? 0.0 : at, P.max_temperature_drift_c, false);
+  }
+
+  if (threadIdx.x != 0) return;
+  // ---- trial scalars and gates (thread 0) ----------------------------------
+  double* to = R.trial_out + (size_t)trial * PM_TO_COUNT;
+  for (int f = 0; f < PM_TO_COUNT; ++f) to[f] = dnan();
+  uint64_t iss = 0, base = 0, pair = 0, warn = 0;
+  auto phase_issue_bits = [&](uint32_t f) -> uint64_t {
+    uint64_t b = 0;
+    if (f & (1u << PM_PF_MISSING)) b |= 1ull << 0;
+    if (f & (1u << PM_PF_INVALID_WINDOW)) b |= 1ull << 1;
+    if (f & (1u << PM_PF_SHORT_PLATEAU)) b |= 1ull << 2;
+    if (f & (1u << PM_PF_TOO_FEW_SAMPLES)) b |= 1ull << 3;
+    if (f & (1u << PM_PF_TELEMETRY_GAP)) b |= 1ull << 4;
+    if (f & (1u << PM_PF_NEGATIVE_POWER)) b |= 1ull << 5;
+    if (f & (1u << PM_PF_MISSING_POWER_COVERAGE)) b |= 1ull << 6;
+    if (f & (1u << PM_PF_COUNTER_DISAGREEMENT)) b |= 1ull << 7;
+    return b;
+  };
+  iss |= phase_issue_bits(mf) << PM_IT_M_MISSING_PHASE;
+  if (S.ep[0].issue >= 0) iss |= 1ull << (PM_IT_EP_PHASE_WINDOW + S.ep[0].issue);
+  base |= phase_issue_bits(S.pf[PM_IDLE_PRE]) << PM_IB_PRE_MISSING_PHASE;
+  base |= phase_issue_bits(S.pf[PM_IDLE_POST]) << PM_IB_POST_MISSING_PHASE;
+  if (S.pf[PM_IDLE_PRE] & (1u << PM_PF_COUNTER_RESET)) warn |= 1ull << PM_W_COUNTER_RESET_PRE;
+  if (mf & (1u << PM_PF_COUNTER_RESET)) warn |= 1ull << PM_W_COUNTER_RESET_MEASURE;
+  if (S.pf[PM_IDLE_POST] & (1u << PM_PF_COUNTER_RESET)) warn |= 1ull << PM_W_COUNTER_RESET_POST;
+  if (has_control && (S.pf[PM_CONTROL] & (1u << PM_PF_COUNTER_RESET))) warn |= 1ull << PM_W_COUNTER_RESET_CONTROL;
+
+  // Requested vs achieved clocks (analysis.py:631-646).
+  const bool treat_sm = (mf >> PM_PF_ANY_SM_FINITE) & 1u;
+  const double req[3] = {ts[PM_TS_REQ_GRAPHICS_MHZ], ts[PM_TS_REQ_MEMORY_MHZ], ts[PM_TS_REQ_SM_MHZ]};
+  const int min_slot[3] = {PM_PO_GFX_MIN, PM_PO_MEM_MIN, PM_PO_SM_MIN};
+  const int max_slot[3] = {PM_PO_GFX_MAX, PM_PO_MEM_MAX, PM_PO_SM_MAX};
+  const int nonpos_flag[3] = {PM_PF_GFX_NONPOS, PM_PF_MEM_NONPOS, PM_PF_SM_NONPOS};
+  for (int k = 0; k < (treat_sm ? 3 : 2); ++k) {
+    const double actual = mea[med_slot[k]];
+    if (!none(req[k]) && req[k] > 0) {
+      if (none(actual)) iss |= 1ull << (PM_IT_MISSING_CLOCK_GFX + k);
+      else if (fabs(actual - req[k]) / req[k] > P.clock_tolerance_fraction) iss |= 1ull << (PM_IT_CLOCK_MISMATCH_GFX + k);
+    } else if (k != 2) {
+      warn |= 1ull << (PM_W_UNCONTROLLED_GFX + k);
+    }
+    const double low = mea[min_slot[k]], high = mea[max_slot[k]];
+    if (truthy(actual) && !none(low) && !none(high) && (high - low) / actual > P.max_clock_drift_fraction)
+      iss |= 1ull << (PM_IT_CLOCK_DRIFT_GFX + k);
+  }
+  {
+    const double lo_t = mea[PM_PO_TEMP_MIN], hi_t = mea[PM_PO_TEMP_MAX];
+    if (!none(lo_t) && !none(hi_t) && hi_t - lo_t > P.max_temperature_drift_c) iss |= 1ull << PM_IT_TEMPERATURE_DRIFT;
+  }
+  const bool sel_any = truthy(mea[PM_PO_SAMPLES]);
+  if (sel_any && (mf & (1u << PM_PF_TEMP_MISSING))) iss |= 1ull << PM_IT_MISSING_TEMPERATURE;
+  for (int k = 0; k < (treat_sm ? 3 : 2); ++k)
+    if (sel_any && (mf & (1u << nonpos_flag[k]))) iss |= 1ull << (PM_IT_MISSING_CLOCK_GFX + k);
+  if (sel_any && (mf & (1u << PM_PF_THROTTLE_MISSING))) iss |= 1ull << PM_IT_MISSING_THROTTLING;
+  const double thr = none(mea[PM_PO_THROTTLE_OR]) ? 0.0 : mea[PM_PO_THROTTLE_OR];
+  if (thr != 0.0) iss |= 1ull << PM_IT_ACTIVE_THROTTLING;
+  // Process inventory: measure -> issues, other phases (idle, control) -> baseline.
+  if (mf & (1u << PM_PF_NO_COMPUTE_INV)) iss |= 1ull << PM_IT_MISSING_INV_COMPUTE;
+  if (mf & (1u << PM_PF_NO_GRAPHICS_INV)) iss |= 1ull << PM_IT_MISSING_INV_GRAPHICS;
+  if (mf & (1u << PM_PF_PID_UNKNOWN)) iss |= 1ull << PM_IT_MISSING_MEASUREMENT_PID;
+  if (mf & (1u << PM_PF_FOREIGN_PID)) iss |= 1ull << PM_IT_OTHER_GPU_PROCESSES;
+  if (mf & (1u << PM_PF_MPS)) iss |= 1ull << PM_IT_MPS_ACTIVE;
+  {
+    uint32_t of = S.pf[PM_IDLE_PRE] | S.pf[PM_IDLE_POST] | (has_control ? S.pf[PM_CONTROL] : 0u);
+    if (of & (1u << PM_PF_NO_COMPUTE_INV)) base |= 1ull << PM_IB_B_MISSING_INV_COMPUTE;
+    if (of & (1u << PM_PF_NO_GRAPHICS_INV)) base |= 1ull << PM_IB_B_MISSING_INV_GRAPHICS;
+    if (of & (1u << PM_PF_PID_UNKNOWN)) base |= 1ull << PM_IB_B_MISSING_MEASUREMENT_PID;
+    if (of & (1u << PM_PF_FOREIGN_PID)) base |= 1ull << PM_IB_B_OTHER_GPU_PROCESSES;
+    if (of & (1u << PM_PF_MPS)) base |= 1ull << PM_IB_B_MPS_ACTIVE;
+  }
+  // Idle delta (analysis.py:713-727).
+  const double idle_power = idle_at(pre, post, mea, PM_PO_POWER_W);
+  const double idle_memory_power = idle_at(pre, post, mea, PM_PO_MEMORY_POWER_W);
+  {
+    const double a = pre[PM_PO_POWER_W], b = post[PM_PO_POWER_W];
+    if (!none(a) && !none(b)) {
+      const double den = fmax((a + b) / 2, 1e-9);
+      if (fabs(a - b) / den > P.max_idle_drift_fraction) base |= 1ull << PM_IB_IDLE_DRIFT;
+    }
+  }
+  const double duration = mea[PM_PO_DURATION_S];
+  double total = mea[PM_PO_COUNTER_J];
+  bool trapezoid = false;
+  if (none(total)) { total = mea[PM_PO_ENERGY_J]; trapezoid = true; }
+  const double board_power = (!none(total) && truthy(duration) && duration > 0) ? total / duration : dnan();
+  const double idle_energy = (!none(idle_power) && truthy(duration)) ? idle_power * duration : dnan();
+  const double incremental = (!none(total) && !none(idle_energy)) ? total - idle_energy : dnan();
+  if (none(idle_power)) base |= 1ull << PM_IB_MISSING_IDLE;
+  if (!none(incremental) && incremental < 0) base |= 1ull << PM_IB_NEGATIVE_INCREMENTAL;
+  const double device_duration = ts[PM_TS_BENCH_DURATION_S];
+  const double host_duration = ts[PM_TS_BENCH_HOST_DURATION_S];
+  const double measured_duration = truthy(host_duration) ? host_duration : device_duration;
+  if (truthy(device_duration) && truthy(measured_duration) && fabs(device_duration - measured_duration) / measured_duration > 0.05)
+    iss |= 1ull << PM_IT_DURATION_DISAGREEMENT;
+  const double operations = ts[PM_TS_BENCH_OPERATIONS], logical_bytes = ts[PM_TS_BENCH_LOGICAL_BYTES];
+  const bool md_ok = truthy(measured_duration) && measured_duration > 0;
+  double ops_rate = (!none(operations) && md_ok) ? operations / measured_duration : dnan();
+  double byte_rate = (!none(logical_bytes) && md_ok) ? logical_bytes / measured_duration : dnan();
+  const EpochResult& E = S.ep[0];
+  const bool have_epochs = E.n_inner > 0 && E.issue < 0;
+  const bool exact = have_epochs && E.exact;
+  const double counted_ops = have_epochs ? E.ops : dnan();
+  const double counted_bytes = have_epochs ? E.bytes : dnan();
+  if (have_epochs && truthy(duration) && duration > 0) { ops_rate = counted_ops / duration; byte_rate = counted_bytes / duration; }
+  if (!exact) warn |= 1ull << PM_W_ALIGNMENT_UNVERIFIED;
+  if (none(measured_duration) || measured_duration <= 0) iss |= 1ull << PM_IT_MISSING_BENCH_DURATION;
+  if (tensor && (none(ops_rate) || ops_rate <= 0)) iss |= 1ull << PM_IT_MISSING_OPERATION_COUNT;
+  if (memory && (none(byte_rate) || byte_rate <= 0)) iss |= 1ull << PM_IT_MISSING_LOGICAL_BYTE_COUNT;
+  if (nonlinear && !exact) iss |= 1ull << PM_IT_NONLINEAR_EPOCHS;
+  if (sfu && !exact) iss |= 1ull << PM_IT_SFU_EPOCHS;
+  const double incremental_power = (!none(incremental) && truthy(duration)) ? incremental / duration : dnan();
+  const double rail_energy = mea[PM_PO_MEMORY_ENERGY_J];
+  double rail_incremental = (!none(rail_energy) && !none(idle_memory_power) && truthy(duration))
+                                ? rail_energy - idle_memory_power * duration : dnan();
+  {
+    unsigned srcs = (unsigned)(none(pre[PM_PO_MEM_SOURCES]) ? 0 : pre[PM_PO_MEM_SOURCES]) |
+                    (unsigned)(none(mea[PM_PO_MEM_SOURCES]) ? 0 : mea[PM_PO_MEM_SOURCES]) |
+                    (unsigned)(none(post[PM_PO_MEM_SOURCES]) ? 0 : post[PM_PO_MEM_SOURCES]) |
+                    (has_control && !none(S.po[PM_CONTROL][PM_PO_MEM_SOURCES]) ? (unsigned)S.po[PM_CONTROL][PM_PO_MEM_SOURCES] : 0u);
+    if (__popc(srcs) > 1) { warn |= 1ull << PM_W_RAIL_SOURCE_CHANGED; rail_incremental = dnan(); }
+  }
+  // power_limit = median(selected) or record-level fallback (analysis.py:781-783)
+  double power_limit = mea[PM_PO_PLIMIT_MED];
+  if (!truthy(power_limit)) power_limit = ts[PM_TS_POWER_LIMIT_FALLBACK_W];
+  double tensor_peak = dnan();
+  const bool peak_sm = truthy(mea[PM_PO_SM_MED]) && mea[PM_PO_SM_MED] > 0;
+  const double peak_clock = peak_sm ? mea[PM_PO_SM_MED] : mea[PM_PO_GFX_MED];
+  if (tensor && !none(peak_clock) && peak_clock > 0) {
+    if (tflags & PM_T_TENSOR_PEAK_KNOWN) {
+      tensor_peak = ts[PM_TS_TENSOR_FLOPS_PER_CLOCK] * peak_clock * 1e6 / 1e12;
+      if (!peak_sm) warn |= 1ull << PM_W_PEAK_GRAPHICS_PROXY;
+    } else {
+      warn |= 1ull << PM_W_PEAK_UNAVAILABLE;
+    }
+  }
+  // Baseline state matching (analysis.py:801-835).
+  bool clock_matched = true, temp_matched = true, cap_matched = true;
+  bool enf_compared = false, pst_compared = false, state_mismatch = false;
+  const double* idles[2] = {pre, post};
+  const int base_ph[2] = {PM_IDLE_PRE, PM_IDLE_POST};
+  for (int side = 0; side < 2; ++side) {
+    const double* bp = idles[side];
+    const int dbase = side ? PM_TO_DPOST_GFX : PM_TO_DPRE_GFX;
+    for (int k = 0; k < (base_sm ? 3 : 2); ++k) {
+      const double ac = mea[med_slot[k]], ic = bp[med_slot[k]];
+      to[dbase + k] = (!none(ac) && !none(ic)) ? ac - ic : dnan();
+      if (none(ac) || none(ic) || ac <= 0 || fabs(ac - ic) / ac > P.clock_tolerance_fraction) clock_matched = false;
+    }
+    if (scan_idle_clock[side]) clock_matched = false;
+    const double at = mea[PM_PO_TEMP_MED], it = bp[PM_PO_TEMP_MED];
+    to[dbase + 3] = (!none(at) && !none(it)) ? at - it : dnan();
+    if (none(at) || none(it) || fabs(at - it) > P.max_temperature_drift_c) temp_matched = false;
+    if (scan_idle_temp[side]) temp_matched = false;
+    // caps: set equality of _finite(power_limit_w) over selected samples
+    {
+      const bool a_single = mea[PM_PO_PLIMIT_NONE] == 0 && mea[PM_PO_PLIMIT_FIN] > 0 && mea[PM_PO_PLIMIT_MIN] == mea[PM_PO_PLIMIT_MAX];
+      const bool b_single = bp[PM_PO_PLIMIT_NONE] == 0 && bp[PM_PO_PLIMIT_FIN] > 0 && bp[PM_PO_PLIMIT_MIN] == bp[PM_PO_PLIMIT_MAX];
+      const bool a_has_none = !(mea[PM_PO_PLIMIT_NONE] == 0) ;
+      const bool b_has_none = !(bp[PM_PO_PLIMIT_NONE] == 0);
+      if (a_has_none || b_has_none || !a_single || !b_single || mea[PM_PO_PLIMIT_MIN] != bp[PM_PO_PLIMIT_MIN]) cap_matched = false;
+    }
+    const int fields[2][5] = {{PM_PO_ENF_NONE, PM_PO_ENF_FIN, PM_PO_ENF_MIN, PM_PO_ENF_MAX, PM_PO_ENF_MED},
+                              {PM_PO_PSTATE_NONE, PM_PO_PSTATE_FIN, PM_PO_PSTATE_MIN, PM_PO_PSTATE_MAX, PM_PO_PSTATE_MED}};
+    for (int g = 0; g < 2; ++g) {
+      const int* F = fields[g];
+      const double an = none(mea[F[0]]) ? 0 : mea[F[0]], af = none(mea[F[1]]) ? 0 : mea[F[1]];
+      const double bn = none(bp[F[0]]) ? 0 : bp[F[0]], bf = none(bp[F[1]]) ? 0 : bp[F[1]];
+      if (af + bf > 0) {
+        if (g == 0) enf_compared = true; else pst_compared = true;
+        const double amed = truthy(mea[F[4]]) ? mea[F[4]] : 0.0, bmed = truthy(bp[F[4]]) ? bp[F[4]] : 0.0;
+        to[dbase + 4 + g] = (an == 0 && bn == 0) ? amed - bmed : dnan();
+        const bool a_single = an == 0 && af > 0 && mea[F[2]] == mea[F[3]];
+        const bool b_single = bn == 0 && bf > 0 && bp[F[2]] == bp[F[3]];
+        if (an > 0 || bn > 0 || !a_single || !b_single || mea[F[2]] != bp[F[2]]) {
+          base |= 1ull << (side ? (g ? PM_IB_STATE_POST_PSTATE : PM_IB_STATE_POST_ENF) : (g ? PM_IB_STATE_PRE_PSTATE : PM_IB_STATE_PRE_ENF));
+          state_mismatch = true;
+        }
+      }
+    }
+    (void)base_ph;
+  }
+  if (state_mismatch) warn |= 1ull << PM_W_STATE_MISMATCH;
+  if (!cap_matched) warn |= 1ull << PM_W_CAP_MISMATCH;
+  if (!clock_matched) warn |= 1ull << PM_W_CLOCK_MISMATCH;
+  if (!temp_matched) warn |= 1ull << PM_W_TEMP_MISMATCH;
+
+  const bool host_issues = tflags & PM_T_HOST_ISSUES;
+  const bool valid = !host_issues && iss == 0;
+  const bool baseline_valid = !(tflags & PM_T_HOST_BASELINE) && base == 0;
+  const bool idle_inc_eligible = valid && baseline_valid && exact && clock_matched && temp_matched && cap_matched;
+
+  to[PM_TO_DURATION_S] = duration;
+  to[PM_TO_BENCH_MEASURED_DURATION_S] = measured_duration;
+  to[PM_TO_BENCH_DEVICE_DURATION_S] = device_duration;
+  to[PM_TO_IDLE_POWER_W] = idle_power; to[PM_TO_IDLE_MEMORY_POWER_W] = idle_memory_power;
+  to[PM_TO_TOTAL_ENERGY_J] = total; to[PM_TO_ENERGY_SOURCE_TRAPEZOID] = trapezoid ? 1 : 0;
+  to[PM_TO_BOARD_POWER_W] = board_power; to[PM_TO_IDLE_ENERGY_J] = idle_energy;
+  to[PM_TO_INCREMENTAL_ENERGY_J] = incremental; to[PM_TO_INCREMENTAL_POWER_W] = incremental_power;
+  to[PM_TO_OPS_RATE] = ops_rate; to[PM_TO_BYTE_RATE] = byte_rate;
+  to[PM_TO_DEVICE_OPS_RATE] = (!none(operations) && truthy(device_duration) && device_duration > 0) ? operations / device_duration : dnan();
+  to[PM_TO_DEVICE_BYTE_RATE] = (!none(logical_bytes) && truthy(device_duration) && device_duration > 0) ? logical_bytes / device_duration : dnan();
+  to[PM_TO_COUNTED_OPS] = counted_ops; to[PM_TO_COUNTED_BYTES] = counted_bytes;
+  to[PM_TO_EPOCHS] = have_epochs ? E.n_inner : 0; to[PM_TO_EXACT] = exact;
+  to[PM_TO_RAIL_ENERGY_J] = rail_energy; to[PM_TO_RAIL_INCREMENTAL_J] = rail_incremental;
+  to[PM_TO_RAIL_INCREMENTAL_W] = (!none(rail_incremental) && truthy(duration)) ? rail_incremental / duration : dnan();
+  to[PM_TO_POWER_LIMIT_W] = power_limit;
+  to[PM_TO_TENSOR_PEAK_TFLOPS] = tensor_peak; to[PM_TO_PEAK_CLOCK_IS_SM] = peak_sm;
+  to[PM_TO_TENSOR_UTILIZATION] = (!none(ops_rate) && !none(tensor_peak) && tensor_peak > 0) ? ops_rate / 1e12 / tensor_peak : dnan();
+  to[PM_TO_IDLE_FRAC_MEASURED] = (!none(idle_power) && truthy(board_power) && board_power > 0) ? idle_power / board_power : dnan();
+  to[PM_TO_IDLE_FRAC_LIMIT] = (!none(idle_power) && truthy(power_limit) && power_limit > 0) ? idle_power / power_limit : dnan();
+  to[PM_TO_LIMIT_UTILIZATION] = (!none(board_power) && truthy(power_limit) && power_limit > 0) ? board_power / power_limit : dnan();
+  const bool ops_ok = truthy(ops_rate) && ops_rate > 0, bytes_ok = truthy(byte_rate) && byte_rate > 0;
+  to[PM_TO_PJ_PER_OP] = (!none(incremental_power) && ops_ok && energy_wl) ? incremental_power / ops_rate * 1e12 : dnan();
+  to[PM_TO_PJ_PER_LOGICAL_BYTE] = (!none(incremental_power) && bytes_ok) ? incremental_power / byte_rate * 1e12 : dnan();
+  to[PM_TO_TOTAL_PJ_PER_OP] = (!none(board_power) && ops_ok && energy_wl) ? board_power / ops_rate * 1e12 : dnan();
+  to[PM_TO_TOTAL_PJ_PER_LOGICAL_BYTE] = (!none(board_power) && bytes_ok) ? board_power / byte_rate * 1e12 : dnan();
+  to[PM_TO_TOTAL_PJ_PER_FLOP] = (tensor && !none(board_power) && ops_ok) ? board_power / ops_rate * 1e12 : dnan();
+  to[PM_TO_TOTAL_PJ_PER_BIT] = (memory && !none(board_power) && bytes_ok) ? board_power / byte_rate / 8 * 1e12 : dnan();
+  to[PM_TO_INC_PJ_PER_FLOP] = (tensor && !none(incremental_power) && ops_ok) ? incremental_power / ops_rate * 1e12 : dnan();
+  to[PM_TO_INC_PJ_PER_BIT] = (memory && !none(incremental_power) && bytes_ok) ? incremental_power / byte_rate / 8 * 1e12 : dnan();
+  to[PM_TO_BASE_CLOCK_MATCHED] = clock_matched; to[PM_TO_BASE_TEMP_MATCHED] = temp_matched;
+  to[PM_TO_BASE_CAP_MATCHED] = cap_matched; to[PM_TO_BASE_STATE_MATCHED] = !state_mismatch;
+  to[PM_TO_BASE_SM_COMPARED] = base_sm; to[PM_TO_BASE_ENF_COMPARED] = enf_compared; to[PM_TO_BASE_PSTATE_COMPARED] = pst_compared;
+  to[PM_TO_THROTTLE_MASK] = thr;
+  to[PM_TO_VALID] = valid; to[PM_TO_BASELINE_VALID] = baseline_valid; to[PM_TO_IDLE_INC_ELIGIBLE] = idle_inc_eligible;
+  if (has_control) {
+    const double* ctl = S.po[PM_CONTROL];
+    const double cidle = idle_at(pre, post, ctl, PM_PO_POWER_W), cp = ctl[PM_PO_POWER_W];
+    to[PM_TO_CONTROL_INC_POWER_W] = (!none(cp) && !none(cidle)) ? cp - cidle : dnan();
+  }
+
+  // ---- paired active reference (analysis.py:292-423) -----------------------
+  double contrast = dnan();
+  bool paired_eligible = false;
+  double ref_slots = dnan();
+  if (!has_ref) {
+    pair |= 1ull << PM_IP_MISSING_REFERENCE_PHASE;
+  } else {
+    const uint32_t rf = S.pf[PM_REFERENCE];
+    pair |= phase_issue_bits(rf) << PM_IP_R_MISSING_PHASE;
+    const EpochResult& RE = S.ep[1];
+    if (RE.issue >= 0) pair |= 1ull << (PM_IP_REP_PHASE_WINDOW + RE.issue);
+    const bool ref_have = RE.n_inner > 0 && RE.issue < 0;
+    if (!ref_have || !RE.exact) pair |= 1ull << PM_IP_REF_WINDOW_UNVERIFIED;
+    const int nsel_ref = none(ref[PM_PO_SAMPLES]) ? 0 : (int)ref[PM_PO_SAMPLES];
+    for (int k = 0; k < (paired_sm ? 3 : 2); ++k) {
+      const double active = mea[med_slot[k]], baseline = ref[med_slot[k]];
+      to[PM_TO_PAIRED_D_GFX + k] = (!none(active) && !none(baseline)) ? active - baseline : dnan();
+      if (none(active) || none(baseline) || nsel_ref == 0 || scan_ref[k]) pair |= 1ull << (PM_IP_STATE_GFX + k);
+    }
+    {
+      const double active = mea[PM_PO_TEMP_MED], baseline = ref[PM_PO_TEMP_MED];
+      to[PM_TO_PAIRED_D_TEMP] = (!none(active) && !none(baseline)) ? active - baseline : dnan();
+      if (none(active) || none(baseline) || nsel_ref == 0 || scan_ref[3]) pair |= 1ull << PM_IP_STATE_TEMP;
+    }
+    to[PM_TO_PAIRED_SM_COMPARED] = paired_sm;
+    if (rf & ((1u << PM_PF_THROTTLE_MISSING) | (1u << PM_PF_THROTTLE_ACTIVE))) pair |= 1ull << PM_IP_REF_THROTTLE;
+    if (rf & (1u << PM_PF_NO_COMPUTE_INV)) pair |= 1ull << PM_IP_REF_INV_COMPUTE;
+    if (rf & (1u << PM_PF_NO_GRAPHICS_INV)) pair |= 1ull << PM_IP_REF_INV_GRAPHICS;
+    if (rf & (1u << PM_PF_REF_FOREIGN)) pair |= 1ull << PM_IP_REF_FOREIGN;
+    // caps over treatment + reference selected samples
+    {
+      const double n_none = (none(mea[PM_PO_PLIMIT_NONE]) ? 0 : mea[PM_PO_PLIMIT_NONE]) + (none(ref[PM_PO_PLIMIT_NONE]) ? 0 : ref[PM_PO_PLIMIT_NONE]);
+      const double n_fin = (none(mea[PM_PO_PLIMIT_FIN]) ? 0 : mea[PM_PO_PLIMIT_FIN]) + (none(ref[PM_PO_PLIMIT_FIN]) ? 0 : ref[PM_PO_PLIMIT_FIN]);
+      const double mn = fmin(none(mea[PM_PO_PLIMIT_MIN]) ? dinf() : mea[PM_PO_PLIMIT_MIN], none(ref[PM_PO_PLIMIT_MIN]) ? dinf() : ref[PM_PO_PLIMIT_MIN]);
+      const double mx = fmax(none(mea[PM_PO_PLIMIT_MAX]) ? -dinf() : mea[PM_PO_PLIMIT_MAX], none(ref[PM_PO_PLIMIT_MAX]) ? -dinf() : ref[PM_PO_PLIMIT_MAX]);
+      if (n_none + n_fin == 0 || n_none > 0 || mn <= 0) pair |= 1ull << PM_IP_CAP_UNVERIFIED;
+      else if (mx - mn > 1e-6) pair |= 1ull << PM_IP_CAP_CHANGED;
+    }
+    const int fields[2][4] = {{PM_PO_ENF_NONE, PM_PO_ENF_FIN, PM_PO_ENF_MIN, PM_PO_ENF_MAX},
+                              {PM_PO_PSTATE_NONE, PM_PO_PSTATE_FIN, PM_PO_PSTATE_MIN, PM_PO_PSTATE_MAX}};
+    for (int g = 0; g < 2; ++g) {
+      const int* F = fields[g];
+      const double an = none(mea[F[0]]) ? 0 : mea[F[0]], af = none(mea[F[1]]) ? 0 : mea[F[1]];
+      const double bn = none(ref[F[0]]) ? 0 : ref[F[0]], bf = none(ref[F[1]]) ? 0 : ref[F[1]];
+      const bool a_only_none = an > 0 && af == 0, b_only_none = bn > 0 && bf == 0;
+      if (!a_only_none || !b_only_none) {
+        const bool a_single = an == 0 && af > 0 && mea[F[2]] == mea[F[3]];
+        const bool b_single = bn == 0 && bf > 0 && ref[F[2]] == ref[F[3]];
+        if (an > 0 || bn > 0 || !a_single || !b_single || mea[F[2]] != ref[F[2]]) pair |= 1ull << (g ? PM_IP_STATE_PSTATE : PM_IP_STATE_ENF);
+      }
+    }
+    const double reference_power = ref[PM_PO_POWER_W];
+    contrast = (!none(board_power) && !none(reference_power)) ? board_power - reference_power : dnan();
+    if (none(contrast)) pair |= 1ull << PM_IP_POWER_UNAVAILABLE;
+    else if (contrast <= 0 && !sfu) pair |= 1ull << PM_IP_NONPOSITIVE_CONTRAST;
+    paired_eligible = valid && exact && pair == 0 && !(tflags & PM_T_HOST_PAIRED);
+    to[PM_TO_PAIRED_POWER_W] = contrast;
+    to[PM_TO_PAIRED_ENERGY_J] = (!none(contrast) && truthy(duration)) ? contrast * duration : dnan();
+    to[PM_TO_REF_POWER_W] = reference_power;
+    to[PM_TO_REF_DURATION_S] = ref[PM_PO_DURATION_S];
+    to[PM_TO_REF_TOTAL_ENERGY_J] = !none(ref[PM_PO_COUNTER_J]) ? ref[PM_PO_COUNTER_J] : ref[PM_PO_ENERGY_J];
+    to[PM_TO_REF_EPOCHS] = ref_have ? RE.n_inner : 0; to[PM_TO_REF_EXACT] = ref_have && RE.exact;
+    if (sfu) {
+      ref_slots = ref_have ? RE.slots : dnan();
+      to[PM_TO_REF_SLOTS] = ref_slots;
+      to[PM_TO_REF_SLOTS_RATE] = (!none(ref_slots) && truthy(ref[PM_PO_DURATION_S])) ? ref_slots / ref[PM_PO_DURATION_S] : dnan();
+    }
+    to[PM_TO_PAIRED_PJ_PER_FLOP] = (tensor && !none(contrast) && ops_ok) ? contrast / ops_rate * 1e12 : dnan();
+    to[PM_TO_PAIRED_PJ_PER_BIT] = (memory && !none(contrast) && bytes_ok) ? contrast / byte_rate / 8 * 1e12 : dnan();
+    const double t_idle = idle_at(pre, post, mea, PM_PO_POWER_W), r_idle = idle_at(pre, post, ref, PM_PO_POWER_W);
+    to[PM_TO_PAIRED_DRIFT_ADJUSTED_W] = (idle_inc_eligible && !none(board_power) && !none(t_idle) && !none(reference_power) && !none(r_idle))
+        ? (board_power - t_idle) - (reference_power - r_idle) : dnan();
+  }
+  to[PM_TO_PAIRED_ELIGIBLE] = paired_eligible;
+
+  // ---- SFU and nonlinear normalisation (analysis.py:999-1040) --------------
+  double sfu_rate = dnan();
+  if (sfu) {
+    sfu_rate = ((tflags & PM_T_SFU_CONTRACT_OK) && exact && ops_ok) ? ops_rate : dnan();
+    to[PM_TO_SFU_RATE] = sfu_rate;
+    to[PM_TO_SFU_COUNTED] = !none(sfu_rate) ? counted_ops : dnan();
+    to[PM_TO_SFU_TOTAL_PJ] = (!none(board_power) && truthy(sfu_rate)) ? board_power / sfu_rate * 1e12 : dnan();
+    to[PM_TO_SFU_INC_PJ] = (!none(incremental_power) && truthy(sfu_rate)) ? incremental_power / sfu_rate * 1e12 : dnan();
+    to[PM_TO_SFU_PAIRED_PJ] = (!none(contrast) && truthy(sfu_rate)) ? contrast / sfu_rate * 1e12 : dnan();
+    to[PM_TO_PJ_PER_OP] = dnan(); to[PM_TO_TOTAL_PJ_PER_OP] = dnan();
+  }
+  const double element_rate = (nonlinear && (tflags & PM_T_NONLINEAR_OK) && exact && ops_ok) ? ops_rate : dnan();
+  const double width = (tflags & PM_T_ROWWISE) ? ts[PM_TS_ROW_WIDTH] : dnan();
+  const double row_rate = (truthy(element_rate) && truthy(width)) ? element_rate / width : dnan();
+  to[PM_TO_ELEMENT_RATE] = element_rate; to[PM_TO_ROW_RATE] = row_rate;
+  to[PM_TO_COUNTED_ELEMENTS] = truthy(element_rate) ? counted_ops : dnan();
+  if (nonlinear && none(element_rate)) { to[PM_TO_PJ_PER_OP] = dnan(); to[PM_TO_TOTAL_PJ_PER_OP] = dnan(); }
+  {
+    const double powers[3] = {board_power, incremental_power, contrast};
+    for (int k = 0; k < 3; ++k) {
+      to[PM_TO_PJ_ELEMENT_TOTAL + k] = (!none(powers[k]) && truthy(element_rate)) ? powers[k] / element_rate * 1e12 : dnan();
+      to[PM_TO_PJ_ROW_TOTAL + k] = (!none(powers[k]) && truthy(row_rate)) ? powers[k] / row_rate * 1e12 : dnan();
+    }
+  }
+
+  // ---- outputs ----------------------------------------------------------------
+  uint64_t* ib = R.issue_bits + (size_t)trial * PM_ISSUE_WORDS;
+  ib[0] = iss; ib[1] = base; ib[2] = pair; ib[3] = warn;
+  R.valid[trial] = valid;
+  for (int p = 0; p < PM_PHASES; ++p) {
+    double* dst = R.phase_out + ((size_t)trial * PM_PHASES + p) * PM_PO_COUNT;
+    for (int f = 0; f < PM_PO_COUNT; ++f) dst[f] = S.po[p][f];
+    R.phase_flags[trial * PM_PHASES + p] = S.pf[p];
+  }
+  double* m = R.metrics + (size_t)trial * PM_N_METRICS;
+  for (int k = 0; k < PM_N_METRICS; ++k) m[k] = dnan();
+  m[PM_M_board_power_w] = board_power;
+  m[PM_M_idle_power_w] = idle_power;
+  m[PM_M_incremental_power_w] = incremental_power;
+  m[PM_M_throughput_ops_s] = ops_rate;
+  m[PM_M_throughput_bytes_s] = byte_rate;
+  m[PM_M_pj_per_op] = to[PM_TO_PJ_PER_OP];
+  m[PM_M_pj_per_logical_byte] = to[PM_TO_PJ_PER_LOGICAL_BYTE];
+  m[PM_M_total_pj_per_op] = to[PM_TO_TOTAL_PJ_PER_OP];
+  m[PM_M_total_pj_per_logical_byte] = to[PM_TO_TOTAL_PJ_PER_LOGICAL_BYTE];
+  m[PM_M_memory_rail_power_w] = mea[PM_PO_MEMORY_POWER_W];
+  m[PM_M_memory_rail_incremental_power_w] = to[PM_TO_RAIL_INCREMENTAL_W];
+  m[PM_M_graphics_clock_mhz] = mea[PM_PO_GFX_MED];
+  m[PM_M_sm_clock_mhz] = mea[PM_PO_SM_MED];
+  m[PM_M_memory_clock_mhz] = mea[PM_PO_MEM_MED];
+  m[PM_M_temperature_c] = mea[PM_PO_TEMP_MED];
+  m[PM_M_idle_fraction_of_measured_power] = to[PM_TO_IDLE_FRAC_MEASURED];
+  m[PM_M_idle_fraction_of_power_limit] = to[PM_TO_IDLE_FRAC_LIMIT];
+  m[PM_M_power_limit_utilization] = to[PM_TO_LIMIT_UTILIZATION];
+  m[PM_M_tensor_peak_tflops_at_achieved_clock] = tensor_peak;
+  m[PM_M_tensor_utilization_vs_dense_clock_peak] = to[PM_TO_TENSOR_UTILIZATION];
+  m[PM_M_total_pj_per_flop] = to[PM_TO_TOTAL_PJ_PER_FLOP];
+  m[PM_M_total_pj_per_logical_bit] = to[PM_TO_TOTAL_PJ_PER_BIT];
+  m[PM_M_operational_idle_increment_power_w] = incremental_power;
+  m[PM_M_operational_idle_increment_energy_j] = incremental;
+  m[PM_M_operational_idle_increment_pj_per_flop] = to[PM_TO_INC_PJ_PER_FLOP];
+  m[PM_M_operational_idle_increment_pj_per_logical_bit] = to[PM_TO_INC_PJ_PER_BIT];
+  m[PM_M_paired_active_reference_power_w] = to[PM_TO_PAIRED_POWER_W];
+  m[PM_M_paired_active_reference_energy_j] = to[PM_TO_PAIRED_ENERGY_J];
+  m[PM_M_paired_active_reference_pj_per_flop] = to[PM_TO_PAIRED_PJ_PER_FLOP];
+  m[PM_M_paired_active_reference_pj_per_logical_bit] = to[PM_TO_PAIRED_PJ_PER_BIT];
+  m[PM_M_throughput_elements_s] = element_rate;
+  m[PM_M_throughput_rows_s] = row_rate;
+  m[PM_M_total_pj_per_element] = to[PM_TO_PJ_ELEMENT_TOTAL];
+  m[PM_M_total_pj_per_row] = to[PM_TO_PJ_ROW_TOTAL];
+  m[PM_M_operational_idle_increment_pj_per_element] = to[PM_TO_PJ_ELEMENT_INC];
+  m[PM_M_operational_idle_increment_pj_per_row] = to[PM_TO_PJ_ROW_INC];
+  m[PM_M_paired_active_reference_pj_per_element] = to[PM_TO_PJ_ELEMENT_PAIRED];
+  m[PM_M_paired_active_reference_pj_per_row] = to[PM_TO_PJ_ROW_PAIRED];
+  if (sfu) {
+    m[PM_M_throughput_sfu_instructions_s] = sfu_rate;
+    m[PM_M_total_pj_per_instruction] = to[PM_TO_SFU_TOTAL_PJ];
+    m[PM_M_operational_idle_increment_pj_per_instruction] = to[PM_TO_SFU_INC_PJ];
+    m[PM_M_paired_active_reference_pj_per_instruction] = to[PM_TO_SFU_PAIRED_PJ];
+    m[PM_M_sfu_reference_delta_pj_per_instruction] = to[PM_TO_SFU_PAIRED_PJ];
+    m[PM_M_sfu_reference_delta_power_w] = has_ref ? contrast : dnan();
+    m[PM_M_active_reference_counted_loop_slots] = to[PM_TO_REF_SLOTS];
+    m[PM_M_active_reference_loop_slots_s] = to[PM_TO_REF_SLOTS_RATE];
+  }
+  m[PM_M_active_reference_duration_s] = has_ref ? ref[PM_PO_DURATION_S] : dnan();
+}
+
+}  // namespace pm
+
+// ---------------------------------------------------------------------------
+// Host launcher (called from capi.cu).
+namespace pm {
+int launch_analyze(const pm_trials& T, const pm_policy& P, const pm_trial_results& R, int max_covering,
+                   double* gscratch, cudaStream_t stream, size_t* scratch_bytes_needed) {
+  int SP = 32;
+  while (SP < max_covering + 1) SP <<= 1;
+  const size_t smem = (size_t)C_COUNT * SP * sizeof(double);
+  const bool use_global = smem > kSmemSortBytes;
+  if (scratch_bytes_needed) *scratch_bytes_needed = use_global ? (size_t)T.n_trials * smem : 0;
+  if (use_global && !gscratch) return 1;  // caller must supply scratch
+  if (T.n_trials == 0) return 0;
+  const size_t dyn = use_global ? 0 : smem;
+  if (dyn > 48 * 1024) cudaFuncSetAttribute(analyze_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)dyn);
+  analyze_kernel<<<T.n_trials, kThreads, dyn, stream>>>(T, P, R, SP, use_global ? gscratch : nullptr);
+  return 0;
+}
+}  // namespace pm

@@ -1,0 +1,497 @@
+// C ABI of libpmb200 (analysis half): argument checks, staging of host
+// buffers through pinned memory, grow-only device workspaces and kernel
+// launches.  Nothing here computes a result on the host; every number that
+// leaves these functions was produced by a kernel.
+#include <cuda_runtime.h>
+#include <cstdarg>
+#include <cstdio>
+#include <cstring>
+#include <mutex>
+#include <string>
+#include <type_traits>
+
+#include "pmb200.h"
+#include "pm_layout.h"
+#include "pm_capi.h"
+
+namespace pm {
+int launch_analyze(const pm_trials& T, const pm_policy& P, const pm_trial_results& R, int max_covering,
+                   double* gscratch, cudaStream_t stream, size_t* scratch_bytes_needed);
+int launch_bootstrap(const BootArgs& A, cudaStream_t stream);
+int launch_resample_indices(uint64_t seed, int n, int B, int32_t* out, cudaStream_t stream);
+int prepare_bootstrap_constants(int device);
+size_t bootstrap_scratch_bytes(int n_groups, int max_members, int resamples);
+
+static thread_local std::string t_error;
+
+int fail(int code, const char* fmt, ...) {
+  char buf[1024];
+  va_list ap; va_start(ap, fmt); vsnprintf(buf, sizeof buf, fmt, ap); va_end(ap);
+  t_error = buf;
+  return code;
+}
+int cuda_fail(cudaError_t e, const char* where) {
+  return fail(PM_E_CUDA, "%s: %s", where, cudaGetErrorString(e));
+}
+
+Arena g_arenas[kMaxDevices];
+
+int current_device(int* device) {
+  int n = 0;
+  cudaError_t e = cudaGetDeviceCount(&n);
+  if (e != cudaSuccess || n == 0) { cudaGetLastError(); return fail(PM_E_NODEVICE, "no CUDA device visible (%s)", cudaGetErrorString(e)); }
+  e = cudaGetDevice(device);
+  if (e != cudaSuccess) return cuda_fail(e, "cudaGetDevice");
+  if (*device < 0 || *device >= kMaxDevices) return fail(PM_E_LIMIT, "device ordinal %d beyond %d", *device, kMaxDevices);
+  return PM_OK;
+}
+
+int arena_reserve(Arena& a, size_t dev_bytes, size_t host_bytes) {
+  if (dev_bytes > a.dev_bytes) {
+    if (a.dev) cudaFree(a.dev);
+    a.dev = nullptr; a.dev_bytes = 0;
+    cudaError_t e = cudaMalloc(&a.dev, dev_bytes);
+    if (e != cudaSuccess) return cuda_fail(e, "cudaMalloc(workspace)");
+    a.dev_bytes = dev_bytes;
+  }
+  if (host_bytes > a.host_bytes) {
+    if (a.host) cudaFreeHost(a.host);
+    a.host = nullptr; a.host_bytes = 0;
+    cudaError_t e = cudaMallocHost(&a.host, host_bytes);
+    if (e != cudaSuccess) return cuda_fail(e, "cudaMallocHost(staging)");
+    a.host_bytes = host_bytes;
+  }
+  if (!a.stream) {
+    cudaError_t e = cudaStreamCreateWithFlags(&a.stream, cudaStreamNonBlocking);
+    if (e != cudaSuccess) return cuda_fail(e, "cudaStreamCreate");
+  }
+  return PM_OK;
+}
+
+namespace {
+
+// Visit every array of a pm_trials batch with its element count, in one
+// fixed order shared by the sizing and the staging passes.
+template <class T, class F> void visit_trials(T& t, F f) {
+  const size_t nt = (size_t)t.n_trials, ns = (size_t)t.n_samples, ne = (size_t)t.n_epochs;
+  f(t.phase_offsets, nt * PM_PHASES + 1);
+  f(t.phase_start_s, nt * PM_PHASES); f(t.phase_end_s, nt * PM_PHASES); f(t.phase_present, nt * PM_PHASES);
+  f(t.t_s, ns); f(t.power_w, ns); f(t.memory_power_w, ns);
+  f(t.graphics_clock_mhz, ns); f(t.sm_clock_mhz, ns); f(t.memory_clock_mhz, ns); f(t.temperature_c, ns);
+  f(t.power_limit_w, ns); f(t.enforced_power_limit_w, ns); f(t.pstate, ns);
+  f(t.energy_int, ns); f(t.energy_float, ns); f(t.throttle_reasons, ns); f(t.sample_flags, ns);
+  f(t.memory_power_source, ns);
+  f(t.epoch_offsets, nt * 2 + 1); f(t.epoch_status, nt * 2);
+  f(t.epoch_start_s, ne); f(t.epoch_end_s, ne); f(t.epoch_operations, ne); f(t.epoch_logical_bytes, ne);
+  f(t.epoch_loop_slots, ne); f(t.epoch_counts_exact, ne);
+  f(t.trial_scalars, nt * PM_TS_COUNT); f(t.trial_flags, nt);
+}
+
+constexpr size_t align256(size_t x) { return (x + 255) & ~size_t(255); }
+
+int check_trials_host(const pm_trials& T, int* max_covering) {
+  if (T.n_trials < 0 || T.n_samples < 0 || T.n_epochs < 0) return fail(PM_E_INVALID, "negative batch size");
+  bool null_seen = false;
+  visit_trials(T, [&](const auto* p, size_t n) { if (n && !p) null_seen = true; });
+  if (null_seen) return fail(PM_E_INVALID, "a pm_trials array is NULL");
+  if (T.phase_offsets[0] != 0 || T.phase_offsets[(size_t)T.n_trials * PM_PHASES] != T.n_samples)
+    return fail(PM_E_INVALID, "phase_offsets must start at 0 and end at n_samples");
+  int64_t mc = 0;
+  for (size_t s = 0; s < (size_t)T.n_trials * PM_PHASES; ++s) {
+    const int64_t b = T.phase_offsets[s], e = T.phase_offsets[s + 1];
+    if (e < b) return fail(PM_E_INVALID, "phase_offsets must be non-decreasing");
+    if (e - b > kMaxPhaseSamples) return fail(PM_E_LIMIT, "a phase holds %lld samples; the limit is %d", (long long)(e - b), kMaxPhaseSamples);
+    for (int64_t i = b + 1; i < e; ++i)
+      if (!(T.t_s[i] > T.t_s[i - 1])) return fail(PM_E_INVALID, "t_s must increase strictly within a phase (slot %zu)", s);
+    if (e - b > mc) mc = e - b;
+  }
+  if (T.epoch_offsets[0] != 0 || T.epoch_offsets[(size_t)T.n_trials * 2] != T.n_epochs)
+    return fail(PM_E_INVALID, "epoch_offsets must start at 0 and end at n_epochs");
+  for (size_t s = 0; s < (size_t)T.n_trials * 2; ++s) {
+    const int32_t n = T.epoch_offsets[s + 1] - T.epoch_offsets[s];
+    if (n < 0) return fail(PM_E_INVALID, "epoch_offsets must be non-decreasing");
+    if (n > kMaxEpochsPerArm) return fail(PM_E_LIMIT, "an arm lists %d epochs; the limit is %d", n, kMaxEpochsPerArm);
+  }
+  *max_covering = (int)mc;
+  return PM_OK;
+}
+
+template <class F> void visit_results(pm_trial_results& r, size_t n, F f) {
+  f(r.phase_out, n * PM_PHASES * PM_PO_COUNT); f(r.phase_flags, n * PM_PHASES); f(r.trial_out, n * PM_TO_COUNT);
+  f(r.issue_bits, n * PM_ISSUE_WORDS); f(r.metrics, n * PM_N_METRICS); f(r.valid, n);
+}
+
+// Lay out arrays back to back (256-byte aligned) starting at `base`.
+struct Layout {
+  char* base; size_t used = 0;
+  template <class P> void place(P*& p, size_t count) {
+    used = align256(used);
+    p = reinterpret_cast<P*>(base + used);
+    used += count * sizeof(P);
+  }
+};
+
+}  // namespace
+
+size_t analyze_scratch_bytes(int n_trials, int max_phase_samples) {
+  int SP = 32;
+  while (SP < max_phase_samples + 1) SP <<= 1;
+  const size_t tile = (size_t)kSortColumns * SP * sizeof(double);
+  return tile > kSmemSortBytes ? (size_t)n_trials * tile : 0;
+}
+
+}  // namespace pm
+
+using namespace pm;
+
+extern "C" {
+
+size_t pm_last_error(char* buffer, size_t cap) {
+  if (buffer && cap) {
+    const size_t n = t_error.size() < cap - 1 ? t_error.size() : cap - 1;
+    memcpy(buffer, t_error.data(), n);
+    buffer[n] = 0;
+  }
+  return t_error.size();
+}
+
+int32_t pm_abi_version(void) { return PM_ABI_VERSION; }
+
+int32_t pm_device_count(void) {
+  int n = 0;
+  if (cudaGetDeviceCount(&n) != cudaSuccess) { cudaGetLastError(); return 0; }
+  return n;
+}
+
+int32_t pm_layout(const char* name) {
+  if (!name) return -1;
+#define PM_LOOKUP(list)                                                     \
+  {                                                                         \
+    static const char* names[] = {list};                                    \
+    for (int i = 0; i < (int)(sizeof(names) / sizeof(names[0])); ++i)       \
+      if (!strcmp(name, names[i])) return i;                                \
+  }
+#define PM_NAME_PO(n) "PM_PO_" #n,
+#define PM_NAME_PF(n) "PM_PF_" #n,
+#define PM_NAME_TO(n) "PM_TO_" #n,
+#define PM_NAME_IT(n) "PM_IT_" #n,
+#define PM_NAME_IB(n) "PM_IB_" #n,
+#define PM_NAME_IP(n) "PM_IP_" #n,
+#define PM_NAME_W(n) "PM_W_" #n,
+#define PM_NAME_M(n) "PM_M_" #n,
+  PM_LOOKUP(PM_PHASE_FIELDS(PM_NAME_PO))
+  PM_LOOKUP(PM_PHASE_FLAGS(PM_NAME_PF))
+  PM_LOOKUP(PM_TRIAL_FIELDS(PM_NAME_TO))
+  PM_LOOKUP(PM_ISSUES_TREATMENT(PM_NAME_IT))
+  PM_LOOKUP(PM_ISSUES_BASELINE(PM_NAME_IB))
+  PM_LOOKUP(PM_ISSUES_PAIRED(PM_NAME_IP))
+  PM_LOOKUP(PM_WARNINGS(PM_NAME_W))
+  PM_LOOKUP(PM_METRIC_NAMES(PM_NAME_M))
+  static const struct { const char* n; int v; } counts[] = {
+    {"PM_PO_COUNT", PM_PO_COUNT}, {"PM_PF_COUNT", PM_PF_COUNT}, {"PM_TO_COUNT", PM_TO_COUNT},
+    {"PM_IT_COUNT", PM_IT_COUNT}, {"PM_IB_COUNT", PM_IB_COUNT}, {"PM_IP_COUNT", PM_IP_COUNT},
+    {"PM_W_COUNT", PM_W_COUNT}, {"PM_M_COUNT", PM_M_COUNT}, {"PM_ISSUE_WORDS", PM_ISSUE_WORDS},
+    {"PM_TS_COUNT", PM_TS_COUNT}, {"PM_PHASES", PM_PHASES},
+    {"PM_MAX_PHASE_SAMPLES", kMaxPhaseSamples}, {"PM_MAX_EPOCHS_PER_ARM", kMaxEpochsPerArm},
+    {"PM_MAX_GROUP_MEMBERS", kMaxGroupMembers}};
+  for (auto& c : counts) if (!strcmp(name, c.n)) return c.v;
+  return -1;
+}
+
+size_t pm_analyze_scratch_bytes(int32_t n_trials, int32_t max_phase_samples) {
+  return analyze_scratch_bytes(n_trials < 0 ? 0 : n_trials, max_phase_samples < 0 ? 0 : max_phase_samples);
+}
+
+int pm_analyze_trials_device(const pm_trials* trials, const pm_policy* policy, pm_trial_results* out,
+                             void* scratch, size_t scratch_bytes, void* stream) {
+  if (!trials || !policy || !out) return fail(PM_E_INVALID, "NULL argument");
+  if (trials->n_trials < 0 || trials->max_phase_samples < 0) return fail(PM_E_INVALID, "negative size");
+  if (trials->max_phase_samples > kMaxPhaseSamples) return fail(PM_E_LIMIT, "max_phase_samples beyond %d", kMaxPhaseSamples);
+  if (policy->min_samples < 2) return fail(PM_E_INVALID, "min_samples must be >= 2");
+  const size_t need = analyze_scratch_bytes(trials->n_trials, trials->max_phase_samples);
+  if (need > scratch_bytes || (need && !scratch))
+    return fail(PM_E_INVALID, "analysis needs %zu bytes of device scratch, got %zu", need, scratch_bytes);
+  launch_analyze(*trials, *policy, *out, trials->max_phase_samples, need ? (double*)scratch : nullptr, (cudaStream_t)stream, nullptr);
+  cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) return cuda_fail(e, "analyze_kernel launch");
+  return PM_OK;
+}
+
+}  // extern "C"
+
+namespace pm {
+namespace {
+
+struct StagedTrials {
+  pm_trials dev;              // device view of the staged batch
+  pm_trial_results dres, hres;
+  size_t in_bytes = 0, res_bytes = 0, end = 0;   // byte extents inside the arena
+  int max_cov = 0;
+  double* gscratch = nullptr;
+};
+
+// Size, reserve (plus `extra_dev`/`extra_host` bytes after the results) and
+// stage a host batch into the device arena; enqueue the H2D copy.
+int stage_trials(Arena& A, const pm_trials& T, size_t extra_dev, size_t extra_host, StagedTrials& S) {
+  int rc = check_trials_host(T, &S.max_cov);
+  if (rc) return rc;
+  const size_t n = (size_t)T.n_trials;
+  visit_trials(T, [&](const auto* p, size_t count) { S.in_bytes = align256(S.in_bytes) + count * sizeof(*p); });
+  S.in_bytes = align256(S.in_bytes);
+  pm_trial_results probe{};
+  visit_results(probe, n, [&](auto* p, size_t count) { S.res_bytes = align256(S.res_bytes) + count * sizeof(*p); });
+  S.res_bytes = align256(S.res_bytes);
+  const size_t scratch = analyze_scratch_bytes((int)n, S.max_cov);
+  S.end = S.in_bytes + S.res_bytes;
+  if ((rc = arena_reserve(A, S.end + scratch + extra_dev, S.end + extra_host))) return rc;
+  S.dev = T;
+  S.dev.max_phase_samples = S.max_cov;
+  Layout hl{static_cast<char*>(A.host)};
+  size_t offs[32]; int k = 0;
+  visit_trials(T, [&](const auto* p, size_t count) {
+    using E = std::remove_cv_t<std::remove_pointer_t<decltype(p)>>;
+    E* dst = nullptr;
+    hl.place(dst, count);
+    if (count) memcpy(dst, p, count * sizeof(E));
+    offs[k++] = reinterpret_cast<char*>(dst) - static_cast<char*>(A.host);
+  });
+  k = 0;
+  visit_trials(S.dev, [&](auto& p, size_t) {
+    using Ptr = std::remove_reference_t<decltype(p)>;
+    p = reinterpret_cast<Ptr>(static_cast<char*>(A.dev) + offs[k++]);
+  });
+  cudaError_t e = cudaMemcpyAsync(A.dev, A.host, S.in_bytes, cudaMemcpyHostToDevice, A.stream);
+  if (e != cudaSuccess) return cuda_fail(e, "cudaMemcpyAsync(inputs)");
+  Layout dl{static_cast<char*>(A.dev) + S.in_bytes}, rl{static_cast<char*>(A.host) + S.in_bytes};
+  visit_results(S.dres, n, [&](auto*& p, size_t count) { dl.place(p, count); });
+  visit_results(S.hres, n, [&](auto*& p, size_t count) { rl.place(p, count); });
+  S.gscratch = scratch ? reinterpret_cast<double*>(static_cast<char*>(A.dev) + S.end + extra_dev) : nullptr;
+  return PM_OK;
+}
+
+void copy_results_out(const StagedTrials& S, size_t n, pm_trial_results* out) {
+  if (out->phase_out) memcpy(out->phase_out, S.hres.phase_out, n * PM_PHASES * PM_PO_COUNT * sizeof(double));
+  if (out->phase_flags) memcpy(out->phase_flags, S.hres.phase_flags, n * PM_PHASES * sizeof(uint32_t));
+  if (out->trial_out) memcpy(out->trial_out, S.hres.trial_out, n * PM_TO_COUNT * sizeof(double));
+  if (out->issue_bits) memcpy(out->issue_bits, S.hres.issue_bits, n * PM_ISSUE_WORDS * sizeof(uint64_t));
+  if (out->metrics) memcpy(out->metrics, S.hres.metrics, n * PM_N_METRICS * sizeof(double));
+  if (out->valid) memcpy(out->valid, S.hres.valid, n);
+}
+
+}  // namespace
+}  // namespace pm
+
+extern "C" {
+
+int pm_analyze_trials(const pm_trials* trials, const pm_policy* policy, pm_trial_results* out) {
+  if (!trials || !policy || !out) return fail(PM_E_INVALID, "NULL argument");
+  int device = 0, rc = current_device(&device);
+  if (rc) return rc;
+  if (policy->min_samples < 2) return fail(PM_E_INVALID, "min_samples must be >= 2");
+  const size_t n = (size_t)trials->n_trials;
+  if (trials->n_trials < 0) return fail(PM_E_INVALID, "negative n_trials");
+  if (n == 0) return PM_OK;
+  Arena& A = g_arenas[device];
+  std::lock_guard<std::mutex> guard(A.lock);
+  StagedTrials S;
+  if ((rc = stage_trials(A, *trials, 0, 0, S))) return rc;
+  launch_analyze(S.dev, *policy, S.dres, S.max_cov, S.gscratch, A.stream, nullptr);
+  cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) return cuda_fail(e, "analyze_kernel launch");
+  e = cudaMemcpyAsync(static_cast<char*>(A.host) + S.in_bytes, static_cast<char*>(A.dev) + S.in_bytes, S.res_bytes,
+                      cudaMemcpyDeviceToHost, A.stream);
+  if (e != cudaSuccess) return cuda_fail(e, "cudaMemcpyAsync(results)");
+  e = cudaStreamSynchronize(A.stream);
+  if (e != cudaSuccess) return cuda_fail(e, "analyze_kernel");
+  copy_results_out(S, n, out);
+  return PM_OK;
+}
+
+// ---------------------------------------------------------------------------
+static int check_bootstrap(const pm_bootstrap_job* j) {
+  if (!j) return fail(PM_E_INVALID, "NULL job");
+  if (j->n_groups < 0 || j->n_metrics <= 0 || j->n_metrics > kMaxMetrics || j->n_members < 0 || j->n_rows < 0)
+    return fail(PM_E_INVALID, "bad bootstrap sizes");
+  if (j->resamples < 40 || j->resamples > (1 << 24)) return fail(PM_E_INVALID, "resamples must be in [40, 2^24]");
+  if (j->max_members < 0 || j->max_members > kMaxGroupMembers)
+    return fail(PM_E_LIMIT, "max_members %d outside [0, %d]", j->max_members, kMaxGroupMembers);
+  if (!j->values || !j->group_offsets || !j->seeds || !j->medians || !j->ci_lo || !j->ci_hi)
+    return fail(PM_E_INVALID, "a pm_bootstrap_job array is NULL");
+  return PM_OK;
+}
+
+size_t pm_bootstrap_scratch_bytes(int32_t n_groups, int32_t max_members, int32_t resamples) {
+  if (n_groups < 0 || max_members < 0 || resamples < 0) return 0;
+  return bootstrap_scratch_bytes(n_groups, max_members, resamples);
+}
+
+int pm_group_bootstrap_device(const pm_bootstrap_job* job, void* scratch, size_t scratch_bytes, void* stream) {
+  int rc = check_bootstrap(job);
+  if (rc) return rc;
+  int device = 0;
+  if ((rc = current_device(&device))) return rc;
+  if (prepare_bootstrap_constants(device)) return fail(PM_E_CUDA, "bootstrap constants upload failed");
+  const size_t need = bootstrap_scratch_bytes(job->n_groups, job->max_members, job->resamples);
+  if (need > scratch_bytes || (need && !scratch))
+    return fail(PM_E_INVALID, "bootstrap needs %zu bytes of device scratch, got %zu", need, scratch_bytes);
+  BootArgs A{job->n_groups, job->n_metrics, job->resamples, job->max_members, job->values, job->group_offsets,
+             job->member_rows, job->member_valid, job->seeds, job->medians, job->ci_lo, job->ci_hi,
+             need ? static_cast<uint8_t*>(scratch) : nullptr};
+  launch_bootstrap(A, (cudaStream_t)stream);
+  cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) return cuda_fail(e, "bootstrap_kernel launch");
+  return PM_OK;
+}
+
+int pm_group_bootstrap(const pm_bootstrap_job* job) {
+  int rc = check_bootstrap(job);
+  if (rc) return rc;
+  int device = 0;
+  if ((rc = current_device(&device))) return rc;
+  if (prepare_bootstrap_constants(device)) return fail(PM_E_CUDA, "bootstrap constants upload failed");
+  const size_t G = (size_t)job->n_groups, M = (size_t)job->n_metrics;
+  int mm = 0;
+  for (size_t g = 0; g < G; ++g) {
+    const int c = job->group_offsets[g + 1] - job->group_offsets[g];
+    if (c < 0) return fail(PM_E_INVALID, "group_offsets must be non-decreasing");
+    if (c > kMaxGroupMembers) return fail(PM_E_LIMIT, "group %zu lists %d members; the limit is %d", g, c, kMaxGroupMembers);
+    if (c > mm) mm = c;
+  }
+  if (G && (job->group_offsets[0] != 0 || job->group_offsets[G] != job->n_members))
+    return fail(PM_E_INVALID, "group_offsets must start at 0 and end at n_members");
+  const size_t rows = job->member_rows || job->member_valid ? (size_t)job->n_rows : (size_t)job->n_members;
+  if (job->member_rows)
+    for (int i = 0; i < job->n_members; ++i)
+      if (job->member_rows[i] < 0 || (size_t)job->member_rows[i] >= rows) return fail(PM_E_INVALID, "member_rows[%d] out of range", i);
+  if (G == 0) return PM_OK;
+  const size_t scratch = bootstrap_scratch_bytes((int)G, mm, job->resamples);
+  size_t in_bytes = align256(rows * M * 8) + align256((G + 1) * 4) + align256((size_t)job->n_members * 4) + align256(rows) + align256(G * 8);
+  size_t out_bytes = 3 * align256(G * M * 8);
+  Arena& A = g_arenas[device];
+  std::lock_guard<std::mutex> guard(A.lock);
+  if ((rc = arena_reserve(A, in_bytes + out_bytes + scratch, in_bytes + out_bytes))) return rc;
+  Layout hl{static_cast<char*>(A.host)};
+  double* hv; int32_t* ho; int32_t* hr = nullptr; uint8_t* hvalid = nullptr; uint64_t* hs;
+  hl.place(hv, rows * M); memcpy(hv, job->values, rows * M * 8);
+  hl.place(ho, G + 1); memcpy(ho, job->group_offsets, (G + 1) * 4);
+  int32_t* tmp_r; hl.place(tmp_r, job->n_members); if (job->member_rows) { memcpy(tmp_r, job->member_rows, (size_t)job->n_members * 4); hr = tmp_r; }
+  uint8_t* tmp_v; hl.place(tmp_v, rows); if (job->member_valid) { memcpy(tmp_v, job->member_valid, rows); hvalid = tmp_v; }
+  hl.place(hs, G); memcpy(hs, job->seeds, G * 8);
+  auto dev_of = [&](const void* h) { return static_cast<char*>(A.dev) + (static_cast<const char*>(h) - static_cast<char*>(A.host)); };
+  cudaStream_t st = A.stream;
+  cudaError_t e = cudaMemcpyAsync(A.dev, A.host, in_bytes, cudaMemcpyHostToDevice, st);
+  if (e != cudaSuccess) return cuda_fail(e, "cudaMemcpyAsync(bootstrap inputs)");
+  char* dout = static_cast<char*>(A.dev) + in_bytes;
+  double* dmed = reinterpret_cast<double*>(dout);
+  double* dlo = reinterpret_cast<double*>(dout + align256(G * M * 8));
+  double* dhi = reinterpret_cast<double*>(dout + 2 * align256(G * M * 8));
+  BootArgs args{(int)G, (int)M, job->resamples, mm, reinterpret_cast<const double*>(dev_of(hv)),
+                reinterpret_cast<const int32_t*>(dev_of(ho)), hr ? reinterpret_cast<const int32_t*>(dev_of(hr)) : nullptr,
+                hvalid ? reinterpret_cast<const uint8_t*>(dev_of(hvalid)) : nullptr,
+                reinterpret_cast<const uint64_t*>(dev_of(hs)), dmed, dlo, dhi,
+                scratch ? reinterpret_cast<uint8_t*>(dout + out_bytes) : nullptr};
+  launch_bootstrap(args, st);
+  e = cudaGetLastError();
+  if (e != cudaSuccess) return cuda_fail(e, "bootstrap_kernel launch");
+  char* hout = static_cast<char*>(A.host) + in_bytes;
+  e = cudaMemcpyAsync(hout, dout, out_bytes, cudaMemcpyDeviceToHost, st);
+  if (e != cudaSuccess) return cuda_fail(e, "cudaMemcpyAsync(bootstrap results)");
+  e = cudaStreamSynchronize(st);
+  if (e != cudaSuccess) return cuda_fail(e, "bootstrap_kernel");
+  memcpy(job->medians, hout, G * M * 8);
+  memcpy(job->ci_lo, hout + align256(G * M * 8), G * M * 8);
+  memcpy(job->ci_hi, hout + 2 * align256(G * M * 8), G * M * 8);
+  return PM_OK;
+}
+
+int pm_analyze_sweep(const pm_trials* trials, const pm_policy* policy, pm_trial_results* out, pm_bootstrap_job* groups) {
+  if (!trials || !policy || !out || !groups) return fail(PM_E_INVALID, "NULL argument");
+  if (policy->min_samples < 2) return fail(PM_E_INVALID, "min_samples must be >= 2");
+  if (trials->n_trials < 0) return fail(PM_E_INVALID, "negative n_trials");
+  pm_bootstrap_job J = *groups;
+  J.n_rows = trials->n_trials; J.n_metrics = PM_N_METRICS;
+  const size_t G = J.n_groups < 0 ? 0 : (size_t)J.n_groups, M = PM_N_METRICS, n = (size_t)trials->n_trials;
+  if (J.n_groups < 0 || J.n_members < 0) return fail(PM_E_INVALID, "negative group sizes");
+  if (J.resamples < 40 || J.resamples > (1 << 24)) return fail(PM_E_INVALID, "resamples must be in [40, 2^24]");
+  if (!J.group_offsets || !J.seeds || !J.medians || !J.ci_lo || !J.ci_hi) return fail(PM_E_INVALID, "a group array is NULL");
+  int mm = 0;
+  for (size_t g = 0; g < G; ++g) {
+    const int c = J.group_offsets[g + 1] - J.group_offsets[g];
+    if (c < 0) return fail(PM_E_INVALID, "group_offsets must be non-decreasing");
+    if (c > kMaxGroupMembers) return fail(PM_E_LIMIT, "group %zu lists %d members; the limit is %d", g, c, kMaxGroupMembers);
+    if (c > mm) mm = c;
+  }
+  if (G && (J.group_offsets[0] != 0 || J.group_offsets[G] != J.n_members))
+    return fail(PM_E_INVALID, "group_offsets must start at 0 and end at n_members");
+  for (int i = 0; i < J.n_members; ++i)
+    if (J.member_rows && (J.member_rows[i] < 0 || (size_t)J.member_rows[i] >= n)) return fail(PM_E_INVALID, "member_rows[%d] out of range", i);
+  int device = 0, rc = current_device(&device);
+  if (rc) return rc;
+  if (prepare_bootstrap_constants(device)) return fail(PM_E_CUDA, "bootstrap constants upload failed");
+  if (n == 0) return PM_OK;
+  const size_t gin = align256((G + 1) * 4) + align256((size_t)J.n_members * 4) + align256(G * 8);
+  const size_t gout = 3 * align256(G * M * 8);
+  const size_t bscratch = bootstrap_scratch_bytes((int)G, mm, J.resamples);
+  Arena& A = g_arenas[device];
+  std::lock_guard<std::mutex> guard(A.lock);
+  StagedTrials S;
+  // extra host bytes hold the group inputs then outputs; extra device bytes mirror them plus scratch
+  if ((rc = stage_trials(A, *trials, gin + gout + bscratch, gin + gout, S))) return rc;
+  char* hbase = static_cast<char*>(A.host) + S.end;
+  char* dbase = static_cast<char*>(A.dev) + S.end;
+  Layout hl{hbase};
+  int32_t* ho; int32_t* hr; uint64_t* hs;
+  hl.place(ho, G + 1); memcpy(ho, J.group_offsets, (G + 1) * 4);
+  hl.place(hr, J.n_members); if (J.member_rows) memcpy(hr, J.member_rows, (size_t)J.n_members * 4);
+  else for (int i = 0; i < J.n_members; ++i) hr[i] = i;
+  hl.place(hs, G); memcpy(hs, J.seeds, G * 8);
+  cudaError_t e = cudaMemcpyAsync(dbase, hbase, gin, cudaMemcpyHostToDevice, A.stream);
+  if (e != cudaSuccess) return cuda_fail(e, "cudaMemcpyAsync(groups)");
+  launch_analyze(S.dev, *policy, S.dres, S.max_cov, S.gscratch, A.stream, nullptr);
+  auto dptr = [&](const void* h) { return dbase + (static_cast<const char*>(h) - hbase); };
+  char* dout = dbase + gin;
+  BootArgs args{(int)G, (int)M, J.resamples, mm, S.dres.metrics, reinterpret_cast<const int32_t*>(dptr(ho)),
+                reinterpret_cast<const int32_t*>(dptr(hr)), S.dres.valid, reinterpret_cast<const uint64_t*>(dptr(hs)),
+                reinterpret_cast<double*>(dout), reinterpret_cast<double*>(dout + align256(G * M * 8)),
+                reinterpret_cast<double*>(dout + 2 * align256(G * M * 8)),
+                bscratch ? reinterpret_cast<uint8_t*>(dout + gout) : nullptr};
+  if (G) launch_bootstrap(args, A.stream);
+  e = cudaGetLastError();
+  if (e != cudaSuccess) return cuda_fail(e, "sweep kernels launch");
+  e = cudaMemcpyAsync(static_cast<char*>(A.host) + S.in_bytes, static_cast<char*>(A.dev) + S.in_bytes, S.res_bytes,
+                      cudaMemcpyDeviceToHost, A.stream);
+  if (e == cudaSuccess && G) e = cudaMemcpyAsync(hbase + gin, dout, gout, cudaMemcpyDeviceToHost, A.stream);
+  if (e != cudaSuccess) return cuda_fail(e, "cudaMemcpyAsync(sweep results)");
+  e = cudaStreamSynchronize(A.stream);
+  if (e != cudaSuccess) return cuda_fail(e, "sweep kernels");
+  copy_results_out(S, n, out);
+  if (G) {
+    memcpy(groups->medians, hbase + gin, G * M * 8);
+    memcpy(groups->ci_lo, hbase + gin + align256(G * M * 8), G * M * 8);
+    memcpy(groups->ci_hi, hbase + gin + 2 * align256(G * M * 8), G * M * 8);
+  }
+  groups->n_rows = (int32_t)n; groups->n_metrics = PM_N_METRICS; groups->max_members = mm;
+  return PM_OK;
+}
+
+int pm_resample_indices(uint64_t seed, int32_t n, int32_t resamples, int32_t* out) {
+  if (!out || n < 1 || n > kMaxGroupMembers || resamples < 1 || (int64_t)n * resamples > (1 << 26))
+    return fail(PM_E_INVALID, "pm_resample_indices: n in [1, %d], resamples >= 1, n*resamples <= 2^26", kMaxGroupMembers);
+  int device = 0, rc = current_device(&device);
+  if (rc) return rc;
+  if (prepare_bootstrap_constants(device)) return fail(PM_E_CUDA, "bootstrap constants upload failed");
+  const size_t bytes = (size_t)n * resamples * 4;
+  Arena& A = g_arenas[device];
+  std::lock_guard<std::mutex> guard(A.lock);
+  if ((rc = arena_reserve(A, bytes, bytes))) return rc;
+  launch_resample_indices(seed, n, resamples, static_cast<int32_t*>(A.dev), A.stream);
+  cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) return cuda_fail(e, "resample_indices launch");
+  e = cudaMemcpyAsync(A.host, A.dev, bytes, cudaMemcpyDeviceToHost, A.stream);
+  if (e == cudaSuccess) e = cudaStreamSynchronize(A.stream);
+  if (e != cudaSuccess) return cuda_fail(e, "resample_indices");
+  memcpy(out, A.host, bytes);
+  return PM_OK;
+}
+
+}  // extern "C"

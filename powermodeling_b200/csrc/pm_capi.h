@@ -1,0 +1,45 @@
+// Host-side declarations shared by the C ABI translation units.
+#pragma once
+#include <cuda_runtime.h>
+#include <cstddef>
+#include <cstdint>
+#include <mutex>
+
+namespace pm {
+
+constexpr int kMaxDevices = 64;
+constexpr int kMaxPhaseSamples = 1 << 24;   // samples in one (trial, phase) segment
+constexpr int kMaxEpochsPerArm = 256;
+constexpr int kMaxGroupMembers = 128;       // bootstrap rows per group
+constexpr int kMaxMetrics = 256;
+constexpr int kSortColumns = 10;            // columns sorted per phase for medians
+constexpr size_t kSmemSortBytes = 160 * 1024;
+
+// Arguments of the group bootstrap kernel.
+struct BootArgs {
+  int n_groups, n_metrics, resamples, max_members;
+  const double* values;
+  const int32_t* offsets;
+  const int32_t* member_rows;     // NULL: identity
+  const uint8_t* member_valid;    // NULL: all rows count
+  const uint64_t* seeds;
+  double* medians; double* lo; double* hi;
+  uint8_t* scratch;               // index streams of groups with more than 7 members
+};
+
+// Grow-only device workspace, pinned staging buffer and private stream of a device.
+struct Arena {
+  void* dev = nullptr; size_t dev_bytes = 0;
+  void* host = nullptr; size_t host_bytes = 0;
+  cudaStream_t stream = nullptr;
+  std::mutex lock;
+};
+extern Arena g_arenas[kMaxDevices];
+
+int fail(int code, const char* fmt, ...);
+int cuda_fail(cudaError_t e, const char* where);
+int current_device(int* device);
+int arena_reserve(Arena& a, size_t dev_bytes, size_t host_bytes);
+size_t analyze_scratch_bytes(int n_trials, int max_phase_samples);
+
+}  // namespace pm

@@ -1,0 +1,93 @@
+"""GPU parity: libpmb200's analysis against the reference's outputs and the oracle."""
+from __future__ import annotations
+
+import math
+
+import numpy as np
+import pytest
+
+from conftest import close, diff, load_golden
+from oracle import analysis_oracle as O
+from trial_builders import scenarios
+from tests.golden.make_golden import TRIAL_KEYS, PHASE_KEYS, records_digest
+
+pytestmark = pytest.mark.gpu
+
+# Floating tolerance of the north star: 1e-6 relative for energies and pJ/op.
+REL = 1e-6
+EXACT_KEYS = ("total_energy_j", "integrated_power_energy_j", "energy_counter_j", "board_power_w", "idle_power_w",
+              "incremental_energy_j", "pj_per_op", "throughput_ops_s", "paired_active_reference_power_w")
+
+
+@pytest.fixture(scope="module")
+def golden_trials():
+    return {c["name"]: c for c in load_golden("analysis_trials.json.gz")["cases"]}
+
+
+@pytest.mark.parametrize("name,record,policy", scenarios(), ids=[s[0] for s in scenarios()])
+def test_trial_matches_reference(gpu_ready, golden_trials, name, record, policy):
+    from powermodeling_b200.analysis import analyze_trial
+    case = golden_trials[name]
+    assert case["digest"] == records_digest([record])
+    got = analyze_trial(record, policy)
+    expected = case["expected"]
+    problems = diff(expected, got, TRIAL_KEYS, rel=REL)
+    for phase, stats in expected["phases"].items():
+        problems += [f"{phase}.{p}" for p in diff(stats, got["phases"].get(phase, {}), PHASE_KEYS, rel=REL)]
+    assert not problems, problems
+    # The energy integrals follow CPython's arithmetic exactly.
+    for key in EXACT_KEYS:
+        if key in expected:
+            assert close(expected[key], got.get(key), rel=0.0), (key, expected[key], got.get(key))
+
+
+def test_sweep_groups_match_reference(gpu_ready):
+    from powermodeling_b200.analysis import group_key, summarize, METRICS
+    from powermodeling_b200.synthetic import ANALYSIS_POLICY, SweepShape, make_sweep
+    for sweep in load_golden("analysis_sweeps.json.gz")["sweeps"]:
+        shape = SweepShape(**{k: tuple(v) if isinstance(v, list) else v for k, v in sweep["shape"].items()})
+        records = make_sweep(shape, sweep["seed"])
+        summary = summarize(records, policy=ANALYSIS_POLICY)
+        assert [group_key(t) for t in summary["trials"]] == sweep["group_keys"]
+        assert len(summary["groups"]) == len(sweep["groups"])
+        for got, exp in zip(summary["groups"], sweep["groups"]):
+            assert got["group_id"] == exp["group_id"] and got["valid_repeats"] == exp["valid_repeats"]
+            for metric in METRICS:
+                assert close(exp["medians"][metric], got[metric], rel=0.0), (metric, exp["medians"][metric], got[metric])
+                assert close(exp["ci95"][metric], got["ci95"][metric], rel=0.0), (metric, exp["ci95"][metric], got["ci95"][metric])
+            assert got["paired_reference_order_counts"] == exp["paired_reference_order_counts"]
+            assert got["paired_active_reference_eligible"] == exp["paired_active_reference_eligible"]
+            assert close(exp["paired_reference_order_effect_power_w"], got["paired_reference_order_effect_power_w"], rel=0.0)
+
+
+def test_median_ci_matches_reference_at_1000_and_10000_draws(gpu_ready):
+    from powermodeling_b200.analysis import median_ci
+    for case in load_golden("median_ci.json.gz")["cases"]:
+        assert median_ci(case["values"], case["seed"]) == case["ci_1000"], case
+        assert median_ci(case["values"], case["seed"], 10000) == case["ci_10000"], case
+
+
+def test_resample_index_stream_is_bit_exact(gpu_ready):
+    for s in load_golden("median_ci.json.gz")["streams"]:
+        rows = gpu_ready.resample_indices(s["seed"], s["n"], len(s["rows"]))
+        assert rows.tolist() == s["rows"]
+
+
+def test_full_size_sweep_against_oracle(gpu_ready):
+    """64 points x 4 repeats, B = 10 000: trial numbers for every trial, CIs for a sample of groups."""
+    from powermodeling_b200.analysis import METRICS, summarize
+    from powermodeling_b200.synthetic import ANALYSIS_POLICY, SweepShape, make_sweep
+    records = make_sweep(SweepShape(), seed=0)
+    summary = summarize(records, policy=ANALYSIS_POLICY, resamples=10000)
+    assert len(summary["trials"]) == 256 and len(summary["groups"]) == 64
+    for record, trial in zip(records, summary["trials"]):
+        expected = O.analyze(record, ANALYSIS_POLICY)
+        assert trial["valid"]
+        assert not diff(expected, trial, ("total_energy_j", "board_power_w", "idle_power_w", "pj_per_op",
+                                          "paired_active_reference_pj_per_flop", "throughput_ops_s"), rel=0.0)
+    for g in summary["groups"][:3]:
+        members = [summary["trials"][records.index(next(r for r in records if r["trial_id"] == tid))] for tid in g["trial_ids"]]
+        seed = int(g["group_id"], 16)
+        for metric in METRICS:
+            vals = [v for t in members if (v := O.num(t.get(metric))) is not None]
+            assert g["ci95"][metric] == O.median_ci(vals, seed, 10000), metric
