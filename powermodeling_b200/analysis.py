@@ -540,14 +540,14 @@ def analyze_trials(records: Iterable[Mapping[str, Any]], policy: AnalysisPolicy 
             "baseline_temperature_matched": bool(to[TO["BASE_TEMP_MATCHED"]]),
             "baseline_power_cap_matched": bool(to[TO["BASE_CAP_MATCHED"]]),
             "baseline_state_matched": bool(to[TO["BASE_STATE_MATCHED"]]),
-            "baseline_state_issues": sorted(s for s in baseline_issues if s.startswith("idle_state_mismatch_or_unverified")),
             "baseline_clock_domains_compared": ["graphics_clock_mhz", "memory_clock_mhz"] + (["sm_clock_mhz"] if to[TO["BASE_SM_COMPARED"]] else []),
             "baseline_sm_clock_uses_graphics_proxy": not bool(to[TO["BASE_SM_COMPARED"]]),
             "baseline_state_domains_compared": sorted(([ "enforced_power_limit_w"] if to[TO["BASE_ENF_COMPARED"]] else [])
                                                       + (["pstate"] if to[TO["BASE_PSTATE_COMPARED"]] else [])),
             "policy": asdict(policy), "phases": {},
         }
-        result["baseline_state_issues"] = [s for s in sorted(set(baseline_issues)) if s.startswith("idle_state_mismatch_or_unverified")]
+        # insertion order of the reference: idle_pre before idle_post, enforced limit before pstate (= bit order)
+        result["baseline_state_issues"] = [s for s in baseline_issues if s.startswith("idle_state_mismatch_or_unverified")]
         result["active_minus_idle_state_deltas"] = _state_deltas(to, TO)
         tensor, memory = workload in TENSOR_WORKLOADS, workload in MEMORY_WORKLOADS
         result["total_pj_per_flop"] = g("TOTAL_PJ_PER_FLOP")

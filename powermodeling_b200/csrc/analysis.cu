@@ -102,6 +102,7 @@ __device__ void measure_epochs(const pm_trials& T, const pm_policy& P, int trial
   if (none(phase_start) || none(phase_end)) { r.issue = 0; return; }
   const int32_t b = T.epoch_offsets[trial * 2 + arm], e = T.epoch_offsets[trial * 2 + arm + 1];
   const int n = e - b;
+  if (n < 0 || n > kMaxEpochs) { r.issue = 5; return; }   // the host entry points reject these lists first
   for (int k = 0; k < n; ++k) {
     const double a = T.epoch_start_s[b + k], z = T.epoch_end_s[b + k];
     if (none(a) || none(z) || z <= a || a < phase_start - 1e-6 || z > phase_end + 1e-6) { r.issue = 1; return; }

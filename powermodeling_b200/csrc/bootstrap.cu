@@ -141,6 +141,11 @@ __global__ void __launch_bounds__(kBootThreads) bootstrap_kernel(BootArgs A) {
   const int m0 = A.offsets[g], m1 = A.offsets[g + 1];
   const int members = m1 - m0;
   const int M = A.n_metrics;
+  if (members < 0 || members > A.max_members) {            // caller broke the stated bound: no output
+    for (int m = threadIdx.x; m < M; m += blockDim.x)
+      A.medians[(size_t)g * M + m] = A.lo[(size_t)g * M + m] = A.hi[(size_t)g * M + m] = dnan();
+    return;
+  }
   const BootSmem L(M, A.max_members, A.max_members > kHistMaxN);
   double* vals = reinterpret_cast<double*>(dsm + L.vals);
   int* cnt = reinterpret_cast<int*>(dsm + L.cnt);
