@@ -216,6 +216,28 @@ int pm_group_bootstrap_device(const pm_bootstrap_job* job, void* scratch, size_t
 int pm_analyze_sweep(const pm_trials* trials, const pm_policy* policy, pm_trial_results* out,
                      pm_bootstrap_job* groups);
 
+/*
+ * The measured-workload engine behind the powerbench command line
+ * (the reference's cuda/gpu_bench.cu main and experiment(), lines 121-254,
+ * 519-602, 611-1192, and cuda/sfu.cuh experiment_sfu, 226-356): the same
+ * flags, phase order, completion epochs and JSONL records, emitted one line
+ * per callback.  Returns 0, or 1 with the reason in pm_last_error() (a record
+ * may already have been emitted when a post-run check fails).
+ */
+typedef void (*pm_line_cb)(const char* line, void* user);
+int pm_powerbench(int argc, const char* const* argv, pm_line_cb cb, void* user);
+
+/*
+ * One CTA of the tcgen05 tensor arm on its own: fills A (128 x 64) and
+ * B (256 x 64) fp16 like the tensor workload does (seed, uniform[-1,1) when
+ * `uniform`), runs `iterations` x 4 K-slices into accumulator 0 of
+ * `accumulators` and copies accumulator 0 (128 x N fp32, N = 512/accumulators
+ * rounded down to 16, at most 256) to `out`; optionally the operands too.
+ * No counterpart in the reference: it checks the MMA path numerically.
+ */
+int pm_tensor_probe(int accumulators, uint64_t iterations, int uniform, uint64_t seed, float* out,
+                    size_t out_count, uint16_t* a_out, uint16_t* b_out);
+
 /* Raw resample index stream of random.Random(seed).choices(range(n), k=n),
  * repeated `resamples` times: out[r*n + j] (host buffer). Pins the generator. */
 int pm_resample_indices(uint64_t seed, int32_t n, int32_t resamples, int32_t* out);

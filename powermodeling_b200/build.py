@@ -32,8 +32,12 @@ def nvcc() -> str:
     return path
 
 
+EXECUTABLE = PACKAGE / "bin" / "powerbench"
+MAIN = CSRC / "powerbench_main.cpp"
+
+
 def _sources() -> list[Path]:
-    return sorted(CSRC.glob("*.cu")) + sorted(CSRC.glob("*.cpp"))
+    return sorted(CSRC.glob("*.cu")) + sorted(p for p in CSRC.glob("*.cpp") if p != MAIN)
 
 
 def _stale(obj: Path, src: Path, headers: list[Path]) -> bool:
@@ -65,10 +69,17 @@ def build(verbose: bool = False, jobs: int | None = None) -> Path:
         _drain(p)
     if commands or not LIBRARY.exists():
         link = [nvcc(), *ARCH, "-shared", "-o", str(LIBRARY), *map(str, objects),
-                "-lcuda", "-ldl", "-lpthread"]
+                "-lcublas", "-lcuda", "-ldl", "-lpthread"]
         if verbose:
             print(" ".join(link), file=sys.stderr)
         _drain(subprocess.Popen(link, stdout=subprocess.PIPE, stderr=subprocess.STDOUT, text=True))
+    if _stale(EXECUTABLE, MAIN, [LIBRARY, INCLUDE / "pmb200.h"]):
+        EXECUTABLE.parent.mkdir(exist_ok=True)
+        exe = [shutil.which("g++") or "g++", "-std=c++17", "-O2", "-I" + str(INCLUDE), str(MAIN), "-o", str(EXECUTABLE),
+               "-L" + str(PACKAGE), "-lpmb200", "-Wl,-rpath,$ORIGIN/.."]
+        if verbose:
+            print(" ".join(exe), file=sys.stderr)
+        _drain(subprocess.Popen(exe, stdout=subprocess.PIPE, stderr=subprocess.STDOUT, text=True))
     return LIBRARY
 
 

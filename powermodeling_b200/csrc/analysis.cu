@@ -24,7 +24,10 @@ namespace pm {
 constexpr int kThreads = 256;
 constexpr int kMaxEpochs = 256;        // per arm; the host rejects longer lists
 enum Col { C_GAP = 0, C_CHANGE, C_POWER, C_GFX, C_SM, C_MEM, C_TEMP, C_PLIMIT, C_ENF, C_PSTATE, C_COUNT };
-static_assert(C_COUNT == kSortColumns, "sort column count");
+// Staged (unsorted) covering samples that follow the sort columns in the tile.
+enum Stage { S_T = 0, S_POWER, S_MEMORY, S_REL, S_TERM_P, S_TERM_M, S_COUNT };
+constexpr int kTileColumns = C_COUNT + S_COUNT;
+static_assert(kTileColumns == kSortColumns, "tile column count");
 
 struct EpochResult {
   int32_t n_inner;            // complete epochs kept (0 = none)
@@ -44,6 +47,8 @@ struct Shared {
   double wstart, wend;
   int32_t nchange;
   int32_t nfin[C_COUNT];
+  double cmin[C_COUNT], cmax[C_COUNT];
+  int32_t sort_cols[C_COUNT], nsort, sort_p;
 };
 
 __device__ __forceinline__ double col_value(const pm_trials& T, int c, int64_t i) {
@@ -57,37 +62,6 @@ __device__ __forceinline__ double col_value(const pm_trials& T, int c, int64_t i
     case C_ENF: return T.enforced_power_limit_w[i];
     default: return T.pstate[i];
   }
-}
-
-// Value of the reference's _interpolate(samples, field, x) over covering
-// samples [cb, ce) whose values come from `val`.
-template <class V>
-__device__ double interpolate(const double* t, int64_t cb, int64_t ce, double x, V val) {
-  if (ce <= cb || x < t[cb] || x > t[ce - 1]) return dnan();
-  const int64_t i = lower_bound(t, cb, ce, x);
-  if (t[i] == x) return val(i);
-  const double a = val(i - 1), b = val(i);
-  if (none(a) || none(b)) return dnan();
-  const double ratio = (x - t[i - 1]) / (t[i] - t[i - 1]);
-  return a + ratio * (b - a);
-}
-
-// The reference's _integrate(covering, field, start, end).
-template <class V>
-__device__ double integrate(const double* t, int64_t cb, int64_t ce, double start, double end, V val) {
-  const double first = interpolate(t, cb, ce, start, val);
-  const double last = interpolate(t, cb, ce, end, val);
-  if (none(first) || none(last) || end <= start) return dnan();
-  NeumaierSum s;
-  double pt = start, pv = first;
-  for (int64_t i = upper_bound(t, cb, ce, start); i < ce && t[i] < end; ++i) {
-    const double v = val(i);
-    if (none(v)) return dnan();
-    s.add((t[i] - pt) * (pv + v) * 0.5);
-    pt = t[i]; pv = v;
-  }
-  s.add((end - pt) * (pv + last) * 0.5);
-  return s.result();
 }
 
 // ---------------------------------------------------------------------------
@@ -284,15 +258,31 @@ __device__ void phase_stats(const pm_trials& T, const pm_policy& P, Shared& S, d
     const double v = T.power_w[i];
     if (!none(v) && v < 0) neg_power = true;
   }
-  // per-column finite counts (selected columns; gaps counted from ncov)
+  // per-column finite counts, minima and maxima (selected columns; gaps from covering)
   int fin[C_COUNT];
-  for (int c = 0; c < C_COUNT; ++c) fin[c] = 0;
-  for (int64_t i = lo + threadIdx.x; i < hi; i += blockDim.x)
-    for (int c = C_POWER; c < C_COUNT; ++c) fin[c] += !none(col_value(T, c, i));
-  // CTA reductions
+  double cmn[C_COUNT], cmx[C_COUNT];
+  for (int c = 0; c < C_COUNT; ++c) { fin[c] = 0; cmn[c] = inf; cmx[c] = -inf; }
+  for (int q = threadIdx.x; q < SP; q += blockDim.x) {
+    for (int c = 0; c < C_COUNT; ++c) {
+      const double v = sortbuf[c * SP + q];
+      if (v != inf) { ++fin[c]; cmn[c] = fmin(cmn[c], v); cmx[c] = fmax(cmx[c], v); }
+    }
+  }
   {
     __shared__ uint32_t red_flags; __shared__ unsigned long long red_thr; __shared__ unsigned red_src;
     __shared__ int red_neg, red_pn, red_en, red_sn;
+    __shared__ double wmin[kThreads / 32][C_COUNT], wmax[kThreads / 32][C_COUNT];
+    __shared__ int wfin[kThreads / 32][C_COUNT];
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    for (int c = 0; c < C_COUNT; ++c) {
+      double mn = cmn[c], mx = cmx[c]; int f = fin[c];
+      for (int o = 16; o; o >>= 1) {
+        mn = fmin(mn, __shfl_xor_sync(0xffffffffu, mn, o));
+        mx = fmax(mx, __shfl_xor_sync(0xffffffffu, mx, o));
+        f += __shfl_xor_sync(0xffffffffu, f, o);
+      }
+      if (lane == 0) { wmin[warp][c] = mn; wmax[warp][c] = mx; wfin[warp][c] = f; }
+    }
     if (threadIdx.x == 0) { red_flags = 0; red_thr = 0; red_src = 0; red_neg = 0; red_pn = red_en = red_sn = 0; }
     __syncthreads();
     if (flags) atomicOr(&red_flags, flags);
@@ -302,58 +292,119 @@ __device__ void phase_stats(const pm_trials& T, const pm_policy& P, Shared& S, d
     if (plim_none) atomicAdd(&red_pn, plim_none);
     if (enf_none) atomicAdd(&red_en, enf_none);
     if (pst_none) atomicAdd(&red_sn, pst_none);
-    for (int c = C_POWER; c < C_COUNT; ++c) if (fin[c]) atomicAdd(&S.nfin[c], fin[c]);
+    if (threadIdx.x < C_COUNT) {
+      const int c = threadIdx.x;
+      double mn = inf, mx = -inf; int f = 0;
+      for (int w = 0; w < (int)(blockDim.x >> 5); ++w) { mn = fmin(mn, wmin[w][c]); mx = fmax(mx, wmax[w][c]); f += wfin[w][c]; }
+      S.cmin[c] = mn; S.cmax[c] = mx; S.nfin[c] = f;
+    }
     __syncthreads();
     if (threadIdx.x == 0) {
-      uint32_t f = red_flags;
-      if (red_thr) f |= 1u << PM_PF_THROTTLE_ACTIVE;
-      if (red_neg) f |= 1u << PM_PF_NEGATIVE_POWER;
-      S.pf[p] |= f | (1u << PM_PF_COMPUTED);
+      uint32_t fl = red_flags;
+      if (red_thr) fl |= 1u << PM_PF_THROTTLE_ACTIVE;
+      if (red_neg) fl |= 1u << PM_PF_NEGATIVE_POWER;
+      S.pf[p] |= fl | (1u << PM_PF_COMPUTED);
       po[PM_PO_THROTTLE_OR] = (double)red_thr;
       po[PM_PO_MEM_SOURCES] = (double)red_src;
       po[PM_PO_PLIMIT_NONE] = red_pn; po[PM_PO_ENF_NONE] = red_en; po[PM_PO_PSTATE_NONE] = red_sn;
-      S.nfin[C_GAP] = ncov > 1 ? ncov - 1 : 0;
-      S.nfin[C_CHANGE] = S.nchange > 1 ? S.nchange - 1 : 0;
+      // Only columns holding more than one distinct value need an order.
+      int ns = 0, longest = 2;
+      for (int c = 0; c < C_COUNT; ++c)
+        if (S.nfin[c] > 1 && S.cmin[c] != S.cmax[c]) { S.sort_cols[ns++] = c; longest = max(longest, S.nfin[c]); }
+      int P = 2;
+      while (P < longest) P <<= 1;
+      S.nsort = ns; S.sort_p = P;
     }
   }
   __syncthreads();
-  // ---- sort the columns (medians, minima, maxima, distinct values)
-  bitonic_sort_arrays(sortbuf, C_COUNT, SP);
-  // ---- sequential integrals on three lanes of three different warps
-  const int lane_id = threadIdx.x;
-  if (lane_id == 0) {
-    const double energy = integrate(t, cb, ce, start, end, [&](int64_t i) { return T.power_w[i]; });
+  // ---- sort the varying columns over their finite prefix length (power of two)
+  if (S.nsort) bitonic_sort_columns(sortbuf, SP, S.sort_cols, S.nsort, S.sort_p);
+  // ---- energies: stage the covering samples, form trapezoid terms in
+  // parallel, then accumulate each sum on one lane in the reference's order.
+  double* st_t = sortbuf + (size_t)(C_COUNT + S_T) * SP;
+  double* st_p = sortbuf + (size_t)(C_COUNT + S_POWER) * SP;
+  double* st_m = sortbuf + (size_t)(C_COUNT + S_MEMORY) * SP;
+  double* st_r = sortbuf + (size_t)(C_COUNT + S_REL) * SP;
+  double* term_p = sortbuf + (size_t)(C_COUNT + S_TERM_P) * SP;
+  double* term_m = sortbuf + (size_t)(C_COUNT + S_TERM_M) * SP;
+  __shared__ int anchor_idx;
+  if (threadIdx.x == 0) anchor_idx = 0x7fffffff;
+  __syncthreads();
+  for (int q = threadIdx.x; q < ncov; q += blockDim.x) {
+    st_t[q] = t[cb + q]; st_p[q] = T.power_w[cb + q]; st_m[q] = T.memory_power_w[cb + q];
+    if (T.sample_flags[cb + q] & PM_S_ENERGY_ANCHOR) atomicMin(&anchor_idx, q);
+  }
+  __syncthreads();
+  {
+    const int64_t anchor = anchor_idx == 0x7fffffff ? 0 : T.energy_int[cb + anchor_idx];
+    for (int q = threadIdx.x; q < ncov; q += blockDim.x) {
+      const uint16_t sf = T.sample_flags[cb + q];
+      double v;
+      if (sf & PM_S_ENERGY_INT) v = (double)(long long)((unsigned long long)T.energy_int[cb + q] - (unsigned long long)anchor);
+      else if (sf & PM_S_ENERGY_FLOAT) v = T.energy_float[cb + q] - (double)anchor;
+      else v = dnan();
+      st_r[q] = isfinite(v) ? v : dnan();
+    }
+  }
+  __syncthreads();
+  // Interior samples are covering indices [ia, ib): start < t < end.
+  const int ia = (int)(upper_bound(st_t, 0, ncov, start)), ib = (int)(lower_bound(st_t, 0, ncov, end));
+  const int nterms = ib > ia ? ib - ia + 1 : 1;
+  auto value_at = [&](const double* v, double x) -> double {
+    if (ncov <= 0 || x < st_t[0] || x > st_t[ncov - 1]) return dnan();
+    const int i = (int)lower_bound(st_t, 0, ncov, x);
+    if (st_t[i] == x) return v[i];
+    const double a = v[i - 1], b = v[i];
+    if (none(a) || none(b)) return dnan();
+    const double ratio = (x - st_t[i - 1]) / (st_t[i] - st_t[i - 1]);
+    return a + ratio * (b - a);
+  };
+  const double p0 = value_at(st_p, start), p1 = value_at(st_p, end);
+  const double m0 = value_at(st_m, start), m1 = value_at(st_m, end);
+  bool gap_p = false, gap_m = false;
+  for (int k = threadIdx.x; k < nterms; k += blockDim.x) {
+    // term k joins point k-1 and point k of [start, interior..., end]
+    const double ta = k == 0 ? start : st_t[ia + k - 1];
+    const double tb = k == nterms - 1 ? end : st_t[ia + k];
+    const double pa = k == 0 ? p0 : st_p[ia + k - 1], pb = k == nterms - 1 ? p1 : st_p[ia + k];
+    const double ma = k == 0 ? m0 : st_m[ia + k - 1], mb = k == nterms - 1 ? m1 : st_m[ia + k];
+    if (k < nterms - 1) { gap_p |= none(st_p[ia + k]); gap_m |= none(st_m[ia + k]); }
+    term_p[k] = (tb - ta) * (pa + pb) * 0.5;
+    term_m[k] = (tb - ta) * (ma + mb) * 0.5;
+  }
+  gap_p = __syncthreads_or(gap_p);
+  gap_m = __syncthreads_or(gap_m);
+  if (threadIdx.x == 0) {
+    double energy = dnan();
+    if (!none(p0) && !none(p1) && end > start && !gap_p) {
+      NeumaierSum sum;
+      for (int k = 0; k < nterms; ++k) sum.add(term_p[k]);
+      energy = sum.result();
+    }
     po[PM_PO_ENERGY_J] = energy;
     po[PM_PO_INTEGRATED_POWER_W] = none(energy) ? dnan() : energy / duration;
-  } else if (lane_id == 32) {
-    const double me = integrate(t, cb, ce, start, end, [&](int64_t i) { return T.memory_power_w[i]; });
+  } else if (threadIdx.x == 32) {
+    double me = dnan();
+    if (!none(m0) && !none(m1) && end > start && !gap_m) {
+      NeumaierSum sum;
+      for (int k = 0; k < nterms; ++k) sum.add(term_m[k]);
+      me = sum.result();
+    }
     po[PM_PO_MEMORY_ENERGY_J] = me;
     po[PM_PO_MEMORY_POWER_W] = none(me) ? dnan() : me / duration;
-  } else if (lane_id == 64) {
-    // Energy counter relative to the first exact-int reading in covering.
-    int64_t anchor = 0;
-    for (int64_t i = cb; i < ce; ++i) if (T.sample_flags[i] & PM_S_ENERGY_ANCHOR) { anchor = T.energy_int[i]; break; }
-    auto rel = [&](int64_t i) -> double {
-      const uint16_t sf = T.sample_flags[i];
-      double v;
-      if (sf & PM_S_ENERGY_INT) v = (double)(long long)((unsigned long long)T.energy_int[i] - (unsigned long long)anchor);
-      else if (sf & PM_S_ENERGY_FLOAT) v = T.energy_float[i] - (double)anchor;
-      else return dnan();
-      return isfinite(v) ? v : dnan();
-    };
-    const double c0 = interpolate(t, cb, ce, start, rel);
-    const double c1 = interpolate(t, cb, ce, end, rel);
+  } else if (threadIdx.x == 64) {
+    const double c0 = value_at(st_r, start), c1 = value_at(st_r, end);
     bool reset = false, have = false;
     double prev = 0.0;
-    for (int64_t i = cb; i < ce; ++i) {
-      const double v = rel(i);
+    for (int q = 0; q < ncov; ++q) {
+      const double v = st_r[q];
       if (none(v)) continue;
       if (have && v < prev) reset = true;
       prev = v; have = true;
     }
     double counter = dnan();
     if (!none(c0) && !none(c1)) {
-      if (reset || c1 < c0) S.pf[p] |= 1u << PM_PF_COUNTER_RESET;  // only lane 64 writes here now
+      if (reset || c1 < c0) S.pf[p] |= 1u << PM_PF_COUNTER_RESET;
       else counter = (c1 - c0) / 1000.0;
     }
     po[PM_PO_COUNTER_J] = counter;
@@ -365,16 +416,26 @@ __device__ void phase_stats(const pm_trials& T, const pm_policy& P, Shared& S, d
     po[PM_PO_SAMPLES] = nsel;
     po[PM_PO_SEL_LO] = (double)(lo - seg_b); po[PM_PO_SEL_HI] = (double)(hi - seg_b);
     po[PM_PO_COV_LO] = (double)(cb - seg_b); po[PM_PO_COV_HI] = (double)(ce - seg_b);
-    const double* gap = sortbuf + C_GAP * SP;
+    // A column that was not sorted holds one repeated value: its median,
+    // minimum and maximum are that value.
+    auto column_median = [&](int c) -> double {
+      const int n = S.nfin[c];
+      if (n == 0) return dnan();
+      if (S.cmin[c] == S.cmax[c]) return S.cmin[c];
+      return sorted_median(sortbuf + c * SP, n);
+    };
     const int ngap = S.nfin[C_GAP];
-    po[PM_PO_GAP_MEDIAN_S] = sorted_median(gap, ngap);
-    po[PM_PO_GAP_MAX_S] = ngap ? gap[ngap - 1] : dnan();
-    po[PM_PO_CHANGE_MEDIAN_S] = sorted_median(sortbuf + C_CHANGE * SP, S.nfin[C_CHANGE]);
+    po[PM_PO_GAP_MEDIAN_S] = column_median(C_GAP);
+    po[PM_PO_GAP_MAX_S] = ngap ? S.cmax[C_GAP] : dnan();
+    po[PM_PO_CHANGE_MEDIAN_S] = column_median(C_CHANGE);
     {
-      const double* pw = sortbuf + C_POWER * SP;
       const int n = S.nfin[C_POWER];
-      int distinct = 0;
-      for (int i = 0; i < n; ++i) distinct += (i == 0 || pw[i] != pw[i - 1]);
+      int distinct = n ? 1 : 0;
+      if (n > 1 && S.cmin[C_POWER] != S.cmax[C_POWER]) {
+        const double* pw = sortbuf + C_POWER * SP;
+        distinct = 0;
+        for (int i = 0; i < n; ++i) distinct += (i == 0 || pw[i] != pw[i - 1]);
+      }
       po[PM_PO_DISTINCT_POWER] = distinct;
     }
     const int stat_cols[7] = {C_GFX, C_SM, C_MEM, C_TEMP, C_PLIMIT, C_ENF, C_PSTATE};
@@ -382,11 +443,10 @@ __device__ void phase_stats(const pm_trials& T, const pm_policy& P, Shared& S, d
     const int min_slot[7] = {PM_PO_GFX_MIN, PM_PO_SM_MIN, PM_PO_MEM_MIN, PM_PO_TEMP_MIN, PM_PO_PLIMIT_MIN, PM_PO_ENF_MIN, PM_PO_PSTATE_MIN};
     const int max_slot[7] = {PM_PO_GFX_MAX, PM_PO_SM_MAX, PM_PO_MEM_MAX, PM_PO_TEMP_MAX, PM_PO_PLIMIT_MAX, PM_PO_ENF_MAX, PM_PO_PSTATE_MAX};
     for (int k = 0; k < 7; ++k) {
-      const double* v = sortbuf + stat_cols[k] * SP;
-      const int n = S.nfin[stat_cols[k]];
-      po[med_slot[k]] = sorted_median(v, n);
-      po[min_slot[k]] = n ? v[0] : dnan();
-      po[max_slot[k]] = n ? v[n - 1] : dnan();
+      const int c = stat_cols[k], n = S.nfin[c];
+      po[med_slot[k]] = column_median(c);
+      po[min_slot[k]] = n ? S.cmin[c] : dnan();
+      po[max_slot[k]] = n ? S.cmax[c] : dnan();
     }
     po[PM_PO_PLIMIT_FIN] = S.nfin[C_PLIMIT]; po[PM_PO_ENF_FIN] = S.nfin[C_ENF]; po[PM_PO_PSTATE_FIN] = S.nfin[C_PSTATE];
     // power_w: counter rate if present else trapezoid rate
@@ -396,7 +456,7 @@ __device__ void phase_stats(const pm_trials& T, const pm_policy& P, Shared& S, d
     const double minimum = idle ? P.min_idle_s : P.min_measure_s;
     if (duration + 1e-9 < minimum) f |= 1u << PM_PF_SHORT_PLATEAU;
     if (nsel < P.min_samples) f |= 1u << PM_PF_TOO_FEW_SAMPLES;
-    if (ngap && gap[ngap - 1] > P.max_sample_gap_s) f |= 1u << PM_PF_TELEMETRY_GAP;
+    if (ngap && S.cmax[C_GAP] > P.max_sample_gap_s) f |= 1u << PM_PF_TELEMETRY_GAP;
     if (none(energy)) f |= 1u << PM_PF_MISSING_POWER_COVERAGE;
     if (!none(counter) && !none(energy) && energy > 0) {
       const double d = fabs(counter - energy) / energy;
@@ -443,7 +503,7 @@ analyze_kernel(pm_trials T, pm_policy P, pm_trial_results R, int SP, double* gsc
   __shared__ Shared S;
   extern __shared__ double dyn[];
   const int trial = blockIdx.x;
-  double* sortbuf = gscratch ? gscratch + (size_t)blockIdx.x * C_COUNT * SP : dyn;
+  double* sortbuf = gscratch ? gscratch + (size_t)blockIdx.x * kTileColumns * SP : dyn;
   const double* ts = T.trial_scalars + (size_t)trial * PM_TS_COUNT;
   const uint32_t tflags = T.trial_flags[trial];
   const int wl = tflags & PM_T_WORKLOAD_MASK;
@@ -921,7 +981,7 @@ int launch_analyze(const pm_trials& T, const pm_policy& P, const pm_trial_result
                    double* gscratch, cudaStream_t stream, size_t* scratch_bytes_needed) {
   int SP = 32;
   while (SP < max_covering + 1) SP <<= 1;
-  const size_t smem = (size_t)C_COUNT * SP * sizeof(double);
+  const size_t smem = (size_t)kTileColumns * SP * sizeof(double);
   const bool use_global = smem > kSmemSortBytes;
   if (scratch_bytes_needed) *scratch_bytes_needed = use_global ? (size_t)T.n_trials * smem : 0;
   if (use_global && !gscratch) return 1;  // caller must supply scratch

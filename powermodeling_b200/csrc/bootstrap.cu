@@ -31,7 +31,7 @@ constexpr int kMtN = 624, kMtM = 397;
 constexpr int kHistMaxN = 7;            // multiset histogram path
 constexpr int kMaxBins = 1716;          // C(13, 7)
 constexpr int kDirectMaxN = 128;        // direct path limit
-constexpr int kRing = 2 * kMtN;
+constexpr int kRing = 3 * kMtN;      // block b in slot b % 3: the two newest stay readable
 
 __constant__ uint32_t c_mt_init[kMtN];  // init_genrand(19650218), filled by the host
 __constant__ uint32_t c_binom[16][16];  // C(a, b)
@@ -54,42 +54,45 @@ __device__ void seed_state(uint32_t* mt, uint64_t seed) {
   uint32_t key[2] = {(uint32_t)seed, (uint32_t)(seed >> 32)};
   const int key_len = (seed >> 32) ? 2 : 1;
   int i = 1, j = 0;
+  uint32_t prev = mt[0];
   for (int k = kMtN; k; --k) {
-    mt[i] = (mt[i] ^ ((mt[i - 1] ^ (mt[i - 1] >> 30)) * 1664525u)) + key[j] + (uint32_t)j;
+    prev = (mt[i] ^ ((prev ^ (prev >> 30)) * 1664525u)) + key[j] + (uint32_t)j;
+    mt[i] = prev;
     ++i; ++j;
-    if (i >= kMtN) { mt[0] = mt[kMtN - 1]; i = 1; }
+    if (i >= kMtN) { mt[0] = prev; i = 1; }
     if (j >= key_len) j = 0;
   }
   for (int k = kMtN - 1; k; --k) {
-    mt[i] = (mt[i] ^ ((mt[i - 1] ^ (mt[i - 1] >> 30)) * 1566083941u)) - (uint32_t)i;
+    prev = (mt[i] ^ ((prev ^ (prev >> 30)) * 1566083941u)) - (uint32_t)i;
+    mt[i] = prev;
     ++i;
-    if (i >= kMtN) { mt[0] = mt[kMtN - 1]; i = 1; }
+    if (i >= kMtN) { mt[0] = prev; i = 1; }
   }
   mt[0] = 0x80000000u;
 }
 
-// One full twist of the state by the CTA (three dependency segments), then
-// the 624 tempered outputs land in ring[dst .. dst+624).
-__device__ void twist_block(uint32_t* mt, uint32_t* ring, int dst) {
-  constexpr int A = kMtN - kMtM;          // 227: mt[i+397] still old
-  uint32_t v[3]; int idx[3]; int cnt = 0;
-  for (int i = threadIdx.x; i < A; i += blockDim.x) { v[cnt] = twist_one(mt[i], mt[i + 1], mt[i + kMtM]); idx[cnt++] = i; }
+// One twist of the MT19937 state by the CTA.  `src` holds the current
+// state and `dst` receives the next one (ping-pong buffers), so each of the
+// three dependency segments needs a single barrier: segment 1 (i < 227)
+// reads only old words, segments 2 and 3 read new words of the segment
+// before.  Outputs are tempered as they are produced, into ring[base + i].
+__device__ __forceinline__ void twist_block(const uint32_t* src, uint32_t* dst, uint32_t* ring, int base) {
+  constexpr int A = kMtN - kMtM;          // 227
+  for (int i = threadIdx.x; i < A; i += blockDim.x) {
+    const uint32_t v = twist_one(src[i], src[i + 1], src[i + kMtM]);
+    dst[i] = v; ring[base + i] = temper(v);
+  }
   __syncthreads();
-  for (int c = 0; c < cnt; ++c) mt[idx[c]] = v[c];
+  for (int i = A + threadIdx.x; i < 2 * A; i += blockDim.x) {
+    const uint32_t v = twist_one(src[i], src[i + 1], dst[i - A]);
+    dst[i] = v; ring[base + i] = temper(v);
+  }
   __syncthreads();
-  cnt = 0;
-  for (int i = A + threadIdx.x; i < 2 * A; i += blockDim.x) { v[cnt] = twist_one(mt[i], mt[i + 1], mt[i - A]); idx[cnt++] = i; }
-  __syncthreads();
-  for (int c = 0; c < cnt; ++c) mt[idx[c]] = v[c];
-  __syncthreads();
-  cnt = 0;
-  for (int i = 2 * A + threadIdx.x; i < kMtN - 1; i += blockDim.x) { v[cnt] = twist_one(mt[i], mt[i + 1], mt[i - A]); idx[cnt++] = i; }
-  __syncthreads();
-  for (int c = 0; c < cnt; ++c) mt[idx[c]] = v[c];
-  __syncthreads();
-  if (threadIdx.x == 0) mt[kMtN - 1] = twist_one(mt[kMtN - 1], mt[0], mt[kMtM - 1]);
-  __syncthreads();
-  for (int i = threadIdx.x; i < kMtN; i += blockDim.x) ring[dst + i] = temper(mt[i]);
+  for (int i = 2 * A + threadIdx.x; i < kMtN; i += blockDim.x) {
+    const uint32_t v = i < kMtN - 1 ? twist_one(src[i], src[i + 1], dst[i - A])
+                                    : twist_one(src[kMtN - 1], dst[0], dst[kMtM - 1]);
+    dst[i] = v; ring[base + i] = temper(v);
+  }
   __syncthreads();
 }
 
@@ -100,18 +103,19 @@ __device__ __forceinline__ int draw_index(uint32_t w0, uint32_t w1, double n) {
 
 // Rank of a non-decreasing n-tuple over [0, n) among multisets (combinatorial
 // number system on b_i = a_i + i, strictly increasing in [0, 2n-1)).
-__device__ __forceinline__ int multiset_rank(const int* a, int n) {
+// `binom` is a shared-memory copy of c_binom: lookups here are thread-divergent.
+__device__ __forceinline__ int multiset_rank(const int* a, int n, const uint32_t (*binom)[16]) {
   int r = 0;
-  for (int i = 0; i < n; ++i) r += c_binom[a[i] + i][i + 1];
+  for (int i = 0; i < n; ++i) r += binom[a[i] + i][i + 1];
   return r;
 }
-__device__ void multiset_unrank(int r, int n, int* a) {
+__device__ void multiset_unrank(int r, int n, int* a, const uint32_t (*binom)[16]) {
   // Largest b_{i} with C(b_i, i+1) <= r, from the top index down.
   int top = 2 * n - 2;
   for (int i = n - 1; i >= 0; --i) {
     int b = top;
-    while (c_binom[b][i + 1] > (uint32_t)r) --b;
-    r -= (int)c_binom[b][i + 1];
+    while (binom[b][i + 1] > (uint32_t)r) --b;
+    r -= (int)binom[b][i + 1];
     a[i] = b - i;
     top = b - 1;
   }
@@ -132,10 +136,12 @@ struct BootSmem {
 
 __global__ void __launch_bounds__(kBootThreads) bootstrap_kernel(BootArgs A) {
   extern __shared__ __align__(16) unsigned char dsm[];
-  __shared__ uint32_t mt[kMtN];
+  __shared__ uint32_t mt[2][kMtN];
   __shared__ uint32_t ring[kRing];
   __shared__ uint32_t hist[kMaxBins];
+  __shared__ uint32_t binom[16][16];
   __shared__ int n_list[kDirectMaxN + 1];
+  for (int i = threadIdx.x; i < 256; i += blockDim.x) binom[i >> 4][i & 15] = c_binom[i >> 4][i & 15];
   __shared__ int n_distinct;
   const int g = blockIdx.x;
   const int m0 = A.offsets[g], m1 = A.offsets[g + 1];
@@ -200,36 +206,48 @@ __global__ void __launch_bounds__(kBootThreads) bootstrap_kernel(BootArgs A) {
     const int n = n_list[d];
     const bool histogram = n <= kHistMaxN;
     if (!histogram && n > kDirectMaxN) continue;   // host rejects this before launch
-    const int nbins = histogram ? (int)c_binom[2 * n - 1][n] : 0;
+    const int nbins = histogram ? (int)binom[2 * n - 1][n] : 0;
     for (int i = threadIdx.x; i < kMaxBins; i += blockDim.x) hist[i] = 0;
-    if (threadIdx.x == 0) seed_state(mt, A.seeds[g]);
+    if (threadIdx.x == 0) seed_state(mt[0], A.seeds[g]);
     __syncthreads();
     const double nd = (double)n;
-    const long long words = 2LL * n * B;
-    const long long blocks = (words + kMtN - 1) / kMtN;
-    long long next_r = 0;
+    const uint32_t words_per_draw = 2u * (uint32_t)n;          // 2nB < 2^32 (B <= 2^24, n <= 128)
+    const uint32_t blocks = (uint32_t)((2ull * n * B + kMtN - 1) / kMtN);
+    uint32_t next_r = 0;
     uint8_t* stream = A.scratch ? A.scratch + (size_t)g * B * kDirectMaxN : nullptr;
-    for (long long blk = 0; blk < blocks; ++blk) {
-      twist_block(mt, ring, (int)(blk & 1) * kMtN);
-      const long long avail = (blk + 1) * kMtN;               // words generated so far
-      long long r_end = avail / (2LL * n);
-      if (r_end > B) r_end = B;
-      for (long long r = next_r + threadIdx.x; r < r_end; r += blockDim.x) {
-        const long long w = 2LL * n * r;
+    int slot = 0;                                               // ring slot of the current block
+    for (uint32_t blk = 0; blk < blocks; ++blk) {
+      twist_block(mt[blk & 1], mt[(blk & 1) ^ 1], ring, slot * kMtN);
+      // Words [first, avail) are readable: the previous block and this one.
+      const uint32_t avail = (blk + 1) * (uint32_t)kMtN;
+      const uint32_t first = blk ? avail - 2 * kMtN : 0;
+      const int first_slot = blk ? (slot + 2) % 3 : 0;          // slot of word `first`
+      uint32_t r_end = avail / words_per_draw;
+      if (r_end > (uint32_t)B) r_end = B;
+      for (uint32_t r = next_r + threadIdx.x; r < r_end; r += blockDim.x) {
+        uint32_t pos = first_slot * kMtN + (r * words_per_draw - first);
+        if (pos >= (uint32_t)kRing) pos -= kRing;
         if (histogram) {
           int t[kHistMaxN];
-          for (int j = 0; j < n; ++j)
-            t[j] = draw_index(ring[(w + 2 * j) % kRing], ring[(w + 2 * j + 1) % kRing], nd);
+          for (int j = 0; j < n; ++j) {
+            const uint32_t w0 = ring[pos]; if (++pos == (uint32_t)kRing) pos = 0;
+            const uint32_t w1 = ring[pos]; if (++pos == (uint32_t)kRing) pos = 0;
+            t[j] = draw_index(w0, w1, nd);
+          }
           for (int i = 1; i < n; ++i) { int v = t[i], k = i - 1; while (k >= 0 && t[k] > v) { t[k + 1] = t[k]; --k; } t[k + 1] = v; }
-          atomicAdd(&hist[multiset_rank(t, n)], 1u);
+          atomicAdd(&hist[multiset_rank(t, n, binom)], 1u);
         } else {
-          for (int j = 0; j < n; ++j)
-            stream[(size_t)r * n + j] = (uint8_t)draw_index(ring[(w + 2 * j) % kRing], ring[(w + 2 * j + 1) % kRing], nd);
+          for (int j = 0; j < n; ++j) {
+            const uint32_t w0 = ring[pos]; if (++pos == (uint32_t)kRing) pos = 0;
+            const uint32_t w1 = ring[pos]; if (++pos == (uint32_t)kRing) pos = 0;
+            stream[(size_t)r * n + j] = (uint8_t)draw_index(w0, w1, nd);
+          }
         }
       }
       next_r = r_end;
-      __syncthreads();
+      slot = slot == 2 ? 0 : slot + 1;
     }
+    __syncthreads();
     if (histogram) {
       // Per metric: fold multiset bins into median rank pairs, then select.
       for (int m = threadIdx.x; m < M; m += blockDim.x) {
@@ -248,7 +266,7 @@ __global__ void __launch_bounds__(kBootThreads) bootstrap_kernel(BootArgs A) {
           const uint32_t c = hist[bin];
           if (!c) continue;
           int ms[kHistMaxN], rk[kHistMaxN];
-          multiset_unrank(bin, n, ms);
+          multiset_unrank(bin, n, ms, binom);
           for (int i = 0; i < n; ++i) rk[i] = rank_of[ms[i]];
           for (int i = 1; i < n; ++i) { int x = rk[i], k = i - 1; while (k >= 0 && rk[k] > x) { rk[k + 1] = rk[k]; --k; } rk[k + 1] = x; }
           const int ra = (n & 1) ? rk[n / 2] : rk[n / 2 - 1];
@@ -340,24 +358,32 @@ __global__ void __launch_bounds__(kBootThreads) bootstrap_kernel(BootArgs A) {
 
 // Raw index stream (diagnostic): out[r*n + j] for one seed, by one CTA.
 __global__ void resample_indices_kernel(uint64_t seed, int n, int B, int32_t* out) {
-  __shared__ uint32_t mt[kMtN];
+  __shared__ uint32_t mt[2][kMtN];
   __shared__ uint32_t ring[kRing];
-  if (threadIdx.x == 0) seed_state(mt, seed);
+  if (threadIdx.x == 0) seed_state(mt[0], seed);
   __syncthreads();
-  const long long words = 2LL * n * B;
-  const long long blocks = (words + kMtN - 1) / kMtN;
-  long long next_r = 0;
-  for (long long blk = 0; blk < blocks; ++blk) {
-    twist_block(mt, ring, (int)(blk & 1) * kMtN);
-    long long r_end = (blk + 1) * kMtN / (2LL * n);
-    if (r_end > B) r_end = B;
-    for (long long r = next_r + threadIdx.x; r < r_end; r += blockDim.x) {
-      const long long w = 2LL * n * r;
-      for (int j = 0; j < n; ++j)
-        out[r * n + j] = draw_index(ring[(w + 2 * j) % kRing], ring[(w + 2 * j + 1) % kRing], (double)n);
+  const uint32_t words_per_draw = 2u * (uint32_t)n;
+  const uint32_t blocks = (uint32_t)((2ull * n * B + kMtN - 1) / kMtN);
+  uint32_t next_r = 0;
+  int slot = 0;
+  for (uint32_t blk = 0; blk < blocks; ++blk) {
+    twist_block(mt[blk & 1], mt[(blk & 1) ^ 1], ring, slot * kMtN);
+    const uint32_t avail = (blk + 1) * (uint32_t)kMtN;
+    const uint32_t first = blk ? avail - 2 * kMtN : 0;
+    const int first_slot = blk ? (slot + 2) % 3 : 0;
+    uint32_t r_end = avail / words_per_draw;
+    if (r_end > (uint32_t)B) r_end = B;
+    for (uint32_t r = next_r + threadIdx.x; r < r_end; r += blockDim.x) {
+      uint32_t pos = first_slot * kMtN + (r * words_per_draw - first);
+      if (pos >= (uint32_t)kRing) pos -= kRing;
+      for (int j = 0; j < n; ++j) {
+        const uint32_t w0 = ring[pos]; if (++pos == (uint32_t)kRing) pos = 0;
+        const uint32_t w1 = ring[pos]; if (++pos == (uint32_t)kRing) pos = 0;
+        out[(size_t)r * n + j] = draw_index(w0, w1, (double)n);
+      }
     }
     next_r = r_end;
-    __syncthreads();
+    slot = slot == 2 ? 0 : slot + 1;
   }
 }
 

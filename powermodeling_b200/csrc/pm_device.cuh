@@ -62,21 +62,22 @@ __device__ __forceinline__ void insertion_sort(double* a, int n) {
   }
 }
 
-// CTA-wide ascending bitonic sort of `count` arrays of length P (a power of
-// two) stored back to back at `base`.  +inf pads and marks excluded values.
-__device__ inline void bitonic_sort_arrays(double* base, int count, int P) {
+// CTA-wide ascending bitonic sort of the arrays base + cols[c]*stride
+// (c < ncols), each of length P (a power of two, P <= stride).  +inf pads
+// and marks excluded values so finite values lead.
+__device__ inline void bitonic_sort_columns(double* base, int stride, const int* cols, int ncols, int P) {
   const int half = P >> 1;
-  const int pairs = half * count;
+  const int lg_half = 31 - __clz(half);
+  const int pairs = half * ncols;
   for (int k = 2; k <= P; k <<= 1) {
     for (int j = k >> 1; j > 0; j >>= 1) {
       for (int q = threadIdx.x; q < pairs; q += blockDim.x) {
-        const int a = q / half, p = q - a * half;
-        const int i = 2 * j * (p / j) + (p % j);
-        const int l = i + j;
-        double* v = base + (size_t)a * P;
+        const int a = q >> lg_half, p = q & (half - 1);
+        const int i = ((p & ~(j - 1)) << 1) | (p & (j - 1));
+        double* v = base + (size_t)cols[a] * stride;
         const bool ascending = (i & k) == 0;
-        const double x = v[i], y = v[l];
-        if ((x > y) == ascending) { v[i] = y; v[l] = x; }
+        const double x = v[i], y = v[i + j];
+        if ((x > y) == ascending) { v[i] = y; v[i + j] = x; }
       }
       __syncthreads();
     }

@@ -1,0 +1,67 @@
+// Workload kernels of the measured arms (declarations and shared device helpers).
+//
+// The deterministic word fill, the per-thread read-sum semantics, the
+// four-stream write/copy streams, the integer issue loop, the dependent
+// chase and the SFU recurrence reproduce the reference's observable results
+// (cuda/gpu_bench.cu:277-473, cuda/sfu.cuh:43-117) so checksums and terminal
+// indices compare bit for bit; the vector (16-byte) read/copy and the
+// line-granular chase are additional B200 modes with their own version tags.
+#pragma once
+#include <cstdint>
+#include <cuda_runtime.h>
+
+namespace pm {
+
+constexpr unsigned kSmSlots = 4096;          // per-SM admission/telemetry counters
+
+// splitmix64 finaliser (Steele, Lea & Flood 2014) truncated to 32 bits: the
+// deterministic payload of every memory buffer (gpu_bench.cu:277-282).
+__host__ __device__ __forceinline__ uint32_t random_word(uint64_t x) {
+  x += 0x9e3779b97f4a7c15ULL;
+  x = (x ^ (x >> 30)) * 0xbf58476d1ce4e5b9ULL;
+  x = (x ^ (x >> 27)) * 0x94d049bb133111ebULL;
+  return uint32_t(x ^ (x >> 31));
+}
+
+// First operand of an SFU chain: a [0.5, 1) mantissa from the lane hash (sfu.cuh:73-75).
+__host__ __device__ __forceinline__ uint32_t sfu_initial_bits(uint64_t lane, uint64_t seed, int chain) {
+  return (random_word(lane ^ seed ^ (uint64_t(chain + 1) * 0x9e3779b97f4a7c15ULL)) & 0x007fffffU) | 0x3f000000U;
+}
+
+// Cache policies of the read arms.
+enum ReadPolicy { RP_CA = 0, RP_CG = 1, RP_CS = 2 };
+enum SfuOp { SFU_EX2 = 0, SFU_TANH = 1, SFU_RSQRT = 2, SFU_RCP = 3, SFU_LG2 = 4, SFU_SQRT = 5 };
+
+struct Admission {
+  const unsigned char* mask;      // kSmSlots bytes, 1 = admit blocks dispatched to that SM
+  bool filtered;
+  unsigned long long* blocks_per_sm;
+};
+
+// Host launchers (workloads.cu).  All return cudaGetLastError() of the launch.
+cudaError_t launch_fill_words(uint32_t* data, uint64_t n, uint64_t seed, int sms, cudaStream_t s);
+cudaError_t launch_fill_halves(void* data, uint64_t n, uint64_t seed, int uniform_pm1, int sms, cudaStream_t s);
+cudaError_t launch_read_scalar(int policy, bool l1, const uint32_t* in, uint32_t* sink, uint64_t words, uint64_t slice,
+                               uint64_t stride, uint64_t iterations, int blocks, int threads, Admission adm, cudaStream_t s);
+cudaError_t launch_read_vector(int policy, const uint32_t* in, uint32_t* sink, uint64_t quads, uint64_t stride,
+                               uint64_t iterations, int blocks, int threads, Admission adm, cudaStream_t s);
+cudaError_t launch_write_copy_scalar(bool copy, const uint32_t* in, uint32_t* out, uint32_t* sink, uint64_t words,
+                                     uint64_t stride, uint64_t iterations, int blocks, int threads, Admission adm,
+                                     cudaStream_t s);
+cudaError_t launch_copy_vector(const uint32_t* in, uint32_t* out, uint32_t* sink, uint64_t quads, uint64_t stride,
+                               uint64_t iterations, int blocks, int threads, Admission adm, cudaStream_t s);
+cudaError_t launch_control(uint32_t* sink, uint64_t iterations, int blocks, int threads, Admission adm, cudaStream_t s);
+cudaError_t launch_chase_words(const uint32_t* links, uint32_t* sink, uint64_t words, uint64_t iterations, uint64_t nonce,
+                               int blocks, int threads, Admission adm, unsigned long long* cycles,
+                               unsigned long long* loads, cudaStream_t s);
+cudaError_t launch_chase_lines(const uint64_t* lines, uint64_t* terminal, uint64_t nodes, uint64_t iterations,
+                               uint64_t nonce, int blocks, int threads, Admission adm, unsigned long long* cycles,
+                               unsigned long long* loads, cudaStream_t s);
+cudaError_t launch_sfu(int op, bool control, int chains, uint32_t* sink, uint64_t lanes, uint64_t iterations,
+                       uint64_t seed, int blocks, int threads, cudaStream_t s);
+cudaError_t launch_sfu_check(int op, uint32_t* sample, uint64_t lanes, uint64_t seed, int chains, cudaStream_t s);
+cudaError_t sfu_attributes(int op, bool control, int chains, cudaFuncAttributes* attr);
+const void* kernel_symbol(const char* name, int a, int b, int c);
+const void* sfu_kernel_handle(int op, bool control, int chains);
+
+}  // namespace pm
