@@ -238,6 +238,26 @@ int pm_powerbench(int argc, const char* const* argv, pm_line_cb cb, void* user);
 int pm_tensor_probe(int accumulators, uint64_t iterations, int uniform, uint64_t seed, float* out,
                     size_t out_count, uint16_t* a_out, uint16_t* b_out);
 
+/*
+ * pm_group_bootstrap_device for callers that cannot allocate device memory
+ * (a process whose own pool owns the whole device, a runtime that forbids
+ * foreign allocations, a service that must fix the library's footprint in
+ * advance).  No counterpart in the reference.  It calls no cudaMalloc,
+ * cudaFree or allocating library routine: the index streams of groups with
+ * more than seven members live in one fixed array inside this library, of
+ * pm_bootstrap_static_scratch_capacity() bytes (32 MiB), which every GPU that
+ * loads the library holds until the process exits.  A job needing more
+ * (n_groups x resamples x 128 bytes when max_members > 7) is rejected with
+ * PM_E_LIMIT.  Inputs and outputs are the caller's device buffers, as for
+ * pm_group_bootstrap_device; job->max_members must bound every group.
+ * The first call on a device looks up the array's device address and uploads
+ * the generator constants; make that first call before any stream capture.
+ * All calls share the array (nothing in it needs to start at zero), so calls
+ * whose kernels overlap on the GPU race: serialize them on one stream.
+ */
+size_t pm_bootstrap_static_scratch_capacity(void);
+int pm_group_bootstrap_device_static(const pm_bootstrap_job* job, void* stream);
+
 /* Raw resample index stream of random.Random(seed).choices(range(n), k=n),
  * repeated `resamples` times: out[r*n + j] (host buffer). Pins the generator. */
 int pm_resample_indices(uint64_t seed, int32_t n, int32_t resamples, int32_t* out);

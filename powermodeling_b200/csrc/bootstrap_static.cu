@@ -1,0 +1,89 @@
+// Group bootstrap for callers that must not allocate device memory.
+//
+// Some callers cannot let a library call cudaMalloc: a host process that has
+// already handed every byte of the device to its own memory pool, an
+// allocator-owning runtime that forbids foreign allocations on its device,
+// or a service that must bound the library's footprint in advance.  For
+// them pm_group_bootstrap_device_static runs the same bootstrap kernel as
+// pm_group_bootstrap_device, but the index streams of groups with more than
+// seven members live in a fixed array compiled into this library
+// (kStaticStreamBytes, held by every GPU that loads the library until the
+// process exits) instead of a caller-provided scratch buffer.  Inputs and
+// outputs are still the caller's device buffers.
+#include <cuda_runtime.h>
+
+#include <cstdint>
+#include <mutex>
+
+#include "pmb200.h"
+#include "pm_capi.h"
+
+namespace pm {
+
+int launch_bootstrap(const BootArgs& A, cudaStream_t stream);
+int prepare_bootstrap_constants(int device);
+size_t bootstrap_scratch_bytes(int n_groups, int max_members, int resamples);
+
+namespace {
+
+// Index streams: groups x resamples x 128 bytes at most; 32 MiB covers, for
+// example, 26 groups of 8 or more members at 10 000 resamples.
+constexpr size_t kStaticStreamBytes = size_t(32) << 20;
+static __device__ __align__(256) uint8_t g_static_streams[kStaticStreamBytes];
+
+// Device address of g_static_streams per device.  In host code the symbol
+// name is only a stand-in; the address must come from cudaGetSymbolAddress
+// with that device current.
+void* g_static_address[kMaxDevices] = {};
+std::mutex g_static_lock;
+
+}  // namespace
+}  // namespace pm
+
+using namespace pm;
+
+extern "C" size_t pm_bootstrap_static_scratch_capacity(void) { return kStaticStreamBytes; }
+
+extern "C" int pm_group_bootstrap_device_static(const pm_bootstrap_job* job, void* stream) {
+  if (!job) return fail(PM_E_INVALID, "pm_group_bootstrap_device_static: NULL job");
+  if (job->n_groups < 0 || job->n_metrics <= 0 || job->n_metrics > kMaxMetrics || job->n_members < 0)
+    return fail(PM_E_INVALID, "pm_group_bootstrap_device_static: bad sizes");
+  if (job->resamples < 40 || job->resamples > (1 << 24))
+    return fail(PM_E_INVALID, "pm_group_bootstrap_device_static: resamples must be in [40, 2^24]");
+  if (job->max_members < 0 || job->max_members > kMaxGroupMembers)
+    return fail(PM_E_LIMIT, "pm_group_bootstrap_device_static: max_members %d outside [0, %d]", job->max_members,
+                kMaxGroupMembers);
+  if (!job->values || !job->group_offsets || !job->seeds || !job->medians || !job->ci_lo || !job->ci_hi)
+    return fail(PM_E_INVALID, "pm_group_bootstrap_device_static: a job array is NULL");
+  const size_t need = bootstrap_scratch_bytes(job->n_groups, job->max_members, job->resamples);
+  if (need > kStaticStreamBytes)
+    return fail(PM_E_LIMIT,
+                "pm_group_bootstrap_device_static: %d groups of up to %d members at %d resamples need %zu bytes of "
+                "index streams; the fixed array holds %zu (use pm_group_bootstrap_device with your own scratch)",
+                job->n_groups, job->max_members, job->resamples, need, kStaticStreamBytes);
+  int device = 0, rc = current_device(&device);
+  if (rc) return rc;
+  void* scratch = nullptr;
+  {
+    std::lock_guard<std::mutex> guard(g_static_lock);
+    if (!g_static_address[device]) {
+      // Once per device, with that device current: the array's device address.
+      cudaError_t e = cudaGetSymbolAddress(&g_static_address[device], g_static_streams);
+      if (e != cudaSuccess) {
+        g_static_address[device] = nullptr;
+        return cuda_fail(e, "cudaGetSymbolAddress(g_static_streams)");
+      }
+    }
+    scratch = g_static_address[device];
+  }
+  if (prepare_bootstrap_constants(device)) return fail(PM_E_CUDA, "bootstrap constants upload failed");
+  // Nothing in the array must start at zero: each launch writes a group's
+  // stream completely before it reads it back.
+  BootArgs A{job->n_groups, job->n_metrics, job->resamples, job->max_members, job->values, job->group_offsets,
+             job->member_rows, job->member_valid, job->seeds, job->medians, job->ci_lo, job->ci_hi,
+             need ? static_cast<uint8_t*>(scratch) : nullptr};
+  launch_bootstrap(A, static_cast<cudaStream_t>(stream));
+  cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) return cuda_fail(e, "bootstrap_kernel launch");
+  return PM_OK;
+}
