@@ -49,7 +49,7 @@ def measured_peaks() -> dict:
 class ClockSampler:
     QUERY = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
-             "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+             "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap,clocks.mem")
 
     def __init__(self, index: int):
         self.index, self.proc, self.path = index, None, None
@@ -69,11 +69,15 @@ class ClockSampler:
         self.proc.terminate()
         self.proc.wait(timeout=10)
         rows = [line.split(", ") for line in self.path.read_text().splitlines() if line.strip()]
-        sm = [float(r[1]) for r in rows if len(r) >= 9 and r[1].replace(".", "").isdigit()]
-        mx = [float(r[2]) for r in rows if len(r) >= 9 and r[2].replace(".", "").isdigit()]
+        sm = [float(r[1]) for r in rows if len(r) >= 10 and r[1].replace(".", "").isdigit()]
+        mx = [float(r[2]) for r in rows if len(r) >= 10 and r[2].replace(".", "").isdigit()]
+        mem = [float(r[9]) for r in rows if len(r) >= 10 and r[9].strip().replace(".", "").isdigit()]
+        power = [float(r[3]) for r in rows if len(r) >= 10 and r[3].replace(".", "").isdigit()]
         names = ("hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap")
-        reasons = sorted({name for r in rows if len(r) >= 9 for name, v in zip(names, r[5:9]) if v.strip() == "Active"})
+        reasons = sorted({name for r in rows if len(r) >= 10 for name, v in zip(names, r[5:9]) if v.strip() == "Active"})
         return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": max(mx) if mx else None,
+                "mem_mhz": statistics.median(mem) if mem else None,
+                "power_w_median": statistics.median(power) if power else None,
                 "reasons": reasons, "samples": len(rows)}
 
 
@@ -232,7 +236,76 @@ def run_b200(args, rank: int, world: int) -> dict | None:
             "roofline": roofline, "clocks": clock_info}
     if world == 1 and not args.no_cpu_baseline:
         line["cpu_baseline"] = cpu_baseline(records, policy)
+    if not args.no_arms and world == 1:
+        line["arms"] = run_arms(local, peaks)
     return line
+
+
+# --------------------------------------------------------------------------- workload arms
+ARM_QUICK = ["--seconds", "5", "--warmup-seconds", "0", "--idle-seconds", "0", "--warmup-batches", "2"]
+
+
+def _arm(args):
+    from powermodeling_b200 import powerbench
+    records = powerbench.run(args)
+    device = next(r for r in records if r["type"] == "device")
+    return device, next(r for r in records if r["type"] == "result")
+
+
+def run_arms(local: int, peaks: dict) -> dict:
+    """HBM read/copy, tcgen05 tensor, cuBLAS GEMM and SFU arms through the powerbench engine."""
+    sms = 148
+    out = {}
+    clocks = ClockSampler(local)
+    clocks.start()
+    hbm = ["--workload", "hbm", "--memory-vector-bytes", "16", "--read-cache-policy", "cs", "--blocks", str(sms * 8),
+           "--threads", "256", "--working-set-bytes", str(4 << 30), "--iterations", "1024",
+           "--batch-launches", "8", "--fixed-batches", "6", *ARM_QUICK]
+    device, r = _arm(hbm)
+    sms = device["sm_count"]
+    bus = device["memory_bus_width_bits"]
+    out["hbm_read"] = {"gbs": r["throughput_bytes_s"] / 1e9, "bytes": r["logical_bytes"], "duration_s": r["duration_s"],
+                       "validation": r["memory_read_validation"]["status"], "config": "16 B loads (.cs), 4 GiB, grid 148x8x256"}
+    _, r = _arm(["--workload", "hbm", "--access", "copy", "--memory-vector-bytes", "16", "--blocks", str(sms * 8),
+                 "--threads", "256", "--working-set-bytes", str(4 << 30), "--iterations", "512", "--batch-launches", "8",
+                 "--fixed-batches", "6", *ARM_QUICK])
+    out["hbm_copy"] = {"gbs": r["throughput_bytes_s"] / 1e9, "config": "16 B load+store, 4 GiB, grid 148x8x256"}
+    tensor = {}
+    for acc in (1, 2, 4, 8):
+        _, r = _arm(["--workload", "tensor", "--blocks", str(sms), "--threads", "128", "--iterations", "8192",
+                     "--tensor-accumulators", str(acc), "--batch-launches", "4", "--fixed-batches", "3", *ARM_QUICK])
+        tensor[str(acc)] = {"tflops": r["throughput_ops_s"] / 1e12, "tile_n": r["tensor_tile_n"],
+                            "timeouts": r["tensor_status"]["bounded_wait_timeouts"]}
+    out["tensor_tcgen05"] = tensor
+    _, r = _arm(["--workload", "gemm", "--gemm-m", "8192", "--gemm-n", "8192", "--gemm-k", "8192", "--batch-launches", "4",
+                 "--fixed-batches", "3", *ARM_QUICK])
+    out["gemm_cublas_8192"] = {"tflops": r["throughput_ops_s"] / 1e12}
+    _, r = _arm(["--workload", "sfu_ex2", "--grid-mode", "fixed", "--blocks", str(sms * 8), "--threads", "256",
+                 "--sfu-lanes", str(sms * 8 * 256), "--sfu-chains", "4", "--iterations", "65536", "--batch-launches", "1",
+                 "--fixed-batches", "4", *ARM_QUICK])
+    out["sfu_ex2"] = {"ops_s": r["throughput_ops_s"], "checksum": r["checksum"]}
+    clock = clocks.stop()
+    mem_mhz = clock.get("mem_mhz") or device["nominal_max_memory_clock_khz"] / 1e3
+    theory = 2 * mem_mhz * 1e6 * bus / 8 / 1e9
+    hbm_peak = peaks.get("hbm_gbs", 6650.0)
+    for key in ("hbm_read", "hbm_copy"):
+        out[key]["frac_of_measured_copy_peak"] = out[key]["gbs"] / hbm_peak
+        out[key]["frac_of_clock_bus_theory"] = out[key]["gbs"] / theory
+    out["hbm_theory_gbs"] = theory
+    sm_mhz = clock.get("sm_mhz") or 1965.0
+    dense_peak = 8192 * sms * sm_mhz * 1e6 / 1e12
+    best = max(v["tflops"] for v in tensor.values())
+    out["tensor_peak_at_clock_tflops"] = dense_peak
+    out["tensor_best_frac_of_dense_clock_peak"] = best / dense_peak
+    out["tensor_best_frac_of_measured_bf16_gemm"] = best / peaks.get("bf16_tflops", 1590.0)
+    out["sfu_ex2"]["ops_per_sm_per_clock"] = out["sfu_ex2"]["ops_s"] / (sms * sm_mhz * 1e6)
+    out["clocks"] = clock
+    return out
+
+
+# DRAM bytes (read + write) per launch from one ncu capture of the same
+# workload (profiles/analysis_sweep_64x4_B10000.md); None where none was taken.
+NCU_TRAFFIC_BYTES = {"analyze_kernel": 19_193_856, "bootstrap_kernel": None}
 
 
 def roofline_entry(dominant, a_ms, b_ms, in_bytes, out_bytes, G, M, packed, peaks, resamples):
@@ -241,13 +314,13 @@ def roofline_entry(dominant, a_ms, b_ms, in_bytes, out_bytes, G, M, packed, peak
     if dominant == "analyze_kernel":
         achieved = (in_bytes + out_bytes) / (a_ms / 1e3) / 1e9
         return {"kernel": dominant, "bound": "hbm", "achieved": achieved, "peak": hbm, "unit": "GB/s",
-                "frac": achieved / hbm, "traffic": None, "peak_source": src,
+                "frac": achieved / hbm, "traffic": NCU_TRAFFIC_BYTES["analyze_kernel"], "peak_source": src,
                 "algorithmic_bytes": in_bytes + out_bytes}
     # The bootstrap kernel moves a few KB; its bound is the MT19937 stream (2 words per draw).
     words = 2 * 4 * RESAMPLES * G
     achieved = words * 4 / (b_ms / 1e3) / 1e9
     return {"kernel": dominant, "bound": "hbm", "achieved": achieved, "peak": hbm, "unit": "GB/s",
-            "frac": achieved / hbm, "traffic": None, "peak_source": src,
+            "frac": achieved / hbm, "traffic": NCU_TRAFFIC_BYTES["bootstrap_kernel"], "peak_source": src,
             "note": "random-stream bytes generated per launch; the kernel is latency-bound on the sequential MT19937 twist"}
 
 
@@ -308,6 +381,7 @@ def main():
     parser.add_argument("--warmup", type=int, default=5)
     parser.add_argument("--impl", choices=("b200", "reference"), default="b200")
     parser.add_argument("--no-cpu-baseline", action="store_true")
+    parser.add_argument("--no-arms", action="store_true", help="skip the HBM/tensor/GEMM/SFU arm measurements")
     args = parser.parse_args()
     if args.warmup < 3:
         parser.error("--warmup must be >= 3")

@@ -122,6 +122,31 @@ __device__ void multiset_unrank(int r, int n, int* a, const uint32_t (*binom)[16
 }
 
 // Dynamic shared memory layout (byte offsets) for a launch.
+// One resample of a group with exactly N members: draw N indices from the
+// ring, sort them (registers only) and count the multiset.  N <= 7.
+template <int N>
+__device__ __forceinline__ void histogram_resample(const uint32_t* ring, uint32_t pos, uint32_t* hist,
+                                                   const uint32_t (*binom)[16]) {
+  int t[N];
+#pragma unroll
+  for (int j = 0; j < N; ++j) {
+    const uint32_t w0 = ring[pos]; if (++pos == (uint32_t)kRing) pos = 0;
+    const uint32_t w1 = ring[pos]; if (++pos == (uint32_t)kRing) pos = 0;
+    t[j] = draw_index(w0, w1, double(N));
+  }
+#pragma unroll
+  for (int i = 0; i < N; ++i)
+#pragma unroll
+    for (int k = 0; k < N - 1 - i; ++k) {
+      const int a = t[k], b = t[k + 1];
+      t[k] = min(a, b); t[k + 1] = max(a, b);
+    }
+  int r = 0;
+#pragma unroll
+  for (int i = 0; i < N; ++i) r += binom[t[i] + i][i + 1];
+  atomicAdd(&hist[r], 1u);
+}
+
 struct BootSmem {
   size_t vals, cnt, rank_of, sorted_v, ptab, total;
   __host__ __device__ BootSmem(int M, int mm, bool direct) {
@@ -228,14 +253,13 @@ __global__ void __launch_bounds__(kBootThreads) bootstrap_kernel(BootArgs A) {
         uint32_t pos = first_slot * kMtN + (r * words_per_draw - first);
         if (pos >= (uint32_t)kRing) pos -= kRing;
         if (histogram) {
-          int t[kHistMaxN];
-          for (int j = 0; j < n; ++j) {
-            const uint32_t w0 = ring[pos]; if (++pos == (uint32_t)kRing) pos = 0;
-            const uint32_t w1 = ring[pos]; if (++pos == (uint32_t)kRing) pos = 0;
-            t[j] = draw_index(w0, w1, nd);
+          switch (n) {
+            case 3: histogram_resample<3>(ring, pos, hist, binom); break;
+            case 4: histogram_resample<4>(ring, pos, hist, binom); break;
+            case 5: histogram_resample<5>(ring, pos, hist, binom); break;
+            case 6: histogram_resample<6>(ring, pos, hist, binom); break;
+            default: histogram_resample<7>(ring, pos, hist, binom); break;
           }
-          for (int i = 1; i < n; ++i) { int v = t[i], k = i - 1; while (k >= 0 && t[k] > v) { t[k + 1] = t[k]; --k; } t[k + 1] = v; }
-          atomicAdd(&hist[multiset_rank(t, n, binom)], 1u);
         } else {
           for (int j = 0; j < n; ++j) {
             const uint32_t w0 = ring[pos]; if (++pos == (uint32_t)kRing) pos = 0;
