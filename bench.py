@@ -56,7 +56,7 @@ class ClockSampler:
 
     def start(self):
         try:
-            self.path = Path(os.environ.get("TMPDIR", "/tmp")) / f"pmb200_clocks_{os.getpid()}.csv"
+            self.path = Path(os.environ.get("TMPDIR", "/tmp")) / f"pmb200_clocks_{os.getpid()}_{id(self)}.csv"
             self.proc = subprocess.Popen(["nvidia-smi", "-i", str(self.index), f"--query-gpu={self.QUERY}",
                                           "--format=csv,noheader,nounits", "-lms", "100"],
                                          stdout=open(self.path, "w"), stderr=subprocess.DEVNULL)
@@ -252,6 +252,68 @@ def _arm(args):
     return device, next(r for r in records if r["type"] == "result")
 
 
+def _pynvml_sample_cost(uuid: str, reads: int = 200) -> float | None:
+    """Median seconds of one sample read the reference's way: its NVML calls
+    (powermodeling/telemetry.py:195-243) from Python through pynvml."""
+    try:
+        import pynvml as nv
+    except ImportError:
+        return None
+    nv.nvmlInit()
+    try:
+        h = nv.nvmlDeviceGetHandleByUUID(uuid)
+        fields = [(nv.NVML_FI_DEV_POWER_INSTANT, nv.NVML_POWER_SCOPE_GPU),
+                  (nv.NVML_FI_DEV_POWER_AVERAGE, nv.NVML_POWER_SCOPE_GPU),
+                  (nv.NVML_FI_DEV_POWER_INSTANT, nv.NVML_POWER_SCOPE_MEMORY),
+                  (nv.NVML_FI_DEV_POWER_AVERAGE, nv.NVML_POWER_SCOPE_MEMORY)]
+        calls = [lambda: nv.nvmlDeviceGetPowerUsage(h), lambda: nv.nvmlDeviceGetFieldValues(h, fields),
+                 lambda: nv.nvmlDeviceGetTotalEnergyConsumption(h),
+                 lambda: nv.nvmlDeviceGetClockInfo(h, nv.NVML_CLOCK_GRAPHICS),
+                 lambda: nv.nvmlDeviceGetClockInfo(h, nv.NVML_CLOCK_SM),
+                 lambda: nv.nvmlDeviceGetClockInfo(h, nv.NVML_CLOCK_MEM),
+                 lambda: nv.nvmlDeviceGetTemperature(h, nv.NVML_TEMPERATURE_GPU),
+                 lambda: nv.nvmlDeviceGetPerformanceState(h), lambda: nv.nvmlDeviceGetCurrentClocksEventReasons(h),
+                 lambda: nv.nvmlDeviceGetUtilizationRates(h), lambda: nv.nvmlDeviceGetPowerManagementLimit(h),
+                 lambda: nv.nvmlDeviceGetEnforcedPowerLimit(h), lambda: nv.nvmlDeviceGetComputeRunningProcesses(h),
+                 lambda: nv.nvmlDeviceGetGraphicsRunningProcesses(h),
+                 lambda: nv.nvmlDeviceGetMPSComputeRunningProcesses(h)]
+        times = []
+        for _ in range(reads):
+            t0 = time.perf_counter()
+            for call in calls:
+                try:
+                    call()
+                except nv.NVMLError:
+                    pass
+            times.append(time.perf_counter() - t0)
+        return statistics.median(times)
+    finally:
+        nv.nvmlShutdown()
+
+
+def run_telemetry_arm(uuid: str) -> dict:
+    """Native sampler: achieved tick rate and query latency at 10 ms and 1 ms intervals."""
+    from powermodeling_b200.telemetry import NvmlDevice, Sampler
+    out = {}
+    device = NvmlDevice(uuid=uuid)
+    try:
+        for interval in (0.01, 0.001):
+            sampler = Sampler(device, interval_s=interval).start()
+            time.sleep(1.0)
+            samples = sampler.stop()
+            q = sorted(s["query_duration_s"] for s in samples)
+            span = samples[-1]["t_s"] - samples[0]["t_s"]
+            out[f"interval_{interval * 1e3:g}ms"] = {
+                "samples": len(samples), "samples_per_s": (len(samples) - 1) / span if span > 0 else None,
+                "query_ms_p50": 1e3 * q[len(q) // 2], "query_ms_p99": 1e3 * q[min(len(q) - 1, int(len(q) * 0.99))],
+                "fatal": sum(1 for s in samples if s["fatal_errors"])}
+    finally:
+        device.close()
+    cost = _pynvml_sample_cost(uuid)
+    out["pynvml_reference_calls_query_ms_p50"] = None if cost is None else 1e3 * cost
+    return out
+
+
 def run_arms(local: int, peaks: dict) -> dict:
     """HBM read/copy, tcgen05 tensor, cuBLAS GEMM and SFU arms through the powerbench engine."""
     sms = 148
@@ -272,10 +334,19 @@ def run_arms(local: int, peaks: dict) -> dict:
     out["hbm_copy"] = {"gbs": r["throughput_bytes_s"] / 1e9, "config": "16 B load+store, 4 GiB, grid 148x8x256"}
     tensor = {}
     for acc in (1, 2, 4, 8):
+        # 2 s per arm: long enough for the power-capped clock to settle and be sampled.
+        arm_clock = ClockSampler(local)
+        arm_clock.start()
         _, r = _arm(["--workload", "tensor", "--blocks", str(sms), "--threads", "128", "--iterations", "8192",
-                     "--tensor-accumulators", str(acc), "--batch-launches", "4", "--fixed-batches", "3", *ARM_QUICK])
-        tensor[str(acc)] = {"tflops": r["throughput_ops_s"] / 1e12, "tile_n": r["tensor_tile_n"],
-                            "timeouts": r["tensor_status"]["bounded_wait_timeouts"]}
+                     "--tensor-accumulators", str(acc), "--batch-launches", "4", "--seconds", "2",
+                     "--warmup-seconds", "0", "--idle-seconds", "0", "--warmup-batches", "2"])
+        c = arm_clock.stop()
+        tflops = r["throughput_ops_s"] / 1e12
+        entry = {"tflops": tflops, "tile_n": r["tensor_tile_n"], "timeouts": r["tensor_status"]["bounded_wait_timeouts"],
+                 "sm_mhz": c.get("sm_mhz"), "power_w": c.get("power_w_median"), "reasons": c.get("reasons")}
+        if c.get("sm_mhz"):
+            entry["frac_of_dense_peak_at_arm_clock"] = tflops / (8192 * sms * c["sm_mhz"] * 1e6 / 1e12)
+        tensor[str(acc)] = entry
     out["tensor_tcgen05"] = tensor
     _, r = _arm(["--workload", "gemm", "--gemm-m", "8192", "--gemm-n", "8192", "--gemm-k", "8192", "--batch-launches", "4",
                  "--fixed-batches", "3", *ARM_QUICK])
@@ -285,6 +356,7 @@ def run_arms(local: int, peaks: dict) -> dict:
                  "--fixed-batches", "4", *ARM_QUICK])
     out["sfu_ex2"] = {"ops_s": r["throughput_ops_s"], "checksum": r["checksum"]}
     clock = clocks.stop()
+    out["telemetry"] = run_telemetry_arm(device["uuid"])
     mem_mhz = clock.get("mem_mhz") or device["nominal_max_memory_clock_khz"] / 1e3
     theory = 2 * mem_mhz * 1e6 * bus / 8 / 1e9
     hbm_peak = peaks.get("hbm_gbs", 6650.0)
