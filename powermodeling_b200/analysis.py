@@ -30,6 +30,10 @@ from . import _native as N
 from . import contracts
 from .pack import (MEMORY_WORKLOADS, NONLINEAR_WORKLOADS, ROW_WORKLOADS, SFU_WORKLOADS, TENSOR_WORKLOADS,
                    finite, pack_trials, phase_records, trials_struct)
+from .memory_power import ALIASES as SENSOR_ALIASES
+from .memory_power import NUMERIC_FIELDS as SENSOR_FIELDS
+from .memory_power import bootstrap_columns as sensor_columns
+from .memory_power import group_sensor, trial_sensor
 from .profiles import ARCHITECTURES
 
 ENERGY_WORKLOADS = TENSOR_WORKLOADS | MEMORY_WORKLOADS | SFU_WORKLOADS | NONLINEAR_WORKLOADS
@@ -612,6 +616,17 @@ def analyze_trials(records: Iterable[Mapping[str, Any]], policy: AnalysisPolicy 
             result["pj_per_op"] = result["total_pj_per_op"] = None
         selected = _selected(packed, i, 1, views)
         result["hbm_bandwidth"] = trial_bandwidth(record, result, selected, hbm_bandwidth_fraction)
+        sensor = trial_sensor(record, result, result["phases"], phases_rec, policy.max_sample_gap_s,
+                              policy.max_idle_drift_fraction)
+        result["hbm_memory_power"] = sensor
+        if sensor is not None:
+            for alias, field in SENSOR_ALIASES:
+                result[alias] = sensor[field]
+            if _metrics_out is not None:
+                rows = _metrics_out[-1][0]
+                for alias in ("memory_rail_power_w", "memory_rail_incremental_power_w"):
+                    value = result[alias]
+                    rows[i, METRICS.index(alias)] = math.nan if value is None else value
         out.append(result)
     return out
 
@@ -743,12 +758,17 @@ def summarize(records: Iterable[Mapping[str, Any]], throughput_fraction: float =
     metrics_out: list = []
     trials = analyze_trials(kept, policy, hbm_bandwidth_fraction, _metrics_out=metrics_out)
     metric_rows = metrics_out[0][0] if metrics_out else np.zeros((0, len(METRICS)))
+    # HBM groups bootstrap their memory-rail sensor fields too (memory_power.py:169-204):
+    # extra columns, NaN outside each field's repeat population.
+    sensor_rows = np.array([sensor_columns(t.get("hbm_memory_power")) for t in trials], dtype=np.float64)
+    metric_rows = np.concatenate([metric_rows, sensor_rows.reshape(len(trials), len(SENSOR_FIELDS))], axis=1)
     buckets: dict[str, list[int]] = {}
     for index, trial in enumerate(trials):
         buckets.setdefault(group_key(trial), []).append(index)
     ordered = sorted(buckets.items())
-    members, seeds, groups = [], [], []
+    members, seeds, groups, group_indices = [], [], [], []
     for key, indices in ordered:
+        group_indices.append(indices)
         valid, seen_repeats, dup_repeats = [], set(), []
         for index in indices:
             trial = trials[index]
@@ -796,6 +816,17 @@ def summarize(records: Iterable[Mapping[str, Any]], throughput_fraction: float =
             group["ci95"][metric] = [a, b] if a is not None else None
         vt = [trials[i] for i in members[g]]
         group["hbm_bandwidth"] = group_bandwidth(vt, group["workload"], hbm_bandwidth_fraction)
+        base = len(METRICS)
+        sensor_medians = [_none(med[g, base + k]) for k in range(len(SENSOR_FIELDS))]
+        sensor_intervals = [[_none(lo[g, base + k]), _none(hi[g, base + k])] if _none(lo[g, base + k]) is not None
+                            else None for k in range(len(SENSOR_FIELDS))]
+        group["hbm_memory_power"] = group_sensor(vt, group["workload"], [trials[i] for i in group_indices[g]],
+                                                 sensor_medians, sensor_intervals)
+        if group["hbm_memory_power"] is not None:
+            sensor = group["hbm_memory_power"]
+            for alias, field in SENSOR_ALIASES:
+                group[alias] = sensor[field]
+                group["ci95"][alias] = sensor["ci95"][field]
         counts = group["paired_reference_order_counts"]
         group["paired_reference_both_orders_observed"] = all(counts.values())
         group["paired_reference_counterbalanced"] = group["paired_reference_both_orders_observed"] and counts["AB"] == counts["BA"]

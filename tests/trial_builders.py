@@ -237,3 +237,114 @@ def scenarios():
     short = dict(trim_s=0.0, idle_trim_s=0.0, min_measure_s=1.0, min_idle_s=0.5)
     add("short_policy_steady", steady(), short)
     return out
+
+
+# ---------------------------------------------------------------- HBM memory-rail sensor cases
+WALL0 = 1_764_000_000.0  # CLOCK_REALTIME of t_s = 0 in these fixtures
+
+
+def memory_rail(active_memory=60.0, idle_memory=20.0, idle_post_memory=None, source="memory_power_instant_w",
+                ripple=0.25, workload_override=None, **kw):
+    """An HBM trial whose samples carry the NVML memory-scope power field with its sensor metadata."""
+    r = steady(workload=workload_override or "hbm", **kw)
+    field, semantics = (("NVML_FI_DEV_POWER_INSTANT", "driver_instantaneous") if source == "memory_power_instant_w"
+                        else ("NVML_FI_DEV_POWER_AVERAGE", "one_second_average"))
+    levels = {"idle_pre": idle_memory, "measure": active_memory,
+              "idle_post": idle_memory if idle_post_memory is None else idle_post_memory}
+    for name, phase in r["phases"].items():
+        for k, s in enumerate(phase["samples"]):
+            t = s["t_s"]
+            s["memory_power_w"] = levels[name] + ripple * ((k * 7) % 5 - 2)
+            s["memory_power_source"] = source
+            s["query_realtime_start_s"] = WALL0 + t - 0.001
+            s["query_realtime_end_s"] = WALL0 + t + 0.001
+            s["errors"] = {}
+            s["field_metadata"] = {source: {"field": field, "scope": "memory", "scope_id": 2,
+                                            "timestamp_us": int(round((WALL0 + t - 0.004) * 1e6)),
+                                            "timestamp_clock": "unix_epoch_microseconds", "latency_us": 20,
+                                            "semantics": semantics}}
+    return r
+
+
+def _measure_samples(r):
+    return r["phases"]["measure"]["samples"]
+
+
+def memory_rail_scenarios():
+    """(name, record) pairs for the memory-rail sensor (memory_power.py:27-166)."""
+    out = [("fresh", memory_rail()), ("average_source", memory_rail(source="memory_power_average_w"))]
+    r = memory_rail()
+    for s in _measure_samples(r)[10:14]:
+        s["field_metadata"][s["memory_power_source"]]["timestamp_us"] -= 3_000_000
+    out.append(("stale_timestamps", r))
+    r = memory_rail()
+    _measure_samples(r)[12]["field_metadata"]["memory_power_instant_w"]["timestamp_us"] += 2_000_000
+    out.append(("future_timestamp", r))
+    r = memory_rail()
+    for s in r["phases"]["idle_post"]["samples"]:
+        s["memory_power_source"] = "memory_power_average_w"
+        s["field_metadata"] = {"memory_power_average_w": dict(s["field_metadata"]["memory_power_instant_w"],
+                                                              field="NVML_FI_DEV_POWER_AVERAGE",
+                                                              semantics="one_second_average")}
+    out.append(("idle_source_mismatch", r))
+    r = memory_rail()
+    _measure_samples(r)[13]["memory_power_source"] = "memory_power_module_w"
+    out.append(("unknown_source", r))
+    r = memory_rail()
+    _measure_samples(r)[9]["field_metadata"]["memory_power_instant_w"]["scope"] = "gpu"
+    out.append(("wrong_scope", r))
+    r = memory_rail()
+    _measure_samples(r)[11]["field_metadata"]["memory_power_instant_w"]["semantics"] = "one_second_average"
+    out.append(("inconsistent_metadata", r))
+    r = memory_rail()
+    meta = [s["field_metadata"]["memory_power_instant_w"] for s in _measure_samples(r)]
+    meta[20]["timestamp_us"], meta[21]["timestamp_us"] = meta[21]["timestamp_us"], meta[20]["timestamp_us"]
+    out.append(("timestamp_regression", r))
+    r = memory_rail()
+    _measure_samples(r)[15]["memory_power_w"] = None
+    out.append(("missing_value", r))
+    r = memory_rail()
+    _measure_samples(r)[16]["memory_power_w"] = -1.0
+    out.append(("negative_power", r))
+    r = steady(workload="hbm")
+    out.append(("no_memory_sensor", r))
+    r = memory_rail()
+    _measure_samples(r)[14]["errors"] = {"memory_power_instant_w": {"type": "NVMLError_Timeout", "message": "Timeout"}}
+    out.append(("query_error", r))
+    r = memory_rail()
+    _measure_samples(r)[17]["field_metadata"]["memory_power_instant_w"]["latency_us"] = -1
+    out.append(("negative_latency", r))
+    r = memory_rail()
+    _measure_samples(r)[18]["field_metadata"]["memory_power_instant_w"]["timestamp_clock"] = "monotonic"
+    out.append(("other_timestamp_clock", r))
+    r = memory_rail()
+    _measure_samples(r)[19]["query_realtime_end_s"] = _measure_samples(r)[19]["query_realtime_start_s"] - 1
+    out.append(("query_clock_backwards", r))
+    out.append(("idle_drift", memory_rail(idle_post_memory=30.0)))
+    r = memory_rail()
+    for s in _measure_samples(r):
+        s["field_metadata"] = {}
+    out.append(("no_metadata", r))
+    r = memory_rail()
+    r["phases"]["measure"]["samples"] = [s for s in _measure_samples(r) if not 10.0 < s["t_s"] < 13.5]
+    out.append(("sensor_gap", r))
+    r = memory_rail()
+    r["benchmark"].pop("measure_epochs")
+    out.append(("not_count_exact", r))
+    out.append(("l2_workload_has_no_sensor", memory_rail(workload_override="l2")))
+    return out
+
+
+def memory_rail_group():
+    """Repeats of one HBM configuration: valid, stale, drifting idle and board-invalid members."""
+    reps = []
+    for k, active in enumerate((60.0, 63.5, 58.25, 61.0, 59.5, 62.0)):
+        reps.append(memory_rail(active_memory=active, repeat=k, trial_id=f"rail-{k}"))
+    for s in _measure_samples(reps[3])[10:14]:
+        s["field_metadata"][s["memory_power_source"]]["timestamp_us"] -= 3_000_000
+    for s in reps[4]["phases"]["idle_post"]["samples"]:
+        s["memory_power_w"] = 30.0
+    reps[5]["phases"]["measure"]["samples"][15]["compute_processes"].append({"pid": 4321})
+    mixed = [memory_rail(active_memory=60.0 + k, repeat=k, trial_id=f"mixed-{k}", blocks=96,
+                         source="memory_power_average_w" if k == 1 else "memory_power_instant_w") for k in range(3)]
+    return reps + mixed
