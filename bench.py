@@ -35,7 +35,7 @@ sys.path.insert(0, str(ROOT))
 RESAMPLES = 10000
 POINTS, REPEATS = 64, 4
 METRIC = "bootstrap resamples/s"
-WORKLOAD = "analysis: 64 points x 4 paired repeats, 3 s arms / 1 s idles at 10 ms, B=10000"
+WORKLOAD = "analysis: 64 points per GPU x 4 paired repeats, 3 s arms / 1 s idles at 10 ms, B=10000"
 
 
 def measured_peaks() -> dict:
@@ -82,21 +82,37 @@ class ClockSampler:
 
 
 # --------------------------------------------------------------------------- workload
-def build_workload(seed: int):
-    """Records, packed arrays and group structure (keys/seeds) of one rank's sweep."""
+def build_workload(rank: int):
+    """Records, packed arrays and analyzed trials of one rank's 64-point shard of the sweep."""
     from powermodeling_b200 import analysis as A
     from powermodeling_b200.synthetic import ANALYSIS_POLICY, SweepShape, make_sweep
-    records = make_sweep(SweepShape(points=POINTS, repeats=REPEATS), seed=seed)
+    records = make_sweep(SweepShape(points=POINTS, repeats=REPEATS), seed=rank, first_point=rank * POINTS)
     policy = A.AnalysisPolicy(**ANALYSIS_POLICY)
     packed, _, _ = A.prepare(records)
     trials = A.analyze_trials(records, policy)              # one untimed pass for the group keys
+    return records, policy, packed, trials
+
+
+def global_groups(trials: list, world: int):
+    """Group structure of the whole sweep (every rank's trials, rank order): members as global rows, seeds."""
+    from powermodeling_b200 import analysis as A
+    if world > 1:
+        import torch.distributed as dist
+        light = [{k: t.get(k) for k in ("trial_id", "valid", "repeat_index", "config", "gpu_uuid", "workload",
+                                        "experiment_role", "clock_comparison_controlled", "graphics_clock_mhz",
+                                        "memory_clock_mhz", "benchmark_sha256", "measurement_stratum",
+                                        "experiment_contract", "nonlinear_contract", "sfu_contract",
+                                        "treatment_design_stratum", "resource_geometry")} for t in trials]
+        parts: list = [None] * world
+        dist.all_gather_object(parts, light)
+        everything = [t for part in parts for t in part]
+    else:
+        everything = trials
     buckets: dict[str, list[int]] = {}
-    for i, t in enumerate(trials):
+    for i, t in enumerate(everything):
         buckets.setdefault(A.group_key(t), []).append(i)
     keys = sorted(buckets)
-    members = [buckets[k] for k in keys]
-    seeds = [A.group_seed(k) for k in keys]
-    return records, policy, packed, members, seeds
+    return [buckets[k] for k in keys], [A.group_seed(k) for k in keys]
 
 
 def device_arrays(packed, torch):
@@ -114,15 +130,21 @@ def device_arrays(packed, torch):
 
 
 def run_b200(args, rank: int, world: int) -> dict | None:
+    """One step = analyze this rank's trials, exchange metric rows, bootstrap this rank's groups, exchange results."""
     import torch
     import torch.distributed as dist
     from powermodeling_b200 import _native as N
+    from powermodeling_b200.analysis import METRICS
+    from powermodeling_b200.distributed import owned_groups
 
     local = int(os.environ.get("LOCAL_RANK", "0"))
     torch.cuda.set_device(local)
     lib = N.library()
-    records, policy, packed, members, seeds = build_workload(seed=rank)
-    n, M, G = packed.n_trials, len(__import__("powermodeling_b200.analysis", fromlist=["METRICS"]).METRICS), len(members)
+    records, policy, packed, host_trials_list = build_workload(rank)
+    members, seeds = global_groups(host_trials_list, world)
+    n, M, G = packed.n_trials, len(METRICS), len(members)
+    mine = owned_groups(G, world, rank)
+    per_rank = -(-G // world)
     trials, keep, in_bytes = device_arrays(packed, torch)
     PO, TO = N.layout("PM_PO_COUNT"), N.layout("PM_TO_COUNT")
     out = {"phase_out": torch.empty(n * 5 * PO, dtype=torch.float64, device="cuda"),
@@ -133,34 +155,55 @@ def run_b200(args, rank: int, world: int) -> dict | None:
            "valid": torch.empty(n, dtype=torch.uint8, device="cuda")}
     results = N.TrialResults(*(out[k].data_ptr() for k in ("phase_out", "phase_flags", "trial_out", "issue_bits", "metrics", "valid")))
     out_bytes = sum(v.numel() * v.element_size() for v in out.values())
-    offsets = np.zeros(G + 1, dtype=np.int32)
-    np.cumsum([len(m) for m in members], out=offsets[1:])
-    rows = np.concatenate([np.asarray(m, dtype=np.int32) for m in members])
+    # Exchange one lands every rank's metric rows and valid flags here (rank order = global row order).
+    all_metrics = torch.empty(world * n * M, dtype=torch.float64, device="cuda") if world > 1 else out["metrics"]
+    all_valid = torch.empty(world * n, dtype=torch.uint8, device="cuda") if world > 1 else out["valid"]
+    own = [members[g] for g in mine]
+    offsets = np.zeros(len(own) + 1, dtype=np.int32)
+    np.cumsum([len(m) for m in own], out=offsets[1:])
+    rows = np.concatenate([np.asarray(m, dtype=np.int32) for m in own]) if own else np.zeros(1, np.int32)
     d_off, d_rows = torch.from_numpy(offsets).cuda(), torch.from_numpy(rows).cuda()
-    d_seeds = torch.from_numpy(np.asarray(seeds, dtype=np.uint64).view(np.int64)).cuda()
-    med, lo, hi = (torch.empty(G * M, dtype=torch.float64, device="cuda") for _ in range(3))
-    job = N.BootstrapJob(G, M, int(rows.size), n, RESAMPLES, max(len(m) for m in members),
-                         out["metrics"].data_ptr(), d_off.data_ptr(), d_rows.data_ptr(), out["valid"].data_ptr(),
-                         d_seeds.data_ptr(), med.data_ptr(), lo.data_ptr(), hi.data_ptr())
+    own_seeds = np.asarray([seeds[g] for g in mine] or [0], dtype=np.uint64)
+    d_seeds = torch.from_numpy(own_seeds.view(np.int64)).cuda()
+    # Group outputs of this rank: [3, per_rank, M] (medians, lows, highs); exchange two gathers them.
+    group_out = torch.full((3, per_rank, M), float("nan"), dtype=torch.float64, device="cuda")
+    all_group_out = torch.empty((world, 3, per_rank, M), dtype=torch.float64, device="cuda") if world > 1 else None
+    max_members = max((len(m) for m in own), default=1)
+    job = N.BootstrapJob(len(own), M, int(sum(len(m) for m in own)), world * n, RESAMPLES, max_members,
+                         all_metrics.data_ptr(), d_off.data_ptr(), d_rows.data_ptr(), all_valid.data_ptr(),
+                         d_seeds.data_ptr(), group_out[0].data_ptr(), group_out[1].data_ptr(), group_out[2].data_ptr())
     a_scr = lib.pm_analyze_scratch_bytes(n, packed.max_phase_samples)
-    b_scr = lib.pm_bootstrap_scratch_bytes(G, job.max_members, RESAMPLES)
+    b_scr = lib.pm_bootstrap_scratch_bytes(max(1, len(own)), max_members, RESAMPLES)
     scratch = torch.empty(max(1, a_scr + b_scr), dtype=torch.uint8, device="cuda")
     flush = torch.empty(256 * 1024 * 1024 // 4, dtype=torch.float32, device="cuda")
     stream = torch.cuda.current_stream()
     sptr = C.c_void_p(stream.cuda_stream)
     native_policy = policy.native()
+    ev = [torch.cuda.Event(enable_timing=True) for _ in range(5)]
 
     def step():
+        ev[0].record(stream)
         N.check(lib.pm_analyze_trials_device(trials, native_policy, results, C.c_void_p(scratch.data_ptr()), a_scr, sptr), "analyze")
-        e_mid.record(stream)
-        N.check(lib.pm_group_bootstrap_device(job, C.c_void_p(scratch.data_ptr() + a_scr), b_scr, sptr), "bootstrap")
+        ev[1].record(stream)
+        if world > 1:
+            dist.all_gather_into_tensor(all_metrics, out["metrics"])
+            dist.all_gather_into_tensor(all_valid, out["valid"])
+        ev[2].record(stream)
+        if own:
+            N.check(lib.pm_group_bootstrap_device(job, C.c_void_p(scratch.data_ptr() + a_scr), b_scr, sptr), "bootstrap")
+        ev[3].record(stream)
+        if world > 1:
+            dist.all_gather_into_tensor(all_group_out, group_out)
+        ev[4].record(stream)
 
-    e0, e_mid, e1 = (torch.cuda.Event(enable_timing=True) for _ in range(3))
     for _ in range(args.warmup):
         flush.zero_()
         step()
     torch.cuda.synchronize()
-    resamples_per_step = int(torch.isfinite(lo).sum().item()) * RESAMPLES
+    gathered = (all_group_out if world > 1 else group_out.unsqueeze(0)).cpu().numpy()
+    resamples_per_step = int(np.isfinite(gathered[:, 1]).sum()) * RESAMPLES
+    # group g was bootstrapped by rank g % world as its (g // world)-th group
+    lo_global = np.stack([gathered[g % world, 1, g // world] for g in range(G)])
     # correctness guard on the timed configuration: every trial valid, every group filled
     assert int(out["valid"].sum().item()) == n, "synthetic trials must all be valid"
     if world > 1:
@@ -168,71 +211,97 @@ def run_b200(args, rank: int, world: int) -> dict | None:
     torch.cuda.synchronize()
     clocks = ClockSampler(local)
     clocks.start()
-    t_analyze, t_boot = [], []
+    parts_ms = {"analyze": [], "exchange_rows": [], "bootstrap": [], "exchange_groups": []}
     for _ in range(args.steps):
         flush.zero_()                                   # L2 flush, outside the timed events
-        e0.record(stream)
         step()
-        e1.record(stream)
-        e1.synchronize()
-        t_analyze.append(e0.elapsed_time(e_mid))
-        t_boot.append(e_mid.elapsed_time(e1))
+        ev[4].synchronize()
+        for k, name in enumerate(parts_ms):
+            parts_ms[name].append(ev[k].elapsed_time(ev[k + 1]))
     torch.cuda.synchronize()
     clock_info = clocks.stop()
     if world > 1:
         dist.barrier()
-    total_ms = sum(t_analyze) + sum(t_boot)
+    total_ms = sum(sum(v) for v in parts_ms.values())
     if world > 1:
         t = torch.tensor([total_ms], dtype=torch.float64, device="cuda")
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
         total_ms = float(t.item())
     ms_per_step = total_ms / args.steps
-    value = resamples_per_step * world / (ms_per_step / 1e3)
+    value = resamples_per_step / (ms_per_step / 1e3)
+    t_analyze, t_boot = parts_ms["analyze"], parts_ms["bootstrap"]
 
-    # ---- end to end: host buffers through pm_analyze_sweep ----------------------
+    # ---- end to end: host buffers through pm_analyze_sweep, then one gather of group results --------
+    # Each rank's groups are its own points, so a rank summarizes its shard with one library call
+    # (H2D of the packed trials, both kernels, D2H of every result) and the group results are
+    # all-gathered (H2D, NCCL, D2H) inside the timed region.
     from powermodeling_b200.pack import trials_struct
     host_trials = trials_struct(packed)
+    base = rank * n
+    local_groups = [g for g, m in enumerate(members) if m and all(base <= i < base + n for i in m)]
+    l_members = [[i - base for i in members[g]] for g in local_groups]
+    Gl = len(local_groups)
+    l_off = np.zeros(Gl + 1, dtype=np.int32)
+    np.cumsum([len(m) for m in l_members], out=l_off[1:])
+    l_rows = np.concatenate([np.asarray(m, dtype=np.int32) for m in l_members])
+    l_seeds = np.asarray([seeds[g] for g in local_groups], dtype=np.uint64)
     h_out = {"phase_out": np.empty(n * 5 * PO), "phase_flags": np.empty(n * 5, dtype=np.uint32),
              "trial_out": np.empty(n * TO), "issue_bits": np.empty(n * 4, dtype=np.uint64),
              "metrics": np.empty(n * M), "valid": np.empty(n, dtype=np.uint8)}
     h_results = N.TrialResults(*(h_out[k].ctypes.data for k in ("phase_out", "phase_flags", "trial_out", "issue_bits", "metrics", "valid")))
-    h_med, h_lo, h_hi = (np.empty(G * M) for _ in range(3))
-    seeds_np = np.asarray(seeds, dtype=np.uint64)
-    h_job = N.BootstrapJob(G, M, int(rows.size), n, RESAMPLES, 0, None, offsets.ctypes.data, rows.ctypes.data, None,
-                           seeds_np.ctypes.data, h_med.ctypes.data, h_lo.ctypes.data, h_hi.ctypes.data)
-    for _ in range(args.warmup):
+    h_groups = np.empty((3, Gl, M))
+    h_job = N.BootstrapJob(Gl, M, int(l_rows.size), n, RESAMPLES, 0, None, l_off.ctypes.data, l_rows.ctypes.data, None,
+                           l_seeds.ctypes.data, h_groups[0].ctypes.data, h_groups[1].ctypes.data, h_groups[2].ctypes.data)
+    g_send = torch.empty((3, Gl, M), dtype=torch.float64, device="cuda")
+    g_recv = torch.empty((world, 3, Gl, M), dtype=torch.float64, device="cuda")
+
+    def e2e_step():
         N.check(lib.pm_analyze_sweep(host_trials, native_policy, h_results, h_job), "pm_analyze_sweep")
+        if world > 1:
+            g_send.copy_(torch.from_numpy(h_groups))
+            dist.all_gather_into_tensor(g_recv, g_send)
+            return g_recv.cpu().numpy()
+        return h_groups[None]
+
+    for _ in range(args.warmup):
+        e2e_step()
     if world > 1:
         dist.barrier()
     e2e_times = []
     for _ in range(args.steps):
         t0 = time.perf_counter()
-        N.check(lib.pm_analyze_sweep(host_trials, native_policy, h_results, h_job), "pm_analyze_sweep")
+        e2e_step()
         e2e_times.append(time.perf_counter() - t0)
     e2e_s = sum(e2e_times) / args.steps
     if world > 1:
         t = torch.tensor([e2e_s], dtype=torch.float64, device="cuda")
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
         e2e_s = float(t.item())
-    assert np.array_equal(np.nan_to_num(h_lo), np.nan_to_num(lo.cpu().numpy())), "e2e and device paths disagree"
-    h2d = in_bytes + offsets.nbytes + rows.nbytes + seeds_np.nbytes
-    d2h = sum(a.nbytes for a in h_out.values()) + 3 * h_med.nbytes
+    assert np.array_equal(np.nan_to_num(h_groups[1]), np.nan_to_num(lo_global[local_groups])), \
+        "e2e and device paths disagree"
+    h2d = in_bytes + l_off.nbytes + l_rows.nbytes + l_seeds.nbytes + (h_groups.nbytes if world > 1 else 0)
+    d2h = sum(a.nbytes for a in h_out.values()) + h_groups.nbytes * (world + 1 if world > 1 else 1)
     if rank != 0:
         return None
     peaks = measured_peaks()
     a_ms, b_ms = statistics.mean(t_analyze), statistics.mean(t_boot)
     dominant = "bootstrap_kernel" if b_ms >= a_ms else "analyze_kernel"
-    roofline = roofline_entry(dominant, a_ms, b_ms, in_bytes, out_bytes, G, M, packed, peaks, resamples_per_step)
+    roofline = roofline_entry(dominant, a_ms, b_ms, in_bytes, out_bytes, len(own), M, packed, peaks,
+                              resamples_per_step)
     line = {"metric": METRIC, "value": value, "unit": "resamples/s", "n_gpus": world, "steps": args.steps,
             "warmup": args.warmup, "ms_per_step": ms_per_step, "higher_is_better": True, "scaling": "weak",
             "vs_baseline": None, "dtype": "f64", "data": "synthetic",
-            "config": {"workload": WORKLOAD, "points": POINTS, "repeats": REPEATS, "trials": n, "groups": G,
+            "config": {"workload": WORKLOAD, "points": POINTS * world, "points_per_gpu": POINTS, "repeats": REPEATS,
+                       "trials": n * world, "groups": G,
                        "resamples": RESAMPLES, "samples": packed.n_samples, "l2": "flushed (256 MiB write) between steps",
-                       "parallelism": f"sweep-per-gpu x{world}"},
-            "e2e": {"value": resamples_per_step * world / e2e_s, "unit": "resamples/s",
+                       "parallelism": f"sweep-sharded x{world}: trials and groups per rank, rows and group "
+                                      f"results all-gathered over NCCL" if world > 1 else "single GPU"},
+            "e2e": {"value": resamples_per_step / e2e_s, "unit": "resamples/s",
                     "h2d_bytes_per_step": int(h2d), "d2h_bytes_per_step": int(d2h), "ms_per_step": e2e_s * 1e3},
             "gpu_launches": 2 * args.steps,
-            "kernels": {"analyze_kernel_ms": a_ms, "bootstrap_kernel_ms": b_ms},
+            "kernels": {"analyze_kernel_ms": a_ms, "bootstrap_kernel_ms": b_ms,
+                        "exchange_rows_ms": statistics.mean(parts_ms["exchange_rows"]),
+                        "exchange_groups_ms": statistics.mean(parts_ms["exchange_groups"])},
             "roofline": roofline, "clocks": clock_info}
     if world == 1 and not args.no_cpu_baseline:
         line["cpu_baseline"] = cpu_baseline(records, policy)

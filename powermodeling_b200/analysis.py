@@ -735,17 +735,8 @@ def median_ci(values: list[float], seed: int, resamples: int = DEFAULT_RESAMPLES
     return [float(lo[0, 0]), float(hi[0, 0])]
 
 
-def summarize(records: Iterable[Mapping[str, Any]], throughput_fraction: float = 0.95,
-              policy: AnalysisPolicy | Mapping[str, Any] | None = None, min_repeats: int = 3,
-              plan: Mapping[str, Any] | None = None, evaluation_policy=None,
-              hbm_bandwidth_fraction: float = 0.80, resamples: int = DEFAULT_RESAMPLES) -> dict[str, Any]:
-    """summarize's trial and group sections (analysis.py:1400-1519); ``resamples`` generalises the 1000 draws."""
-    if not 0 < throughput_fraction <= 1 or min_repeats < 1:
-        raise ValueError("throughput_fraction must be in (0, 1], min_repeats must be positive")
-    from .hbm import group_bandwidth, validate_fraction
-    hbm_bandwidth_fraction = validate_fraction(hbm_bandwidth_fraction)
-    policy = _policy(policy)
-    records = list(records)
+def dedup_trials(records: list) -> tuple[list, list]:
+    """Records kept (first of each trial_id) and the duplicate ids dropped (analysis.py:1408-1416)."""
     seen, duplicates, kept = set(), [], []
     for record in records:
         trial_id = record.get("trial_id")
@@ -755,13 +746,26 @@ def summarize(records: Iterable[Mapping[str, Any]], throughput_fraction: float =
         if trial_id is not None:
             seen.add(trial_id)
         kept.append(record)
+    return kept, duplicates
+
+
+def analyze_rows(records: list, policy: AnalysisPolicy, hbm_bandwidth_fraction: float) -> tuple[list, np.ndarray]:
+    """Trial results plus one row per trial: the 47 metrics, then the 7 memory-rail sensor fields.
+
+    The sensor columns are NaN outside each field's repeat population, so the
+    bootstrap of an HBM group's sensor fields (memory_power.py:169-204) runs
+    in the same launch as its metrics.
+    """
     metrics_out: list = []
-    trials = analyze_trials(kept, policy, hbm_bandwidth_fraction, _metrics_out=metrics_out)
+    trials = analyze_trials(records, policy, hbm_bandwidth_fraction, _metrics_out=metrics_out)
     metric_rows = metrics_out[0][0] if metrics_out else np.zeros((0, len(METRICS)))
-    # HBM groups bootstrap their memory-rail sensor fields too (memory_power.py:169-204):
-    # extra columns, NaN outside each field's repeat population.
     sensor_rows = np.array([sensor_columns(t.get("hbm_memory_power")) for t in trials], dtype=np.float64)
-    metric_rows = np.concatenate([metric_rows, sensor_rows.reshape(len(trials), len(SENSOR_FIELDS))], axis=1)
+    rows = np.concatenate([metric_rows, sensor_rows.reshape(len(trials), len(SENSOR_FIELDS))], axis=1)
+    return trials, rows
+
+
+def group_structure(trials: list, min_repeats: int) -> tuple[list, list, list, list]:
+    """Groups in key order with their valid members, seeds and all members (analysis.py:1424-1466)."""
     buckets: dict[str, list[int]] = {}
     for index, trial in enumerate(trials):
         buckets.setdefault(group_key(trial), []).append(index)
@@ -808,7 +812,14 @@ def summarize(records: Iterable[Mapping[str, Any]], throughput_fraction: float =
                                                    for o in ("AB", "BA")},
                  "confidence": "repeat_median" if len(valid) >= min_repeats else "insufficient_valid_repeats", "ci95": {}}
         groups.append(group)
-    med, lo, hi = bootstrap_groups(metric_rows, members, seeds, resamples) if groups else (None, None, None)
+    return groups, members, seeds, group_indices
+
+
+def finish_groups(groups: list, trials: list, members: list, group_indices: list, med: np.ndarray, lo: np.ndarray,
+                  hi: np.ndarray, hbm_bandwidth_fraction: float) -> None:
+    """Group medians, intervals and the derived group records, from the bootstrap outputs (in place)."""
+    from .hbm import group_bandwidth
+    base = len(METRICS)
     for g, group in enumerate(groups):
         for m, metric in enumerate(METRICS):
             group[metric] = _none(med[g, m])
@@ -816,7 +827,6 @@ def summarize(records: Iterable[Mapping[str, Any]], throughput_fraction: float =
             group["ci95"][metric] = [a, b] if a is not None else None
         vt = [trials[i] for i in members[g]]
         group["hbm_bandwidth"] = group_bandwidth(vt, group["workload"], hbm_bandwidth_fraction)
-        base = len(METRICS)
         sensor_medians = [_none(med[g, base + k]) for k in range(len(SENSOR_FIELDS))]
         sensor_intervals = [[_none(lo[g, base + k]), _none(hi[g, base + k])] if _none(lo[g, base + k]) is not None
                             else None for k in range(len(SENSOR_FIELDS))]
@@ -839,8 +849,34 @@ def summarize(records: Iterable[Mapping[str, Any]], throughput_fraction: float =
             arm[order] = statistics.median(vals) if vals else None
         group["paired_reference_order_medians_power_w"] = arm
         group["paired_reference_order_effect_power_w"] = arm["AB"] - arm["BA"] if None not in arm.values() else None
+
+
+def summary_record(trials: list, groups: list, duplicates: list, throughput_fraction: float,
+                   hbm_bandwidth_fraction: float, min_repeats: int, resamples: int) -> dict[str, Any]:
     return {"schema_version": 2, "trials": trials, "groups": groups, "duplicate_trial_ids_ignored": duplicates,
             "selection_policy": {"throughput_fraction": throughput_fraction, "hbm_bandwidth_fraction": hbm_bandwidth_fraction,
                                  "min_repeats": min_repeats, "resamples": resamples,
                                  "ci_method": f"deterministic percentile bootstrap of repeat medians ({resamples} draws)"}}
 
+
+def check_summary_arguments(throughput_fraction: float, min_repeats: int, hbm_bandwidth_fraction: float) -> float:
+    if not 0 < throughput_fraction <= 1 or min_repeats < 1:
+        raise ValueError("throughput_fraction must be in (0, 1], min_repeats must be positive")
+    from .hbm import validate_fraction
+    return validate_fraction(hbm_bandwidth_fraction)
+
+
+def summarize(records: Iterable[Mapping[str, Any]], throughput_fraction: float = 0.95,
+              policy: AnalysisPolicy | Mapping[str, Any] | None = None, min_repeats: int = 3,
+              plan: Mapping[str, Any] | None = None, evaluation_policy=None,
+              hbm_bandwidth_fraction: float = 0.80, resamples: int = DEFAULT_RESAMPLES) -> dict[str, Any]:
+    """summarize's trial and group sections (analysis.py:1400-1519); ``resamples`` generalises the 1000 draws."""
+    hbm_bandwidth_fraction = check_summary_arguments(throughput_fraction, min_repeats, hbm_bandwidth_fraction)
+    policy = _policy(policy)
+    kept, duplicates = dedup_trials(list(records))
+    trials, rows = analyze_rows(kept, policy, hbm_bandwidth_fraction)
+    groups, members, seeds, group_indices = group_structure(trials, min_repeats)
+    med, lo, hi = bootstrap_groups(rows, members, seeds, resamples) if groups else (None, None, None)
+    finish_groups(groups, trials, members, group_indices, med, lo, hi, hbm_bandwidth_fraction)
+    return summary_record(trials, groups, duplicates, throughput_fraction, hbm_bandwidth_fraction, min_repeats,
+                          resamples)

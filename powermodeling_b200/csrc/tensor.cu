@@ -11,7 +11,7 @@
 // columns, commits to an mbarrier, and the four warps read accumulator 0 back
 // with tcgen05.ld.  Every wait is bounded by %globaltimer; on expiry the
 // kernel records a timeout, waits (bounded) for its MMAs, frees TMEM and
-// returns.  No load uses cluster multicast.
+// returns.  Every load is a plain per-CTA TMA copy.
 #include <cuda.h>
 #include <cuda_runtime.h>
 

@@ -134,8 +134,13 @@ def make_trial(rng: np.random.Generator, shape: SweepShape, point: int, repeat: 
             "quality": {"valid": True, "measurement_pid": pid}}
 
 
-def make_sweep(shape: SweepShape = SweepShape(), seed: int = 0) -> list[dict]:
-    """``shape.points * shape.repeats`` trial records from one seeded generator."""
+def make_sweep(shape: SweepShape = SweepShape(), seed: int = 0, first_point: int = 0) -> list[dict]:
+    """``shape.points * shape.repeats`` trial records from one seeded generator.
+
+    Points are numbered from ``first_point``, so sweeps built for different
+    shards of a larger sweep never share a group key.
+    """
     rng = np.random.default_rng(seed)
     ops = rng.uniform(*shape.ops_range, size=shape.points)
-    return [make_trial(rng, shape, p, r, float(ops[p])) for p in range(shape.points) for r in range(shape.repeats)]
+    return [make_trial(rng, shape, first_point + p, r, float(ops[p]))
+            for p in range(shape.points) for r in range(shape.repeats)]
