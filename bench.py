@@ -120,6 +120,7 @@ def device_arrays(packed, torch):
     dev = {}
     t = N.Trials()
     t.n_trials, t.max_phase_samples, t.n_samples, t.n_epochs = packed.n_trials, packed.max_phase_samples, packed.n_samples, packed.n_epochs
+    t.broadcast_columns = packed.broadcast
     for name, dtype, _ in N.TRIAL_ARRAYS + N.EPOCH_ARRAYS + N.TAIL_ARRAYS:
         a = packed.arrays[name]
         d = torch.from_numpy(a.copy()).cuda() if a.size else torch.empty(1, dtype=torch.uint8, device="cuda")

@@ -62,6 +62,17 @@ enum { PM_WL_OTHER = 0, PM_WL_TENSOR = 1, PM_WL_MEMORY = 2, PM_WL_SFU = 3, PM_WL
 #define PM_S_REF_FOREIGN      0x0200u /* some inventory entry's pid (None included) != measurement pid */
 #define PM_S_MEMORY_POWER_SET 0x0400u /* memory_power_w is not None */
 
+/* Per-sample columns that may be broadcast (pm_trials.broadcast_columns):
+ * a set bit means that array holds one element standing for every sample.
+ * t_s is never broadcast. */
+enum {
+  PM_COL_POWER_W = 1u << 0, PM_COL_MEMORY_POWER_W = 1u << 1, PM_COL_GRAPHICS_CLOCK = 1u << 2,
+  PM_COL_SM_CLOCK = 1u << 3, PM_COL_MEMORY_CLOCK = 1u << 4, PM_COL_TEMPERATURE = 1u << 5,
+  PM_COL_POWER_LIMIT = 1u << 6, PM_COL_ENFORCED_LIMIT = 1u << 7, PM_COL_PSTATE = 1u << 8,
+  PM_COL_ENERGY_INT = 1u << 9, PM_COL_ENERGY_FLOAT = 1u << 10, PM_COL_THROTTLE = 1u << 11,
+  PM_COL_SAMPLE_FLAGS = 1u << 12, PM_COL_MEMORY_SOURCE = 1u << 13, PM_COL_ALL = (1u << 14) - 1
+};
+
 /* Per-trial flag word (pm_trials.trial_flags). */
 #define PM_T_WORKLOAD_MASK       0x0007u /* PM_WL_* */
 #define PM_T_HOST_ISSUES         0x0008u /* host-side record checks already failed the trial */
@@ -134,6 +145,7 @@ typedef struct {
   const uint8_t* epoch_counts_exact;
   const double* trial_scalars;     /* [n_trials*PM_TS_COUNT] */
   const uint32_t* trial_flags;     /* [n_trials] */
+  uint32_t broadcast_columns;      /* PM_COL_* bits: those per-sample arrays hold 1 element for all samples */
 } pm_trials;
 
 /*

@@ -86,7 +86,16 @@ class Trials(C.Structure):
     _fields_ = ([("n_trials", C.c_int32), ("max_phase_samples", C.c_int32), ("n_samples", C.c_int64)]
                 + [(name, _p) for name, _, _ in TRIAL_ARRAYS]
                 + [("n_epochs", C.c_int32)]
-                + [(name, _p) for name, _, _ in EPOCH_ARRAYS + TAIL_ARRAYS])
+                + [(name, _p) for name, _, _ in EPOCH_ARRAYS + TAIL_ARRAYS]
+                + [("broadcast_columns", C.c_uint32)])
+
+
+# Per-sample columns that the packer may broadcast, with their PM_COL_* bit.
+BROADCAST_COLUMNS = (("power_w", 1 << 0), ("memory_power_w", 1 << 1), ("graphics_clock_mhz", 1 << 2),
+                     ("sm_clock_mhz", 1 << 3), ("memory_clock_mhz", 1 << 4), ("temperature_c", 1 << 5),
+                     ("power_limit_w", 1 << 6), ("enforced_power_limit_w", 1 << 7), ("pstate", 1 << 8),
+                     ("energy_int", 1 << 9), ("energy_float", 1 << 10), ("throttle_reasons", 1 << 11),
+                     ("sample_flags", 1 << 12), ("memory_power_source", 1 << 13))
 
 
 class TrialResults(C.Structure):

@@ -51,16 +51,22 @@ struct Shared {
   int32_t sort_cols[C_COUNT], nsort, sort_p;
 };
 
+// Sample i of a per-sample column; a broadcast column holds one element.
+template <class E>
+__device__ __forceinline__ E col_at(const E* col, uint32_t bit, const pm_trials& T, int64_t i) {
+  return (T.broadcast_columns & bit) ? col[0] : col[i];
+}
+
 __device__ __forceinline__ double col_value(const pm_trials& T, int c, int64_t i) {
   switch (c) {
-    case C_POWER: return T.power_w[i];
-    case C_GFX: return T.graphics_clock_mhz[i];
-    case C_SM: return T.sm_clock_mhz[i];
-    case C_MEM: return T.memory_clock_mhz[i];
-    case C_TEMP: return T.temperature_c[i];
-    case C_PLIMIT: return T.power_limit_w[i];
-    case C_ENF: return T.enforced_power_limit_w[i];
-    default: return T.pstate[i];
+    case C_POWER: return col_at(T.power_w, PM_COL_POWER_W, T, i);
+    case C_GFX: return col_at(T.graphics_clock_mhz, PM_COL_GRAPHICS_CLOCK, T, i);
+    case C_SM: return col_at(T.sm_clock_mhz, PM_COL_SM_CLOCK, T, i);
+    case C_MEM: return col_at(T.memory_clock_mhz, PM_COL_MEMORY_CLOCK, T, i);
+    case C_TEMP: return col_at(T.temperature_c, PM_COL_TEMPERATURE, T, i);
+    case C_PLIMIT: return col_at(T.power_limit_w, PM_COL_POWER_LIMIT, T, i);
+    case C_ENF: return col_at(T.enforced_power_limit_w, PM_COL_ENFORCED_LIMIT, T, i);
+    default: return col_at(T.pstate, PM_COL_PSTATE, T, i);
   }
 }
 
@@ -194,7 +200,7 @@ __device__ void phase_stats(const pm_trials& T, const pm_policy& P, Shared& S, d
       const int q = q0 + threadIdx.x;
       bool change = false;
       if (q < nsel - 1) {
-        const double a = T.power_w[lo + q], b = T.power_w[lo + q + 1];
+        const double a = col_at(T.power_w, PM_COL_POWER_W, T, lo + q), b = col_at(T.power_w, PM_COL_POWER_W, T, lo + q + 1);
         change = none(a) != none(b) || (!none(a) && a != b);
       }
       const unsigned ballot = __ballot_sync(0xffffffffu, change);
@@ -234,28 +240,28 @@ __device__ void phase_stats(const pm_trials& T, const pm_policy& P, Shared& S, d
   bool neg_power = false;
   int plim_none = 0, enf_none = 0, pst_none = 0;
   for (int64_t i = lo + threadIdx.x; i < hi; i += blockDim.x) {
-    const uint16_t sf = T.sample_flags[i];
-    if (!none(T.sm_clock_mhz[i])) flags |= 1u << PM_PF_ANY_SM_FINITE;
-    if (none(T.temperature_c[i])) flags |= 1u << PM_PF_TEMP_MISSING;
-    { const double v = T.graphics_clock_mhz[i]; if (none(v) || v <= 0) flags |= 1u << PM_PF_GFX_NONPOS; }
-    { const double v = T.memory_clock_mhz[i]; if (none(v) || v <= 0) flags |= 1u << PM_PF_MEM_NONPOS; }
-    { const double v = T.sm_clock_mhz[i]; if (none(v) || v <= 0) flags |= 1u << PM_PF_SM_NONPOS; }
+    const uint16_t sf = col_at(T.sample_flags, PM_COL_SAMPLE_FLAGS, T, i);
+    if (!none(col_at(T.sm_clock_mhz, PM_COL_SM_CLOCK, T, i))) flags |= 1u << PM_PF_ANY_SM_FINITE;
+    if (none(col_at(T.temperature_c, PM_COL_TEMPERATURE, T, i))) flags |= 1u << PM_PF_TEMP_MISSING;
+    { const double v = col_at(T.graphics_clock_mhz, PM_COL_GRAPHICS_CLOCK, T, i); if (none(v) || v <= 0) flags |= 1u << PM_PF_GFX_NONPOS; }
+    { const double v = col_at(T.memory_clock_mhz, PM_COL_MEMORY_CLOCK, T, i); if (none(v) || v <= 0) flags |= 1u << PM_PF_MEM_NONPOS; }
+    { const double v = col_at(T.sm_clock_mhz, PM_COL_SM_CLOCK, T, i); if (none(v) || v <= 0) flags |= 1u << PM_PF_SM_NONPOS; }
     if (!(sf & PM_S_THROTTLE_VALID)) flags |= 1u << PM_PF_THROTTLE_MISSING;
-    else thr_or |= (unsigned long long)T.throttle_reasons[i] & ~3ull;
+    else thr_or |= (unsigned long long)col_at(T.throttle_reasons, PM_COL_THROTTLE, T, i) & ~3ull;
     if (sf & PM_S_FOREIGN_PID) flags |= 1u << PM_PF_FOREIGN_PID;
     if (sf & PM_S_NO_COMPUTE_INV) flags |= 1u << PM_PF_NO_COMPUTE_INV;
     if (sf & PM_S_NO_GRAPHICS_INV) flags |= 1u << PM_PF_NO_GRAPHICS_INV;
     if (sf & PM_S_MPS) flags |= 1u << PM_PF_MPS;
     if (sf & PM_S_PID_UNKNOWN) flags |= 1u << PM_PF_PID_UNKNOWN;
     if (sf & PM_S_REF_FOREIGN) flags |= 1u << PM_PF_REF_FOREIGN;
-    if ((sf & PM_S_MEMORY_POWER_SET) && T.memory_power_source[i]) src_mask |= 1u << (T.memory_power_source[i] & 15);
-    plim_none += none(T.power_limit_w[i]);
-    enf_none += none(T.enforced_power_limit_w[i]);
-    pst_none += none(T.pstate[i]);
+    if ((sf & PM_S_MEMORY_POWER_SET) && col_at(T.memory_power_source, PM_COL_MEMORY_SOURCE, T, i)) src_mask |= 1u << (col_at(T.memory_power_source, PM_COL_MEMORY_SOURCE, T, i) & 15);
+    plim_none += none(col_at(T.power_limit_w, PM_COL_POWER_LIMIT, T, i));
+    enf_none += none(col_at(T.enforced_power_limit_w, PM_COL_ENFORCED_LIMIT, T, i));
+    pst_none += none(col_at(T.pstate, PM_COL_PSTATE, T, i));
   }
   // negative power is checked over the covering samples
   for (int64_t i = cb + threadIdx.x; i < ce; i += blockDim.x) {
-    const double v = T.power_w[i];
+    const double v = col_at(T.power_w, PM_COL_POWER_W, T, i);
     if (!none(v) && v < 0) neg_power = true;
   }
   // per-column finite counts, minima and maxima (selected columns; gaps from covering)
@@ -331,17 +337,17 @@ __device__ void phase_stats(const pm_trials& T, const pm_policy& P, Shared& S, d
   if (threadIdx.x == 0) anchor_idx = 0x7fffffff;
   __syncthreads();
   for (int q = threadIdx.x; q < ncov; q += blockDim.x) {
-    st_t[q] = t[cb + q]; st_p[q] = T.power_w[cb + q]; st_m[q] = T.memory_power_w[cb + q];
-    if (T.sample_flags[cb + q] & PM_S_ENERGY_ANCHOR) atomicMin(&anchor_idx, q);
+    st_t[q] = t[cb + q]; st_p[q] = col_at(T.power_w, PM_COL_POWER_W, T, cb + q); st_m[q] = col_at(T.memory_power_w, PM_COL_MEMORY_POWER_W, T, cb + q);
+    if (col_at(T.sample_flags, PM_COL_SAMPLE_FLAGS, T, cb + q) & PM_S_ENERGY_ANCHOR) atomicMin(&anchor_idx, q);
   }
   __syncthreads();
   {
-    const int64_t anchor = anchor_idx == 0x7fffffff ? 0 : T.energy_int[cb + anchor_idx];
+    const int64_t anchor = anchor_idx == 0x7fffffff ? 0 : col_at(T.energy_int, PM_COL_ENERGY_INT, T, cb + anchor_idx);
     for (int q = threadIdx.x; q < ncov; q += blockDim.x) {
-      const uint16_t sf = T.sample_flags[cb + q];
+      const uint16_t sf = col_at(T.sample_flags, PM_COL_SAMPLE_FLAGS, T, cb + q);
       double v;
-      if (sf & PM_S_ENERGY_INT) v = (double)(long long)((unsigned long long)T.energy_int[cb + q] - (unsigned long long)anchor);
-      else if (sf & PM_S_ENERGY_FLOAT) v = T.energy_float[cb + q] - (double)anchor;
+      if (sf & PM_S_ENERGY_INT) v = (double)(long long)((unsigned long long)col_at(T.energy_int, PM_COL_ENERGY_INT, T, cb + q) - (unsigned long long)anchor);
+      else if (sf & PM_S_ENERGY_FLOAT) v = col_at(T.energy_float, PM_COL_ENERGY_FLOAT, T, cb + q) - (double)anchor;
       else v = dnan();
       st_r[q] = isfinite(v) ? v : dnan();
     }

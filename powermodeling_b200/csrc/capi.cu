@@ -5,14 +5,17 @@
 #include <cuda_runtime.h>
 #include <cstdarg>
 #include <cstdio>
+#include <algorithm>
 #include <cstring>
 #include <mutex>
 #include <string>
 #include <type_traits>
+#include <vector>
 
 #include "pmb200.h"
 #include "pm_layout.h"
 #include "pm_capi.h"
+#include "host_pool.h"
 
 namespace pm {
 int launch_analyze(const pm_trials& T, const pm_policy& P, const pm_trial_results& R, int max_covering,
@@ -74,13 +77,18 @@ namespace {
 // fixed order shared by the sizing and the staging passes.
 template <class T, class F> void visit_trials(T& t, F f) {
   const size_t nt = (size_t)t.n_trials, ns = (size_t)t.n_samples, ne = (size_t)t.n_epochs;
+  // A broadcast column holds one element for every sample.
+  auto per = [&](uint32_t bit) { return (t.broadcast_columns & bit) ? (ns ? size_t(1) : size_t(0)) : ns; };
   f(t.phase_offsets, nt * PM_PHASES + 1);
   f(t.phase_start_s, nt * PM_PHASES); f(t.phase_end_s, nt * PM_PHASES); f(t.phase_present, nt * PM_PHASES);
-  f(t.t_s, ns); f(t.power_w, ns); f(t.memory_power_w, ns);
-  f(t.graphics_clock_mhz, ns); f(t.sm_clock_mhz, ns); f(t.memory_clock_mhz, ns); f(t.temperature_c, ns);
-  f(t.power_limit_w, ns); f(t.enforced_power_limit_w, ns); f(t.pstate, ns);
-  f(t.energy_int, ns); f(t.energy_float, ns); f(t.throttle_reasons, ns); f(t.sample_flags, ns);
-  f(t.memory_power_source, ns);
+  f(t.t_s, ns); f(t.power_w, per(PM_COL_POWER_W)); f(t.memory_power_w, per(PM_COL_MEMORY_POWER_W));
+  f(t.graphics_clock_mhz, per(PM_COL_GRAPHICS_CLOCK)); f(t.sm_clock_mhz, per(PM_COL_SM_CLOCK));
+  f(t.memory_clock_mhz, per(PM_COL_MEMORY_CLOCK)); f(t.temperature_c, per(PM_COL_TEMPERATURE));
+  f(t.power_limit_w, per(PM_COL_POWER_LIMIT)); f(t.enforced_power_limit_w, per(PM_COL_ENFORCED_LIMIT));
+  f(t.pstate, per(PM_COL_PSTATE));
+  f(t.energy_int, per(PM_COL_ENERGY_INT)); f(t.energy_float, per(PM_COL_ENERGY_FLOAT));
+  f(t.throttle_reasons, per(PM_COL_THROTTLE)); f(t.sample_flags, per(PM_COL_SAMPLE_FLAGS));
+  f(t.memory_power_source, per(PM_COL_MEMORY_SOURCE));
   f(t.epoch_offsets, nt * 2 + 1); f(t.epoch_status, nt * 2);
   f(t.epoch_start_s, ne); f(t.epoch_end_s, ne); f(t.epoch_operations, ne); f(t.epoch_logical_bytes, ne);
   f(t.epoch_loop_slots, ne); f(t.epoch_counts_exact, ne);
@@ -89,21 +97,20 @@ template <class T, class F> void visit_trials(T& t, F f) {
 
 constexpr size_t align256(size_t x) { return (x + 255) & ~size_t(255); }
 
-int check_trials_host(const pm_trials& T, int* max_covering) {
+// Structural checks of a host batch (sizes, NULL arrays, offsets, limits).
+// The per-sample order check runs in the staging pass (scan_slots).
+int check_trials_host(const pm_trials& T) {
   if (T.n_trials < 0 || T.n_samples < 0 || T.n_epochs < 0) return fail(PM_E_INVALID, "negative batch size");
+  if (T.broadcast_columns & ~uint32_t(PM_COL_ALL)) return fail(PM_E_INVALID, "broadcast_columns has unknown bits");
   bool null_seen = false;
   visit_trials(T, [&](const auto* p, size_t n) { if (n && !p) null_seen = true; });
   if (null_seen) return fail(PM_E_INVALID, "a pm_trials array is NULL");
   if (T.phase_offsets[0] != 0 || T.phase_offsets[(size_t)T.n_trials * PM_PHASES] != T.n_samples)
     return fail(PM_E_INVALID, "phase_offsets must start at 0 and end at n_samples");
-  int64_t mc = 0;
   for (size_t s = 0; s < (size_t)T.n_trials * PM_PHASES; ++s) {
     const int64_t b = T.phase_offsets[s], e = T.phase_offsets[s + 1];
     if (e < b) return fail(PM_E_INVALID, "phase_offsets must be non-decreasing");
     if (e - b > kMaxPhaseSamples) return fail(PM_E_LIMIT, "a phase holds %lld samples; the limit is %d", (long long)(e - b), kMaxPhaseSamples);
-    for (int64_t i = b + 1; i < e; ++i)
-      if (!(T.t_s[i] > T.t_s[i - 1])) return fail(PM_E_INVALID, "t_s must increase strictly within a phase (slot %zu)", s);
-    if (e - b > mc) mc = e - b;
   }
   if (T.epoch_offsets[0] != 0 || T.epoch_offsets[(size_t)T.n_trials * 2] != T.n_epochs)
     return fail(PM_E_INVALID, "epoch_offsets must start at 0 and end at n_epochs");
@@ -112,8 +119,21 @@ int check_trials_host(const pm_trials& T, int* max_covering) {
     if (n < 0) return fail(PM_E_INVALID, "epoch_offsets must be non-decreasing");
     if (n > kMaxEpochsPerArm) return fail(PM_E_LIMIT, "an arm lists %d epochs; the limit is %d", n, kMaxEpochsPerArm);
   }
-  *max_covering = (int)mc;
   return PM_OK;
+}
+
+// Phase slots [s0, s1): the longest phase, and the first slot whose t_s does
+// not increase strictly (-1 if none).
+void scan_slots(const pm_trials& T, size_t s0, size_t s1, int64_t* longest, int64_t* bad_slot) {
+  int64_t mc = 0, bad = -1;
+  for (size_t s = s0; s < s1 && bad < 0; ++s) {
+    const int64_t b = T.phase_offsets[s], e = T.phase_offsets[s + 1];
+    for (int64_t i = b + 1; i < e; ++i)
+      if (!(T.t_s[i] > T.t_s[i - 1])) { bad = (int64_t)s; break; }
+    if (e - b > mc) mc = e - b;
+  }
+  *longest = mc;
+  *bad_slot = bad;
 }
 
 template <class F> void visit_results(pm_trial_results& r, size_t n, F f) {
@@ -206,6 +226,7 @@ int pm_analyze_trials_device(const pm_trials* trials, const pm_policy* policy, p
                              void* scratch, size_t scratch_bytes, void* stream) {
   if (!trials || !policy || !out) return fail(PM_E_INVALID, "NULL argument");
   if (trials->n_trials < 0 || trials->max_phase_samples < 0) return fail(PM_E_INVALID, "negative size");
+  if (trials->broadcast_columns & ~uint32_t(PM_COL_ALL)) return fail(PM_E_INVALID, "broadcast_columns has unknown bits");
   if (trials->max_phase_samples > kMaxPhaseSamples) return fail(PM_E_LIMIT, "max_phase_samples beyond %d", kMaxPhaseSamples);
   if (policy->min_samples < 2) return fail(PM_E_INVALID, "min_samples must be >= 2");
   const size_t need = analyze_scratch_bytes(trials->n_trials, trials->max_phase_samples);
@@ -233,7 +254,7 @@ struct StagedTrials {
 // Size, reserve (plus `extra_dev`/`extra_host` bytes after the results) and
 // stage a host batch into the device arena; enqueue the H2D copy.
 int stage_trials(Arena& A, const pm_trials& T, size_t extra_dev, size_t extra_host, StagedTrials& S) {
-  int rc = check_trials_host(T, &S.max_cov);
+  int rc = check_trials_host(T);
   if (rc) return rc;
   const size_t n = (size_t)T.n_trials;
   visit_trials(T, [&](const auto* p, size_t count) { S.in_bytes = align256(S.in_bytes) + count * sizeof(*p); });
@@ -241,31 +262,80 @@ int stage_trials(Arena& A, const pm_trials& T, size_t extra_dev, size_t extra_ho
   pm_trial_results probe{};
   visit_results(probe, n, [&](auto* p, size_t count) { S.res_bytes = align256(S.res_bytes) + count * sizeof(*p); });
   S.res_bytes = align256(S.res_bytes);
-  const size_t scratch = analyze_scratch_bytes((int)n, S.max_cov);
+  // The scratch size depends on the longest phase, known only after the scan:
+  // reserve for the worst case the batch allows (its longest offsets span).
+  int64_t bound = 0;
+  for (size_t s = 0; s < n * PM_PHASES; ++s) bound = std::max<int64_t>(bound, T.phase_offsets[s + 1] - T.phase_offsets[s]);
+  const size_t scratch = analyze_scratch_bytes((int)n, (int)bound);
   S.end = S.in_bytes + S.res_bytes;
   if ((rc = arena_reserve(A, S.end + scratch + extra_dev, S.end + extra_host))) return rc;
   S.dev = T;
+  S.max_cov = (int)bound;
   S.dev.max_phase_samples = S.max_cov;
+
+  // Copy pieces of at most kPiece bytes in destination order, then the
+  // sample-order scan in slot ranges; pool threads and this thread share them.
+  constexpr size_t kPiece = size_t(1) << 20, kDmaMin = size_t(4) << 20;
+  struct Piece { const char* src; size_t dst; size_t bytes; };
+  std::vector<Piece> pieces;
+  pieces.reserve(S.in_bytes / kPiece + 64);
   Layout hl{static_cast<char*>(A.host)};
   size_t offs[32]; int k = 0;
   visit_trials(T, [&](const auto* p, size_t count) {
     using E = std::remove_cv_t<std::remove_pointer_t<decltype(p)>>;
     E* dst = nullptr;
     hl.place(dst, count);
-    if (count) memcpy(dst, p, count * sizeof(E));
-    offs[k++] = reinterpret_cast<char*>(dst) - static_cast<char*>(A.host);
+    const size_t at = reinterpret_cast<char*>(dst) - static_cast<char*>(A.host);
+    const size_t bytes = count * sizeof(E);
+    for (size_t o = 0; o < bytes; o += kPiece)
+      pieces.push_back({reinterpret_cast<const char*>(p) + o, at + o, std::min(kPiece, bytes - o)});
+    offs[k++] = at;
   });
+  const size_t slots = n * PM_PHASES;
+  const size_t scan_tasks = slots ? std::min<size_t>(64, (slots + 255) / 256) : 0;
+  std::vector<int64_t> longest(scan_tasks, 0), bad(scan_tasks, -1);
+  char* host = static_cast<char*>(A.host);
+  char* dev = static_cast<char*>(A.dev);
+  HostBatch batch(pieces.size() + scan_tasks, [&](size_t i) {
+    if (i < pieces.size()) {
+      memcpy(host + pieces[i].dst, pieces[i].src, pieces[i].bytes);
+    } else {
+      const size_t t = i - pieces.size();
+      scan_slots(T, slots * t / scan_tasks, slots * (t + 1) / scan_tasks, &longest[t], &bad[t]);
+    }
+  });
+  // Start the DMA of each contiguous staged prefix as soon as it is complete.
+  size_t ready = 0, issued = 0;
+  cudaError_t dma = cudaSuccess;
+  auto progress = [&] {
+    while (ready < pieces.size() && batch.done(ready)) ++ready;
+    const size_t upto = ready == pieces.size() ? S.in_bytes : (ready ? pieces[ready - 1].dst + pieces[ready - 1].bytes : 0);
+    if (dma == cudaSuccess && upto > issued && (upto - issued >= kDmaMin || ready == pieces.size())) {
+      dma = cudaMemcpyAsync(dev + issued, host + issued, upto - issued, cudaMemcpyHostToDevice, A.stream);
+      issued = upto;
+    }
+  };
+  run_host_batch(batch, progress);
+  progress();
+  if (dma != cudaSuccess) {
+    cudaStreamSynchronize(A.stream);
+    return cuda_fail(dma, "cudaMemcpyAsync(inputs)");
+  }
+  for (size_t t = 0; t < scan_tasks; ++t) {
+    if (bad[t] >= 0) {
+      cudaStreamSynchronize(A.stream);   // the staged copy must finish before the buffer is reused
+      return fail(PM_E_INVALID, "t_s must increase strictly within a phase (slot %lld)", (long long)bad[t]);
+    }
+  }
   k = 0;
   visit_trials(S.dev, [&](auto& p, size_t) {
     using Ptr = std::remove_reference_t<decltype(p)>;
-    p = reinterpret_cast<Ptr>(static_cast<char*>(A.dev) + offs[k++]);
+    p = reinterpret_cast<Ptr>(dev + offs[k++]);
   });
-  cudaError_t e = cudaMemcpyAsync(A.dev, A.host, S.in_bytes, cudaMemcpyHostToDevice, A.stream);
-  if (e != cudaSuccess) return cuda_fail(e, "cudaMemcpyAsync(inputs)");
-  Layout dl{static_cast<char*>(A.dev) + S.in_bytes}, rl{static_cast<char*>(A.host) + S.in_bytes};
+  Layout dl{dev + S.in_bytes}, rl{host + S.in_bytes};
   visit_results(S.dres, n, [&](auto*& p, size_t count) { dl.place(p, count); });
   visit_results(S.hres, n, [&](auto*& p, size_t count) { rl.place(p, count); });
-  S.gscratch = scratch ? reinterpret_cast<double*>(static_cast<char*>(A.dev) + S.end + extra_dev) : nullptr;
+  S.gscratch = scratch ? reinterpret_cast<double*>(dev + S.end + extra_dev) : nullptr;
   return PM_OK;
 }
 

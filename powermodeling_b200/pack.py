@@ -92,6 +92,7 @@ class Packed:
     max_phase_samples: int
     samples: list = field(default_factory=list)       # per slot: sorted sample dicts (for host-side lists)
     foreign_pids: list = field(default_factory=list)  # per slot: list of (index, pids)
+    broadcast: int = 0                                # PM_COL_* bits of the one-element columns
 
 
 class _Columns:
@@ -313,7 +314,28 @@ def pack_trials(records: list, host_flags: list, architectures: Mapping) -> Pack
         "epoch_counts_exact": np.asarray([r[5] for r in ep_rows], dtype=np.uint8),
         "trial_scalars": np.ascontiguousarray(scalars.reshape(-1)), "trial_flags": tflags,
     }
-    return Packed(arrays, nt, ns, len(ep_rows), longest, slot_samples, slot_foreign)
+    broadcast = broadcast_constant_columns(arrays, ns)
+    return Packed(arrays, nt, ns, len(ep_rows), longest, slot_samples, slot_foreign, broadcast)
+
+
+def broadcast_constant_columns(arrays: dict, n_samples: int) -> int:
+    """Replace every per-sample column whose samples are bitwise identical by its first element.
+
+    Returns the PM_COL_* bits of the replaced columns.  Bitwise comparison
+    keeps NaN payloads and signed zeros exactly as the samples had them, so
+    the kernel reads the same value for every sample either way.
+    """
+    bits = 0
+    if n_samples == 0:
+        return 0
+    ints = {1: np.uint8, 2: np.uint16, 4: np.uint32, 8: np.uint64}
+    for name, bit in N.BROADCAST_COLUMNS:
+        a = arrays[name]
+        raw = a.view(ints[a.itemsize])
+        if (raw == raw[0]).all():
+            arrays[name] = np.ascontiguousarray(a[:1])
+            bits |= bit
+    return bits
 
 
 def trials_struct(p: Packed) -> N.Trials:
@@ -324,4 +346,5 @@ def trials_struct(p: Packed) -> N.Trials:
         a = p.arrays[name]
         assert a.dtype == dtype and a.flags["C_CONTIGUOUS"], name
         setattr(t, name, a.ctypes.data if a.size else None)
+    t.broadcast_columns = p.broadcast
     return t

@@ -91,3 +91,28 @@ def test_full_size_sweep_against_oracle(gpu_ready):
         for metric in METRICS:
             vals = [v for t in members if (v := O.num(t.get(metric))) is not None]
             assert g["ci95"][metric] == O.median_ci(vals, seed, 10000), metric
+
+
+def test_host_staging_rejects_unsorted_samples_then_recovers(gpu_ready):
+    """The staged host path checks sample order while copying; an error leaves the workspace reusable."""
+    from powermodeling_b200 import _native as N
+    from powermodeling_b200 import analysis as A
+    from powermodeling_b200.pack import trials_struct
+    from powermodeling_b200.synthetic import ANALYSIS_POLICY, SweepShape, make_sweep
+    records = make_sweep(SweepShape(points=3, repeats=4), seed=21)
+    packed, _, _ = A.prepare(records)
+    policy = A.AnalysisPolicy(**ANALYSIS_POLICY).native()
+    t_s = packed.arrays["t_s"]
+    offsets = packed.arrays["phase_offsets"]
+    slot = 7
+    i = int(offsets[slot]) + 3
+    good = A._Views(packed.n_trials)
+    assert N.library().pm_analyze_trials(trials_struct(packed), policy, good.struct()) == 0
+    t_s[i], t_s[i + 1] = t_s[i + 1], t_s[i]
+    bad = A._Views(packed.n_trials)
+    rc = N.library().pm_analyze_trials(trials_struct(packed), policy, bad.struct())
+    assert rc == -1 and f"slot {slot}" in N.last_error()   # PM_E_INVALID
+    t_s[i], t_s[i + 1] = t_s[i + 1], t_s[i]
+    again = A._Views(packed.n_trials)
+    assert N.library().pm_analyze_trials(trials_struct(packed), policy, again.struct()) == 0
+    assert np.array_equal(np.nan_to_num(good.trial_out), np.nan_to_num(again.trial_out))
