@@ -109,7 +109,10 @@ typedef struct {
  * (trial, phase) slot are one CSR segment, sorted by strictly increasing t_s
  * (the host applies the reference's last-wins de-duplication, analysis.py:85-91).
  * Every pointer is host memory for pm_analyze_trials and device memory for
- * pm_analyze_trials_device.
+ * pm_analyze_trials_device.  A per-sample array holds n_samples elements, or
+ * exactly one when its PM_COL_* bit is set in broadcast_columns; the device
+ * entry point cannot check device array lengths, so a bit left unset for a
+ * one-element array reads past its end.
  */
 typedef struct {
   int32_t n_trials;

@@ -49,6 +49,7 @@ struct Shared {
   int32_t nfin[C_COUNT];
   double cmin[C_COUNT], cmax[C_COUNT];
   int32_t sort_cols[C_COUNT], nsort, sort_p;
+  int32_t distinct_power;   // distinct finite powers of a sorted power column, -1 if not sorted
 };
 
 // Sample i of a per-sample column; a broadcast column holds one element.
@@ -165,13 +166,20 @@ __device__ void phase_stats(const pm_trials& T, const pm_policy& P, Shared& S, d
   start = start + trim; end = end - trim;
   const double duration = end - start;
   const double* t = T.t_s;
-  if (threadIdx.x == 0) {
-    const int64_t lo = lower_bound(t, seg_b, seg_e, start);
-    const int64_t hi = upper_bound(t, seg_b, seg_e, end);
-    S.sel_lo = lo; S.sel_hi = hi;
-    S.cov_lo = lo > seg_b ? lo - 1 : lo;
-    S.cov_hi = hi < seg_e ? hi + 1 : hi;
+  // Selected window [lower_bound(start), upper_bound(end)): warp 0 and warp 1
+  // search at once, 32 probes per round.
+  if (threadIdx.x < 64) {
+    const int lane = threadIdx.x & 31;
+    const bool upper = threadIdx.x >= 32;
+    const int64_t r = warp_bound(t, seg_b, seg_e, upper ? end : start, upper, lane);
+    if (lane == 0) {
+      if (upper) { S.sel_hi = r; S.cov_hi = r < seg_e ? r + 1 : r; }
+      else { S.sel_lo = r; S.cov_lo = r > seg_b ? r - 1 : r; }
+    }
+  }
+  if (threadIdx.x == 64) {
     S.nchange = 0;
+    S.distinct_power = -1;
     for (int c = 0; c < C_COUNT; ++c) S.nfin[c] = 0;
   }
   __syncthreads();
@@ -324,7 +332,29 @@ __device__ void phase_stats(const pm_trials& T, const pm_policy& P, Shared& S, d
   }
   __syncthreads();
   // ---- sort the varying columns over their finite prefix length (power of two)
-  if (S.nsort) bitonic_sort_columns(sortbuf, SP, S.sort_cols, S.nsort, S.sort_p);
+  // Sort the varying columns one after another, values in registers; the
+  // power column's distinct count follows from its sorted order.
+  if (S.nsort) {
+    const int P = S.sort_p;
+    double* xchg = sortbuf + (size_t)(C_COUNT + S_TERM_P) * SP;   // unused until the energy terms
+    bool power_sorted = false;
+    for (int a = 0; a < S.nsort; ++a) {
+      double* v = sortbuf + (size_t)S.sort_cols[a] * SP;
+      power_sorted |= S.sort_cols[a] == C_POWER;
+      if (P <= (int)blockDim.x) cta_register_sort<1>(v, P, xchg);
+      else if (P <= 2 * (int)blockDim.x) cta_register_sort<2>(v, P, xchg);
+      else if (P <= 4 * (int)blockDim.x) cta_register_sort<4>(v, P, xchg);
+      else if (P <= 8 * (int)blockDim.x) cta_register_sort<8>(v, P, xchg);
+      else { const int col = S.sort_cols[a]; bitonic_sort_columns(sortbuf, SP, &col, 1, P); }
+    }
+    if (power_sorted) {
+      if (threadIdx.x == 0) S.distinct_power = 0;
+      __syncthreads();
+      const int d = warp_share_distinct(sortbuf + (size_t)C_POWER * SP, S.nfin[C_POWER]);
+      if ((threadIdx.x & 31) == 0 && d) atomicAdd(&S.distinct_power, d);
+      __syncthreads();
+    }
+  }
   // ---- energies: stage the covering samples, form trapezoid terms in
   // parallel, then accumulate each sum on one lane in the reference's order.
   double* st_t = sortbuf + (size_t)(C_COUNT + S_T) * SP;
@@ -435,14 +465,10 @@ __device__ void phase_stats(const pm_trials& T, const pm_policy& P, Shared& S, d
     po[PM_PO_GAP_MAX_S] = ngap ? S.cmax[C_GAP] : dnan();
     po[PM_PO_CHANGE_MEDIAN_S] = column_median(C_CHANGE);
     {
+      // A sorted (varying) power column was counted by its warp; otherwise
+      // the column holds one repeated value or none.
       const int n = S.nfin[C_POWER];
-      int distinct = n ? 1 : 0;
-      if (n > 1 && S.cmin[C_POWER] != S.cmax[C_POWER]) {
-        const double* pw = sortbuf + C_POWER * SP;
-        distinct = 0;
-        for (int i = 0; i < n; ++i) distinct += (i == 0 || pw[i] != pw[i - 1]);
-      }
-      po[PM_PO_DISTINCT_POWER] = distinct;
+      po[PM_PO_DISTINCT_POWER] = S.distinct_power >= 0 ? S.distinct_power : (n ? 1 : 0);
     }
     const int stat_cols[7] = {C_GFX, C_SM, C_MEM, C_TEMP, C_PLIMIT, C_ENF, C_PSTATE};
     const int med_slot[7] = {PM_PO_GFX_MED, PM_PO_SM_MED, PM_PO_MEM_MED, PM_PO_TEMP_MED, PM_PO_PLIMIT_MED, PM_PO_ENF_MED, PM_PO_PSTATE_MED};
@@ -510,17 +536,23 @@ analyze_kernel(pm_trials T, pm_policy P, pm_trial_results R, int SP, double* gsc
   extern __shared__ double dyn[];
   const int trial = blockIdx.x;
   double* sortbuf = gscratch ? gscratch + (size_t)blockIdx.x * kTileColumns * SP : dyn;
-  const double* ts = T.trial_scalars + (size_t)trial * PM_TS_COUNT;
+  // The trial's scalars, read many times by the trial-level code: one coalesced load.
+  __shared__ double s_ts[PM_TS_COUNT];
+  for (int i = threadIdx.x; i < PM_TS_COUNT; i += blockDim.x) s_ts[i] = T.trial_scalars[(size_t)trial * PM_TS_COUNT + i];
+  __syncthreads();
+  const double* ts = s_ts;
   const uint32_t tflags = T.trial_flags[trial];
   const int wl = tflags & PM_T_WORKLOAD_MASK;
   const bool tensor = wl == PM_WL_TENSOR, memory = wl == PM_WL_MEMORY, sfu = wl == PM_WL_SFU, nonlinear = wl == PM_WL_NONLINEAR;
   const bool energy_wl = wl != PM_WL_OTHER;
   const int ms = trial * PM_PHASES;
 
+  // The two arms' epochs are independent: one thread of warp 0 and one of warp 1.
   if (threadIdx.x == 0) {
     measure_epochs(T, P, trial, 0, T.phase_present[ms + PM_MEASURE] ? T.phase_start_s[ms + PM_MEASURE] : dnan(),
                    T.phase_present[ms + PM_MEASURE] ? T.phase_end_s[ms + PM_MEASURE] : dnan(),
                    ts[PM_TS_BENCH_OPERATIONS], ts[PM_TS_BENCH_LOGICAL_BYTES], S.ep[0], S.order[0]);
+  } else if (threadIdx.x == 32) {
     if (T.phase_present[ms + PM_REFERENCE])
       measure_epochs(T, P, trial, 1, T.phase_start_s[ms + PM_REFERENCE], T.phase_end_s[ms + PM_REFERENCE],
                      ts[PM_TS_REF_OPERATIONS], ts[PM_TS_REF_LOGICAL_BYTES], S.ep[1], S.order[1]);
@@ -993,7 +1025,13 @@ int launch_analyze(const pm_trials& T, const pm_policy& P, const pm_trial_result
   if (use_global && !gscratch) return 1;  // caller must supply scratch
   if (T.n_trials == 0) return 0;
   const size_t dyn = use_global ? 0 : smem;
-  if (dyn > 48 * 1024) cudaFuncSetAttribute(analyze_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)dyn);
+  // Static plus dynamic shared memory above 48 KB needs the opt-in attribute.
+  static size_t static_bytes = [] {
+    cudaFuncAttributes attr{};
+    return cudaFuncGetAttributes(&attr, analyze_kernel) == cudaSuccess ? attr.sharedSizeBytes : size_t(48 * 1024);
+  }();
+  if (static_bytes + dyn > 48 * 1024)
+    cudaFuncSetAttribute(analyze_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)dyn);
   analyze_kernel<<<T.n_trials, kThreads, dyn, stream>>>(T, P, R, SP, use_global ? gscratch : nullptr);
   return 0;
 }

@@ -48,26 +48,34 @@ __device__ __forceinline__ uint32_t twist_one(uint32_t cur, uint32_t next, uint3
   return far ^ (y >> 1) ^ ((y & 1u) ? 0x9908b0dfu : 0u);
 }
 
-// init_by_array(key, key_len) on a 624-word state (single thread).
+// init_by_array(key, key_len) on a 624-word state (single thread), with the
+// key words of |seed| (one if seed < 2^32, else two).  Both of the reference
+// algorithm's loops are unwound into straight index runs (the wrap of i at
+// 624 and the alternation of j become explicit), so each step is the
+// dependent multiply-xor-add on `prev` and nothing else.
 __device__ void seed_state(uint32_t* mt, uint64_t seed) {
-  for (int i = 0; i < kMtN; ++i) mt[i] = c_mt_init[i];
-  uint32_t key[2] = {(uint32_t)seed, (uint32_t)(seed >> 32)};
-  const int key_len = (seed >> 32) ? 2 : 1;
-  int i = 1, j = 0;
-  uint32_t prev = mt[0];
-  for (int k = kMtN; k; --k) {
-    prev = (mt[i] ^ ((prev ^ (prev >> 30)) * 1664525u)) + key[j] + (uint32_t)j;
-    mt[i] = prev;
-    ++i; ++j;
-    if (i >= kMtN) { mt[0] = prev; i = 1; }
-    if (j >= key_len) j = 0;
+  const bool two = (seed >> 32) != 0;
+  const uint32_t add0 = (uint32_t)seed;                           // key[0] + 0
+  const uint32_t add1 = two ? (uint32_t)(seed >> 32) + 1u : add0;  // key[1] + 1, or key[0] again
+  uint32_t prev = c_mt_init[0];
+  // Loop 1 (624 steps): i = 1..623, then i wraps (mt[0] = mt[623]) and i = 1 once more.
+#pragma unroll 8
+  for (int t = 0; t < kMtN - 1; ++t) {
+    prev = (c_mt_init[1 + t] ^ ((prev ^ (prev >> 30)) * 1664525u)) + ((t & 1) ? add1 : add0);
+    mt[1 + t] = prev;
   }
-  for (int k = kMtN - 1; k; --k) {
+  mt[0] = prev;
+  prev = (mt[1] ^ ((prev ^ (prev >> 30)) * 1664525u)) + (((kMtN - 1) & 1) ? add1 : add0);
+  mt[1] = prev;
+  // Loop 2 (623 steps): i = 2..623, then i wraps (mt[0] = mt[623]) and i = 1.
+#pragma unroll 8
+  for (int i = 2; i < kMtN; ++i) {
     prev = (mt[i] ^ ((prev ^ (prev >> 30)) * 1566083941u)) - (uint32_t)i;
     mt[i] = prev;
-    ++i;
-    if (i >= kMtN) { mt[0] = prev; i = 1; }
   }
+  mt[0] = prev;
+  prev = (mt[1] ^ ((prev ^ (prev >> 30)) * 1566083941u)) - 1u;
+  mt[1] = prev;
   mt[0] = 0x80000000u;
 }
 
@@ -121,7 +129,6 @@ __device__ void multiset_unrank(int r, int n, int* a, const uint32_t (*binom)[16
   }
 }
 
-// Dynamic shared memory layout (byte offsets) for a launch.
 // One resample of a group with exactly N members: draw N indices from the
 // ring, sort them (registers only) and count the multiset.  N <= 7.
 template <int N>
@@ -147,27 +154,39 @@ __device__ __forceinline__ void histogram_resample(const uint32_t* ring, uint32_
   atomicAdd(&hist[r], 1u);
 }
 
+// Dynamic shared memory layout (byte offsets) for a launch.  The histogram
+// path (every group has at most kHistMaxN members) folds in shared tables:
+// per metric the values in rank order and the member index of each rank, a
+// median-pair table per metric, and the index counts of every multiset bin.
 struct BootSmem {
-  size_t vals, cnt, rank_of, sorted_v, ptab, total;
+  size_t vals, cnt, rank_of, sorted_v, ptab, fold_sorted, fold_index, fold_pairs, bin_counts, total;
   __host__ __device__ BootSmem(int M, int mm, bool direct) {
+    auto up = [](size_t x) { return (x + 15) & ~(size_t)15; };
     vals = 0;
     cnt = (size_t)M * mm * sizeof(double);
-    rank_of = (cnt + (size_t)M * sizeof(int) + 15) & ~(size_t)15;
+    rank_of = up(cnt + (size_t)M * sizeof(int));
     sorted_v = rank_of + kDirectMaxN * sizeof(int);
     ptab = sorted_v + kDirectMaxN * sizeof(double);
-    total = direct ? ptab + (size_t)kDirectMaxN * kDirectMaxN * sizeof(uint32_t) : rank_of;
+    fold_sorted = rank_of;
+    fold_index = up(fold_sorted + (size_t)M * kHistMaxN * sizeof(double));
+    fold_pairs = up(fold_index + (size_t)M * kHistMaxN);
+    bin_counts = up(fold_pairs + (size_t)M * kHistMaxN * kHistMaxN * sizeof(uint32_t));
+    total = direct ? ptab + (size_t)kDirectMaxN * kDirectMaxN * sizeof(uint32_t)
+                   : up(bin_counts + (size_t)kMaxBins * kHistMaxN);
   }
 };
 
 __global__ void __launch_bounds__(kBootThreads) bootstrap_kernel(BootArgs A) {
   extern __shared__ __align__(16) unsigned char dsm[];
   __shared__ uint32_t mt[2][kMtN];
+  __shared__ uint32_t mt_seed[kMtN];
   __shared__ uint32_t ring[kRing];
   __shared__ uint32_t hist[kMaxBins];
   __shared__ uint32_t binom[16][16];
-  __shared__ int n_list[kDirectMaxN + 1];
+  __shared__ uint32_t n_mask[(kDirectMaxN + 1 + 31) / 32];
   for (int i = threadIdx.x; i < 256; i += blockDim.x) binom[i >> 4][i & 15] = c_binom[i >> 4][i & 15];
-  __shared__ int n_distinct;
+  for (int i = threadIdx.x; i < (kDirectMaxN + 1 + 31) / 32; i += blockDim.x) n_mask[i] = 0;
+  __syncthreads();
   const int g = blockIdx.x;
   const int m0 = A.offsets[g], m1 = A.offsets[g + 1];
   const int members = m1 - m0;
@@ -177,6 +196,11 @@ __global__ void __launch_bounds__(kBootThreads) bootstrap_kernel(BootArgs A) {
       A.medians[(size_t)g * M + m] = A.lo[(size_t)g * M + m] = A.hi[(size_t)g * M + m] = dnan();
     return;
   }
+  // The seeded state is the same for every metric (each _median_ci call
+  // starts random.Random(seed) afresh): one thread of the last warp computes
+  // it while the others gather the metric values.
+  // (The barrier after the gather orders the seed before its first use.)
+  if (threadIdx.x == blockDim.x - 32) seed_state(mt_seed, A.seeds[g]);
   const BootSmem L(M, A.max_members, A.max_members > kHistMaxN);
   double* vals = reinterpret_cast<double*>(dsm + L.vals);
   int* cnt = reinterpret_cast<int*>(dsm + L.cnt);
@@ -211,29 +235,17 @@ __global__ void __launch_bounds__(kBootThreads) bootstrap_kernel(BootArgs A) {
     A.medians[(size_t)g * M + m] = med;
     A.lo[(size_t)g * M + m] = dnan();
     A.hi[(size_t)g * M + m] = dnan();
-  }
-  __syncthreads();
-  if (threadIdx.x == 0) {
-    int k = 0;
-    for (int m = 0; m < M; ++m) {
-      const int c = cnt[m];
-      if (c < 3) continue;
-      bool seen = false;
-      for (int q = 0; q < k; ++q) seen |= n_list[q] == c;
-      if (!seen) n_list[k++] = c;
-    }
-    n_distinct = k;
+    if (c >= 3) atomicOr(&n_mask[c >> 5], 1u << (c & 31));   // intervals need n >= 3
   }
   __syncthreads();
   const int B = A.resamples;
   const int lo_idx = (int)((25LL * B) / 1000 - 1), hi_idx = (int)((975LL * B) / 1000 - 1);
-  for (int d = 0; d < n_distinct; ++d) {
-    const int n = n_list[d];
+  for (int n = 3; n <= kDirectMaxN; ++n) {
+    if (!((n_mask[n >> 5] >> (n & 31)) & 1u)) continue;      // uniform: n_mask is shared
     const bool histogram = n <= kHistMaxN;
-    if (!histogram && n > kDirectMaxN) continue;   // host rejects this before launch
     const int nbins = histogram ? (int)binom[2 * n - 1][n] : 0;
     for (int i = threadIdx.x; i < kMaxBins; i += blockDim.x) hist[i] = 0;
-    if (threadIdx.x == 0) seed_state(mt[0], A.seeds[g]);
+    for (int i = threadIdx.x; i < kMtN; i += blockDim.x) mt[0][i] = mt_seed[i];
     __syncthreads();
     const double nd = (double)n;
     const uint32_t words_per_draw = 2u * (uint32_t)n;          // 2nB < 2^32 (B <= 2^24, n <= 128)
@@ -273,42 +285,65 @@ __global__ void __launch_bounds__(kBootThreads) bootstrap_kernel(BootArgs A) {
     }
     __syncthreads();
     if (histogram) {
-      // Per metric: fold multiset bins into median rank pairs, then select.
+      // Fold the multiset histogram into each metric's median rank pairs, over
+      // (metric, bin) items on every thread: a bin's median ranks under a
+      // metric follow from the bin's index counts walked in that metric's
+      // rank order.
+      double* fsorted = reinterpret_cast<double*>(dsm + L.fold_sorted);       // [M][kHistMaxN]
+      uint8_t* findex = dsm + L.fold_index;                                   // [M][kHistMaxN]
+      uint32_t* fpairs = reinterpret_cast<uint32_t*>(dsm + L.fold_pairs);     // [M][kHistMaxN^2]
+      uint8_t* bcounts = dsm + L.bin_counts;                                  // [kMaxBins][kHistMaxN]
+      for (int bin = threadIdx.x; bin < nbins; bin += blockDim.x) {
+        int ms[kHistMaxN];
+        multiset_unrank(bin, n, ms, binom);
+        uint8_t* c = bcounts + bin * kHistMaxN;
+        for (int i = 0; i < n; ++i) c[i] = 0;
+        for (int i = 0; i < n; ++i) c[ms[i]]++;
+      }
       for (int m = threadIdx.x; m < M; m += blockDim.x) {
         if (cnt[m] != n) continue;
         const double* v = vals + m * A.max_members;
-        // ranks: stable order of the n values
-        int rank_of[kHistMaxN]; double sorted_v[kHistMaxN];
-        for (int i = 0; i < n; ++i) {
+        for (int i = 0; i < n; ++i) {                  // stable ranks: ties keep member order
           int r = 0;
           for (int k = 0; k < n; ++k) r += (v[k] < v[i]) || (v[k] == v[i] && k < i);
-          rank_of[i] = r; sorted_v[r] = v[i];
+          fsorted[m * kHistMaxN + r] = v[i];
+          findex[m * kHistMaxN + r] = (uint8_t)i;
         }
-        uint32_t pairs[kHistMaxN][kHistMaxN];
-        for (int a2 = 0; a2 < n; ++a2) for (int b2 = 0; b2 < n; ++b2) pairs[a2][b2] = 0;
-        for (int bin = 0; bin < nbins; ++bin) {
-          const uint32_t c = hist[bin];
-          if (!c) continue;
-          int ms[kHistMaxN], rk[kHistMaxN];
-          multiset_unrank(bin, n, ms, binom);
-          for (int i = 0; i < n; ++i) rk[i] = rank_of[ms[i]];
-          for (int i = 1; i < n; ++i) { int x = rk[i], k = i - 1; while (k >= 0 && rk[k] > x) { rk[k + 1] = rk[k]; --k; } rk[k + 1] = x; }
-          const int ra = (n & 1) ? rk[n / 2] : rk[n / 2 - 1];
-          const int rb = rk[n / 2];
-          pairs[ra][rb] += c;
+      }
+      for (int i = threadIdx.x; i < M * n * n; i += blockDim.x) fpairs[(i / (n * n)) * kHistMaxN * kHistMaxN + i % (n * n)] = 0;
+      __syncthreads();
+      const int pa = (n & 1) ? n / 2 : n / 2 - 1, pb = n / 2;
+      for (int it = threadIdx.x; it < M * nbins; it += blockDim.x) {
+        const int m = it / nbins, bin = it - m * nbins;
+        const uint32_t h = hist[bin];
+        if (!h || cnt[m] != n) continue;
+        const uint8_t* c = bcounts + bin * kHistMaxN;
+        const uint8_t* idx = findex + m * kHistMaxN;
+        int seen = 0, ra = -1, rb = -1;
+        for (int r = 0; r < n && rb < 0; ++r) {
+          seen += c[idx[r]];
+          if (ra < 0 && pa < seen) ra = r;
+          if (pb < seen) rb = r;
         }
-        double cv[kHistMaxN * kHistMaxN]; uint32_t cc[kHistMaxN * kHistMaxN]; int nc = 0;
+        atomicAdd(&fpairs[m * kHistMaxN * kHistMaxN + ra * n + rb], h);
+      }
+      __syncthreads();
+      // Per metric: the pair values in ascending order with their counts, then
+      // the two order statistics of the B resampled medians.
+      for (int m = threadIdx.x; m < M; m += blockDim.x) {
+        if (cnt[m] != n) continue;
+        const double* sv = fsorted + m * kHistMaxN;
+        const uint32_t* pt = fpairs + m * kHistMaxN * kHistMaxN;
+        double cv[kHistMaxN * (kHistMaxN + 1) / 2]; uint32_t cc[kHistMaxN * (kHistMaxN + 1) / 2]; int nc = 0;
         for (int a2 = 0; a2 < n; ++a2)
           for (int b2 = a2; b2 < n; ++b2)
-            if (pairs[a2][b2]) {
-              cv[nc] = (n & 1) ? sorted_v[a2] : (sorted_v[a2] + sorted_v[b2]) / 2;
-              cc[nc++] = pairs[a2][b2];
+            if (pt[a2 * n + b2]) {
+              const double x = (n & 1) ? sv[a2] : (sv[a2] + sv[b2]) / 2;
+              const uint32_t y = pt[a2 * n + b2];
+              int k = nc - 1;
+              while (k >= 0 && cv[k] > x) { cv[k + 1] = cv[k]; cc[k + 1] = cc[k]; --k; }
+              cv[k + 1] = x; cc[k + 1] = y; ++nc;
             }
-        for (int i = 1; i < nc; ++i) {
-          double x = cv[i]; uint32_t y = cc[i]; int k = i - 1;
-          while (k >= 0 && cv[k] > x) { cv[k + 1] = cv[k]; cc[k + 1] = cc[k]; --k; }
-          cv[k + 1] = x; cc[k + 1] = y;
-        }
         long long cum = 0; double lo = dnan(), hi = dnan();
         for (int i = 0; i < nc; ++i) {
           const long long next = cum + cc[i];
@@ -438,7 +473,13 @@ size_t bootstrap_scratch_bytes(int n_groups, int max_members, int resamples) {
 int launch_bootstrap(const BootArgs& A, cudaStream_t stream) {
   if (A.n_groups == 0) return 0;
   const size_t smem = BootSmem(A.n_metrics, A.max_members, A.max_members > kHistMaxN).total;
-  if (smem > 48 * 1024) cudaFuncSetAttribute(bootstrap_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+  // Static plus dynamic shared memory above 48 KB needs the opt-in attribute.
+  static size_t static_bytes = [] {
+    cudaFuncAttributes attr{};
+    return cudaFuncGetAttributes(&attr, bootstrap_kernel) == cudaSuccess ? attr.sharedSizeBytes : size_t(48 * 1024);
+  }();
+  if (static_bytes + smem > 48 * 1024)
+    cudaFuncSetAttribute(bootstrap_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
   bootstrap_kernel<<<A.n_groups, kBootThreads, smem, stream>>>(A);
   return 0;
 }

@@ -14,17 +14,15 @@ __device__ __forceinline__ double dnan() { return __longlong_as_double(0x7ff8000
 __device__ __forceinline__ bool none(double x) { return isnan(x); }
 __device__ __forceinline__ double dinf() { return __longlong_as_double(0x7ff0000000000000LL); }
 
-// CPython 3.12's float sum(): the first term is added to int 0, then
-// Neumaier's compensated summation (Neumaier 1974) over the rest, with the
-// compensation added once at the end when it is nonzero and finite.
+// CPython 3.12's float sum(): Neumaier's compensated summation (Neumaier
+// 1974) from 0.0 (the int 0 start, converted) over every term, with the
+// compensation added once at the end when it is nonzero and finite.  The
+// step is branch-free so a long sum pipelines on its one dependent add.
 struct NeumaierSum {
   double f = 0.0, c = 0.0;
-  bool started = false;
   __device__ __forceinline__ void add(double x) {
-    if (!started) { f = 0.0 + x; started = true; return; }
-    double t = f + x;
-    if (fabs(f) >= fabs(x)) c += (f - t) + x;
-    else c += (x - t) + f;
+    const double t = f + x;
+    c += fabs(f) >= fabs(x) ? (f - t) + x : (x - t) + f;
     f = t;
   }
   __device__ __forceinline__ double result() const {
@@ -82,6 +80,112 @@ __device__ inline void bitonic_sort_columns(double* base, int stride, const int*
       __syncthreads();
     }
   }
+}
+
+// CTA-wide ascending bitonic sort of v[0, P) (P a power of two, at most
+// E * blockDim.x) with the values in registers: thread t holds elements
+// [t*E, t*E + E).  Exchanges at distance j < E stay inside a thread, j < 32*E
+// are warp shuffles, and only j >= 32*E go through `xchg` (P doubles of
+// shared memory) with a CTA barrier, so P = 512 on 256 threads needs 6
+// barrier stages instead of 45.  All threads of the CTA call it.
+// The compare-exchanges of one bitonic stage between a thread's own
+// elements (distance J < E).
+template <int E, int J>
+__device__ __forceinline__ void register_exchange(double* r, int t, int k) {
+  if (J >= E) return;
+#pragma unroll
+  for (int e = 0; e < E; ++e) {
+    if (e & J) continue;
+    const bool ascending = ((t * E + e) & k) == 0;
+    const double a = r[e], b = r[e | J];
+    if ((a > b) == ascending) { r[e] = b; r[e | J] = a; }
+  }
+}
+
+template <int E>
+__device__ void cta_register_sort(double* v, int P, double* xchg) {
+  const int t = threadIdx.x;
+  double r[E];
+#pragma unroll
+  for (int e = 0; e < E; ++e) r[e] = t * E + e < P ? v[t * E + e] : dinf();
+  for (int k = 2; k <= P; k <<= 1) {
+    for (int j = k >> 1; j > 0; j >>= 1) {
+      if (j < E) {
+        // compile-time distances keep r[] in registers
+        if (j == 1) register_exchange<E, 1>(r, t, k);
+        else if (j == 2) register_exchange<E, 2>(r, t, k);
+        else register_exchange<E, 4>(r, t, k);
+      } else if (j < 32 * E) {
+        const int m = j / E;
+#pragma unroll
+        for (int e = 0; e < E; ++e) {
+          const double other = __shfl_xor_sync(0xffffffffu, r[e], m);
+          const int i = t * E + e;
+          const bool keep_low = ((i & j) == 0) == ((i & k) == 0);
+          const double a = r[e];
+          const double low = a <= other ? a : other, high = a <= other ? other : a;
+          r[e] = keep_low ? low : high;
+        }
+      } else {
+        __syncthreads();
+#pragma unroll
+        for (int e = 0; e < E; ++e)
+          if (t * E + e < P) xchg[t * E + e] = r[e];
+        __syncthreads();
+#pragma unroll
+        for (int e = 0; e < E; ++e) {
+          const int i = t * E + e;
+          if (i >= P) continue;
+          const double other = xchg[i ^ j];
+          const bool keep_low = ((i & j) == 0) == ((i & k) == 0);
+          const double a = r[e];
+          const double low = a <= other ? a : other, high = a <= other ? other : a;
+          r[e] = keep_low ? low : high;
+        }
+      }
+    }
+  }
+  __syncthreads();
+#pragma unroll
+  for (int e = 0; e < E; ++e)
+    if (t * E + e < P) v[t * E + e] = r[e];
+  __syncthreads();
+}
+
+// This thread's share of the distinct values in the sorted prefix v[0, n),
+// summed over its warp (every lane returns the warp's count).
+__device__ inline int warp_share_distinct(const double* v, int n) {
+  int d = 0;
+  for (int i = threadIdx.x; i < n; i += blockDim.x) d += (i == 0 || v[i] != v[i - 1]);
+  for (int o = 16; o; o >>= 1) d += __shfl_xor_sync(0xffffffffu, d, o);
+  return d;
+}
+
+// lower_bound (strict = false: first t[i] >= x) or upper_bound (strict =
+// true: first t[i] > x) over the sorted t[b, e), by one warp: each round
+// probes 32 evenly spaced positions at once, so a segment of n samples takes
+// about log32(n) rounds of loads instead of log2(n).  All lanes return it.
+__device__ inline int64_t warp_bound(const double* t, int64_t b, int64_t e, double x, bool strict, int lane) {
+  int64_t lo = b, hi = e;                       // the answer lies in [lo, hi]
+  while (hi - lo > 32) {
+    const int64_t step = (hi - lo + 31) / 32;
+    const int64_t probe = lo + (int64_t)lane * step;
+    const bool past = probe >= hi || (strict ? t[probe] > x : t[probe] >= x);
+    const unsigned m = __ballot_sync(0xffffffffu, past);
+    if (!m) {
+      lo = lo + 31 * step + 1;
+    } else {
+      const int f = __ffs(m) - 1;
+      if (f == 0) return lo;
+      const int64_t at = lo + (int64_t)f * step;
+      if (at < hi) hi = at;
+      lo = lo + (int64_t)(f - 1) * step + 1;
+    }
+  }
+  const int64_t probe = lo + lane;
+  const bool past = probe < hi && (strict ? t[probe] > x : t[probe] >= x);
+  const unsigned m = __ballot_sync(0xffffffffu, past);
+  return m ? lo + (__ffs(m) - 1) : hi;
 }
 
 }  // namespace pm

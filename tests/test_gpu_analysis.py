@@ -116,3 +116,18 @@ def test_host_staging_rejects_unsorted_samples_then_recovers(gpu_ready):
     again = A._Views(packed.n_trials)
     assert N.library().pm_analyze_trials(trials_struct(packed), policy, again.struct()) == 0
     assert np.array_equal(np.nan_to_num(good.trial_out), np.nan_to_num(again.trial_out))
+
+
+@pytest.mark.parametrize("arm_s", [7.0, 15.0, 26.0], ids=["P1024", "P2048", "P4096-global-scratch"])
+def test_long_phases_match_oracle(gpu_ready, arm_s):
+    """Phases of ~700, ~1500 and ~2600 samples: every sort width of the analysis kernel."""
+    from powermodeling_b200.analysis import analyze_trials
+    from powermodeling_b200.synthetic import ANALYSIS_POLICY, SweepShape, make_sweep
+    records = make_sweep(SweepShape(points=1, repeats=2, arm_s=arm_s, epochs_per_arm=int(arm_s)), seed=9)
+    got = analyze_trials(records, ANALYSIS_POLICY)
+    for record, trial in zip(records, got):
+        expected = O.analyze(record, ANALYSIS_POLICY)
+        problems = diff(expected, trial, TRIAL_KEYS, rel=0.0)
+        for phase, stats in expected["phases"].items():
+            problems += [f"{phase}.{p}" for p in diff(stats, trial["phases"].get(phase, {}), PHASE_KEYS, rel=0.0)]
+        assert not problems, problems
