@@ -178,20 +178,31 @@ def run_b200(args, rank: int, world: int) -> dict | None:
     scratch = torch.empty(max(1, a_scr + b_scr), dtype=torch.uint8, device="cuda")
     flush = torch.empty(256 * 1024 * 1024 // 4, dtype=torch.float32, device="cuda")
     stream = torch.cuda.current_stream()
-    sptr = C.c_void_p(stream.cuda_stream)
+    side = torch.cuda.Stream()
+    sptr, side_ptr = C.c_void_p(stream.cuda_stream), C.c_void_p(side.cuda_stream)
+    boot_scratch = C.c_void_p(scratch.data_ptr() + a_scr)
     native_policy = policy.native()
     ev = [torch.cuda.Event(enable_timing=True) for _ in range(5)]
+    side_ev = [torch.cuda.Event(enable_timing=True) for _ in range(2)]
 
     def step():
+        # The resample draws need only seeds and group sizes: drawn on a side
+        # stream while this rank's trials are analysed and the rows exchanged.
         ev[0].record(stream)
+        side.wait_event(ev[0])
+        side_ev[0].record(side)
+        if own:
+            N.check(lib.pm_bootstrap_prepare_device(job, boot_scratch, b_scr, side_ptr), "prepare")
+        side_ev[1].record(side)
         N.check(lib.pm_analyze_trials_device(trials, native_policy, results, C.c_void_p(scratch.data_ptr()), a_scr, sptr), "analyze")
         ev[1].record(stream)
         if world > 1:
             dist.all_gather_into_tensor(all_metrics, out["metrics"])
             dist.all_gather_into_tensor(all_valid, out["valid"])
         ev[2].record(stream)
+        stream.wait_event(side_ev[1])
         if own:
-            N.check(lib.pm_group_bootstrap_device(job, C.c_void_p(scratch.data_ptr() + a_scr), b_scr, sptr), "bootstrap")
+            N.check(lib.pm_bootstrap_finish_device(job, boot_scratch, b_scr, sptr), "finish")
         ev[3].record(stream)
         if world > 1:
             dist.all_gather_into_tensor(all_group_out, group_out)
@@ -212,25 +223,28 @@ def run_b200(args, rank: int, world: int) -> dict | None:
     torch.cuda.synchronize()
     clocks = ClockSampler(local)
     clocks.start()
-    parts_ms = {"analyze": [], "exchange_rows": [], "bootstrap": [], "exchange_groups": []}
+    parts_ms = {"analyze": [], "exchange_rows": [], "join_and_finish": [], "exchange_groups": []}
+    prepare_ms, step_ms = [], []
     for _ in range(args.steps):
         flush.zero_()                                   # L2 flush, outside the timed events
         step()
         ev[4].synchronize()
         for k, name in enumerate(parts_ms):
             parts_ms[name].append(ev[k].elapsed_time(ev[k + 1]))
+        prepare_ms.append(side_ev[0].elapsed_time(side_ev[1]))
+        step_ms.append(ev[0].elapsed_time(ev[4]))
     torch.cuda.synchronize()
     clock_info = clocks.stop()
     if world > 1:
         dist.barrier()
-    total_ms = sum(sum(v) for v in parts_ms.values())
+    total_ms = sum(step_ms)
     if world > 1:
         t = torch.tensor([total_ms], dtype=torch.float64, device="cuda")
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
         total_ms = float(t.item())
     ms_per_step = total_ms / args.steps
     value = resamples_per_step / (ms_per_step / 1e3)
-    t_analyze, t_boot = parts_ms["analyze"], parts_ms["bootstrap"]
+    t_analyze, t_boot = parts_ms["analyze"], parts_ms["join_and_finish"]
 
     # ---- end to end: host buffers through pm_analyze_sweep, then one gather of group results --------
     # Each rank's groups are its own points, so a rank summarizes its shard with one library call
@@ -299,8 +313,10 @@ def run_b200(args, rank: int, world: int) -> dict | None:
                                       f"results all-gathered over NCCL" if world > 1 else "single GPU"},
             "e2e": {"value": resamples_per_step / e2e_s, "unit": "resamples/s",
                     "h2d_bytes_per_step": int(h2d), "d2h_bytes_per_step": int(d2h), "ms_per_step": e2e_s * 1e3},
-            "gpu_launches": 2 * args.steps,
-            "kernels": {"analyze_kernel_ms": a_ms, "bootstrap_kernel_ms": b_ms,
+            "gpu_launches": (3 if own else 1) * args.steps,
+            "kernels": {"analyze_kernel_ms": a_ms,
+                        "bootstrap_prepare_kernel_ms (side stream, overlaps analyze)": statistics.mean(prepare_ms),
+                        "join_and_bootstrap_finish_ms": b_ms,
                         "exchange_rows_ms": statistics.mean(parts_ms["exchange_rows"]),
                         "exchange_groups_ms": statistics.mean(parts_ms["exchange_groups"])},
             "roofline": roofline, "clocks": clock_info}

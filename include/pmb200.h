@@ -217,9 +217,21 @@ typedef struct {
 } pm_bootstrap_job;
 
 int pm_group_bootstrap(const pm_bootstrap_job* job);
-/* Device scratch for groups of more than 7 members (their index streams). */
+/* Device scratch: one prepared multiset histogram per group, plus index
+ * streams (resamples x 128 bytes per group) when max_members > 7. */
 size_t pm_bootstrap_scratch_bytes(int32_t n_groups, int32_t max_members, int32_t resamples);
+/* Device buffers, stream-ordered: pm_bootstrap_prepare_device then
+ * pm_bootstrap_finish_device, or both at once. */
 int pm_group_bootstrap_device(const pm_bootstrap_job* job, void* scratch, size_t scratch_bytes, void* stream);
+/* The two halves of pm_group_bootstrap_device.  Prepare draws each group's
+ * resamples for its listed member count into scratch; it reads only
+ * group_offsets and seeds, so it may run on another stream while the metric
+ * values are still being computed.  Finish (same job and scratch, ordered
+ * after prepare) gathers the values, uses the prepared draws for every metric
+ * whose finite count equals the member count, draws afresh for other counts,
+ * and writes medians and intervals. */
+int pm_bootstrap_prepare_device(const pm_bootstrap_job* job, void* scratch, size_t scratch_bytes, void* stream);
+int pm_bootstrap_finish_device(const pm_bootstrap_job* job, void* scratch, size_t scratch_bytes, void* stream);
 
 /*
  * summarize's numeric core in one call (analysis.py:1400-1470): analyze every

@@ -139,6 +139,8 @@ def library() -> C.CDLL:
             lib.pm_analyze_scratch_bytes.argtypes = [C.c_int32, C.c_int32]
             lib.pm_group_bootstrap.argtypes = [C.POINTER(BootstrapJob)]
             lib.pm_group_bootstrap_device.argtypes = [C.POINTER(BootstrapJob), _p, C.c_size_t, _p]
+            lib.pm_bootstrap_prepare_device.argtypes = [C.POINTER(BootstrapJob), _p, C.c_size_t, _p]
+            lib.pm_bootstrap_finish_device.argtypes = [C.POINTER(BootstrapJob), _p, C.c_size_t, _p]
             lib.pm_bootstrap_scratch_bytes.restype = C.c_size_t
             lib.pm_bootstrap_scratch_bytes.argtypes = [C.c_int32, C.c_int32, C.c_int32]
             lib.pm_analyze_sweep.argtypes = [C.POINTER(Trials), C.POINTER(Policy), C.POINTER(TrialResults),

@@ -176,15 +176,105 @@ struct BootSmem {
   }
 };
 
+// Scratch layout: the prepared multiset histograms (one per group, kMaxBins
+// words), then, when a group may have more than kHistMaxN members, one index
+// stream per group (B draws of up to kDirectMaxN one-byte indices).
+__host__ __device__ inline size_t hist_area_bytes(int n_groups) {
+  return ((size_t)n_groups * kMaxBins * sizeof(uint32_t) + 255) & ~(size_t)255;
+}
+__device__ inline uint32_t* prepared_hist(const BootArgs& A, int g) {
+  return reinterpret_cast<uint32_t*>(A.scratch) + (size_t)g * kMaxBins;
+}
+__device__ inline uint8_t* index_stream(const BootArgs& A, int g) {
+  return A.max_members > kHistMaxN ? A.scratch + hist_area_bytes(A.n_groups) + (size_t)g * A.resamples * kDirectMaxN
+                                   : nullptr;
+}
+
+// Shared state of one group's stream.
+struct GenShared {
+  uint32_t mt[2][kMtN];
+  uint32_t mt_seed[kMtN];
+  uint32_t ring[kRing];
+  uint32_t hist[kMaxBins];
+  uint32_t binom[16][16];
+};
+
+// The B resamples of n draws from the seeded state in sh.mt_seed: multiset
+// counts into sh.hist (n <= kHistMaxN, hist cleared here) or raw indices into
+// `stream` (n > kHistMaxN).  All threads call it.
+__device__ __forceinline__ void generate_resamples(GenShared& sh, int n, int B, uint8_t* stream) {
+  const bool histogram = n <= kHistMaxN;
+  if (histogram)
+    for (int i = threadIdx.x; i < kMaxBins; i += blockDim.x) sh.hist[i] = 0;
+  for (int i = threadIdx.x; i < kMtN; i += blockDim.x) sh.mt[0][i] = sh.mt_seed[i];
+  __syncthreads();
+  const double nd = (double)n;
+  const uint32_t words_per_draw = 2u * (uint32_t)n;          // 2nB < 2^32 (B <= 2^24, n <= 128)
+  const uint32_t blocks = (uint32_t)((2ull * n * B + kMtN - 1) / kMtN);
+  uint32_t next_r = 0;
+  int slot = 0;                                               // ring slot of the current block
+  for (uint32_t blk = 0; blk < blocks; ++blk) {
+    twist_block(sh.mt[blk & 1], sh.mt[(blk & 1) ^ 1], sh.ring, slot * kMtN);
+    // Words [first, avail) are readable: the previous block and this one.
+    const uint32_t avail = (blk + 1) * (uint32_t)kMtN;
+    const uint32_t first = blk ? avail - 2 * kMtN : 0;
+    const int first_slot = blk ? (slot + 2) % 3 : 0;          // slot of word `first`
+    uint32_t r_end = avail / words_per_draw;
+    if (r_end > (uint32_t)B) r_end = B;
+    for (uint32_t r = next_r + threadIdx.x; r < r_end; r += blockDim.x) {
+      uint32_t pos = first_slot * kMtN + (r * words_per_draw - first);
+      if (pos >= (uint32_t)kRing) pos -= kRing;
+      if (histogram) {
+        switch (n) {
+          case 3: histogram_resample<3>(sh.ring, pos, sh.hist, sh.binom); break;
+          case 4: histogram_resample<4>(sh.ring, pos, sh.hist, sh.binom); break;
+          case 5: histogram_resample<5>(sh.ring, pos, sh.hist, sh.binom); break;
+          case 6: histogram_resample<6>(sh.ring, pos, sh.hist, sh.binom); break;
+          default: histogram_resample<7>(sh.ring, pos, sh.hist, sh.binom); break;
+        }
+      } else {
+        for (int j = 0; j < n; ++j) {
+          const uint32_t w0 = sh.ring[pos]; if (++pos == (uint32_t)kRing) pos = 0;
+          const uint32_t w1 = sh.ring[pos]; if (++pos == (uint32_t)kRing) pos = 0;
+          stream[(size_t)r * n + j] = (uint8_t)draw_index(w0, w1, nd);
+        }
+      }
+    }
+    next_r = r_end;
+    slot = slot == 2 ? 0 : slot + 1;
+  }
+  __syncthreads();
+}
+
+__device__ __forceinline__ void load_binom(GenShared& sh) {
+  for (int i = threadIdx.x; i < 256; i += blockDim.x) sh.binom[i >> 4][i & 15] = c_binom[i >> 4][i & 15];
+}
+
+// Stream generation ahead of the fold: for each group's member count n (the
+// count every metric has when all listed members are valid and finite), the
+// multiset histogram (n <= kHistMaxN) or the index stream.  It needs only
+// seeds and group sizes, so it can run while the trials are still analysed.
+__global__ void __launch_bounds__(kBootThreads) bootstrap_prepare_kernel(BootArgs A) {
+  __shared__ GenShared sh;
+  const int g = blockIdx.x;
+  const int n = A.offsets[g + 1] - A.offsets[g];
+  if (n < 3 || n > A.max_members || n > kDirectMaxN) return;   // no interval for n < 3 (uniform exit)
+  load_binom(sh);
+  if (threadIdx.x == 0) seed_state(sh.mt_seed, A.seeds[g]);
+  __syncthreads();
+  generate_resamples(sh, n, A.resamples, index_stream(A, g));
+  if (n <= kHistMaxN) {
+    uint32_t* out = prepared_hist(A, g);
+    const int nbins = (int)sh.binom[2 * n - 1][n];
+    for (int i = threadIdx.x; i < nbins; i += blockDim.x) out[i] = sh.hist[i];
+  }
+}
+
 __global__ void __launch_bounds__(kBootThreads) bootstrap_kernel(BootArgs A) {
   extern __shared__ __align__(16) unsigned char dsm[];
-  __shared__ uint32_t mt[2][kMtN];
-  __shared__ uint32_t mt_seed[kMtN];
-  __shared__ uint32_t ring[kRing];
-  __shared__ uint32_t hist[kMaxBins];
-  __shared__ uint32_t binom[16][16];
+  __shared__ GenShared sh;
   __shared__ uint32_t n_mask[(kDirectMaxN + 1 + 31) / 32];
-  for (int i = threadIdx.x; i < 256; i += blockDim.x) binom[i >> 4][i & 15] = c_binom[i >> 4][i & 15];
+  load_binom(sh);
   for (int i = threadIdx.x; i < (kDirectMaxN + 1 + 31) / 32; i += blockDim.x) n_mask[i] = 0;
   __syncthreads();
   const int g = blockIdx.x;
@@ -196,11 +286,10 @@ __global__ void __launch_bounds__(kBootThreads) bootstrap_kernel(BootArgs A) {
       A.medians[(size_t)g * M + m] = A.lo[(size_t)g * M + m] = A.hi[(size_t)g * M + m] = dnan();
     return;
   }
-  // The seeded state is the same for every metric (each _median_ci call
-  // starts random.Random(seed) afresh): one thread of the last warp computes
-  // it while the others gather the metric values.
-  // (The barrier after the gather orders the seed before its first use.)
-  if (threadIdx.x == blockDim.x - 32) seed_state(mt_seed, A.seeds[g]);
+  // Without a prepare pass, one thread of the last warp seeds the generator
+  // while the others gather the metric values (every metric's _median_ci
+  // starts random.Random(seed) afresh, so one seeded state serves them all).
+  if (!A.prepared && threadIdx.x == blockDim.x - 32) seed_state(sh.mt_seed, A.seeds[g]);
   const BootSmem L(M, A.max_members, A.max_members > kHistMaxN);
   double* vals = reinterpret_cast<double*>(dsm + L.vals);
   int* cnt = reinterpret_cast<int*>(dsm + L.cnt);
@@ -240,50 +329,32 @@ __global__ void __launch_bounds__(kBootThreads) bootstrap_kernel(BootArgs A) {
   __syncthreads();
   const int B = A.resamples;
   const int lo_idx = (int)((25LL * B) / 1000 - 1), hi_idx = (int)((975LL * B) / 1000 - 1);
-  for (int n = 3; n <= kDirectMaxN; ++n) {
-    if (!((n_mask[n >> 5] >> (n & 31)) & 1u)) continue;      // uniform: n_mask is shared
+  // The member count first (its stream may be prepared, and a direct-path
+  // stream must be consumed before another count reuses the group's area),
+  // then every other count in ascending order.
+  bool seeded = !A.prepared;
+  for (int step = 0; step <= kDirectMaxN; ++step) {
+    const int n = step == 0 ? members : (step == members ? 0 : step);
+    if (n < 3 || n > kDirectMaxN || !((n_mask[n >> 5] >> (n & 31)) & 1u)) continue;   // uniform: shared mask
     const bool histogram = n <= kHistMaxN;
-    const int nbins = histogram ? (int)binom[2 * n - 1][n] : 0;
-    for (int i = threadIdx.x; i < kMaxBins; i += blockDim.x) hist[i] = 0;
-    for (int i = threadIdx.x; i < kMtN; i += blockDim.x) mt[0][i] = mt_seed[i];
-    __syncthreads();
-    const double nd = (double)n;
-    const uint32_t words_per_draw = 2u * (uint32_t)n;          // 2nB < 2^32 (B <= 2^24, n <= 128)
-    const uint32_t blocks = (uint32_t)((2ull * n * B + kMtN - 1) / kMtN);
-    uint32_t next_r = 0;
-    uint8_t* stream = A.scratch ? A.scratch + (size_t)g * B * kDirectMaxN : nullptr;
-    int slot = 0;                                               // ring slot of the current block
-    for (uint32_t blk = 0; blk < blocks; ++blk) {
-      twist_block(mt[blk & 1], mt[(blk & 1) ^ 1], ring, slot * kMtN);
-      // Words [first, avail) are readable: the previous block and this one.
-      const uint32_t avail = (blk + 1) * (uint32_t)kMtN;
-      const uint32_t first = blk ? avail - 2 * kMtN : 0;
-      const int first_slot = blk ? (slot + 2) % 3 : 0;          // slot of word `first`
-      uint32_t r_end = avail / words_per_draw;
-      if (r_end > (uint32_t)B) r_end = B;
-      for (uint32_t r = next_r + threadIdx.x; r < r_end; r += blockDim.x) {
-        uint32_t pos = first_slot * kMtN + (r * words_per_draw - first);
-        if (pos >= (uint32_t)kRing) pos -= kRing;
-        if (histogram) {
-          switch (n) {
-            case 3: histogram_resample<3>(ring, pos, hist, binom); break;
-            case 4: histogram_resample<4>(ring, pos, hist, binom); break;
-            case 5: histogram_resample<5>(ring, pos, hist, binom); break;
-            case 6: histogram_resample<6>(ring, pos, hist, binom); break;
-            default: histogram_resample<7>(ring, pos, hist, binom); break;
-          }
-        } else {
-          for (int j = 0; j < n; ++j) {
-            const uint32_t w0 = ring[pos]; if (++pos == (uint32_t)kRing) pos = 0;
-            const uint32_t w1 = ring[pos]; if (++pos == (uint32_t)kRing) pos = 0;
-            stream[(size_t)r * n + j] = (uint8_t)draw_index(w0, w1, nd);
-          }
-        }
+    const int nbins = histogram ? (int)sh.binom[2 * n - 1][n] : 0;
+    uint8_t* stream = index_stream(A, g);
+    if (A.prepared && n == members) {
+      if (histogram) {
+        const uint32_t* src = prepared_hist(A, g);
+        for (int i = threadIdx.x; i < nbins; i += blockDim.x) sh.hist[i] = src[i];
       }
-      next_r = r_end;
-      slot = slot == 2 ? 0 : slot + 1;
+      __syncthreads();
+    } else {
+      if (!seeded) {
+        if (threadIdx.x == 0) seed_state(sh.mt_seed, A.seeds[g]);
+        seeded = true;
+      }
+      __syncthreads();
+      generate_resamples(sh, n, B, stream);
     }
-    __syncthreads();
+    uint32_t* hist = sh.hist;
+    const uint32_t (*binom)[16] = sh.binom;
     if (histogram) {
       // Fold the multiset histogram into each metric's median rank pairs, over
       // (metric, bin) items on every thread: a bin's median ranks under a
@@ -467,7 +538,7 @@ int prepare_bootstrap_constants(int device) {
 }
 
 size_t bootstrap_scratch_bytes(int n_groups, int max_members, int resamples) {
-  return max_members > kHistMaxN ? (size_t)n_groups * resamples * kDirectMaxN : 0;
+  return hist_area_bytes(n_groups) + (max_members > kHistMaxN ? (size_t)n_groups * resamples * kDirectMaxN : 0);
 }
 
 int launch_bootstrap(const BootArgs& A, cudaStream_t stream) {
@@ -481,6 +552,12 @@ int launch_bootstrap(const BootArgs& A, cudaStream_t stream) {
   if (static_bytes + smem > 48 * 1024)
     cudaFuncSetAttribute(bootstrap_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
   bootstrap_kernel<<<A.n_groups, kBootThreads, smem, stream>>>(A);
+  return 0;
+}
+
+int launch_bootstrap_prepare(const BootArgs& A, cudaStream_t stream) {
+  if (A.n_groups == 0) return 0;
+  bootstrap_prepare_kernel<<<A.n_groups, kBootThreads, 0, stream>>>(A);
   return 0;
 }
 

@@ -21,13 +21,16 @@
 namespace pm {
 
 int launch_bootstrap(const BootArgs& A, cudaStream_t stream);
+int launch_bootstrap_prepare(const BootArgs& A, cudaStream_t stream);
 int prepare_bootstrap_constants(int device);
 size_t bootstrap_scratch_bytes(int n_groups, int max_members, int resamples);
 
 namespace {
 
-// Index streams: groups x resamples x 128 bytes at most; 32 MiB covers, for
-// example, 26 groups of 8 or more members at 10 000 resamples.
+// Prepared multiset histograms (6.9 KB per group) and, when a group may have
+// more than seven members, index streams (resamples x 128 bytes per group):
+// 32 MiB covers, for example, 4800 groups of up to seven members, or 26 groups
+// of 8 or more members at 10 000 resamples.
 constexpr size_t kStaticStreamBytes = size_t(32) << 20;
 static __device__ __align__(256) uint8_t g_static_streams[kStaticStreamBytes];
 
@@ -77,11 +80,12 @@ extern "C" int pm_group_bootstrap_device_static(const pm_bootstrap_job* job, voi
     scratch = g_static_address[device];
   }
   if (prepare_bootstrap_constants(device)) return fail(PM_E_CUDA, "bootstrap constants upload failed");
-  // Nothing in the array must start at zero: each launch writes a group's
-  // stream completely before it reads it back.
+  // Nothing in the array must start at zero: the prepare launch writes each
+  // group's histogram or stream completely before the fold reads it back.
   BootArgs A{job->n_groups, job->n_metrics, job->resamples, job->max_members, job->values, job->group_offsets,
              job->member_rows, job->member_valid, job->seeds, job->medians, job->ci_lo, job->ci_hi,
-             need ? static_cast<uint8_t*>(scratch) : nullptr};
+             static_cast<uint8_t*>(scratch), 1};
+  launch_bootstrap_prepare(A, static_cast<cudaStream_t>(stream));
   launch_bootstrap(A, static_cast<cudaStream_t>(stream));
   cudaError_t e = cudaGetLastError();
   if (e != cudaSuccess) return cuda_fail(e, "bootstrap_kernel launch");

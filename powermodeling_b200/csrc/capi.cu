@@ -21,6 +21,7 @@ namespace pm {
 int launch_analyze(const pm_trials& T, const pm_policy& P, const pm_trial_results& R, int max_covering,
                    double* gscratch, cudaStream_t stream, size_t* scratch_bytes_needed);
 int launch_bootstrap(const BootArgs& A, cudaStream_t stream);
+int launch_bootstrap_prepare(const BootArgs& A, cudaStream_t stream);
 int launch_resample_indices(uint64_t seed, int n, int B, int32_t* out, cudaStream_t stream);
 int prepare_bootstrap_constants(int device);
 size_t bootstrap_scratch_bytes(int n_groups, int max_members, int resamples);
@@ -67,6 +68,12 @@ int arena_reserve(Arena& a, size_t dev_bytes, size_t host_bytes) {
   if (!a.stream) {
     cudaError_t e = cudaStreamCreateWithFlags(&a.stream, cudaStreamNonBlocking);
     if (e != cudaSuccess) return cuda_fail(e, "cudaStreamCreate");
+  }
+  if (!a.side) {
+    cudaError_t e = cudaStreamCreateWithFlags(&a.side, cudaStreamNonBlocking);
+    if (e == cudaSuccess) e = cudaEventCreateWithFlags(&a.fork, cudaEventDisableTiming);
+    if (e == cudaSuccess) e = cudaEventCreateWithFlags(&a.join, cudaEventDisableTiming);
+    if (e != cudaSuccess) return cuda_fail(e, "side stream / events");
   }
   return PM_OK;
 }
@@ -395,7 +402,8 @@ size_t pm_bootstrap_scratch_bytes(int32_t n_groups, int32_t max_members, int32_t
   return bootstrap_scratch_bytes(n_groups, max_members, resamples);
 }
 
-int pm_group_bootstrap_device(const pm_bootstrap_job* job, void* scratch, size_t scratch_bytes, void* stream) {
+// Shared by the device bootstrap entry points: checks and the kernel arguments.
+static int device_boot_args(const pm_bootstrap_job* job, void* scratch, size_t scratch_bytes, BootArgs* out) {
   int rc = check_bootstrap(job);
   if (rc) return rc;
   int device = 0;
@@ -404,13 +412,35 @@ int pm_group_bootstrap_device(const pm_bootstrap_job* job, void* scratch, size_t
   const size_t need = bootstrap_scratch_bytes(job->n_groups, job->max_members, job->resamples);
   if (need > scratch_bytes || (need && !scratch))
     return fail(PM_E_INVALID, "bootstrap needs %zu bytes of device scratch, got %zu", need, scratch_bytes);
-  BootArgs A{job->n_groups, job->n_metrics, job->resamples, job->max_members, job->values, job->group_offsets,
-             job->member_rows, job->member_valid, job->seeds, job->medians, job->ci_lo, job->ci_hi,
-             need ? static_cast<uint8_t*>(scratch) : nullptr};
+  *out = BootArgs{job->n_groups, job->n_metrics, job->resamples, job->max_members, job->values, job->group_offsets,
+                  job->member_rows, job->member_valid, job->seeds, job->medians, job->ci_lo, job->ci_hi,
+                  static_cast<uint8_t*>(scratch), 1};
+  return PM_OK;
+}
+
+int pm_bootstrap_prepare_device(const pm_bootstrap_job* job, void* scratch, size_t scratch_bytes, void* stream) {
+  BootArgs A;
+  int rc = device_boot_args(job, scratch, scratch_bytes, &A);
+  if (rc) return rc;
+  launch_bootstrap_prepare(A, (cudaStream_t)stream);
+  cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) return cuda_fail(e, "bootstrap_prepare_kernel launch");
+  return PM_OK;
+}
+
+int pm_bootstrap_finish_device(const pm_bootstrap_job* job, void* scratch, size_t scratch_bytes, void* stream) {
+  BootArgs A;
+  int rc = device_boot_args(job, scratch, scratch_bytes, &A);
+  if (rc) return rc;
   launch_bootstrap(A, (cudaStream_t)stream);
   cudaError_t e = cudaGetLastError();
   if (e != cudaSuccess) return cuda_fail(e, "bootstrap_kernel launch");
   return PM_OK;
+}
+
+int pm_group_bootstrap_device(const pm_bootstrap_job* job, void* scratch, size_t scratch_bytes, void* stream) {
+  int rc = pm_bootstrap_prepare_device(job, scratch, scratch_bytes, stream);
+  return rc ? rc : pm_bootstrap_finish_device(job, scratch, scratch_bytes, stream);
 }
 
 int pm_group_bootstrap(const pm_bootstrap_job* job) {
@@ -459,7 +489,8 @@ int pm_group_bootstrap(const pm_bootstrap_job* job) {
                 reinterpret_cast<const int32_t*>(dev_of(ho)), hr ? reinterpret_cast<const int32_t*>(dev_of(hr)) : nullptr,
                 hvalid ? reinterpret_cast<const uint8_t*>(dev_of(hvalid)) : nullptr,
                 reinterpret_cast<const uint64_t*>(dev_of(hs)), dmed, dlo, dhi,
-                scratch ? reinterpret_cast<uint8_t*>(dout + out_bytes) : nullptr};
+                reinterpret_cast<uint8_t*>(dout + out_bytes), 1};
+  launch_bootstrap_prepare(args, st);
   launch_bootstrap(args, st);
   e = cudaGetLastError();
   if (e != cudaSuccess) return cuda_fail(e, "bootstrap_kernel launch");
@@ -517,15 +548,29 @@ int pm_analyze_sweep(const pm_trials* trials, const pm_policy* policy, pm_trial_
   hl.place(hs, G); memcpy(hs, J.seeds, G * 8);
   cudaError_t e = cudaMemcpyAsync(dbase, hbase, gin, cudaMemcpyHostToDevice, A.stream);
   if (e != cudaSuccess) return cuda_fail(e, "cudaMemcpyAsync(groups)");
-  launch_analyze(S.dev, *policy, S.dres, S.max_cov, S.gscratch, A.stream, nullptr);
   auto dptr = [&](const void* h) { return dbase + (static_cast<const char*>(h) - hbase); };
   char* dout = dbase + gin;
   BootArgs args{(int)G, (int)M, J.resamples, mm, S.dres.metrics, reinterpret_cast<const int32_t*>(dptr(ho)),
                 reinterpret_cast<const int32_t*>(dptr(hr)), S.dres.valid, reinterpret_cast<const uint64_t*>(dptr(hs)),
                 reinterpret_cast<double*>(dout), reinterpret_cast<double*>(dout + align256(G * M * 8)),
                 reinterpret_cast<double*>(dout + 2 * align256(G * M * 8)),
-                bscratch ? reinterpret_cast<uint8_t*>(dout + gout) : nullptr};
-  if (G) launch_bootstrap(args, A.stream);
+                reinterpret_cast<uint8_t*>(dout + gout), 1};
+  // The resample streams need only seeds and group sizes: they are generated
+  // on the side stream while the trials are analysed, and the fold waits for both.
+  if (G) {
+    e = cudaEventRecord(A.fork, A.stream);
+    if (e == cudaSuccess) e = cudaStreamWaitEvent(A.side, A.fork, 0);
+    if (e != cudaSuccess) return cuda_fail(e, "fork");
+    launch_bootstrap_prepare(args, A.side);
+    e = cudaEventRecord(A.join, A.side);
+    if (e != cudaSuccess) return cuda_fail(e, "join record");
+  }
+  launch_analyze(S.dev, *policy, S.dres, S.max_cov, S.gscratch, A.stream, nullptr);
+  if (G) {
+    e = cudaStreamWaitEvent(A.stream, A.join, 0);
+    if (e != cudaSuccess) return cuda_fail(e, "join");
+    launch_bootstrap(args, A.stream);
+  }
   e = cudaGetLastError();
   if (e != cudaSuccess) return cuda_fail(e, "sweep kernels launch");
   e = cudaMemcpyAsync(static_cast<char*>(A.host) + S.in_bytes, static_cast<char*>(A.dev) + S.in_bytes, S.res_bytes,

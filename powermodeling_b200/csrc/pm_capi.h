@@ -24,7 +24,8 @@ struct BootArgs {
   const uint8_t* member_valid;    // NULL: all rows count
   const uint64_t* seeds;
   double* medians; double* lo; double* hi;
-  uint8_t* scratch;               // index streams of groups with more than 7 members
+  uint8_t* scratch;               // prepared histograms, then index streams of groups with more than 7 members
+  int prepared;                   // 1: bootstrap_prepare_kernel filled scratch for each group's member count
 };
 
 // Grow-only device workspace, pinned staging buffer and private stream of a device.
@@ -32,6 +33,8 @@ struct Arena {
   void* dev = nullptr; size_t dev_bytes = 0;
   void* host = nullptr; size_t host_bytes = 0;
   cudaStream_t stream = nullptr;
+  cudaStream_t side = nullptr;                 // work that overlaps the main stream (stream generation)
+  cudaEvent_t fork = nullptr, join = nullptr;  // main -> side and side -> main ordering
   std::mutex lock;
 };
 extern Arena g_arenas[kMaxDevices];

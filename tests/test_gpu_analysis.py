@@ -131,3 +131,28 @@ def test_long_phases_match_oracle(gpu_ready, arm_s):
         for phase, stats in expected["phases"].items():
             problems += [f"{phase}.{p}" for p in diff(stats, trial["phases"].get(phase, {}), PHASE_KEYS, rel=0.0)]
         assert not problems, problems
+
+
+@pytest.mark.parametrize("members", [5, 9])
+def test_bootstrap_mixed_member_counts_match_oracle(gpu_ready, members):
+    """Metrics that lose members to NaN: the prepared draws serve count == members, fresh draws the rest."""
+    import hashlib
+    import statistics
+    from powermodeling_b200.analysis import bootstrap_groups
+    rng = np.random.default_rng(members)
+    G, M = 6, 12
+    values = rng.normal(100, 10, size=(G * members, M)).round(3)
+    for g in range(G):
+        for m in range(M):
+            drop = [0, 1, 3, members - 2][m % 4]
+            values[g * members + rng.choice(members, size=drop, replace=False), m] = np.nan
+    groups = [list(range(g * members, (g + 1) * members)) for g in range(G)]
+    seeds = [int(hashlib.sha256(f"mixed-{members}-{g}".encode()).hexdigest()[:16], 16) for g in range(G)]
+    med, lo, hi = bootstrap_groups(values, groups, seeds, 1000)
+    for g in range(G):
+        for m in range(M):
+            vals = [float(v) for v in values[groups[g], m] if not np.isnan(v)]
+            ci = O.median_ci(vals, seeds[g], 1000)
+            got = None if np.isnan(lo[g, m]) else [float(lo[g, m]), float(hi[g, m])]
+            assert got == ci, (g, m, len(vals), got, ci)
+            assert float(med[g, m]) == statistics.median(vals)
