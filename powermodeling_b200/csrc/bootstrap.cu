@@ -32,6 +32,9 @@ constexpr int kHistMaxN = 7;            // multiset histogram path
 constexpr int kMaxBins = 1716;          // C(13, 7)
 constexpr int kDirectMaxN = 128;        // direct path limit
 constexpr int kRing = 3 * kMtN;      // block b in slot b % 3: the two newest stay readable
+constexpr int kFastMaxN = 20;           // direct path in one pass over the draws up to this group size
+constexpr int kPtabWords = kDirectMaxN * kDirectMaxN;   // pair-table words (shared by both direct paths)
+constexpr int kFastCand = kFastMaxN * (kFastMaxN + 1) / 2;   // distinct median pairs a <= b
 
 __constant__ uint32_t c_mt_init[kMtN];  // init_genrand(19650218), filled by the host
 __constant__ uint32_t c_binom[16][16];  // C(a, b)
@@ -159,7 +162,8 @@ __device__ __forceinline__ void histogram_resample(const uint32_t* ring, uint32_
 // per metric the values in rank order and the member index of each rank, a
 // median-pair table per metric, and the index counts of every multiset bin.
 struct BootSmem {
-  size_t vals, cnt, rank_of, sorted_v, ptab, fold_sorted, fold_index, fold_pairs, bin_counts, total;
+  size_t vals, cnt, rank_of, sorted_v, ptab, fold_sorted, fold_index, fold_pairs, bin_counts;
+  size_t fast_list, fast_index, fast_sorted, fast_counts, cand_vals, cand_counts, total;
   __host__ __device__ BootSmem(int M, int mm, bool direct) {
     auto up = [](size_t x) { return (x + 15) & ~(size_t)15; };
     vals = 0;
@@ -171,7 +175,16 @@ struct BootSmem {
     fold_index = up(fold_sorted + (size_t)M * kHistMaxN * sizeof(double));
     fold_pairs = up(fold_index + (size_t)M * kHistMaxN);
     bin_counts = up(fold_pairs + (size_t)M * kHistMaxN * kHistMaxN * sizeof(uint32_t));
-    total = direct ? ptab + (size_t)kDirectMaxN * kDirectMaxN * sizeof(uint32_t)
+    // direct path, one pass: active metric list, per-metric rank order and
+    // sorted values, per-thread index counts, per-warp candidate lists (twice:
+    // as collected and in value order)
+    fast_list = up(ptab + (size_t)kPtabWords * sizeof(uint32_t));
+    fast_index = up(fast_list + (size_t)M * sizeof(int));
+    fast_sorted = up(fast_index + (size_t)M * kFastMaxN);
+    fast_counts = up(fast_sorted + (size_t)M * kFastMaxN * sizeof(double));
+    cand_vals = up(fast_counts + (size_t)kBootThreads * kFastMaxN);
+    cand_counts = up(cand_vals + (size_t)(kBootThreads / 32) * 2 * kFastCand * sizeof(double));
+    total = direct ? up(cand_counts + (size_t)(kBootThreads / 32) * 2 * kFastCand * sizeof(uint32_t))
                    : up(bin_counts + (size_t)kMaxBins * kHistMaxN);
   }
 };
@@ -274,6 +287,7 @@ __global__ void __launch_bounds__(kBootThreads) bootstrap_kernel(BootArgs A) {
   extern __shared__ __align__(16) unsigned char dsm[];
   __shared__ GenShared sh;
   __shared__ uint32_t n_mask[(kDirectMaxN + 1 + 31) / 32];
+  __shared__ int s_active, s_cand[kBootThreads / 32];
   load_binom(sh);
   for (int i = threadIdx.x; i < (kDirectMaxN + 1 + 31) / 32; i += blockDim.x) n_mask[i] = 0;
   __syncthreads();
@@ -427,7 +441,96 @@ __global__ void __launch_bounds__(kBootThreads) bootstrap_kernel(BootArgs A) {
       }
       __syncthreads();
     } else {
-      // Direct path: per metric, histogram the median rank pair of every draw.
+      // Direct path.  The metrics with this count, in order:
+      int* flist = reinterpret_cast<int*>(dsm + L.fast_list);
+      if (threadIdx.x == 0) {
+        int k = 0;
+        for (int m = 0; m < M; ++m) if (cnt[m] == n) flist[k++] = m;
+        s_active = k;
+      }
+      __syncthreads();
+      const int K = s_active;
+      const int pa = (n & 1) ? n / 2 : n / 2 - 1, pb = n / 2;
+      if (n <= kFastMaxN && K * n * n <= kPtabWords) {
+        // One pass over the draws for every metric: each draw's index counts in
+        // the thread's shared row, then each metric's median rank pair by a
+        // walk in that metric's rank order.
+        uint8_t* fidx = dsm + L.fast_index;                                    // [K][kFastMaxN]
+        double* fsv = reinterpret_cast<double*>(dsm + L.fast_sorted);          // [K][kFastMaxN]
+        uint32_t* pairs = reinterpret_cast<uint32_t*>(dsm + L.ptab);           // [K][n*n]
+        uint8_t* counts = dsm + L.fast_counts + threadIdx.x * kFastMaxN;
+        for (int a = threadIdx.x; a < K; a += blockDim.x) {
+          const double* v = vals + flist[a] * A.max_members;
+          for (int i = 0; i < n; ++i) {                  // stable ranks: ties keep member order
+            int r = 0;
+            for (int k = 0; k < n; ++k) r += (v[k] < v[i]) || (v[k] == v[i] && k < i);
+            fidx[a * kFastMaxN + r] = (uint8_t)i;
+            fsv[a * kFastMaxN + r] = v[i];
+          }
+        }
+        for (int i = threadIdx.x; i < K * n * n; i += blockDim.x) pairs[i] = 0;
+        __syncthreads();
+        for (int r = threadIdx.x; r < B; r += blockDim.x) {
+          for (int i = 0; i < n; ++i) counts[i] = 0;
+          const uint8_t* draw = stream + (size_t)r * n;
+          for (int j = 0; j < n; ++j) counts[draw[j]]++;
+          for (int a = 0; a < K; ++a) {
+            const uint8_t* idx = fidx + a * kFastMaxN;
+            int seen = 0, ra = -1, rb = -1;
+            for (int q = 0; q < n && rb < 0; ++q) {
+              seen += counts[idx[q]];
+              if (ra < 0 && pa < seen) ra = q;
+              if (pb < seen) rb = q;
+            }
+            atomicAdd(&pairs[a * n * n + ra * n + rb], 1u);
+          }
+        }
+        __syncthreads();
+        // Per metric, one warp: the distinct pair values in ascending order
+        // with their counts (rank by counting), then the two order statistics.
+        const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, warps = blockDim.x >> 5;
+        double* cv = reinterpret_cast<double*>(dsm + L.cand_vals) + (size_t)warp * 2 * kFastCand;
+        uint32_t* cc = reinterpret_cast<uint32_t*>(dsm + L.cand_counts) + (size_t)warp * 2 * kFastCand;
+        for (int a = warp; a < K; a += warps) {
+          const double* sv = fsv + a * kFastMaxN;
+          const uint32_t* pt = pairs + a * n * n;
+          if (lane == 0) s_cand[warp] = 0;
+          __syncwarp();
+          for (int p2 = lane; p2 < n * n; p2 += 32) {
+            const int a2 = p2 / n, b2 = p2 - a2 * n;
+            if (a2 <= b2 && pt[p2]) {
+              const int k = atomicAdd(&s_cand[warp], 1);
+              cv[k] = (n & 1) ? sv[a2] : (sv[a2] + sv[b2]) / 2;
+              cc[k] = pt[p2];
+            }
+          }
+          __syncwarp();
+          const int kc = s_cand[warp];
+          for (int i = lane; i < kc; i += 32) {
+            const double x = cv[i];
+            int rank = 0;
+            for (int j = 0; j < kc; ++j) rank += (cv[j] < x) || (cv[j] == x && j < i);
+            cv[kFastCand + rank] = x;
+            cc[kFastCand + rank] = cc[i];
+          }
+          __syncwarp();
+          if (lane == 0) {
+            long long cum = 0; double lo = dnan(), hi = dnan();
+            for (int i = 0; i < kc; ++i) {
+              const long long next = cum + cc[kFastCand + i];
+              if (cum <= lo_idx && lo_idx < next) lo = cv[kFastCand + i];
+              if (cum <= hi_idx && hi_idx < next) hi = cv[kFastCand + i];
+              cum = next;
+            }
+            A.lo[(size_t)g * M + flist[a]] = lo;
+            A.hi[(size_t)g * M + flist[a]] = hi;
+          }
+          __syncwarp();
+        }
+        __syncthreads();
+        continue;
+      }
+      // Larger groups: per metric, histogram the median rank pair of every draw.
       int* rank_of = reinterpret_cast<int*>(dsm + L.rank_of);
       double* sorted_v = reinterpret_cast<double*>(dsm + L.sorted_v);
       uint32_t* ptab = reinterpret_cast<uint32_t*>(dsm + L.ptab);   // [n*n] median rank pairs
@@ -445,7 +548,6 @@ __global__ void __launch_bounds__(kBootThreads) bootstrap_kernel(BootArgs A) {
           uint8_t c[kDirectMaxN];
           for (int i = 0; i < n; ++i) c[i] = 0;
           for (int j = 0; j < n; ++j) c[rank_of[stream[(size_t)r * n + j]]]++;
-          const int pa = (n & 1) ? n / 2 : n / 2 - 1, pb = n / 2;
           int seen = 0, ra = -1, rb = -1;
           for (int i = 0; i < n && rb < 0; ++i) {
             const int next = seen + c[i];
@@ -539,6 +641,20 @@ int prepare_bootstrap_constants(int device) {
 
 size_t bootstrap_scratch_bytes(int n_groups, int max_members, int resamples) {
   return hist_area_bytes(n_groups) + (max_members > kHistMaxN ? (size_t)n_groups * resamples * kDirectMaxN : 0);
+}
+
+// Shared memory the fold needs for M metrics and groups of up to mm members,
+// against what one CTA may use on the current device: 0 if it fits, else the
+// bytes needed (written to *available the bytes the device offers).
+size_t bootstrap_smem_shortfall(int M, int mm, size_t* available) {
+  const size_t dyn = BootSmem(M, mm, mm > kHistMaxN).total;
+  cudaFuncAttributes attr{};
+  const size_t static_bytes = cudaFuncGetAttributes(&attr, bootstrap_kernel) == cudaSuccess ? attr.sharedSizeBytes : 0;
+  int dev = 0, optin = 48 * 1024;
+  if (cudaGetDevice(&dev) == cudaSuccess) cudaDeviceGetAttribute(&optin, cudaDevAttrMaxSharedMemoryPerBlockOptin, dev);
+  cudaGetLastError();   // a failed query must not surface as a later launch error
+  if (available) *available = (size_t)optin;
+  return static_bytes + dyn <= (size_t)optin ? 0 : static_bytes + dyn;
 }
 
 int launch_bootstrap(const BootArgs& A, cudaStream_t stream) {

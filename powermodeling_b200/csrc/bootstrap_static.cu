@@ -66,6 +66,7 @@ extern "C" int pm_group_bootstrap_device_static(const pm_bootstrap_job* job, voi
                 job->n_groups, job->max_members, job->resamples, need, kStaticStreamBytes);
   int device = 0, rc = current_device(&device);
   if (rc) return rc;
+  if ((rc = check_bootstrap_fits(job->n_metrics, job->max_members))) return rc;
   void* scratch = nullptr;
   {
     std::lock_guard<std::mutex> guard(g_static_lock);

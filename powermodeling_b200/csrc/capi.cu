@@ -40,6 +40,15 @@ int cuda_fail(cudaError_t e, const char* where) {
 
 Arena g_arenas[kMaxDevices];
 
+int check_bootstrap_fits(int n_metrics, int max_members) {
+  size_t available = 0;
+  const size_t need = bootstrap_smem_shortfall(n_metrics, max_members, &available);
+  if (need)
+    return fail(PM_E_LIMIT, "bootstrap of %d metrics with groups of up to %d members needs %zu bytes of shared memory per "
+                "block; the device offers %zu", n_metrics, max_members, need, available);
+  return PM_OK;
+}
+
 int current_device(int* device) {
   int n = 0;
   cudaError_t e = cudaGetDeviceCount(&n);
@@ -409,6 +418,7 @@ static int device_boot_args(const pm_bootstrap_job* job, void* scratch, size_t s
   int device = 0;
   if ((rc = current_device(&device))) return rc;
   if (prepare_bootstrap_constants(device)) return fail(PM_E_CUDA, "bootstrap constants upload failed");
+  if ((rc = check_bootstrap_fits(job->n_metrics, job->max_members))) return rc;
   const size_t need = bootstrap_scratch_bytes(job->n_groups, job->max_members, job->resamples);
   if (need > scratch_bytes || (need && !scratch))
     return fail(PM_E_INVALID, "bootstrap needs %zu bytes of device scratch, got %zu", need, scratch_bytes);
@@ -464,6 +474,7 @@ int pm_group_bootstrap(const pm_bootstrap_job* job) {
     for (int i = 0; i < job->n_members; ++i)
       if (job->member_rows[i] < 0 || (size_t)job->member_rows[i] >= rows) return fail(PM_E_INVALID, "member_rows[%d] out of range", i);
   if (G == 0) return PM_OK;
+  if ((rc = check_bootstrap_fits((int)M, mm))) return rc;
   const size_t scratch = bootstrap_scratch_bytes((int)G, mm, job->resamples);
   size_t in_bytes = align256(rows * M * 8) + align256((G + 1) * 4) + align256((size_t)job->n_members * 4) + align256(rows) + align256(G * 8);
   size_t out_bytes = 3 * align256(G * M * 8);
@@ -530,6 +541,7 @@ int pm_analyze_sweep(const pm_trials* trials, const pm_policy* policy, pm_trial_
   if (rc) return rc;
   if (prepare_bootstrap_constants(device)) return fail(PM_E_CUDA, "bootstrap constants upload failed");
   if (n == 0) return PM_OK;
+  if (G && (rc = check_bootstrap_fits((int)M, mm))) return rc;
   const size_t gin = align256((G + 1) * 4) + align256((size_t)J.n_members * 4) + align256(G * 8);
   const size_t gout = 3 * align256(G * M * 8);
   const size_t bscratch = bootstrap_scratch_bytes((int)G, mm, J.resamples);

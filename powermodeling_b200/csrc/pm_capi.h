@@ -43,6 +43,9 @@ int fail(int code, const char* fmt, ...);
 int cuda_fail(cudaError_t e, const char* where);
 int current_device(int* device);
 int arena_reserve(Arena& a, size_t dev_bytes, size_t host_bytes);
+size_t bootstrap_smem_shortfall(int n_metrics, int max_members, size_t* available);
+// PM_E_LIMIT when the bootstrap fold for these sizes does not fit one CTA's shared memory.
+int check_bootstrap_fits(int n_metrics, int max_members);
 size_t analyze_scratch_bytes(int n_trials, int max_phase_samples);
 
 }  // namespace pm

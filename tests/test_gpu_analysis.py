@@ -133,7 +133,7 @@ def test_long_phases_match_oracle(gpu_ready, arm_s):
         assert not problems, problems
 
 
-@pytest.mark.parametrize("members", [5, 9])
+@pytest.mark.parametrize("members", [5, 9, 16, 24])
 def test_bootstrap_mixed_member_counts_match_oracle(gpu_ready, members):
     """Metrics that lose members to NaN: the prepared draws serve count == members, fresh draws the rest."""
     import hashlib
@@ -156,3 +156,17 @@ def test_bootstrap_mixed_member_counts_match_oracle(gpu_ready, members):
             got = None if np.isnan(lo[g, m]) else [float(lo[g, m]), float(hi[g, m])]
             assert got == ci, (g, m, len(vals), got, ci)
             assert float(med[g, m]) == statistics.median(vals)
+
+
+def test_bootstrap_beyond_shared_memory_is_a_limit_error(gpu_ready):
+    """256 metrics x groups of 128: the fold cannot fit one block; the call says so before launching."""
+    from powermodeling_b200 import _native as N
+    G, M, n = 1, 256, 128
+    values = np.zeros((n, M))
+    offsets = np.array([0, n], dtype=np.int32)
+    seeds = np.array([1], dtype=np.uint64)
+    out = [np.empty(G * M) for _ in range(3)]
+    job = N.BootstrapJob(G, M, n, n, 1000, n, values.ctypes.data, offsets.ctypes.data, None, None,
+                         seeds.ctypes.data, out[0].ctypes.data, out[1].ctypes.data, out[2].ctypes.data)
+    assert N.library().pm_group_bootstrap(job) == -4     # PM_E_LIMIT
+    assert "shared memory" in N.last_error()
