@@ -73,7 +73,7 @@ __device__ __forceinline__ double col_value(const pm_trials& T, int c, int64_t i
 
 // ---------------------------------------------------------------------------
 // _measure_epochs for one arm (single thread).
-__device__ void measure_epochs(const pm_trials& T, const pm_policy& P, int trial, int arm,
+__device__ __noinline__ void measure_epochs(const pm_trials& T, const pm_policy& P, int trial, int arm,
                                double phase_start, double phase_end, double whole_ops, double whole_bytes,
                                EpochResult& r, int16_t* order) {
   r.n_inner = 0; r.issue = -1; r.start_s = r.end_s = dnan();
@@ -143,7 +143,7 @@ __device__ void measure_epochs(const pm_trials& T, const pm_policy& P, int trial
 // ---------------------------------------------------------------------------
 // _phase_stats for slot (trial, p) on window [start, end] after `trim`.
 // Writes Shared::po[p] / pf[p].  All threads call it.
-__device__ void phase_stats(const pm_trials& T, const pm_policy& P, Shared& S, double* sortbuf, int SP,
+__device__ __noinline__ void phase_stats(const pm_trials& T, const pm_policy& P, Shared& S, double* sortbuf, int SP,
                             int trial, int p, double start, double end, double trim, bool idle, bool aligned) {
   double* po = S.po[p];
   const int slot = trial * PM_PHASES + p;
