@@ -58,6 +58,21 @@ __device__ __forceinline__ E col_at(const E* col, uint32_t bit, const pm_trials&
   return (T.broadcast_columns & bit) ? col[0] : col[i];
 }
 
+// The PM_COL_* bit of a sample column (0: derived columns, never broadcast).
+__device__ __forceinline__ uint32_t column_bit(int c) {
+  switch (c) {
+    case C_POWER: return PM_COL_POWER_W;
+    case C_GFX: return PM_COL_GRAPHICS_CLOCK;
+    case C_SM: return PM_COL_SM_CLOCK;
+    case C_MEM: return PM_COL_MEMORY_CLOCK;
+    case C_TEMP: return PM_COL_TEMPERATURE;
+    case C_PLIMIT: return PM_COL_POWER_LIMIT;
+    case C_ENF: return PM_COL_ENFORCED_LIMIT;
+    case C_PSTATE: return PM_COL_PSTATE;
+    default: return 0u;
+  }
+}
+
 __device__ __forceinline__ double col_value(const pm_trials& T, int c, int64_t i) {
   switch (c) {
     case C_POWER: return col_at(T.power_w, PM_COL_POWER_W, T, i);
@@ -143,8 +158,16 @@ __device__ __noinline__ void measure_epochs(const pm_trials& T, const pm_policy&
 // ---------------------------------------------------------------------------
 // _phase_stats for slot (trial, p) on window [start, end] after `trim`.
 // Writes Shared::po[p] / pf[p].  All threads call it.
-__device__ __noinline__ void phase_stats(const pm_trials& T, const pm_policy& P, Shared& S, double* sortbuf, int SP,
-                            int trial, int p, double start, double end, double trim, bool idle, bool aligned) {
+// The phase tile lives in dynamic shared memory unless it is too large, then
+// in global scratch.  Each case is its own instantiation, so the shared one
+// addresses the tile with shared-memory loads and stores.
+extern __shared__ double dyn_tile[];
+
+template <bool kSharedTile>
+__device__ __noinline__ void phase_stats_impl(const pm_trials& T, const pm_policy& P, Shared& S, double* gtile, int SP,
+                                              int trial, int p, double start, double end, double trim, bool idle,
+                                              bool aligned) {
+  double* sortbuf = kSharedTile ? dyn_tile : gtile;
   double* po = S.po[p];
   const int slot = trial * PM_PHASES + p;
   const int64_t seg_b = T.phase_offsets[slot], seg_e = T.phase_offsets[slot + 1];
@@ -192,6 +215,7 @@ __device__ __noinline__ void phase_stats(const pm_trials& T, const pm_policy& P,
     col[C_GAP * SP + q] = (q < ncov - 1) ? t[cb + q + 1] - t[cb + q] : inf;
     col[C_CHANGE * SP + q] = inf;
     for (int c = C_POWER; c < C_COUNT; ++c) {
+      if (T.broadcast_columns & column_bit(c)) continue;   // one value for every sample: see the reductions
       double v = inf;
       if (q < nsel) { const double x = col_value(T, c, lo + q); if (!none(x)) v = x; }
       col[c * SP + q] = v;
@@ -278,6 +302,7 @@ __device__ __noinline__ void phase_stats(const pm_trials& T, const pm_policy& P,
   for (int c = 0; c < C_COUNT; ++c) { fin[c] = 0; cmn[c] = inf; cmx[c] = -inf; }
   for (int q = threadIdx.x; q < SP; q += blockDim.x) {
     for (int c = 0; c < C_COUNT; ++c) {
+      if (T.broadcast_columns & column_bit(c)) continue;
       const double v = sortbuf[c * SP + q];
       if (v != inf) { ++fin[c]; cmn[c] = fmin(cmn[c], v); cmx[c] = fmax(cmx[c], v); }
     }
@@ -309,7 +334,13 @@ __device__ __noinline__ void phase_stats(const pm_trials& T, const pm_policy& P,
     if (threadIdx.x < C_COUNT) {
       const int c = threadIdx.x;
       double mn = inf, mx = -inf; int f = 0;
-      for (int w = 0; w < (int)(blockDim.x >> 5); ++w) { mn = fmin(mn, wmin[w][c]); mx = fmax(mx, wmax[w][c]); f += wfin[w][c]; }
+      if (T.broadcast_columns & column_bit(c)) {
+        // every selected sample holds the one value: as if staged nsel times
+        const double v = col_value(T, c, 0);
+        if (!none(v) && nsel > 0) { mn = mx = v; f = nsel; }
+      } else {
+        for (int w = 0; w < (int)(blockDim.x >> 5); ++w) { mn = fmin(mn, wmin[w][c]); mx = fmax(mx, wmax[w][c]); f += wfin[w][c]; }
+      }
       S.cmin[c] = mn; S.cmax[c] = mx; S.nfin[c] = f;
     }
     __syncthreads();
@@ -336,16 +367,19 @@ __device__ __noinline__ void phase_stats(const pm_trials& T, const pm_policy& P,
   // power column's distinct count follows from its sorted order.
   if (S.nsort) {
     const int P = S.sort_p;
-    double* xchg = sortbuf + (size_t)(C_COUNT + S_TERM_P) * SP;   // unused until the energy terms
+    // Three staged columns (REL, TERM_P, TERM_M) are unused until the energy
+    // terms: they hold the exchange buffers of up to kSortBatch columns.
+    double* xchg = sortbuf + (size_t)(C_COUNT + S_REL) * SP;
     bool power_sorted = false;
-    for (int a = 0; a < S.nsort; ++a) {
-      double* v = sortbuf + (size_t)S.sort_cols[a] * SP;
-      power_sorted |= S.sort_cols[a] == C_POWER;
-      if (P <= (int)blockDim.x) cta_register_sort<1>(v, P, xchg);
-      else if (P <= 2 * (int)blockDim.x) cta_register_sort<2>(v, P, xchg);
-      else if (P <= 4 * (int)blockDim.x) cta_register_sort<4>(v, P, xchg);
-      else if (P <= 8 * (int)blockDim.x) cta_register_sort<8>(v, P, xchg);
-      else { const int col = S.sort_cols[a]; bitonic_sort_columns(sortbuf, SP, &col, 1, P); }
+    for (int a = 0; a < S.nsort; ++a) power_sorted |= S.sort_cols[a] == C_POWER;
+    for (int a = 0; a < S.nsort; a += kSortBatch) {
+      const int nc = min(kSortBatch, S.nsort - a);
+      const int* cols = S.sort_cols + a;
+      if (P <= (int)blockDim.x) cta_register_sort_batch<1>(sortbuf, SP, cols, nc, P, xchg, SP);
+      else if (P <= 2 * (int)blockDim.x) cta_register_sort_batch<2>(sortbuf, SP, cols, nc, P, xchg, SP);
+      else if (P <= 4 * (int)blockDim.x) cta_register_sort_batch<4>(sortbuf, SP, cols, nc, P, xchg, SP);
+      else if (P <= 8 * (int)blockDim.x) cta_register_sort_batch<8>(sortbuf, SP, cols, nc, P, xchg, SP);
+      else bitonic_sort_columns(sortbuf, SP, cols, nc, P);
     }
     if (power_sorted) {
       if (threadIdx.x == 0) S.distinct_power = 0;
@@ -413,18 +447,14 @@ __device__ __noinline__ void phase_stats(const pm_trials& T, const pm_policy& P,
   if (threadIdx.x == 0) {
     double energy = dnan();
     if (!none(p0) && !none(p1) && end > start && !gap_p) {
-      NeumaierSum sum;
-      for (int k = 0; k < nterms; ++k) sum.add(term_p[k]);
-      energy = sum.result();
+      energy = neumaier_sum(term_p, nterms);
     }
     po[PM_PO_ENERGY_J] = energy;
     po[PM_PO_INTEGRATED_POWER_W] = none(energy) ? dnan() : energy / duration;
   } else if (threadIdx.x == 32) {
     double me = dnan();
     if (!none(m0) && !none(m1) && end > start && !gap_m) {
-      NeumaierSum sum;
-      for (int k = 0; k < nterms; ++k) sum.add(term_m[k]);
-      me = sum.result();
+      me = neumaier_sum(term_m, nterms);
     }
     po[PM_PO_MEMORY_ENERGY_J] = me;
     po[PM_PO_MEMORY_POWER_W] = none(me) ? dnan() : me / duration;
@@ -502,6 +532,14 @@ __device__ __noinline__ void phase_stats(const pm_trials& T, const pm_policy& P,
 
 // CTA-wide: does any selected sample of phase p violate |v - center| <= tol
 // (relative: |v - center| / center <= tol), or miss the value?
+// _phase_stats on the tile in global scratch (gtile != NULL) or in shared memory.
+__device__ __forceinline__ void phase_stats(const pm_trials& T, const pm_policy& P, Shared& S, double* gtile, int SP,
+                                            int trial, int p, double start, double end, double trim, bool idle,
+                                            bool aligned) {
+  if (gtile) phase_stats_impl<false>(T, P, S, gtile, SP, trial, p, start, end, trim, idle, aligned);
+  else phase_stats_impl<true>(T, P, S, gtile, SP, trial, p, start, end, trim, idle, aligned);
+}
+
 __device__ bool any_outside(const pm_trials& T, const Shared& S, int trial, int p, int column,
                             double center, double tol, bool relative) {
   const int slot = trial * PM_PHASES + p;
@@ -533,9 +571,8 @@ __device__ double idle_at(const double* pre, const double* post, const double* a
 __global__ void __launch_bounds__(kThreads)
 analyze_kernel(pm_trials T, pm_policy P, pm_trial_results R, int SP, double* gscratch) {
   __shared__ Shared S;
-  extern __shared__ double dyn[];
   const int trial = blockIdx.x;
-  double* sortbuf = gscratch ? gscratch + (size_t)blockIdx.x * kTileColumns * SP : dyn;
+  double* sortbuf = gscratch ? gscratch + (size_t)blockIdx.x * kTileColumns * SP : nullptr;   // NULL: shared tile
   // The trial's scalars, read many times by the trial-level code: one coalesced load.
   __shared__ double s_ts[PM_TS_COUNT];
   for (int i = threadIdx.x; i < PM_TS_COUNT; i += blockDim.x) s_ts[i] = T.trial_scalars[(size_t)trial * PM_TS_COUNT + i];

@@ -32,6 +32,19 @@ struct NeumaierSum {
   }
 };
 
+// sum(x[0:n]) in CPython's order, loads hoisted four at a time so only the
+// dependent adds remain on the critical path.
+__device__ __forceinline__ double neumaier_sum(const double* x, int n) {
+  NeumaierSum s;
+  int k = 0;
+  for (; k + 4 <= n; k += 4) {
+    const double a = x[k], b = x[k + 1], c = x[k + 2], d = x[k + 3];
+    s.add(a); s.add(b); s.add(c); s.add(d);
+  }
+  for (; k < n; ++k) s.add(x[k]);
+  return s.result();
+}
+
 // First index in [lo, hi) with t[i] >= x.
 __device__ __forceinline__ int64_t lower_bound(const double* t, int64_t lo, int64_t hi, double x) {
   while (lo < hi) { int64_t mid = lo + ((hi - lo) >> 1); if (t[mid] < x) lo = mid + 1; else hi = mid; }
@@ -88,6 +101,9 @@ __device__ inline void bitonic_sort_columns(double* base, int stride, const int*
 // are warp shuffles, and only j >= 32*E go through `xchg` (P doubles of
 // shared memory) with a CTA barrier, so P = 512 on 256 threads needs 6
 // barrier stages instead of 45.  All threads of the CTA call it.
+// Up to kSortBatch columns sorted together by cta_register_sort_batch.
+constexpr int kSortBatch = 3;
+
 // The compare-exchanges of one bitonic stage between a thread's own
 // elements (distance J < E).
 template <int E, int J>
@@ -149,6 +165,83 @@ __device__ void cta_register_sort(double* v, int P, double* xchg) {
 #pragma unroll
   for (int e = 0; e < E; ++e)
     if (t * E + e < P) v[t * E + e] = r[e];
+  __syncthreads();
+}
+
+// cta_register_sort on ncols (<= kSortBatch) columns at once: column c is
+// base + cols[c] * stride, its exchange buffer xchg + c * xstride.  The
+// columns' stages interleave, so their shuffle latencies overlap and they
+// share one set of CTA barriers.  All threads of the CTA call it.
+template <int E>
+__device__ __forceinline__ void cta_register_sort_batch(double* base, int stride, const int* cols, int ncols, int P, double* xchg,
+                                        int xstride) {
+  const int t = threadIdx.x;
+  double r[kSortBatch][E];
+#pragma unroll
+  for (int c = 0; c < kSortBatch; ++c)
+#pragma unroll
+    for (int e = 0; e < E; ++e)
+      r[c][e] = (c < ncols && t * E + e < P) ? base[(size_t)cols[c] * stride + t * E + e] : dinf();
+  for (int k = 2; k <= P; k <<= 1) {
+    for (int j = k >> 1; j > 0; j >>= 1) {
+      if (j < E) {
+#pragma unroll
+        for (int c = 0; c < kSortBatch; ++c) {
+          if (c >= ncols) continue;
+          if (j == 1) register_exchange<E, 1>(r[c], t, k);
+          else if (j == 2) register_exchange<E, 2>(r[c], t, k);
+          else register_exchange<E, 4>(r[c], t, k);
+        }
+      } else if (j < 32 * E) {
+        const int m = j / E;
+#pragma unroll
+        for (int c = 0; c < kSortBatch; ++c) {
+          if (c >= ncols) continue;
+#pragma unroll
+          for (int e = 0; e < E; ++e) {
+            const double other = __shfl_xor_sync(0xffffffffu, r[c][e], m);
+            const int i = t * E + e;
+            const bool keep_low = ((i & j) == 0) == ((i & k) == 0);
+            const double a = r[c][e];
+            const double low = a <= other ? a : other, high = a <= other ? other : a;
+            r[c][e] = keep_low ? low : high;
+          }
+        }
+      } else {
+        __syncthreads();
+#pragma unroll
+        for (int c = 0; c < kSortBatch; ++c) {
+          if (c >= ncols) continue;
+#pragma unroll
+          for (int e = 0; e < E; ++e)
+            if (t * E + e < P) xchg[(size_t)c * xstride + t * E + e] = r[c][e];
+        }
+        __syncthreads();
+#pragma unroll
+        for (int c = 0; c < kSortBatch; ++c) {
+          if (c >= ncols) continue;
+#pragma unroll
+          for (int e = 0; e < E; ++e) {
+            const int i = t * E + e;
+            if (i >= P) continue;
+            const double other = xchg[(size_t)c * xstride + (i ^ j)];
+            const bool keep_low = ((i & j) == 0) == ((i & k) == 0);
+            const double a = r[c][e];
+            const double low = a <= other ? a : other, high = a <= other ? other : a;
+            r[c][e] = keep_low ? low : high;
+          }
+        }
+      }
+    }
+  }
+  __syncthreads();
+#pragma unroll
+  for (int c = 0; c < kSortBatch; ++c) {
+    if (c >= ncols) continue;
+#pragma unroll
+    for (int e = 0; e < E; ++e)
+      if (t * E + e < P) base[(size_t)cols[c] * stride + t * E + e] = r[c][e];
+  }
   __syncthreads();
 }
 
