@@ -1062,13 +1062,13 @@ int launch_analyze(const pm_trials& T, const pm_policy& P, const pm_trial_result
   if (use_global && !gscratch) return 1;  // caller must supply scratch
   if (T.n_trials == 0) return 0;
   const size_t dyn = use_global ? 0 : smem;
-  // Static plus dynamic shared memory above 48 KB needs the opt-in attribute.
+  // The kernel's static shared memory, for the opt-in check.
   static size_t static_bytes = [] {
     cudaFuncAttributes attr{};
     return cudaFuncGetAttributes(&attr, analyze_kernel) == cudaSuccess ? attr.sharedSizeBytes : size_t(48 * 1024);
   }();
-  if (static_bytes + dyn > 48 * 1024)
-    cudaFuncSetAttribute(analyze_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)dyn);
+  static std::atomic<int> limits[kMaxDevices];
+  ensure_dynamic_smem(analyze_kernel, static_bytes, dyn, limits);
   analyze_kernel<<<T.n_trials, kThreads, dyn, stream>>>(T, P, R, SP, use_global ? gscratch : nullptr);
   return 0;
 }

@@ -660,13 +660,13 @@ size_t bootstrap_smem_shortfall(int M, int mm, size_t* available) {
 int launch_bootstrap(const BootArgs& A, cudaStream_t stream) {
   if (A.n_groups == 0) return 0;
   const size_t smem = BootSmem(A.n_metrics, A.max_members, A.max_members > kHistMaxN).total;
-  // Static plus dynamic shared memory above 48 KB needs the opt-in attribute.
+  // The kernel's static shared memory, for the opt-in check.
   static size_t static_bytes = [] {
     cudaFuncAttributes attr{};
     return cudaFuncGetAttributes(&attr, bootstrap_kernel) == cudaSuccess ? attr.sharedSizeBytes : size_t(48 * 1024);
   }();
-  if (static_bytes + smem > 48 * 1024)
-    cudaFuncSetAttribute(bootstrap_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+  static std::atomic<int> limits[kMaxDevices];
+  ensure_dynamic_smem(bootstrap_kernel, static_bytes, smem, limits);
   bootstrap_kernel<<<A.n_groups, kBootThreads, smem, stream>>>(A);
   return 0;
 }

@@ -11,6 +11,9 @@
 #include <string>
 #include <type_traits>
 #include <vector>
+#if defined(__x86_64__)
+#include <emmintrin.h>
+#endif
 
 #include "pmb200.h"
 #include "pm_layout.h"
@@ -82,6 +85,8 @@ int arena_reserve(Arena& a, size_t dev_bytes, size_t host_bytes) {
     cudaError_t e = cudaStreamCreateWithFlags(&a.side, cudaStreamNonBlocking);
     if (e == cudaSuccess) e = cudaEventCreateWithFlags(&a.fork, cudaEventDisableTiming);
     if (e == cudaSuccess) e = cudaEventCreateWithFlags(&a.join, cudaEventDisableTiming);
+    if (e == cudaSuccess) e = cudaEventCreateWithFlags(&a.analysed, cudaEventDisableTiming);
+    if (e == cudaSuccess) e = cudaEventCreateWithFlags(&a.results, cudaEventDisableTiming);
     if (e != cudaSuccess) return cuda_fail(e, "side stream / events");
   }
   return PM_OK;
@@ -166,6 +171,32 @@ struct Layout {
     used += count * sizeof(P);
   }
 };
+
+// memcpy into the pinned staging buffer with non-temporal stores: the lines
+// go to memory instead of this core's cache, so the DMA that reads them next
+// does not have to fetch them back out of other cores' caches, and no line
+// is read for ownership first.  `dst` is 16-byte aligned (arena offsets are).
+void stream_copy(char* dst, const char* src, size_t bytes) {
+#if defined(__x86_64__)
+  size_t i = 0;
+  if ((reinterpret_cast<uintptr_t>(dst) & 15) == 0) {
+    for (; i + 64 <= bytes; i += 64) {
+      const __m128i a = _mm_loadu_si128(reinterpret_cast<const __m128i*>(src + i));
+      const __m128i b = _mm_loadu_si128(reinterpret_cast<const __m128i*>(src + i + 16));
+      const __m128i c = _mm_loadu_si128(reinterpret_cast<const __m128i*>(src + i + 32));
+      const __m128i d = _mm_loadu_si128(reinterpret_cast<const __m128i*>(src + i + 48));
+      _mm_stream_si128(reinterpret_cast<__m128i*>(dst + i), a);
+      _mm_stream_si128(reinterpret_cast<__m128i*>(dst + i + 16), b);
+      _mm_stream_si128(reinterpret_cast<__m128i*>(dst + i + 32), c);
+      _mm_stream_si128(reinterpret_cast<__m128i*>(dst + i + 48), d);
+    }
+    _mm_sfence();   // the streamed lines are visible before the task reports done
+  }
+  if (i < bytes) memcpy(dst + i, src + i, bytes - i);
+#else
+  memcpy(dst, src, bytes);
+#endif
+}
 
 }  // namespace
 
@@ -263,13 +294,14 @@ struct StagedTrials {
   pm_trials dev;              // device view of the staged batch
   pm_trial_results dres, hres;
   size_t in_bytes = 0, res_bytes = 0, end = 0;   // byte extents inside the arena
+  size_t scratch = 0;         // analysis scratch (long phases), after the caller's extra device bytes
   int max_cov = 0;
   double* gscratch = nullptr;
 };
 
-// Size, reserve (plus `extra_dev`/`extra_host` bytes after the results) and
-// stage a host batch into the device arena; enqueue the H2D copy.
-int stage_trials(Arena& A, const pm_trials& T, size_t extra_dev, size_t extra_host, StagedTrials& S) {
+// Check a host batch and size its arena layout: inputs, then results, then
+// (after the caller's extra device bytes) the analysis scratch.
+int plan_trials(const pm_trials& T, StagedTrials& S) {
   int rc = check_trials_host(T);
   if (rc) return rc;
   const size_t n = (size_t)T.n_trials;
@@ -282,16 +314,21 @@ int stage_trials(Arena& A, const pm_trials& T, size_t extra_dev, size_t extra_ho
   // reserve for the worst case the batch allows (its longest offsets span).
   int64_t bound = 0;
   for (size_t s = 0; s < n * PM_PHASES; ++s) bound = std::max<int64_t>(bound, T.phase_offsets[s + 1] - T.phase_offsets[s]);
-  const size_t scratch = analyze_scratch_bytes((int)n, (int)bound);
+  S.scratch = analyze_scratch_bytes((int)n, (int)bound);
   S.end = S.in_bytes + S.res_bytes;
-  if ((rc = arena_reserve(A, S.end + scratch + extra_dev, S.end + extra_host))) return rc;
-  S.dev = T;
   S.max_cov = (int)bound;
-  S.dev.max_phase_samples = S.max_cov;
+  return PM_OK;
+}
 
+// Stage a planned batch into the reserved arena and enqueue its H2D copy on
+// A.stream; points S.dev's arrays into the arena.
+int copy_trials(Arena& A, const pm_trials& T, StagedTrials& S) {
+  const size_t n = (size_t)T.n_trials;
+  S.dev = T;
+  S.dev.max_phase_samples = S.max_cov;
   // Copy pieces of at most kPiece bytes in destination order, then the
   // sample-order scan in slot ranges; pool threads and this thread share them.
-  constexpr size_t kPiece = size_t(1) << 20, kDmaMin = size_t(4) << 20;
+  constexpr size_t kPiece = size_t(1) << 20, kDmaMin = size_t(1) << 20;
   struct Piece { const char* src; size_t dst; size_t bytes; };
   std::vector<Piece> pieces;
   pieces.reserve(S.in_bytes / kPiece + 64);
@@ -314,7 +351,7 @@ int stage_trials(Arena& A, const pm_trials& T, size_t extra_dev, size_t extra_ho
   char* dev = static_cast<char*>(A.dev);
   HostBatch batch(pieces.size() + scan_tasks, [&](size_t i) {
     if (i < pieces.size()) {
-      memcpy(host + pieces[i].dst, pieces[i].src, pieces[i].bytes);
+      stream_copy(host + pieces[i].dst, pieces[i].src, pieces[i].bytes);
     } else {
       const size_t t = i - pieces.size();
       scan_slots(T, slots * t / scan_tasks, slots * (t + 1) / scan_tasks, &longest[t], &bad[t]);
@@ -348,11 +385,26 @@ int stage_trials(Arena& A, const pm_trials& T, size_t extra_dev, size_t extra_ho
     using Ptr = std::remove_reference_t<decltype(p)>;
     p = reinterpret_cast<Ptr>(dev + offs[k++]);
   });
-  Layout dl{dev + S.in_bytes}, rl{host + S.in_bytes};
+  return PM_OK;
+}
+
+// Point S.dres, S.hres and S.gscratch into a reserved arena.
+void place_results(Arena& A, size_t n, size_t extra_dev, StagedTrials& S) {
+  char* dev = static_cast<char*>(A.dev);
+  Layout dl{dev + S.in_bytes}, rl{static_cast<char*>(A.host) + S.in_bytes};
   visit_results(S.dres, n, [&](auto*& p, size_t count) { dl.place(p, count); });
   visit_results(S.hres, n, [&](auto*& p, size_t count) { rl.place(p, count); });
-  S.gscratch = scratch ? reinterpret_cast<double*>(dev + S.end + extra_dev) : nullptr;
-  return PM_OK;
+  S.gscratch = S.scratch ? reinterpret_cast<double*>(dev + S.end + extra_dev) : nullptr;
+}
+
+// plan_trials, arena_reserve (plus `extra_dev`/`extra_host` bytes after the
+// results) and copy_trials in one step.
+int stage_trials(Arena& A, const pm_trials& T, size_t extra_dev, size_t extra_host, StagedTrials& S) {
+  int rc = plan_trials(T, S);
+  if (rc) return rc;
+  if ((rc = arena_reserve(A, S.end + S.scratch + extra_dev, S.end + extra_host))) return rc;
+  place_results(A, (size_t)T.n_trials, extra_dev, S);
+  return copy_trials(A, T, S);
 }
 
 void copy_results_out(const StagedTrials& S, size_t n, pm_trial_results* out) {
@@ -548,8 +600,10 @@ int pm_analyze_sweep(const pm_trials* trials, const pm_policy* policy, pm_trial_
   Arena& A = g_arenas[device];
   std::lock_guard<std::mutex> guard(A.lock);
   StagedTrials S;
+  if ((rc = plan_trials(*trials, S))) return rc;
   // extra host bytes hold the group inputs then outputs; extra device bytes mirror them plus scratch
-  if ((rc = stage_trials(A, *trials, gin + gout + bscratch, gin + gout, S))) return rc;
+  if ((rc = arena_reserve(A, S.end + S.scratch + gin + gout + bscratch, S.end + gin + gout))) return rc;
+  place_results(A, n, gin + gout + bscratch, S);
   char* hbase = static_cast<char*>(A.host) + S.end;
   char* dbase = static_cast<char*>(A.dev) + S.end;
   Layout hl{hbase};
@@ -558,8 +612,6 @@ int pm_analyze_sweep(const pm_trials* trials, const pm_policy* policy, pm_trial_
   hl.place(hr, J.n_members); if (J.member_rows) memcpy(hr, J.member_rows, (size_t)J.n_members * 4);
   else for (int i = 0; i < J.n_members; ++i) hr[i] = i;
   hl.place(hs, G); memcpy(hs, J.seeds, G * 8);
-  cudaError_t e = cudaMemcpyAsync(dbase, hbase, gin, cudaMemcpyHostToDevice, A.stream);
-  if (e != cudaSuccess) return cuda_fail(e, "cudaMemcpyAsync(groups)");
   auto dptr = [&](const void* h) { return dbase + (static_cast<const char*>(h) - hbase); };
   char* dout = dbase + gin;
   BootArgs args{(int)G, (int)M, J.resamples, mm, S.dres.metrics, reinterpret_cast<const int32_t*>(dptr(ho)),
@@ -567,31 +619,49 @@ int pm_analyze_sweep(const pm_trials* trials, const pm_policy* policy, pm_trial_
                 reinterpret_cast<double*>(dout), reinterpret_cast<double*>(dout + align256(G * M * 8)),
                 reinterpret_cast<double*>(dout + 2 * align256(G * M * 8)),
                 reinterpret_cast<uint8_t*>(dout + gout), 1};
-  // The resample streams need only seeds and group sizes: they are generated
-  // on the side stream while the trials are analysed, and the fold waits for both.
+  // The resample draws need only seeds and group sizes: their inputs go first,
+  // on the side stream, and the draws run there while the host stages the
+  // trials (the GPU is otherwise idle then); the fold waits for them.
+  cudaError_t e = cudaSuccess;
   if (G) {
-    e = cudaEventRecord(A.fork, A.stream);
-    if (e == cudaSuccess) e = cudaStreamWaitEvent(A.side, A.fork, 0);
-    if (e != cudaSuccess) return cuda_fail(e, "fork");
+    e = cudaMemcpyAsync(dbase, hbase, gin, cudaMemcpyHostToDevice, A.side);
+    if (e != cudaSuccess) return cuda_fail(e, "cudaMemcpyAsync(groups)");
     launch_bootstrap_prepare(args, A.side);
     e = cudaEventRecord(A.join, A.side);
-    if (e != cudaSuccess) return cuda_fail(e, "join record");
+    if (e != cudaSuccess) { cudaStreamSynchronize(A.side); return cuda_fail(e, "join record"); }
+  }
+  if ((rc = copy_trials(A, *trials, S))) {
+    cudaStreamSynchronize(A.side);   // the draws use the arena: done before it is reused
+    return rc;
   }
   launch_analyze(S.dev, *policy, S.dres, S.max_cov, S.gscratch, A.stream, nullptr);
-  if (G) {
-    e = cudaStreamWaitEvent(A.stream, A.join, 0);
-    if (e != cudaSuccess) return cuda_fail(e, "join");
+  // Per-trial results leave on the side stream while the fold runs; the host
+  // copies them out while the fold's results are still on their way.
+  e = cudaEventRecord(A.analysed, A.stream);
+  if (e == cudaSuccess) e = cudaStreamWaitEvent(A.side, A.analysed, 0);
+  if (e == cudaSuccess)
+    e = cudaMemcpyAsync(static_cast<char*>(A.host) + S.in_bytes, static_cast<char*>(A.dev) + S.in_bytes, S.res_bytes,
+                        cudaMemcpyDeviceToHost, A.side);
+  if (e == cudaSuccess) e = cudaEventRecord(A.results, A.side);
+  if (e == cudaSuccess && G) e = cudaStreamWaitEvent(A.stream, A.join, 0);
+  if (e == cudaSuccess && G) {
     launch_bootstrap(args, A.stream);
+    e = cudaGetLastError();
+    if (e == cudaSuccess) e = cudaMemcpyAsync(hbase + gin, dout, gout, cudaMemcpyDeviceToHost, A.stream);
   }
-  e = cudaGetLastError();
-  if (e != cudaSuccess) return cuda_fail(e, "sweep kernels launch");
-  e = cudaMemcpyAsync(static_cast<char*>(A.host) + S.in_bytes, static_cast<char*>(A.dev) + S.in_bytes, S.res_bytes,
-                      cudaMemcpyDeviceToHost, A.stream);
-  if (e == cudaSuccess && G) e = cudaMemcpyAsync(hbase + gin, dout, gout, cudaMemcpyDeviceToHost, A.stream);
-  if (e != cudaSuccess) return cuda_fail(e, "cudaMemcpyAsync(sweep results)");
-  e = cudaStreamSynchronize(A.stream);
-  if (e != cudaSuccess) return cuda_fail(e, "sweep kernels");
-  copy_results_out(S, n, out);
+  if (e == cudaSuccess) e = cudaGetLastError();
+  if (e != cudaSuccess) {
+    cudaStreamSynchronize(A.side);
+    cudaStreamSynchronize(A.stream);
+    return cuda_fail(e, "sweep kernels and copies");
+  }
+  e = cudaEventSynchronize(A.results);
+  if (e == cudaSuccess) copy_results_out(S, n, out);
+  const cudaError_t e2 = cudaStreamSynchronize(A.stream);
+  if (e != cudaSuccess || e2 != cudaSuccess) {
+    cudaStreamSynchronize(A.side);
+    return cuda_fail(e != cudaSuccess ? e : e2, "sweep kernels");
+  }
   if (G) {
     memcpy(groups->medians, hbase + gin, G * M * 8);
     memcpy(groups->ci_lo, hbase + gin + align256(G * M * 8), G * M * 8);

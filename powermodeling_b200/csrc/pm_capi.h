@@ -3,6 +3,7 @@
 #include <cuda_runtime.h>
 #include <cstddef>
 #include <cstdint>
+#include <atomic>
 #include <mutex>
 
 namespace pm {
@@ -28,6 +29,20 @@ struct BootArgs {
   int prepared;                   // 1: bootstrap_prepare_kernel filled scratch for each group's member count
 };
 
+// Raises `kernel`'s dynamic shared-memory limit on the current device to at
+// least `bytes` (static plus dynamic above 48 KB needs the opt-in); `limits`
+// remembers each device's current limit so the attribute call is made only
+// when it must grow, not on every launch.
+template <class Kernel>
+void ensure_dynamic_smem(Kernel kernel, size_t static_bytes, size_t bytes, std::atomic<int>* limits) {
+  if (static_bytes + bytes <= 48 * 1024) return;
+  int device = 0;
+  if (cudaGetDevice(&device) != cudaSuccess || device < 0 || device >= kMaxDevices) device = 0;
+  if ((int)bytes <= limits[device].load(std::memory_order_relaxed)) return;
+  if (cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)bytes) == cudaSuccess)
+    limits[device].store((int)bytes, std::memory_order_relaxed);
+}
+
 // Grow-only device workspace, pinned staging buffer and private stream of a device.
 struct Arena {
   void* dev = nullptr; size_t dev_bytes = 0;
@@ -35,6 +50,7 @@ struct Arena {
   cudaStream_t stream = nullptr;
   cudaStream_t side = nullptr;                 // work that overlaps the main stream (stream generation)
   cudaEvent_t fork = nullptr, join = nullptr;  // main -> side and side -> main ordering
+  cudaEvent_t analysed = nullptr, results = nullptr;   // trial results ready on the device / on the host
   std::mutex lock;
 };
 extern Arena g_arenas[kMaxDevices];
