@@ -83,26 +83,27 @@ __device__ void seed_state(uint32_t* mt, uint64_t seed) {
 }
 
 // One twist of the MT19937 state by the CTA.  `src` holds the current
-// state and `dst` receives the next one (ping-pong buffers), so each of the
-// three dependency segments needs a single barrier: segment 1 (i < 227)
-// reads only old words, segments 2 and 3 read new words of the segment
-// before.  Outputs are tempered as they are produced, into ring[base + i].
+// state and `dst` receives the next one (ping-pong buffers).  Word i < 227
+// reads old words only; word i >= 227 reads new word i - 227.  Thread
+// t < 227 therefore produces the chain t, t + 227, t + 454 (t < 170) with
+// every new operand in its own registers, and the last word (623), which
+// also reads new word 0, recomputes that word from the old state: a single
+// barrier per twist.  Outputs are tempered as they are produced, into
+// ring[base + i].
 __device__ __forceinline__ void twist_block(const uint32_t* src, uint32_t* dst, uint32_t* ring, int base) {
   constexpr int A = kMtN - kMtM;          // 227
-  for (int i = threadIdx.x; i < A; i += blockDim.x) {
-    const uint32_t v = twist_one(src[i], src[i + 1], src[i + kMtM]);
-    dst[i] = v; ring[base + i] = temper(v);
-  }
-  __syncthreads();
-  for (int i = A + threadIdx.x; i < 2 * A; i += blockDim.x) {
-    const uint32_t v = twist_one(src[i], src[i + 1], dst[i - A]);
-    dst[i] = v; ring[base + i] = temper(v);
-  }
-  __syncthreads();
-  for (int i = 2 * A + threadIdx.x; i < kMtN; i += blockDim.x) {
-    const uint32_t v = i < kMtN - 1 ? twist_one(src[i], src[i + 1], dst[i - A])
-                                    : twist_one(src[kMtN - 1], dst[0], dst[kMtM - 1]);
-    dst[i] = v; ring[base + i] = temper(v);
+  const int t = threadIdx.x;
+  if (t < A) {
+    const uint32_t a = twist_one(src[t], src[t + 1], src[t + kMtM]);
+    const uint32_t b = twist_one(src[t + A], src[t + A + 1], a);
+    dst[t] = a; ring[base + t] = temper(a);
+    dst[t + A] = b; ring[base + t + A] = temper(b);
+    if (t < kMtN - 2 * A) {
+      const int i = t + 2 * A;
+      const uint32_t next = i < kMtN - 1 ? src[i + 1] : twist_one(src[0], src[1], src[kMtM]);
+      const uint32_t c = twist_one(src[i], next, b);
+      dst[i] = c; ring[base + i] = temper(c);
+    }
   }
   __syncthreads();
 }
