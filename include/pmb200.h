@@ -9,7 +9,9 @@
  *   - "host" entry points take host pointers and copy in and out themselves
  *     (the end-to-end path); "_device" variants take device pointers and a
  *     cudaStream_t passed as void* and never synchronize the stream;
- *   - a floating value that the reference reports as None travels as NaN.
+ *   - a floating value that the reference reports as None travels as NaN;
+ *     every other floating input is finite (the reference reads a non-finite
+ *     number as None).
  *
  * The analysis entry points replace the numeric core of
  * powermodeling/analysis.py (the reference's Python): _interpolate/_integrate

@@ -50,6 +50,7 @@ struct Shared {
   double cmin[C_COUNT], cmax[C_COUNT];
   int32_t sort_cols[C_COUNT], nsort, sort_p;
   int32_t distinct_power;   // distinct finite powers of a sorted power column, -1 if not sorted
+  int32_t anchor_q;         // first covering sample flagged as energy anchor (INT32_MAX: none)
 };
 
 // Sample i of a per-sample column; a broadcast column holds one element.
@@ -265,93 +266,106 @@ __device__ __noinline__ void phase_stats_impl(const pm_trials& T, const pm_polic
       __syncthreads();
     }
   }
-  // ---- flag reductions over selected samples.
-  uint32_t flags = 0;
-  unsigned long long thr_or = 0ull;
-  unsigned src_mask = 0;
-  bool neg_power = false;
-  int plim_none = 0, enf_none = 0, pst_none = 0;
-  for (int64_t i = lo + threadIdx.x; i < hi; i += blockDim.x) {
-    const uint16_t sf = col_at(T.sample_flags, PM_COL_SAMPLE_FLAGS, T, i);
-    if (!none(col_at(T.sm_clock_mhz, PM_COL_SM_CLOCK, T, i))) flags |= 1u << PM_PF_ANY_SM_FINITE;
-    if (none(col_at(T.temperature_c, PM_COL_TEMPERATURE, T, i))) flags |= 1u << PM_PF_TEMP_MISSING;
-    { const double v = col_at(T.graphics_clock_mhz, PM_COL_GRAPHICS_CLOCK, T, i); if (none(v) || v <= 0) flags |= 1u << PM_PF_GFX_NONPOS; }
-    { const double v = col_at(T.memory_clock_mhz, PM_COL_MEMORY_CLOCK, T, i); if (none(v) || v <= 0) flags |= 1u << PM_PF_MEM_NONPOS; }
-    { const double v = col_at(T.sm_clock_mhz, PM_COL_SM_CLOCK, T, i); if (none(v) || v <= 0) flags |= 1u << PM_PF_SM_NONPOS; }
-    if (!(sf & PM_S_THROTTLE_VALID)) flags |= 1u << PM_PF_THROTTLE_MISSING;
-    else thr_or |= (unsigned long long)col_at(T.throttle_reasons, PM_COL_THROTTLE, T, i) & ~3ull;
-    if (sf & PM_S_FOREIGN_PID) flags |= 1u << PM_PF_FOREIGN_PID;
-    if (sf & PM_S_NO_COMPUTE_INV) flags |= 1u << PM_PF_NO_COMPUTE_INV;
-    if (sf & PM_S_NO_GRAPHICS_INV) flags |= 1u << PM_PF_NO_GRAPHICS_INV;
-    if (sf & PM_S_MPS) flags |= 1u << PM_PF_MPS;
-    if (sf & PM_S_PID_UNKNOWN) flags |= 1u << PM_PF_PID_UNKNOWN;
-    if (sf & PM_S_REF_FOREIGN) flags |= 1u << PM_PF_REF_FOREIGN;
-    if ((sf & PM_S_MEMORY_POWER_SET) && col_at(T.memory_power_source, PM_COL_MEMORY_SOURCE, T, i)) src_mask |= 1u << (col_at(T.memory_power_source, PM_COL_MEMORY_SOURCE, T, i) & 15);
-    plim_none += none(col_at(T.power_limit_w, PM_COL_POWER_LIMIT, T, i));
-    enf_none += none(col_at(T.enforced_power_limit_w, PM_COL_ENFORCED_LIMIT, T, i));
-    pst_none += none(col_at(T.pstate, PM_COL_PSTATE, T, i));
-  }
-  // negative power is checked over the covering samples
-  for (int64_t i = cb + threadIdx.x; i < ce; i += blockDim.x) {
-    const double v = col_at(T.power_w, PM_COL_POWER_W, T, i);
-    if (!none(v) && v < 0) neg_power = true;
-  }
-  // per-column finite counts, minima and maxima (selected columns; gaps from covering)
-  int fin[C_COUNT];
-  double cmn[C_COUNT], cmx[C_COUNT];
-  for (int c = 0; c < C_COUNT; ++c) { fin[c] = 0; cmn[c] = inf; cmx[c] = -inf; }
-  for (int q = threadIdx.x; q < SP; q += blockDim.x) {
-    for (int c = 0; c < C_COUNT; ++c) {
-      if (T.broadcast_columns & column_bit(c)) continue;
-      const double v = sortbuf[c * SP + q];
-      if (v != inf) { ++fin[c]; cmn[c] = fmin(cmn[c], v); cmx[c] = fmax(cmx[c], v); }
-    }
-  }
+  // The covering samples' times and powers (the energy inputs) are staged
+  // by the pass below; the energy counter and the trapezoid terms follow the
+  // sort, whose exchange buffers share their columns.
+  double* st_t = sortbuf + (size_t)(C_COUNT + S_T) * SP;
+  double* st_p = sortbuf + (size_t)(C_COUNT + S_POWER) * SP;
+  double* st_m = sortbuf + (size_t)(C_COUNT + S_MEMORY) * SP;
+  double* st_r = sortbuf + (size_t)(C_COUNT + S_REL) * SP;
+  double* term_p = sortbuf + (size_t)(C_COUNT + S_TERM_P) * SP;
+  double* term_m = sortbuf + (size_t)(C_COUNT + S_TERM_M) * SP;
+  // ---- reductions over the selected samples.
+  // Each staged column (finite values, +inf for None) is reduced by one warp:
+  // finite count, minimum and maximum.  The flags of the staged clock,
+  // temperature, limit and pstate columns follow from those; sample flags,
+  // throttle reasons and memory-power sources are read in one pass over the
+  // covering samples, which also stages the energy inputs.
   {
-    __shared__ uint32_t red_flags; __shared__ unsigned long long red_thr; __shared__ unsigned red_src;
-    __shared__ int red_neg, red_pn, red_en, red_sn;
-    __shared__ double wmin[kThreads / 32][C_COUNT], wmax[kThreads / 32][C_COUNT];
-    __shared__ int wfin[kThreads / 32][C_COUNT];
-    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-    for (int c = 0; c < C_COUNT; ++c) {
-      double mn = cmn[c], mx = cmx[c]; int f = fin[c];
-      for (int o = 16; o; o >>= 1) {
-        mn = fmin(mn, __shfl_xor_sync(0xffffffffu, mn, o));
-        mx = fmax(mx, __shfl_xor_sync(0xffffffffu, mx, o));
-        f += __shfl_xor_sync(0xffffffffu, f, o);
-      }
-      if (lane == 0) { wmin[warp][c] = mn; wmax[warp][c] = mx; wfin[warp][c] = f; }
-    }
-    if (threadIdx.x == 0) { red_flags = 0; red_thr = 0; red_src = 0; red_neg = 0; red_pn = red_en = red_sn = 0; }
-    __syncthreads();
-    if (flags) atomicOr(&red_flags, flags);
-    if (thr_or) atomicOr(&red_thr, thr_or);
-    if (src_mask) atomicOr(&red_src, src_mask);
-    if (neg_power) atomicOr(&red_neg, 1);
-    if (plim_none) atomicAdd(&red_pn, plim_none);
-    if (enf_none) atomicAdd(&red_en, enf_none);
-    if (pst_none) atomicAdd(&red_sn, pst_none);
-    if (threadIdx.x < C_COUNT) {
-      const int c = threadIdx.x;
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, nwarps = blockDim.x >> 5;
+    const int span = ncov > nsel ? ncov : nsel;          // every staged entry lies below it
+    for (int c = warp; c < C_COUNT; c += nwarps) {
       double mn = inf, mx = -inf; int f = 0;
       if (T.broadcast_columns & column_bit(c)) {
         // every selected sample holds the one value: as if staged nsel times
         const double v = col_value(T, c, 0);
         if (!none(v) && nsel > 0) { mn = mx = v; f = nsel; }
       } else {
-        for (int w = 0; w < (int)(blockDim.x >> 5); ++w) { mn = fmin(mn, wmin[w][c]); mx = fmax(mx, wmax[w][c]); f += wfin[w][c]; }
+        const double* col = sortbuf + (size_t)c * SP;
+        for (int q = lane; q < span; q += 32) {
+          const double v = col[q];
+          if (v != inf) { ++f; mn = fmin(mn, v); mx = fmax(mx, v); }
+        }
+        for (int o = 16; o; o >>= 1) {
+          mn = fmin(mn, __shfl_xor_sync(0xffffffffu, mn, o));
+          mx = fmax(mx, __shfl_xor_sync(0xffffffffu, mx, o));
+          f += __shfl_xor_sync(0xffffffffu, f, o);
+        }
       }
-      S.cmin[c] = mn; S.cmax[c] = mx; S.nfin[c] = f;
+      if (lane == 0) { S.cmin[c] = mn; S.cmax[c] = mx; S.nfin[c] = f; }
+    }
+    uint32_t flags = 0, thr_lo = 0, thr_hi = 0, src_mask = 0, anchor_q = 0x7fffffffu;
+    bool neg_power = false;
+    for (int q = threadIdx.x; q < ncov; q += blockDim.x) {
+      const int64_t i = cb + q;
+      const double pw = col_at(T.power_w, PM_COL_POWER_W, T, i);
+      const uint16_t sf = col_at(T.sample_flags, PM_COL_SAMPLE_FLAGS, T, i);
+      st_t[q] = t[i]; st_p[q] = pw; st_m[q] = col_at(T.memory_power_w, PM_COL_MEMORY_POWER_W, T, i);
+      if ((sf & PM_S_ENERGY_ANCHOR) && (uint32_t)q < anchor_q) anchor_q = (uint32_t)q;
+      if (!none(pw) && pw < 0) neg_power = true;   // negative power is checked over the covering samples
+      if (i < lo || i >= hi) continue;             // the rest concerns the selected samples
+      if (!(sf & PM_S_THROTTLE_VALID)) flags |= 1u << PM_PF_THROTTLE_MISSING;
+      else {
+        const unsigned long long thr = (unsigned long long)col_at(T.throttle_reasons, PM_COL_THROTTLE, T, i) & ~3ull;
+        thr_lo |= (uint32_t)thr; thr_hi |= (uint32_t)(thr >> 32);
+      }
+      if (sf & PM_S_FOREIGN_PID) flags |= 1u << PM_PF_FOREIGN_PID;
+      if (sf & PM_S_NO_COMPUTE_INV) flags |= 1u << PM_PF_NO_COMPUTE_INV;
+      if (sf & PM_S_NO_GRAPHICS_INV) flags |= 1u << PM_PF_NO_GRAPHICS_INV;
+      if (sf & PM_S_MPS) flags |= 1u << PM_PF_MPS;
+      if (sf & PM_S_PID_UNKNOWN) flags |= 1u << PM_PF_PID_UNKNOWN;
+      if (sf & PM_S_REF_FOREIGN) flags |= 1u << PM_PF_REF_FOREIGN;
+      if (sf & PM_S_MEMORY_POWER_SET) {
+        const uint8_t src = col_at(T.memory_power_source, PM_COL_MEMORY_SOURCE, T, i);
+        if (src) src_mask |= 1u << (src & 15);
+      }
+    }
+    flags = __reduce_or_sync(0xffffffffu, flags);
+    anchor_q = __reduce_min_sync(0xffffffffu, anchor_q);
+    thr_lo = __reduce_or_sync(0xffffffffu, thr_lo);
+    thr_hi = __reduce_or_sync(0xffffffffu, thr_hi);
+    src_mask = __reduce_or_sync(0xffffffffu, src_mask);
+    const bool any_neg = __any_sync(0xffffffffu, neg_power);
+    __shared__ uint32_t red_flags, red_thr_lo, red_thr_hi, red_src;
+    __shared__ int red_neg;
+    if (threadIdx.x == 0) { red_flags = 0; red_thr_lo = red_thr_hi = 0; red_src = 0; red_neg = 0; S.anchor_q = 0x7fffffff; }
+    __syncthreads();
+    if (lane == 0) {
+      if (anchor_q != 0x7fffffffu) atomicMin(&S.anchor_q, (int)anchor_q);
+      if (flags) atomicOr(&red_flags, flags);
+      if (thr_lo) atomicOr(&red_thr_lo, thr_lo);
+      if (thr_hi) atomicOr(&red_thr_hi, thr_hi);
+      if (src_mask) atomicOr(&red_src, src_mask);
+      if (any_neg) red_neg = 1;
     }
     __syncthreads();
     if (threadIdx.x == 0) {
       uint32_t fl = red_flags;
-      if (red_thr) fl |= 1u << PM_PF_THROTTLE_ACTIVE;
+      const unsigned long long thr = ((unsigned long long)red_thr_hi << 32) | red_thr_lo;
+      if (S.nfin[C_SM] > 0) fl |= 1u << PM_PF_ANY_SM_FINITE;
+      if (S.nfin[C_TEMP] < nsel) fl |= 1u << PM_PF_TEMP_MISSING;
+      // "None or <= 0" for some selected sample: a None, or a minimum <= 0
+      if (S.nfin[C_GFX] < nsel || S.cmin[C_GFX] <= 0) fl |= 1u << PM_PF_GFX_NONPOS;
+      if (S.nfin[C_MEM] < nsel || S.cmin[C_MEM] <= 0) fl |= 1u << PM_PF_MEM_NONPOS;
+      if (S.nfin[C_SM] < nsel || S.cmin[C_SM] <= 0) fl |= 1u << PM_PF_SM_NONPOS;
+      if (thr) fl |= 1u << PM_PF_THROTTLE_ACTIVE;
       if (red_neg) fl |= 1u << PM_PF_NEGATIVE_POWER;
       S.pf[p] |= fl | (1u << PM_PF_COMPUTED);
-      po[PM_PO_THROTTLE_OR] = (double)red_thr;
+      po[PM_PO_THROTTLE_OR] = (double)thr;
       po[PM_PO_MEM_SOURCES] = (double)red_src;
-      po[PM_PO_PLIMIT_NONE] = red_pn; po[PM_PO_ENF_NONE] = red_en; po[PM_PO_PSTATE_NONE] = red_sn;
+      po[PM_PO_PLIMIT_NONE] = nsel - S.nfin[C_PLIMIT];
+      po[PM_PO_ENF_NONE] = nsel - S.nfin[C_ENF];
+      po[PM_PO_PSTATE_NONE] = nsel - S.nfin[C_PSTATE];
       // Only columns holding more than one distinct value need an order.
       int ns = 0, longest = 2;
       for (int c = 0; c < C_COUNT; ++c)
@@ -389,24 +403,21 @@ __device__ __noinline__ void phase_stats_impl(const pm_trials& T, const pm_polic
       __syncthreads();
     }
   }
-  // ---- energies: stage the covering samples, form trapezoid terms in
-  // parallel, then accumulate each sum on one lane in the reference's order.
-  double* st_t = sortbuf + (size_t)(C_COUNT + S_T) * SP;
-  double* st_p = sortbuf + (size_t)(C_COUNT + S_POWER) * SP;
-  double* st_m = sortbuf + (size_t)(C_COUNT + S_MEMORY) * SP;
-  double* st_r = sortbuf + (size_t)(C_COUNT + S_REL) * SP;
-  double* term_p = sortbuf + (size_t)(C_COUNT + S_TERM_P) * SP;
-  double* term_m = sortbuf + (size_t)(C_COUNT + S_TERM_M) * SP;
-  __shared__ int anchor_idx;
-  if (threadIdx.x == 0) anchor_idx = 0x7fffffff;
-  __syncthreads();
-  for (int q = threadIdx.x; q < ncov; q += blockDim.x) {
-    st_t[q] = t[cb + q]; st_p[q] = col_at(T.power_w, PM_COL_POWER_W, T, cb + q); st_m[q] = col_at(T.memory_power_w, PM_COL_MEMORY_POWER_W, T, cb + q);
-    if (col_at(T.sample_flags, PM_COL_SAMPLE_FLAGS, T, cb + q) & PM_S_ENERGY_ANCHOR) atomicMin(&anchor_idx, q);
+  // ---- energies: stage the energy counter relative to its anchor (its
+  // column held a sort exchange buffer) while warps 0-2 find the window's
+  // edges in the staged times; form the trapezoid terms in parallel, then
+  // accumulate each sum on one lane in the reference's order.
+  __shared__ int s_edge[3];   // upper_bound(start), lower_bound(start), lower_bound(end) over st_t
+  __shared__ int s_gap;
+  if (threadIdx.x < 96) {
+    const int w = threadIdx.x >> 5;
+    const int64_t r = warp_bound(st_t, 0, ncov, w == 2 ? end : start, w == 0, threadIdx.x & 31);
+    if ((threadIdx.x & 31) == 0) s_edge[w] = (int)r;
   }
-  __syncthreads();
+  if (threadIdx.x == 0) s_gap = 0;
   {
-    const int64_t anchor = anchor_idx == 0x7fffffff ? 0 : col_at(T.energy_int, PM_COL_ENERGY_INT, T, cb + anchor_idx);
+    const int aq = S.anchor_q;
+    const int64_t anchor = aq == 0x7fffffff ? 0 : col_at(T.energy_int, PM_COL_ENERGY_INT, T, cb + aq);
     for (int q = threadIdx.x; q < ncov; q += blockDim.x) {
       const uint16_t sf = col_at(T.sample_flags, PM_COL_SAMPLE_FLAGS, T, cb + q);
       double v;
@@ -418,19 +429,19 @@ __device__ __noinline__ void phase_stats_impl(const pm_trials& T, const pm_polic
   }
   __syncthreads();
   // Interior samples are covering indices [ia, ib): start < t < end.
-  const int ia = (int)(upper_bound(st_t, 0, ncov, start)), ib = (int)(lower_bound(st_t, 0, ncov, end));
+  const int ia = s_edge[0], lb_start = s_edge[1], ib = s_edge[2];
   const int nterms = ib > ia ? ib - ia + 1 : 1;
-  auto value_at = [&](const double* v, double x) -> double {
+  // _interpolate at x, given i = lower_bound(st_t, x).
+  auto value_at = [&](const double* v, double x, int i) -> double {
     if (ncov <= 0 || x < st_t[0] || x > st_t[ncov - 1]) return dnan();
-    const int i = (int)lower_bound(st_t, 0, ncov, x);
     if (st_t[i] == x) return v[i];
     const double a = v[i - 1], b = v[i];
     if (none(a) || none(b)) return dnan();
     const double ratio = (x - st_t[i - 1]) / (st_t[i] - st_t[i - 1]);
     return a + ratio * (b - a);
   };
-  const double p0 = value_at(st_p, start), p1 = value_at(st_p, end);
-  const double m0 = value_at(st_m, start), m1 = value_at(st_m, end);
+  const double p0 = value_at(st_p, start, lb_start), p1 = value_at(st_p, end, ib);
+  const double m0 = value_at(st_m, start, lb_start), m1 = value_at(st_m, end, ib);
   bool gap_p = false, gap_m = false;
   for (int k = threadIdx.x; k < nterms; k += blockDim.x) {
     // term k joins point k-1 and point k of [start, interior..., end]
@@ -442,8 +453,13 @@ __device__ __noinline__ void phase_stats_impl(const pm_trials& T, const pm_polic
     term_p[k] = (tb - ta) * (pa + pb) * 0.5;
     term_m[k] = (tb - ta) * (ma + mb) * 0.5;
   }
-  gap_p = __syncthreads_or(gap_p);
-  gap_m = __syncthreads_or(gap_m);
+  {
+    const unsigned gp = __ballot_sync(0xffffffffu, gap_p), gm = __ballot_sync(0xffffffffu, gap_m);
+    if ((threadIdx.x & 31) == 0 && (gp | gm)) atomicOr(&s_gap, (gp ? 1 : 0) | (gm ? 2 : 0));
+  }
+  __syncthreads();
+  gap_p = (s_gap & 1) != 0;
+  gap_m = (s_gap & 2) != 0;
   if (threadIdx.x == 0) {
     double energy = dnan();
     if (!none(p0) && !none(p1) && end > start && !gap_p) {
@@ -459,7 +475,7 @@ __device__ __noinline__ void phase_stats_impl(const pm_trials& T, const pm_polic
     po[PM_PO_MEMORY_ENERGY_J] = me;
     po[PM_PO_MEMORY_POWER_W] = none(me) ? dnan() : me / duration;
   } else if (threadIdx.x == 64) {
-    const double c0 = value_at(st_r, start), c1 = value_at(st_r, end);
+    const double c0 = value_at(st_r, start, lb_start), c1 = value_at(st_r, end, ib);
     bool reset = false, have = false;
     double prev = 0.0;
     for (int q = 0; q < ncov; ++q) {
