@@ -24,7 +24,7 @@ namespace pm {
 constexpr int kThreads = 256;
 constexpr int kMaxEpochs = 256;        // per arm; the host rejects longer lists
 enum Col { C_GAP = 0, C_CHANGE, C_POWER, C_GFX, C_SM, C_MEM, C_TEMP, C_PLIMIT, C_ENF, C_PSTATE, C_COUNT };
-// Staged (unsorted) covering samples that follow the sort columns in the tile.
+// Staged covering samples that follow the sample columns in the tile.
 enum Stage { S_T = 0, S_POWER, S_MEMORY, S_REL, S_TERM_P, S_TERM_M, S_COUNT };
 constexpr int kTileColumns = C_COUNT + S_COUNT;
 static_assert(kTileColumns == kSortColumns, "tile column count");
@@ -48,8 +48,9 @@ struct Shared {
   int32_t nchange;
   int32_t nfin[C_COUNT];
   double cmin[C_COUNT], cmax[C_COUNT];
-  int32_t sort_cols[C_COUNT], nsort, sort_p;
-  int32_t distinct_power;   // distinct finite powers of a sorted power column, -1 if not sorted
+  int32_t med_cols[C_COUNT], nmed;   // varying columns whose median is selected (power excluded)
+  double cmed[C_COUNT];              // their medians
+  int32_t distinct_power;   // distinct finite powers of a varying power column, -1 if it holds one value or none
   int32_t anchor_q;         // first covering sample flagged as energy anchor (INT32_MAX: none)
 };
 
@@ -163,6 +164,8 @@ __device__ __noinline__ void measure_epochs(const pm_trials& T, const pm_policy&
 // in global scratch.  Each case is its own instantiation, so the shared one
 // addresses the tile with shared-memory loads and stores.
 extern __shared__ double dyn_tile[];
+// Radix-select bins of each warp (one copy per CTA for both tile placements).
+__shared__ __align__(8) uint32_t g_sel_hist[kThreads / 32][256];
 
 template <bool kSharedTile>
 __device__ __noinline__ void phase_stats_impl(const pm_trials& T, const pm_policy& P, Shared& S, double* gtile, int SP,
@@ -339,6 +342,8 @@ __device__ __noinline__ void phase_stats_impl(const pm_trials& T, const pm_polic
     __shared__ uint32_t red_flags, red_thr_lo, red_thr_hi, red_src;
     __shared__ int red_neg;
     if (threadIdx.x == 0) { red_flags = 0; red_thr_lo = red_thr_hi = 0; red_src = 0; red_neg = 0; S.anchor_q = 0x7fffffff; }
+    // the distinct-power set (two free columns of the tile) starts empty
+    for (int q = threadIdx.x; q < 2 * SP; q += blockDim.x) reinterpret_cast<unsigned long long*>(term_p)[q] = kSetEmpty;
     __syncthreads();
     if (lane == 0) {
       if (anchor_q != 0x7fffffffu) atomicMin(&S.anchor_q, (int)anchor_q);
@@ -366,43 +371,43 @@ __device__ __noinline__ void phase_stats_impl(const pm_trials& T, const pm_polic
       po[PM_PO_PLIMIT_NONE] = nsel - S.nfin[C_PLIMIT];
       po[PM_PO_ENF_NONE] = nsel - S.nfin[C_ENF];
       po[PM_PO_PSTATE_NONE] = nsel - S.nfin[C_PSTATE];
-      // Only columns holding more than one distinct value need an order.
-      int ns = 0, longest = 2;
+      // Only columns holding more than one distinct value need a selection;
+      // of the power column only its distinct count is used.
+      int nm = 0;
       for (int c = 0; c < C_COUNT; ++c)
-        if (S.nfin[c] > 1 && S.cmin[c] != S.cmax[c]) { S.sort_cols[ns++] = c; longest = max(longest, S.nfin[c]); }
-      int P = 2;
-      while (P < longest) P <<= 1;
-      S.nsort = ns; S.sort_p = P;
+        if (c != C_POWER && S.nfin[c] > 1 && S.cmin[c] != S.cmax[c]) S.med_cols[nm++] = c;
+      S.nmed = nm;
+      S.distinct_power = S.nfin[C_POWER] > 1 && S.cmin[C_POWER] != S.cmax[C_POWER] ? 0 : -1;
     }
   }
   __syncthreads();
-  // ---- sort the varying columns over their finite prefix length (power of two)
-  // Sort the varying columns one after another, values in registers; the
-  // power column's distinct count follows from its sorted order.
-  if (S.nsort) {
-    const int P = S.sort_p;
-    // Three staged columns (REL, TERM_P, TERM_M) are unused until the energy
-    // terms: they hold the exchange buffers of up to kSortBatch columns.
-    double* xchg = sortbuf + (size_t)(C_COUNT + S_REL) * SP;
-    bool power_sorted = false;
-    for (int a = 0; a < S.nsort; ++a) power_sorted |= S.sort_cols[a] == C_POWER;
-    for (int a = 0; a < S.nsort; a += kSortBatch) {
-      const int nc = min(kSortBatch, S.nsort - a);
-      const int* cols = S.sort_cols + a;
-      if (P <= (int)blockDim.x) cta_register_sort_batch<1>(sortbuf, SP, cols, nc, P, xchg, SP);
-      else if (P <= 2 * (int)blockDim.x) cta_register_sort_batch<2>(sortbuf, SP, cols, nc, P, xchg, SP);
-      else if (P <= 4 * (int)blockDim.x) cta_register_sort_batch<4>(sortbuf, SP, cols, nc, P, xchg, SP);
-      else if (P <= 8 * (int)blockDim.x) cta_register_sort_batch<8>(sortbuf, SP, cols, nc, P, xchg, SP);
-      else bitonic_sort_columns(sortbuf, SP, cols, nc, P);
+  // ---- medians of the varying columns, distinct finite powers.
+  // A median needs order statistics (n-1)/2 and n/2 only: one warp selects
+  // them per column (warp_median); the warps without a column fill the
+  // distinct-power set (all warps when every warp has a column).
+  {
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, nwarps = blockDim.x >> 5;
+    const int span = ncov > nsel ? ncov : nsel;
+    const int nmed = S.nmed;
+    for (int a = warp; a < nmed; a += nwarps) {
+      const int c = S.med_cols[a];
+      const double m = warp_median(sortbuf + (size_t)c * SP, span, S.nfin[c], S.cmin[c], S.cmax[c], g_sel_hist[warp]);
+      if (lane == 0) S.cmed[c] = m;
     }
-    if (power_sorted) {
-      if (threadIdx.x == 0) S.distinct_power = 0;
-      __syncthreads();
-      const int d = warp_share_distinct(sortbuf + (size_t)C_POWER * SP, S.nfin[C_POWER]);
-      if ((threadIdx.x & 31) == 0 && d) atomicAdd(&S.distinct_power, d);
-      __syncthreads();
+    if (S.distinct_power >= 0) {
+      const int first = nmed < nwarps ? nmed : 0;
+      if (warp >= first) {
+        const double* pw = sortbuf + (size_t)C_POWER * SP;
+        unsigned long long* set = reinterpret_cast<unsigned long long*>(term_p);
+        int added = 0;
+        for (int q = threadIdx.x - first * 32; q < nsel; q += (nwarps - first) * 32)
+          if (pw[q] != inf) added += set_insert(set, 2 * SP, pw[q]);
+        added = __reduce_add_sync(0xffffffffu, added);
+        if (lane == 0 && added) atomicAdd(&S.distinct_power, added);
+      }
     }
   }
+  __syncthreads();
   // ---- energies: stage the energy counter relative to its anchor (its
   // column held a sort exchange buffer) while warps 0-2 find the window's
   // edges in the staged times; form the trapezoid terms in parallel, then
@@ -504,15 +509,15 @@ __device__ __noinline__ void phase_stats_impl(const pm_trials& T, const pm_polic
       const int n = S.nfin[c];
       if (n == 0) return dnan();
       if (S.cmin[c] == S.cmax[c]) return S.cmin[c];
-      return sorted_median(sortbuf + c * SP, n);
+      return S.cmed[c];
     };
     const int ngap = S.nfin[C_GAP];
     po[PM_PO_GAP_MEDIAN_S] = column_median(C_GAP);
     po[PM_PO_GAP_MAX_S] = ngap ? S.cmax[C_GAP] : dnan();
     po[PM_PO_CHANGE_MEDIAN_S] = column_median(C_CHANGE);
     {
-      // A sorted (varying) power column was counted by its warp; otherwise
-      // the column holds one repeated value or none.
+      // A varying power column's distinct values were counted in a hash
+      // set; otherwise the column holds one repeated value or none.
       const int n = S.nfin[C_POWER];
       po[PM_PO_DISTINCT_POWER] = S.distinct_power >= 0 ? S.distinct_power : (n ? 1 : 0);
     }

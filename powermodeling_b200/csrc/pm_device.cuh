@@ -73,187 +73,6 @@ __device__ __forceinline__ void insertion_sort(double* a, int n) {
   }
 }
 
-// CTA-wide ascending bitonic sort of the arrays base + cols[c]*stride
-// (c < ncols), each of length P (a power of two, P <= stride).  +inf pads
-// and marks excluded values so finite values lead.
-__device__ inline void bitonic_sort_columns(double* base, int stride, const int* cols, int ncols, int P) {
-  const int half = P >> 1;
-  const int lg_half = 31 - __clz(half);
-  const int pairs = half * ncols;
-  for (int k = 2; k <= P; k <<= 1) {
-    for (int j = k >> 1; j > 0; j >>= 1) {
-      for (int q = threadIdx.x; q < pairs; q += blockDim.x) {
-        const int a = q >> lg_half, p = q & (half - 1);
-        const int i = ((p & ~(j - 1)) << 1) | (p & (j - 1));
-        double* v = base + (size_t)cols[a] * stride;
-        const bool ascending = (i & k) == 0;
-        const double x = v[i], y = v[i + j];
-        if ((x > y) == ascending) { v[i] = y; v[i + j] = x; }
-      }
-      __syncthreads();
-    }
-  }
-}
-
-// CTA-wide ascending bitonic sort of v[0, P) (P a power of two, at most
-// E * blockDim.x) with the values in registers: thread t holds elements
-// [t*E, t*E + E).  Exchanges at distance j < E stay inside a thread, j < 32*E
-// are warp shuffles, and only j >= 32*E go through `xchg` (P doubles of
-// shared memory) with a CTA barrier, so P = 512 on 256 threads needs 6
-// barrier stages instead of 45.  All threads of the CTA call it.
-// Up to kSortBatch columns sorted together by cta_register_sort_batch.
-constexpr int kSortBatch = 3;
-
-// The compare-exchanges of one bitonic stage between a thread's own
-// elements (distance J < E).
-template <int E, int J>
-__device__ __forceinline__ void register_exchange(double* r, int t, int k) {
-  if (J >= E) return;
-#pragma unroll
-  for (int e = 0; e < E; ++e) {
-    if (e & J) continue;
-    const bool ascending = ((t * E + e) & k) == 0;
-    const double a = r[e], b = r[e | J];
-    if ((a > b) == ascending) { r[e] = b; r[e | J] = a; }
-  }
-}
-
-template <int E>
-__device__ void cta_register_sort(double* v, int P, double* xchg) {
-  const int t = threadIdx.x;
-  double r[E];
-#pragma unroll
-  for (int e = 0; e < E; ++e) r[e] = t * E + e < P ? v[t * E + e] : dinf();
-  for (int k = 2; k <= P; k <<= 1) {
-    for (int j = k >> 1; j > 0; j >>= 1) {
-      if (j < E) {
-        // compile-time distances keep r[] in registers
-        if (j == 1) register_exchange<E, 1>(r, t, k);
-        else if (j == 2) register_exchange<E, 2>(r, t, k);
-        else register_exchange<E, 4>(r, t, k);
-      } else if (j < 32 * E) {
-        const int m = j / E;
-#pragma unroll
-        for (int e = 0; e < E; ++e) {
-          const double other = __shfl_xor_sync(0xffffffffu, r[e], m);
-          const int i = t * E + e;
-          const bool keep_low = ((i & j) == 0) == ((i & k) == 0);
-          const double a = r[e];
-          const double low = a <= other ? a : other, high = a <= other ? other : a;
-          r[e] = keep_low ? low : high;
-        }
-      } else {
-        __syncthreads();
-#pragma unroll
-        for (int e = 0; e < E; ++e)
-          if (t * E + e < P) xchg[t * E + e] = r[e];
-        __syncthreads();
-#pragma unroll
-        for (int e = 0; e < E; ++e) {
-          const int i = t * E + e;
-          if (i >= P) continue;
-          const double other = xchg[i ^ j];
-          const bool keep_low = ((i & j) == 0) == ((i & k) == 0);
-          const double a = r[e];
-          const double low = a <= other ? a : other, high = a <= other ? other : a;
-          r[e] = keep_low ? low : high;
-        }
-      }
-    }
-  }
-  __syncthreads();
-#pragma unroll
-  for (int e = 0; e < E; ++e)
-    if (t * E + e < P) v[t * E + e] = r[e];
-  __syncthreads();
-}
-
-// cta_register_sort on ncols (<= kSortBatch) columns at once: column c is
-// base + cols[c] * stride, its exchange buffer xchg + c * xstride.  The
-// columns' stages interleave, so their shuffle latencies overlap and they
-// share one set of CTA barriers.  All threads of the CTA call it.
-template <int E>
-__device__ __forceinline__ void cta_register_sort_batch(double* base, int stride, const int* cols, int ncols, int P, double* xchg,
-                                        int xstride) {
-  const int t = threadIdx.x;
-  double r[kSortBatch][E];
-#pragma unroll
-  for (int c = 0; c < kSortBatch; ++c)
-#pragma unroll
-    for (int e = 0; e < E; ++e)
-      r[c][e] = (c < ncols && t * E + e < P) ? base[(size_t)cols[c] * stride + t * E + e] : dinf();
-  for (int k = 2; k <= P; k <<= 1) {
-    for (int j = k >> 1; j > 0; j >>= 1) {
-      if (j < E) {
-#pragma unroll
-        for (int c = 0; c < kSortBatch; ++c) {
-          if (c >= ncols) continue;
-          if (j == 1) register_exchange<E, 1>(r[c], t, k);
-          else if (j == 2) register_exchange<E, 2>(r[c], t, k);
-          else register_exchange<E, 4>(r[c], t, k);
-        }
-      } else if (j < 32 * E) {
-        const int m = j / E;
-#pragma unroll
-        for (int c = 0; c < kSortBatch; ++c) {
-          if (c >= ncols) continue;
-#pragma unroll
-          for (int e = 0; e < E; ++e) {
-            const double other = __shfl_xor_sync(0xffffffffu, r[c][e], m);
-            const int i = t * E + e;
-            const bool keep_low = ((i & j) == 0) == ((i & k) == 0);
-            const double a = r[c][e];
-            const double low = a <= other ? a : other, high = a <= other ? other : a;
-            r[c][e] = keep_low ? low : high;
-          }
-        }
-      } else {
-        __syncthreads();
-#pragma unroll
-        for (int c = 0; c < kSortBatch; ++c) {
-          if (c >= ncols) continue;
-#pragma unroll
-          for (int e = 0; e < E; ++e)
-            if (t * E + e < P) xchg[(size_t)c * xstride + t * E + e] = r[c][e];
-        }
-        __syncthreads();
-#pragma unroll
-        for (int c = 0; c < kSortBatch; ++c) {
-          if (c >= ncols) continue;
-#pragma unroll
-          for (int e = 0; e < E; ++e) {
-            const int i = t * E + e;
-            if (i >= P) continue;
-            const double other = xchg[(size_t)c * xstride + (i ^ j)];
-            const bool keep_low = ((i & j) == 0) == ((i & k) == 0);
-            const double a = r[c][e];
-            const double low = a <= other ? a : other, high = a <= other ? other : a;
-            r[c][e] = keep_low ? low : high;
-          }
-        }
-      }
-    }
-  }
-  __syncthreads();
-#pragma unroll
-  for (int c = 0; c < kSortBatch; ++c) {
-    if (c >= ncols) continue;
-#pragma unroll
-    for (int e = 0; e < E; ++e)
-      if (t * E + e < P) base[(size_t)cols[c] * stride + t * E + e] = r[c][e];
-  }
-  __syncthreads();
-}
-
-// This thread's share of the distinct values in the sorted prefix v[0, n),
-// summed over its warp (every lane returns the warp's count).
-__device__ inline int warp_share_distinct(const double* v, int n) {
-  int d = 0;
-  for (int i = threadIdx.x; i < n; i += blockDim.x) d += (i == 0 || v[i] != v[i - 1]);
-  for (int o = 16; o; o >>= 1) d += __shfl_xor_sync(0xffffffffu, d, o);
-  return d;
-}
-
 // lower_bound (strict = false: first t[i] >= x) or upper_bound (strict =
 // true: first t[i] > x) over the sorted t[b, e), by one warp: each round
 // probes 32 evenly spaced positions at once, so a segment of n samples takes
@@ -279,6 +98,161 @@ __device__ inline int64_t warp_bound(const double* t, int64_t b, int64_t e, doub
   const bool past = probe < hi && (strict ? t[probe] > x : t[probe] >= x);
   const unsigned m = __ballot_sync(0xffffffffu, past);
   return m ? lo + (__ffs(m) - 1) : hi;
+}
+
+// Key of a non-NaN double whose unsigned order is the values' order (the
+// sign bit flipped for positives, every bit for negatives), and back.
+__device__ __forceinline__ uint64_t order_key(double v) {
+  const uint64_t b = (uint64_t)__double_as_longlong(v);
+  return (b >> 63) ? ~b : (b | 0x8000000000000000ull);
+}
+__device__ __forceinline__ double key_value(uint64_t k) {
+  return __longlong_as_double((long long)((k >> 63) ? (k & 0x7fffffffffffffffull) : ~k));
+}
+
+// statistics.median of the n finite values of col[0, span) (+inf marks "no
+// value"), whose minimum and maximum (cmin < cmax) are known, by one warp.
+// Order statistic (n-1)/2 comes from an MSD radix select over the order
+// keys, eight bits a pass from the first bit in which cmin and cmax differ
+// (every value shares the bits above it), until its bin holds at most 64
+// values; those are gathered and ranked by counting, which also gives
+// order statistic n/2 unless that one lies past the bin.  Loads are issued
+// four at a time ahead of the shared-memory updates they feed.  `hist` is
+// 256 words (8-byte aligned) of this warp's shared memory.  All lanes
+// return it.
+__device__ inline double warp_median(const double* col, int span, int n, double cmin, double cmax, uint32_t* hist) {
+  const int lane = threadIdx.x & 31;
+  const double inf = dinf();
+  const uint64_t kmin = order_key(cmin), kmax = order_key(cmax);
+  int shift = ((63 - __clzll((long long)(kmin ^ kmax))) >> 3) << 3;   // digit bits [shift, shift + 8)
+  uint64_t prefix = kmin;                                             // bits above the digit are final
+  int k = (n - 1) / 2;
+  const int rounds = (span + 31) >> 5;
+  auto load4 = [&](int r0, double* v) {
+#pragma unroll
+    for (int u = 0; u < 4; ++u) {
+      const int q = ((r0 + u) << 5) + lane;
+      v[u] = q < span ? col[q] : inf;
+    }
+  };
+  uint32_t count = 0;
+  for (;;) {
+    const uint64_t above = shift >= 56 ? 0ull : ~0ull << (shift + 8);
+    for (int i = lane; i < 256; i += 32) hist[i] = 0;
+    __syncwarp();
+    for (int r0 = 0; r0 < rounds; r0 += 4) {
+      double v[4];
+      load4(r0, v);
+#pragma unroll
+      for (int u = 0; u < 4; ++u) {
+        const uint64_t key = order_key(v[u]);
+        if (v[u] != inf && ((key ^ prefix) & above) == 0) atomicAdd(&hist[(unsigned)(key >> shift) & 0xffu], 1u);
+      }
+    }
+    __syncwarp();
+    // the bin holding rank k: each lane owns eight consecutive bins
+    uint32_t c[8], own = 0;
+#pragma unroll
+    for (int j = 0; j < 8; ++j) { c[j] = hist[lane * 8 + j]; own += c[j]; }
+    uint32_t incl = own;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+      const uint32_t x = __shfl_up_sync(0xffffffffu, incl, o);
+      if (lane >= o) incl += x;
+    }
+    const uint32_t excl = incl - own;
+    const unsigned holder = __ballot_sync(0xffffffffu, excl <= (uint32_t)k && (uint32_t)k < incl);
+    const int src = __ffs(holder) - 1;
+    uint32_t below = excl, bin = 0;
+    count = 0;
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+      if (count == 0 && (uint32_t)k < below + c[j]) { bin = (uint32_t)(lane * 8 + j); count = c[j]; }
+      else if (count == 0) below += c[j];
+    }
+    bin = __shfl_sync(0xffffffffu, bin, src);
+    below = __shfl_sync(0xffffffffu, below, src);
+    count = __shfl_sync(0xffffffffu, count, src);
+    __syncwarp();                                  // every lane has read hist before it is reused
+    prefix = (prefix & above) | ((uint64_t)bin << shift);
+    k -= (int)below;
+    if (count <= 64 || shift == 0) break;
+    shift -= 8;
+  }
+  double a, b = inf;
+  bool have_b = (n & 1) != 0;                      // odd n: order statistic n/2 is a
+  if (count <= 64) {
+    // gather the bin (every bit >= shift equals the prefix), then rank each
+    // gathered value by counting the smaller and equal ones
+    double* buf = reinterpret_cast<double*>(hist);
+    const uint64_t mask = ~0ull << shift;
+    uint32_t base = 0;
+    for (int r0 = 0; r0 < rounds; r0 += 4) {
+      double v[4];
+      load4(r0, v);
+#pragma unroll
+      for (int u = 0; u < 4; ++u) {
+        const bool in = v[u] != inf && ((order_key(v[u]) ^ prefix) & mask) == 0;
+        const unsigned ballot = __ballot_sync(0xffffffffu, in);
+        if (in) buf[base + __popc(ballot & ((1u << lane) - 1u))] = v[u];
+        base += __popc(ballot);
+      }
+    }
+    __syncwarp();
+    const double x0 = lane < (int)count ? buf[lane] : inf;
+    const double x1 = lane + 32 < (int)count ? buf[lane + 32] : inf;
+    int less0 = 0, eq0 = 0, less1 = 0, eq1 = 0;
+#pragma unroll 4
+    for (int i = 0; i < (int)count; ++i) {
+      const double y = buf[i];
+      less0 += y < x0; eq0 += y == x0;
+      less1 += y < x1; eq1 += y == x1;
+    }
+    __syncwarp();
+    auto pick = [&](int r, double* out) -> bool {
+      const bool h0 = lane < (int)count && less0 <= r && r < less0 + eq0;
+      const bool h1 = lane + 32 < (int)count && less1 <= r && r < less1 + eq1;
+      const unsigned m0 = __ballot_sync(0xffffffffu, h0), m1 = __ballot_sync(0xffffffffu, h1);
+      if (!(m0 | m1)) return false;
+      *out = m0 ? __shfl_sync(0xffffffffu, x0, __ffs(m0) - 1) : __shfl_sync(0xffffffffu, x1, __ffs(m1) - 1);
+      return true;
+    };
+    pick(k, &a);
+    if (have_b) b = a;
+    else have_b = pick(k + 1, &b);
+  } else {
+    a = key_value(prefix);                         // all 64 bits fixed: every value in the bin equals it
+    if (have_b) b = a;
+    else if (k + 1 < (int)count) { b = a; have_b = true; }
+  }
+  if (!have_b) {
+    // order statistic n/2 is the least value above the bin, which ends at a
+    for (int r0 = 0; r0 < rounds; r0 += 4) {
+      double v[4];
+      load4(r0, v);
+#pragma unroll
+      for (int u = 0; u < 4; ++u)
+        if (v[u] > a && v[u] < b) b = v[u];
+    }
+    for (int o = 16; o; o >>= 1) b = fmin(b, __shfl_xor_sync(0xffffffffu, b, o));
+  }
+  return (n & 1) ? a : (a + b) / 2;
+}
+
+// Insert the bits of finite v (-0.0 as +0.0: equal values share a slot) into
+// an open-addressing set of `slots` (a power of two, more than the values
+// inserted) 64-bit words cleared to kSetEmpty; true if v was not there yet.
+constexpr unsigned long long kSetEmpty = ~0ull;   // a NaN pattern: never a finite value's bits
+__device__ __forceinline__ bool set_insert(unsigned long long* set, int slots, double v) {
+  const unsigned long long bits = v == 0.0 ? 0ull : (unsigned long long)__double_as_longlong(v);
+  unsigned h = (unsigned)((bits * 0x9E3779B97F4A7C15ull) >> 32) & (unsigned)(slots - 1);
+  for (int probe = 0; probe < slots; ++probe) {
+    const unsigned long long old = atomicCAS(set + h, kSetEmpty, bits);
+    if (old == kSetEmpty) return true;
+    if (old == bits) return false;
+    h = (h + 1) & (unsigned)(slots - 1);
+  }
+  return false;
 }
 
 }  // namespace pm
