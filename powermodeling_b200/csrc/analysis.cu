@@ -25,7 +25,8 @@ constexpr int kThreads = 256;
 constexpr int kMaxEpochs = 256;        // per arm; the host rejects longer lists
 enum Col { C_GAP = 0, C_CHANGE, C_POWER, C_GFX, C_SM, C_MEM, C_TEMP, C_PLIMIT, C_ENF, C_PSTATE, C_COUNT };
 // Staged covering samples that follow the sample columns in the tile.
-enum Stage { S_T = 0, S_POWER, S_MEMORY, S_REL, S_TERM_P, S_TERM_M, S_COUNT };
+// S_SET0/S_SET1: the distinct-power hash set (2 x SP 64-bit slots).
+enum Stage { S_T = 0, S_POWER, S_MEMORY, S_REL, S_TERM_P, S_TERM_M, S_SET0, S_SET1, S_COUNT };
 constexpr int kTileColumns = C_COUNT + S_COUNT;
 static_assert(kTileColumns == kSortColumns, "tile column count");
 
@@ -278,6 +279,7 @@ __device__ __noinline__ void phase_stats_impl(const pm_trials& T, const pm_polic
   double* st_r = sortbuf + (size_t)(C_COUNT + S_REL) * SP;
   double* term_p = sortbuf + (size_t)(C_COUNT + S_TERM_P) * SP;
   double* term_m = sortbuf + (size_t)(C_COUNT + S_TERM_M) * SP;
+  unsigned long long* pset = reinterpret_cast<unsigned long long*>(sortbuf + (size_t)(C_COUNT + S_SET0) * SP);
   // ---- reductions over the selected samples.
   // Each staged column (finite values, +inf for None) is reduced by one warp:
   // finite count, minimum and maximum.  The flags of the staged clock,
@@ -342,8 +344,8 @@ __device__ __noinline__ void phase_stats_impl(const pm_trials& T, const pm_polic
     __shared__ uint32_t red_flags, red_thr_lo, red_thr_hi, red_src;
     __shared__ int red_neg;
     if (threadIdx.x == 0) { red_flags = 0; red_thr_lo = red_thr_hi = 0; red_src = 0; red_neg = 0; S.anchor_q = 0x7fffffff; }
-    // the distinct-power set (two free columns of the tile) starts empty
-    for (int q = threadIdx.x; q < 2 * SP; q += blockDim.x) reinterpret_cast<unsigned long long*>(term_p)[q] = kSetEmpty;
+    // the distinct-power set starts empty
+    for (int q = threadIdx.x; q < 2 * SP; q += blockDim.x) pset[q] = kSetEmpty;
     __syncthreads();
     if (lane == 0) {
       if (anchor_q != 0x7fffffffu) atomicMin(&S.anchor_q, (int)anchor_q);
@@ -381,37 +383,9 @@ __device__ __noinline__ void phase_stats_impl(const pm_trials& T, const pm_polic
     }
   }
   __syncthreads();
-  // ---- medians of the varying columns, distinct finite powers.
-  // A median needs order statistics (n-1)/2 and n/2 only: one warp selects
-  // them per column (warp_median); the warps without a column fill the
-  // distinct-power set (all warps when every warp has a column).
-  {
-    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, nwarps = blockDim.x >> 5;
-    const int span = ncov > nsel ? ncov : nsel;
-    const int nmed = S.nmed;
-    for (int a = warp; a < nmed; a += nwarps) {
-      const int c = S.med_cols[a];
-      const double m = warp_median(sortbuf + (size_t)c * SP, span, S.nfin[c], S.cmin[c], S.cmax[c], g_sel_hist[warp]);
-      if (lane == 0) S.cmed[c] = m;
-    }
-    if (S.distinct_power >= 0) {
-      const int first = nmed < nwarps ? nmed : 0;
-      if (warp >= first) {
-        const double* pw = sortbuf + (size_t)C_POWER * SP;
-        unsigned long long* set = reinterpret_cast<unsigned long long*>(term_p);
-        int added = 0;
-        for (int q = threadIdx.x - first * 32; q < nsel; q += (nwarps - first) * 32)
-          if (pw[q] != inf) added += set_insert(set, 2 * SP, pw[q]);
-        added = __reduce_add_sync(0xffffffffu, added);
-        if (lane == 0 && added) atomicAdd(&S.distinct_power, added);
-      }
-    }
-  }
-  __syncthreads();
-  // ---- energies: stage the energy counter relative to its anchor (its
-  // column held a sort exchange buffer) while warps 0-2 find the window's
-  // edges in the staged times; form the trapezoid terms in parallel, then
-  // accumulate each sum on one lane in the reference's order.
+  // ---- energies: stage the energy counter relative to its anchor while
+  // warps 0-2 find the window's edges in the staged times; form the
+  // trapezoid terms in parallel; the sums follow, beside the medians.
   __shared__ int s_edge[3];   // upper_bound(start), lower_bound(start), lower_bound(end) over st_t
   __shared__ int s_gap;
   if (threadIdx.x < 96) {
@@ -465,36 +439,59 @@ __device__ __noinline__ void phase_stats_impl(const pm_trials& T, const pm_polic
   __syncthreads();
   gap_p = (s_gap & 1) != 0;
   gap_m = (s_gap & 2) != 0;
-  if (threadIdx.x == 0) {
-    double energy = dnan();
-    if (!none(p0) && !none(p1) && end > start && !gap_p) {
-      energy = neumaier_sum(term_p, nterms);
+  // ---- side by side, all independent of one another: each energy sum on
+  // one lane (lane 0 of the last three warps) in the reference's order; the
+  // median of each varying column by one warp from warp 0 (warp_median: a
+  // median needs order statistics (n-1)/2 and n/2 only); the distinct
+  // finite powers into a hash set by the warps from the first one without a
+  // column (at most the last three).
+  {
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, nwarps = blockDim.x >> 5;
+    if (lane == 0 && warp == nwarps - 1) {
+      double energy = dnan();
+      if (!none(p0) && !none(p1) && end > start && !gap_p) energy = neumaier_sum(term_p, nterms);
+      po[PM_PO_ENERGY_J] = energy;
+      po[PM_PO_INTEGRATED_POWER_W] = none(energy) ? dnan() : energy / duration;
+    } else if (lane == 0 && warp == nwarps - 2) {
+      double me = dnan();
+      if (!none(m0) && !none(m1) && end > start && !gap_m) me = neumaier_sum(term_m, nterms);
+      po[PM_PO_MEMORY_ENERGY_J] = me;
+      po[PM_PO_MEMORY_POWER_W] = none(me) ? dnan() : me / duration;
+    } else if (lane == 0 && warp == nwarps - 3) {
+      const double c0 = value_at(st_r, start, lb_start), c1 = value_at(st_r, end, ib);
+      bool reset = false, have = false;
+      double prev = 0.0;
+      for (int q = 0; q < ncov; ++q) {
+        const double v = st_r[q];
+        if (none(v)) continue;
+        if (have && v < prev) reset = true;
+        prev = v; have = true;
+      }
+      double counter = dnan();
+      if (!none(c0) && !none(c1)) {
+        if (reset || c1 < c0) atomicOr(&S.pf[p], 1u << PM_PF_COUNTER_RESET);
+        else counter = (c1 - c0) / 1000.0;
+      }
+      po[PM_PO_COUNTER_J] = counter;
     }
-    po[PM_PO_ENERGY_J] = energy;
-    po[PM_PO_INTEGRATED_POWER_W] = none(energy) ? dnan() : energy / duration;
-  } else if (threadIdx.x == 32) {
-    double me = dnan();
-    if (!none(m0) && !none(m1) && end > start && !gap_m) {
-      me = neumaier_sum(term_m, nterms);
+    const int span = ncov > nsel ? ncov : nsel;
+    const int nmed = S.nmed;
+    for (int a = warp; a < nmed; a += nwarps) {
+      const int c = S.med_cols[a];
+      const double m = warp_median(sortbuf + (size_t)c * SP, span, S.nfin[c], S.cmin[c], S.cmax[c], g_sel_hist[warp]);
+      if (lane == 0) S.cmed[c] = m;
     }
-    po[PM_PO_MEMORY_ENERGY_J] = me;
-    po[PM_PO_MEMORY_POWER_W] = none(me) ? dnan() : me / duration;
-  } else if (threadIdx.x == 64) {
-    const double c0 = value_at(st_r, start, lb_start), c1 = value_at(st_r, end, ib);
-    bool reset = false, have = false;
-    double prev = 0.0;
-    for (int q = 0; q < ncov; ++q) {
-      const double v = st_r[q];
-      if (none(v)) continue;
-      if (have && v < prev) reset = true;
-      prev = v; have = true;
+    if (S.distinct_power >= 0) {
+      const int first = nmed < nwarps - 3 ? nmed : nwarps - 3;
+      if (warp >= first) {
+        const double* pw = sortbuf + (size_t)C_POWER * SP;
+        int added = 0;
+        for (int q = threadIdx.x - first * 32; q < nsel; q += (nwarps - first) * 32)
+          if (pw[q] != inf) added += set_insert(pset, 2 * SP, pw[q]);
+        added = __reduce_add_sync(0xffffffffu, added);
+        if (lane == 0 && added) atomicAdd(&S.distinct_power, added);
+      }
     }
-    double counter = dnan();
-    if (!none(c0) && !none(c1)) {
-      if (reset || c1 < c0) S.pf[p] |= 1u << PM_PF_COUNTER_RESET;
-      else counter = (c1 - c0) / 1000.0;
-    }
-    po[PM_PO_COUNTER_J] = counter;
   }
   __syncthreads();
   if (threadIdx.x == 0) {

@@ -13,7 +13,7 @@ constexpr int kMaxPhaseSamples = 1 << 24;   // samples in one (trial, phase) seg
 constexpr int kMaxEpochsPerArm = 256;
 constexpr int kMaxGroupMembers = 128;       // bootstrap rows per group
 constexpr int kMaxMetrics = 256;
-constexpr int kSortColumns = 16;            // per-phase tile: 10 sample columns + 6 staged columns
+constexpr int kSortColumns = 18;            // per-phase tile: 10 sample columns + 8 staged columns
 constexpr size_t kSmemSortBytes = 160 * 1024;
 
 // Arguments of the group bootstrap kernel.
