@@ -407,13 +407,25 @@ int stage_trials(Arena& A, const pm_trials& T, size_t extra_dev, size_t extra_ho
   return copy_trials(A, T, S);
 }
 
+// Copy the pinned results into the caller's arrays (those not NULL), in
+// 64 KiB pieces shared by the host pool and this thread.
 void copy_results_out(const StagedTrials& S, size_t n, pm_trial_results* out) {
-  if (out->phase_out) memcpy(out->phase_out, S.hres.phase_out, n * PM_PHASES * PM_PO_COUNT * sizeof(double));
-  if (out->phase_flags) memcpy(out->phase_flags, S.hres.phase_flags, n * PM_PHASES * sizeof(uint32_t));
-  if (out->trial_out) memcpy(out->trial_out, S.hres.trial_out, n * PM_TO_COUNT * sizeof(double));
-  if (out->issue_bits) memcpy(out->issue_bits, S.hres.issue_bits, n * PM_ISSUE_WORDS * sizeof(uint64_t));
-  if (out->metrics) memcpy(out->metrics, S.hres.metrics, n * PM_N_METRICS * sizeof(double));
-  if (out->valid) memcpy(out->valid, S.hres.valid, n);
+  struct Piece { char* dst; const char* src; size_t bytes; };
+  std::vector<Piece> pieces;
+  auto add = [&](void* dst, const void* src, size_t bytes) {
+    constexpr size_t kPiece = size_t(64) << 10;
+    if (!dst) return;
+    for (size_t o = 0; o < bytes; o += kPiece)
+      pieces.push_back({static_cast<char*>(dst) + o, static_cast<const char*>(src) + o, std::min(kPiece, bytes - o)});
+  };
+  add(out->phase_out, S.hres.phase_out, n * PM_PHASES * PM_PO_COUNT * sizeof(double));
+  add(out->phase_flags, S.hres.phase_flags, n * PM_PHASES * sizeof(uint32_t));
+  add(out->trial_out, S.hres.trial_out, n * PM_TO_COUNT * sizeof(double));
+  add(out->issue_bits, S.hres.issue_bits, n * PM_ISSUE_WORDS * sizeof(uint64_t));
+  add(out->metrics, S.hres.metrics, n * PM_N_METRICS * sizeof(double));
+  add(out->valid, S.hres.valid, n);
+  HostBatch batch(pieces.size(), [&](size_t i) { memcpy(pieces[i].dst, pieces[i].src, pieces[i].bytes); });
+  run_host_batch(batch, nullptr);
 }
 
 }  // namespace

@@ -1,10 +1,14 @@
 #include "host_pool.h"
 
+#include <chrono>
 #include <condition_variable>
 #include <cstdlib>
 #include <mutex>
 #include <thread>
 #include <vector>
+#if defined(__x86_64__)
+#include <immintrin.h>
+#endif
 
 namespace pm {
 
@@ -28,15 +32,34 @@ size_t drain(HostBatch& b) {
   }
 }
 
+// How long a worker keeps polling for the next batch before it sleeps:
+// back-to-back calls then start without a thread wake-up.
+// PM_HOST_SPIN_US overrides the default.
+int spin_microseconds() {
+  if (const char* env = std::getenv("PM_HOST_SPIN_US")) {
+    const int v = std::atoi(env);
+    return v < 0 ? 0 : v > 100000 ? 100000 : v;
+  }
+  return 500;
+}
+
+inline void cpu_relax() {
+#if defined(__x86_64__)
+  _mm_pause();
+#else
+  std::this_thread::yield();
+#endif
+}
+
 class Pool {
  public:
-  explicit Pool(int threads) {
+  explicit Pool(int threads) : spin_(std::chrono::microseconds(spin_microseconds())) {
     for (int t = 0; t < threads; ++t) workers_.emplace_back([this] { loop(); });
   }
   ~Pool() {
     {
       std::lock_guard<std::mutex> g(m_);
-      quit_ = true;
+      quit_.store(true, std::memory_order_relaxed);
     }
     cv_.notify_all();
     for (auto& w : workers_) w.join();
@@ -48,7 +71,7 @@ class Pool {
     {
       std::lock_guard<std::mutex> g(m_);
       batch_ = &b;
-      ++generation_;
+      generation_.fetch_add(1, std::memory_order_release);
     }
     cv_.notify_all();
     for (;;) {
@@ -73,12 +96,17 @@ class Pool {
   void loop() {
     uint64_t seen = 0;
     for (;;) {
+      // poll for a while before blocking (the lock and the condition decide)
+      const auto until = std::chrono::steady_clock::now() + spin_;
+      while (generation_.load(std::memory_order_acquire) == seen && !quit_.load(std::memory_order_relaxed) &&
+             std::chrono::steady_clock::now() < until)
+        cpu_relax();
       HostBatch* b = nullptr;
       {
         std::unique_lock<std::mutex> g(m_);
-        cv_.wait(g, [&] { return quit_ || (generation_ != seen && batch_ != nullptr); });
-        if (quit_) return;
-        seen = generation_;
+        cv_.wait(g, [&] { return quit_.load(std::memory_order_relaxed) || (generation_.load(std::memory_order_relaxed) != seen && batch_ != nullptr); });
+        if (quit_.load(std::memory_order_relaxed)) return;
+        seen = generation_.load(std::memory_order_relaxed);
         b = batch_;
         ++inside_;
       }
@@ -95,9 +123,10 @@ class Pool {
   std::mutex m_, run_lock_;
   std::condition_variable cv_, idle_cv_;
   HostBatch* batch_ = nullptr;
-  uint64_t generation_ = 0;
+  std::atomic<uint64_t> generation_{0};
   int inside_ = 0;
-  bool quit_ = false;
+  std::atomic<bool> quit_{false};
+  const std::chrono::microseconds spin_;
 };
 
 int configured_threads() {
