@@ -17,12 +17,19 @@ __device__ __forceinline__ double dinf() { return __longlong_as_double(0x7ff0000
 // CPython 3.12's float sum(): Neumaier's compensated summation (Neumaier
 // 1974) from 0.0 (the int 0 start, converted) over every term, with the
 // compensation added once at the end when it is nonzero and finite.  The
-// step is branch-free so a long sum pipelines on its one dependent add.
+// step is branch-free: the operand of larger magnitude (|f| >= |x| picks f)
+// is chosen by an integer compare of the bit patterns without their sign
+// bits, which orders magnitudes as the float compare does, so each term
+// costs four double adds, (big - t) + small being Neumaier's branch taken.
 struct NeumaierSum {
   double f = 0.0, c = 0.0;
   __device__ __forceinline__ void add(double x) {
     const double t = f + x;
-    c += fabs(f) >= fabs(x) ? (f - t) + x : (x - t) + f;
+    const unsigned long long mf = (unsigned long long)__double_as_longlong(f) & 0x7fffffffffffffffull;
+    const unsigned long long mx = (unsigned long long)__double_as_longlong(x) & 0x7fffffffffffffffull;
+    const bool f_big = mf >= mx;
+    const double big = f_big ? f : x, small = f_big ? x : f;
+    c += (big - t) + small;
     f = t;
   }
   __device__ __forceinline__ double result() const {
