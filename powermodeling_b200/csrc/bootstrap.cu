@@ -308,13 +308,26 @@ __global__ void __launch_bounds__(kBootThreads) bootstrap_kernel(BootArgs A) {
   const BootSmem L(M, A.max_members, A.max_members > kHistMaxN);
   double* vals = reinterpret_cast<double*>(dsm + L.vals);
   int* cnt = reinterpret_cast<int*>(dsm + L.cnt);
+  // The group's rows (-1: not valid) first, so each metric's value loads are
+  // independent of one another.
+  __shared__ int s_rows[kDirectMaxN];
+  for (int i = threadIdx.x; i < members; i += blockDim.x) {
+    const int row = A.member_rows ? A.member_rows[m0 + i] : m0 + i;
+    s_rows[i] = (A.member_valid && !A.member_valid[row]) ? -1 : row;
+  }
+  __syncthreads();
   for (int m = threadIdx.x; m < M; m += blockDim.x) {
     int c = 0;
-    for (int i = 0; i < members; ++i) {
-      const int row = A.member_rows ? A.member_rows[m0 + i] : m0 + i;
-      if (A.member_valid && !A.member_valid[row]) continue;
-      const double v = A.values[(size_t)row * M + m];
-      if (!none(v)) vals[m * A.max_members + c++] = v;
+    for (int i0 = 0; i0 < members; i0 += 4) {
+      double v[4];
+#pragma unroll
+      for (int u = 0; u < 4; ++u) {
+        const int row = i0 + u < members ? s_rows[i0 + u] : -1;
+        v[u] = row >= 0 ? A.values[(size_t)row * M + m] : dnan();
+      }
+#pragma unroll
+      for (int u = 0; u < 4; ++u)
+        if (!none(v[u])) vals[m * A.max_members + c++] = v[u];
     }
     cnt[m] = c;
     double tmp[64];
@@ -399,8 +412,10 @@ __global__ void __launch_bounds__(kBootThreads) bootstrap_kernel(BootArgs A) {
       for (int i = threadIdx.x; i < M * n * n; i += blockDim.x) fpairs[(i / (n * n)) * kHistMaxN * kHistMaxN + i % (n * n)] = 0;
       __syncthreads();
       const int pa = (n & 1) ? n / 2 : n / 2 - 1, pb = n / 2;
+      // bin-major: the lanes of a warp take different metrics, so their
+      // pair-count atomics rarely meet
       for (int it = threadIdx.x; it < M * nbins; it += blockDim.x) {
-        const int m = it / nbins, bin = it - m * nbins;
+        const int bin = it / M, m = it - bin * M;
         const uint32_t h = hist[bin];
         if (!h || cnt[m] != n) continue;
         const uint8_t* c = bcounts + bin * kHistMaxN;
@@ -649,11 +664,25 @@ size_t bootstrap_scratch_bytes(int n_groups, int max_members, int resamples) {
 // bytes needed (written to *available the bytes the device offers).
 size_t bootstrap_smem_shortfall(int M, int mm, size_t* available) {
   const size_t dyn = BootSmem(M, mm, mm > kHistMaxN).total;
-  cudaFuncAttributes attr{};
-  const size_t static_bytes = cudaFuncGetAttributes(&attr, bootstrap_kernel) == cudaSuccess ? attr.sharedSizeBytes : 0;
+  // Both queries are answered once (per process, per device): they sit on
+  // every bootstrap call's host path.
+  static const size_t static_bytes = [] {
+    cudaFuncAttributes attr{};
+    const size_t b = cudaFuncGetAttributes(&attr, bootstrap_kernel) == cudaSuccess ? attr.sharedSizeBytes : 0;
+    cudaGetLastError();   // a failed query must not surface as a later launch error
+    return b;
+  }();
+  static std::atomic<int> optin_of[kMaxDevices];
   int dev = 0, optin = 48 * 1024;
-  if (cudaGetDevice(&dev) == cudaSuccess) cudaDeviceGetAttribute(&optin, cudaDevAttrMaxSharedMemoryPerBlockOptin, dev);
-  cudaGetLastError();   // a failed query must not surface as a later launch error
+  if (cudaGetDevice(&dev) == cudaSuccess && dev >= 0 && dev < kMaxDevices) {
+    optin = optin_of[dev].load(std::memory_order_relaxed);
+    if (optin == 0) {
+      optin = 48 * 1024;
+      if (cudaDeviceGetAttribute(&optin, cudaDevAttrMaxSharedMemoryPerBlockOptin, dev) == cudaSuccess)
+        optin_of[dev].store(optin, std::memory_order_relaxed);
+    }
+  }
+  cudaGetLastError();
   if (available) *available = (size_t)optin;
   return static_bytes + dyn <= (size_t)optin ? 0 : static_bytes + dyn;
 }
