@@ -361,9 +361,27 @@ __global__ void __launch_bounds__(kBootThreads) bootstrap_kernel(BootArgs A) {
   // stream must be consumed before another count reuses the group's area),
   // then every other count in ascending order.
   bool seeded = !A.prepared;
-  for (int step = 0; step <= kDirectMaxN; ++step) {
-    const int n = step == 0 ? members : (step == members ? 0 : step);
-    if (n < 3 || n > kDirectMaxN || !((n_mask[n >> 5] >> (n & 31)) & 1u)) continue;   // uniform: shared mask
+  // The counts present come from the shared mask (read after a barrier, so
+  // every thread walks the same list): the member count, then its set bits
+  // in ascending order.
+  constexpr int kMaskWords = (kDirectMaxN + 1 + 31) / 32;
+  uint32_t rest[kMaskWords];
+#pragma unroll
+  for (int w = 0; w < kMaskWords; ++w) rest[w] = n_mask[w];
+  bool member_count_first = members >= 3 && members <= kDirectMaxN && ((rest[members >> 5] >> (members & 31)) & 1u);
+  if (member_count_first) rest[members >> 5] &= ~(1u << (members & 31));
+  for (;;) {
+    int n = -1;
+    if (member_count_first) {
+      n = members;
+      member_count_first = false;
+    } else {
+#pragma unroll
+      for (int w = 0; w < kMaskWords; ++w)
+        if (n < 0 && rest[w]) { n = w * 32 + __ffs(rest[w]) - 1; rest[w] &= rest[w] - 1; }
+      if (n < 0) break;
+    }
+    if (n < 3) continue;                                   // counts below 3 carry no interval
     const bool histogram = n <= kHistMaxN;
     const int nbins = histogram ? (int)sh.binom[2 * n - 1][n] : 0;
     uint8_t* stream = index_stream(A, g);
