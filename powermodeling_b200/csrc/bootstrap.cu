@@ -430,21 +430,41 @@ __global__ void __launch_bounds__(kBootThreads) bootstrap_kernel(BootArgs A) {
       for (int i = threadIdx.x; i < M * n * n; i += blockDim.x) fpairs[(i / (n * n)) * kHistMaxN * kHistMaxN + i % (n * n)] = 0;
       __syncthreads();
       const int pa = (n & 1) ? n / 2 : n / 2 - 1, pb = n / 2;
-      // bin-major: the lanes of a warp take different metrics, so their
-      // pair-count atomics rarely meet
-      for (int it = threadIdx.x; it < M * nbins; it += blockDim.x) {
-        const int bin = it / M, m = it - bin * M;
-        const uint32_t h = hist[bin];
-        if (!h || cnt[m] != n) continue;
-        const uint8_t* c = bcounts + bin * kHistMaxN;
-        const uint8_t* idx = findex + m * kHistMaxN;
-        int seen = 0, ra = -1, rb = -1;
-        for (int r = 0; r < n && rb < 0; ++r) {
-          seen += c[idx[r]];
-          if (ra < 0 && pa < seen) ra = r;
-          if (pb < seen) rb = r;
+      // Each thread takes a run of consecutive (metric, bin) items, metric
+      // major: mostly the bins of one metric, whose rank-to-member map it
+      // holds in registers; a metric's items fall to a few threads only.
+      {
+        const int items = M * nbins;
+        const int per = (items + (int)blockDim.x - 1) / (int)blockDim.x;
+        const int i0 = (int)threadIdx.x * per, i1 = min(items, i0 + per);
+        int m = i0 / nbins, bin = i0 - m * nbins, cur = -1;
+        bool live = false;
+        int id[kHistMaxN];
+        uint32_t* pt = fpairs;
+        for (int it = i0; it < i1; ++it) {
+          if (m != cur) {
+            cur = m;
+            live = cnt[m] == n;
+#pragma unroll
+            for (int r = 0; r < kHistMaxN; ++r) id[r] = r < n ? findex[m * kHistMaxN + r] : 0;
+            pt = fpairs + m * kHistMaxN * kHistMaxN;
+          }
+          const uint32_t h = live ? hist[bin] : 0u;
+          if (h) {
+            const uint8_t* c = bcounts + bin * kHistMaxN;
+            int seen = 0, ra = -1, rb = -1;
+#pragma unroll
+            for (int r = 0; r < kHistMaxN; ++r) {
+              if (r < n && rb < 0) {
+                seen += c[id[r]];
+                if (ra < 0 && pa < seen) ra = r;
+                if (pb < seen) rb = r;
+              }
+            }
+            atomicAdd(&pt[ra * n + rb], h);
+          }
+          if (++bin == nbins) { bin = 0; ++m; }
         }
-        atomicAdd(&fpairs[m * kHistMaxN * kHistMaxN + ra * n + rb], h);
       }
       __syncthreads();
       // Per metric: the pair values in ascending order with their counts, then
