@@ -328,7 +328,10 @@ int copy_trials(Arena& A, const pm_trials& T, StagedTrials& S) {
   S.dev.max_phase_samples = S.max_cov;
   // Copy pieces of at most kPiece bytes in destination order, then the
   // sample-order scan in slot ranges; pool threads and this thread share them.
-  constexpr size_t kPiece = size_t(1) << 20, kDmaMin = size_t(1) << 20;
+  // Small pieces make the staged prefix grow steadily, so its DMA (issued a
+  // kDma chunk at a time: on B200 1 MiB copies reach 43 GB/s where one 3.4 MB
+  // copy reached 20) runs alongside the staging instead of after it.
+  constexpr size_t kPiece = size_t(128) << 10, kDma = size_t(1) << 20;
   struct Piece { const char* src; size_t dst; size_t bytes; };
   std::vector<Piece> pieces;
   pieces.reserve(S.in_bytes / kPiece + 64);
@@ -357,15 +360,18 @@ int copy_trials(Arena& A, const pm_trials& T, StagedTrials& S) {
       scan_slots(T, slots * t / scan_tasks, slots * (t + 1) / scan_tasks, &longest[t], &bad[t]);
     }
   });
-  // Start the DMA of each contiguous staged prefix as soon as it is complete.
+  // Start the DMA of the contiguous staged prefix a chunk at a time as soon
+  // as it is complete (the last chunk may be shorter).
   size_t ready = 0, issued = 0;
   cudaError_t dma = cudaSuccess;
   auto progress = [&] {
     while (ready < pieces.size() && batch.done(ready)) ++ready;
-    const size_t upto = ready == pieces.size() ? S.in_bytes : (ready ? pieces[ready - 1].dst + pieces[ready - 1].bytes : 0);
-    if (dma == cudaSuccess && upto > issued && (upto - issued >= kDmaMin || ready == pieces.size())) {
-      dma = cudaMemcpyAsync(dev + issued, host + issued, upto - issued, cudaMemcpyHostToDevice, A.stream);
-      issued = upto;
+    const bool all = ready == pieces.size();
+    const size_t upto = all ? S.in_bytes : (ready ? pieces[ready - 1].dst + pieces[ready - 1].bytes : 0);
+    while (dma == cudaSuccess && upto > issued && (upto - issued >= kDma || all)) {
+      const size_t bytes = std::min(kDma, upto - issued);
+      dma = cudaMemcpyAsync(dev + issued, host + issued, bytes, cudaMemcpyHostToDevice, A.stream);
+      issued += bytes;
     }
   };
   run_host_batch(batch, progress);
