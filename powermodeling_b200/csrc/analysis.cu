@@ -548,31 +548,12 @@ __device__ __noinline__ void phase_stats_impl(const pm_trials& T, const pm_polic
   __syncthreads();
 }
 
-// CTA-wide: does any selected sample of phase p violate |v - center| <= tol
-// (relative: |v - center| / center <= tol), or miss the value?
 // _phase_stats on the tile in global scratch (gtile != NULL) or in shared memory.
 __device__ __forceinline__ void phase_stats(const pm_trials& T, const pm_policy& P, Shared& S, double* gtile, int SP,
                                             int trial, int p, double start, double end, double trim, bool idle,
                                             bool aligned) {
   if (gtile) phase_stats_impl<false>(T, P, S, gtile, SP, trial, p, start, end, trim, idle, aligned);
   else phase_stats_impl<true>(T, P, S, gtile, SP, trial, p, start, end, trim, idle, aligned);
-}
-
-__device__ bool any_outside(const pm_trials& T, const Shared& S, int trial, int p, int column,
-                            double center, double tol, bool relative) {
-  const int slot = trial * PM_PHASES + p;
-  const int64_t b = T.phase_offsets[slot];
-  bool bad = false;
-  if (S.pf[p] & (1u << PM_PF_COMPUTED)) {
-    const int64_t lo = b + (int64_t)S.po[p][PM_PO_SEL_LO], hi = b + (int64_t)S.po[p][PM_PO_SEL_HI];
-    for (int64_t i = lo + threadIdx.x; i < hi; i += blockDim.x) {
-      const double v = col_value(T, column, i);
-      if (none(v)) { bad = true; break; }
-      const double d = fabs(v - center);
-      if (relative ? (d / center > tol) : (d > tol)) { bad = true; break; }
-    }
-  }
-  return __syncthreads_or(bad) != 0;
 }
 
 __device__ __forceinline__ double fin(double x) { return x; }   // NaN already means None
@@ -593,7 +574,9 @@ analyze_kernel(pm_trials T, pm_policy P, pm_trial_results R, int SP, double* gsc
   double* sortbuf = gscratch ? gscratch + (size_t)blockIdx.x * kTileColumns * SP : nullptr;   // NULL: shared tile
   // The trial's scalars, read many times by the trial-level code: one coalesced load.
   __shared__ double s_ts[PM_TS_COUNT];
+  __shared__ uint32_t s_scan;   // per-sample state scans: one bit per check failed
   for (int i = threadIdx.x; i < PM_TS_COUNT; i += blockDim.x) s_ts[i] = T.trial_scalars[(size_t)trial * PM_TS_COUNT + i];
+  if (threadIdx.x == 0) s_scan = 0;
   __syncthreads();
   const double* ts = s_ts;
   const uint32_t tflags = T.trial_flags[trial];
@@ -645,33 +628,64 @@ analyze_kernel(pm_trials T, pm_policy P, pm_trial_results R, int SP, double* gsc
   const uint32_t mf = S.pf[PM_MEASURE];
 
   // ---- per-sample baseline and paired state scans (all threads) -------------
-  // analyze_trial:780-805: each idle phase's selected samples vs the active median.
+  // analyze_trial:780-805: each idle phase's selected samples vs the active
+  // median (clocks relative, temperature absolute); _paired_reference_contrast
+  // :335-342: the reference's selected samples vs the treatment median (all
+  // absolute).  Every check of a phase is made in one pass over its samples
+  // (check k of phase j is bit 4j + k: graphics, memory and SM clock, then
+  // temperature); a sample with no value fails a check as well.
   const bool base_sm = ((mf | S.pf[PM_IDLE_PRE] | S.pf[PM_IDLE_POST]) >> PM_PF_ANY_SM_FINITE) & 1u;
+  const bool paired_sm = ((mf | S.pf[PM_REFERENCE]) >> PM_PF_ANY_SM_FINITE) & 1u;
   const int clock_cols[3] = {C_GFX, C_MEM, C_SM};
   const int med_slot[3] = {PM_PO_GFX_MED, PM_PO_MEM_MED, PM_PO_SM_MED};
-  bool scan_idle_clock[2] = {false, false}, scan_idle_temp[2] = {false, false};
-  for (int side = 0; side < 2; ++side) {
-    const int ph = side ? PM_IDLE_POST : PM_IDLE_PRE;
-    for (int k = 0; k < (base_sm ? 3 : 2); ++k) {
-      const double active = mea[med_slot[k]];
-      if (!none(active) && active > 0 && any_outside(T, S, trial, ph, clock_cols[k], active, P.clock_tolerance_fraction, true))
-        scan_idle_clock[side] = true;
+  {
+    uint32_t bad = 0;
+    const int scan_phase[3] = {PM_IDLE_PRE, PM_IDLE_POST, PM_REFERENCE};
+    for (int j = 0; j < 3; ++j) {
+      const int ph = scan_phase[j];
+      const bool ref = j == 2;
+      if (ref && !has_ref) continue;
+      bool on[4];
+      double center[4], tol[4];
+      const int nclk = (ref ? paired_sm : base_sm) ? 3 : 2;
+      for (int k = 0; k < 3; ++k) {
+        const double active = mea[med_slot[k]];
+        if (ref) {
+          on[k] = k < nclk;
+          center[k] = none(active) ? 0.0 : active;
+          tol[k] = center[k] * P.clock_tolerance_fraction;
+        } else {
+          on[k] = k < nclk && !none(active) && active > 0;
+          center[k] = active;
+          tol[k] = P.clock_tolerance_fraction;   // relative
+        }
+      }
+      const double at = mea[PM_PO_TEMP_MED];
+      on[3] = ref || !none(at);
+      center[3] = none(at) ? 0.0 : at;
+      tol[3] = P.max_temperature_drift_c;
+      if (!(S.pf[ph] & (1u << PM_PF_COMPUTED)) || !(on[0] || on[1] || on[2] || on[3])) continue;
+      const int64_t b = T.phase_offsets[trial * PM_PHASES + ph];
+      const int64_t lo = b + (int64_t)S.po[ph][PM_PO_SEL_LO], hi = b + (int64_t)S.po[ph][PM_PO_SEL_HI];
+      for (int64_t i = lo + threadIdx.x; i < hi; i += blockDim.x) {
+#pragma unroll
+        for (int k = 0; k < 4; ++k) {
+          if (!on[k]) continue;
+          const double v = col_value(T, k < 3 ? clock_cols[k] : C_TEMP, i);
+          const double d = fabs(v - center[k]);
+          const bool fail = none(v) || ((!ref && k < 3) ? (d / center[k] > tol[k]) : (d > tol[k]));
+          if (fail) bad |= 1u << (4 * j + k);
+        }
+      }
     }
-    const double at = mea[PM_PO_TEMP_MED];
-    if (!none(at) && any_outside(T, S, trial, ph, C_TEMP, at, P.max_temperature_drift_c, false)) scan_idle_temp[side] = true;
+    bad = __reduce_or_sync(0xffffffffu, bad);
+    if ((threadIdx.x & 31) == 0 && bad) atomicOr(&s_scan, bad);
+    __syncthreads();
   }
-  // _paired_reference_contrast:335-342: reference selected samples vs the treatment median.
-  const bool paired_sm = ((mf | S.pf[PM_REFERENCE]) >> PM_PF_ANY_SM_FINITE) & 1u;
-  bool scan_ref[4] = {false, false, false, false};
-  if (has_ref) {
-    for (int k = 0; k < (paired_sm ? 3 : 2); ++k) {
-      const double active = mea[med_slot[k]];
-      const double tol = (none(active) ? 0.0 : active) * P.clock_tolerance_fraction;
-      scan_ref[k] = any_outside(T, S, trial, PM_REFERENCE, clock_cols[k], none(active) ? 0.0 : active, tol, false);
-    }
-    const double at = mea[PM_PO_TEMP_MED];
-    scan_ref[3] = any_outside(T, S, trial, PM_REFERENCE, C_TEMP, none(at) ? 0.0 : at, P.max_temperature_drift_c, false);
-  }
+  const uint32_t scan = s_scan;
+  const bool scan_idle_clock[2] = {(scan & 0x7u) != 0, (scan & 0x70u) != 0};
+  const bool scan_idle_temp[2] = {(scan & 0x8u) != 0, (scan & 0x80u) != 0};
+  const bool scan_ref[4] = {(scan & 0x100u) != 0, (scan & 0x200u) != 0, (scan & 0x400u) != 0, (scan & 0x800u) != 0};
 
   if (threadIdx.x != 0) return;
   // ---- trial scalars and gates (thread 0) ----------------------------------
