@@ -17,6 +17,7 @@ from __future__ import annotations
 
 import argparse
 import ctypes as C
+import datetime
 import json
 import math
 import multiprocessing as mp
@@ -47,21 +48,40 @@ def measured_peaks() -> dict:
 
 # --------------------------------------------------------------------------- clocks
 class ClockSampler:
-    QUERY = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+    """nvidia-smi clock, power and throttle-reason samples around a measurement.
+
+    Sampling starts (and its first row is awaited) before the measurement;
+    with mark_begin()/mark_end() around a timed region, the statistics use
+    the rows stamped inside it (the rows nearest to it when it is shorter
+    than one interval)."""
+    QUERY = ("timestamp,index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap,clocks.mem")
 
-    def __init__(self, index: int):
-        self.index, self.proc, self.path = index, None, None
+    def __init__(self, index: int, interval_ms: int = 20):
+        self.index, self.interval_ms, self.proc, self.path = index, interval_ms, None, None
+        self.t0 = self.t1 = None
 
     def start(self):
         try:
             self.path = Path(os.environ.get("TMPDIR", "/tmp")) / f"pmb200_clocks_{os.getpid()}_{id(self)}.csv"
             self.proc = subprocess.Popen(["nvidia-smi", "-i", str(self.index), f"--query-gpu={self.QUERY}",
-                                          "--format=csv,noheader,nounits", "-lms", "100"],
+                                          "--format=csv,noheader,nounits", "-lms", str(self.interval_ms)],
                                          stdout=open(self.path, "w"), stderr=subprocess.DEVNULL)
         except OSError:
             self.proc = None
+            return
+        deadline = time.time() + 3.0
+        while time.time() < deadline and self.proc.poll() is None:
+            if self.path.exists() and self.path.read_text().strip():
+                break
+            time.sleep(0.01)
+
+    def mark_begin(self):
+        self.t0 = time.time()
+
+    def mark_end(self):
+        self.t1 = time.time()
 
     def stop(self) -> dict:
         if self.proc is None:
@@ -69,16 +89,34 @@ class ClockSampler:
         self.proc.terminate()
         self.proc.wait(timeout=10)
         rows = [line.split(", ") for line in self.path.read_text().splitlines() if line.strip()]
-        sm = [float(r[1]) for r in rows if len(r) >= 10 and r[1].replace(".", "").isdigit()]
-        mx = [float(r[2]) for r in rows if len(r) >= 10 and r[2].replace(".", "").isdigit()]
-        mem = [float(r[9]) for r in rows if len(r) >= 10 and r[9].strip().replace(".", "").isdigit()]
-        power = [float(r[3]) for r in rows if len(r) >= 10 and r[3].replace(".", "").isdigit()]
+        rows = [r for r in rows if len(r) >= 11]
+        stamped = []
+        for r in rows:
+            try:
+                stamped.append((datetime.datetime.strptime(r[0].strip(), "%Y/%m/%d %H:%M:%S.%f").timestamp(), r))
+            except ValueError:
+                pass
+        window = rows
+        if self.t0 is not None and self.t1 is not None and stamped:
+            inside = [r for t, r in stamped if self.t0 <= t <= self.t1]
+            if inside:
+                window = inside
+            else:   # region shorter than one interval: the rows on either side of it
+                before = [r for t, r in stamped if t < self.t0][-1:]
+                after = [r for t, r in stamped if t > self.t1][:1]
+                window = before + after or rows
+        num = lambda v: v.strip().replace(".", "", 1).isdigit()
+        sm = [float(r[2]) for r in window if num(r[2])]
+        mx = [float(r[3]) for r in rows if num(r[3])]
+        mem = [float(r[10]) for r in window if num(r[10])]
+        power = [float(r[4]) for r in window if num(r[4])]
         names = ("hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap")
-        reasons = sorted({name for r in rows if len(r) >= 10 for name, v in zip(names, r[5:9]) if v.strip() == "Active"})
+        reasons = sorted({name for r in window for name, v in zip(names, r[6:10]) if v.strip() == "Active"})
         return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": max(mx) if mx else None,
                 "mem_mhz": statistics.median(mem) if mem else None,
                 "power_w_median": statistics.median(power) if power else None,
-                "reasons": reasons, "samples": len(rows)}
+                "reasons": reasons, "samples": len(window), "samples_total": len(rows),
+                "interval_ms": self.interval_ms}
 
 
 # --------------------------------------------------------------------------- workload
@@ -223,6 +261,7 @@ def run_b200(args, rank: int, world: int) -> dict | None:
     torch.cuda.synchronize()
     clocks = ClockSampler(local)
     clocks.start()
+    clocks.mark_begin()
     parts_ms = {"analyze": [], "exchange_rows": [], "join_and_finish": [], "exchange_groups": []}
     prepare_ms, step_ms = [], []
     for _ in range(args.steps):
@@ -234,6 +273,7 @@ def run_b200(args, rank: int, world: int) -> dict | None:
         prepare_ms.append(side_ev[0].elapsed_time(side_ev[1]))
         step_ms.append(ev[0].elapsed_time(ev[4]))
     torch.cuda.synchronize()
+    clocks.mark_end()
     clock_info = clocks.stop()
     if world > 1:
         dist.barrier()
