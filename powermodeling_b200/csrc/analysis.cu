@@ -680,6 +680,14 @@ analyze_kernel(pm_trials T, pm_policy P, pm_trial_results R, int SP, double* gsc
     }
     bad = __reduce_or_sync(0xffffffffu, bad);
     if ((threadIdx.x & 31) == 0 && bad) atomicOr(&s_scan, bad);
+    // The phase records are final: all threads write them out, and fill the
+    // trial's scalar and metric rows with None (thread 0 sets the rest after
+    // the barrier).
+    for (int i = threadIdx.x; i < PM_PHASES * PM_PO_COUNT; i += blockDim.x)
+      R.phase_out[(size_t)trial * PM_PHASES * PM_PO_COUNT + i] = S.po[i / PM_PO_COUNT][i % PM_PO_COUNT];
+    if (threadIdx.x < PM_PHASES) R.phase_flags[trial * PM_PHASES + threadIdx.x] = S.pf[threadIdx.x];
+    for (int i = threadIdx.x; i < PM_TO_COUNT; i += blockDim.x) R.trial_out[(size_t)trial * PM_TO_COUNT + i] = dnan();
+    for (int i = threadIdx.x; i < PM_N_METRICS; i += blockDim.x) R.metrics[(size_t)trial * PM_N_METRICS + i] = dnan();
     __syncthreads();
   }
   const uint32_t scan = s_scan;
@@ -689,8 +697,7 @@ analyze_kernel(pm_trials T, pm_policy P, pm_trial_results R, int SP, double* gsc
 
   if (threadIdx.x != 0) return;
   // ---- trial scalars and gates (thread 0) ----------------------------------
-  double* to = R.trial_out + (size_t)trial * PM_TO_COUNT;
-  for (int f = 0; f < PM_TO_COUNT; ++f) to[f] = dnan();
+  double* to = R.trial_out + (size_t)trial * PM_TO_COUNT;   // filled with None above
   uint64_t iss = 0, base = 0, pair = 0, warn = 0;
   auto phase_issue_bits = [&](uint32_t f) -> uint64_t {
     uint64_t b = 0;
@@ -1021,13 +1028,7 @@ analyze_kernel(pm_trials T, pm_policy P, pm_trial_results R, int SP, double* gsc
   uint64_t* ib = R.issue_bits + (size_t)trial * PM_ISSUE_WORDS;
   ib[0] = iss; ib[1] = base; ib[2] = pair; ib[3] = warn;
   R.valid[trial] = valid;
-  for (int p = 0; p < PM_PHASES; ++p) {
-    double* dst = R.phase_out + ((size_t)trial * PM_PHASES + p) * PM_PO_COUNT;
-    for (int f = 0; f < PM_PO_COUNT; ++f) dst[f] = S.po[p][f];
-    R.phase_flags[trial * PM_PHASES + p] = S.pf[p];
-  }
-  double* m = R.metrics + (size_t)trial * PM_N_METRICS;
-  for (int k = 0; k < PM_N_METRICS; ++k) m[k] = dnan();
+  double* m = R.metrics + (size_t)trial * PM_N_METRICS;   // filled with None above
   m[PM_M_board_power_w] = board_power;
   m[PM_M_idle_power_w] = idle_power;
   m[PM_M_incremental_power_w] = incremental_power;
