@@ -364,7 +364,74 @@ def run_b200(args, rank: int, world: int) -> dict | None:
         line["cpu_baseline"] = cpu_baseline(records, policy)
     if not args.no_arms and world == 1:
         line["arms"] = run_arms(local, peaks)
+        line["arms"]["analysis_scaled"] = run_scaled_analysis(packed, native_policy, peaks)
     return line
+
+
+def replicate_packed(packed, copies: int):
+    """The packed batch repeated `copies` times (offsets rebased; broadcast columns stay one element)."""
+    from types import SimpleNamespace
+    from powermodeling_b200 import _native as N
+    a, k = packed.arrays, copies
+    out = {}
+    for name, _, key in N.TRIAL_ARRAYS + N.EPOCH_ARRAYS + N.TAIL_ARRAYS:
+        x = a[name]
+        if name in ("phase_offsets", "epoch_offsets"):
+            step = packed.n_samples if name == "phase_offsets" else packed.n_epochs
+            out[name] = np.concatenate([x[:-1] + c * step for c in range(k)] + [x[-1:] + (k - 1) * step]).astype(x.dtype)
+        elif key == "samples" and x.size == 1 and packed.n_samples > 1:
+            out[name] = x
+        else:
+            out[name] = np.tile(x, k)
+    return SimpleNamespace(arrays=out, n_trials=packed.n_trials * k, n_samples=packed.n_samples * k,
+                           n_epochs=packed.n_epochs * k, max_phase_samples=packed.max_phase_samples,
+                           broadcast=packed.broadcast)
+
+
+def run_scaled_analysis(packed, native_policy, peaks: dict) -> dict:
+    """The analysis kernel alone on the sweep repeated up to 65 536 trials (16 384 points): trials
+    integrated per second and input bytes read per second as the batch outgrows the L2."""
+    import torch
+    from powermodeling_b200 import _native as N
+    lib = N.library()
+    PO, TO, M = N.layout("PM_PO_COUNT"), N.layout("PM_TO_COUNT"), N.layout("PM_M_COUNT")
+    stream = torch.cuda.current_stream()
+    sptr = C.c_void_p(stream.cuda_stream)
+    hbm = peaks.get("hbm_gbs", 6650.0)
+    out = {}
+    for copies in (1, 16, 64, 256):
+        big = replicate_packed(packed, copies)
+        trials, keep, in_bytes = device_arrays(big, torch)
+        n = big.n_trials
+        res = {"phase_out": torch.empty(n * 5 * PO, dtype=torch.float64, device="cuda"),
+               "phase_flags": torch.empty(n * 5, dtype=torch.int32, device="cuda"),
+               "trial_out": torch.empty(n * TO, dtype=torch.float64, device="cuda"),
+               "issue_bits": torch.empty(n * 4, dtype=torch.int64, device="cuda"),
+               "metrics": torch.empty(n * M, dtype=torch.float64, device="cuda"),
+               "valid": torch.empty(n, dtype=torch.uint8, device="cuda")}
+        results = N.TrialResults(*(res[k].data_ptr() for k in ("phase_out", "phase_flags", "trial_out", "issue_bits", "metrics", "valid")))
+        out_bytes = sum(v.numel() * v.element_size() for v in res.values())
+        scr_n = lib.pm_analyze_scratch_bytes(n, big.max_phase_samples)
+        scr = torch.empty(max(1, scr_n), dtype=torch.uint8, device="cuda")
+        run = lambda: N.check(lib.pm_analyze_trials_device(trials, native_policy, results, C.c_void_p(scr.data_ptr()),
+                                                             scr_n, sptr), "analyze (scaled)")
+        for _ in range(3):
+            run()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        reps = 5
+        torch.cuda.synchronize()
+        e0.record(stream)
+        for _ in range(reps):
+            run()
+        e1.record(stream)
+        e1.synchronize()
+        ms = e0.elapsed_time(e1) / reps
+        assert int(res["valid"].sum().item()) == n, "replicated trials must all be valid"
+        gbs = (in_bytes + out_bytes) / (ms / 1e3) / 1e9
+        out[str(n)] = {"points": n // 4, "ms": ms, "trials_per_s": n / (ms / 1e3), "samples_per_s": big.n_samples / (ms / 1e3),
+                       "algorithmic_gbs": gbs, "frac_of_hbm": gbs / hbm, "input_bytes": int(in_bytes)}
+        del trials, keep, res, scr
+    return out
 
 
 # --------------------------------------------------------------------------- workload arms
