@@ -153,6 +153,13 @@ def global_groups(trials: list, world: int):
     return [buckets[k] for k in keys], [A.group_seed(k) for k in keys]
 
 
+def device_view(ptr: int, shape: tuple, typestr: str, torch):
+    """A torch tensor over device memory the library allocated (no copy)."""
+    class _View:
+        __cuda_array_interface__ = {"shape": shape, "typestr": typestr, "data": (ptr, False), "version": 3, "strides": None}
+    return torch.as_tensor(_View(), device="cuda")
+
+
 def device_arrays(packed, torch):
     from powermodeling_b200 import _native as N
     dev = {}
@@ -194,9 +201,47 @@ def run_b200(args, rank: int, world: int) -> dict | None:
            "valid": torch.empty(n, dtype=torch.uint8, device="cuda")}
     results = N.TrialResults(*(out[k].data_ptr() for k in ("phase_out", "phase_flags", "trial_out", "issue_bits", "metrics", "valid")))
     out_bytes = sum(v.numel() * v.element_size() for v in out.values())
-    # Exchange one lands every rank's metric rows and valid flags here (rank order = global row order).
-    all_metrics = torch.empty(world * n * M, dtype=torch.float64, device="cuda") if world > 1 else out["metrics"]
-    all_valid = torch.empty(world * n, dtype=torch.uint8, device="cuda") if world > 1 else out["valid"]
+    # Exchange one lands every rank's metric rows and valid flags in the gathered buffers (rank order =
+    # global row order): by default the analysis kernel stores them into every rank's buffers over
+    # NVLink (peer memory, pmb200_peer.h); with --exchange nccl, an all-gather after it.
+    peer = world > 1 and args.exchange == "peer"
+    peer_bufs = []
+    if peer:
+        gathered_ptrs = []
+        per_rank_groups = -(-len(members) // world)
+        # rows, valid flags, row arrival flags + counter, group results, group arrival flags + counter
+        for nbytes in (world * n * M * 8, world * n, (world + 1) * 4, world * 3 * per_rank_groups * M * 8, (world + 1) * 4):
+            ptr, handle = C.c_void_p(), N.PeerHandle()
+            N.check(lib.pm_peer_alloc(nbytes, C.byref(ptr), C.byref(handle)), "pm_peer_alloc")
+            peer_bufs.append(ptr.value)
+            gathered_ptrs.append((ptr.value, bytes(handle.bytes)))
+        handles: list = [None] * world
+        dist.all_gather_object(handles, [h for _, h in gathered_ptrs])
+        opened = []
+        X, XG = N.PeerRows(), N.PeerGroups()
+        X.n_ranks, X.rank, X.row_offset, X.epoch = world, rank, rank * n, 0
+        XG.n_ranks, XG.rank, XG.per_rank, XG.epoch = world, rank, per_rank_groups, 0
+        for r in range(world):
+            ptrs = []
+            for b, (mine_ptr, _) in enumerate(gathered_ptrs):
+                if r == rank:
+                    ptrs.append(mine_ptr)
+                else:
+                    h = N.PeerHandle()
+                    C.memmove(h.bytes, handles[r][b], 64)
+                    q = C.c_void_p()
+                    N.check(lib.pm_peer_open(C.byref(h), C.byref(q)), "pm_peer_open")
+                    opened.append(q.value)
+                    ptrs.append(q.value)
+            X.metrics[r], X.valid[r], X.flags[r], XG.out[r], XG.flags[r] = ptrs
+        X.done = peer_bufs[2] + world * 4
+        XG.done = peer_bufs[4] + world * 4
+        wait_error = torch.zeros(1, dtype=torch.int32, device="cuda")
+        all_metrics_ptr, all_valid_ptr = peer_bufs[0], peer_bufs[1]
+    else:
+        all_metrics = torch.empty(world * n * M, dtype=torch.float64, device="cuda") if world > 1 else out["metrics"]
+        all_valid = torch.empty(world * n, dtype=torch.uint8, device="cuda") if world > 1 else out["valid"]
+        all_metrics_ptr, all_valid_ptr = all_metrics.data_ptr(), all_valid.data_ptr()
     own = [members[g] for g in mine]
     offsets = np.zeros(len(own) + 1, dtype=np.int32)
     np.cumsum([len(m) for m in own], out=offsets[1:])
@@ -206,10 +251,10 @@ def run_b200(args, rank: int, world: int) -> dict | None:
     d_seeds = torch.from_numpy(own_seeds.view(np.int64)).cuda()
     # Group outputs of this rank: [3, per_rank, M] (medians, lows, highs); exchange two gathers them.
     group_out = torch.full((3, per_rank, M), float("nan"), dtype=torch.float64, device="cuda")
-    all_group_out = torch.empty((world, 3, per_rank, M), dtype=torch.float64, device="cuda") if world > 1 else None
+    all_group_out = torch.empty((world, 3, per_rank, M), dtype=torch.float64, device="cuda") if world > 1 and not peer else None
     max_members = max((len(m) for m in own), default=1)
     job = N.BootstrapJob(len(own), M, int(sum(len(m) for m in own)), world * n, RESAMPLES, max_members,
-                         all_metrics.data_ptr(), d_off.data_ptr(), d_rows.data_ptr(), all_valid.data_ptr(),
+                         all_metrics_ptr, d_off.data_ptr(), d_rows.data_ptr(), all_valid_ptr,
                          d_seeds.data_ptr(), group_out[0].data_ptr(), group_out[1].data_ptr(), group_out[2].data_ptr())
     a_scr = lib.pm_analyze_scratch_bytes(n, packed.max_phase_samples)
     b_scr = lib.pm_bootstrap_scratch_bytes(max(1, len(own)), max_members, RESAMPLES)
@@ -232,17 +277,31 @@ def run_b200(args, rank: int, world: int) -> dict | None:
         if own:
             N.check(lib.pm_bootstrap_prepare_device(job, boot_scratch, b_scr, side_ptr), "prepare")
         side_ev[1].record(side)
-        N.check(lib.pm_analyze_trials_device(trials, native_policy, results, C.c_void_p(scratch.data_ptr()), a_scr, sptr), "analyze")
+        if peer:
+            X.epoch += 1
+            N.check(lib.pm_analyze_trials_device_exchange(trials, native_policy, results, C.c_void_p(scratch.data_ptr()),
+                                                          a_scr, C.byref(X), sptr), "analyze + row exchange")
+        else:
+            N.check(lib.pm_analyze_trials_device(trials, native_policy, results, C.c_void_p(scratch.data_ptr()), a_scr, sptr), "analyze")
         ev[1].record(stream)
-        if world > 1:
+        if peer:
+            N.check(lib.pm_peer_wait_device(C.c_void_p(peer_bufs[2]), world, X.epoch, 5000, C.c_void_p(wait_error.data_ptr()),
+                                            sptr), "row arrival wait")
+        elif world > 1:
             dist.all_gather_into_tensor(all_metrics, out["metrics"])
             dist.all_gather_into_tensor(all_valid, out["valid"])
         ev[2].record(stream)
         stream.wait_event(side_ev[1])
-        if own:
+        if peer:
+            XG.epoch += 1
+            N.check(lib.pm_bootstrap_finish_device_exchange(job, boot_scratch, b_scr, C.byref(XG), sptr), "finish + group exchange")
+        elif own:
             N.check(lib.pm_bootstrap_finish_device(job, boot_scratch, b_scr, sptr), "finish")
         ev[3].record(stream)
-        if world > 1:
+        if peer:
+            N.check(lib.pm_peer_wait_device(C.c_void_p(peer_bufs[4]), world, XG.epoch, 5000, C.c_void_p(wait_error.data_ptr()),
+                                            sptr), "group arrival wait")
+        elif world > 1:
             dist.all_gather_into_tensor(all_group_out, group_out)
         ev[4].record(stream)
 
@@ -250,7 +309,10 @@ def run_b200(args, rank: int, world: int) -> dict | None:
         flush.zero_()
         step()
     torch.cuda.synchronize()
-    gathered = (all_group_out if world > 1 else group_out.unsqueeze(0)).cpu().numpy()
+    if peer:
+        gathered = device_view(peer_bufs[3], (world, 3, per_rank_groups, M), "<f8", torch).cpu().numpy()
+    else:
+        gathered = (all_group_out if world > 1 else group_out.unsqueeze(0)).cpu().numpy()
     resamples_per_step = int(np.isfinite(gathered[:, 1]).sum()) * RESAMPLES
     # group g was bootstrapped by rank g % world as its (g // world)-th group
     lo_global = np.stack([gathered[g % world, 1, g // world] for g in range(G)])
@@ -334,6 +396,14 @@ def run_b200(args, rank: int, world: int) -> dict | None:
         e2e_s = float(t.item())
     assert np.array_equal(np.nan_to_num(h_groups[1]), np.nan_to_num(lo_global[local_groups])), \
         "e2e and device paths disagree"
+    if peer:
+        torch.cuda.synchronize()
+        assert int(wait_error.item()) == 0, "a rank's rows did not arrive within the wait limit"
+        dist.barrier()                       # every rank is done with every peer buffer
+        for q in opened:
+            N.check(lib.pm_peer_close(C.c_void_p(q)), "pm_peer_close")
+        for q in peer_bufs:
+            N.check(lib.pm_peer_free(C.c_void_p(q)), "pm_peer_free")
     h2d = in_bytes + l_off.nbytes + l_rows.nbytes + l_seeds.nbytes + (h_groups.nbytes if world > 1 else 0)
     d2h = sum(a.nbytes for a in h_out.values()) + h_groups.nbytes * (world + 1 if world > 1 else 1)
     if rank != 0:
@@ -349,15 +419,18 @@ def run_b200(args, rank: int, world: int) -> dict | None:
             "config": {"workload": WORKLOAD, "points": POINTS * world, "points_per_gpu": POINTS, "repeats": REPEATS,
                        "trials": n * world, "groups": G,
                        "resamples": RESAMPLES, "samples": packed.n_samples, "l2": "flushed (256 MiB write) between steps",
-                       "parallelism": f"sweep-sharded x{world}: trials and groups per rank, rows and group "
-                                      f"results all-gathered over NCCL" if world > 1 else "single GPU"},
+                       "parallelism": (f"sweep-sharded x{world}: trials and groups per rank; metric rows stored into "
+                                       f"every rank by the analysis kernel over NVLink peer memory, group results "
+                                       f"all-gathered over NCCL" if peer else
+                                       f"sweep-sharded x{world}: trials and groups per rank, rows and group results "
+                                       f"all-gathered over NCCL") if world > 1 else "single GPU"},
             "e2e": {"value": resamples_per_step / e2e_s, "unit": "resamples/s",
                     "h2d_bytes_per_step": int(h2d), "d2h_bytes_per_step": int(d2h), "ms_per_step": e2e_s * 1e3},
             "gpu_launches": (3 if own else 1) * args.steps,
             "kernels": {"analyze_kernel_ms": a_ms,
                         "bootstrap_prepare_kernel_ms (side stream, overlaps analyze)": statistics.mean(prepare_ms),
                         "join_and_bootstrap_finish_ms": b_ms,
-                        "exchange_rows_ms": statistics.mean(parts_ms["exchange_rows"]),
+                        ("rows_arrival_wait_ms" if peer else "exchange_rows_ms"): statistics.mean(parts_ms["exchange_rows"]),
                         "exchange_groups_ms": statistics.mean(parts_ms["exchange_groups"])},
             "roofline": roofline, "clocks": clock_info}
     if world == 1 and not args.no_cpu_baseline:
@@ -645,6 +718,8 @@ def main():
     parser.add_argument("--steps", type=int, default=200)
     parser.add_argument("--warmup", type=int, default=5)
     parser.add_argument("--impl", choices=("b200", "reference"), default="b200")
+    parser.add_argument("--exchange", choices=("peer", "nccl"), default="peer",
+                        help="N>1: metric rows stored into every rank by the analysis kernel over NVLink, or all-gathered by NCCL")
     parser.add_argument("--no-cpu-baseline", action="store_true")
     parser.add_argument("--no-arms", action="store_true", help="skip the HBM/tensor/GEMM/SFU arm measurements")
     args = parser.parse_args()

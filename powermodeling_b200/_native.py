@@ -110,6 +110,23 @@ class BootstrapJob(C.Structure):
                 ("seeds", _p), ("medians", _p), ("ci_lo", _p), ("ci_hi", _p)]
 
 
+MAX_RANKS = 8   # PM_MAX_RANKS (include/pmb200_peer.h)
+
+
+class PeerHandle(C.Structure):
+    _fields_ = [("bytes", C.c_ubyte * 64)]
+
+
+class PeerRows(C.Structure):
+    _fields_ = [("n_ranks", C.c_int32), ("rank", C.c_int32), ("row_offset", C.c_int32), ("epoch", C.c_uint32),
+                ("metrics", _p * MAX_RANKS), ("valid", _p * MAX_RANKS), ("flags", _p * MAX_RANKS), ("done", _p)]
+
+
+class PeerGroups(C.Structure):
+    _fields_ = [("n_ranks", C.c_int32), ("rank", C.c_int32), ("per_rank", C.c_int32), ("epoch", C.c_uint32),
+                ("out", _p * MAX_RANKS), ("flags", _p * MAX_RANKS), ("done", _p)]
+
+
 class NativeError(RuntimeError):
     """A libpmb200 entry point returned an error code."""
 
@@ -146,6 +163,15 @@ def library() -> C.CDLL:
             lib.pm_analyze_sweep.argtypes = [C.POINTER(Trials), C.POINTER(Policy), C.POINTER(TrialResults),
                                              C.POINTER(BootstrapJob)]
             lib.pm_resample_indices.argtypes = [C.c_uint64, C.c_int32, C.c_int32, C.POINTER(C.c_int32)]
+            lib.pm_peer_alloc.argtypes = [C.c_size_t, C.POINTER(_p), C.POINTER(PeerHandle)]
+            lib.pm_peer_free.argtypes = [_p]
+            lib.pm_peer_open.argtypes = [C.POINTER(PeerHandle), C.POINTER(_p)]
+            lib.pm_peer_close.argtypes = [_p]
+            lib.pm_analyze_trials_device_exchange.argtypes = [C.POINTER(Trials), C.POINTER(Policy), C.POINTER(TrialResults),
+                                                              _p, C.c_size_t, C.POINTER(PeerRows), _p]
+            lib.pm_peer_wait_device.argtypes = [_p, C.c_int32, C.c_uint32, C.c_uint32, _p, _p]
+            lib.pm_bootstrap_finish_device_exchange.argtypes = [C.POINTER(BootstrapJob), _p, C.c_size_t,
+                                                                C.POINTER(PeerGroups), _p]
             _lib = lib
     return _lib
 

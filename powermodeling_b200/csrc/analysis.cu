@@ -18,6 +18,7 @@
 #include "pm_layout.h"
 #include "pm_device.cuh"
 #include "pm_capi.h"
+#include "pmb200_peer.h"
 
 namespace pm {
 
@@ -567,8 +568,30 @@ __device__ double idle_at(const double* pre, const double* post, const double* a
   return a + (b - a) * (t - t0) / (t1 - t0);
 }
 
+// Deliver one trial's metric row and valid flag to every rank's gathered
+// buffers (peer stores over NVLink); the last CTA of the launch to get here
+// raises this rank's arrival flag on every rank.  Each CTA counts with an
+// acquire-release add (GPU scope: every counting CTA is on this GPU), so its
+// row stores are released to the counter; the last CTA, having acquired every
+// earlier count, releases them all with its system-scope flag stores: a rank
+// that acquires the flag sees all of this launch's rows.
+__device__ __noinline__ void deliver_rows(const pm_peer_rows& X, int trial, const double* m, uint8_t valid,
+                                          uint32_t n_trials) {
+  const size_t row = (size_t)(X.row_offset + trial);
+  for (int r = 0; r < X.n_ranks; ++r) {
+    double* dst = X.metrics[r] + row * PM_N_METRICS;
+    for (int k = 0; k < PM_N_METRICS; ++k) dst[k] = m[k];
+    X.valid[r][row] = valid;
+  }
+  uint32_t prev;
+  asm volatile("atom.add.acq_rel.gpu.global.u32 %0, [%1], 1;" : "=r"(prev) : "l"(X.done) : "memory");
+  if (prev + 1u == X.epoch * n_trials)
+    for (int r = 0; r < X.n_ranks; ++r)
+      asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(X.flags[r] + X.rank), "r"(X.epoch) : "memory");
+}
+
 __global__ void __launch_bounds__(kThreads)
-analyze_kernel(pm_trials T, pm_policy P, pm_trial_results R, int SP, double* gscratch) {
+analyze_kernel(pm_trials T, pm_policy P, pm_trial_results R, int SP, double* gscratch, pm_peer_rows X) {
   __shared__ Shared S;
   const int trial = blockIdx.x;
   double* sortbuf = gscratch ? gscratch + (size_t)blockIdx.x * kTileColumns * SP : nullptr;   // NULL: shared tile
@@ -1078,6 +1101,7 @@ analyze_kernel(pm_trials T, pm_policy P, pm_trial_results R, int SP, double* gsc
     m[PM_M_active_reference_loop_slots_s] = to[PM_TO_REF_SLOTS_RATE];
   }
   m[PM_M_active_reference_duration_s] = has_ref ? ref[PM_PO_DURATION_S] : dnan();
+  if (X.n_ranks > 0) deliver_rows(X, trial, m, valid, gridDim.x);
 }
 
 }  // namespace pm
@@ -1086,7 +1110,7 @@ analyze_kernel(pm_trials T, pm_policy P, pm_trial_results R, int SP, double* gsc
 // Host launcher (called from capi.cu).
 namespace pm {
 int launch_analyze(const pm_trials& T, const pm_policy& P, const pm_trial_results& R, int max_covering,
-                   double* gscratch, cudaStream_t stream, size_t* scratch_bytes_needed) {
+                   double* gscratch, cudaStream_t stream, size_t* scratch_bytes_needed, const pm_peer_rows* rows) {
   int SP = 32;
   while (SP < max_covering + 1) SP <<= 1;
   const size_t smem = (size_t)kTileColumns * SP * sizeof(double);
@@ -1102,7 +1126,9 @@ int launch_analyze(const pm_trials& T, const pm_policy& P, const pm_trial_result
   }();
   static std::atomic<int> limits[kMaxDevices];
   ensure_dynamic_smem(analyze_kernel, static_bytes, dyn, limits);
-  analyze_kernel<<<T.n_trials, kThreads, dyn, stream>>>(T, P, R, SP, use_global ? gscratch : nullptr);
+  pm_peer_rows X{};
+  if (rows) X = *rows;
+  analyze_kernel<<<T.n_trials, kThreads, dyn, stream>>>(T, P, R, SP, use_global ? gscratch : nullptr, X);
   return 0;
 }
 }  // namespace pm

@@ -23,6 +23,7 @@
 #include "pm_layout.h"
 #include "pm_device.cuh"
 #include "pm_capi.h"
+#include "pmb200_peer.h"
 
 namespace pm {
 
@@ -284,7 +285,12 @@ __global__ void __launch_bounds__(kBootThreads) bootstrap_prepare_kernel(BootArg
   }
 }
 
-__global__ void __launch_bounds__(kBootThreads) bootstrap_kernel(BootArgs A) {
+__device__ __noinline__ void deliver_groups(const pm_peer_groups& X, const BootArgs& A, int g);
+
+// The finish of one group (the CTA's): medians, fold and intervals.
+// kDeliver: the sharded form, which also delivers the group to every rank.
+template <bool kDeliver>
+__global__ void __launch_bounds__(kBootThreads) bootstrap_kernel(BootArgs A, pm_peer_groups X) {
   extern __shared__ __align__(16) unsigned char dsm[];
   __shared__ GenShared sh;
   __shared__ uint32_t n_mask[(kDirectMaxN + 1 + 31) / 32];
@@ -299,6 +305,10 @@ __global__ void __launch_bounds__(kBootThreads) bootstrap_kernel(BootArgs A) {
   if (members < 0 || members > A.max_members) {            // caller broke the stated bound: no output
     for (int m = threadIdx.x; m < M; m += blockDim.x)
       A.medians[(size_t)g * M + m] = A.lo[(size_t)g * M + m] = A.hi[(size_t)g * M + m] = dnan();
+    if constexpr (kDeliver) {
+      __syncthreads();
+      deliver_groups(X, A, g);
+    }
     return;
   }
   // Without a prepare pass, one thread of the last warp seeds the generator
@@ -640,6 +650,41 @@ __global__ void __launch_bounds__(kBootThreads) bootstrap_kernel(BootArgs A) {
     }
     __syncthreads();
   }
+  if constexpr (kDeliver) {
+    __syncthreads();   // the group's outputs (written by several threads) are complete
+    deliver_groups(X, A, g);
+  }
+}
+
+// Deliver the CTA's group (medians, lows, highs) to every rank's gathered
+// buffer (peer stores over NVLink); the last CTA of the launch raises this
+// rank's arrival flag on every rank.  The barrier orders the CTA's stores
+// before thread 0's acquire-release count (GPU scope: every counting CTA is
+// on this GPU), and the last CTA releases them all with its system-scope
+// flag stores.
+__device__ __noinline__ void deliver_groups(const pm_peer_groups& X, const BootArgs& A, int g) {
+  const int M = A.n_metrics;
+  for (int r = 0; r < X.n_ranks; ++r)
+    for (int i = threadIdx.x; i < 3 * M; i += blockDim.x) {
+      const int k = i / M, m = i - k * M;
+      const double* src = k == 0 ? A.medians : k == 1 ? A.lo : A.hi;
+      X.out[r][(((size_t)X.rank * 3 + k) * X.per_rank + g) * M + m] = src[(size_t)g * M + m];
+    }
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    uint32_t prev;
+    asm volatile("atom.add.acq_rel.gpu.global.u32 %0, [%1], 1;" : "=r"(prev) : "l"(X.done) : "memory");
+    if (prev + 1u == X.epoch * gridDim.x)
+      for (int r = 0; r < X.n_ranks; ++r)
+        asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(X.flags[r] + X.rank), "r"(X.epoch) : "memory");
+  }
+}
+
+// This rank owns no group: raise its arrival flag on every rank at once.
+__global__ void signal_groups_kernel(pm_peer_groups X) {
+  if (threadIdx.x == 0)
+    for (int r = 0; r < X.n_ranks; ++r)
+      asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(X.flags[r] + X.rank), "r"(X.epoch) : "memory");
 }
 
 // Raw index stream (diagnostic): out[r*n + j] for one seed, by one CTA.
@@ -706,7 +751,7 @@ size_t bootstrap_smem_shortfall(int M, int mm, size_t* available) {
   // every bootstrap call's host path.
   static const size_t static_bytes = [] {
     cudaFuncAttributes attr{};
-    const size_t b = cudaFuncGetAttributes(&attr, bootstrap_kernel) == cudaSuccess ? attr.sharedSizeBytes : 0;
+    const size_t b = cudaFuncGetAttributes(&attr, bootstrap_kernel<false>) == cudaSuccess ? attr.sharedSizeBytes : 0;
     cudaGetLastError();   // a failed query must not surface as a later launch error
     return b;
   }();
@@ -725,17 +770,28 @@ size_t bootstrap_smem_shortfall(int M, int mm, size_t* available) {
   return static_bytes + dyn <= (size_t)optin ? 0 : static_bytes + dyn;
 }
 
-int launch_bootstrap(const BootArgs& A, cudaStream_t stream) {
-  if (A.n_groups == 0) return 0;
+int launch_bootstrap(const BootArgs& A, cudaStream_t stream, const pm_peer_groups* groups) {
+  pm_peer_groups X{};
+  if (groups) X = *groups;
+  if (A.n_groups == 0) {
+    if (X.n_ranks > 0) signal_groups_kernel<<<1, 32, 0, stream>>>(X);
+    return 0;
+  }
   const size_t smem = BootSmem(A.n_metrics, A.max_members, A.max_members > kHistMaxN).total;
   // The kernel's static shared memory, for the opt-in check.
   static size_t static_bytes = [] {
     cudaFuncAttributes attr{};
-    return cudaFuncGetAttributes(&attr, bootstrap_kernel) == cudaSuccess ? attr.sharedSizeBytes : size_t(48 * 1024);
+    return cudaFuncGetAttributes(&attr, bootstrap_kernel<false>) == cudaSuccess ? attr.sharedSizeBytes : size_t(48 * 1024);
   }();
-  static std::atomic<int> limits[kMaxDevices];
-  ensure_dynamic_smem(bootstrap_kernel, static_bytes, smem, limits);
-  bootstrap_kernel<<<A.n_groups, kBootThreads, smem, stream>>>(A);
+  if (X.n_ranks > 0) {
+    static std::atomic<int> limits[kMaxDevices];
+    ensure_dynamic_smem(bootstrap_kernel<true>, static_bytes, smem, limits);
+    bootstrap_kernel<true><<<A.n_groups, kBootThreads, smem, stream>>>(A, X);
+  } else {
+    static std::atomic<int> limits[kMaxDevices];
+    ensure_dynamic_smem(bootstrap_kernel<false>, static_bytes, smem, limits);
+    bootstrap_kernel<false><<<A.n_groups, kBootThreads, smem, stream>>>(A, X);
+  }
   return 0;
 }
 

@@ -16,11 +16,12 @@
 #include <mutex>
 
 #include "pmb200.h"
+#include "pmb200_peer.h"
 #include "pm_capi.h"
 
 namespace pm {
 
-int launch_bootstrap(const BootArgs& A, cudaStream_t stream);
+int launch_bootstrap(const BootArgs& A, cudaStream_t stream, const pm_peer_groups* groups = nullptr);
 int launch_bootstrap_prepare(const BootArgs& A, cudaStream_t stream);
 int prepare_bootstrap_constants(int device);
 size_t bootstrap_scratch_bytes(int n_groups, int max_members, int resamples);

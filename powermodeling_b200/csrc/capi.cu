@@ -16,14 +16,16 @@
 #endif
 
 #include "pmb200.h"
+#include "pmb200_peer.h"
 #include "pm_layout.h"
 #include "pm_capi.h"
 #include "host_pool.h"
 
 namespace pm {
 int launch_analyze(const pm_trials& T, const pm_policy& P, const pm_trial_results& R, int max_covering,
-                   double* gscratch, cudaStream_t stream, size_t* scratch_bytes_needed);
-int launch_bootstrap(const BootArgs& A, cudaStream_t stream);
+                   double* gscratch, cudaStream_t stream, size_t* scratch_bytes_needed,
+                   const pm_peer_rows* rows = nullptr);
+int launch_bootstrap(const BootArgs& A, cudaStream_t stream, const pm_peer_groups* groups = nullptr);
 int launch_bootstrap_prepare(const BootArgs& A, cudaStream_t stream);
 int launch_resample_indices(uint64_t seed, int n, int B, int32_t* out, cudaStream_t stream);
 int prepare_bootstrap_constants(int device);
@@ -285,6 +287,29 @@ int pm_analyze_trials_device(const pm_trials* trials, const pm_policy* policy, p
   return PM_OK;
 }
 
+int pm_analyze_trials_device_exchange(const pm_trials* trials, const pm_policy* policy, pm_trial_results* out,
+                                      void* scratch, size_t scratch_bytes, const pm_peer_rows* rows, void* stream) {
+  if (!rows) return fail(PM_E_INVALID, "NULL rows");
+  if (rows->n_ranks < 1 || rows->n_ranks > PM_MAX_RANKS || rows->rank < 0 || rows->rank >= rows->n_ranks)
+    return fail(PM_E_INVALID, "bad rank geometry");
+  if (rows->row_offset < 0 || rows->epoch == 0 || !rows->done) return fail(PM_E_INVALID, "bad row offset, epoch or counter");
+  for (int r = 0; r < rows->n_ranks; ++r)
+    if (!rows->metrics[r] || !rows->valid[r] || !rows->flags[r]) return fail(PM_E_INVALID, "a rank's buffer is NULL");
+  if (!trials || !policy || !out) return fail(PM_E_INVALID, "NULL argument");
+  if (trials->n_trials < 0 || trials->max_phase_samples < 0) return fail(PM_E_INVALID, "negative size");
+  if (trials->broadcast_columns & ~uint32_t(PM_COL_ALL)) return fail(PM_E_INVALID, "broadcast_columns has unknown bits");
+  if (trials->max_phase_samples > kMaxPhaseSamples) return fail(PM_E_LIMIT, "max_phase_samples beyond %d", kMaxPhaseSamples);
+  if (policy->min_samples < 2) return fail(PM_E_INVALID, "min_samples must be >= 2");
+  const size_t need = analyze_scratch_bytes(trials->n_trials, trials->max_phase_samples);
+  if (need > scratch_bytes || (need && !scratch))
+    return fail(PM_E_INVALID, "analysis needs %zu bytes of device scratch, got %zu", need, scratch_bytes);
+  launch_analyze(*trials, *policy, *out, trials->max_phase_samples, need ? (double*)scratch : nullptr, (cudaStream_t)stream,
+                 nullptr, rows);
+  cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) return cuda_fail(e, "analyze_kernel launch");
+  return PM_OK;
+}
+
 }  // extern "C"
 
 namespace pm {
@@ -513,6 +538,24 @@ int pm_bootstrap_finish_device(const pm_bootstrap_job* job, void* scratch, size_
   int rc = device_boot_args(job, scratch, scratch_bytes, &A);
   if (rc) return rc;
   launch_bootstrap(A, (cudaStream_t)stream);
+  cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) return cuda_fail(e, "bootstrap_kernel launch");
+  return PM_OK;
+}
+
+int pm_bootstrap_finish_device_exchange(const pm_bootstrap_job* job, void* scratch, size_t scratch_bytes,
+                                        const pm_peer_groups* groups, void* stream) {
+  if (!groups) return fail(PM_E_INVALID, "NULL groups");
+  if (groups->n_ranks < 1 || groups->n_ranks > PM_MAX_RANKS || groups->rank < 0 || groups->rank >= groups->n_ranks)
+    return fail(PM_E_INVALID, "bad rank geometry");
+  if (groups->epoch == 0 || !groups->done) return fail(PM_E_INVALID, "bad epoch or counter");
+  for (int r = 0; r < groups->n_ranks; ++r)
+    if (!groups->out[r] || !groups->flags[r]) return fail(PM_E_INVALID, "a rank's buffer is NULL");
+  BootArgs A;
+  int rc = device_boot_args(job, scratch, scratch_bytes, &A);
+  if (rc) return rc;
+  if (groups->per_rank < A.n_groups) return fail(PM_E_INVALID, "per_rank below this rank's group count");
+  launch_bootstrap(A, (cudaStream_t)stream, groups);
   cudaError_t e = cudaGetLastError();
   if (e != cudaSuccess) return cuda_fail(e, "bootstrap_kernel launch");
   return PM_OK;
