@@ -153,13 +153,6 @@ def global_groups(trials: list, world: int):
     return [buckets[k] for k in keys], [A.group_seed(k) for k in keys]
 
 
-def device_view(ptr: int, shape: tuple, typestr: str, torch):
-    """A torch tensor over device memory the library allocated (no copy)."""
-    class _View:
-        __cuda_array_interface__ = {"shape": shape, "typestr": typestr, "data": (ptr, False), "version": 3, "strides": None}
-    return torch.as_tensor(_View(), device="cuda")
-
-
 def device_arrays(packed, torch):
     from powermodeling_b200 import _native as N
     dev = {}
@@ -205,39 +198,11 @@ def run_b200(args, rank: int, world: int) -> dict | None:
     # global row order): by default the analysis kernel stores them into every rank's buffers over
     # NVLink (peer memory, pmb200_peer.h); with --exchange nccl, an all-gather after it.
     peer = world > 1 and args.exchange == "peer"
-    peer_bufs = []
     if peer:
-        gathered_ptrs = []
+        from powermodeling_b200.peer import PeerExchange
         per_rank_groups = -(-len(members) // world)
-        # rows, valid flags, row arrival flags + counter, group results, group arrival flags + counter
-        for nbytes in (world * n * M * 8, world * n, (world + 1) * 4, world * 3 * per_rank_groups * M * 8, (world + 1) * 4):
-            ptr, handle = C.c_void_p(), N.PeerHandle()
-            N.check(lib.pm_peer_alloc(nbytes, C.byref(ptr), C.byref(handle)), "pm_peer_alloc")
-            peer_bufs.append(ptr.value)
-            gathered_ptrs.append((ptr.value, bytes(handle.bytes)))
-        handles: list = [None] * world
-        dist.all_gather_object(handles, [h for _, h in gathered_ptrs])
-        opened = []
-        X, XG = N.PeerRows(), N.PeerGroups()
-        X.n_ranks, X.rank, X.row_offset, X.epoch = world, rank, rank * n, 0
-        XG.n_ranks, XG.rank, XG.per_rank, XG.epoch = world, rank, per_rank_groups, 0
-        for r in range(world):
-            ptrs = []
-            for b, (mine_ptr, _) in enumerate(gathered_ptrs):
-                if r == rank:
-                    ptrs.append(mine_ptr)
-                else:
-                    h = N.PeerHandle()
-                    C.memmove(h.bytes, handles[r][b], 64)
-                    q = C.c_void_p()
-                    N.check(lib.pm_peer_open(C.byref(h), C.byref(q)), "pm_peer_open")
-                    opened.append(q.value)
-                    ptrs.append(q.value)
-            X.metrics[r], X.valid[r], X.flags[r], XG.out[r], XG.flags[r] = ptrs
-        X.done = peer_bufs[2] + world * 4
-        XG.done = peer_bufs[4] + world * 4
-        wait_error = torch.zeros(1, dtype=torch.int32, device="cuda")
-        all_metrics_ptr, all_valid_ptr = peer_bufs[0], peer_bufs[1]
+        px = PeerExchange(rank, world, n, M, per_rank_groups)
+        all_metrics_ptr, all_valid_ptr = px.metrics_ptr, px.valid_ptr
     else:
         all_metrics = torch.empty(world * n * M, dtype=torch.float64, device="cuda") if world > 1 else out["metrics"]
         all_valid = torch.empty(world * n, dtype=torch.uint8, device="cuda") if world > 1 else out["valid"]
@@ -278,29 +243,27 @@ def run_b200(args, rank: int, world: int) -> dict | None:
             N.check(lib.pm_bootstrap_prepare_device(job, boot_scratch, b_scr, side_ptr), "prepare")
         side_ev[1].record(side)
         if peer:
-            X.epoch += 1
+            px.next_epoch()
             N.check(lib.pm_analyze_trials_device_exchange(trials, native_policy, results, C.c_void_p(scratch.data_ptr()),
-                                                          a_scr, C.byref(X), sptr), "analyze + row exchange")
+                                                          a_scr, C.byref(px.rows), sptr), "analyze + row exchange")
         else:
             N.check(lib.pm_analyze_trials_device(trials, native_policy, results, C.c_void_p(scratch.data_ptr()), a_scr, sptr), "analyze")
         ev[1].record(stream)
         if peer:
-            N.check(lib.pm_peer_wait_device(C.c_void_p(peer_bufs[2]), world, X.epoch, 5000, C.c_void_p(wait_error.data_ptr()),
-                                            sptr), "row arrival wait")
+            px.wait_rows(stream.cuda_stream)
         elif world > 1:
             dist.all_gather_into_tensor(all_metrics, out["metrics"])
             dist.all_gather_into_tensor(all_valid, out["valid"])
         ev[2].record(stream)
         stream.wait_event(side_ev[1])
         if peer:
-            XG.epoch += 1
-            N.check(lib.pm_bootstrap_finish_device_exchange(job, boot_scratch, b_scr, C.byref(XG), sptr), "finish + group exchange")
+            N.check(lib.pm_bootstrap_finish_device_exchange(job, boot_scratch, b_scr, C.byref(px.groups), sptr),
+                    "finish + group exchange")
         elif own:
             N.check(lib.pm_bootstrap_finish_device(job, boot_scratch, b_scr, sptr), "finish")
         ev[3].record(stream)
         if peer:
-            N.check(lib.pm_peer_wait_device(C.c_void_p(peer_bufs[4]), world, XG.epoch, 5000, C.c_void_p(wait_error.data_ptr()),
-                                            sptr), "group arrival wait")
+            px.wait_groups(stream.cuda_stream)
         elif world > 1:
             dist.all_gather_into_tensor(all_group_out, group_out)
         ev[4].record(stream)
@@ -310,7 +273,7 @@ def run_b200(args, rank: int, world: int) -> dict | None:
         step()
     torch.cuda.synchronize()
     if peer:
-        gathered = device_view(peer_bufs[3], (world, 3, per_rank_groups, M), "<f8", torch).cpu().numpy()
+        gathered = px.view("groups").cpu().numpy()
     else:
         gathered = (all_group_out if world > 1 else group_out.unsqueeze(0)).cpu().numpy()
     resamples_per_step = int(np.isfinite(gathered[:, 1]).sum()) * RESAMPLES
@@ -397,13 +360,8 @@ def run_b200(args, rank: int, world: int) -> dict | None:
     assert np.array_equal(np.nan_to_num(h_groups[1]), np.nan_to_num(lo_global[local_groups])), \
         "e2e and device paths disagree"
     if peer:
-        torch.cuda.synchronize()
-        assert int(wait_error.item()) == 0, "a rank's rows did not arrive within the wait limit"
-        dist.barrier()                       # every rank is done with every peer buffer
-        for q in opened:
-            N.check(lib.pm_peer_close(C.c_void_p(q)), "pm_peer_close")
-        for q in peer_bufs:
-            N.check(lib.pm_peer_free(C.c_void_p(q)), "pm_peer_free")
+        px.check()
+        px.close()
     h2d = in_bytes + l_off.nbytes + l_rows.nbytes + l_seeds.nbytes + (h_groups.nbytes if world > 1 else 0)
     d2h = sum(a.nbytes for a in h_out.values()) + h_groups.nbytes * (world + 1 if world > 1 else 1)
     if rank != 0:

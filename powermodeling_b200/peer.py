@@ -1,0 +1,132 @@
+"""The sharded summarize's exchanges over NVLink peer memory (include/pmb200_peer.h).
+
+One process per GPU.  ``PeerExchange`` allocates this rank's gathered
+buffers (metric rows and valid flags of every rank's trials; medians and
+interval ends of every rank's groups; arrival flags and counters), swaps
+their CUDA IPC handles over a torch process group, opens the other ranks'
+buffers and fills the ``pm_peer_rows`` / ``pm_peer_groups`` descriptors that
+``pm_analyze_trials_device_exchange`` and ``pm_bootstrap_finish_device_exchange``
+take.  The kernels store straight into every rank's buffers; ``wait_rows`` /
+``wait_groups`` hold a stream until every rank's launch has delivered, each
+wait bounded (an expired wait raises here, after the stream drains).
+
+The exchanges replace the two all-gathers of ``distributed.summarize_sharded``
+(rows before the bootstrap, group results after it).
+"""
+from __future__ import annotations
+
+import ctypes as C
+
+from . import _native as N
+
+
+class PeerExchange:
+    """Gathered row and group buffers of one rank, shared with every other rank.
+
+    rows_per_rank: trials each rank analyses (rank r's trial t is global row
+    r * rows_per_rank + t); groups_per_rank: the group stride of the gathered
+    group buffer ([world][3][groups_per_rank][n_metrics])."""
+
+    def __init__(self, rank: int, world: int, rows_per_rank: int, n_metrics: int, groups_per_rank: int,
+                 group=None, timeout_ms: int = 5000):
+        import torch
+        import torch.distributed as dist
+        if not 1 <= world <= N.MAX_RANKS:
+            raise ValueError(f"world size must be 1..{N.MAX_RANKS}")
+        self.lib = N.library()
+        self.rank, self.world, self.timeout_ms = rank, world, timeout_ms
+        self.rows_per_rank, self.n_metrics, self.groups_per_rank = rows_per_rank, n_metrics, groups_per_rank
+        total_rows = world * rows_per_rank
+        sizes = (total_rows * n_metrics * 8, total_rows, (world + 1) * 4,
+                 world * 3 * max(1, groups_per_rank) * n_metrics * 8, (world + 1) * 4)
+        self.own, self.opened, handles = [], [], []
+        for nbytes in sizes:
+            ptr, handle = C.c_void_p(), N.PeerHandle()
+            N.check(self.lib.pm_peer_alloc(nbytes, C.byref(ptr), C.byref(handle)), "pm_peer_alloc")
+            self.own.append(ptr.value)
+            handles.append(bytes(handle.bytes))
+        everyone: list = [None] * world
+        dist.all_gather_object(everyone, handles, group=group)
+        per_rank = []
+        for r in range(world):
+            if r == rank:
+                per_rank.append(list(self.own))
+                continue
+            ptrs = []
+            for raw in everyone[r]:
+                h, q = N.PeerHandle(), C.c_void_p()
+                C.memmove(h.bytes, raw, 64)
+                N.check(self.lib.pm_peer_open(C.byref(h), C.byref(q)), "pm_peer_open")
+                self.opened.append(q.value)
+                ptrs.append(q.value)
+            per_rank.append(ptrs)
+        self.rows, self.groups = N.PeerRows(), N.PeerGroups()
+        self.rows.n_ranks, self.rows.rank, self.rows.row_offset, self.rows.epoch = world, rank, rank * rows_per_rank, 0
+        self.groups.n_ranks, self.groups.rank, self.groups.per_rank, self.groups.epoch = world, rank, groups_per_rank, 0
+        for r, ptrs in enumerate(per_rank):
+            self.rows.metrics[r], self.rows.valid[r], self.rows.flags[r], self.groups.out[r], self.groups.flags[r] = ptrs
+        self.rows.done = self.own[2] + world * 4
+        self.groups.done = self.own[4] + world * 4
+        self.error = torch.zeros(1, dtype=torch.int32, device="cuda")
+        self._group = group
+
+    # gathered buffers of this rank (device pointers) ----------------------------------------------
+    @property
+    def metrics_ptr(self) -> int:
+        return self.own[0]
+
+    @property
+    def valid_ptr(self) -> int:
+        return self.own[1]
+
+    @property
+    def groups_ptr(self) -> int:
+        return self.own[3]
+
+    def view(self, which: str):
+        """A torch tensor over this rank's gathered 'metrics', 'valid' or 'groups' buffer (no copy)."""
+        import torch
+        total = self.world * self.rows_per_rank
+        shape, typestr, ptr = {
+            "metrics": ((total, self.n_metrics), "<f8", self.own[0]),
+            "valid": ((total,), "|u1", self.own[1]),
+            "groups": ((self.world, 3, max(1, self.groups_per_rank), self.n_metrics), "<f8", self.own[3]),
+        }[which]
+
+        class _View:
+            __cuda_array_interface__ = {"shape": shape, "typestr": typestr, "data": (ptr, False), "version": 3,
+                                        "strides": None}
+        return torch.as_tensor(_View(), device="cuda")
+
+    # one step -----------------------------------------------------------------------------------
+    def next_epoch(self) -> None:
+        """Advance both exchanges to the next step (every launch uses a new epoch)."""
+        self.rows.epoch += 1
+        self.groups.epoch += 1
+
+    def wait_rows(self, stream_ptr: int) -> None:
+        N.check(self.lib.pm_peer_wait_device(C.c_void_p(self.own[2]), self.world, self.rows.epoch, self.timeout_ms,
+                                             C.c_void_p(self.error.data_ptr()), C.c_void_p(stream_ptr)), "row arrival wait")
+
+    def wait_groups(self, stream_ptr: int) -> None:
+        N.check(self.lib.pm_peer_wait_device(C.c_void_p(self.own[4]), self.world, self.groups.epoch, self.timeout_ms,
+                                             C.c_void_p(self.error.data_ptr()), C.c_void_p(stream_ptr)), "group arrival wait")
+
+    def check(self) -> None:
+        """Raise if any wait expired (synchronizes the device)."""
+        import torch
+        torch.cuda.synchronize()
+        if int(self.error.item()):
+            raise N.NativeError("a rank's rows or groups did not arrive within the wait limit")
+
+    def close(self) -> None:
+        """Release the buffers (a barrier first: no rank may still be storing into them)."""
+        import torch
+        import torch.distributed as dist
+        torch.cuda.synchronize()
+        dist.barrier(group=self._group)
+        for q in self.opened:
+            N.check(self.lib.pm_peer_close(C.c_void_p(q)), "pm_peer_close")
+        for q in self.own:
+            N.check(self.lib.pm_peer_free(C.c_void_p(q)), "pm_peer_free")
+        self.opened, self.own = [], []
