@@ -268,6 +268,9 @@ def run_b200(args, rank: int, world: int) -> dict | None:
             dist.all_gather_into_tensor(all_group_out, group_out)
         ev[4].record(stream)
 
+    if world > 1:
+        torch.cuda.synchronize()
+        dist.barrier()                                  # every rank launches its first step together
     for _ in range(args.warmup):
         flush.zero_()
         step()
@@ -377,9 +380,9 @@ def run_b200(args, rank: int, world: int) -> dict | None:
             "config": {"workload": WORKLOAD, "points": POINTS * world, "points_per_gpu": POINTS, "repeats": REPEATS,
                        "trials": n * world, "groups": G,
                        "resamples": RESAMPLES, "samples": packed.n_samples, "l2": "flushed (256 MiB write) between steps",
-                       "parallelism": (f"sweep-sharded x{world}: trials and groups per rank; metric rows stored into "
-                                       f"every rank by the analysis kernel over NVLink peer memory, group results "
-                                       f"all-gathered over NCCL" if peer else
+                       "parallelism": (f"sweep-sharded x{world}: trials and groups per rank; metric rows and group "
+                                       f"results stored into every rank by the analysis and bootstrap kernels over "
+                                       f"NVLink peer memory" if peer else
                                        f"sweep-sharded x{world}: trials and groups per rank, rows and group results "
                                        f"all-gathered over NCCL") if world > 1 else "single GPU"},
             "e2e": {"value": resamples_per_step / e2e_s, "unit": "resamples/s",
