@@ -582,6 +582,7 @@ def run_arms(local: int, peaks: dict) -> dict:
                  "--sfu-lanes", str(sms * 8 * 256), "--sfu-chains", "4", "--iterations", "65536", "--batch-launches", "1",
                  "--fixed-batches", "4", *ARM_QUICK])
     out["sfu_ex2"] = {"ops_s": r["throughput_ops_s"], "checksum": r["checksum"]}
+    out["nonlinear"] = run_nonlinear_arms(sms, peaks)
     clock = clocks.stop()
     out["telemetry"] = run_telemetry_arm(device["uuid"])
     mem_mhz = clock.get("mem_mhz") or device["nominal_max_memory_clock_khz"] / 1e3
@@ -599,6 +600,37 @@ def run_arms(local: int, peaks: dict) -> dict:
     out["tensor_best_frac_of_measured_bf16_gemm"] = best / peaks.get("bf16_tflops", 1590.0)
     out["sfu_ex2"]["ops_per_sm_per_clock"] = out["sfu_ex2"]["ops_s"] / (sms * sm_mhz * 1e6)
     out["clocks"] = clock
+    return out
+
+
+NONLINEAR_ELEMENTS = 1 << 28          # 1 GiB of fp32 input, 1 GiB of output: far above the 126 MB L2
+NONLINEAR_ROW_WIDTH = 1024            # the reference's default row width
+
+
+def run_nonlinear_arms(sms: int, peaks: dict) -> dict:
+    """The complete FP32 nonlinear functions through powerbench at HBM scale.
+
+    Each arm: 2^28 inputs, fixed grid of 8 CTAs x 256 threads per SM, one
+    application per launch, 8 launches per batch.  ``logical_gbs`` is the
+    reference's count (8 B per element pointwise, 16 B row-wise: x read two
+    or three times); ``hbm_gbs`` counts what the algorithm must move, x once
+    and y once (8 B per element; RMSNorm's gamma row stays in L2), against the
+    measured copy peak."""
+    hbm = peaks.get("hbm_gbs", 6650.0)
+    out = {}
+    for fn in ("exp", "tanh", "silu", "rmsnorm", "softmax"):
+        args = ["--workload", fn, "--nonlinear-mode", "streaming", "--grid-mode", "fixed", "--blocks", str(sms * 8),
+                "--threads", "256", "--working-set-bytes", str(NONLINEAR_ELEMENTS * 4), "--iterations", "1",
+                "--batch-launches", "8", "--fixed-batches", "6", *ARM_QUICK]
+        if fn in ("rmsnorm", "softmax"):
+            args += ["--row-width", str(NONLINEAR_ROW_WIDTH)]
+        _, r = _arm(args)
+        algorithmic = r["elements"] * 8 / r["duration_s"] / 1e9
+        out[fn] = {"elements_s": r["throughput_ops_s"], "logical_gbs": r["throughput_bytes_s"] / 1e9,
+                   "hbm_gbs": algorithmic, "frac_of_measured_copy_peak": algorithmic / hbm,
+                   "validation_passed": r["sanity"]["numerical_validation_passed"], "checksum": r["checksum"],
+                   "ms_per_launch": r["duration_s"] / r["kernel_launches"] * 1e3,
+                   "config": f"2^28 fp32 inputs, grid {sms}x8x256" + (f", rows of {NONLINEAR_ROW_WIDTH}" if fn in ("rmsnorm", "softmax") else "")}
     return out
 
 

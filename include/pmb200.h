@@ -287,6 +287,24 @@ int pm_tensor_probe(int accumulators, uint64_t iterations, int uniform, uint64_t
 size_t pm_bootstrap_static_scratch_capacity(void);
 int pm_group_bootstrap_device_static(const pm_bootstrap_job* job, void* stream);
 
+/*
+ * The complete FP32 nonlinear functions of the powerbench
+ * exp|tanh|silu|rmsnorm|softmax workloads on caller device buffers (the
+ * reference's cuda/nonlinear.cuh: init_nonlinear 5-14, pointwise_nonlinear_kernel
+ * 23-38, row_nonlinear_kernel 59-89, launched as gpu_bench.cu:796-801).
+ * pm_nonlinear_fill_device writes n inputs ((int(w & 0xffff) - 32768) / 8192 +
+ * shift) or, with gamma != 0, RMSNorm weights (0.75 + (w & 0xffff) / 131072),
+ * w = splitmix64 finaliser of (i ^ seed) truncated to 32 bits.
+ * pm_nonlinear_apply_device applies `function` `iterations` times to n inputs
+ * on a blocks x threads grid (softmax/RMSNorm: rows of row_width, one row per
+ * block, grid-stride over rows; pointwise: row_width 0).  Buffers are 16-byte
+ * aligned; gamma (row_width floats) is read by RMSNorm only.
+ */
+enum { PM_NL_EXP = 0, PM_NL_TANH = 1, PM_NL_SILU = 2, PM_NL_SOFTMAX = 3, PM_NL_RMSNORM = 4 };
+int pm_nonlinear_fill_device(float* data, uint64_t n, uint64_t seed, float shift, int gamma, void* stream);
+int pm_nonlinear_apply_device(int32_t function, const float* input, const float* gamma, float* output, uint64_t n,
+                              int32_t row_width, uint64_t iterations, int32_t blocks, int32_t threads, void* stream);
+
 /* Raw resample index stream of random.Random(seed).choices(range(n), k=n),
  * repeated `resamples` times: out[r*n + j] (host buffer). Pins the generator. */
 int pm_resample_indices(uint64_t seed, int32_t n, int32_t resamples, int32_t* out);

@@ -172,6 +172,9 @@ def library() -> C.CDLL:
             lib.pm_peer_wait_device.argtypes = [_p, C.c_int32, C.c_uint32, C.c_uint32, _p, _p]
             lib.pm_bootstrap_finish_device_exchange.argtypes = [C.POINTER(BootstrapJob), _p, C.c_size_t,
                                                                 C.POINTER(PeerGroups), _p]
+            lib.pm_nonlinear_fill_device.argtypes = [_p, C.c_uint64, C.c_uint64, C.c_float, C.c_int, _p]
+            lib.pm_nonlinear_apply_device.argtypes = [C.c_int32, _p, _p, _p, C.c_uint64, C.c_int32, C.c_uint64,
+                                                      C.c_int32, C.c_int32, _p]
             _lib = lib
     return _lib
 

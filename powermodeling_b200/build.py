@@ -25,6 +25,11 @@ COMMON = ["-std=c++17", "-O3", "-lineinfo", "--fmad=false", "-Xcompiler", "-fPIC
           "-I" + str(INCLUDE), "-I" + str(CSRC)]
 
 
+# Compiled with contraction on, as the reference's nonlinear kernels are: the
+# pointwise functions then round exactly as the reference's do.
+FMAD_DEFAULT = {"nonlinear.cu"}
+
+
 def nvcc() -> str:
     path = shutil.which("nvcc") or "/usr/local/cuda/bin/nvcc"
     if not Path(path).exists():
@@ -56,7 +61,8 @@ def build(verbose: bool = False, jobs: int | None = None) -> Path:
         objects.append(obj)
         if _stale(obj, src, headers):
             extra = ARCH if src.suffix == ".cu" else []
-            commands.append([nvcc(), *COMMON, *extra, "-c", str(src), "-o", str(obj)])
+            flags = [f for f in COMMON if f != "--fmad=false"] if src.name in FMAD_DEFAULT else COMMON
+            commands.append([nvcc(), *flags, *extra, "-c", str(src), "-o", str(obj)])
     procs = []
     limit = jobs or max(1, min(8, os.cpu_count() or 1))
     for cmd in commands:

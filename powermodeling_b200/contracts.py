@@ -1,14 +1,12 @@
 """Count contracts that a workload record must satisfy to be analysed.
 
-Restates the reference's powermodeling/sfu.py:count_issues (sfu.py:23-115)
-and powermodeling/memory.py:count_issues (memory.py:114-144): the issues a
+Restates the reference's powermodeling/sfu.py:count_issues (sfu.py:23-115),
+powermodeling/memory.py:count_issues (memory.py:114-144) and
+powermodeling/nonlinear.py:count_issues (nonlinear.py:22-128): the issues a
 powerbench ``result`` (or ``active_reference_result``) record raises when its
 reported counts disagree with its own launch geometry.  libpmb200's workload
 front end emits records that pass these checks; analyze_trial applies them.
-
-The legacy streaming nonlinear functions (nonlinear.py) are outside this
-library's scope: their records are reported with the single issue
-``nonlinear_contract_not_evaluated`` instead of being silently accepted.
+The issue strings are the reference's, since analysis output carries them.
 """
 from __future__ import annotations
 
@@ -167,5 +165,140 @@ def memory_count_issues(benchmark, workload) -> list[str]:
     return issues
 
 
+NONLINEAR_ROW_WORKLOADS = {"rmsnorm", "softmax"}
+NONLINEAR_STREAMING_MATH = "cuda_fp32_standard_streaming_v1"
+NONLINEAR_Q_GRID_MATH = "cuda_fp32_q_grid_v2"
+NONLINEAR_Q_GRID_VERSION = "fp32_complete_nonlinear_q_grid_v2"
+NONLINEAR_COUNT_SOURCE = "synchronized_completed_launches"
+RMS_EPSILON = 1e-5
+
+
+def nonlinear_bytes_per_element(workload) -> int:
+    """Logical bytes of one output element: RMSNorm reads x twice, gamma once and writes y;
+    softmax reads x three times and writes y (nonlinear.py:17-19)."""
+    return 16 if workload in NONLINEAR_ROW_WORKLOADS else 8
+
+
 def nonlinear_count_issues(benchmark, workload) -> list[str]:
-    return ["nonlinear_contract_not_evaluated"] if workload in NONLINEAR_WORKLOADS else []
+    """Denominator checks of a complete-nonlinear-function record (nonlinear.py:22-128).
+
+    An element is one output value (a whole row reduction included for RMSNorm
+    and softmax).  Q-grid records (cuda_fp32_q_grid_v2) must account for every
+    completed launch: launches x Q x iterations elements, launches x blocks
+    CTAs, per epoch and in total; older records are checked per admitted block.
+    """
+    if workload not in NONLINEAR_WORKLOADS:
+        return []
+    row = workload in NONLINEAR_ROW_WORKLOADS
+    per_element = nonlinear_bytes_per_element(workload)
+    issues: list[str] = []
+
+    def count(key, obj=benchmark):
+        v = obj.get(key)
+        if isinstance(v, bool) or not isinstance(v, (int, float)) or not math.isfinite(v) or v < 0 or v != int(v):
+            issues.append("invalid_nonlinear_count:" + key)
+            return None
+        return v
+
+    def agree(name, actual, expected):
+        if actual is None or expected is None or not math.isclose(actual, expected, rel_tol=1e-9, abs_tol=1e-6):
+            issues.append("nonlinear_count_disagreement:" + name)
+
+    def times(*values):
+        out = 1
+        for v in values:
+            if v is None:
+                return None
+            out *= v
+        return out
+
+    elements, operations = count("elements"), count("operations")
+    if elements is not None and elements <= 0:
+        issues.append("missing_nonlinear_elements")
+    agree("operations_are_elements", operations, elements)
+    agree("logical_bytes", count("logical_bytes"), times(elements, per_element))
+    width = count("row_width")
+    if row:
+        if width is None or not 1 <= width <= 65536 or width != int(width):
+            issues.append("invalid_nonlinear_row_width")
+        agree("row_evaluations", count("row_evaluations"), elements / width if elements is not None and width else None)
+    else:
+        agree("row_width", width, 0)
+        agree("row_evaluations", count("row_evaluations"), 0)
+    blocks, ws, iterations, admitted = (count(k) for k in ("blocks", "working_set_bytes", "iterations_per_launch",
+                                                             "admitted_blocks"))
+    math_tag, version = benchmark.get("math_implementation"), benchmark.get("kernel_implementation_version")
+    q_grid = math_tag == NONLINEAR_Q_GRID_MATH or version == NONLINEAR_Q_GRID_VERSION
+    launches = batch_launches = q = None
+    if q_grid:
+        if math_tag != NONLINEAR_Q_GRID_MATH or version != NONLINEAR_Q_GRID_VERSION:
+            issues.append("unsupported_nonlinear_q_grid_implementation")
+        if benchmark.get("block_completion_count_source") != NONLINEAR_COUNT_SOURCE:
+            issues.append("unsupported_nonlinear_block_completion_count_source")
+        q, threads, launches = count("input_elements"), count("threads"), count("kernel_launches")
+        if "batch_launches" in benchmark:
+            batch_launches = count("batch_launches")
+            if not batch_launches:
+                issues.append("invalid_nonlinear_batch_launches")
+        if "batches" in benchmark:
+            agree("completed_batch_kernel_launches", launches, times(count("batches"), batch_launches))
+        if ws is None or ws <= 0 or ws % 4:
+            issues.append("invalid_nonlinear_input_word_alignment")
+        agree("input_elements", q, ws / 4 if ws is not None else None)
+        if q is None or q <= 0 or (width and row and q % width):
+            issues.append("incomplete_nonlinear_input_or_row")
+        if threads is None or not 32 <= threads <= 1024 or threads % 32:
+            issues.append("invalid_nonlinear_threads")
+        mode = benchmark.get("grid_mode")
+        if mode not in ("auto", "fixed"):
+            issues.append("invalid_nonlinear_grid_mode")
+        elif mode == "auto" and q and threads and (not row or width):
+            agree("auto_grid_blocks", blocks, q / width if row else math.ceil(q / threads))
+        if not blocks or blocks > 1000000 or not iterations or not launches:
+            issues.append("missing_nonlinear_execution_counts")
+        if launches is not None and blocks is not None:
+            agree("completed_launch_admissions", admitted, launches * blocks)
+        agree("completed_launch_elements", elements, times(launches, q, iterations))
+    elif blocks and ws and iterations and admitted:
+        # Contiguous per-CTA slices of the first streaming implementation.
+        agree("admission_elements", elements, admitted * (ws / 4 / blocks) * iterations)
+        if ws % (4 * blocks * (width if row and width else 1)):
+            issues.append("incomplete_nonlinear_block_slice_or_row")
+    else:
+        issues.append("missing_nonlinear_execution_counts")
+    if math_tag not in (NONLINEAR_STREAMING_MATH, NONLINEAR_Q_GRID_MATH) or benchmark.get("input_precision") != "fp32":
+        issues.append("unsupported_nonlinear_math_contract")
+    if workload == "rmsnorm" and (benchmark.get("rms_epsilon") != RMS_EPSILON or benchmark.get("affine_gamma") is not True):
+        issues.append("unsupported_rmsnorm_definition")
+    if (benchmark.get("sanity") or {}).get("numerical_validation_passed") is not True:
+        issues.append("nonlinear_numerical_validation_failed_or_missing")
+    checked = (benchmark.get("numerical_validation") or {}).get("checked_values")
+    if isinstance(checked, bool) or not isinstance(checked, (int, float)) or not math.isfinite(checked) or checked <= 0:
+        issues.append("missing_nonlinear_numerical_reference_checks")
+    epochs = benchmark.get("measure_epochs")
+    if not isinstance(epochs, list) or not epochs:
+        issues.append("missing_nonlinear_measure_epochs")
+        return sorted(set(issues))
+    for epoch in epochs:
+        if not isinstance(epoch, dict):
+            issues.append("invalid_nonlinear_epoch")
+            continue
+        e = count("elements", epoch)
+        agree("epoch_operations_are_elements", count("operations", epoch), e)
+        agree("epoch_logical_bytes", count("logical_bytes", epoch), times(e, per_element))
+        agree("epoch_rows", count("row_evaluations", epoch), e / width if e is not None and width and row else 0)
+        if q_grid:
+            epoch_launches = count("kernel_launches", epoch)
+            if "batches" in epoch:
+                agree("epoch_completed_batch_kernel_launches", epoch_launches, times(count("batches", epoch), batch_launches))
+            agree("epoch_completed_launch_admissions", count("admitted_blocks", epoch), times(epoch_launches, blocks))
+            agree("epoch_completed_launch_elements", e, times(epoch_launches, q, iterations))
+        if epoch.get("counts_exact") is not True:
+            issues.append("inexact_nonlinear_measure_epoch")
+
+    def total(key):
+        return sum(ep.get(key, 0) for ep in epochs if isinstance(ep, dict) and isinstance(ep.get(key), (int, float)))
+    agree("epoch_total_elements", total("elements"), elements)
+    if q_grid:
+        agree("epoch_total_kernel_launches", total("kernel_launches"), launches)
+    return sorted(set(issues))

@@ -120,6 +120,9 @@ struct Options {
   int sfu_chains = 4;
   int vector_bytes = 4;            // 4: scalar reference access; 16: one uint4 per access
   std::string chase_granularity = "word";
+  std::string nonlinear_mode;      // "streaming" opts in to the complete nonlinear functions
+  int row_width = 0;               // RMSNorm/softmax row width (default 1024)
+  bool nonlinear_mode_explicit = false;
   bool tensor_uniform = false;     // fp16 operands uniform[-1,1) instead of [-0.25,0.25)
   std::vector<unsigned> sm_ids;
   bool describe = false, profile_region = false, paired_reference = false;
@@ -151,13 +154,16 @@ double parse_seconds(const std::string& v, const char* flag) {
 const char* kUsage =
   "powerbench --describe [--device N]\n"
   "powerbench --workload tensor|gemm|l1|l2|l2_latency|hbm|control|sfu_ex2|sfu_lg2|sfu_rcp|sfu_rsqrt|sfu_sqrt|sfu_tanh [options]\n"
+  "powerbench --workload exp|tanh|silu|rmsnorm|softmax --nonlinear-mode streaming [--row-width 1024] [options]\n"
   "  --device N --seconds 10 --warmup-seconds 3 --idle-seconds 6\n"
   "  --blocks N --threads 256 --iterations N --tensor-accumulators 1..8\n"
   "  --batch-launches N --fixed-batches N --warmup-batches N --profile-region\n"
   "  --paired-reference --reference-order AB|BA\n"
   "  --working-set-bytes N --stride-words N (alias --stride-elements) --offset-bytes N\n"
   "  --access read|write|copy --sm-ids 0,1,... --seed N --read-cache-policy auto|ca|cg|cs\n"
-  "  --gemm-m 4096 --gemm-n 4096 --gemm-k 4096 --grid-mode auto|fixed --sfu-lanes N --sfu-chains 1|4|8\n"
+  "  --gemm-m 4096 --gemm-n 4096 --gemm-k 4096 --grid-mode auto|fixed (nonlinear/SFU) --sfu-lanes N --sfu-chains 1|4|8\n"
+  "  --nonlinear-mode streaming (required opt-in for complete exp/tanh/silu/rmsnorm/softmax)\n"
+  "  --row-width N (RMSNorm/softmax row width, 1..65536, default 1024)\n"
   "  --memory-vector-bytes 4|16 (16: one 16-byte access per thread and iteration)\n"
   "  --chase-granularity word|line (line: 64-bit links on 128-byte lines)\n"
   "  --tensor-input uniform (fp16 operands uniform in [-1,1))\n"
@@ -204,8 +210,11 @@ Options parse_options(int argc, const char* const* argv, const Sink& out, bool* 
     else if (flag == "--memory-vector-bytes") o.vector_bytes = parse_int(v, f);
     else if (flag == "--chase-granularity") o.chase_granularity = v;
     else if (flag == "--tensor-input") { if (v != "uniform" && v != "reference") throw Failure("--tensor-input must be uniform or reference"); o.tensor_uniform = v == "uniform"; }
-    else if (flag == "--nonlinear-mode" || flag == "--row-width")
-      throw Failure("complete streaming nonlinear functions are not part of this build; use the sfu_* register workloads");
+    else if (flag == "--nonlinear-mode") { o.nonlinear_mode = v; o.nonlinear_mode_explicit = true; }
+    else if (flag == "--row-width") {
+      o.row_width = parse_int(v, f);
+      if (!o.row_width) throw Failure("--row-width must be positive");
+    }
     else if (flag == "--sm-ids") {
       std::stringstream ss(v);
       std::string item;
@@ -243,19 +252,29 @@ Options parse_options(int argc, const char* const* argv, const Sink& out, bool* 
   if (o.offset_bytes % 4 || o.working_set_bytes % 4) throw Failure("memory offset/footprint must be multiples of 4 bytes");
   if (o.iterations > (1ULL << 32)) throw Failure("--iterations must be <= 2^32");
   if (o.batch_launches > 65536) throw Failure("--batch-launches must be <= 65536");
-  const bool known = o.workload == "tensor" || o.workload == "gemm" || memory || o.workload == "l2_latency" || o.workload == "control" || is_sfu(o.workload);
-  if (is_nonlinear(o.workload))
-    throw Failure("complete streaming nonlinear functions are not part of this build; use the sfu_* register workloads");
+  const bool nonlinear = is_nonlinear(o.workload);
+  const bool known = o.workload == "tensor" || o.workload == "gemm" || memory || o.workload == "l2_latency" || o.workload == "control" ||
+                     is_sfu(o.workload) || nonlinear;
   if (!known) throw Failure("unknown workload " + o.workload);
+  if (nonlinear && o.nonlinear_mode != "streaming")
+    throw Failure("complete nonlinear functions require explicit --nonlinear-mode streaming; these include global I/O and supporting arithmetic/reductions; use sfu_* workloads for SFU-only experiments (EXP is not EX2)");
+  if (!nonlinear && o.nonlinear_mode_explicit)
+    throw Failure("--nonlinear-mode streaming applies only to complete exp/tanh/silu/rmsnorm/softmax workloads");
   if (o.access != "read" && o.access != "write" && o.access != "copy") throw Failure("unknown memory access " + o.access);
   if (o.workload == "l1" && o.access != "read") throw Failure("L1 global-store/copy attribution is unsupported; use L1 read");
   if (o.workload == "l2_latency" && o.access != "read") throw Failure("dependent latency probes support read only");
   if (o.workload == "l2_latency" && o.stride != 1) throw Failure("latency probes use randomized dependent links; --stride-elements must be 1");
   if (o.workload == "gemm" && !o.sm_ids.empty()) throw Failure("cuBLAS GEMM cannot honor --sm-ids");
   if (o.gemm_m <= 0 || o.gemm_n <= 0 || o.gemm_k <= 0) throw Failure("GEMM dimensions must be positive");
+  const bool rowwise = o.workload == "rmsnorm" || o.workload == "softmax";
+  if (rowwise && !o.row_width) o.row_width = 1024;
+  if ((rowwise && o.row_width > 65536) || (!rowwise && o.row_width))
+    throw Failure("--row-width 1..65536 applies only to RMSNorm/Softmax");
+  if (nonlinear && (!o.sm_ids.empty() || o.offset_bytes || o.stride != 1 || o.access != "read"))
+    throw Failure("nonlinear workloads require a full grid, offset=0, stride=1 and access=read");
   if (o.grid_mode != "auto" && o.grid_mode != "fixed") throw Failure("--grid-mode must be auto or fixed");
-  if (o.grid_mode_explicit && !is_sfu(o.workload)) throw Failure("--grid-mode applies only to nonlinear/SFU workloads");
-  if (is_sfu(o.workload) && o.grid_mode == "fixed" && (!o.blocks_explicit || o.blocks <= 0))
+  if (o.grid_mode_explicit && !is_sfu(o.workload) && !nonlinear) throw Failure("--grid-mode applies only to nonlinear/SFU workloads");
+  if ((is_sfu(o.workload) || nonlinear) && o.grid_mode == "fixed" && (!o.blocks_explicit || o.blocks <= 0))
     throw Failure("fixed nonlinear/SFU grid requires explicit positive --blocks");
   if (!o.sfu_lanes || (o.sfu_chains != 1 && o.sfu_chains != 4 && o.sfu_chains != 8))
     throw Failure("--sfu-lanes must be positive and --sfu-chains must be 1, 4 or 8");
@@ -588,6 +607,223 @@ void experiment_sfu(Options o, const cudaDeviceProp& p, const Sink& out) {
   if (!numerical.passed) throw Failure("native SFU one-step output failed CPU double validation after measurement");
 }
 
+// ---------------------------------------------------------------- nonlinear arms
+int nonlinear_fn(const std::string& w) {
+  return w == "exp" ? NL_EXP : w == "tanh" ? NL_TANH : w == "silu" ? NL_SILU : w == "softmax" ? NL_SOFTMAX : NL_RMSNORM;
+}
+
+struct NonlinearCheck { uint64_t checked = 0, checksum = 0; double max_abs = 0, max_rel = 0; bool passed = true; };
+
+// Sampled CPU double check of the device outputs (nonlinear.cuh:97-143 rule):
+// up to eight items (elements, or whole rows for softmax/RMSNorm) at the
+// global first, middle, last and evenly spread positions; |y - e| <= 2e-6 +
+// 2e-4 |e|; softmax rows must also sum to 1 within 2e-4.  The checksum folds
+// the checked output bits in order (h = h * 1315423911 + bits).
+NonlinearCheck check_nonlinear(const Options& o, int fn, const float* in, const float* outp, const float* gamma,
+                               uint64_t q) {
+  NonlinearCheck r;
+  const bool rowwise = fn == NL_SOFTMAX || fn == NL_RMSNORM;
+  const uint64_t width = rowwise ? uint64_t(o.row_width) : 1;
+  const uint64_t items = q / width, samples = std::min<uint64_t>(items, 8);
+  std::vector<float> weights(width, 1.0f), x(width), y(width);
+  if (fn == NL_RMSNORM) check(cudaMemcpy(weights.data(), gamma, width * 4, cudaMemcpyDeviceToHost), "cudaMemcpy");
+  auto compare = [&](float actual, double expected) {
+    const double err = std::fabs(double(actual) - expected), rel = err / std::max(std::fabs(expected), 1e-30);
+    r.max_abs = std::max(r.max_abs, err);
+    r.max_rel = std::max(r.max_rel, rel);
+    r.passed = r.passed && std::isfinite(actual) && std::isfinite(expected) && err <= 2e-6 + 2e-4 * std::fabs(expected);
+    uint32_t bits;
+    memcpy(&bits, &actual, 4);
+    r.checksum = r.checksum * 1315423911ULL + bits;
+    ++r.checked;
+  };
+  for (uint64_t k = 0; k < samples; ++k) {
+    const uint64_t item = samples == 1 ? 0 : k == samples / 2 ? items / 2 : k * (items - 1) / (samples - 1);
+    check(cudaMemcpy(x.data(), in + item * width, width * 4, cudaMemcpyDeviceToHost), "cudaMemcpy");
+    check(cudaMemcpy(y.data(), outp + item * width, width * 4, cudaMemcpyDeviceToHost), "cudaMemcpy");
+    if (!rowwise) {
+      const double v = x[0];
+      compare(y[0], fn == NL_EXP ? std::exp(v) : fn == NL_TANH ? std::tanh(v) : v / (1.0 + std::exp(-v)));
+      continue;
+    }
+    const double maximum = *std::max_element(x.begin(), x.end());
+    double sum = 0, ysum = 0;
+    for (float v : x) sum += fn == NL_SOFTMAX ? std::exp(double(v) - maximum) : double(v) * v;
+    for (uint64_t c = 0; c < width; ++c) {
+      const double e = fn == NL_SOFTMAX ? std::exp(double(x[c]) - maximum) / sum
+                                        : double(x[c]) / std::sqrt(sum / double(width) + double(1e-5f)) * weights[c];
+      compare(y[c], e);
+      ysum += y[c];
+    }
+    if (fn == NL_SOFTMAX) r.passed = r.passed && std::fabs(ysum - 1.0) <= 2e-4;
+  }
+  return r;
+}
+
+// The exp|tanh|silu|rmsnorm|softmax arms (gpu_bench.cu:611-631, 712-716,
+// 796-818, 857-911, 930-933, 976-984, 1030-1176 for these workloads): Q =
+// working-set bytes / 4 input elements; the auto grid is ceil(Q / threads)
+// blocks (pointwise) or one block per row; completed CTAs and elements follow
+// from synchronized launch counts (no per-CTA admission counters).
+void experiment_nonlinear(Options o, const cudaDeviceProp& p, const Sink& out) {
+  const int fn = nonlinear_fn(o.workload);
+  const bool rowwise = fn == NL_SOFTMAX || fn == NL_RMSNORM;
+  if (o.threads > p.maxThreadsPerBlock) throw Failure("thread count exceeds this device limit");
+  if (!o.working_set_bytes) o.working_set_bytes = uint64_t(1048576) * 4;
+  const uint64_t requested_ws = o.working_set_bytes;
+  const uint64_t q = o.working_set_bytes / 4;
+  if (!q || (rowwise && q % uint64_t(o.row_width)))
+    throw Failure("nonlinear Q must be positive; rowwise Q must contain complete rows");
+  if (o.grid_mode == "auto") {
+    const uint64_t derived = rowwise ? q / uint64_t(o.row_width) : (q + o.threads - 1) / o.threads;
+    if (derived > 1000000 || derived > uint64_t(p.maxGridSize[0]))
+      throw Failure("nonlinear auto grid exceeds practical/hardware block limit; use explicit fixed grid for grid-stride traversal");
+    if (o.blocks_explicit && uint64_t(o.blocks) != derived)
+      throw Failure("explicit --blocks must equal the Q-derived auto grid; use --grid-mode fixed for a block sweep");
+    o.blocks = int(derived);
+  }
+  if (o.blocks <= 0 || o.blocks > 1000000 || o.blocks > p.maxGridSize[0])
+    throw Failure("--blocks must be positive within practical/hardware limit");
+  if (!o.iterations) o.iterations = 1;
+  if (!o.batch_launches) o.batch_launches = 16;
+  const uint64_t lanes = uint64_t(o.blocks) * o.threads;
+  const bool context = o.paired_reference, paired = context && !o.profile_region;
+  const uint64_t gamma_count = fn == NL_RMSNORM ? uint64_t(o.row_width) : 1;
+  if ((long double)q * 8 + gamma_count * 4 + 4 + (context ? lanes : 1) * 4 + 262144 > (long double)p.totalGlobalMem * 0.7)
+    throw Failure("nonlinear input/output/gamma and reference allocations exceed 70% of device memory");
+  const int width = rowwise ? o.row_width : 0;
+  DevBuf<float> input(q), output(q), gamma(gamma_count);
+  DevBuf<uint32_t> ref_sink(context ? lanes : 1);
+  // Large-offset logits exercise max-subtracted softmax without overflow (gpu_bench.cu:712-716).
+  check(launch_nonlinear_fill(input.p, q, o.seed, fn == NL_SOFTMAX ? 100.0f : 0.0f, 0, p.multiProcessorCount, 0), "fill");
+  check(launch_nonlinear_fill(gamma.p, gamma_count, o.seed ^ 12345ULL, 0.0f, 1, p.multiProcessorCount, 0), "fill");
+  check(cudaMemset(output.p, 0, q * 4), "cudaMemset");
+  check(cudaMemset(ref_sink.p, 0, (context ? lanes : 1) * 4), "cudaMemset");
+  check(cudaDeviceSynchronize(), "fill kernels");
+  auto single = [&] {
+    check(launch_nonlinear(fn, input.p, gamma.p, output.p, q, width, o.iterations, o.blocks, o.threads, 0), "nonlinear launch");
+  };
+  auto treat = [&] { for (int k = 0; k < o.batch_launches; ++k) single(); };
+  auto ref = [&] {
+    for (int k = 0; k < o.batch_launches; ++k)
+      check(launch_control_plain(ref_sink.p, o.iterations, o.blocks, o.threads, 0), "control launch");
+  };
+  single();
+  check(cudaDeviceSynchronize(), "nonlinear kernel");
+  NonlinearCheck numerical = check_nonlinear(o, fn, input.p, output.p, gamma.p, q);
+  if (!numerical.passed) throw Failure("nonlinear output differs from CPU double reference before measurement");
+  const size_t smem = nonlinear_dynamic_smem(fn, width);
+  cudaFuncAttributes attr{};
+  int max_blocks = 0;
+  check(cudaFuncGetAttributes(&attr, nonlinear_kernel(fn, width)), "cudaFuncGetAttributes");
+  check(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&max_blocks, nonlinear_kernel(fn, width), o.threads, smem), "occupancy");
+  out.line(protocol_json(o, paired, context, true, "issue_loop",
+                         "paired integer issue-loop operational contrast; launch geometry, iterations and batching match the nonlinear kernel; instruction mix, residency, register pressure, occupancy and duration per launch are not counterfactual equivalents; not isolated component energy"));
+  run_phase(out, "warmup", o.warmup_seconds, o.warmup_batches, treat);
+  idle_phase(out, "idle_pre", o.idle_seconds);
+  Timing t, rt;
+  std::function<uint64_t()> none = [] { return uint64_t(0); };
+  auto treatment_arm = [&] {
+    if (paired) run_phase(out, "warmup_treatment", o.warmup_seconds, o.warmup_batches, treat);
+    t = run_phase(out, "measure", o.seconds, o.fixed_batches, treat, none, o.profile_region);
+  };
+  auto reference_arm = [&] {
+    run_phase(out, "warmup_reference", o.warmup_seconds, o.warmup_batches, ref);
+    rt = run_phase(out, "active_reference", o.seconds, o.fixed_batches, ref, none);
+  };
+  if (paired && o.reference_order == "AB") reference_arm();
+  treatment_arm();
+  if (paired && o.reference_order == "BA") reference_arm();
+  idle_phase(out, "idle_post", o.idle_seconds);
+  for (Timing* tm : {&t, &rt})
+    for (Epoch& e : tm->epochs) { e.admitted = e.batches * uint64_t(o.batch_launches) * uint64_t(o.blocks); e.readback_ns = 0; }
+  const NonlinearCheck post = check_nonlinear(o, fn, input.p, output.p, gamma.p, q);
+  numerical.checked += post.checked;
+  numerical.max_abs = std::max(numerical.max_abs, post.max_abs);
+  numerical.max_rel = std::max(numerical.max_rel, post.max_rel);
+  numerical.passed = numerical.passed && post.passed;
+  const uint64_t bytes_per_element = rowwise ? 16 : 8;
+  const std::string distribution = fn == NL_SOFTMAX ? "deterministic uniform FP32 [96,104); stable max subtraction"
+                                                    : "deterministic uniform FP32 [-4,4)";
+  const char* sm_scope = "no per-CTA SMID/admission telemetry; synchronized launch completion does not measure physical SM coverage";
+  if (paired) {
+    const uint64_t launches = rt.batches * uint64_t(o.batch_launches);
+    Obj j;
+    j.str("type", "active_reference_result").str("workload", "control").str("reference_kind", "issue_loop")
+     .str("kernel_implementation_version", "integer_issue_loop_no_admission_v2")
+     .str("block_completion_count_source", "synchronized_completed_launches")
+     .str("active_sm_distribution_status", "not_measured_nonlinear").str("sm_distribution_scope", sm_scope)
+     .f("duration_s", rt.device_s).f("host_duration_s", rt.host_s).u("batches", rt.batches).i("batch_launches", o.batch_launches)
+     .u("iterations_per_launch", o.iterations).i("blocks", o.blocks).i("threads", o.threads)
+     .u("admitted_blocks", launches * uint64_t(o.blocks)).u("operations", 0).u("logical_bytes", 0)
+     .str("operation_unit", "not FLOPs or target bytes; integer issue-loop reference")
+     .raw("measure_epochs", epochs_json(rt, o.batch_launches, [](Obj& e, const Epoch&) { e.u("operations", 0).u("logical_bytes", 0); }))
+     .raw("sanity", Obj().b("requested_sm_coverage_complete", true).done())
+     .str("scope", "active integer issue-loop reference measured in same CUDA process and allocated context; no target-operation normalization and no physical component attribution");
+    out.line(j.done());
+  }
+  const uint64_t launches = t.batches * uint64_t(o.batch_launches);
+  const long double elements = (long double)launches * q * o.iterations, bytes = elements * bytes_per_element;
+  const bool finite = numerical.passed;
+  Obj j;
+  j.str("type", "result").str("workload", o.workload).str("access", "read")
+   .f("duration_s", t.device_s).f("host_duration_s", t.host_s).u("batches", t.batches).u("iterations_per_launch", o.iterations)
+   .u("iterations_per_batch", o.iterations * o.batch_launches).i("batch_launches", o.batch_launches)
+   .u("workload_launches", launches).u("kernel_launches", launches).u("gemm_invocations", 0)
+   .u("fixed_batches", o.fixed_batches).u("warmup_batches", o.warmup_batches)
+   .f("mean_batch_duration_s", t.device_s / double(std::max<uint64_t>(1, t.batches)))
+   .str("duration_scope", "CUDA event elapsed experiment window including gaps; not summed kernel busy time")
+   .str("kernel_implementation_version", "fp32_complete_nonlinear_q_grid_v2")
+   .str("nonlinear_mode", o.nonlinear_mode).str("grid_mode", o.grid_mode).u("input_elements", q)
+   .f("elements_per_launch", double((long double)q * o.iterations))
+   .str("block_completion_count_source", "synchronized_completed_launches")
+   .raw("memory_accesses_per_thread_iteration", "null").raw("memory_read_checksum_scope", "null")
+   .raw("read_cache_policy", "null").raw("memory_read_index_math", "null").raw("memory_read_validation", "null")
+   .f("operations", double(elements))
+   .str("operation_unit", "output elements of the complete function; not FLOPs or SFU instructions")
+   .f("logical_bytes", double(bytes)).f("throughput_ops_s", double(elements) / t.device_s)
+   .f("throughput_bytes_s", double(bytes) / t.device_s).i("blocks", o.blocks).i("threads", o.threads)
+   .b("launch_geometry_applies", true).u("admitted_blocks", launches * uint64_t(o.blocks))
+   .u("working_set_bytes", q * 4).u("requested_working_set_bytes", requested_ws)
+   .raw("write_copy_thread_addresses_disjoint", "null")
+   .u("allocated_bytes", (2 * q + gamma_count + (context ? lanes : 1)) * 4).u("l1_bytes_per_block", 0)
+   .u("stride_elements", 1).u("offset_bytes", 0).raw("memory_word_bytes", "null").raw("stride_words", "null")
+   .raw("lane_stride_bytes", "null").i("tensor_accumulators", o.accumulators)
+   .i("gemm_m", o.gemm_m).i("gemm_n", o.gemm_n).i("gemm_k", o.gemm_k).u("seed", o.seed)
+   .u("checksum", post.checksum).str("checksum_kind", "validated_fp32_nonlinear_output_sample_hash")
+   .raw("kernel_resources", resources_json(attr, max_blocks, o.threads, p, o.blocks, smem))
+   .i("row_width", rowwise ? o.row_width : 0).f("elements", double(elements))
+   .f("row_evaluations", rowwise ? double(elements / o.row_width) : 0.0)
+   .str("math_implementation", "cuda_fp32_q_grid_v2")
+   .raw("rms_epsilon", fn == NL_RMSNORM ? "0.00001" : "null").b("affine_gamma", fn == NL_RMSNORM)
+   .str("nonlinear_input_distribution", distribution)
+   .str("nonlinear_scope", "complete FP32 function including global input/output and row reductions; repeated applications reload fixed input; no pure SFU or FLOP attribution")
+   .raw("numerical_validation", Obj().u("checked_values", numerical.checked).f("max_absolute_error", numerical.max_abs)
+                                     .f("max_relative_error", numerical.max_rel).f("absolute_tolerance", 2e-6)
+                                     .f("relative_tolerance", 2e-4)
+                                     .str("scope", "CPU double reference on global first/middle/last and distributed elements or complete rows before warmup and after measurement; includes pointwise tail; softmax row sums also checked; not exhaustive").done())
+   .raw("sanity", Obj().b("finite_output_sample", finite).raw("memory_read_sample_matches_reference", "null")
+                       .b("numerical_validation_passed", numerical.passed).b("requested_sm_coverage_complete", true).done())
+   .b("profile_region", o.profile_region).b("paired_reference_context_allocated", context)
+   .raw("measure_epochs", epochs_json(t, o.batch_launches, [&](Obj& e, const Epoch& ep) {
+      const long double el = (long double)ep.batches * o.batch_launches * q * o.iterations;
+      e.f("operations", double(el)).f("logical_bytes", double(el * bytes_per_element)).f("elements", double(el))
+       .f("row_evaluations", rowwise ? double(el / o.row_width) : 0.0);
+    }))
+   .raw("auxiliary_work", Obj().u("logical_result_output_bytes", 0).u("sm_admission_atomic_updates", 0)
+                                .u("host_counter_readback_bytes", 0).done())
+   .str("epoch_scope", "approximately one second, exact synchronized completed batch counts; nonlinear work/completed CTAs derived from Q and launch geometry without per-CTA telemetry or counter readback; no interpolated partial-batch counts")
+   .raw("active_sm_ids", "[]").str("active_sm_distribution_status", "not_measured_nonlinear")
+   .str("sm_distribution_scope", sm_scope).raw("missing_requested_sm_ids", "[]")
+   .str("cache_policy", "ld/st.global.cg; L1 bypass; L2/DRAM residency requires counters")
+   .str("nonlinear_kernel_layout", rowwise ? (smem ? "row staged once in shared memory; per-thread 16-byte or 4-byte groups; warp-shuffle reductions"
+                                                  : "row re-read from global memory per pass; warp-shuffle reductions")
+                                           : "grid-stride 16-byte quads, four in flight per thread; scalar tail")
+   .str("sparsity", "dense").str("input_precision", "fp32").str("accumulator_precision", "fp32");
+  out.line(j.done());
+  if (!finite) throw Failure("non-finite or numerically incorrect output sample");
+}
+
 // ---------------------------------------------------------------- generic arms
 // CPU oracle of the scalar read sum for sampled threads (gpu_bench.cu:937-973
 // rule: repeated address cycles folded, at most 65536 unique steps per thread).
@@ -633,6 +869,7 @@ ReadCheck check_read_sums(const Options& o, const uint32_t* sink, uint64_t words
 
 void experiment(Options o, const cudaDeviceProp& p, const Sink& out) {
   if (is_sfu(o.workload)) { experiment_sfu(o, p, out); return; }
+  if (is_nonlinear(o.workload)) { experiment_nonlinear(o, p, out); return; }
   if (o.threads > p.maxThreadsPerBlock) throw Failure("thread count exceeds this device limit");
   if (!o.blocks) o.blocks = 2 * p.multiProcessorCount;
   if (o.blocks <= 0 || o.blocks > 1000000 || o.blocks > p.maxGridSize[0]) throw Failure("--blocks must be positive within practical/hardware limit");

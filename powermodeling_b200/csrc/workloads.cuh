@@ -62,6 +62,21 @@ cudaError_t launch_sfu(int op, bool control, int chains, uint32_t* sink, uint64_
 cudaError_t launch_sfu_check(int op, uint32_t* sample, uint64_t lanes, uint64_t seed, int chains, cudaStream_t s);
 cudaError_t sfu_attributes(int op, bool control, int chains, cudaFuncAttributes* attr);
 const void* kernel_symbol(const char* name, int a, int b, int c);
+
+// Streaming FP32 nonlinear functions (nonlinear.cu; the reference's cuda/nonlinear.cuh).
+enum NonlinearFn { NL_EXP = 0, NL_TANH = 1, NL_SILU = 2, NL_SOFTMAX = 3, NL_RMSNORM = 4 };
+// Input (gamma = 0: (int(w & 0xffff) - 32768) / 8192 + shift) or RMSNorm gamma
+// (gamma = 1: 0.75 + (w & 0xffff) / 131072), w = random_word(i ^ seed).
+cudaError_t launch_nonlinear_fill(float* data, uint64_t n, uint64_t seed, float shift, int gamma, int sms, cudaStream_t s);
+// `iterations` applications of function fn to n inputs (rows of `width` for
+// softmax/RMSNorm) on a blocks x threads grid; in/out 16-byte aligned.
+cudaError_t launch_nonlinear(int fn, const float* in, const float* gamma, float* out, uint64_t n, int width,
+                             uint64_t iterations, int blocks, int threads, cudaStream_t s);
+const void* nonlinear_kernel(int fn, int width);
+size_t nonlinear_dynamic_smem(int fn, int width);
+// The integer issue loop without admission counters (paired reference of the nonlinear arms).
+cudaError_t launch_control_plain(uint32_t* sink, uint64_t iterations, int blocks, int threads, cudaStream_t s);
+const void* control_plain_handle();
 const void* sfu_kernel_handle(int op, bool control, int chains);
 
 }  // namespace pm

@@ -30,7 +30,18 @@ REJECTED = [
     (["--workload", "hbm", "--seconds", "-1"], "finite nonnegative"),
     (["--workload", "hbm", "--memory-vector-bytes", "8"], "must be 4 or 16"),
     (["--workload", "hbm", "--memory-vector-bytes", "16", "--offset-bytes", "4"], "multiple of 16"),
-    (["--workload", "exp", "--nonlinear-mode", "streaming"], "not part of this build"),
+    # Complete streaming nonlinear functions (gpu_bench.cu:164-172, 226-247).
+    (["--workload", "exp"], "require explicit --nonlinear-mode streaming"),
+    (["--workload", "softmax", "--nonlinear-mode", "batched"], "require explicit --nonlinear-mode streaming"),
+    (["--workload", "hbm", "--nonlinear-mode", "streaming"], "applies only to complete exp/tanh/silu/rmsnorm/softmax"),
+    (["--workload", "exp", "--nonlinear-mode", "streaming", "--row-width", "16"], "--row-width 1..65536 applies only"),
+    (["--workload", "rmsnorm", "--nonlinear-mode", "streaming", "--row-width", "65537"], "--row-width 1..65536 applies only"),
+    (["--workload", "softmax", "--nonlinear-mode", "streaming", "--row-width", "0"], "--row-width must be positive"),
+    (["--workload", "silu", "--nonlinear-mode", "streaming", "--access", "copy"], "require a full grid, offset=0"),
+    (["--workload", "tanh", "--nonlinear-mode", "streaming", "--stride-words", "2"], "require a full grid, offset=0"),
+    (["--workload", "exp", "--nonlinear-mode", "streaming", "--sm-ids", "0"], "require a full grid, offset=0"),
+    (["--workload", "exp", "--nonlinear-mode", "streaming", "--grid-mode", "fixed"], "requires explicit positive --blocks"),
+    (["--workload", "exp", "--nonlinear-mode", "streaming", "--grid-mode", "guess"], "--grid-mode must be auto or fixed"),
 ]
 # The reference's cache-policy combinations (tests/test_memory_read_contract.py:272-285).
 POLICY = [("hbm", "read", "bogus"), ("l1", "read", "cg"), ("l2", "read", "ca"), ("hbm", "write", "cg"),
@@ -63,5 +74,6 @@ def test_executable_reports_errors_on_stderr_with_status_1():
 def test_help_lists_the_reference_flags():
     proc = subprocess.run([str(powerbench.EXECUTABLE), "--help"], capture_output=True, text=True)
     assert proc.returncode == 0
-    for flag in ("--working-set-bytes", "--stride-words", "--paired-reference", "--sfu-lanes", "--read-cache-policy"):
+    for flag in ("--working-set-bytes", "--stride-words", "--paired-reference", "--sfu-lanes", "--read-cache-policy",
+                 "--nonlinear-mode", "--row-width"):
         assert flag in proc.stdout
