@@ -12,6 +12,7 @@ powermodeling/analysis.py:
   paired contrast                 analysis.py:292-423
   median_ci                       analysis.py:1096-1101 (generalised to B draws)
   group medians                   analysis.py:1455-1470
+  nonlinear element energies      analysis.py:1027-1041 (count contract: nonlinear_oracle)
 Arithmetic follows the reference operation by operation with CPython's own
 float semantics (sum() is CPython 3.12's compensated sum, statistics.median,
 random.Random), so the oracle's numbers equal the reference's.  The oracle is
@@ -22,6 +23,8 @@ from __future__ import annotations
 import math
 import random
 import statistics
+
+from .nonlinear_oracle import count_issues as nonlinear_count_issues
 
 TENSOR = {"tensor", "fp16_tensor", "tensor_fp16", "gemm"}
 MEMORY = {"l1", "l2", "hbm"}
@@ -310,6 +313,21 @@ def analyze(record, policy=None):
                    paired_active_reference_pj_per_logical_bit=contrast / byte_rate / 8 * 1e12 if workload in MEMORY and contrast is not None and ok_bytes else None,
                    reference_epoch_issues=r_issues)
         out["phases"]["active_reference"] = {x: y for x, y in ref.items() if not x.startswith("_")}
+    # complete nonlinear functions: per-element and per-row energies (analysis.py:1027-1041)
+    nonlinear = workload in NONLINEAR
+    contract_ok = nonlinear and not nonlinear_count_issues(bench, workload)
+    element_rate = ops_rate if contract_ok and exact and ops_rate and ops_rate > 0 else None
+    width = bench.get("row_width") if workload in ("rmsnorm", "softmax") else None
+    row_rate = element_rate / width if element_rate and width else None
+    out.update(throughput_elements_s=element_rate, throughput_rows_s=row_rate,
+               row_width=bench.get("row_width") if nonlinear else None,
+               counted_measure_elements=c_ops if element_rate else None)
+    if nonlinear and element_rate is None:
+        out["pj_per_op"] = out["total_pj_per_op"] = None
+    for prefix, power in (("total_", board), ("operational_idle_increment_", inc_p),
+                          ("paired_active_reference_", out.get("paired_active_reference_power_w"))):
+        out[prefix + "pj_per_element"] = power / element_rate * 1e12 if power is not None and element_rate else None
+        out[prefix + "pj_per_row"] = power / row_rate * 1e12 if power is not None and row_rate else None
     return out
 
 

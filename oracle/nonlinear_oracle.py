@@ -96,3 +96,125 @@ def sample_checksum(function: str, output: np.ndarray, width: int = 0) -> int:
         for b in bits[item * w:(item + 1) * w]:
             h = (h * 1315423911 + int(b)) & MASK64
     return h
+
+
+# ---------------------------------------------------------------- count contract
+def _count(obj, key, bad):
+    v = obj.get(key)
+    ok = not isinstance(v, bool) and isinstance(v, (int, float)) and np.isfinite(v) and v >= 0 and v == int(v)
+    if not ok:
+        bad.add("invalid_nonlinear_count:" + key)
+    return v if ok else None
+
+
+def _mul(*vals):
+    if any(v is None for v in vals):
+        return None
+    out = 1
+    for v in vals:
+        out *= v
+    return out
+
+
+def count_issues(bench: dict, workload: str) -> list[str]:
+    """The reference's nonlinear.count_issues (nonlinear.py:22-128), restated independently of the product."""
+    if workload not in FUNCTIONS:
+        return []
+    import math
+    bad: set[str] = set()
+    row = workload in ROW_FUNCTIONS
+    bpe = 16 if row else 8
+    c = lambda key, obj=bench: _count(obj, key, bad)  # noqa: E731
+
+    def eq(name, a, b):
+        if a is None or b is None or not math.isclose(a, b, rel_tol=1e-9, abs_tol=1e-6):
+            bad.add("nonlinear_count_disagreement:" + name)
+
+    el, ops = c("elements"), c("operations")
+    if el is not None and el <= 0:
+        bad.add("missing_nonlinear_elements")
+    eq("operations_are_elements", ops, el)
+    eq("logical_bytes", c("logical_bytes"), _mul(el, bpe))
+    w = c("row_width")
+    if row:
+        if w is None or not 1 <= w <= 65536:
+            bad.add("invalid_nonlinear_row_width")
+        eq("row_evaluations", c("row_evaluations"), el / w if el is not None and w else None)
+    else:
+        eq("row_width", w, 0)
+        eq("row_evaluations", c("row_evaluations"), 0)
+    blocks, ws, it, adm = c("blocks"), c("working_set_bytes"), c("iterations_per_launch"), c("admitted_blocks")
+    qg = bench.get("math_implementation") == "cuda_fp32_q_grid_v2" or \
+        bench.get("kernel_implementation_version") == "fp32_complete_nonlinear_q_grid_v2"
+    launches = bl = q = None
+    if qg:
+        if (bench.get("math_implementation"), bench.get("kernel_implementation_version")) != \
+                ("cuda_fp32_q_grid_v2", "fp32_complete_nonlinear_q_grid_v2"):
+            bad.add("unsupported_nonlinear_q_grid_implementation")
+        if bench.get("block_completion_count_source") != "synchronized_completed_launches":
+            bad.add("unsupported_nonlinear_block_completion_count_source")
+        q, th, launches = c("input_elements"), c("threads"), c("kernel_launches")
+        if "batch_launches" in bench:
+            bl = c("batch_launches")
+            if not bl:
+                bad.add("invalid_nonlinear_batch_launches")
+        if "batches" in bench:
+            eq("completed_batch_kernel_launches", launches, _mul(c("batches"), bl))
+        if ws is None or ws <= 0 or ws % 4:
+            bad.add("invalid_nonlinear_input_word_alignment")
+        eq("input_elements", q, ws / 4 if ws is not None else None)
+        if q is None or q <= 0 or (w and row and q % w):
+            bad.add("incomplete_nonlinear_input_or_row")
+        if th is None or not 32 <= th <= 1024 or th % 32:
+            bad.add("invalid_nonlinear_threads")
+        mode = bench.get("grid_mode")
+        if mode not in ("auto", "fixed"):
+            bad.add("invalid_nonlinear_grid_mode")
+        elif mode == "auto" and q and th and (not row or w):
+            eq("auto_grid_blocks", blocks, q / w if row else math.ceil(q / th))
+        if not blocks or blocks > 1000000 or not it or not launches:
+            bad.add("missing_nonlinear_execution_counts")
+        if launches is not None and blocks is not None:
+            eq("completed_launch_admissions", adm, launches * blocks)
+        eq("completed_launch_elements", el, _mul(launches, q, it))
+    elif blocks and ws and it and adm:
+        eq("admission_elements", el, adm * (ws / 4 / blocks) * it)
+        if ws % (4 * blocks * (w if row and w else 1)):
+            bad.add("incomplete_nonlinear_block_slice_or_row")
+    else:
+        bad.add("missing_nonlinear_execution_counts")
+    if bench.get("math_implementation") not in ("cuda_fp32_standard_streaming_v1", "cuda_fp32_q_grid_v2") \
+            or bench.get("input_precision") != "fp32":
+        bad.add("unsupported_nonlinear_math_contract")
+    if workload == "rmsnorm" and (bench.get("rms_epsilon") != 1e-5 or bench.get("affine_gamma") is not True):
+        bad.add("unsupported_rmsnorm_definition")
+    if (bench.get("sanity") or {}).get("numerical_validation_passed") is not True:
+        bad.add("nonlinear_numerical_validation_failed_or_missing")
+    chk = (bench.get("numerical_validation") or {}).get("checked_values")
+    if isinstance(chk, bool) or not isinstance(chk, (int, float)) or not np.isfinite(chk) or chk <= 0:
+        bad.add("missing_nonlinear_numerical_reference_checks")
+    epochs = bench.get("measure_epochs")
+    if not isinstance(epochs, list) or not epochs:
+        bad.add("missing_nonlinear_measure_epochs")
+        return sorted(bad)
+    for ep in epochs:
+        if not isinstance(ep, dict):
+            bad.add("invalid_nonlinear_epoch")
+            continue
+        e = _count(ep, "elements", bad)
+        eq("epoch_operations_are_elements", _count(ep, "operations", bad), e)
+        eq("epoch_logical_bytes", _count(ep, "logical_bytes", bad), _mul(e, bpe))
+        eq("epoch_rows", _count(ep, "row_evaluations", bad), e / w if e is not None and w and row else 0)
+        if qg:
+            el_ = _count(ep, "kernel_launches", bad)
+            if "batches" in ep:
+                eq("epoch_completed_batch_kernel_launches", el_, _mul(_count(ep, "batches", bad), bl))
+            eq("epoch_completed_launch_admissions", _count(ep, "admitted_blocks", bad), _mul(el_, blocks))
+            eq("epoch_completed_launch_elements", e, _mul(el_, q, it))
+        if ep.get("counts_exact") is not True:
+            bad.add("inexact_nonlinear_measure_epoch")
+    tot = lambda k: sum(ep.get(k, 0) for ep in epochs if isinstance(ep, dict) and isinstance(ep.get(k), (int, float)))  # noqa: E731
+    eq("epoch_total_elements", tot("elements"), el)
+    if qg:
+        eq("epoch_total_kernel_launches", tot("kernel_launches"), launches)
+    return sorted(bad)

@@ -46,6 +46,9 @@ TRIAL_KEYS = (
     "paired_active_reference_pj_per_flop", "paired_active_reference_pj_per_logical_bit",
     "paired_active_reference_drift_adjusted_power_w", "active_reference_power_w", "active_reference_duration_s",
     "active_reference_total_energy_j", "paired_active_reference_state_deltas", "active_control_incremental_power_w",
+    "throughput_elements_s", "throughput_rows_s", "counted_measure_elements", "row_width", "total_pj_per_element",
+    "total_pj_per_row", "operational_idle_increment_pj_per_element", "operational_idle_increment_pj_per_row",
+    "paired_active_reference_pj_per_element", "paired_active_reference_pj_per_row",
 )
 PHASE_KEYS = ("issues", "warnings", "start_s", "end_s", "duration_s", "midpoint_s", "samples",
               "sample_interval_median_s", "max_sample_gap_s", "integrated_power_energy_j", "integrated_power_w",

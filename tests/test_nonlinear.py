@@ -29,6 +29,7 @@ def test_count_issues_match_reference(index):
     gold = GOLDEN[index]
     assert gold["digest"] == record_digest(record), "the case builder changed; regenerate the fixture"
     assert contracts.nonlinear_count_issues(record, workload) == gold["issues"], name
+    assert O.count_issues(record, workload) == gold["issues"], name
 
 
 def test_fill_is_exact_and_in_range():

@@ -15,7 +15,10 @@ NUMERIC = ("duration_s", "total_energy_j", "board_power_w", "idle_power_w", "idl
            "total_pj_per_logical_bit", "operational_idle_increment_pj_per_logical_bit", "energy_source",
            "paired_active_reference_power_w", "paired_active_reference_energy_j", "active_reference_power_w",
            "active_reference_duration_s", "paired_active_reference_pj_per_flop",
-           "paired_active_reference_pj_per_logical_bit")
+           "paired_active_reference_pj_per_logical_bit", "throughput_elements_s", "throughput_rows_s",
+           "counted_measure_elements", "row_width", "total_pj_per_element", "total_pj_per_row",
+           "operational_idle_increment_pj_per_element", "operational_idle_increment_pj_per_row",
+           "paired_active_reference_pj_per_element", "paired_active_reference_pj_per_row")
 PHASE_NUMERIC = ("start_s", "end_s", "duration_s", "midpoint_s", "samples", "sample_interval_median_s",
                  "max_sample_gap_s", "integrated_power_energy_j", "power_w", "memory_rail_energy_j", "energy_counter_j",
                  "distinct_power_values", "observed_power_change_interval_median_s", "graphics_clock_mhz",

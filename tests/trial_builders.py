@@ -93,6 +93,20 @@ def with_reference(record, order="AB", reference_power=80.0):
     return r
 
 
+def nonlinear_steady(workload="rmsnorm", batches_per_epoch=50, **kw):
+    """steady() carrying a Q-grid result of a complete nonlinear function
+    (the record shape of powerbench's exp|tanh|silu|rmsnorm|softmax arms), one
+    epoch per second of the 12 s measure window."""
+    from nonlinear_cases import q_grid_record
+    r = steady(workload=workload, **kw)
+    bench = q_grid_record(workload, epoch_batches=(batches_per_epoch,) * 12)
+    for k, e in enumerate(bench["measure_epochs"]):
+        e.update(start_s=6.0 + k, end_s=7.0 + k)
+    bench["duration_s"] = 12.0
+    r["benchmark"] = bench
+    return r
+
+
 def scenarios():
     """(name, record, policy) triples; policy None means the reference defaults."""
     out = []
@@ -236,6 +250,16 @@ def scenarios():
     add("invalid_measure_window", r)
     short = dict(trim_s=0.0, idle_trim_s=0.0, min_measure_s=1.0, min_idle_s=0.5)
     add("short_policy_steady", steady(), short)
+    add("nonlinear_rmsnorm_q_grid", nonlinear_steady("rmsnorm"))
+    add("nonlinear_exp_trapezoid", nonlinear_steady("exp", counter=None))
+    add("nonlinear_softmax_paired_ab", with_reference(nonlinear_steady("softmax", counter=None), "AB", reference_power=90.0))
+    add("nonlinear_silu_paired_ba", with_reference(nonlinear_steady("silu", counter=None), "BA", reference_power=120.0))
+    r = nonlinear_steady("tanh")
+    r["benchmark"]["elements"] += 1
+    add("nonlinear_count_disagreement", r)
+    r = nonlinear_steady("rmsnorm")
+    r["benchmark"]["sanity"]["numerical_validation_passed"] = False
+    add("nonlinear_validation_failed", r)
     return out
 
 
