@@ -712,11 +712,12 @@ void experiment_nonlinear(Options o, const cudaDeviceProp& p, const Sink& out) {
   check(cudaDeviceSynchronize(), "nonlinear kernel");
   NonlinearCheck numerical = check_nonlinear(o, fn, input.p, output.p, gamma.p, q);
   if (!numerical.passed) throw Failure("nonlinear output differs from CPU double reference before measurement");
-  const size_t smem = nonlinear_dynamic_smem(fn, width);
+  const NonlinearLayout layout = nonlinear_layout(fn, q, width, o.blocks, o.threads);
+  const size_t smem = layout.dynamic_smem;
   cudaFuncAttributes attr{};
   int max_blocks = 0;
-  check(cudaFuncGetAttributes(&attr, nonlinear_kernel(fn, width)), "cudaFuncGetAttributes");
-  check(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&max_blocks, nonlinear_kernel(fn, width), o.threads, smem), "occupancy");
+  check(cudaFuncGetAttributes(&attr, layout.kernel), "cudaFuncGetAttributes");
+  check(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&max_blocks, layout.kernel, o.threads, smem), "occupancy");
   out.line(protocol_json(o, paired, context, true, "issue_loop",
                          "paired integer issue-loop operational contrast; launch geometry, iterations and batching match the nonlinear kernel; instruction mix, residency, register pressure, occupancy and duration per launch are not counterfactual equivalents; not isolated component energy"));
   run_phase(out, "warmup", o.warmup_seconds, o.warmup_batches, treat);
@@ -816,9 +817,7 @@ void experiment_nonlinear(Options o, const cudaDeviceProp& p, const Sink& out) {
    .raw("active_sm_ids", "[]").str("active_sm_distribution_status", "not_measured_nonlinear")
    .str("sm_distribution_scope", sm_scope).raw("missing_requested_sm_ids", "[]")
    .str("cache_policy", "ld/st.global.cg; L1 bypass; L2/DRAM residency requires counters")
-   .str("nonlinear_kernel_layout", rowwise ? (smem ? "row staged once in shared memory; per-thread 16-byte or 4-byte groups; warp-shuffle reductions"
-                                                  : "row re-read from global memory per pass; warp-shuffle reductions")
-                                           : "grid-stride 16-byte quads, four in flight per thread; scalar tail")
+   .str("nonlinear_kernel_layout", layout.description)
    .str("sparsity", "dense").str("input_precision", "fp32").str("accumulator_precision", "fp32");
   out.line(j.done());
   if (!finite) throw Failure("non-finite or numerically incorrect output sample");

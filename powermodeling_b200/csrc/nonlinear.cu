@@ -10,13 +10,18 @@
 // a CTA does inside it is B200-specific:
 //  * pointwise: grid-stride over 16-byte quads, four independent quads in
 //    flight per thread (64 bytes), ld/st.global.cg, a scalar tail of n mod 4;
-//  * row-wise: each thread owns the same quads of a row in every pass; the row
-//    is staged in shared memory once (rows up to kRowStageFloats floats), so
-//    HBM sees each input byte once instead of two (RMSNorm) or three (softmax)
-//    times; softmax keeps exp(x - max) in the staged row instead of
-//    re-evaluating it; reductions are warp shuffles plus one cross-warp step
-//    in a fixed order, alternating two buffers so one barrier per reduction
-//    suffices.  Wider rows re-read global memory in each pass.
+//  * row-wise, grid-stride grids with at least one row per warp and rows of
+//    at most 1024 floats (a multiple of 4): one warp per row, the row held in
+//    registers (up to 8 quads per lane), warp-shuffle reductions, no shared
+//    memory or barriers; every input byte crosses HBM once;
+//  * row-wise otherwise (one CTA per row, as the auto grid launches): each
+//    thread owns the same quads of a row in every pass; the row is staged in
+//    shared memory once (rows up to kRowStageFloats floats), so HBM sees each
+//    input byte once instead of two (RMSNorm) or three (softmax) times;
+//    softmax keeps exp(x - max) in the staged row instead of re-evaluating
+//    it; reductions are warp shuffles plus one cross-warp step in a fixed
+//    order, alternating two buffers so one barrier per reduction suffices.
+//    Wider rows re-read global memory in each pass.
 // This file is compiled with contraction (fmad) enabled like the reference, so
 // the pointwise outputs equal the reference kernel's bit for bit.
 #include "workloads.cuh"
@@ -232,6 +237,77 @@ __global__ void __launch_bounds__(1024) row_stream_kernel(const float* in, const
   }
 }
 
+// One warp per row, K quads per lane (width <= 128 K, width % 4 == 0).  With 8
+// quads the row needs more than the 64 registers a 1024-thread block leaves a
+// thread, so that variant is built for blocks of at most 512 threads.
+constexpr int kWarpRowMaxThreads8 = 512;
+
+template <bool Softmax, int K, int MaxThreads = (K == 8 ? kWarpRowMaxThreads8 : 1024)>
+__global__ void __launch_bounds__(MaxThreads, 1) row_warp_kernel(const float* in, const float* gamma, float* out,
+                                                        uint64_t rows, int width, uint64_t iterations) {
+  const int lane = threadIdx.x & 31, quads = width >> 2;
+  const uint64_t first = (uint64_t(blockIdx.x) * blockDim.x + threadIdx.x) >> 5;
+  const uint64_t warps = (uint64_t(gridDim.x) * blockDim.x) >> 5;
+  for (uint64_t r = 0; r < iterations; ++r) {
+    for (uint64_t row = first; row < rows; row += warps) {
+      const float* x = in + row * uint64_t(width);
+      float* y = out + row * uint64_t(width);
+      float v[K][4];
+#pragma unroll
+      for (int k = 0; k < K; ++k) {
+        const int q = lane + 32 * k;
+        if (q < quads) {
+          const uint4 u = ld_cg4(x + 4 * q);
+          v[k][0] = __uint_as_float(u.x); v[k][1] = __uint_as_float(u.y);
+          v[k][2] = __uint_as_float(u.z); v[k][3] = __uint_as_float(u.w);
+        }
+      }
+      float scale;
+      if constexpr (Softmax) {
+        float m = -__int_as_float(0x7f800000);
+#pragma unroll
+        for (int k = 0; k < K; ++k)
+          if (lane + 32 * k < quads) m = fmaxf(fmaxf(m, fmaxf(v[k][0], v[k][1])), fmaxf(v[k][2], v[k][3]));
+        m = warp_max(m);
+        float sum = 0.0f;
+#pragma unroll
+        for (int k = 0; k < K; ++k)
+          if (lane + 32 * k < quads) {
+#pragma unroll
+            for (int e = 0; e < 4; ++e) { v[k][e] = expf(v[k][e] - m); sum += v[k][e]; }
+          }
+        scale = 1.0f / warp_sum(sum);
+      } else {
+        float ss = 0.0f;
+#pragma unroll
+        for (int k = 0; k < K; ++k)
+          if (lane + 32 * k < quads) {
+#pragma unroll
+            for (int e = 0; e < 4; ++e) ss += v[k][e] * v[k][e];
+          }
+        scale = rsqrtf(warp_sum(ss) / float(width) + kRmsEpsilon);
+      }
+#pragma unroll
+      for (int k = 0; k < K; ++k) {
+        const int q = lane + 32 * k;
+        if (q < quads) {
+          float o[4];
+          if constexpr (Softmax) {
+#pragma unroll
+            for (int e = 0; e < 4; ++e) o[e] = v[k][e] * scale;
+          } else {
+            const float4 g = __ldg(reinterpret_cast<const float4*>(gamma) + q);
+            o[0] = v[k][0] * scale * g.x; o[1] = v[k][1] * scale * g.y;
+            o[2] = v[k][2] * scale * g.z; o[3] = v[k][3] * scale * g.w;
+          }
+          st_cg4(y + 4 * q, make_uint4(__float_as_uint(o[0]), __float_as_uint(o[1]), __float_as_uint(o[2]),
+                                       __float_as_uint(o[3])));
+        }
+      }
+    }
+  }
+}
+
 // ---------------------------------------------------------------- paired control
 // The integer issue loop of the paired reference without per-CTA admission
 // counters (gpu_bench.cu:420-430 arithmetic).
@@ -256,6 +332,24 @@ int row_variant(int fn, int width) {
   return (fn == NL_SOFTMAX ? 4 : 0) | (staged_row(width) ? 2 : 0) | (width % 4 == 0 ? 1 : 0);
 }
 
+// Quads per lane of the warp-per-row layout, or 0 when a CTA must own each row:
+// rows wider than 1024 floats or not a multiple of 4, or fewer rows than warps.
+int warp_row_quads(int width, uint64_t rows, int blocks, int threads) {
+  if (width % 4 || width > 1024 || uint64_t(blocks) * uint64_t(threads / 32) > rows) return 0;
+  if (width > 512 && threads > kWarpRowMaxThreads8) return 0;
+  return width <= 128 ? 1 : width <= 256 ? 2 : width <= 512 ? 4 : 8;
+}
+
+template <bool Softmax>
+const void* warp_row_handle(int k) {
+  switch (k) {
+    case 1: return reinterpret_cast<const void*>(row_warp_kernel<Softmax, 1>);
+    case 2: return reinterpret_cast<const void*>(row_warp_kernel<Softmax, 2>);
+    case 4: return reinterpret_cast<const void*>(row_warp_kernel<Softmax, 4>);
+    default: return reinterpret_cast<const void*>(row_warp_kernel<Softmax, 8>);
+  }
+}
+
 const void* row_kernel(int fn, int width) {
   switch (row_variant(fn, width)) {
     case 7: return row_handle<true, true, 4>();
@@ -273,17 +367,28 @@ std::atomic<int> g_row_smem_limit[8][kMaxDevices];
 
 }  // namespace
 
-const void* nonlinear_kernel(int fn, int width) {
+NonlinearLayout nonlinear_layout(int fn, uint64_t n, int width, int blocks, int threads) {
+  NonlinearLayout l{};
   switch (fn) {
-    case NL_EXP: return reinterpret_cast<const void*>(pointwise_stream_kernel<NL_EXP>);
-    case NL_TANH: return reinterpret_cast<const void*>(pointwise_stream_kernel<NL_TANH>);
-    case NL_SILU: return reinterpret_cast<const void*>(pointwise_stream_kernel<NL_SILU>);
-    default: return row_kernel(fn, width);
+    case NL_EXP: l.kernel = reinterpret_cast<const void*>(pointwise_stream_kernel<NL_EXP>); break;
+    case NL_TANH: l.kernel = reinterpret_cast<const void*>(pointwise_stream_kernel<NL_TANH>); break;
+    case NL_SILU: l.kernel = reinterpret_cast<const void*>(pointwise_stream_kernel<NL_SILU>); break;
+    default: {
+      const int k = warp_row_quads(width, n / uint64_t(width), blocks, threads);
+      if (k) {
+        l.kernel = fn == NL_SOFTMAX ? warp_row_handle<true>(k) : warp_row_handle<false>(k);
+        l.warp_rows = true;
+      } else {
+        l.kernel = row_kernel(fn, width);
+        l.dynamic_smem = staged_row(width) ? size_t(width) * 4 : 0;
+      }
+    }
   }
-}
-
-size_t nonlinear_dynamic_smem(int fn, int width) {
-  return (fn == NL_SOFTMAX || fn == NL_RMSNORM) && staged_row(width) ? size_t(width) * 4 : 0;
+  l.description = fn < NL_SOFTMAX ? "grid-stride 16-byte quads, four in flight per thread; scalar tail"
+                  : l.warp_rows ? "one warp per row, row in registers (16-byte groups); warp-shuffle reductions"
+                  : l.dynamic_smem ? "one CTA per row, row staged once in shared memory; warp-shuffle reductions"
+                  : "one CTA per row, row re-read from global memory per pass; warp-shuffle reductions";
+  return l;
 }
 
 cudaError_t launch_nonlinear_fill(float* data, uint64_t n, uint64_t seed, float shift, int gamma, int sms, cudaStream_t s) {
@@ -300,12 +405,12 @@ cudaError_t launch_nonlinear(int fn, const float* in, const float* gamma, float*
   else if (fn == NL_TANH) pointwise_stream_kernel<NL_TANH><<<blocks, threads, 0, s>>>(in, out, n, iterations);
   else if (fn == NL_SILU) pointwise_stream_kernel<NL_SILU><<<blocks, threads, 0, s>>>(in, out, n, iterations);
   else {
-    const size_t smem = nonlinear_dynamic_smem(fn, width);
-    const void* k = row_kernel(fn, width);
-    ensure_dynamic_smem(k, 2 * kMaxWarps * sizeof(float), smem, g_row_smem_limit[row_variant(fn, width)]);
+    const NonlinearLayout l = nonlinear_layout(fn, n, width, blocks, threads);
+    if (!l.warp_rows)
+      ensure_dynamic_smem(l.kernel, 2 * kMaxWarps * sizeof(float), l.dynamic_smem, g_row_smem_limit[row_variant(fn, width)]);
     const uint64_t rows = n / uint64_t(width);
     void* args[] = {&in, &gamma, &out, const_cast<uint64_t*>(&rows), &width, &iterations};
-    return cudaLaunchKernel(k, dim3(blocks), dim3(threads), args, smem, s);
+    return cudaLaunchKernel(l.kernel, dim3(blocks), dim3(threads), args, l.dynamic_smem, s);
   }
   return cudaGetLastError();
 }

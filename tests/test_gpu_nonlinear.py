@@ -69,7 +69,10 @@ def test_pointwise_within_reference_tolerance(gpu_ready, function, n, threads, b
 ROWWISE = [(f, w, rows, t, b) for f in ("softmax", "rmsnorm")
            for w, rows, t, b in ((1, 5, 96, None), (3, 7, 32, None), (129, 3, 96, None), (129, 5, 96, 2),
                                  (1024, 5, 96, None), (1024, 300, 256, 148), (4096, 37, 1024, None),
-                                 (40960, 3, 256, None), (40961, 2, 96, None), (65536, 2, 512, 1), (5000, 9, 64, 4))]
+                                 (40960, 3, 256, None), (40961, 2, 96, None), (65536, 2, 512, 1), (5000, 9, 64, 4),
+                                 # one warp per row: fixed grids with at least one row per warp
+                                 (4, 1000, 64, 3), (128, 700, 96, 5), (256, 999, 256, 2), (512, 613, 1024, 1),
+                                 (516, 300, 128, 2), (1024, 2000, 256, 7), (1024, 2000, 1024, 1), (1020, 97, 32, 3))]
 
 
 @pytest.mark.parametrize("function,width,rows,threads,blocks", ROWWISE)
