@@ -250,6 +250,21 @@ def scenarios():
     add("invalid_measure_window", r)
     short = dict(trim_s=0.0, idle_trim_s=0.0, min_measure_s=1.0, min_idle_s=0.5)
     add("short_policy_steady", steady(), short)
+    for count in (32, 33, 48):
+        # Epoch lists on both sides of the 32 a CTA copies to shared memory.
+        r = steady()
+        width = 12.0 / count
+        r["benchmark"]["measure_epochs"] = [{"start_s": 6.0 + k * width, "end_s": 6.0 + (k + 1) * width,
+                                             "operations": 1e12 * width, "logical_bytes": 0.0, "counts_exact": True}
+                                            for k in range(count)]
+        r["benchmark"]["measure_epochs"].reverse()
+        add(f"epochs_{count}_unsorted", r)
+    r = with_reference(steady(workload="l2", counter=None), "AB")
+    for e_list in (r["benchmark"]["measure_epochs"], r["active_reference"]["measure_epochs"]):
+        base = e_list[0]["start_s"]
+        e_list[:] = [{"start_s": base + k * 0.25, "end_s": base + (k + 1) * 0.25, "operations": e_list[0]["operations"] / 4,
+                      "logical_bytes": e_list[0]["logical_bytes"] / 4, "counts_exact": True} for k in range(48)]
+    add("paired_48_epochs_per_arm", r)
     add("nonlinear_rmsnorm_q_grid", nonlinear_steady("rmsnorm"))
     add("nonlinear_exp_trapezoid", nonlinear_steady("exp", counter=None))
     add("nonlinear_softmax_paired_ab", with_reference(nonlinear_steady("softmax", counter=None), "AB", reference_power=90.0))
