@@ -218,10 +218,53 @@ def tensor_flops_per_clock(record: Mapping, architectures: Mapping) -> float | N
         return None
 
 
-def pack_trials(records: list, host_flags: list, architectures: Mapping) -> Packed:
-    """Build the pm_trials arrays for ``records``; ``host_flags[i]`` are extra trial flag bits."""
-    nt = len(records)
+SAMPLE_COLUMNS = (("t_s", np.float64), ("power_w", np.float64), ("memory_power_w", np.float64),
+                  ("graphics_clock_mhz", np.float64), ("sm_clock_mhz", np.float64), ("memory_clock_mhz", np.float64),
+                  ("temperature_c", np.float64), ("power_limit_w", np.float64), ("enforced_power_limit_w", np.float64),
+                  ("pstate", np.float64), ("energy_int", np.int64), ("energy_float", np.float64),
+                  ("throttle_reasons", np.int64), ("sample_flags", np.uint16), ("memory_power_source", np.uint8))
+
+
+def _native_packer():
+    try:
+        from . import _packnative
+    except ImportError as exc:
+        raise N.NativeError("the record packer extension (_packnative) is not built; run powermodeling_b200.build") from exc
+    return _packnative
+
+
+def _pack_slots_python(slot_raw: list, slot_pid: list):
+    """The per-sample packing in Python (the native packer's specification; tests compare the two)."""
     cols = _Columns()
+    counts, slot_samples, slot_foreign = [], [], []
+    for raw, pid in zip(slot_raw, slot_pid):
+        samples = sorted_samples({"samples": raw})
+        foreign = []
+        for i, s in enumerate(samples):
+            f = _pack_sample(s, pid, cols)
+            if f:
+                foreign.append((i, f))
+        counts.append(len(samples))
+        slot_samples.append(samples)
+        slot_foreign.append(foreign)
+    lists = (cols.t, cols.power, cols.memory, cols.gfx, cols.sm, cols.mem, cols.temp, cols.plimit, cols.enf,
+             cols.pstate, cols.e_int, cols.e_float, cols.throttle, cols.flags, cols.source)
+    arrays = {name: np.asarray(values, dtype=dtype) for (name, dtype), values in zip(SAMPLE_COLUMNS, lists)}
+    return arrays, counts, slot_samples, slot_foreign
+
+
+def _pack_slots_native(slot_raw: list, slot_pid: list):
+    columns, counts, slot_samples, slot_foreign = _native_packer().pack(slot_raw, slot_pid, _SOURCE_IDS)
+    arrays = {name: np.frombuffer(columns[name], dtype=dtype).copy() for name, dtype in SAMPLE_COLUMNS}
+    return arrays, counts, slot_samples, slot_foreign
+
+
+def pack_trials(records: list, host_flags: list, architectures: Mapping, native: bool = True) -> Packed:
+    """Build the pm_trials arrays for ``records``; ``host_flags[i]`` are extra trial flag bits.
+
+    The per-sample work (sorting, coercion, flags) runs in the native packer;
+    ``native=False`` runs the same rules in Python."""
+    nt = len(records)
     offsets = np.zeros(nt * N.PM_PHASES + 1, dtype=np.int64)
     starts = np.full(nt * N.PM_PHASES, NAN)
     ends = np.full(nt * N.PM_PHASES, NAN)
@@ -231,30 +274,21 @@ def pack_trials(records: list, host_flags: list, architectures: Mapping) -> Pack
     ep_rows = []
     scalars = np.full((nt, N.TS_COUNT), NAN)
     tflags = np.zeros(nt, dtype=np.uint32)
-    slot_samples, slot_foreign = [], []
-    cursor, longest = 0, 0
+    slot_raw, slot_pid = [], []
     for t, record in enumerate(records):
         phases = phase_records(record)
         pid = (record.get("quality") or {}).get("measurement_pid")
         for p, name in enumerate(PHASES):
             slot = t * N.PM_PHASES + p
             phase = phases.get(name)
-            samples = []
+            raw = []
             if phase and isinstance(phase, Mapping):
                 present[slot] = 1
                 starts[slot] = nan_if_none(phase.get("start_s"))
                 ends[slot] = nan_if_none(phase.get("end_s"))
-                samples = sorted_samples(phase)
-            foreign = []
-            for i, s in enumerate(samples):
-                f = _pack_sample(s, pid, cols)
-                if f:
-                    foreign.append((i, f))
-            slot_samples.append(samples)
-            slot_foreign.append(foreign)
-            cursor += len(samples)
-            longest = max(longest, len(samples))
-            offsets[slot + 1] = cursor
+                raw = phase.get("samples", [])
+            slot_raw.append(raw)
+            slot_pid.append(pid)
         bench = record.get("benchmark") or record.get("result") or {}
         reference = record.get("active_reference") or {}
         for arm, source in enumerate((bench, reference)):
@@ -293,18 +327,13 @@ def pack_trials(records: list, host_flags: list, architectures: Mapping) -> Pack
         elif protocol.get("order") == "BA":
             flags |= N.T_ORDER_BA
         tflags[t] = flags
-    ns = cursor
+    sample_arrays, counts, slot_samples, slot_foreign = (_pack_slots_native if native else _pack_slots_python)(slot_raw, slot_pid)
+    np.cumsum(counts, out=offsets[1:])
+    ns = int(offsets[-1])
+    longest = max(counts, default=0)
     arrays = {
         "phase_offsets": offsets, "phase_start_s": starts, "phase_end_s": ends, "phase_present": present,
-        "t_s": np.asarray(cols.t, dtype=np.float64), "power_w": np.asarray(cols.power, dtype=np.float64),
-        "memory_power_w": np.asarray(cols.memory, dtype=np.float64),
-        "graphics_clock_mhz": np.asarray(cols.gfx, dtype=np.float64), "sm_clock_mhz": np.asarray(cols.sm, dtype=np.float64),
-        "memory_clock_mhz": np.asarray(cols.mem, dtype=np.float64), "temperature_c": np.asarray(cols.temp, dtype=np.float64),
-        "power_limit_w": np.asarray(cols.plimit, dtype=np.float64),
-        "enforced_power_limit_w": np.asarray(cols.enf, dtype=np.float64), "pstate": np.asarray(cols.pstate, dtype=np.float64),
-        "energy_int": np.asarray(cols.e_int, dtype=np.int64), "energy_float": np.asarray(cols.e_float, dtype=np.float64),
-        "throttle_reasons": np.asarray(cols.throttle, dtype=np.int64), "sample_flags": np.asarray(cols.flags, dtype=np.uint16),
-        "memory_power_source": np.asarray(cols.source, dtype=np.uint8),
+        **sample_arrays,
         "epoch_offsets": ep_off, "epoch_status": ep_status,
         "epoch_start_s": np.asarray([r[0] for r in ep_rows], dtype=np.float64),
         "epoch_end_s": np.asarray([r[1] for r in ep_rows], dtype=np.float64),

@@ -1,0 +1,120 @@
+"""The native record packer (_packnative) against the Python packer it replaces.
+
+Both apply the reference's sample rules (_samples, _finite, _throttle_mask,
+energy-counter kinds, process inventories, memory-power sources); every
+array, the sorted sample lists and the foreign pids must be identical, and a
+value the reference's coercion lets raise must raise the same exception."""
+from __future__ import annotations
+
+import copy
+
+import numpy as np
+import pytest
+
+from powermodeling_b200 import pack as P
+from powermodeling_b200.profiles import ARCHITECTURES
+from powermodeling_b200.synthetic import SweepShape, make_sweep
+from trial_builders import memory_rail_scenarios, scenarios
+
+
+def both(records):
+    flags = [0] * len(records)
+    P._SOURCE_IDS.clear()
+    a = P.pack_trials(records, flags, ARCHITECTURES, native=True)
+    ids_a = dict(P._SOURCE_IDS)
+    P._SOURCE_IDS.clear()
+    b = P.pack_trials(records, flags, ARCHITECTURES, native=False)
+    assert ids_a == P._SOURCE_IDS
+    return a, b
+
+
+def assert_same(a, b):
+    assert a.arrays.keys() == b.arrays.keys()
+    for k in a.arrays:
+        x, y = a.arrays[k], b.arrays[k]
+        assert x.dtype == y.dtype and x.shape == y.shape, k
+        assert np.array_equal(x.view(np.uint8), y.view(np.uint8)), k
+    assert (a.n_trials, a.n_samples, a.n_epochs, a.max_phase_samples, a.broadcast) == \
+           (b.n_trials, b.n_samples, b.n_epochs, b.max_phase_samples, b.broadcast)
+    # the same sample objects in the same order (packing never copies or mutates them)
+    assert [[id(x) for x in slot] for slot in a.samples] == [[id(x) for x in slot] for slot in b.samples]
+    assert a.foreign_pids == b.foreign_pids
+
+
+def test_scenario_records():
+    records = [r for _, r, _ in scenarios()] + [r for _, r in memory_rail_scenarios()]
+    assert_same(*both(records))
+
+
+def test_synthetic_sweeps():
+    for shape, seed in ((SweepShape(points=6, repeats=4), 3), (SweepShape(points=3, repeats=5, with_energy_counter=True), 4)):
+        assert_same(*both(make_sweep(shape, seed)))
+
+
+class IntLike(int):
+    pass
+
+
+class Floaty:
+    def __float__(self):
+        return 7.5
+
+
+def awkward_samples():
+    base = {"t_s": 0.0, "power_w": 100.0, "compute_processes": [], "graphics_processes": []}
+    odd = [
+        {"power_w": "123.5", "graphics_clock_mhz": True, "sm_clock_mhz": float("nan"), "memory_clock_mhz": float("inf"),
+         "temperature_c": "hot", "power_limit_w": IntLike(400), "enforced_power_limit_w": Floaty(), "pstate": b"3"},
+        {"energy_mj": 2 ** 63 + 5, "throttle_reasons": "0x10"},
+        {"energy_mj": 2 ** 64 + 9, "throttle_reasons": "0b101"},
+        {"energy_mj": -5, "throttle_reasons": "010"},
+        {"energy_mj": -(2 ** 64), "throttle_reasons": "junk"},
+        {"energy_mj": IntLike(12), "throttle_reasons": 2 ** 64 - 1},
+        {"energy_mj": IntLike(-3), "throttle_reasons": 2 ** 64},
+        {"energy_mj": 3.5, "throttle_reasons": -(2 ** 63) - 1},
+        {"energy_mj": float("nan"), "throttle_reasons": float("nan")},
+        {"energy_mj": float("inf"), "throttle_reasons": True},
+        {"energy_mj": True, "throttle_reasons": 3.9},
+        {"energy_mj": "12", "throttle_reasons": b"12"},
+        {"compute_processes": [{"pid": 777}, {"pid": None}, 778, {"other": 1}], "graphics_processes": None},
+        {"compute_processes": ({"pid": 1},), "graphics_processes": [777], "mps_compute_processes": [1]},
+        {"mps_compute_processes": [], "memory_power_w": None, "memory_power_source": ""},
+        {"memory_power_w": 0.0, "memory_power_source": "memory_power_instant_w"},
+        {"memory_power_source": 17},
+        {"memory_power_source": ("a", 1)},
+        {"memory_power_source": "memory_power_instant_w"},
+    ]
+    out = []
+    for k, extra in enumerate(odd):
+        s = dict(base, t_s=float(k) * 0.5)
+        s.update(extra)
+        out.append(s)
+    out += [dict(base, t_s=3.0, power_w=1.0), dict(base, t_s=3.0, power_w=2.0),        # last one wins
+            dict(base, t_s=-0.0, power_w=5.0), dict(base, t_s=0.0, power_w=6.0),      # -0.0 == 0.0
+            dict(base, t_s="2.25"), dict(base, t_s=IntLike(4)), "not a sample", 7, dict(base, t_s=None),
+            dict(base, t_s=float("nan")), dict(base, t_s=True)]
+    out.reverse()
+    return out
+
+
+@pytest.mark.parametrize("pid", [777, None, "777"])
+def test_awkward_values(pid):
+    record = [r for name, r, _ in scenarios() if name == "steady_float_counter"][0]
+    record = copy.deepcopy(record)
+    record["quality"]["measurement_pid"] = pid
+    record["phases"]["measure"]["samples"] = awkward_samples()
+    record["phases"]["idle_pre"]["samples"] = tuple(awkward_samples()[:5])
+    assert_same(*both([record]))
+
+
+@pytest.mark.parametrize("field,value,error", [
+    ("power_w", 2 ** 2000, OverflowError),            # float() of a huge int raises (not caught by _finite)
+    ("energy_mj", 2 ** 64 + 2 ** 63, OverflowError),  # still outside int64 after the 2**64 fold
+    ("throttle_reasons", float("inf"), OverflowError),
+])
+def test_errors_the_reference_lets_raise(field, value, error):
+    record = copy.deepcopy([r for name, r, _ in scenarios() if name == "steady_float_counter"][0])
+    record["phases"]["measure"]["samples"][3][field] = value
+    for native in (True, False):
+        with pytest.raises(error):
+            P.pack_trials([copy.deepcopy(record)], [0], ARCHITECTURES, native=native)
