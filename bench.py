@@ -387,7 +387,9 @@ def run_b200(args, rank: int, world: int) -> dict | None:
                                        f"all-gathered over NCCL") if world > 1 else "single GPU"},
             "e2e": {"value": resamples_per_step / e2e_s, "unit": "resamples/s",
                     "h2d_bytes_per_step": int(h2d), "d2h_bytes_per_step": int(d2h), "ms_per_step": e2e_s * 1e3},
-            "gpu_launches": (3 if own else 1) * args.steps,
+            # per step: analyze, the draws and the finish (or, owning no group, analyze and the
+            # group signal), plus the two arrival waits of the peer exchange
+            "gpu_launches": ((3 if own else 2) if peer else (3 if own else 1)) * args.steps + (2 * args.steps if peer else 0),
             "kernels": {"analyze_kernel_ms": a_ms,
                         "bootstrap_prepare_kernel_ms (side stream, overlaps analyze)": statistics.mean(prepare_ms),
                         "join_and_bootstrap_finish_ms": b_ms,
