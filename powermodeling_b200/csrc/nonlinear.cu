@@ -14,7 +14,10 @@
 //    at most 1024 floats (a multiple of 4): one warp per row, the row held in
 //    registers (up to 8 quads per lane), warp-shuffle reductions, no shared
 //    memory or barriers; every input byte crosses HBM once;
-//  * row-wise otherwise (one CTA per row, as the auto grid launches): each
+//  * row-wise, one CTA per row (as the auto grid launches) with rows of at most
+//    16 x threads floats (a multiple of 4): the row in registers (up to 4
+//    quads per thread), two block reductions over float4-read partials;
+//  * row-wise otherwise (wider rows, widths not a multiple of 4): each
 //    thread owns the same quads of a row in every pass; the row is staged in
 //    shared memory once (rows up to kRowStageFloats floats), so HBM sees each
 //    input byte once instead of two (RMSNorm) or three (softmax) times;
@@ -308,6 +311,94 @@ __global__ void __launch_bounds__(MaxThreads, 1) row_warp_kernel(const float* in
   }
 }
 
+// One CTA per row with the row in registers: R quads per thread (width a
+// multiple of 4, at most 4 R threads floats).  The cross-warp step reads the
+// warps' partials as float4s from buffers padded with the reduction's
+// identity, so every thread combines them in the same fixed order.
+template <bool Max>
+__device__ __forceinline__ float cta_reduce_padded(float v, float* red) {
+  v = Max ? warp_max(v) : warp_sum(v);
+  if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = v;
+  __syncthreads();
+  const int groups = ((blockDim.x >> 5) + 3) >> 2;
+  const float4* r4 = reinterpret_cast<const float4*>(red);
+  float r = Max ? -__int_as_float(0x7f800000) : 0.0f;
+  for (int g = 0; g < groups; ++g) {
+    const float4 q = r4[g];
+    r = Max ? fmaxf(fmaxf(fmaxf(r, q.x), q.y), fmaxf(q.z, q.w)) : ((r + q.x) + q.y) + (q.z + q.w);
+  }
+  return r;
+}
+
+template <bool Softmax, int R>
+__global__ void __launch_bounds__(1024) row_cta_kernel(const float* in, const float* gamma, float* out,
+                                                       uint64_t rows, int width, uint64_t iterations) {
+  __shared__ __align__(16) float red[2][kMaxWarps];
+  const int quads = width >> 2, t = threadIdx.x, T = blockDim.x;
+  for (int i = t; i < 2 * kMaxWarps; i += T) red[i / kMaxWarps][i % kMaxWarps] = (Softmax && i < kMaxWarps) ? -__int_as_float(0x7f800000) : 0.0f;
+  __syncthreads();
+  int parity = 0;
+  for (uint64_t r = 0; r < iterations; ++r) {
+    for (uint64_t row = blockIdx.x; row < rows; row += gridDim.x) {
+      const float* x = in + row * uint64_t(width);
+      float* y = out + row * uint64_t(width);
+      float v[R][4];
+#pragma unroll
+      for (int k = 0; k < R; ++k) {
+        const int q = t + k * T;
+        if (q < quads) {
+          const uint4 u = ld_cg4(x + 4 * q);
+          v[k][0] = __uint_as_float(u.x); v[k][1] = __uint_as_float(u.y);
+          v[k][2] = __uint_as_float(u.z); v[k][3] = __uint_as_float(u.w);
+        }
+      }
+      float scale;
+      if constexpr (Softmax) {
+        float m = -__int_as_float(0x7f800000);
+#pragma unroll
+        for (int k = 0; k < R; ++k)
+          if (t + k * T < quads) m = fmaxf(fmaxf(m, fmaxf(v[k][0], v[k][1])), fmaxf(v[k][2], v[k][3]));
+        m = cta_reduce_padded<true>(m, red[0]);
+        float sum = 0.0f;
+#pragma unroll
+        for (int k = 0; k < R; ++k)
+          if (t + k * T < quads) {
+#pragma unroll
+            for (int e = 0; e < 4; ++e) { v[k][e] = expf(v[k][e] - m); sum += v[k][e]; }
+          }
+        scale = 1.0f / cta_reduce_padded<false>(sum, red[1]);
+      } else {
+        float ss = 0.0f;
+#pragma unroll
+        for (int k = 0; k < R; ++k)
+          if (t + k * T < quads) {
+#pragma unroll
+            for (int e = 0; e < 4; ++e) ss += v[k][e] * v[k][e];
+          }
+        scale = rsqrtf(cta_reduce_padded<false>(ss, red[parity]) / float(width) + kRmsEpsilon);
+        parity ^= 1;
+      }
+#pragma unroll
+      for (int k = 0; k < R; ++k) {
+        const int q = t + k * T;
+        if (q < quads) {
+          float o[4];
+          if constexpr (Softmax) {
+#pragma unroll
+            for (int e = 0; e < 4; ++e) o[e] = v[k][e] * scale;
+          } else {
+            const float4 g = __ldg(reinterpret_cast<const float4*>(gamma) + q);
+            o[0] = v[k][0] * scale * g.x; o[1] = v[k][1] * scale * g.y;
+            o[2] = v[k][2] * scale * g.z; o[3] = v[k][3] * scale * g.w;
+          }
+          st_cg4(y + 4 * q, make_uint4(__float_as_uint(o[0]), __float_as_uint(o[1]), __float_as_uint(o[2]),
+                                       __float_as_uint(o[3])));
+        }
+      }
+    }
+  }
+}
+
 // ---------------------------------------------------------------- paired control
 // The integer issue loop of the paired reference without per-CTA admission
 // counters (gpu_bench.cu:420-430 arithmetic).
@@ -338,6 +429,23 @@ int warp_row_quads(int width, uint64_t rows, int blocks, int threads) {
   if (width % 4 || width > 1024 || uint64_t(blocks) * uint64_t(threads / 32) > rows) return 0;
   if (width > 512 && threads > kWarpRowMaxThreads8) return 0;
   return width <= 128 ? 1 : width <= 256 ? 2 : width <= 512 ? 4 : 8;
+}
+
+// Quads per thread of the register CTA-per-row layout, or 0: rows not a
+// multiple of 4 or wider than 16 x threads floats.
+int cta_row_quads(int width, int threads) {
+  if (width % 4) return 0;
+  const int per_thread = (width / 4 + threads - 1) / threads;
+  return per_thread <= 1 ? 1 : per_thread <= 2 ? 2 : per_thread <= 4 ? 4 : 0;
+}
+
+template <bool Softmax>
+const void* cta_row_handle(int r) {
+  switch (r) {
+    case 1: return reinterpret_cast<const void*>(row_cta_kernel<Softmax, 1>);
+    case 2: return reinterpret_cast<const void*>(row_cta_kernel<Softmax, 2>);
+    default: return reinterpret_cast<const void*>(row_cta_kernel<Softmax, 4>);
+  }
 }
 
 template <bool Softmax>
@@ -375,9 +483,13 @@ NonlinearLayout nonlinear_layout(int fn, uint64_t n, int width, int blocks, int 
     case NL_SILU: l.kernel = reinterpret_cast<const void*>(pointwise_stream_kernel<NL_SILU>); break;
     default: {
       const int k = warp_row_quads(width, n / uint64_t(width), blocks, threads);
+      const int r = cta_row_quads(width, threads);
       if (k) {
         l.kernel = fn == NL_SOFTMAX ? warp_row_handle<true>(k) : warp_row_handle<false>(k);
         l.warp_rows = true;
+      } else if (r) {
+        l.kernel = fn == NL_SOFTMAX ? cta_row_handle<true>(r) : cta_row_handle<false>(r);
+        l.cta_registers = true;
       } else {
         l.kernel = row_kernel(fn, width);
         l.dynamic_smem = staged_row(width) ? size_t(width) * 4 : 0;
@@ -386,6 +498,7 @@ NonlinearLayout nonlinear_layout(int fn, uint64_t n, int width, int blocks, int 
   }
   l.description = fn < NL_SOFTMAX ? "grid-stride 16-byte quads, four in flight per thread; scalar tail"
                   : l.warp_rows ? "one warp per row, row in registers (16-byte groups); warp-shuffle reductions"
+                  : l.cta_registers ? "one CTA per row, row in registers (16-byte groups); warp-shuffle reductions"
                   : l.dynamic_smem ? "one CTA per row, row staged once in shared memory; warp-shuffle reductions"
                   : "one CTA per row, row re-read from global memory per pass; warp-shuffle reductions";
   return l;
@@ -406,7 +519,7 @@ cudaError_t launch_nonlinear(int fn, const float* in, const float* gamma, float*
   else if (fn == NL_SILU) pointwise_stream_kernel<NL_SILU><<<blocks, threads, 0, s>>>(in, out, n, iterations);
   else {
     const NonlinearLayout l = nonlinear_layout(fn, n, width, blocks, threads);
-    if (!l.warp_rows)
+    if (!l.warp_rows && !l.cta_registers)
       ensure_dynamic_smem(l.kernel, 2 * kMaxWarps * sizeof(float), l.dynamic_smem, g_row_smem_limit[row_variant(fn, width)]);
     const uint64_t rows = n / uint64_t(width);
     void* args[] = {&in, &gamma, &out, const_cast<uint64_t*>(&rows), &width, &iterations};

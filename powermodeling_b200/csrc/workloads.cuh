@@ -74,7 +74,7 @@ cudaError_t launch_nonlinear(int fn, const float* in, const float* gamma, float*
                              uint64_t iterations, int blocks, int threads, cudaStream_t s);
 // The kernel, its dynamic shared memory and a one-line description of how a
 // launch of function fn over n inputs on blocks x threads lays out the work.
-struct NonlinearLayout { const void* kernel; size_t dynamic_smem; bool warp_rows; const char* description; };
+struct NonlinearLayout { const void* kernel; size_t dynamic_smem; bool warp_rows, cta_registers; const char* description; };
 NonlinearLayout nonlinear_layout(int fn, uint64_t n, int width, int blocks, int threads);
 // The integer issue loop without admission counters (paired reference of the nonlinear arms).
 cudaError_t launch_control_plain(uint32_t* sink, uint64_t iterations, int blocks, int threads, cudaStream_t s);

@@ -70,6 +70,8 @@ ROWWISE = [(f, w, rows, t, b) for f in ("softmax", "rmsnorm")
            for w, rows, t, b in ((1, 5, 96, None), (3, 7, 32, None), (129, 3, 96, None), (129, 5, 96, 2),
                                  (1024, 5, 96, None), (1024, 300, 256, 148), (4096, 37, 1024, None),
                                  (40960, 3, 256, None), (40961, 2, 96, None), (65536, 2, 512, 1), (5000, 9, 64, 4),
+                                 # one CTA per row, row in registers: 1, 2 and 4 quads per thread
+                                 (128, 9, 32, None), (2048, 5, 256, None), (1024, 6, 96, None), (16384, 2, 1024, None),
                                  # one warp per row: fixed grids with at least one row per warp
                                  (4, 1000, 64, 3), (128, 700, 96, 5), (256, 999, 256, 2), (512, 613, 1024, 1),
                                  (516, 300, 128, 2), (1024, 2000, 256, 7), (1024, 2000, 1024, 1), (1020, 97, 32, 3))]
