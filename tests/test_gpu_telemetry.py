@@ -107,3 +107,28 @@ def test_captured_hbm_trial_analysis_matches_oracle(device):
         assert close(expected.get(key), got.get(key), rel=0.0), (key, expected.get(key), got.get(key))
     assert got["board_power_w"] > got["idle_power_w"] > 0
     assert got["total_energy_j"] > 0
+
+
+def test_captured_nonlinear_trial_analysis_matches_oracle(device):
+    """A captured RMSNorm trial (complete nonlinear function, Q-grid record) through the same path:
+    the record passes the count contract and its per-element and per-row energies match the oracle."""
+    from powermodeling_b200.analysis import analyze_trial
+    from powermodeling_b200.capture import capture_trial
+    from powermodeling_b200.contracts import nonlinear_count_issues
+    from powermodeling_b200.synthetic import ANALYSIS_POLICY
+    args = ["--workload", "rmsnorm", "--nonlinear-mode", "streaming", "--row-width", 1024, "--grid-mode", "fixed",
+            "--blocks", 148 * 8, "--threads", 256, "--working-set-bytes", 1 << 30,
+            "--seconds", 2, "--warmup-seconds", 0.5, "--idle-seconds", 1]
+    record = capture_trial(args, device, sample_interval_s=0.01)
+    assert record["quality"]["benchmark_exit_code"] == 0, record["quality"]["runner_errors"]
+    assert not record["quality"]["runner_errors"], record["quality"]["runner_errors"]
+    assert nonlinear_count_issues(record["benchmark"], "rmsnorm") == []
+    got = analyze_trial(record, ANALYSIS_POLICY)
+    expected = O.analyze(record, ANALYSIS_POLICY)
+    problems = diff(expected, got, TRIAL_KEYS, rel=1e-6)
+    assert not problems, problems
+    for key in ("total_energy_j", "board_power_w", "idle_power_w", "throughput_elements_s", "total_pj_per_element",
+                "total_pj_per_row"):
+        assert close(expected.get(key), got.get(key), rel=0.0), (key, expected.get(key), got.get(key))
+    assert not [i for i in got["issues"] if "nonlinear" in i], got["issues"]
+    assert got["throughput_elements_s"] > 1e11 and got["total_pj_per_element"] > 0
