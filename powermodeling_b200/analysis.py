@@ -880,3 +880,49 @@ def summarize(records: Iterable[Mapping[str, Any]], throughput_fraction: float =
     finish_groups(groups, trials, members, group_indices, med, lo, hi, hbm_bandwidth_fraction)
     return summary_record(trials, groups, duplicates, throughput_fraction, hbm_bandwidth_fraction, min_repeats,
                           resamples)
+
+
+# trials.csv columns (analysis.py:1565-1573), in the reference's order.
+TRIAL_CSV_FIELDS = (
+    "trial_id", "gpu_uuid", "gpu_name", "workload", "experiment_role", "valid", "target_verified", "ncu_status",
+    "ncu_target_suitability", "ncu_utilization_status", "profiler_suitability_status", "memory_access_geometry",
+    "memory_coalescing", "memory_coalescing_energy_eligible", "energy_peak_population_eligible",
+    "verified_selection_eligible", "count_energy_time_alignment_exact", "energy_per_work_kind", "issues", "warnings",
+    "baseline_valid", "baseline_issues", "operational_idle_increment_eligible", "paired_active_reference_eligible",
+    "paired_active_reference_issues", "treatment_design_stratum", "baseline_clock_domains_compared",
+    "baseline_sm_clock_uses_graphics_proxy", "baseline_state_matched", "baseline_state_issues",
+    "baseline_state_domains_compared", "resource_geometry", "row_width", "nonlinear_contract",
+    "counted_measure_elements", "element_count_convention", "row_operation_convention",
+    "paired_reference_clock_domains_compared", "paired_reference_sm_clock_uses_graphics_proxy", "duration_s", *METRICS,
+    "total_energy_j", "incremental_energy_j", "energy_source", "power_limit_w", "tensor_peak_clock_source",
+    "hbm_memory_power", "hbm_bandwidth", "memory_rail_energy_j", "memory_rail_idle_power_w",
+    "memory_rail_incremental_energy_j", "memory_rail_sources",
+    "sfu_contract", "counted_measure_sfu_instructions", "sfu_instruction_count_convention",
+    "sfu_reference_delta_measurement_valid", "sfu_reference_delta_positive_optimum_eligible",
+    "sfu_reference_delta_estimator", "sfu_reference_delta_diagnostics", "sfu_reference_delta_issues",
+    "sfu_hardware_attribution_proven")
+
+
+def write_summary(summary: Mapping[str, Any], output_dir) -> dict[str, str]:
+    """summary.json and trials.csv of a summary (analysis.py:1559-1583).
+
+    summary.json is the summary as indented JSON (non-finite numbers refused,
+    as the reference refuses them); trials.csv holds one row per trial with
+    the reference's columns, lists and dicts as JSON text and absent fields
+    empty.  The evaluation report files the reference adds for a summary with
+    an ``evaluation`` entry are not written."""
+    import csv
+    from pathlib import Path
+    destination = Path(output_dir)
+    destination.mkdir(parents=True, exist_ok=True)
+    json_path = destination / "summary.json"
+    json_path.write_text(json.dumps(summary, indent=2, ensure_ascii=False, allow_nan=False) + "\n")
+    csv_path = destination / "trials.csv"
+    with csv_path.open("w", newline="") as stream:
+        writer = csv.DictWriter(stream, fieldnames=TRIAL_CSV_FIELDS)
+        writer.writeheader()
+        for trial in summary.get("trials", []):
+            writer.writerow({f: json.dumps(trial[f]) if isinstance(trial.get(f), (list, dict)) else trial.get(f)
+                             for f in TRIAL_CSV_FIELDS})
+    return {"summary_json": str(json_path), "trials_csv": str(csv_path)}
+

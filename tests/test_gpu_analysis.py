@@ -170,3 +170,31 @@ def test_bootstrap_beyond_shared_memory_is_a_limit_error(gpu_ready):
                          seeds.ctypes.data, out[0].ctypes.data, out[1].ctypes.data, out[2].ctypes.data)
     assert N.library().pm_group_bootstrap(job) == -4     # PM_E_LIMIT
     assert "shared memory" in N.last_error()
+
+
+@pytest.mark.parametrize("label,shape,seed", [("trapezoid", dict(points=2, repeats=4), 21),
+                                               ("counter", dict(points=2, repeats=3, with_energy_counter=True), 22)])
+def test_trials_csv_matches_reference(gpu_ready, tmp_path, label, shape, seed):
+    """summarize on the GPU, written by write_summary: the metric columns of trials.csv equal the
+    reference's file for the same records (tests/golden/summary_files.json.gz)."""
+    import csv
+    import io
+    from powermodeling_b200.analysis import METRICS, summarize, write_summary
+    from powermodeling_b200.synthetic import ANALYSIS_POLICY, SweepShape, make_sweep
+    case = next(c for c in load_golden("summary_files.json.gz") if c["label"] == label)
+    summary = summarize(make_sweep(SweepShape(**shape), seed), policy=ANALYSIS_POLICY)
+    write_summary(summary, tmp_path)
+    ours = list(csv.DictReader(io.StringIO((tmp_path / "trials.csv").read_text())))
+    theirs = list(csv.DictReader(io.StringIO(case["files"]["trials.csv"])))
+    assert [r["trial_id"] for r in ours] == [r["trial_id"] for r in theirs]
+    exact = ("trial_id", "workload", "valid", "issues", "warnings", "energy_source", "count_energy_time_alignment_exact",
+             "baseline_valid", "operational_idle_increment_eligible", "paired_active_reference_eligible",
+             "board_power_w", "idle_power_w", "total_energy_j", "incremental_energy_j")
+    numeric = tuple(METRICS) + ("duration_s", "power_limit_w")
+    for mine, ref in zip(ours, theirs):
+        for col in exact:
+            assert mine[col] == ref[col], (mine["trial_id"], col, mine[col], ref[col])
+        for col in numeric:
+            a = float(mine[col]) if mine[col] else None
+            b = float(ref[col]) if ref[col] else None
+            assert close(a, b, rel=REL), (mine["trial_id"], col, a, b)
