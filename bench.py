@@ -638,7 +638,7 @@ def run_nonlinear_arms(sms: int, peaks: dict) -> dict:
 
 # DRAM bytes (read + write) per launch from one ncu capture of the same
 # workload (profiles/analysis_sweep_64x4_B10000.md); None where none was taken.
-NCU_TRAFFIC_BYTES = {"analyze_kernel": 3_718_144, "bootstrap_kernel": 180_992}
+NCU_TRAFFIC_BYTES = {"analyze_kernel": 5_149_184, "bootstrap_kernel": 183_040}
 
 
 def roofline_entry(dominant, a_ms, b_ms, in_bytes, out_bytes, G, M, packed, peaks, resamples):
