@@ -132,3 +132,30 @@ def test_captured_nonlinear_trial_analysis_matches_oracle(device):
         assert close(expected.get(key), got.get(key), rel=0.0), (key, expected.get(key), got.get(key))
     assert not [i for i in got["issues"] if "nonlinear" in i], got["issues"]
     assert got["throughput_elements_s"] > 1e11 and got["total_pj_per_element"] > 0
+
+
+def test_captured_paired_softmax_trial(device):
+    """A captured softmax trial with the paired active reference (the reference's minimum arms: 10 s,
+    1 s warm-up, 6 s idles): the engine's no-admission issue-loop record matches the treatment's
+    geometry, the paired checks raise nothing, and the paired per-element energy equals the oracle's."""
+    from powermodeling_b200.analysis import analyze_trial
+    from powermodeling_b200.capture import capture_trial
+    args = ["--workload", "softmax", "--nonlinear-mode", "streaming", "--row-width", 1024, "--grid-mode", "fixed",
+            "--blocks", 148 * 8, "--threads", 256, "--working-set-bytes", 1 << 28, "--paired-reference",
+            "--reference-order", "BA", "--seconds", 10, "--warmup-seconds", 1, "--idle-seconds", 6]
+    record = capture_trial(args, device, sample_interval_s=0.01)
+    assert record["quality"]["benchmark_exit_code"] == 0, record["quality"]["runner_errors"]
+    ref = record["active_reference"]
+    assert ref["kernel_implementation_version"] == "integer_issue_loop_no_admission_v2"
+    for key in ("blocks", "threads", "batch_launches", "iterations_per_launch"):
+        assert ref[key] == record["benchmark"][key], key
+    assert ref["admitted_blocks"] == ref["batches"] * ref["batch_launches"] * ref["blocks"]
+    got = analyze_trial(record)
+    expected = O.analyze(record)
+    problems = diff(expected, got, TRIAL_KEYS, rel=1e-6)
+    assert not problems, problems
+    assert not [i for i in got["paired_active_reference_issues"] if i.startswith("paired_protocol")
+                or i.startswith("paired_geometry") or "definition" in i], got["paired_active_reference_issues"]
+    assert got["throughput_elements_s"] > 1e11
+    for key in ("paired_active_reference_power_w", "paired_active_reference_pj_per_element"):
+        assert close(expected.get(key), got.get(key), rel=0.0), (key, expected.get(key), got.get(key))
