@@ -197,16 +197,16 @@ def run_b200(args, rank: int, world: int) -> dict | None:
     # Exchange one lands every rank's metric rows and valid flags in the gathered buffers (rank order =
     # global row order): by default the analysis kernel stores them into every rank's buffers over
     # NVLink (peer memory, pmb200_peer.h); with --exchange nccl, an all-gather after it.
+    # If the peer exchange cannot be set up, or fails the check against NCCL after the warm-up
+    # steps, every rank takes the NCCL form instead and the line says why.
     peer = world > 1 and args.exchange == "peer"
+    px, exchange_note = None, None
     if peer:
-        from powermodeling_b200.peer import PeerExchange
-        per_rank_groups = -(-len(members) // world)
-        px = PeerExchange(rank, world, n, M, per_rank_groups)
-        all_metrics_ptr, all_valid_ptr = px.metrics_ptr, px.valid_ptr
-    else:
-        all_metrics = torch.empty(world * n * M, dtype=torch.float64, device="cuda") if world > 1 else out["metrics"]
-        all_valid = torch.empty(world * n, dtype=torch.uint8, device="cuda") if world > 1 else out["valid"]
-        all_metrics_ptr, all_valid_ptr = all_metrics.data_ptr(), all_valid.data_ptr()
+        from powermodeling_b200.peer import PeerExchange, PeerExchangeError
+        try:
+            px = PeerExchange(rank, world, n, M, per_rank)
+        except PeerExchangeError as exc:
+            peer, exchange_note = False, f"NVLink peer exchange not set up ({exc}); NCCL all-gathers used"
     own = [members[g] for g in mine]
     offsets = np.zeros(len(own) + 1, dtype=np.int32)
     np.cumsum([len(m) for m in own], out=offsets[1:])
@@ -216,11 +216,23 @@ def run_b200(args, rank: int, world: int) -> dict | None:
     d_seeds = torch.from_numpy(own_seeds.view(np.int64)).cuda()
     # Group outputs of this rank: [3, per_rank, M] (medians, lows, highs); exchange two gathers them.
     group_out = torch.full((3, per_rank, M), float("nan"), dtype=torch.float64, device="cuda")
-    all_group_out = torch.empty((world, 3, per_rank, M), dtype=torch.float64, device="cuda") if world > 1 and not peer else None
     max_members = max((len(m) for m in own), default=1)
-    job = N.BootstrapJob(len(own), M, int(sum(len(m) for m in own)), world * n, RESAMPLES, max_members,
-                         all_metrics_ptr, d_off.data_ptr(), d_rows.data_ptr(), all_valid_ptr,
-                         d_seeds.data_ptr(), group_out[0].data_ptr(), group_out[1].data_ptr(), group_out[2].data_ptr())
+
+    def exchange_buffers():
+        """Gathered rows, valid flags and group results for the current exchange form, and the job reading them."""
+        if peer:
+            a_m, a_v, a_g, m_ptr, v_ptr = None, None, None, px.metrics_ptr, px.valid_ptr
+        else:
+            a_m = torch.empty(world * n * M, dtype=torch.float64, device="cuda") if world > 1 else out["metrics"]
+            a_v = torch.empty(world * n, dtype=torch.uint8, device="cuda") if world > 1 else out["valid"]
+            a_g = torch.empty((world, 3, per_rank, M), dtype=torch.float64, device="cuda") if world > 1 else None
+            m_ptr, v_ptr = a_m.data_ptr(), a_v.data_ptr()
+        j = N.BootstrapJob(len(own), M, int(sum(len(m) for m in own)), world * n, RESAMPLES, max_members,
+                           m_ptr, d_off.data_ptr(), d_rows.data_ptr(), v_ptr,
+                           d_seeds.data_ptr(), group_out[0].data_ptr(), group_out[1].data_ptr(), group_out[2].data_ptr())
+        return a_m, a_v, a_g, j
+
+    all_metrics, all_valid, all_group_out, job = exchange_buffers()
     a_scr = lib.pm_analyze_scratch_bytes(n, packed.max_phase_samples)
     b_scr = lib.pm_bootstrap_scratch_bytes(max(1, len(own)), max_members, RESAMPLES)
     scratch = torch.empty(max(1, a_scr + b_scr), dtype=torch.uint8, device="cuda")
@@ -275,6 +287,32 @@ def run_b200(args, rank: int, world: int) -> dict | None:
         flush.zero_()
         step()
     torch.cuda.synchronize()
+    if peer:
+        # The rows and group results the kernels stored into this rank must equal NCCL
+        # all-gathers of every rank's own outputs, bit for bit, and no arrival wait may have expired.
+        want_rows = torch.empty(world * n * M, dtype=torch.float64, device="cuda")
+        want_valid = torch.empty(world * n, dtype=torch.uint8, device="cuda")
+        want_groups = torch.empty((world, 3, per_rank, M), dtype=torch.float64, device="cuda")
+        dist.all_gather_into_tensor(want_rows, out["metrics"])
+        dist.all_gather_into_tensor(want_valid, out["valid"])
+        dist.all_gather_into_tensor(want_groups, group_out)
+        torch.cuda.synchronize()
+        good = (int(px.error.item()) == 0
+                and torch.equal(px.view("metrics").reshape(-1).view(torch.int64), want_rows.view(torch.int64))
+                and torch.equal(px.view("valid"), want_valid)
+                and torch.equal(px.view("groups").reshape(-1).view(torch.int64), want_groups.reshape(-1).view(torch.int64)))
+        verdict = torch.tensor([0 if good else 1], dtype=torch.int32, device="cuda")
+        dist.all_reduce(verdict, op=dist.ReduceOp.MAX)
+        del want_rows, want_valid, want_groups
+        if int(verdict.item()):
+            px.close()
+            px, peer = None, False
+            exchange_note = "NVLink peer exchange failed its check against NCCL after the warm-up; NCCL all-gathers used"
+            all_metrics, all_valid, all_group_out, job = exchange_buffers()
+            for _ in range(args.warmup):
+                flush.zero_()
+                step()
+            torch.cuda.synchronize()
     if peer:
         gathered = px.view("groups").cpu().numpy()
     else:
@@ -396,6 +434,10 @@ def run_b200(args, rank: int, world: int) -> dict | None:
                         ("rows_arrival_wait_ms" if peer else "exchange_rows_ms"): statistics.mean(parts_ms["exchange_rows"]),
                         "exchange_groups_ms": statistics.mean(parts_ms["exchange_groups"])},
             "roofline": roofline, "clocks": clock_info}
+    if world > 1:
+        line["exchange"] = "nvlink-peer" if peer else "nccl"
+        if exchange_note:
+            line["exchange_note"] = exchange_note
     if world == 1 and not args.no_cpu_baseline:
         line["cpu_baseline"] = cpu_baseline(records, policy)
     if not args.no_arms and world == 1:

@@ -20,6 +20,10 @@ import ctypes as C
 from . import _native as N
 
 
+class PeerExchangeError(RuntimeError):
+    """The exchange could not be set up; every rank of the group raises it together."""
+
+
 class PeerExchange:
     """Gathered row and group buffers of one rank, shared with every other rank.
 
@@ -39,27 +43,46 @@ class PeerExchange:
         total_rows = world * rows_per_rank
         sizes = (total_rows * n_metrics * 8, total_rows, (world + 1) * 4,
                  world * 3 * max(1, groups_per_rank) * n_metrics * 8, (world + 1) * 4)
-        self.own, self.opened, handles = [], [], []
-        for nbytes in sizes:
-            ptr, handle = C.c_void_p(), N.PeerHandle()
-            N.check(self.lib.pm_peer_alloc(nbytes, C.byref(ptr), C.byref(handle)), "pm_peer_alloc")
-            self.own.append(ptr.value)
-            handles.append(bytes(handle.bytes))
+        # Every rank takes both collectives below, whatever failed locally, so a
+        # failure on one rank becomes the same PeerExchangeError on all of them.
+        self.own, self.opened, handles, failure = [], [], [], None
+        try:
+            for nbytes in sizes:
+                ptr, handle = C.c_void_p(), N.PeerHandle()
+                N.check(self.lib.pm_peer_alloc(nbytes, C.byref(ptr), C.byref(handle)), "pm_peer_alloc")
+                self.own.append(ptr.value)
+                handles.append(bytes(handle.bytes))
+        except N.NativeError as exc:
+            failure = str(exc)
         everyone: list = [None] * world
-        dist.all_gather_object(everyone, handles, group=group)
+        dist.all_gather_object(everyone, None if failure else handles, group=group)
+        missing = [r for r, h in enumerate(everyone) if h is None]
+        if missing:
+            self._release()
+            raise PeerExchangeError(f"peer buffers could not be allocated on rank(s) {missing}"
+                                    + (f": {failure}" if failure else ""))
         per_rank = []
-        for r in range(world):
-            if r == rank:
-                per_rank.append(list(self.own))
-                continue
-            ptrs = []
-            for raw in everyone[r]:
-                h, q = N.PeerHandle(), C.c_void_p()
-                C.memmove(h.bytes, raw, 64)
-                N.check(self.lib.pm_peer_open(C.byref(h), C.byref(q)), "pm_peer_open")
-                self.opened.append(q.value)
-                ptrs.append(q.value)
-            per_rank.append(ptrs)
+        try:
+            for r in range(world):
+                if r == rank:
+                    per_rank.append(list(self.own))
+                    continue
+                ptrs = []
+                for raw in everyone[r]:
+                    h, q = N.PeerHandle(), C.c_void_p()
+                    C.memmove(h.bytes, raw, 64)
+                    N.check(self.lib.pm_peer_open(C.byref(h), C.byref(q)), "pm_peer_open")
+                    self.opened.append(q.value)
+                    ptrs.append(q.value)
+                per_rank.append(ptrs)
+        except N.NativeError as exc:
+            failure = str(exc)
+        opened = torch.tensor([0 if failure else 1], dtype=torch.int32, device="cuda")
+        dist.all_reduce(opened, op=dist.ReduceOp.MIN, group=group)
+        if not int(opened.item()):
+            self._release()
+            raise PeerExchangeError("another rank's buffers could not be opened"
+                                    + (f" on rank {rank}: {failure}" if failure else " (on another rank)"))
         self.rows, self.groups = N.PeerRows(), N.PeerGroups()
         self.rows.n_ranks, self.rows.rank, self.rows.row_offset, self.rows.epoch = world, rank, rank * rows_per_rank, 0
         self.groups.n_ranks, self.groups.rank, self.groups.per_rank, self.groups.epoch = world, rank, groups_per_rank, 0
@@ -125,8 +148,15 @@ class PeerExchange:
         import torch.distributed as dist
         torch.cuda.synchronize()
         dist.barrier(group=self._group)
+        self._release(check=True)
+
+    def _release(self, check: bool = False) -> None:
         for q in self.opened:
-            N.check(self.lib.pm_peer_close(C.c_void_p(q)), "pm_peer_close")
+            rc = self.lib.pm_peer_close(C.c_void_p(q))
+            if check:
+                N.check(rc, "pm_peer_close")
         for q in self.own:
-            N.check(self.lib.pm_peer_free(C.c_void_p(q)), "pm_peer_free")
+            rc = self.lib.pm_peer_free(C.c_void_p(q))
+            if check:
+                N.check(rc, "pm_peer_free")
         self.opened, self.own = [], []
