@@ -7,11 +7,14 @@ idle-delta, paired pJ/FLOP) and computes every group's medians and
 10 000-draw percentile-bootstrap intervals.  ``value`` counts
 resamples = sum over groups of (metrics with an interval) x B per second of
 device time with inputs resident in HBM (L2 flushed between steps); ``e2e``
-is the same metric through the host-buffer C-ABI call pm_analyze_sweep.
+is the same metric through the drop-in call summarize(records) on the
+runner's record dicts, and ``e2e_c_abi`` through the host-buffer C-ABI call
+pm_analyze_sweep on packed arrays.
 
 python bench.py [--gpus N] [--steps K] [--warmup W] [--impl b200|reference]
-Under torchrun each rank analyzes its own sweep (weak scaling); device time
-is the maximum over ranks.
+Under torchrun each rank analyzes its own 64 points and bootstraps their
+groups (weak scaling); the group results are gathered on rank 0 every step;
+device time is the maximum over ranks.
 """
 from __future__ import annotations
 
@@ -119,6 +122,56 @@ class ClockSampler:
                 "interval_ms": self.interval_ms}
 
 
+class NvmlPoller:
+    """SM clock, power and clock-event reasons read through NVML while the timed steps run.
+
+    The steps are enqueued ahead, so the launching thread is free while the
+    GPUs work: it polls every ~0.2 ms until the last step's event completes,
+    giving many samples inside a region of a few milliseconds (nvidia-smi's
+    loop yields one every 20 ms)."""
+    REASONS = {0x8: "hw_slowdown", 0x40: "hw_thermal_slowdown", 0x20: "sw_thermal_slowdown", 0x4: "sw_power_cap"}
+
+    def __init__(self, indices):
+        self.nv, self.handles, self.rows = None, [], []
+        try:
+            import pynvml as nv
+            nv.nvmlInit()
+            self.nv = nv
+            self.handles = [nv.nvmlDeviceGetHandleByIndex(i) for i in indices]
+        except Exception:                                  # no NVML: the nvidia-smi record stands alone
+            self.nv = None
+
+    def poll_until(self, done) -> None:
+        if self.nv is None:
+            return
+        nv = self.nv
+        while True:
+            finished = done()
+            for h in self.handles:
+                try:
+                    self.rows.append((nv.nvmlDeviceGetClockInfo(h, nv.NVML_CLOCK_SM),
+                                      nv.nvmlDeviceGetCurrentClocksEventReasons(h)))
+                except Exception:
+                    pass
+            if finished:
+                return
+            time.sleep(0.0002)
+
+    def summary(self) -> dict | None:
+        if self.nv is None:
+            return None
+        try:
+            self.nv.nvmlShutdown()
+        except Exception:
+            pass
+        if not self.rows:
+            return None
+        sm = [r[0] for r in self.rows]
+        reasons = sorted({name for _, bits in self.rows for bit, name in self.REASONS.items() if bits & bit})
+        return {"sm_mhz": statistics.median(sm), "sm_mhz_min": min(sm), "reasons": reasons, "samples": len(self.rows),
+                "source": "NVML, polled every ~0.2 ms during the timed steps"}
+
+
 # --------------------------------------------------------------------------- workload
 def build_workload(rank: int):
     """Records, packed arrays and analyzed trials of one rank's 64-point shard of the sweep."""
@@ -131,23 +184,14 @@ def build_workload(rank: int):
     return records, policy, packed, trials
 
 
-def global_groups(trials: list, world: int):
-    """Group structure of the whole sweep (every rank's trials, rank order): members as global rows, seeds."""
+def local_groups(trials: list):
+    """Groups of this rank's own trials (key order): member rows, sha256 seeds.
+
+    Every group is bootstrapped on the rank that analysed its members (the
+    sweep's points are partitioned over ranks), so no metric row leaves its GPU."""
     from powermodeling_b200 import analysis as A
-    if world > 1:
-        import torch.distributed as dist
-        light = [{k: t.get(k) for k in ("trial_id", "valid", "repeat_index", "config", "gpu_uuid", "workload",
-                                        "experiment_role", "clock_comparison_controlled", "graphics_clock_mhz",
-                                        "memory_clock_mhz", "benchmark_sha256", "measurement_stratum",
-                                        "experiment_contract", "nonlinear_contract", "sfu_contract",
-                                        "treatment_design_stratum", "resource_geometry")} for t in trials]
-        parts: list = [None] * world
-        dist.all_gather_object(parts, light)
-        everything = [t for part in parts for t in part]
-    else:
-        everything = trials
     buckets: dict[str, list[int]] = {}
-    for i, t in enumerate(everything):
+    for i, t in enumerate(trials):
         buckets.setdefault(A.group_key(t), []).append(i)
     keys = sorted(buckets)
     return [buckets[k] for k in keys], [A.group_seed(k) for k in keys]
@@ -169,21 +213,23 @@ def device_arrays(packed, torch):
 
 
 def run_b200(args, rank: int, world: int) -> dict | None:
-    """One step = analyze this rank's trials, exchange metric rows, bootstrap this rank's groups, exchange results."""
+    """One step = analyze this rank's trials, bootstrap this rank's groups, gather the group results on rank 0."""
     import torch
     import torch.distributed as dist
     from powermodeling_b200 import _native as N
     from powermodeling_b200.analysis import METRICS
-    from powermodeling_b200.distributed import owned_groups
 
     local = int(os.environ.get("LOCAL_RANK", "0"))
     torch.cuda.set_device(local)
     lib = N.library()
     records, policy, packed, host_trials_list = build_workload(rank)
-    members, seeds = global_groups(host_trials_list, world)
+    members, seeds = local_groups(host_trials_list)
     n, M, G = packed.n_trials, len(METRICS), len(members)
-    mine = owned_groups(G, world, rank)
-    per_rank = -(-G // world)
+    per_rank = G
+    if world > 1:
+        most = torch.tensor([G], dtype=torch.int64, device="cuda")
+        dist.all_reduce(most, op=dist.ReduceOp.MAX)
+        per_rank = int(most.item())
     trials, keep, in_bytes = device_arrays(packed, torch)
     PO, TO = N.layout("PM_PO_COUNT"), N.layout("PM_TO_COUNT")
     out = {"phase_out": torch.empty(n * 5 * PO, dtype=torch.float64, device="cuda"),
@@ -194,47 +240,36 @@ def run_b200(args, rank: int, world: int) -> dict | None:
            "valid": torch.empty(n, dtype=torch.uint8, device="cuda")}
     results = N.TrialResults(*(out[k].data_ptr() for k in ("phase_out", "phase_flags", "trial_out", "issue_bits", "metrics", "valid")))
     out_bytes = sum(v.numel() * v.element_size() for v in out.values())
-    # Exchange one lands every rank's metric rows and valid flags in the gathered buffers (rank order =
-    # global row order): by default the analysis kernel stores them into every rank's buffers over
-    # NVLink (peer memory, pmb200_peer.h); with --exchange nccl, an all-gather after it.
-    # If the peer exchange cannot be set up, or fails the check against NCCL after the warm-up
-    # steps, every rank takes the NCCL form instead and the line says why.
+    # Groups are owned by the rank that analysed their members, so the only
+    # exchange is the gather of every rank's group results on rank 0: by
+    # default the finish kernel stores them into rank 0's gathered buffer over
+    # NVLink (peer memory, pmb200_peer.h) and rank 0's stream waits for every
+    # rank's arrival flag of the step; with --exchange nccl, an all-gather.
+    # If the peer gather cannot be set up, or fails the check against NCCL
+    # after the warm-up steps, every rank takes the NCCL form instead and the
+    # line says why.
     peer = world > 1 and args.exchange == "peer"
     px, exchange_note = None, None
     if peer:
         from powermodeling_b200.peer import PeerExchange, PeerExchangeError
         try:
-            px = PeerExchange(rank, world, n, M, per_rank)
+            px = PeerExchange(rank, world, 0, M, per_rank, root=0)
         except PeerExchangeError as exc:
-            peer, exchange_note = False, f"NVLink peer exchange not set up ({exc}); NCCL all-gathers used"
-    own = [members[g] for g in mine]
-    offsets = np.zeros(len(own) + 1, dtype=np.int32)
-    np.cumsum([len(m) for m in own], out=offsets[1:])
-    rows = np.concatenate([np.asarray(m, dtype=np.int32) for m in own]) if own else np.zeros(1, np.int32)
+            peer, exchange_note = False, f"NVLink peer gather not set up ({exc}); NCCL all-gathers used"
+    offsets = np.zeros(G + 1, dtype=np.int32)
+    np.cumsum([len(m) for m in members], out=offsets[1:])
+    rows = np.concatenate([np.asarray(m, dtype=np.int32) for m in members]) if members else np.zeros(1, np.int32)
     d_off, d_rows = torch.from_numpy(offsets).cuda(), torch.from_numpy(rows).cuda()
-    own_seeds = np.asarray([seeds[g] for g in mine] or [0], dtype=np.uint64)
-    d_seeds = torch.from_numpy(own_seeds.view(np.int64)).cuda()
-    # Group outputs of this rank: [3, per_rank, M] (medians, lows, highs); exchange two gathers them.
+    d_seeds = torch.from_numpy(np.asarray(seeds or [0], dtype=np.uint64).view(np.int64)).cuda()
+    # Group outputs of this rank: [3, per_rank, M] (medians, lows, highs).
     group_out = torch.full((3, per_rank, M), float("nan"), dtype=torch.float64, device="cuda")
-    max_members = max((len(m) for m in own), default=1)
-
-    def exchange_buffers():
-        """Gathered rows, valid flags and group results for the current exchange form, and the job reading them."""
-        if peer:
-            a_m, a_v, a_g, m_ptr, v_ptr = None, None, None, px.metrics_ptr, px.valid_ptr
-        else:
-            a_m = torch.empty(world * n * M, dtype=torch.float64, device="cuda") if world > 1 else out["metrics"]
-            a_v = torch.empty(world * n, dtype=torch.uint8, device="cuda") if world > 1 else out["valid"]
-            a_g = torch.empty((world, 3, per_rank, M), dtype=torch.float64, device="cuda") if world > 1 else None
-            m_ptr, v_ptr = a_m.data_ptr(), a_v.data_ptr()
-        j = N.BootstrapJob(len(own), M, int(sum(len(m) for m in own)), world * n, RESAMPLES, max_members,
-                           m_ptr, d_off.data_ptr(), d_rows.data_ptr(), v_ptr,
-                           d_seeds.data_ptr(), group_out[0].data_ptr(), group_out[1].data_ptr(), group_out[2].data_ptr())
-        return a_m, a_v, a_g, j
-
-    all_metrics, all_valid, all_group_out, job = exchange_buffers()
+    all_group_out = torch.full((world, 3, per_rank, M), float("nan"), dtype=torch.float64, device="cuda") if world > 1 else None
+    max_members = max((len(m) for m in members), default=1)
+    job = N.BootstrapJob(G, M, int(sum(len(m) for m in members)), n, RESAMPLES, max_members,
+                         out["metrics"].data_ptr(), d_off.data_ptr(), d_rows.data_ptr(), out["valid"].data_ptr(),
+                         d_seeds.data_ptr(), group_out[0].data_ptr(), group_out[1].data_ptr(), group_out[2].data_ptr())
     a_scr = lib.pm_analyze_scratch_bytes(n, packed.max_phase_samples)
-    b_scr = lib.pm_bootstrap_scratch_bytes(max(1, len(own)), max_members, RESAMPLES)
+    b_scr = lib.pm_bootstrap_scratch_bytes(max(1, G), max_members, RESAMPLES)
     scratch = torch.empty(max(1, a_scr + b_scr), dtype=torch.uint8, device="cuda")
     flush = torch.empty(256 * 1024 * 1024 // 4, dtype=torch.float32, device="cuda")
     stream = torch.cuda.current_stream()
@@ -242,105 +277,118 @@ def run_b200(args, rank: int, world: int) -> dict | None:
     sptr, side_ptr = C.c_void_p(stream.cuda_stream), C.c_void_p(side.cuda_stream)
     boot_scratch = C.c_void_p(scratch.data_ptr() + a_scr)
     native_policy = policy.native()
-    ev = [torch.cuda.Event(enable_timing=True) for _ in range(5)]
-    side_ev = [torch.cuda.Event(enable_timing=True) for _ in range(2)]
 
-    def step():
+    def step(ev, side_ev):
         # The resample draws need only seeds and group sizes: drawn on a side
-        # stream while this rank's trials are analysed and the rows exchanged.
+        # stream while this rank's trials are analysed.
         ev[0].record(stream)
         side.wait_event(ev[0])
         side_ev[0].record(side)
-        if own:
+        if G:
             N.check(lib.pm_bootstrap_prepare_device(job, boot_scratch, b_scr, side_ptr), "prepare")
         side_ev[1].record(side)
+        N.check(lib.pm_analyze_trials_device(trials, native_policy, results, C.c_void_p(scratch.data_ptr()), a_scr, sptr),
+                "analyze")
+        ev[1].record(stream)
+        stream.wait_event(side_ev[1])
+        ev[2].record(stream)
         if peer:
             px.next_epoch()
-            N.check(lib.pm_analyze_trials_device_exchange(trials, native_policy, results, C.c_void_p(scratch.data_ptr()),
-                                                          a_scr, C.byref(px.rows), sptr), "analyze + row exchange")
-        else:
-            N.check(lib.pm_analyze_trials_device(trials, native_policy, results, C.c_void_p(scratch.data_ptr()), a_scr, sptr), "analyze")
-        ev[1].record(stream)
-        if peer:
-            px.wait_rows(stream.cuda_stream)
-        elif world > 1:
-            dist.all_gather_into_tensor(all_metrics, out["metrics"])
-            dist.all_gather_into_tensor(all_valid, out["valid"])
-        ev[2].record(stream)
-        stream.wait_event(side_ev[1])
-        if peer:
             N.check(lib.pm_bootstrap_finish_device_exchange(job, boot_scratch, b_scr, C.byref(px.groups), sptr),
-                    "finish + group exchange")
-        elif own:
+                    "finish + group gather")
+        elif G:
             N.check(lib.pm_bootstrap_finish_device(job, boot_scratch, b_scr, sptr), "finish")
         ev[3].record(stream)
         if peer:
-            px.wait_groups(stream.cuda_stream)
+            if rank == 0:
+                px.wait_groups(stream.cuda_stream)
         elif world > 1:
             dist.all_gather_into_tensor(all_group_out, group_out)
         ev[4].record(stream)
 
+    def new_events(k):
+        return ([[torch.cuda.Event(enable_timing=True) for _ in range(5)] for _ in range(k)],
+                [[torch.cuda.Event(enable_timing=True) for _ in range(2)] for _ in range(k)])
+
+    def run_steps(k):
+        """k steps enqueued back to back (L2 flushed before each, outside its events); no host wait between them."""
+        evs, side_evs = new_events(k)
+        if peer:
+            px.gate(stream.cuda_stream)                 # every rank's GPU starts the steps together
+        for i in range(k):
+            flush.zero_()
+            step(evs[i], side_evs[i])
+        return evs, side_evs
+
     if world > 1:
         torch.cuda.synchronize()
-        dist.barrier()                                  # every rank launches its first step together
-    for _ in range(args.warmup):
-        flush.zero_()
-        step()
+        dist.barrier()
+    run_steps(args.warmup)
     torch.cuda.synchronize()
     if peer:
-        # The rows and group results the kernels stored into this rank must equal NCCL
-        # all-gathers of every rank's own outputs, bit for bit, and no arrival wait may have expired.
-        want_rows = torch.empty(world * n * M, dtype=torch.float64, device="cuda")
-        want_valid = torch.empty(world * n, dtype=torch.uint8, device="cuda")
+        # The group results the kernels stored into rank 0 must equal an NCCL
+        # all-gather of every rank's own outputs, bit for bit (each rank's owned
+        # slots), and no arrival wait may have expired.
         want_groups = torch.empty((world, 3, per_rank, M), dtype=torch.float64, device="cuda")
-        dist.all_gather_into_tensor(want_rows, out["metrics"])
-        dist.all_gather_into_tensor(want_valid, out["valid"])
         dist.all_gather_into_tensor(want_groups, group_out)
+        counts = torch.tensor([G], dtype=torch.int64, device="cuda")
+        all_counts = torch.empty(world, dtype=torch.int64, device="cuda")
+        dist.all_gather_into_tensor(all_counts, counts)
         torch.cuda.synchronize()
-        good = (int(px.error.item()) == 0
-                and torch.equal(px.view("metrics").reshape(-1).view(torch.int64), want_rows.view(torch.int64))
-                and torch.equal(px.view("valid"), want_valid)
-                and torch.equal(px.view("groups").reshape(-1).view(torch.int64), want_groups.reshape(-1).view(torch.int64)))
+        good = int(px.error.item()) == 0
+        if rank == 0:
+            got = px.view("groups")
+            for r in range(world):
+                c = int(all_counts[r].item())
+                good = good and torch.equal(got[r, :, :c].reshape(-1).view(torch.int64),
+                                            want_groups[r, :, :c].reshape(-1).view(torch.int64))
         verdict = torch.tensor([0 if good else 1], dtype=torch.int32, device="cuda")
         dist.all_reduce(verdict, op=dist.ReduceOp.MAX)
-        del want_rows, want_valid, want_groups
+        del want_groups
         if int(verdict.item()):
             px.close()
             px, peer = None, False
-            exchange_note = "NVLink peer exchange failed its check against NCCL after the warm-up; NCCL all-gathers used"
-            all_metrics, all_valid, all_group_out, job = exchange_buffers()
-            for _ in range(args.warmup):
-                flush.zero_()
-                step()
+            exchange_note = "NVLink peer gather failed its check against NCCL after the warm-up; NCCL all-gathers used"
+            run_steps(args.warmup)
             torch.cuda.synchronize()
-    if peer:
-        gathered = px.view("groups").cpu().numpy()
-    else:
-        gathered = (all_group_out if world > 1 else group_out.unsqueeze(0)).cpu().numpy()
-    resamples_per_step = int(np.isfinite(gathered[:, 1]).sum()) * RESAMPLES
-    # group g was bootstrapped by rank g % world as its (g // world)-th group
-    lo_global = np.stack([gathered[g % world, 1, g // world] for g in range(G)])
-    # correctness guard on the timed configuration: every trial valid, every group filled
+    # correctness guard on the timed configuration: every trial valid
     assert int(out["valid"].sum().item()) == n, "synthetic trials must all be valid"
+    finite = torch.tensor([int(np.isfinite(group_out[1].cpu().numpy()).sum())], dtype=torch.int64, device="cuda")
+    if world > 1:
+        dist.all_reduce(finite)
+    resamples_per_step = int(finite.item()) * RESAMPLES
+    lo_local = group_out[1].cpu().numpy()
     if world > 1:
         dist.barrier()
     torch.cuda.synchronize()
-    clocks = ClockSampler(local)
-    clocks.start()
-    clocks.mark_begin()
-    parts_ms = {"analyze": [], "exchange_rows": [], "join_and_finish": [], "exchange_groups": []}
+    clocks = ClockSampler(",".join(str(i) for i in range(world))) if rank == 0 else None
+    if clocks:
+        clocks.start()
+    if world > 1:
+        dist.barrier()
+    torch.cuda.synchronize()
+    poller = NvmlPoller(range(world)) if rank == 0 else None
+    if clocks:
+        clocks.mark_begin()
+    evs, side_evs = run_steps(args.steps)
+    if poller:
+        poller.poll_until(evs[-1][4].query)
+    torch.cuda.synchronize()
+    if clocks:
+        clocks.mark_end()
+    clock_info = clocks.stop() if clocks else None
+    if poller and (polled := poller.summary()):
+        clock_info = dict(clock_info or {}, nvidia_smi_samples=(clock_info or {}).get("samples"),
+                          sm_mhz=polled["sm_mhz"], sm_mhz_min=polled["sm_mhz_min"],
+                          reasons=sorted(set(polled["reasons"]) | set((clock_info or {}).get("reasons") or [])),
+                          samples=polled["samples"], source=polled["source"])
+    parts_ms = {"analyze": [], "join": [], "finish": [], "gather_groups": []}
     prepare_ms, step_ms = [], []
-    for _ in range(args.steps):
-        flush.zero_()                                   # L2 flush, outside the timed events
-        step()
-        ev[4].synchronize()
+    for ev, side_ev in zip(evs, side_evs):
         for k, name in enumerate(parts_ms):
             parts_ms[name].append(ev[k].elapsed_time(ev[k + 1]))
         prepare_ms.append(side_ev[0].elapsed_time(side_ev[1]))
         step_ms.append(ev[0].elapsed_time(ev[4]))
-    torch.cuda.synchronize()
-    clocks.mark_end()
-    clock_info = clocks.stop()
     if world > 1:
         dist.barrier()
     total_ms = sum(step_ms)
@@ -350,89 +398,98 @@ def run_b200(args, rank: int, world: int) -> dict | None:
         total_ms = float(t.item())
     ms_per_step = total_ms / args.steps
     value = resamples_per_step / (ms_per_step / 1e3)
-    t_analyze, t_boot = parts_ms["analyze"], parts_ms["join_and_finish"]
+    t_analyze, t_finish = parts_ms["analyze"], parts_ms["finish"]
 
-    # ---- end to end: host buffers through pm_analyze_sweep, then one gather of group results --------
-    # Each rank's groups are its own points, so a rank summarizes its shard with one library call
-    # (H2D of the packed trials, both kernels, D2H of every result) and the group results are
-    # all-gathered (H2D, NCCL, D2H) inside the timed region.
+    # ---- end to end ------------------------------------------------------------------------------
+    # e2e: the drop-in call itself, summarize(records) (analysis.py:1400), on the runner's record
+    # dicts: record checks and packing, H2D, both kernels, D2H, issue strings and the trial and
+    # group dicts.  Each rank summarizes its own points (weak scaling).
+    # e2e_c_abi: the same numeric work through the host-buffer C-ABI call pm_analyze_sweep on the
+    # packed arrays (H2D of the packed trials and group inputs, D2H of every result).
+    from powermodeling_b200 import analysis as A
     from powermodeling_b200.pack import trials_struct
     host_trials = trials_struct(packed)
-    base = rank * n
-    local_groups = [g for g, m in enumerate(members) if m and all(base <= i < base + n for i in m)]
-    l_members = [[i - base for i in members[g]] for g in local_groups]
-    Gl = len(local_groups)
-    l_off = np.zeros(Gl + 1, dtype=np.int32)
-    np.cumsum([len(m) for m in l_members], out=l_off[1:])
-    l_rows = np.concatenate([np.asarray(m, dtype=np.int32) for m in l_members])
-    l_seeds = np.asarray([seeds[g] for g in local_groups], dtype=np.uint64)
     h_out = {"phase_out": np.empty(n * 5 * PO), "phase_flags": np.empty(n * 5, dtype=np.uint32),
              "trial_out": np.empty(n * TO), "issue_bits": np.empty(n * 4, dtype=np.uint64),
              "metrics": np.empty(n * M), "valid": np.empty(n, dtype=np.uint8)}
     h_results = N.TrialResults(*(h_out[k].ctypes.data for k in ("phase_out", "phase_flags", "trial_out", "issue_bits", "metrics", "valid")))
-    h_groups = np.empty((3, Gl, M))
-    h_job = N.BootstrapJob(Gl, M, int(l_rows.size), n, RESAMPLES, 0, None, l_off.ctypes.data, l_rows.ctypes.data, None,
-                           l_seeds.ctypes.data, h_groups[0].ctypes.data, h_groups[1].ctypes.data, h_groups[2].ctypes.data)
-    g_send = torch.empty((3, Gl, M), dtype=torch.float64, device="cuda")
-    g_recv = torch.empty((world, 3, Gl, M), dtype=torch.float64, device="cuda")
+    h_groups = np.empty((3, G, M))
+    h_seeds = np.asarray(seeds, dtype=np.uint64)
+    h_job = N.BootstrapJob(G, M, int(rows.size), n, RESAMPLES, 0, None, offsets.ctypes.data, rows.ctypes.data, None,
+                           h_seeds.ctypes.data, h_groups[0].ctypes.data, h_groups[1].ctypes.data, h_groups[2].ctypes.data)
 
-    def e2e_step():
-        N.check(lib.pm_analyze_sweep(host_trials, native_policy, h_results, h_job), "pm_analyze_sweep")
+    def timed(fn):
+        for _ in range(args.warmup):
+            fn()
         if world > 1:
-            g_send.copy_(torch.from_numpy(h_groups))
-            dist.all_gather_into_tensor(g_recv, g_send)
-            return g_recv.cpu().numpy()
-        return h_groups[None]
+            dist.barrier()
+        times = []
+        for _ in range(args.steps):
+            t0 = time.perf_counter()
+            fn()
+            times.append(time.perf_counter() - t0)
+        mean = sum(times) / len(times)
+        if world > 1:
+            t = torch.tensor([mean], dtype=torch.float64, device="cuda")
+            dist.all_reduce(t, op=dist.ReduceOp.MAX)
+            mean = float(t.item())
+        return mean
 
-    for _ in range(args.warmup):
-        e2e_step()
-    if world > 1:
-        dist.barrier()
-    e2e_times = []
-    for _ in range(args.steps):
-        t0 = time.perf_counter()
-        e2e_step()
-        e2e_times.append(time.perf_counter() - t0)
-    e2e_s = sum(e2e_times) / args.steps
-    if world > 1:
-        t = torch.tensor([e2e_s], dtype=torch.float64, device="cuda")
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        e2e_s = float(t.item())
-    assert np.array_equal(np.nan_to_num(h_groups[1]), np.nan_to_num(lo_global[local_groups])), \
-        "e2e and device paths disagree"
+    c_abi_s = timed(lambda: N.check(lib.pm_analyze_sweep(host_trials, native_policy, h_results, h_job), "pm_analyze_sweep"))
+    assert np.array_equal(np.nan_to_num(h_groups[1]), np.nan_to_num(lo_local[:G])), "C-ABI and device paths disagree"
+    summary = {}
+
+    def api_step():
+        summary["last"] = A.summarize(records, policy=policy, resamples=RESAMPLES)
+
+    api_s = timed(api_step)
+    api_groups = summary["last"]["groups"]
+    assert len(api_groups) == G
+    for g, group in enumerate(api_groups):
+        for m, metric in enumerate(METRICS):
+            ci = group["ci95"].get(metric)
+            want = lo_local[g, m]
+            assert (ci is None and not np.isfinite(want)) or (ci is not None and ci[0] == want), \
+                f"summarize and device paths disagree (group {g}, {metric})"
     if peer:
         px.check()
         px.close()
-    h2d = in_bytes + l_off.nbytes + l_rows.nbytes + l_seeds.nbytes + (h_groups.nbytes if world > 1 else 0)
-    d2h = sum(a.nbytes for a in h_out.values()) + h_groups.nbytes * (world + 1 if world > 1 else 1)
+    c_h2d = in_bytes + offsets.nbytes + rows.nbytes + h_seeds.nbytes
+    c_d2h = sum(a.nbytes for a in h_out.values()) + h_groups.nbytes
+    # summarize uploads the packed trials, then the metric and memory-rail rows with the group
+    # inputs, and reads back every trial result and every group's medians and interval ends.
+    width = M + len(A.SENSOR_FIELDS)
+    api_h2d = in_bytes + n * width * 8 + offsets.nbytes + rows.nbytes + h_seeds.nbytes
+    api_d2h = sum(a.nbytes for a in h_out.values()) + 3 * G * width * 8
     if rank != 0:
         return None
     peaks = measured_peaks()
-    a_ms, b_ms = statistics.mean(t_analyze), statistics.mean(t_boot)
-    dominant = "bootstrap_kernel" if b_ms >= a_ms else "analyze_kernel"
-    roofline = roofline_entry(dominant, a_ms, b_ms, in_bytes, out_bytes, len(own), M, packed, peaks,
-                              resamples_per_step)
+    a_ms, f_ms, p_ms = statistics.mean(t_analyze), statistics.mean(t_finish), statistics.mean(prepare_ms)
+    roofline = roofline_entry(a_ms, p_ms, f_ms, in_bytes, out_bytes, G, M, packed, peaks,
+                              (clock_info or {}).get("sm_mhz"))
     line = {"metric": METRIC, "value": value, "unit": "resamples/s", "n_gpus": world, "steps": args.steps,
             "warmup": args.warmup, "ms_per_step": ms_per_step, "higher_is_better": True, "scaling": "weak",
             "vs_baseline": None, "dtype": "f64", "data": "synthetic",
             "config": {"workload": WORKLOAD, "points": POINTS * world, "points_per_gpu": POINTS, "repeats": REPEATS,
-                       "trials": n * world, "groups": G,
+                       "trials": n * world, "groups": G * world,
                        "resamples": RESAMPLES, "samples": packed.n_samples, "l2": "flushed (256 MiB write) between steps",
-                       "parallelism": (f"sweep-sharded x{world}: trials and groups per rank; metric rows and group "
-                                       f"results stored into every rank by the analysis and bootstrap kernels over "
-                                       f"NVLink peer memory" if peer else
-                                       f"sweep-sharded x{world}: trials and groups per rank, rows and group results "
-                                       f"all-gathered over NCCL") if world > 1 else "single GPU"},
-            "e2e": {"value": resamples_per_step / e2e_s, "unit": "resamples/s",
-                    "h2d_bytes_per_step": int(h2d), "d2h_bytes_per_step": int(d2h), "ms_per_step": e2e_s * 1e3},
-            # per step: analyze, the draws and the finish (or, owning no group, analyze and the
-            # group signal), plus the two arrival waits of the peer exchange
-            "gpu_launches": ((3 if own else 2) if peer else (3 if own else 1)) * args.steps + (2 * args.steps if peer else 0),
+                       "parallelism": (f"sweep-partitioned x{world}: each rank analyses its points and bootstraps their "
+                                       f"groups; group results gathered on rank 0 " +
+                                       ("by the finish kernel's NVLink peer stores" if peer else "by NCCL all-gathers"))
+                       if world > 1 else "single GPU"},
+            "e2e": {"value": resamples_per_step / api_s, "unit": "resamples/s",
+                    "h2d_bytes_per_step": int(api_h2d), "d2h_bytes_per_step": int(api_d2h), "ms_per_step": api_s * 1e3,
+                    "call": "summarize(records): record dicts in, summary dicts out"},
+            "e2e_c_abi": {"value": resamples_per_step / c_abi_s, "unit": "resamples/s", "h2d_bytes_per_step": int(c_h2d),
+                          "d2h_bytes_per_step": int(c_d2h), "ms_per_step": c_abi_s * 1e3,
+                          "call": "pm_analyze_sweep on packed host arrays"},
+            # per step: analyze, the draws and the finish, plus rank 0's arrival wait of the peer gather
+            "gpu_launches": 3 * args.steps + (args.steps if peer else 0),
             "kernels": {"analyze_kernel_ms": a_ms,
-                        "bootstrap_prepare_kernel_ms (side stream, overlaps analyze)": statistics.mean(prepare_ms),
-                        "join_and_bootstrap_finish_ms": b_ms,
-                        ("rows_arrival_wait_ms" if peer else "exchange_rows_ms"): statistics.mean(parts_ms["exchange_rows"]),
-                        "exchange_groups_ms": statistics.mean(parts_ms["exchange_groups"])},
+                        "bootstrap_prepare_kernel_ms (side stream, overlaps analyze)": p_ms,
+                        "join_wait_ms": statistics.mean(parts_ms["join"]),
+                        "bootstrap_finish_kernel_ms": f_ms,
+                        "gather_groups_ms (rank 0)": statistics.mean(parts_ms["gather_groups"])},
             "roofline": roofline, "clocks": clock_info}
     if world > 1:
         line["exchange"] = "nvlink-peer" if peer else "nccl"
@@ -678,25 +735,51 @@ def run_nonlinear_arms(sms: int, peaks: dict) -> dict:
     return out
 
 
-# DRAM bytes (read + write) per launch from one ncu capture of the same
-# workload (profiles/analysis_sweep_64x4_B10000.md); None where none was taken.
-NCU_TRAFFIC_BYTES = {"analyze_kernel": 5_149_184, "bootstrap_kernel": 183_040}
+# Per launch, from one ncu capture of this workload (the committed analysis
+# profile summary): warp instructions executed (smsp__inst_executed.sum) and
+# DRAM bytes read + written.  The kernels are deterministic for the fixed
+# seeds, so the counts are the same on every launch; None where not captured.
+NCU_PER_LAUNCH = {
+    "analyze_kernel": {"inst": None, "dram": 5_149_184},
+    "bootstrap_prepare_kernel": {"inst": None, "dram": None},
+    "bootstrap_kernel<0>": {"inst": None, "dram": 183_040},
+}
+# Blackwell SM: four schedulers, each issuing one warp instruction per clock.
+ISSUE_PER_SM_CLOCK = 4
+SMS = 148
 
 
-def roofline_entry(dominant, a_ms, b_ms, in_bytes, out_bytes, G, M, packed, peaks, resamples):
+def roofline_entry(a_ms, p_ms, f_ms, in_bytes, out_bytes, G, M, packed, peaks, sm_mhz=None):
+    """The longest of the three kernels against the bound that limits it.
+
+    The analysis step moves a few MB and does integer/FP64 work per sample
+    and per draw, so its roof is instruction issue: warp instructions per
+    launch (ncu) over the launch's CUDA-event time, against 4 per SM per
+    clock x 148 SMs x the SM clock sampled during the timed steps.  The HBM
+    figure of the analysis kernel (input + output bytes over its time) rides
+    along for comparison."""
     hbm = peaks.get("hbm_gbs", 6650.0)
     src = "measured" if not peaks.get("fallback") else "fallback"
-    if dominant == "analyze_kernel":
+    times = {"analyze_kernel": a_ms, "bootstrap_prepare_kernel": p_ms, "bootstrap_kernel<0>": f_ms}
+    dominant = max(times, key=times.get)
+    ms = times[dominant]
+    counts = NCU_PER_LAUNCH[dominant]
+    clock = sm_mhz or peaks.get("sm_max_mhz", 1965.0)
+    issue_peak = ISSUE_PER_SM_CLOCK * SMS * clock * 1e6 / 1e9           # G warp-instructions/s
+    entry = {"kernel": dominant, "launch_ms": ms, "traffic": counts["dram"],
+             "analyze_kernel_hbm": {"achieved_gbs": (in_bytes + out_bytes) / (a_ms / 1e3) / 1e9, "peak_gbs": hbm,
+                                    "frac": (in_bytes + out_bytes) / (a_ms / 1e3) / 1e9 / hbm,
+                                    "algorithmic_bytes": in_bytes + out_bytes, "peak_source": src}}
+    if counts["inst"] is not None:
+        achieved = counts["inst"] / (ms / 1e3) / 1e9
+        entry.update(bound="issue", achieved=achieved, peak=issue_peak, unit="G warp-instructions/s",
+                     frac=achieved / issue_peak, instructions=counts["inst"],
+                     peak_source=f"{ISSUE_PER_SM_CLOCK} warp instructions/clk/SM x {SMS} SMs x {clock:.0f} MHz (sampled)")
+    else:
         achieved = (in_bytes + out_bytes) / (a_ms / 1e3) / 1e9
-        return {"kernel": dominant, "bound": "hbm", "achieved": achieved, "peak": hbm, "unit": "GB/s",
-                "frac": achieved / hbm, "traffic": NCU_TRAFFIC_BYTES["analyze_kernel"], "peak_source": src,
-                "algorithmic_bytes": in_bytes + out_bytes}
-    # The bootstrap kernel moves a few KB; its bound is the MT19937 stream (2 words per draw).
-    words = 2 * 4 * RESAMPLES * G
-    achieved = words * 4 / (b_ms / 1e3) / 1e9
-    return {"kernel": dominant, "bound": "hbm", "achieved": achieved, "peak": hbm, "unit": "GB/s",
-            "frac": achieved / hbm, "traffic": NCU_TRAFFIC_BYTES["bootstrap_kernel"], "peak_source": src,
-            "note": "random-stream bytes generated per launch; the kernel is latency-bound on the sequential MT19937 twist"}
+        entry.update(kernel="analyze_kernel", bound="hbm", achieved=achieved, peak=hbm, unit="GB/s", frac=achieved / hbm,
+                     traffic=NCU_PER_LAUNCH["analyze_kernel"]["dram"], peak_source=src)
+    return entry
 
 
 # --------------------------------------------------------------------------- CPU arms
@@ -762,7 +845,7 @@ def main():
     parser.add_argument("--warmup", type=int, default=5)
     parser.add_argument("--impl", choices=("b200", "reference"), default="b200")
     parser.add_argument("--exchange", choices=("peer", "nccl"), default="peer",
-                        help="N>1: metric rows stored into every rank by the analysis kernel over NVLink, or all-gathered by NCCL")
+                        help="N>1: group results stored into rank 0 by the bootstrap kernel over NVLink, or all-gathered by NCCL")
     parser.add_argument("--no-cpu-baseline", action="store_true")
     parser.add_argument("--no-arms", action="store_true", help="skip the HBM/tensor/GEMM/SFU arm measurements")
     args = parser.parse_args()

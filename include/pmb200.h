@@ -268,6 +268,15 @@ int pm_tensor_probe(int accumulators, uint64_t iterations, int uniform, uint64_t
                     size_t out_count, uint16_t* a_out, uint16_t* b_out);
 
 /*
+ * The powerbench gemm arm's own cuBLAS call (cublasGemmEx, fp16 A and B,
+ * fp32 C, column-major, the arm's operand fill; cuda/gpu_bench.cu:784-790 is
+ * the reference's call) once on m x k by k x n (each 1..4096): C to `out`
+ * (m * n floats, column-major), optionally the operands too.  It checks the
+ * library comparison arm numerically.
+ */
+int pm_gemm_probe(int m, int n, int k, int uniform, uint64_t seed, float* out, uint16_t* a_out, uint16_t* b_out);
+
+/*
  * pm_group_bootstrap_device for callers that cannot allocate device memory
  * (a process whose own pool owns the whole device, a runtime that forbids
  * foreign allocations, a service that must fix the library's footprint in

@@ -65,25 +65,29 @@ typedef struct pm_peer_rows {
 int pm_analyze_trials_device_exchange(const pm_trials* trials, const pm_policy* policy, pm_trial_results* out,
                                       void* scratch, size_t scratch_bytes, const pm_peer_rows* rows, void* stream);
 
-/* Where a bootstrap finish on rank `rank` delivers its groups: each rank's
- * gathered buffer is [n_ranks][3][per_rank][n_metrics] (medians, interval
- * lows, interval highs), this rank's local group j going to
- * [rank][k][j]. */
+/* Where a bootstrap finish on rank `rank` delivers its groups: each
+ * receiving rank's gathered buffer is [n_ranks][3][per_rank][n_metrics]
+ * (medians, interval lows, interval highs), this rank's local group j going
+ * to [rank][k][j].  root < 0: every rank receives (an all-gather); root >= 0:
+ * only rank `root` does (a gather), and out[r] / flags[r] of the other ranks
+ * may be NULL. */
 typedef struct pm_peer_groups {
   int32_t n_ranks;                    /* 1..PM_MAX_RANKS */
   int32_t rank;                       /* this rank */
   int32_t per_rank;                   /* group stride: groups owned per rank (>= this launch's n_groups) */
   uint32_t epoch;                     /* > the previous launch's epoch */
-  double* out[PM_MAX_RANKS];          /* each rank's gathered group buffer */
-  uint32_t* flags[PM_MAX_RANKS];      /* each rank's arrival flags [n_ranks]; this rank sets entry `rank` */
+  double* out[PM_MAX_RANKS];          /* each receiving rank's gathered group buffer */
+  uint32_t* flags[PM_MAX_RANKS];      /* each receiving rank's arrival flags [n_ranks]; this rank sets entry `rank` */
   uint32_t* done;                     /* this rank's CTA counter (starts at 0) */
+  int32_t root;                       /* -1: all-gather; 0..n_ranks-1: gather to that rank only */
 } pm_peer_groups;
 
 /* pm_bootstrap_finish_device, plus every group's medians and interval ends
- * stored into every rank's gathered buffer, and this rank's flag raised to
- * `epoch` on every rank once they are all out (at once when this rank owns
- * no group).  Same epoch rules as pm_analyze_trials_device_exchange, with
- * the group count in place of the trial count. */
+ * stored into every receiving rank's gathered buffer, and this rank's flag
+ * raised to `epoch` on every receiving rank once they are all out (at once
+ * when this rank owns no group).  Same epoch rules as
+ * pm_analyze_trials_device_exchange, with the group count in place of the
+ * trial count. */
 int pm_bootstrap_finish_device_exchange(const pm_bootstrap_job* job, void* scratch, size_t scratch_bytes,
                                         const pm_peer_groups* groups, void* stream);
 
@@ -92,6 +96,15 @@ int pm_bootstrap_finish_device_exchange(const pm_bootstrap_job* job, void* scrat
  * kernel stores 1 into *error (device memory) and returns. */
 int pm_peer_wait_device(const uint32_t* flags, int32_t n_ranks, uint32_t epoch, uint32_t timeout_ms, int32_t* error,
                         void* stream);
+
+/* A device-side start line for all ranks: store `epoch` into entry `rank` of
+ * every rank's flag array (flags[r], n_ranks entries each, system-scope
+ * release stores), then hold `stream` until this rank's own array
+ * (flags[rank]) has every entry at `epoch` or beyond.  Ranks whose hosts
+ * enqueue work after it at different moments start that work together on
+ * their GPUs.  The wait is bounded like pm_peer_wait_device's. */
+int pm_peer_gate_device(uint32_t* const* flags, int32_t n_ranks, int32_t rank, uint32_t epoch, uint32_t timeout_ms,
+                        int32_t* error, void* stream);
 
 #ifdef __cplusplus
 }

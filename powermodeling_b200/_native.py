@@ -124,7 +124,7 @@ class PeerRows(C.Structure):
 
 class PeerGroups(C.Structure):
     _fields_ = [("n_ranks", C.c_int32), ("rank", C.c_int32), ("per_rank", C.c_int32), ("epoch", C.c_uint32),
-                ("out", _p * MAX_RANKS), ("flags", _p * MAX_RANKS), ("done", _p)]
+                ("out", _p * MAX_RANKS), ("flags", _p * MAX_RANKS), ("done", _p), ("root", C.c_int32)]
 
 
 class NativeError(RuntimeError):
@@ -170,6 +170,7 @@ def library() -> C.CDLL:
             lib.pm_analyze_trials_device_exchange.argtypes = [C.POINTER(Trials), C.POINTER(Policy), C.POINTER(TrialResults),
                                                               _p, C.c_size_t, C.POINTER(PeerRows), _p]
             lib.pm_peer_wait_device.argtypes = [_p, C.c_int32, C.c_uint32, C.c_uint32, _p, _p]
+            lib.pm_peer_gate_device.argtypes = [C.POINTER(_p), C.c_int32, C.c_int32, C.c_uint32, C.c_uint32, _p, _p]
             lib.pm_bootstrap_finish_device_exchange.argtypes = [C.POINTER(BootstrapJob), _p, C.c_size_t,
                                                                 C.POINTER(PeerGroups), _p]
             lib.pm_nonlinear_fill_device.argtypes = [_p, C.c_uint64, C.c_uint64, C.c_float, C.c_int, _p]

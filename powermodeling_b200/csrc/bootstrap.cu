@@ -19,6 +19,9 @@
 // folds bins into (rank_a, rank_b) median pairs whose values are sorted once.
 // For n >= 8 each draw's median rank pair is binned directly per metric from
 // an index stream kept in global scratch.
+#include <atomic>
+#include <mutex>
+
 #include "pmb200.h"
 #include "pm_layout.h"
 #include "pm_device.cuh"
@@ -656,35 +659,41 @@ __global__ void __launch_bounds__(kBootThreads) bootstrap_kernel(BootArgs A, pm_
   }
 }
 
-// Deliver the CTA's group (medians, lows, highs) to every rank's gathered
-// buffer (peer stores over NVLink); the last CTA of the launch raises this
-// rank's arrival flag on every rank.  The barrier orders the CTA's stores
-// before thread 0's acquire-release count (GPU scope: every counting CTA is
-// on this GPU), and the last CTA releases them all with its system-scope
-// flag stores.
+// Deliver the CTA's group (medians, lows, highs) to the gathered buffer of
+// every receiving rank (all of them, or only X.root) with peer stores over
+// NVLink; the last CTA of the launch raises this rank's arrival flag there.
+// The barrier orders the CTA's stores before thread 0's acquire-release count
+// (GPU scope: every counting CTA is on this GPU), and the last CTA releases
+// them all with its system-scope flag stores.
+__device__ __forceinline__ bool receives(const pm_peer_groups& X, int r) { return X.root < 0 || r == X.root; }
+
 __device__ __noinline__ void deliver_groups(const pm_peer_groups& X, const BootArgs& A, int g) {
   const int M = A.n_metrics;
-  for (int r = 0; r < X.n_ranks; ++r)
+  for (int r = 0; r < X.n_ranks; ++r) {
+    if (!receives(X, r)) continue;
     for (int i = threadIdx.x; i < 3 * M; i += blockDim.x) {
       const int k = i / M, m = i - k * M;
       const double* src = k == 0 ? A.medians : k == 1 ? A.lo : A.hi;
       X.out[r][(((size_t)X.rank * 3 + k) * X.per_rank + g) * M + m] = src[(size_t)g * M + m];
     }
+  }
   __syncthreads();
   if (threadIdx.x == 0) {
     uint32_t prev;
     asm volatile("atom.add.acq_rel.gpu.global.u32 %0, [%1], 1;" : "=r"(prev) : "l"(X.done) : "memory");
     if (prev + 1u == X.epoch * gridDim.x)
       for (int r = 0; r < X.n_ranks; ++r)
-        asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(X.flags[r] + X.rank), "r"(X.epoch) : "memory");
+        if (receives(X, r))
+          asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(X.flags[r] + X.rank), "r"(X.epoch) : "memory");
   }
 }
 
-// This rank owns no group: raise its arrival flag on every rank at once.
+// This rank owns no group: raise its arrival flag on every receiving rank at once.
 __global__ void signal_groups_kernel(pm_peer_groups X) {
   if (threadIdx.x == 0)
     for (int r = 0; r < X.n_ranks; ++r)
-      asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(X.flags[r] + X.rank), "r"(X.epoch) : "memory");
+      if (receives(X, r))
+        asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(X.flags[r] + X.rank), "r"(X.epoch) : "memory");
 }
 
 // Raw index stream (diagnostic): out[r*n + j] for one seed, by one CTA.
@@ -719,11 +728,16 @@ __global__ void resample_indices_kernel(uint64_t seed, int n, int B, int32_t* ou
 }
 
 // ---------------------------------------------------------------------------
-static bool g_constants_ready[64] = {};
+// Generator constants uploaded per device, once: host threads calling on the
+// same device take the lock; a device whose upload is done skips it.
+static std::atomic<bool> g_constants_ready[64];
+static std::mutex g_constants_lock;
 
 int prepare_bootstrap_constants(int device) {
   if (device < 0 || device >= 64) return 1;
-  if (g_constants_ready[device]) return 0;
+  if (g_constants_ready[device].load(std::memory_order_acquire)) return 0;
+  std::lock_guard<std::mutex> guard(g_constants_lock);
+  if (g_constants_ready[device].load(std::memory_order_relaxed)) return 0;
   uint32_t init[kMtN];
   init[0] = 19650218u;
   for (int i = 1; i < kMtN; ++i) init[i] = 1812433253u * (init[i - 1] ^ (init[i - 1] >> 30)) + (uint32_t)i;
@@ -734,7 +748,7 @@ int prepare_bootstrap_constants(int device) {
   }
   if (cudaMemcpyToSymbol(c_mt_init, init, sizeof(init)) != cudaSuccess) return 2;
   if (cudaMemcpyToSymbol(c_binom, binom, sizeof(binom)) != cudaSuccess) return 2;
-  g_constants_ready[device] = true;
+  g_constants_ready[device].store(true, std::memory_order_release);
   return 0;
 }
 

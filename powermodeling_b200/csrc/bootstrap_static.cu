@@ -49,24 +49,17 @@ using namespace pm;
 extern "C" size_t pm_bootstrap_static_scratch_capacity(void) { return kStaticStreamBytes; }
 
 extern "C" int pm_group_bootstrap_device_static(const pm_bootstrap_job* job, void* stream) {
-  if (!job) return fail(PM_E_INVALID, "pm_group_bootstrap_device_static: NULL job");
-  if (job->n_groups < 0 || job->n_metrics <= 0 || job->n_metrics > kMaxMetrics || job->n_members < 0)
-    return fail(PM_E_INVALID, "pm_group_bootstrap_device_static: bad sizes");
-  if (job->resamples < 40 || job->resamples > (1 << 24))
-    return fail(PM_E_INVALID, "pm_group_bootstrap_device_static: resamples must be in [40, 2^24]");
-  if (job->max_members < 0 || job->max_members > kMaxGroupMembers)
-    return fail(PM_E_LIMIT, "pm_group_bootstrap_device_static: max_members %d outside [0, %d]", job->max_members,
-                kMaxGroupMembers);
-  if (!job->values || !job->group_offsets || !job->seeds || !job->medians || !job->ci_lo || !job->ci_hi)
-    return fail(PM_E_INVALID, "pm_group_bootstrap_device_static: a job array is NULL");
+  // The checks of every other bootstrap entry point (sizes, limits, arrays).
+  int rc = check_bootstrap(job);
+  if (rc) return rc;
   const size_t need = bootstrap_scratch_bytes(job->n_groups, job->max_members, job->resamples);
   if (need > kStaticStreamBytes)
     return fail(PM_E_LIMIT,
                 "pm_group_bootstrap_device_static: %d groups of up to %d members at %d resamples need %zu bytes of "
                 "index streams; the fixed array holds %zu (use pm_group_bootstrap_device with your own scratch)",
                 job->n_groups, job->max_members, job->resamples, need, kStaticStreamBytes);
-  int device = 0, rc = current_device(&device);
-  if (rc) return rc;
+  int device = 0;
+  if ((rc = current_device(&device))) return rc;
   if ((rc = check_bootstrap_fits(job->n_metrics, job->max_members))) return rc;
   void* scratch = nullptr;
   {
@@ -87,9 +80,12 @@ extern "C" int pm_group_bootstrap_device_static(const pm_bootstrap_job* job, voi
   BootArgs A{job->n_groups, job->n_metrics, job->resamples, job->max_members, job->values, job->group_offsets,
              job->member_rows, job->member_valid, job->seeds, job->medians, job->ci_lo, job->ci_hi,
              static_cast<uint8_t*>(scratch), 1};
-  launch_bootstrap_prepare(A, static_cast<cudaStream_t>(stream));
-  launch_bootstrap(A, static_cast<cudaStream_t>(stream));
+  if (launch_bootstrap_prepare(A, static_cast<cudaStream_t>(stream)))
+    return fail(PM_E_CUDA, "bootstrap_prepare_kernel launch failed");
   cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) return cuda_fail(e, "bootstrap_prepare_kernel launch");
+  if (launch_bootstrap(A, static_cast<cudaStream_t>(stream))) return fail(PM_E_CUDA, "bootstrap_kernel launch failed");
+  e = cudaGetLastError();
   if (e != cudaSuccess) return cuda_fail(e, "bootstrap_kernel launch");
   return PM_OK;
 }

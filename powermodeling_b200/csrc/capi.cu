@@ -462,6 +462,20 @@ void copy_results_out(const StagedTrials& S, size_t n, pm_trial_results* out) {
 }  // namespace
 }  // namespace pm
 
+// ---------------------------------------------------------------------------
+// Shared by every bootstrap entry point (the allocation-free one included).
+int pm::check_bootstrap(const pm_bootstrap_job* j) {
+  if (!j) return fail(PM_E_INVALID, "NULL job");
+  if (j->n_groups < 0 || j->n_metrics <= 0 || j->n_metrics > kMaxMetrics || j->n_members < 0 || j->n_rows < 0)
+    return fail(PM_E_INVALID, "bad bootstrap sizes");
+  if (j->resamples < 40 || j->resamples > (1 << 24)) return fail(PM_E_INVALID, "resamples must be in [40, 2^24]");
+  if (j->max_members < 0 || j->max_members > kMaxGroupMembers)
+    return fail(PM_E_LIMIT, "max_members %d outside [0, %d]", j->max_members, kMaxGroupMembers);
+  if (!j->values || !j->group_offsets || !j->seeds || !j->medians || !j->ci_lo || !j->ci_hi)
+    return fail(PM_E_INVALID, "a pm_bootstrap_job array is NULL");
+  return PM_OK;
+}
+
 extern "C" {
 
 int pm_analyze_trials(const pm_trials* trials, const pm_policy* policy, pm_trial_results* out) {
@@ -485,19 +499,6 @@ int pm_analyze_trials(const pm_trials* trials, const pm_policy* policy, pm_trial
   e = cudaStreamSynchronize(A.stream);
   if (e != cudaSuccess) return cuda_fail(e, "analyze_kernel");
   copy_results_out(S, n, out);
-  return PM_OK;
-}
-
-// ---------------------------------------------------------------------------
-static int check_bootstrap(const pm_bootstrap_job* j) {
-  if (!j) return fail(PM_E_INVALID, "NULL job");
-  if (j->n_groups < 0 || j->n_metrics <= 0 || j->n_metrics > kMaxMetrics || j->n_members < 0 || j->n_rows < 0)
-    return fail(PM_E_INVALID, "bad bootstrap sizes");
-  if (j->resamples < 40 || j->resamples > (1 << 24)) return fail(PM_E_INVALID, "resamples must be in [40, 2^24]");
-  if (j->max_members < 0 || j->max_members > kMaxGroupMembers)
-    return fail(PM_E_LIMIT, "max_members %d outside [0, %d]", j->max_members, kMaxGroupMembers);
-  if (!j->values || !j->group_offsets || !j->seeds || !j->medians || !j->ci_lo || !j->ci_hi)
-    return fail(PM_E_INVALID, "a pm_bootstrap_job array is NULL");
   return PM_OK;
 }
 
@@ -548,9 +549,11 @@ int pm_bootstrap_finish_device_exchange(const pm_bootstrap_job* job, void* scrat
   if (!groups) return fail(PM_E_INVALID, "NULL groups");
   if (groups->n_ranks < 1 || groups->n_ranks > PM_MAX_RANKS || groups->rank < 0 || groups->rank >= groups->n_ranks)
     return fail(PM_E_INVALID, "bad rank geometry");
+  if (groups->root < -1 || groups->root >= groups->n_ranks) return fail(PM_E_INVALID, "root must be -1 or a rank");
   if (groups->epoch == 0 || !groups->done) return fail(PM_E_INVALID, "bad epoch or counter");
   for (int r = 0; r < groups->n_ranks; ++r)
-    if (!groups->out[r] || !groups->flags[r]) return fail(PM_E_INVALID, "a rank's buffer is NULL");
+    if ((groups->root < 0 || r == groups->root) && (!groups->out[r] || !groups->flags[r]))
+      return fail(PM_E_INVALID, "a receiving rank's buffer is NULL");
   BootArgs A;
   int rc = device_boot_args(job, scratch, scratch_bytes, &A);
   if (rc) return rc;

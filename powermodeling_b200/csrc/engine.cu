@@ -1226,6 +1226,38 @@ extern "C" int pm_tensor_probe(int accumulators, uint64_t iterations, int unifor
   }
 }
 
+extern "C" int pm_gemm_probe(int m, int n, int k, int uniform, uint64_t seed, float* out, uint16_t* a_out,
+                             uint16_t* b_out) {
+  if (m <= 0 || n <= 0 || k <= 0 || m > 4096 || n > 4096 || k > 4096 || !out)
+    return fail(PM_E_INVALID, "pm_gemm_probe: dimensions must be 1..4096 and out non-NULL");
+  try {
+    int sms = 0;
+    check(cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, 0), "attr");
+    DevBuf<uint16_t> a(size_t(m) * k), b(size_t(k) * n);
+    DevBuf<float> c(size_t(m) * n);
+    // The gemm arm's operands and call: column-major A (m x k) and B (k x n)
+    // filled as the arm fills them, fp32 C from cublasGemmEx on the tensor cores.
+    check(launch_fill_halves(a.p, size_t(m) * k, seed, uniform, sms, 0), "fill");
+    check(launch_fill_halves(b.p, size_t(k) * n, seed ^ 12345ULL, uniform, sms, 0), "fill");
+    cublasHandle_t blas = nullptr;
+    check_blas(cublasCreate(&blas), "cublasCreate");
+    const float alpha = 1.0f, beta = 0.0f;
+    cublasStatus_t st = cublasSetMathMode(blas, CUBLAS_TENSOR_OP_MATH);
+    if (st == CUBLAS_STATUS_SUCCESS)
+      st = cublasGemmEx(blas, CUBLAS_OP_N, CUBLAS_OP_N, m, n, k, &alpha, a.p, CUDA_R_16F, m, b.p, CUDA_R_16F, k, &beta,
+                        c.p, CUDA_R_32F, m, CUBLAS_COMPUTE_32F, CUBLAS_GEMM_DEFAULT_TENSOR_OP);
+    cublasDestroy(blas);
+    check_blas(st, "cublasGemmEx");
+    check(cudaDeviceSynchronize(), "gemm");
+    check(cudaMemcpy(out, c.p, size_t(m) * n * 4, cudaMemcpyDeviceToHost), "cudaMemcpy");
+    if (a_out) check(cudaMemcpy(a_out, a.p, size_t(m) * k * 2, cudaMemcpyDeviceToHost), "cudaMemcpy");
+    if (b_out) check(cudaMemcpy(b_out, b.p, size_t(k) * n * 2, cudaMemcpyDeviceToHost), "cudaMemcpy");
+    return PM_OK;
+  } catch (const std::exception& e) {
+    return fail(PM_E_CUDA, "%s", e.what());
+  }
+}
+
 extern "C" int pm_powerbench(int argc, const char* const* argv, pm_line_cb cb, void* user) {
   if (!cb || argc < 1 || !argv) return fail(PM_E_INVALID, "pm_powerbench: NULL argument");
   const Sink out{cb, user};

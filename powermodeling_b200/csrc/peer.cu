@@ -34,6 +34,32 @@ __global__ void peer_wait_kernel(const uint32_t* flags, int n, uint32_t epoch, u
   __syncthreads();
 }
 
+// The start line: thread 0 stores `epoch` into this rank's entry of every
+// rank's flag array, then thread r polls entry r of this rank's own array,
+// as peer_wait_kernel does.
+struct GateFlags {
+  uint32_t* flags[PM_MAX_RANKS];
+};
+
+__global__ void peer_gate_kernel(GateFlags F, int n, int rank, uint32_t epoch, uint64_t timeout_ns, int32_t* error) {
+  if (threadIdx.x == 0)
+    for (int r = 0; r < n; ++r)
+      asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(F.flags[r] + rank), "r"(epoch) : "memory");
+  const int r = threadIdx.x;
+  if (r < n) {
+    const uint32_t* own = F.flags[rank];
+    const uint64_t t0 = global_ns();
+    for (;;) {
+      uint32_t v;
+      asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(own + r) : "memory");
+      if ((int32_t)(v - epoch) >= 0) break;
+      if (global_ns() - t0 > timeout_ns) { atomicExch(error, 1); break; }
+      __nanosleep(256);
+    }
+  }
+  __syncthreads();
+}
+
 }  // namespace pm
 
 using namespace pm;
@@ -89,6 +115,20 @@ int pm_peer_wait_device(const uint32_t* flags, int32_t n_ranks, uint32_t epoch, 
   peer_wait_kernel<<<1, 32, 0, (cudaStream_t)stream>>>(flags, n_ranks, epoch, (uint64_t)timeout_ms * 1000000ull, error);
   const cudaError_t e = cudaGetLastError();
   return e == cudaSuccess ? PM_OK : cuda_fail(e, "peer_wait_kernel launch");
+}
+
+int pm_peer_gate_device(uint32_t* const* flags, int32_t n_ranks, int32_t rank, uint32_t epoch, uint32_t timeout_ms,
+                        int32_t* error, void* stream) {
+  if (!flags || !error || n_ranks < 1 || n_ranks > PM_MAX_RANKS || rank < 0 || rank >= n_ranks)
+    return fail(PM_E_INVALID, "pm_peer_gate_device: bad argument");
+  GateFlags F{};
+  for (int r = 0; r < n_ranks; ++r) {
+    if (!flags[r]) return fail(PM_E_INVALID, "pm_peer_gate_device: rank %d's flags are NULL", r);
+    F.flags[r] = flags[r];
+  }
+  peer_gate_kernel<<<1, 32, 0, (cudaStream_t)stream>>>(F, n_ranks, rank, epoch, (uint64_t)timeout_ms * 1000000ull, error);
+  const cudaError_t e = cudaGetLastError();
+  return e == cudaSuccess ? PM_OK : cuda_fail(e, "peer_gate_kernel launch");
 }
 
 }  // extern "C"

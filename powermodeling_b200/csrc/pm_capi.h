@@ -6,6 +6,8 @@
 #include <atomic>
 #include <mutex>
 
+#include "pmb200.h"
+
 namespace pm {
 
 constexpr int kMaxDevices = 64;
@@ -62,6 +64,8 @@ int arena_reserve(Arena& a, size_t dev_bytes, size_t host_bytes);
 size_t bootstrap_smem_shortfall(int n_metrics, int max_members, size_t* available);
 // PM_E_LIMIT when the bootstrap fold for these sizes does not fit one CTA's shared memory.
 int check_bootstrap_fits(int n_metrics, int max_members);
+// PM_E_INVALID / PM_E_LIMIT for a job whose sizes, limits or arrays are unusable.
+int check_bootstrap(const pm_bootstrap_job* j);
 size_t analyze_scratch_bytes(int n_trials, int max_phase_samples);
 
 }  // namespace pm

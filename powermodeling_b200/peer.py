@@ -1,17 +1,21 @@
 """The sharded summarize's exchanges over NVLink peer memory (include/pmb200_peer.h).
 
 One process per GPU.  ``PeerExchange`` allocates this rank's gathered
-buffers (metric rows and valid flags of every rank's trials; medians and
-interval ends of every rank's groups; arrival flags and counters), swaps
-their CUDA IPC handles over a torch process group, opens the other ranks'
-buffers and fills the ``pm_peer_rows`` / ``pm_peer_groups`` descriptors that
-``pm_analyze_trials_device_exchange`` and ``pm_bootstrap_finish_device_exchange``
-take.  The kernels store straight into every rank's buffers; ``wait_rows`` /
-``wait_groups`` hold a stream until every rank's launch has delivered, each
-wait bounded (an expired wait raises here, after the stream drains).
+buffers (metric rows and valid flags of every rank's trials, when rows move
+at all; medians and interval ends of every rank's groups; arrival flags and
+counters; the start-line flags), swaps their CUDA IPC handles over a torch
+process group, opens the other ranks' buffers and fills the
+``pm_peer_rows`` / ``pm_peer_groups`` descriptors that
+``pm_analyze_trials_device_exchange`` and
+``pm_bootstrap_finish_device_exchange`` take.  The kernels store straight
+into the receiving ranks' buffers; ``wait_rows`` / ``wait_groups`` hold a
+stream until every rank's launch has delivered, each wait bounded (an
+expired wait raises here, after the stream drains); ``gate`` starts all
+ranks' following work together on their GPUs.
 
-The exchanges replace the two all-gathers of ``distributed.summarize_sharded``
-(rows before the bootstrap, group results after it).
+With ``rows_per_rank=0`` no rows move: every group is bootstrapped on the
+rank that analysed its members, and only the group results travel, to every
+rank (``root=-1``) or to one rank (a gather).
 """
 from __future__ import annotations
 
@@ -28,29 +32,36 @@ class PeerExchange:
     """Gathered row and group buffers of one rank, shared with every other rank.
 
     rows_per_rank: trials each rank analyses (rank r's trial t is global row
-    r * rows_per_rank + t); groups_per_rank: the group stride of the gathered
-    group buffer ([world][3][groups_per_rank][n_metrics])."""
+    r * rows_per_rank + t), 0 when no rows are exchanged; groups_per_rank: the
+    group stride of the gathered group buffer ([world][3][groups_per_rank][n_metrics]);
+    root: -1 to deliver group results to every rank, else the one rank that
+    receives them."""
 
     def __init__(self, rank: int, world: int, rows_per_rank: int, n_metrics: int, groups_per_rank: int,
-                 group=None, timeout_ms: int = 5000):
+                 group=None, timeout_ms: int = 5000, root: int = -1):
         import torch
         import torch.distributed as dist
         if not 1 <= world <= N.MAX_RANKS:
             raise ValueError(f"world size must be 1..{N.MAX_RANKS}")
+        if not -1 <= root < world:
+            raise ValueError("root must be -1 or a rank")
         self.lib = N.library()
-        self.rank, self.world, self.timeout_ms = rank, world, timeout_ms
+        self.rank, self.world, self.timeout_ms, self.root = rank, world, timeout_ms, root
         self.rows_per_rank, self.n_metrics, self.groups_per_rank = rows_per_rank, n_metrics, groups_per_rank
         total_rows = world * rows_per_rank
-        sizes = (total_rows * n_metrics * 8, total_rows, (world + 1) * 4,
-                 world * 3 * max(1, groups_per_rank) * n_metrics * 8, (world + 1) * 4)
+        sizes = {"groups": world * 3 * max(1, groups_per_rank) * n_metrics * 8, "group_flags": (world + 1) * 4,
+                 "gate": world * 4}
+        if rows_per_rank > 0:
+            sizes.update(metrics=total_rows * n_metrics * 8, valid=total_rows, row_flags=(world + 1) * 4)
+        names = list(sizes)
         # Every rank takes both collectives below, whatever failed locally, so a
         # failure on one rank becomes the same PeerExchangeError on all of them.
-        self.own, self.opened, handles, failure = [], [], [], None
+        self.own, self.opened, handles, failure = {}, [], [], None
         try:
-            for nbytes in sizes:
+            for name in names:
                 ptr, handle = C.c_void_p(), N.PeerHandle()
-                N.check(self.lib.pm_peer_alloc(nbytes, C.byref(ptr), C.byref(handle)), "pm_peer_alloc")
-                self.own.append(ptr.value)
+                N.check(self.lib.pm_peer_alloc(sizes[name], C.byref(ptr), C.byref(handle)), "pm_peer_alloc")
+                self.own[name] = ptr.value
                 handles.append(bytes(handle.bytes))
         except N.NativeError as exc:
             failure = str(exc)
@@ -61,19 +72,19 @@ class PeerExchange:
             self._release()
             raise PeerExchangeError(f"peer buffers could not be allocated on rank(s) {missing}"
                                     + (f": {failure}" if failure else ""))
-        per_rank = []
+        per_rank: list[dict] = []
         try:
             for r in range(world):
                 if r == rank:
-                    per_rank.append(list(self.own))
+                    per_rank.append(dict(self.own))
                     continue
-                ptrs = []
-                for raw in everyone[r]:
+                ptrs = {}
+                for name, raw in zip(names, everyone[r]):
                     h, q = N.PeerHandle(), C.c_void_p()
                     C.memmove(h.bytes, raw, 64)
                     N.check(self.lib.pm_peer_open(C.byref(h), C.byref(q)), "pm_peer_open")
                     self.opened.append(q.value)
-                    ptrs.append(q.value)
+                    ptrs[name] = q.value
                 per_rank.append(ptrs)
         except N.NativeError as exc:
             failure = str(exc)
@@ -86,34 +97,41 @@ class PeerExchange:
         self.rows, self.groups = N.PeerRows(), N.PeerGroups()
         self.rows.n_ranks, self.rows.rank, self.rows.row_offset, self.rows.epoch = world, rank, rank * rows_per_rank, 0
         self.groups.n_ranks, self.groups.rank, self.groups.per_rank, self.groups.epoch = world, rank, groups_per_rank, 0
+        self.groups.root = root
+        self.gate_flags = (C.c_void_p * world)()
         for r, ptrs in enumerate(per_rank):
-            self.rows.metrics[r], self.rows.valid[r], self.rows.flags[r], self.groups.out[r], self.groups.flags[r] = ptrs
-        self.rows.done = self.own[2] + world * 4
-        self.groups.done = self.own[4] + world * 4
+            if rows_per_rank > 0:
+                self.rows.metrics[r], self.rows.valid[r], self.rows.flags[r] = ptrs["metrics"], ptrs["valid"], ptrs["row_flags"]
+            self.groups.out[r], self.groups.flags[r] = ptrs["groups"], ptrs["group_flags"]
+            self.gate_flags[r] = ptrs["gate"]
+        if rows_per_rank > 0:
+            self.rows.done = self.own["row_flags"] + world * 4
+        self.groups.done = self.own["group_flags"] + world * 4
+        self.gate_epoch = 0
         self.error = torch.zeros(1, dtype=torch.int32, device="cuda")
         self._group = group
 
     # gathered buffers of this rank (device pointers) ----------------------------------------------
     @property
     def metrics_ptr(self) -> int:
-        return self.own[0]
+        return self.own["metrics"]
 
     @property
     def valid_ptr(self) -> int:
-        return self.own[1]
+        return self.own["valid"]
 
     @property
     def groups_ptr(self) -> int:
-        return self.own[3]
+        return self.own["groups"]
 
     def view(self, which: str):
         """A torch tensor over this rank's gathered 'metrics', 'valid' or 'groups' buffer (no copy)."""
         import torch
         total = self.world * self.rows_per_rank
         shape, typestr, ptr = {
-            "metrics": ((total, self.n_metrics), "<f8", self.own[0]),
-            "valid": ((total,), "|u1", self.own[1]),
-            "groups": ((self.world, 3, max(1, self.groups_per_rank), self.n_metrics), "<f8", self.own[3]),
+            "metrics": ((total, self.n_metrics), "<f8", self.own.get("metrics")),
+            "valid": ((total,), "|u1", self.own.get("valid")),
+            "groups": ((self.world, 3, max(1, self.groups_per_rank), self.n_metrics), "<f8", self.own["groups"]),
         }[which]
 
         class _View:
@@ -128,12 +146,21 @@ class PeerExchange:
         self.groups.epoch += 1
 
     def wait_rows(self, stream_ptr: int) -> None:
-        N.check(self.lib.pm_peer_wait_device(C.c_void_p(self.own[2]), self.world, self.rows.epoch, self.timeout_ms,
-                                             C.c_void_p(self.error.data_ptr()), C.c_void_p(stream_ptr)), "row arrival wait")
+        N.check(self.lib.pm_peer_wait_device(C.c_void_p(self.own["row_flags"]), self.world, self.rows.epoch,
+                                             self.timeout_ms, C.c_void_p(self.error.data_ptr()), C.c_void_p(stream_ptr)),
+                "row arrival wait")
 
     def wait_groups(self, stream_ptr: int) -> None:
-        N.check(self.lib.pm_peer_wait_device(C.c_void_p(self.own[4]), self.world, self.groups.epoch, self.timeout_ms,
-                                             C.c_void_p(self.error.data_ptr()), C.c_void_p(stream_ptr)), "group arrival wait")
+        """Hold the stream until every rank's groups of this epoch are here (receiving ranks only)."""
+        N.check(self.lib.pm_peer_wait_device(C.c_void_p(self.own["group_flags"]), self.world, self.groups.epoch,
+                                             self.timeout_ms, C.c_void_p(self.error.data_ptr()), C.c_void_p(stream_ptr)),
+                "group arrival wait")
+
+    def gate(self, stream_ptr: int) -> None:
+        """Start line: work this rank enqueues after it starts on its GPU once every rank has reached it."""
+        self.gate_epoch += 1
+        N.check(self.lib.pm_peer_gate_device(self.gate_flags, self.world, self.rank, self.gate_epoch, self.timeout_ms,
+                                             C.c_void_p(self.error.data_ptr()), C.c_void_p(stream_ptr)), "start gate")
 
     def check(self) -> None:
         """Raise if any wait expired (synchronizes the device)."""
@@ -155,8 +182,8 @@ class PeerExchange:
             rc = self.lib.pm_peer_close(C.c_void_p(q))
             if check:
                 N.check(rc, "pm_peer_close")
-        for q in self.own:
+        for q in self.own.values():
             rc = self.lib.pm_peer_free(C.c_void_p(q))
             if check:
                 N.check(rc, "pm_peer_free")
-        self.opened, self.own = [], []
+        self.opened, self.own = [], {}

@@ -50,3 +50,16 @@ def tensor_probe(accumulators: int = 1, iterations: int = 1, uniform: bool = Fal
     N.check(lib.pm_tensor_probe(accumulators, iterations, int(uniform), seed, out.ctypes.data, out.size,
                                 a.ctypes.data, b.ctypes.data), "pm_tensor_probe")
     return out, a.view(np.float16), b.view(np.float16)
+
+
+def gemm_probe(m: int, n: int, k: int, uniform: bool = False, seed: int = 1):
+    """The gemm arm's cuBLAS call once: (C [m, n], A [m, k], B [k, n]) as float32 / float16 arrays."""
+    import numpy as np
+    lib = N.library()
+    lib.pm_gemm_probe.argtypes = [C.c_int, C.c_int, C.c_int, C.c_int, C.c_uint64, C.c_void_p, C.c_void_p, C.c_void_p]
+    out = np.zeros(m * n, dtype=np.float32)
+    a = np.zeros(m * k, dtype=np.uint16)
+    b = np.zeros(k * n, dtype=np.uint16)
+    N.check(lib.pm_gemm_probe(m, n, k, int(uniform), seed, out.ctypes.data, a.ctypes.data, b.ctypes.data), "pm_gemm_probe")
+    col = lambda x, rows, cols: x.reshape(cols, rows).T      # column-major storage
+    return col(out, m, n), col(a.view(np.float16), m, k), col(b.view(np.float16), k, n)

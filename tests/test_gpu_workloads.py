@@ -24,9 +24,14 @@ def result_of(records, kind="result"):
     return found[0]
 
 
-def reference_result(args):
-    """The reference's own powerbench (built from its sources for sm_100a) on the same arguments."""
+def reference_result(args, required: bool = False):
+    """The reference's own powerbench (built from its sources for sm_100a) on the same arguments.
+
+    required: the reference binary is the only checker (SFU checksums depend on
+    the hardware's MUFU approximations), so its absence fails the test."""
     if not REF_BIN.exists():
+        if required:
+            pytest.fail(f"{REF_BIN.relative_to(ROOT)} is missing: build it with oracle/build_oracle.py")
         return None
     proc = subprocess.run([str(REF_BIN), *map(str, args)], capture_output=True, text=True, timeout=120)
     assert proc.returncode == 0, proc.stderr
@@ -143,9 +148,8 @@ def test_sfu_arms(gpu_ready, workload):
     assert r["numerical_validation"]["checked_values"] == 16 and r["sanity"]["numerical_validation_passed"] is True
     assert contracts.sfu_count_issues(r, workload) == []
     assert r["kernel_resources"]["local_bytes_per_thread"] == 0
-    ref = reference_result(args)
-    if ref is not None:
-        assert ref["checksum"] == r["checksum"], workload
+    ref = reference_result(args, required=True)
+    assert ref["checksum"] == r["checksum"], workload
 
 
 @pytest.mark.parametrize("accumulators,iterations,uniform", [(1, 1, False), (3, 2, True), (8, 5, True), (2, 1, True)])
@@ -169,3 +173,17 @@ def test_tensor_workload_counts(gpu_ready):
 def test_gemm_arm_runs(gpu_ready):
     r = result_of(powerbench.run(["--workload", "gemm", "--gemm-m", "512", "--gemm-n", "512", "--gemm-k", "512", *QUICK]))
     assert r["operations"] == 2 * 2 * 512 ** 3 and r["sanity"]["finite_output_sample"] is True
+
+
+@pytest.mark.parametrize("m,n,k,uniform", [(512, 512, 512, False), (256, 384, 1024, True), (8192 // 16, 64, 8192, True)])
+def test_gemm_arm_matches_fp64_product(gpu_ready, m, n, k, uniform):
+    """cuBLAS fp16 x fp16 -> fp32 against the fp64 product of the same operands.
+
+    fp16 products are exact in fp32, so the error is the fp32 accumulation's:
+    within 1e-5 of sum |a||b| (the tcgen05 probe's tolerance)."""
+    c, a, b = powerbench.gemm_probe(m, n, k, uniform, seed=23)
+    a64, b64 = a.astype(np.float64), b.astype(np.float64)
+    ref = a64 @ b64
+    scale = np.abs(a64) @ np.abs(b64)
+    assert np.all(np.isfinite(c))
+    assert np.all(np.abs(c - ref) <= 1e-5 * scale + 1e-6), float(np.max(np.abs(c - ref) / (scale + 1e-30)))
