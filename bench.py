@@ -777,8 +777,8 @@ def roofline_entry(a_ms, p_ms, f_ms, in_bytes, out_bytes, G, M, packed, peaks, s
                      peak_source=f"{ISSUE_PER_SM_CLOCK} warp instructions/clk/SM x {SMS} SMs x {clock:.0f} MHz (sampled)")
     else:
         achieved = (in_bytes + out_bytes) / (a_ms / 1e3) / 1e9
-        entry.update(kernel="analyze_kernel", bound="hbm", achieved=achieved, peak=hbm, unit="GB/s", frac=achieved / hbm,
-                     traffic=NCU_PER_LAUNCH["analyze_kernel"]["dram"], peak_source=src)
+        entry.update(kernel="analyze_kernel", launch_ms=a_ms, bound="hbm", achieved=achieved, peak=hbm, unit="GB/s",
+                     frac=achieved / hbm, traffic=NCU_PER_LAUNCH["analyze_kernel"]["dram"], peak_source=src)
     return entry
 
 
