@@ -104,6 +104,13 @@ def _none(x) -> float | None:
     return None if math.isnan(x) else x
 
 
+def _py_rows(values: np.ndarray, width: int) -> list[list]:
+    """A result array as rows of Python floats, NaN (the ABI's None) as None: _none on every element at once."""
+    obj = values.astype(object)
+    obj[np.isnan(values)] = None
+    return obj.reshape(-1, width).tolist() if width else []
+
+
 # --- issue strings for each bit word ----------------------------------------
 _PHASE_ISSUES = ("missing_phase", "invalid_phase_window", "short_plateau", "too_few_samples", "telemetry_gap",
                  "negative_power", "missing_power_coverage", "energy_counter_disagreement")
@@ -339,50 +346,65 @@ def _po_names():
     return _PO_NAMES
 
 
-def _phase_dict(name: str, po: np.ndarray, flags: int, policy: AnalysisPolicy) -> dict:
-    """The reference's _phase_stats dict without its private _selected list."""
+_PF = None
+
+
+def _pf_bits():
+    """Phase flag bit positions: (missing, invalid window, counter reset, [(bit, issue) in report order])."""
+    global _PF
+    if _PF is None:
+        issues = (("SHORT_PLATEAU", "short_plateau"), ("TOO_FEW_SAMPLES", "too_few_samples"),
+                  ("TELEMETRY_GAP", "telemetry_gap"), ("NEGATIVE_POWER", "negative_power"),
+                  ("MISSING_POWER_COVERAGE", "missing_power_coverage"), ("COUNTER_DISAGREEMENT", "energy_counter_disagreement"))
+        _PF = (N.layout("PM_PF_MISSING"), N.layout("PM_PF_INVALID_WINDOW"), N.layout("PM_PF_COUNTER_RESET"),
+               tuple((N.layout("PM_PF_" + key), text) for key, text in issues))
+    return _PF
+
+
+_CADENCE_NOTE = "Changes are not proof of sensor refresh cadence; unchanged values may be steady power."
+
+
+def _phase_dict(name: str, po: np.ndarray, flags: int, policy: AnalysisPolicy, pv: list | None = None) -> dict:
+    """The reference's _phase_stats dict without its private _selected list.
+
+    ``pv``: the same phase row as Python values with None for NaN (``_py_rows``); derived from ``po`` when absent."""
     L = _po_names()
+    missing, invalid, reset, issue_bits = _pf_bits()
     out: dict[str, Any] = {"name": name, "issues": [], "warnings": []}
-    pf = {k: N.layout("PM_PF_" + k) for k in ("MISSING", "INVALID_WINDOW", "COUNTER_RESET", "COMPUTED")}
-    if flags >> pf["MISSING"] & 1:
+    if flags >> missing & 1:
         out["issues"].append(f"missing_phase:{name}")
         return out
-    if flags >> pf["INVALID_WINDOW"] & 1:
+    if flags >> invalid & 1:
         out["issues"].append(f"invalid_phase_window:{name}")
         return out
+    if pv is None:
+        pv = _py_rows(np.asarray(po, dtype=np.float64), len(po))[0]
     samples = int(po[L["SAMPLES"]])
-    out.update(start_s=_none(po[L["START_S"]]), end_s=_none(po[L["END_S"]]), duration_s=_none(po[L["DURATION_S"]]),
-               midpoint_s=_none(po[L["MIDPOINT_S"]]), samples=samples,
-               sample_interval_median_s=_none(po[L["GAP_MEDIAN_S"]]), max_sample_gap_s=_none(po[L["GAP_MAX_S"]]))
-    issue_bits = {"SHORT_PLATEAU": "short_plateau", "TOO_FEW_SAMPLES": "too_few_samples", "TELEMETRY_GAP": "telemetry_gap",
-                  "NEGATIVE_POWER": "negative_power", "MISSING_POWER_COVERAGE": "missing_power_coverage",
-                  "COUNTER_DISAGREEMENT": "energy_counter_disagreement"}
-    order = ("SHORT_PLATEAU", "TOO_FEW_SAMPLES", "TELEMETRY_GAP", "NEGATIVE_POWER", "MISSING_POWER_COVERAGE",
-             "COUNTER_DISAGREEMENT")
-    for key in order:
-        if flags >> N.layout("PM_PF_" + key) & 1:
-            out["issues"].append(f"{issue_bits[key]}:{name}")
-    energy = _none(po[L["ENERGY_J"]])
-    out["integrated_power_energy_j"] = energy
-    out["integrated_power_w"] = _none(po[L["INTEGRATED_POWER_W"]])
-    out["power_w"] = _none(po[L["POWER_W"]])
-    memory_energy = _none(po[L["MEMORY_ENERGY_J"]])
-    out["memory_rail_energy_j"] = memory_energy
-    out["memory_power_w"] = _none(po[L["MEMORY_POWER_W"]])
-    if flags >> pf["COUNTER_RESET"] & 1:
+    out.update(start_s=pv[L["START_S"]], end_s=pv[L["END_S"]], duration_s=pv[L["DURATION_S"]],
+               midpoint_s=pv[L["MIDPOINT_S"]], samples=samples,
+               sample_interval_median_s=pv[L["GAP_MEDIAN_S"]], max_sample_gap_s=pv[L["GAP_MAX_S"]])
+    for bit, text in issue_bits:
+        if flags >> bit & 1:
+            out["issues"].append(f"{text}:{name}")
+    out["integrated_power_energy_j"] = pv[L["ENERGY_J"]]
+    out["integrated_power_w"] = pv[L["INTEGRATED_POWER_W"]]
+    out["power_w"] = pv[L["POWER_W"]]
+    out["memory_rail_energy_j"] = pv[L["MEMORY_ENERGY_J"]]
+    out["memory_power_w"] = pv[L["MEMORY_POWER_W"]]
+    if flags >> reset & 1:
         out["warnings"].append(f"energy_counter_reset:{name}")
-    out["energy_counter_j"] = _none(po[L["COUNTER_J"]])
-    disagreement = _none(po[L["DISAGREEMENT"]])
+    out["energy_counter_j"] = pv[L["COUNTER_J"]]
+    disagreement = pv[L["DISAGREEMENT"]]
     if disagreement is not None:
         out["counter_power_disagreement_fraction"] = disagreement
     out["distinct_power_values"] = int(po[L["DISTINCT_POWER"]])
-    out["observed_power_change_interval_median_s"] = _none(po[L["CHANGE_MEDIAN_S"]])
-    out["power_update_cadence_note"] = "Changes are not proof of sensor refresh cadence; unchanged values may be steady power."
+    out["observed_power_change_interval_median_s"] = pv[L["CHANGE_MEDIAN_S"]]
+    out["power_update_cadence_note"] = _CADENCE_NOTE
     for field in ("graphics_clock_mhz", "sm_clock_mhz", "memory_clock_mhz", "temperature_c"):
         med, lo, hi = L[field]
-        out[field] = _none(po[med])
-        out[f"{field}_min"] = _none(po[lo])
-        out[f"{field}_max"] = _none(po[hi])
+        out[field] = pv[med]
+        out[f"{field}_min"] = pv[lo]
+        out[f"{field}_max"] = pv[hi]
     return out
 
 
@@ -445,6 +467,9 @@ def analyze_trials(records: Iterable[Mapping[str, Any]], policy: AnalysisPolicy 
     if _metrics_out is not None:
         _metrics_out.append((views.metrics.reshape(len(records), len(METRICS)).copy(), views.valid.copy()))
     TO = {name: N.layout("PM_TO_" + name) for name in _TO_NAMES}
+    po_rows, to_rows = _py_rows(views.phase_out, views.PO), _py_rows(views.trial_out, views.TO)
+    policy_dict = asdict(policy)
+    sel_lo, sel_hi = N.layout("PM_PO_SEL_LO"), N.layout("PM_PO_SEL_HI")
     out = []
     for i, record in enumerate(records):
         bench = record.get("benchmark") or record.get("result") or {}
@@ -452,7 +477,8 @@ def analyze_trials(records: Iterable[Mapping[str, Any]], policy: AnalysisPolicy 
         device = record.get("device") or {}
         phases_rec = phase_records(record)
         to = views.trial_out[i * views.TO:(i + 1) * views.TO]
-        g = lambda name: _none(to[TO[name]])  # noqa: E731
+        to_py = to_rows[i]
+        g = lambda name: to_py[TO[name]]  # noqa: E731
         ib = [int(x) for x in views.issue_bits[i * 4:(i + 1) * 4]]
         issues = host_issues[i] + _bits(ib[0], words[0])
         baseline_issues = _bits(ib[1], words[1])
@@ -460,12 +486,13 @@ def analyze_trials(records: Iterable[Mapping[str, Any]], policy: AnalysisPolicy 
         warnings = _bits(ib[3], words[3])
         phase_dicts = {}
         for p, name in enumerate(N.PHASE_NAMES):
-            po = views.phase_out[(i * N.PM_PHASES + p) * views.PO:(i * N.PM_PHASES + p + 1) * views.PO]
-            phase_dicts[name] = _phase_dict(name, po, int(views.phase_flags[i * N.PM_PHASES + p]), policy)
+            slot = i * N.PM_PHASES + p
+            po = views.phase_out[slot * views.PO:(slot + 1) * views.PO]
+            phase_dicts[name] = _phase_dict(name, po, int(views.phase_flags[slot]), policy, po_rows[slot])
         other_pids = set()
         measure_slot = i * N.PM_PHASES + 1
         mpo = views.phase_out[measure_slot * views.PO:(measure_slot + 1) * views.PO]
-        lo, hi_ = mpo[N.layout("PM_PO_SEL_LO")], mpo[N.layout("PM_PO_SEL_HI")]
+        lo, hi_ = mpo[sel_lo], mpo[sel_hi]
         if not math.isnan(lo):
             for index, pids in packed.foreign_pids[measure_slot]:
                 if lo <= index < hi_:
@@ -548,7 +575,7 @@ def analyze_trials(records: Iterable[Mapping[str, Any]], policy: AnalysisPolicy 
             "baseline_sm_clock_uses_graphics_proxy": not bool(to[TO["BASE_SM_COMPARED"]]),
             "baseline_state_domains_compared": sorted(([ "enforced_power_limit_w"] if to[TO["BASE_ENF_COMPARED"]] else [])
                                                       + (["pstate"] if to[TO["BASE_PSTATE_COMPARED"]] else [])),
-            "policy": asdict(policy), "phases": {},
+            "policy": dict(policy_dict), "phases": {},
         }
         # insertion order of the reference: idle_pre before idle_post, enforced limit before pstate (= bit order)
         result["baseline_state_issues"] = [s for s in baseline_issues if s.startswith("idle_state_mismatch_or_unverified")]

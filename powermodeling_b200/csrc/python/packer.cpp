@@ -20,6 +20,9 @@
 #include <Python.h>
 
 #include <algorithm>
+#include <atomic>
+#include <cstdlib>
+#include <thread>
 #include <cmath>
 #include <cstdint>
 #include <cstring>
@@ -306,6 +309,246 @@ PyObject* as_bytes(const std::vector<T>& v) {
   return PyBytes_FromStringAndSize(reinterpret_cast<const char*>(v.data()), (Py_ssize_t)(v.size() * sizeof(T)));
 }
 
+// ---------------------------------------------------------------------------
+// Parallel fast path.
+//
+// Most records hold plain data: lists of exact dicts whose values are exact
+// floats, small exact ints, None, bools and empty or small lists.  For those,
+// worker threads read the dicts directly while the calling thread holds the
+// GIL and waits for them, so no Python code can run, allocate, free or mutate
+// anything meanwhile.  The workers only read immutable payloads (float
+// values, compact int digits, string bytes) and dict and list entry tables;
+// they never change a reference count, allocate a Python object or raise.
+// A slot holding anything else (strings to parse, big ints, subclasses,
+// objects with __float__, unusual process entries) is marked and packed by
+// the object-API path above on the calling thread, so both paths produce
+// exactly what the Python packer specifies.
+//
+// Pass one reads every sample dict of a slot once (its values under our
+// keys), keeps the samples with a finite time in time order and counts them;
+// the calling thread then places every slot in the output columns; pass two
+// converts the kept samples straight into the final column buffers.
+struct SlotPlan {
+  bool fast = false;                   // packed by the workers
+  Py_ssize_t base = 0;                 // first output row
+  std::vector<Py_ssize_t> order;       // kept items of the raw list, in time order
+  std::vector<double> t;               // their times
+  std::vector<PyObject*> vals;         // per raw item, its values under our keys (borrowed, NULL: absent)
+  std::vector<uint8_t> source_ids;     // per kept sample, numbered on the calling thread in slot order
+  std::vector<std::pair<Py_ssize_t, std::vector<PyObject*>>> foreign;   // (kept position, borrowed pids)
+};
+
+// Output columns in their final buffers (bytes objects the calling thread allocated).
+struct OutColumns {
+  double *t, *power, *memory, *gfx, *sm, *mem, *temp, *plimit, *enf, *pstate, *e_float;
+  int64_t *e_int, *throttle;
+  uint16_t* flags;
+  uint8_t* source;
+};
+
+// Key of an exact str by content (-1: not one of ours, -2: not an exact str), with a pointer cache per worker.
+struct KeyCache {
+  PyObject* key[64] = {};
+  int8_t index[64] = {};
+  size_t length[K_COUNT];
+  KeyCache() { for (int j = 0; j < K_COUNT; ++j) length[j] = strlen(kKeyNames[j]); }
+  int find(PyObject* k) {
+    const size_t h = (reinterpret_cast<uintptr_t>(k) >> 4) & 63;
+    if (key[h] == k) return index[h];
+    int found = -1;
+    if (!PyUnicode_CheckExact(k)) {
+      found = -2;                      // equality of such a key with our names is the object API's call
+    } else if (PyUnicode_KIND(k) == PyUnicode_1BYTE_KIND) {
+      const size_t n = (size_t)PyUnicode_GET_LENGTH(k);
+      const char* data = reinterpret_cast<const char*>(PyUnicode_1BYTE_DATA(k));
+      for (int j = 0; j < K_COUNT; ++j)
+        if (length[j] == n && memcmp(kKeyNames[j], data, n) == 0) { found = j; break; }
+    }
+    key[h] = k;
+    index[h] = (int8_t)found;
+    return found;
+  }
+};
+
+bool compact_int(PyObject* v, int64_t* out) {
+  if (!PyLong_CheckExact(v) || !PyUnstable_Long_IsCompact(reinterpret_cast<PyLongObject*>(v))) return false;
+  *out = (int64_t)PyUnstable_Long_CompactValue(reinterpret_cast<PyLongObject*>(v));
+  return true;
+}
+
+// _finite on plain values: 1 finite (*out), 0 None/absent/bool/non-finite, -1 needs the object API.
+int plain_finite(PyObject* v, double* out) {
+  if (!v || v == Py_None || PyBool_Check(v)) return 0;
+  if (PyFloat_CheckExact(v)) {
+    const double d = PyFloat_AS_DOUBLE(v);
+    if (!std::isfinite(d)) return 0;
+    *out = d;
+    return 1;
+  }
+  int64_t i;
+  if (compact_int(v, &i)) { *out = (double)i; return 1; }
+  return -1;
+}
+
+// The dict's values under our keys (NULL: absent); false when a key needs the object API.
+bool read_keys(PyObject* d, KeyCache& cache, PyObject** vals) {
+  for (int j = 0; j < K_COUNT; ++j) vals[j] = nullptr;
+  Py_ssize_t pos = 0;
+  PyObject *k, *v;
+  while (PyDict_Next(d, &pos, &k, &v)) {
+    const int j = cache.find(k);
+    if (j == -2) return false;
+    if (j >= 0) vals[j] = v;
+  }
+  return true;
+}
+
+// Inventory entry pid against the measurement pid: 1 differs, 0 equal, -1 needs the object API.
+int plain_differs(PyObject* p, PyObject* pid) {
+  if (p == pid) return 0;
+  if (p == Py_None || pid == Py_None) return 1;
+  int64_t a, b;
+  if (compact_int(p, &a) && compact_int(pid, &b)) return a != b;
+  return -1;
+}
+
+// Pass one: read, keep and order a slot's samples.
+bool plan_slot(PyObject* raw, SlotPlan& plan, KeyCache& cache) {
+  const Py_ssize_t n = PyList_GET_SIZE(raw);
+  struct Item { double t; Py_ssize_t index; };
+  std::vector<Item> items;
+  items.reserve((size_t)n);
+  plan.vals.assign((size_t)n * K_COUNT, nullptr);
+  bool ascending = true;
+  for (Py_ssize_t i = 0; i < n; ++i) {
+    PyObject* item = PyList_GET_ITEM(raw, i);
+    if (!PyDict_Check(item)) continue;            // not a sample (the reference skips it)
+    if (!PyDict_CheckExact(item)) return false;
+    PyObject** v = &plan.vals[(size_t)i * K_COUNT];
+    if (!read_keys(item, cache, v)) return false;
+    double t;
+    const int r = plain_finite(v[K_T], &t);
+    if (r < 0) return false;
+    if (!r) continue;
+    if (!items.empty() && !(items.back().t < t)) ascending = false;
+    items.push_back({t, i});
+  }
+  if (!ascending) {
+    std::stable_sort(items.begin(), items.end(), [](const Item& a, const Item& b) { return a.t < b.t; });
+    size_t w = 0;
+    for (size_t k = 0; k < items.size(); ++k)     // equal timestamps: the last one wins
+      if (!(k + 1 < items.size() && items[k + 1].t == items[k].t)) items[w++] = items[k];
+    items.resize(w);
+  }
+  plan.order.resize(items.size());
+  plan.t.resize(items.size());
+  for (size_t k = 0; k < items.size(); ++k) { plan.order[k] = items[k].index; plan.t[k] = items[k].t; }
+  return true;
+}
+
+// Pass two: the kept samples into rows base.. of the output.
+bool fill_slot(SlotPlan& plan, PyObject* pid, KeyCache& cache, const OutColumns& c) {
+  const Key fields[9] = {K_POWER, K_MEMORY, K_GFX, K_SM, K_MEM, K_TEMP, K_PLIMIT, K_ENF, K_PSTATE};
+  double* cols[9] = {c.power, c.memory, c.gfx, c.sm, c.mem, c.temp, c.plimit, c.enf, c.pstate};
+  std::vector<PyObject*> found;
+  const size_t m = plan.order.size();
+  for (size_t k = 0; k < m; ++k) {
+    const size_t row = (size_t)plan.base + k;
+    PyObject** v = &plan.vals[(size_t)plan.order[k] * K_COUNT];
+    c.t[row] = plan.t[k];
+    for (int j = 0; j < 9; ++j) {
+      double x;
+      const int r = plain_finite(v[fields[j]], &x);
+      if (r < 0) return false;
+      cols[j][row] = r ? x : kNaN;
+    }
+    uint32_t flags = 0;
+    int64_t e_int = 0;
+    double e_float = kNaN;
+    if (PyObject* e = v[K_ENERGY]; e && e != Py_None && !PyBool_Check(e)) {
+      int64_t i;
+      if (compact_int(e, &i)) {
+        flags |= PM_S_ENERGY_ANCHOR;
+        e_int = i;
+        if (i >= 0) flags |= PM_S_ENERGY_INT;
+      } else if (PyFloat_CheckExact(e)) {
+        if (PyFloat_AS_DOUBLE(e) >= 0) { flags |= PM_S_ENERGY_FLOAT; e_float = PyFloat_AS_DOUBLE(e); }
+      } else {
+        return false;
+      }
+    }
+    c.e_int[row] = e_int;
+    c.e_float[row] = e_float;
+    int64_t mask = 0;
+    if (PyObject* tr = v[K_THROTTLE]; tr && tr != Py_None) {
+      if (!compact_int(tr, &mask)) return false;
+      flags |= PM_S_THROTTLE_VALID;
+    }
+    c.throttle[row] = mask;
+    const Key inventories[2] = {K_COMPUTE, K_GRAPHICS};
+    const uint32_t missing[2] = {PM_S_NO_COMPUTE_INV, PM_S_NO_GRAPHICS_INV};
+    found.clear();
+    for (int j = 0; j < 2; ++j) {
+      PyObject* inv = v[inventories[j]];
+      if (!inv || !PyList_Check(inv)) { flags |= missing[j]; continue; }
+      if (!PyList_CheckExact(inv)) return false;
+      const Py_ssize_t q = PyList_GET_SIZE(inv);
+      if (q > 0 && pid == Py_None) flags |= PM_S_PID_UNKNOWN;
+      for (Py_ssize_t e = 0; e < q; ++e) {
+        PyObject* entry = PyList_GET_ITEM(inv, e);
+        PyObject* p = entry;
+        if (PyDict_Check(entry)) {
+          if (!PyDict_CheckExact(entry)) return false;
+          PyObject* ev[K_COUNT];
+          if (!read_keys(entry, cache, ev)) return false;
+          p = ev[K_PID] ? ev[K_PID] : Py_None;
+        }
+        const int ne = plain_differs(p, pid);
+        if (ne < 0) return false;
+        if (ne) {
+          flags |= PM_S_REF_FOREIGN;
+          if (p != Py_None) { flags |= PM_S_FOREIGN_PID; found.push_back(p); }
+        }
+      }
+    }
+    if (!found.empty()) plan.foreign.emplace_back((Py_ssize_t)k, found);
+    if (PyObject* mps = v[K_MPS]) {
+      if (PyList_CheckExact(mps)) { if (PyList_GET_SIZE(mps) > 0) flags |= PM_S_MPS; }
+      else if (mps == Py_True) flags |= PM_S_MPS;
+      else if (mps != Py_None && mps != Py_False) return false;
+    }
+    if (v[K_MEMORY] && v[K_MEMORY] != Py_None) flags |= PM_S_MEMORY_POWER_SET;
+    c.source[row] = plan.source_ids[k];
+    c.flags[row] = (uint16_t)flags;
+  }
+  return true;
+}
+
+// Slots the last pack() call packed on the fast path (for tests and diagnostics).
+Py_ssize_t g_last_fast_slots = 0;
+
+int pack_threads() {
+  static const int n = [] {
+    const char* env = getenv("PM_PACK_THREADS");
+    int v = env ? atoi(env) : (int)std::min(8u, std::max(1u, std::thread::hardware_concurrency()));
+    return std::max(1, std::min(v, 64));
+  }();
+  return n;
+}
+
+// Runs fn(slot index) over `slots` on up to `workers` threads (the calling thread included).
+template <class F>
+void parallel_for(const std::vector<Py_ssize_t>& slots, int workers, F fn) {
+  std::atomic<size_t> next{0};
+  auto work = [&] {
+    for (size_t j; (j = next.fetch_add(1)) < slots.size();) fn(slots[j]);
+  };
+  std::vector<std::thread> pool;
+  for (int w = 1; w < workers; ++w) pool.emplace_back(work);
+  work();
+  for (auto& th : pool) th.join();
+}
+
 // pack(slots, pids, source_ids) -> (columns, counts, sorted, foreign)
 //   slots: list of iterables of raw samples (one per (trial, phase) slot)
 //   pids: list of the measurement pid of each slot's trial
@@ -315,50 +558,198 @@ PyObject* pack(PyObject*, PyObject* args) {
   if (!PyArg_ParseTuple(args, "O!O!O!", &PyList_Type, &slots, &PyList_Type, &pids, &PyDict_Type, &table)) return nullptr;
   const Py_ssize_t n = PyList_GET_SIZE(slots);
   if (PyList_GET_SIZE(pids) != n) { PyErr_SetString(PyExc_ValueError, "slots and pids differ in length"); return nullptr; }
-  Columns c;
-  PyObject* counts = PyList_New(n);
-  PyObject* sorted = PyList_New(n);
-  PyObject* foreign = PyList_New(n);
-  if (!counts || !sorted || !foreign) { Py_XDECREF(counts); Py_XDECREF(sorted); Py_XDECREF(foreign); return nullptr; }
-  auto fail = [&]() -> PyObject* { Py_DECREF(counts); Py_DECREF(sorted); Py_DECREF(foreign); return nullptr; };
+  std::vector<SlotPlan> plans((size_t)n);
+  std::vector<Py_ssize_t> lists;
+  Py_ssize_t raw_total = 0;
   for (Py_ssize_t i = 0; i < n; ++i) {
+    PyObject* raw = PyList_GET_ITEM(slots, i);
+    if (PyList_CheckExact(raw)) { lists.push_back(i); raw_total += PyList_GET_SIZE(raw); }
+  }
+  const int workers = raw_total >= 4096 ? std::min<int>(pack_threads(), (int)lists.size()) : 1;
+  parallel_for(lists, workers, [&](Py_ssize_t i) {
+    KeyCache cache;
+    SlotPlan& plan = plans[(size_t)i];
+    plan.fast = plan_slot(PyList_GET_ITEM(slots, i), plan, cache);
+    if (!plan.fast) plan = SlotPlan{};
+  });
+  // Every other slot through the object-API path, then every slot's place in the output.
+  std::vector<PyObject*> sorted_lists((size_t)n, nullptr);
+  std::vector<Columns> slow((size_t)n);
+  std::vector<PyObject*> slow_foreign((size_t)n, nullptr);
+  auto release = [&] {
+    for (PyObject* o : sorted_lists) Py_XDECREF(o);
+    for (PyObject* o : slow_foreign) Py_XDECREF(o);
+  };
+  // Memory-power sources are numbered in first-seen order over slots and samples, so every
+  // slot's sources are numbered here, in slot order, whichever path packs it.
+  Py_ssize_t rows = 0;
+  PyObject* cached_source = nullptr;
+  uint8_t cached_id = 0;
+  for (Py_ssize_t i = 0; i < n; ++i) {
+    SlotPlan& plan = plans[(size_t)i];
+    plan.base = rows;
+    if (plan.fast) {
+      plan.source_ids.resize(plan.order.size());
+      for (size_t k = 0; k < plan.order.size(); ++k) {
+        PyObject* src = plan.vals[(size_t)plan.order[k] * K_COUNT + K_SOURCE];
+        if (src && src != cached_source) {
+          if (source_id(src, table, &cached_id) < 0) { release(); return nullptr; }
+          cached_source = src;
+        }
+        plan.source_ids[k] = src ? cached_id : 0;
+      }
+      rows += (Py_ssize_t)plan.order.size();
+      continue;
+    }
+    cached_source = nullptr;
     PyObject* samples = sorted_samples(PyList_GET_ITEM(slots, i));
-    if (!samples) return fail();
-    PyList_SET_ITEM(sorted, i, samples);
+    if (!samples) { release(); return nullptr; }
+    sorted_lists[(size_t)i] = samples;
     PyObject* slot_foreign = PyList_New(0);
-    if (!slot_foreign) return fail();
-    PyList_SET_ITEM(foreign, i, slot_foreign);
-    PyObject* pid = PyList_GET_ITEM(pids, i);
+    if (!slot_foreign) { release(); return nullptr; }
+    slow_foreign[(size_t)i] = slot_foreign;
     const Py_ssize_t m = PyList_GET_SIZE(samples);
     for (Py_ssize_t k = 0; k < m; ++k) {
       PyObject* found = PyList_New(0);
-      if (!found) return fail();
-      if (pack_sample(PyList_GET_ITEM(samples, k), pid, table, c, found) < 0) { Py_DECREF(found); return fail(); }
+      if (!found) { release(); return nullptr; }
+      if (pack_sample(PyList_GET_ITEM(samples, k), PyList_GET_ITEM(pids, i), table, slow[(size_t)i], found) < 0) {
+        Py_DECREF(found); release(); return nullptr;
+      }
       if (PyList_GET_SIZE(found) > 0) {
         PyObject* entry = Py_BuildValue("(nN)", k, found);
-        if (!entry || PyList_Append(slot_foreign, entry) < 0) { Py_XDECREF(entry); return fail(); }
+        if (!entry || PyList_Append(slot_foreign, entry) < 0) { Py_XDECREF(entry); release(); return nullptr; }
         Py_DECREF(entry);
       } else {
         Py_DECREF(found);
+      }
+    }
+    rows += m;
+  }
+  // The output columns, allocated once; pass two fills the fast slots' rows in parallel.
+  const char* names[15] = {"t_s", "power_w", "memory_power_w", "graphics_clock_mhz", "sm_clock_mhz", "memory_clock_mhz",
+                           "temperature_c", "power_limit_w", "enforced_power_limit_w", "pstate", "energy_int",
+                           "energy_float", "throttle_reasons", "sample_flags", "memory_power_source"};
+  const size_t widths[15] = {8, 8, 8, 8, 8, 8, 8, 8, 8, 8, 8, 8, 8, 2, 1};
+  PyObject* columns = PyDict_New();
+  if (!columns) { release(); return nullptr; }
+  char* buf[15];
+  for (int j = 0; j < 15; ++j) {
+    PyObject* b = PyBytes_FromStringAndSize(nullptr, (Py_ssize_t)(rows * widths[j]));
+    if (!b || PyDict_SetItemString(columns, names[j], b) < 0) { Py_XDECREF(b); Py_DECREF(columns); release(); return nullptr; }
+    Py_DECREF(b);
+    buf[j] = PyBytes_AS_STRING(b);
+  }
+  const OutColumns out{reinterpret_cast<double*>(buf[0]), reinterpret_cast<double*>(buf[1]),
+                       reinterpret_cast<double*>(buf[2]), reinterpret_cast<double*>(buf[3]),
+                       reinterpret_cast<double*>(buf[4]), reinterpret_cast<double*>(buf[5]),
+                       reinterpret_cast<double*>(buf[6]), reinterpret_cast<double*>(buf[7]),
+                       reinterpret_cast<double*>(buf[8]), reinterpret_cast<double*>(buf[9]),
+                       reinterpret_cast<double*>(buf[11]), reinterpret_cast<int64_t*>(buf[10]),
+                       reinterpret_cast<int64_t*>(buf[12]), reinterpret_cast<uint16_t*>(buf[13]),
+                       reinterpret_cast<uint8_t*>(buf[14])};
+  std::vector<Py_ssize_t> fast;
+  for (Py_ssize_t i = 0; i < n; ++i)
+    if (plans[(size_t)i].fast) fast.push_back(i);
+  std::vector<char> refill((size_t)n, 0);        // a fast slot pass two could not convert
+  parallel_for(fast, workers, [&](Py_ssize_t i) {
+    KeyCache cache;
+    if (!fill_slot(plans[(size_t)i], PyList_GET_ITEM(pids, i), cache, out)) refill[(size_t)i] = 1;
+  });
+  // Slots pass two gave up on: the object-API path into the same rows.
+  for (Py_ssize_t i : fast) {
+    if (!refill[(size_t)i]) continue;
+    SlotPlan& plan = plans[(size_t)i];
+    plan.fast = false;
+    PyObject* samples = sorted_samples(PyList_GET_ITEM(slots, i));
+    PyObject* slot_foreign = samples ? PyList_New(0) : nullptr;
+    if (!slot_foreign) { Py_XDECREF(samples); Py_DECREF(columns); release(); return nullptr; }
+    sorted_lists[(size_t)i] = samples;
+    slow_foreign[(size_t)i] = slot_foreign;
+    for (Py_ssize_t k = 0; k < PyList_GET_SIZE(samples); ++k) {
+      PyObject* found = PyList_New(0);
+      if (!found || pack_sample(PyList_GET_ITEM(samples, k), PyList_GET_ITEM(pids, i), table, slow[(size_t)i], found) < 0) {
+        Py_XDECREF(found); Py_DECREF(columns); release(); return nullptr;
+      }
+      if (PyList_GET_SIZE(found) > 0) {
+        PyObject* entry = Py_BuildValue("(nN)", k, found);
+        if (!entry || PyList_Append(slot_foreign, entry) < 0) { Py_XDECREF(entry); Py_DECREF(columns); release(); return nullptr; }
+        Py_DECREF(entry);
+      } else {
+        Py_DECREF(found);
+      }
+    }
+  }
+  // Object-API slots: their columns into their rows.
+  for (Py_ssize_t i = 0; i < n; ++i) {
+    if (plans[(size_t)i].fast) continue;
+    const Columns& c = slow[(size_t)i];
+    const size_t b = (size_t)plans[(size_t)i].base, m = c.t.size();
+    auto put = [&](auto* dst, const auto& src) { if (m) memcpy(dst + b, src.data(), m * sizeof(src[0])); };
+    put(out.t, c.t); put(out.power, c.power); put(out.memory, c.memory); put(out.gfx, c.gfx); put(out.sm, c.sm);
+    put(out.mem, c.mem); put(out.temp, c.temp); put(out.plimit, c.plimit); put(out.enf, c.enf);
+    put(out.pstate, c.pstate); put(out.e_float, c.e_float); put(out.e_int, c.e_int); put(out.throttle, c.throttle);
+    put(out.flags, c.flags); put(out.source, c.source);
+  }
+  g_last_fast_slots = (Py_ssize_t)std::count_if(plans.begin(), plans.end(), [](const SlotPlan& p) { return p.fast; });
+  PyObject* counts = PyList_New(n);
+  PyObject* sorted = PyList_New(n);
+  PyObject* foreign = PyList_New(n);
+  auto fail = [&]() -> PyObject* {
+    Py_XDECREF(counts); Py_XDECREF(sorted); Py_XDECREF(foreign); Py_DECREF(columns); release(); return nullptr;
+  };
+  if (!counts || !sorted || !foreign) return fail();
+  for (Py_ssize_t i = 0; i < n; ++i) {
+    SlotPlan& plan = plans[(size_t)i];
+    PyObject* raw = PyList_GET_ITEM(slots, i);
+    Py_ssize_t m;
+    if (!plan.fast) {
+      PyList_SET_ITEM(sorted, i, sorted_lists[(size_t)i]);
+      sorted_lists[(size_t)i] = nullptr;
+      PyList_SET_ITEM(foreign, i, slow_foreign[(size_t)i]);
+      slow_foreign[(size_t)i] = nullptr;
+      m = PyList_GET_SIZE(PyList_GET_ITEM(sorted, i));
+    } else {
+      m = (Py_ssize_t)plan.order.size();
+      // A raw list already in time order with every item kept is its own sorted
+      // list (the packer never mutates it): no new list and no per-sample
+      // reference count to touch (each sample dict is a cache miss).
+      bool whole = m == PyList_GET_SIZE(raw);
+      for (Py_ssize_t k = 0; whole && k < m; ++k) whole = plan.order[(size_t)k] == k;
+      PyObject* samples = whole ? (Py_INCREF(raw), raw) : PyList_New(m);
+      if (!samples) return fail();
+      PyList_SET_ITEM(sorted, i, samples);
+      for (Py_ssize_t k = 0; !whole && k < m; ++k) {
+        PyObject* item = PyList_GET_ITEM(raw, plan.order[(size_t)k]);
+        Py_INCREF(item);
+        PyList_SET_ITEM(samples, k, item);
+      }
+      PyObject* slot_foreign = PyList_New(0);
+      if (!slot_foreign) return fail();
+      PyList_SET_ITEM(foreign, i, slot_foreign);
+      for (auto& [k, found_pids] : plan.foreign) {
+        PyObject* found = PyList_New((Py_ssize_t)found_pids.size());
+        if (!found) return fail();
+        for (size_t q = 0; q < found_pids.size(); ++q) {
+          Py_INCREF(found_pids[q]);
+          PyList_SET_ITEM(found, (Py_ssize_t)q, found_pids[q]);
+        }
+        PyObject* entry = Py_BuildValue("(nN)", k, found);
+        if (!entry || PyList_Append(slot_foreign, entry) < 0) { Py_XDECREF(entry); return fail(); }
+        Py_DECREF(entry);
       }
     }
     PyObject* count = PyLong_FromSsize_t(m);
     if (!count) return fail();
     PyList_SET_ITEM(counts, i, count);
   }
-  PyObject* columns = Py_BuildValue("{s:N,s:N,s:N,s:N,s:N,s:N,s:N,s:N,s:N,s:N,s:N,s:N,s:N,s:N,s:N}",
-      "t_s", as_bytes(c.t), "power_w", as_bytes(c.power), "memory_power_w", as_bytes(c.memory),
-      "graphics_clock_mhz", as_bytes(c.gfx), "sm_clock_mhz", as_bytes(c.sm), "memory_clock_mhz", as_bytes(c.mem),
-      "temperature_c", as_bytes(c.temp), "power_limit_w", as_bytes(c.plimit),
-      "enforced_power_limit_w", as_bytes(c.enf), "pstate", as_bytes(c.pstate), "energy_int", as_bytes(c.e_int),
-      "energy_float", as_bytes(c.e_float), "throttle_reasons", as_bytes(c.throttle),
-      "sample_flags", as_bytes(c.flags), "memory_power_source", as_bytes(c.source));
-  if (!columns) return fail();
   return Py_BuildValue("(NNNN)", columns, counts, sorted, foreign);
 }
 
+PyObject* last_fast_slots(PyObject*, PyObject*) { return PyLong_FromSsize_t(g_last_fast_slots); }
+
 PyMethodDef kMethods[] = {
     {"pack", pack, METH_VARARGS, "pack(slots, pids, source_ids) -> (columns, counts, sorted, foreign)"},
+    {"last_fast_slots", last_fast_slots, METH_NOARGS, "slots the last pack() call packed on its parallel fast path"},
     {nullptr, nullptr, 0, nullptr}};
 
 PyModuleDef kModule = {PyModuleDef_HEAD_INIT, "_packnative",

@@ -31,6 +31,11 @@ NAN = float("nan")
 
 def finite(value) -> float | None:
     """The reference's _finite: float(value) when finite, else None."""
+    kind = type(value)
+    if kind is float:                      # the common cases first (bools are neither)
+        return value if math.isfinite(value) else None
+    if kind is int:
+        return float(value)                # finite, or OverflowError as float() raises it
     if isinstance(value, bool):
         return None
     try:
@@ -255,7 +260,8 @@ def _pack_slots_python(slot_raw: list, slot_pid: list):
 
 def _pack_slots_native(slot_raw: list, slot_pid: list):
     columns, counts, slot_samples, slot_foreign = _native_packer().pack(slot_raw, slot_pid, _SOURCE_IDS)
-    arrays = {name: np.frombuffer(columns[name], dtype=dtype).copy() for name, dtype in SAMPLE_COLUMNS}
+    # read-only views of the packer's buffers (nothing writes into packed arrays)
+    arrays = {name: np.frombuffer(columns[name], dtype=dtype) for name, dtype in SAMPLE_COLUMNS}
     return arrays, counts, slot_samples, slot_foreign
 
 

@@ -118,3 +118,22 @@ def test_errors_the_reference_lets_raise(field, value, error):
     for native in (True, False):
         with pytest.raises(error):
             P.pack_trials([copy.deepcopy(record)], [0], ARCHITECTURES, native=native)
+
+
+def test_fast_and_object_paths_number_sources_in_slot_order():
+    """Slots packed on the parallel path and on the object-API path interleave; memory-power
+    source ids still follow first sight over slots in order, as the Python packer numbers them."""
+    from trial_builders import memory_rail_scenarios as rails
+    records = [copy.deepcopy(r) for _, r in rails()][:4] + make_sweep(SweepShape(points=4, repeats=4), 5)
+    for k, record in enumerate(records):
+        for name, phase in record["phases"].items():
+            for i, s in enumerate(phase.get("samples", [])):
+                if isinstance(s, dict):
+                    s["memory_power_source"] = ("src_a", "src_b", "memory_power_instant_w")[(k + i) % 3]
+        if k % 3 == 1:      # an object the parallel path hands back to the object API
+            record["phases"]["measure"]["samples"][0]["power_w"] = IntLike(3)
+    a, b = both(records)
+    assert_same(a, b)
+    from powermodeling_b200 import _packnative
+    P.pack_trials(records, [0] * len(records), ARCHITECTURES, native=True)
+    assert 0 < _packnative.last_fast_slots() < 5 * len(records)
