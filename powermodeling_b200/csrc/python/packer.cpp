@@ -304,11 +304,6 @@ PyObject* sorted_samples(PyObject* raw) {
   return out;
 }
 
-template <class T>
-PyObject* as_bytes(const std::vector<T>& v) {
-  return PyBytes_FromStringAndSize(reinterpret_cast<const char*>(v.data()), (Py_ssize_t)(v.size() * sizeof(T)));
-}
-
 // ---------------------------------------------------------------------------
 // Parallel fast path.
 //
@@ -634,10 +629,10 @@ PyObject* pack(PyObject*, PyObject* args) {
   if (!columns) { release(); return nullptr; }
   char* buf[15];
   for (int j = 0; j < 15; ++j) {
-    PyObject* b = PyBytes_FromStringAndSize(nullptr, (Py_ssize_t)(rows * widths[j]));
+    PyObject* b = PyByteArray_FromStringAndSize(nullptr, (Py_ssize_t)(rows * widths[j]));
     if (!b || PyDict_SetItemString(columns, names[j], b) < 0) { Py_XDECREF(b); Py_DECREF(columns); release(); return nullptr; }
     Py_DECREF(b);
-    buf[j] = PyBytes_AS_STRING(b);
+    buf[j] = PyByteArray_AS_STRING(b);
   }
   const OutColumns out{reinterpret_cast<double*>(buf[0]), reinterpret_cast<double*>(buf[1]),
                        reinterpret_cast<double*>(buf[2]), reinterpret_cast<double*>(buf[3]),

@@ -260,7 +260,7 @@ def _pack_slots_python(slot_raw: list, slot_pid: list):
 
 def _pack_slots_native(slot_raw: list, slot_pid: list):
     columns, counts, slot_samples, slot_foreign = _native_packer().pack(slot_raw, slot_pid, _SOURCE_IDS)
-    # read-only views of the packer's buffers (nothing writes into packed arrays)
+    # views of the bytearrays the packer filled (no copy)
     arrays = {name: np.frombuffer(columns[name], dtype=dtype) for name, dtype in SAMPLE_COLUMNS}
     return arrays, counts, slot_samples, slot_foreign
 
