@@ -805,36 +805,42 @@ def cpu_baseline(records, policy, groups: int = 8) -> dict:
 
 
 def run_reference(args) -> dict:
-    """The reference's CPU analysis restated (oracle), all host cores, on the same workload."""
-    from dataclasses import asdict
+    """The reference's CPU analysis restated (oracle), all host cores, on the same workload.
+
+    One step = the 64-point sweep of one GPU's share (256 trials, 64 groups of 4
+    at B = 10 000) from the record dicts: the trials are analysed and every
+    group's medians and intervals computed by processes over groups on every
+    host core (the records of each group are sent to its process inside the
+    step, as summarize(records) receives them)."""
     from powermodeling_b200.synthetic import ANALYSIS_POLICY, SweepShape, make_sweep
     records = make_sweep(SweepShape(points=POINTS, repeats=REPEATS), seed=0)
     pol = dict(__import__("oracle.analysis_oracle", fromlist=["DEFAULT_POLICY"]).DEFAULT_POLICY, **ANALYSIS_POLICY)
     cores = os.cpu_count() or 1
     jobs = [(records[i * REPEATS:(i + 1) * REPEATS], 1000003 + i, pol, RESAMPLES) for i in range(POINTS)]
-    # Each step is a bounded sample of the sweep: one group per host core, the
-    # groups taken in turn, so K steps end within minutes on any core count.
-    per_step = max(1, min(POINTS, cores))
+    samples = sum(len(ph.get("samples", [])) for r in records for ph in (r.get("phases") or {}).values())
     ctx = mp.get_context("spawn")
     with ctx.Pool(cores) as pool:
         for _ in range(args.warmup):
-            pool.map(_oracle_group, jobs[:per_step])
+            pool.map(_oracle_group, jobs, chunksize=1)
         times, resamples = [], 0
-        for k in range(args.steps):
-            batch = [jobs[(k * per_step + j) % POINTS] for j in range(per_step)]
+        for _ in range(args.steps):
             t0 = time.perf_counter()
-            resamples += sum(pool.map(_oracle_group, batch))
+            resamples += sum(pool.map(_oracle_group, jobs, chunksize=1))
             times.append(time.perf_counter() - t0)
     step_s = sum(times) / len(times)
     value = resamples / sum(times)
+    world = max(1, args.gpus)
     return {"impl": "reference", "metric": METRIC, "value": value, "unit": "resamples/s", "n_gpus": args.gpus,
             "steps": args.steps, "warmup": args.warmup, "ms_per_step": step_s * 1e3, "higher_is_better": True,
             "scaling": "weak", "vs_baseline": None, "dtype": "f64", "data": "synthetic",
-            "config": {"workload": WORKLOAD, "points": POINTS * max(1, args.gpus), "points_per_gpu": POINTS,
-                       "repeats": REPEATS, "resamples": RESAMPLES},
+            "config": {"workload": WORKLOAD, "points": POINTS * world, "points_per_gpu": POINTS, "repeats": REPEATS,
+                       "trials": POINTS * REPEATS * world, "groups": POINTS * world, "resamples": RESAMPLES,
+                       "samples": samples, "l2": "n/a (host)",
+                       "parallelism": f"processes over groups, {cores} host cores"},
             "cpu_baseline": {"value": value, "unit": "resamples/s", "cores": cores, "kind": "port",
-                             "sample": f"{per_step} of the {POINTS} groups per step (one per core, in turn), "
-                                       f"processes over groups"},
+                             "sample": f"each step the {POINTS}-point sweep of one GPU's share "
+                                       f"({POINTS * REPEATS} trials, {POINTS} groups) from the record dicts, "
+                                       f"processes over groups on {cores} cores"},
             "e2e": {"value": value, "unit": "resamples/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
 
 
