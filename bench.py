@@ -498,8 +498,16 @@ def run_b200(args, rank: int, world: int) -> dict | None:
     if world == 1 and not args.no_cpu_baseline:
         line["cpu_baseline"] = cpu_baseline(records, policy)
     if not args.no_arms and world == 1:
-        line["arms"] = run_arms(local, peaks)
-        line["arms"]["analysis_scaled"] = run_scaled_analysis(packed, native_policy, peaks)
+        arms, detail = run_arms(local, peaks, energy=not args.no_energy)
+        scaled = run_scaled_analysis(packed, native_policy, peaks)
+        detail["analysis_scaled"] = scaled
+        largest = scaled[max(scaled, key=int)]
+        arms["analysis_kernel_65536_trials"] = {"trials_per_s": _sig(largest["trials_per_s"]),
+                                                "samples_per_s": _sig(largest["samples_per_s"]),
+                                                "frac_of_hbm": _sig(largest["frac_of_hbm"], 3)}
+        if args.arms_detail:
+            Path(args.arms_detail).write_text(json.dumps(detail, indent=1, default=str))
+        line["arms"] = arms
     return line
 
 
@@ -642,24 +650,35 @@ def run_telemetry_arm(uuid: str) -> dict:
     return out
 
 
-def run_arms(local: int, peaks: dict) -> dict:
-    """HBM read/copy, tcgen05 tensor, cuBLAS GEMM and SFU arms through the powerbench engine."""
-    sms = 148
-    out = {}
+def _sig(x, digits: int = 4):
+    """A float rounded to a few significant digits (the JSON line stays short)."""
+    if not isinstance(x, float) or x != x or x in (float("inf"), float("-inf")) or x == 0:
+        return x
+    from math import floor, log10
+    return round(x, max(0, digits - 1 - int(floor(log10(abs(x))))))
+
+
+def compact(obj, digits: int = 5, keep=("value", "ms_per_step")):
+    """The result line with every nested float rounded (the driver keeps the tail of stdout),
+    except the headline keys."""
+    if isinstance(obj, dict):
+        return {k: (v if k in keep else compact(v, digits, ())) for k, v in obj.items()}
+    if isinstance(obj, list):
+        return [compact(v, digits, ()) for v in obj]
+    return _sig(obj, digits) if isinstance(obj, float) else obj
+
+
+def run_arms(local: int, peaks: dict, energy: bool = True) -> dict:
+    """The workload arms on this GPU (powermodeling_b200.sweeps, quick grids): HBM read/copy against the
+    interface ceiling, tcgen05 and cuBLAS tensor throughput, the six SFU opcodes at 148 x 8 CTAs,
+    L1 and the dependent chase at 96 MiB, and NVML energy per byte, per FLOP and per SFU instruction
+    from captured 10 s trials.  Returns (compact summary, full detail)."""
+    from powermodeling_b200 import sweeps as S
+    dev = S.describe()
+    sms, bus = dev["sm_count"], dev["memory_bus_width_bits"]
     clocks = ClockSampler(local)
     clocks.start()
-    hbm = ["--workload", "hbm", "--memory-vector-bytes", "16", "--read-cache-policy", "cs", "--blocks", str(sms * 8),
-           "--threads", "256", "--working-set-bytes", str(4 << 30), "--iterations", "1024",
-           "--batch-launches", "8", "--fixed-batches", "6", *ARM_QUICK]
-    device, r = _arm(hbm)
-    sms = device["sm_count"]
-    bus = device["memory_bus_width_bits"]
-    out["hbm_read"] = {"gbs": r["throughput_bytes_s"] / 1e9, "bytes": r["logical_bytes"], "duration_s": r["duration_s"],
-                       "validation": r["memory_read_validation"]["status"], "config": "16 B loads (.cs), 4 GiB, grid 148x8x256"}
-    _, r = _arm(["--workload", "hbm", "--access", "copy", "--memory-vector-bytes", "16", "--blocks", str(sms * 8),
-                 "--threads", "256", "--working-set-bytes", str(4 << 30), "--iterations", "512", "--batch-launches", "8",
-                 "--fixed-batches", "6", *ARM_QUICK])
-    out["hbm_copy"] = {"gbs": r["throughput_bytes_s"] / 1e9, "config": "16 B load+store, 4 GiB, grid 148x8x256"}
+    hbm = S.hbm_sweep(sms, quick=True)
     tensor = {}
     for acc in (1, 2, 4, 8):
         # 2 s per arm: long enough for the power-capped clock to settle and be sampled.
@@ -675,33 +694,54 @@ def run_arms(local: int, peaks: dict) -> dict:
         if c.get("sm_mhz"):
             entry["frac_of_dense_peak_at_arm_clock"] = tflops / (8192 * sms * c["sm_mhz"] * 1e6 / 1e12)
         tensor[str(acc)] = entry
-    out["tensor_tcgen05"] = tensor
     _, r = _arm(["--workload", "gemm", "--gemm-m", "8192", "--gemm-n", "8192", "--gemm-k", "8192", "--batch-launches", "4",
                  "--fixed-batches", "3", *ARM_QUICK])
-    out["gemm_cublas_8192"] = {"tflops": r["throughput_ops_s"] / 1e12}
-    _, r = _arm(["--workload", "sfu_ex2", "--grid-mode", "fixed", "--blocks", str(sms * 8), "--threads", "256",
-                 "--sfu-lanes", str(sms * 8 * 256), "--sfu-chains", "4", "--iterations", "65536", "--batch-launches", "1",
-                 "--fixed-batches", "4", *ARM_QUICK])
-    out["sfu_ex2"] = {"ops_s": r["throughput_ops_s"], "checksum": r["checksum"]}
-    out["nonlinear"] = run_nonlinear_arms(sms, peaks)
+    gemm_tflops = r["throughput_ops_s"] / 1e12
+    sfu = S.sfu_sweep(sms, ks=(8,))
+    cache = S.cache_sweep(sms, quick=True)
+    nonlinear = run_nonlinear_arms(sms, peaks)
     clock = clocks.stop()
-    out["telemetry"] = run_telemetry_arm(device["uuid"])
-    mem_mhz = clock.get("mem_mhz") or device["nominal_max_memory_clock_khz"] / 1e3
-    theory = 2 * mem_mhz * 1e6 * bus / 8 / 1e9
-    hbm_peak = peaks.get("hbm_gbs", 6650.0)
-    for key in ("hbm_read", "hbm_copy"):
-        out[key]["frac_of_measured_copy_peak"] = out[key]["gbs"] / hbm_peak
-        out[key]["frac_of_clock_bus_theory"] = out[key]["gbs"] / theory
-    out["hbm_theory_gbs"] = theory
+    mem_mhz = clock.get("mem_mhz") or dev["nominal_max_memory_clock_khz"] / 1e3
     sm_mhz = clock.get("sm_mhz") or 1965.0
+    S.with_theory(hbm, mem_mhz)
+    S.per_sm_clock(sfu, sms, sm_mhz)
+    telemetry = run_telemetry_arm(dev["uuid"])
+    energy_rows = S.energy_arms(sms) if energy else {}
     dense_peak = 8192 * sms * sm_mhz * 1e6 / 1e12
     best = max(v["tflops"] for v in tensor.values())
-    out["tensor_peak_at_clock_tflops"] = dense_peak
-    out["tensor_best_frac_of_dense_clock_peak"] = best / dense_peak
-    out["tensor_best_frac_of_measured_bf16_gemm"] = best / peaks.get("bf16_tflops", 1590.0)
-    out["sfu_ex2"]["ops_per_sm_per_clock"] = out["sfu_ex2"]["ops_s"] / (sms * sm_mhz * 1e6)
-    out["clocks"] = clock
-    return out
+    hbm_by = {row["factor"]: row for row in hbm}
+    summary = {
+        "hbm": {k: {"gbs": _sig(v["gbs"]), "frac_of_theory": _sig(v["frac_of_theory"], 3),
+                    "frac_of_measured_copy_peak": _sig(v["gbs"] / peaks.get("hbm_gbs", 6650.0), 3)}
+                for k, v in (("read_16B_cs_4GiB", hbm_by["base"]), ("copy_16B_4GiB", hbm_by["access"]),
+                             ("read_4B_cg_4GiB", hbm_by["scalar"]), ("read_16B_cs_lcg_fill", hbm_by["fill"]))},
+        "hbm_theory_gbs": _sig(2 * mem_mhz * 1e6 * bus / 8 / 1e9),
+        "tensor_tcgen05": {"best_tflops": _sig(best), "best_frac_of_dense_peak_at_clock": _sig(max(
+            (v.get("frac_of_dense_peak_at_arm_clock") or 0) for v in tensor.values()), 3),
+            "frac_of_measured_bf16_gemm": _sig(best / peaks.get("bf16_tflops", 1590.0), 3),
+            "by_accumulators_tflops": {k: _sig(v["tflops"]) for k, v in tensor.items()}},
+        "gemm_cublas_8192_tflops": _sig(gemm_tflops),
+        "sfu_148x8_ops_per_sm_clk": {row["opcode"]: _sig(row["ops_per_sm_per_clock"], 3) for row in sfu},
+        "l1_ca_192KiB_per_sm_gbs": _sig(cache["l1"][0]["gbs"]),
+        "chase_96MiB_cycles_per_access": {row["granularity"]: _sig(row["cycles_per_access_median"])
+                                          for row in cache["chase"]},
+        "nonlinear_frac_of_copy_peak": {k: _sig(v["frac_of_measured_copy_peak"], 3) for k, v in nonlinear.items()},
+        "telemetry_samples_per_s_at_10ms": _sig(telemetry["interval_10ms"]["samples_per_s"], 3),
+    }
+    if energy_rows:
+        e_hbm, e_tc = energy_rows["hbm_read"], energy_rows["tensor_tcgen05"]
+        e_sfu = energy_rows.get("sfu_ex2_paired") or {}
+        summary["energy_nvml_10s"] = {
+            "hbm_read_pj_per_byte": _sig(e_hbm.get("pj_per_logical_byte")),
+            "hbm_read_total_pj_per_byte": _sig(e_hbm.get("total_pj_per_logical_byte")),
+            "tcgen05_pj_per_flop": _sig(e_tc.get("operational_idle_increment_pj_per_flop")),
+            "tcgen05_total_pj_per_flop": _sig(e_tc.get("total_pj_per_flop")),
+            "sfu_ex2_delta_pj_per_instruction": _sig(e_sfu.get("sfu_reference_delta_pj_per_instruction")),
+            "valid": [bool(e_hbm.get("valid")), bool(e_tc.get("valid")), bool(e_sfu.get("valid"))]}
+    summary["clocks"] = {"sm_mhz": clock.get("sm_mhz"), "mem_mhz": clock.get("mem_mhz"), "reasons": clock.get("reasons")}
+    detail = {"hbm": hbm, "tensor": tensor, "gemm_tflops": gemm_tflops, "sfu": sfu, "cache": cache,
+              "nonlinear": nonlinear, "telemetry": telemetry, "energy": energy_rows, "clocks": clock}
+    return summary, detail
 
 
 NONLINEAR_ELEMENTS = 1 << 28          # 1 GiB of fp32 input, 1 GiB of output: far above the 126 MB L2
@@ -854,6 +894,8 @@ def main():
                         help="N>1: group results stored into rank 0 by the bootstrap kernel over NVLink, or all-gathered by NCCL")
     parser.add_argument("--no-cpu-baseline", action="store_true")
     parser.add_argument("--no-arms", action="store_true", help="skip the HBM/tensor/GEMM/SFU arm measurements")
+    parser.add_argument("--no-energy", action="store_true", help="skip the captured 10 s energy trials of the arms")
+    parser.add_argument("--arms-detail", help="also write every arm row to this JSON file")
     args = parser.parse_args()
     if args.warmup < 3:
         parser.error("--warmup must be >= 3")
@@ -872,7 +914,7 @@ def main():
     try:
         line = run_b200(args, rank, world)
         if line is not None:
-            print(json.dumps(line), flush=True)
+            print(json.dumps(compact(line)), flush=True)
     finally:
         if world > 1:
             import torch.distributed as dist

@@ -9,6 +9,7 @@
 // oracle/build_oracle.py into liboracle_words.so and called from the tests.
 #include <algorithm>
 #include <cstdint>
+#include <cstring>
 #include <numeric>
 #include <random>
 #include <vector>
@@ -36,6 +37,28 @@ uint64_t oracle_u64_hash(const uint64_t* words, uint64_t n) {
 
 // Sum32 of every thread's reads.  unit = 1 (scalar word) or 4 (16-byte quad);
 // for L1 (slice > 0) thread ids restart per block and each block reads its slice.
+// As oracle_read_sums over an explicit payload (buffer word i = payload[i]),
+// for the fills other than random_word.
+void oracle_read_sums_of(const uint32_t* payload, uint64_t words, uint64_t offset_words, uint64_t blocks,
+                         uint64_t threads, uint64_t stride, uint64_t iterations, uint64_t slice, uint64_t unit,
+                         uint32_t* out, uint64_t count) {
+  const bool l1 = slice > 0;
+  const uint64_t lanes = blocks * threads;
+  const uint64_t region = (l1 ? slice : words) / unit;
+  const uint64_t region_lanes = l1 ? threads : lanes;
+  const uint64_t advance = (region_lanes * stride) % region;
+  for (uint64_t g = 0; g < count && g < lanes; ++g) {
+    const uint64_t block = g / threads, tid = l1 ? g % threads : g;
+    uint64_t pos = (tid * stride) % region;
+    uint32_t sum = 0;
+    for (uint64_t k = 0; k < iterations; ++k) {
+      for (uint64_t w = 0; w < unit; ++w) sum += payload[offset_words + (l1 ? block * slice : 0) + pos * unit + w];
+      pos = (pos + advance) % region;
+    }
+    out[g] = sum;
+  }
+}
+
 void oracle_read_sums(uint64_t words, uint64_t offset_words, uint64_t seed, uint64_t blocks, uint64_t threads,
                       uint64_t stride, uint64_t iterations, uint64_t slice, uint64_t unit, uint32_t* out, uint64_t count) {
   const bool l1 = slice > 0;
@@ -122,6 +145,28 @@ uint64_t oracle_chase_terminal(const uint32_t* next, uint64_t nodes, uint64_t it
 
 uint32_t oracle_sfu_initial_bits(uint64_t lane, uint64_t seed, int chain) {
   return (oracle_random_word(lane ^ seed ^ (uint64_t(chain + 1) * 0x9e3779b97f4a7c15ULL)) & 0x007fffffU) | 0x3f000000U;
+}
+
+// Seeded uint32 LCG fill (the memory arms' extra mode): x_0 = low 32 bits of the
+// seed, x_{i+1} = 1664525 x_i + 1013904223 mod 2^32, stepped one word at a time
+// (the product reaches word i by squaring the step; the two must agree).
+void oracle_lcg_words(uint64_t n, uint64_t seed, uint32_t* out) {
+  uint32_t x = uint32_t(seed);
+  for (uint64_t i = 0; i < n; ++i) {
+    out[i] = x;
+    x = 1664525U * x + 1013904223U;
+  }
+}
+
+// The SFU arm's extra-mode operand: uniform [0.5, 2.0) from the lane hash,
+// 0.5 + 1.5 m / 2^24 for the hash's top 24 bits m, each float operation rounded.
+uint32_t oracle_sfu_uniform_bits(uint64_t lane, uint64_t seed, int chain) {
+  const uint32_t m = oracle_random_word(lane ^ seed ^ (uint64_t(chain + 1) * 0x9e3779b97f4a7c15ULL)) >> 8;
+  volatile float scaled = float(m) * (1.5f / 16777216.0f);
+  const float x = scaled + 0.5f;
+  uint32_t bits;
+  memcpy(&bits, &x, 4);
+  return bits;
 }
 
 }  // extern "C"

@@ -124,6 +124,8 @@ struct Options {
   int row_width = 0;               // RMSNorm/softmax row width (default 1024)
   bool nonlinear_mode_explicit = false;
   bool tensor_uniform = false;     // fp16 operands uniform[-1,1) instead of [-0.25,0.25)
+  int fill = FILL_RANDOM_WORD;     // memory payload: random_word (the reference's) or a seeded uint32 LCG
+  int sfu_input = SFU_INPUT_PARITY;  // SFU operands: the reference's [0.5,1) or uniform [0.5,2) with XOR checksums
   std::vector<unsigned> sm_ids;
   bool describe = false, profile_region = false, paired_reference = false;
   bool blocks_explicit = false, grid_mode_explicit = false, sfu_explicit = false;
@@ -167,6 +169,8 @@ const char* kUsage =
   "  --memory-vector-bytes 4|16 (16: one 16-byte access per thread and iteration)\n"
   "  --chase-granularity word|line (line: 64-bit links on 128-byte lines)\n"
   "  --tensor-input uniform (fp16 operands uniform in [-1,1))\n"
+  "  --fill random_word|lcg (memory payload; lcg: seeded uint32 LCG 1664525 x + 1013904223)\n"
+  "  --sfu-input reference|uniform_0p5_2 (uniform_0p5_2: thread-hash operands in [0.5,2), per-thread XOR checksum)\n"
   "stdout is JSONL, except for this --help text.\n";
 
 Options parse_options(int argc, const char* const* argv, const Sink& out, bool* help) {
@@ -209,6 +213,15 @@ Options parse_options(int argc, const char* const* argv, const Sink& out, bool* 
     else if (flag == "--gemm-k") o.gemm_k = parse_int(v, f);
     else if (flag == "--memory-vector-bytes") o.vector_bytes = parse_int(v, f);
     else if (flag == "--chase-granularity") o.chase_granularity = v;
+    else if (flag == "--fill") {
+      if (v != "random_word" && v != "lcg") throw Failure("--fill must be random_word or lcg");
+      o.fill = v == "lcg" ? FILL_LCG : FILL_RANDOM_WORD;
+    }
+    else if (flag == "--sfu-input") {
+      if (v != "reference" && v != "uniform_0p5_2") throw Failure("--sfu-input must be reference or uniform_0p5_2");
+      o.sfu_input = v == "uniform_0p5_2" ? SFU_INPUT_UNIFORM_0P5_2 : SFU_INPUT_PARITY;
+      o.sfu_explicit = true;
+    }
     else if (flag == "--tensor-input") { if (v != "uniform" && v != "reference") throw Failure("--tensor-input must be uniform or reference"); o.tensor_uniform = v == "uniform"; }
     else if (flag == "--nonlinear-mode") { o.nonlinear_mode = v; o.nonlinear_mode_explicit = true; }
     else if (flag == "--row-width") {
@@ -285,6 +298,8 @@ Options parse_options(int argc, const char* const* argv, const Sink& out, bool* 
   if (o.vector_bytes == 16 && (!(o.workload == "hbm" || o.workload == "l2") || o.access == "write"))
     throw Failure("--memory-vector-bytes 16 applies to L2/HBM read and copy");
   if (o.vector_bytes == 16 && o.offset_bytes % 16) throw Failure("16-byte accesses need --offset-bytes to be a multiple of 16");
+  if (o.fill == FILL_LCG && o.workload != "l1" && o.workload != "l2" && o.workload != "hbm")
+    throw Failure("--fill applies only to l1/l2/hbm memory workloads");
   if (o.chase_granularity != "word" && o.chase_granularity != "line") throw Failure("--chase-granularity must be word or line");
   if (o.chase_granularity == "line" && o.workload != "l2_latency") throw Failure("--chase-granularity applies only to l2_latency");
   return o;
@@ -450,7 +465,8 @@ const char* sfu_opcode(int op) {
 struct SfuCheck { uint64_t checked = 0; double max_abs = 0, max_rel = 0; bool passed = true; };
 
 SfuCheck check_sfu(int op, uint32_t* sample, const Options& o) {
-  check(launch_sfu_check(op, sample, o.sfu_lanes, o.seed, o.sfu_chains, 0), "sfu check launch");
+  check(launch_sfu_check(op, sample, o.sfu_lanes, o.seed, o.sfu_chains, 0, o.sfu_input), "sfu check launch");
+  const float top = o.sfu_input == SFU_INPUT_UNIFORM_0P5_2 ? 2.0f : 1.0f;   // operands lie in [0.5, top)
   check(cudaDeviceSynchronize(), "sfu check");
   uint32_t host[16];
   check(cudaMemcpy(host, sample, sizeof host, cudaMemcpyDeviceToHost), "cudaMemcpy");
@@ -465,7 +481,7 @@ SfuCheck check_sfu(int op, uint32_t* sample, const Options& o) {
     const double err = std::fabs(double(y) - e), rel = err / std::max(std::fabs(e), 1e-30);
     r.max_abs = std::max(r.max_abs, err);
     r.max_rel = std::max(r.max_rel, rel);
-    r.passed = r.passed && std::isfinite(x) && std::isfinite(y) && x >= 0.5f && x < 1.0f && err <= 2e-6 + 2e-5 * std::fabs(e);
+    r.passed = r.passed && std::isfinite(x) && std::isfinite(y) && x >= 0.5f && x < top && err <= 2e-6 + 2e-5 * std::fabs(e);
     ++r.checked;
   }
   return r;
@@ -483,9 +499,21 @@ uint64_t sfu_checksum(const uint32_t* sink, uint64_t lanes) {
   return h;
 }
 
+// XOR of every lane's sink word (the BASELINE-mode per-thread XOR checksums folded into one).
+uint32_t xor_all(const uint32_t* sink, uint64_t lanes) {
+  std::vector<uint32_t> host(lanes);
+  check(cudaMemcpy(host.data(), sink, lanes * 4, cudaMemcpyDeviceToHost), "cudaMemcpy");
+  uint32_t x = 0;
+  for (uint32_t w : host) x ^= w;
+  return x;
+}
+
 void sfu_metadata(Obj& j, const Options& o, int op) {
   j.str("sfu_primitive", o.workload.substr(4)).u("sfu_lanes", o.sfu_lanes).i("sfu_chains", o.sfu_chains)
-   .str("sfu_input_policy", "feedback_xor_iteration_mantissa_0p5_1_v1").str("sfu_ptx_opcode", sfu_opcode(op))
+   .str("sfu_input_policy", o.sfu_input == SFU_INPUT_UNIFORM_0P5_2
+                                ? "thread_hash_uniform_0p5_2_then_feedback_xor_iteration_mantissa_0p5_1_v1"
+                                : "feedback_xor_iteration_mantissa_0p5_1_v1")
+   .str("sfu_ptx_opcode", sfu_opcode(op))
    .b("sfu_approximate", true).b("sfu_flush_to_zero", op != SFU_TANH)
    .raw("sfu_exponent_base", (op == SFU_EX2 || op == SFU_LG2) ? "2" : "null")
    .str("math_implementation", "ptx_approx_register_v1").str("grid_mode", o.grid_mode)
@@ -520,7 +548,7 @@ void experiment_sfu(Options o, const cudaDeviceProp& p, const Sink& out) {
   auto launch = [&](bool control) {
     for (int k = 0; k < o.batch_launches; ++k)
       check(launch_sfu(op, control, o.sfu_chains, control ? ref_sink.p : sink.p, o.sfu_lanes, o.iterations, o.seed,
-                       o.blocks, o.threads, 0), "sfu launch");
+                       o.blocks, o.threads, 0, o.sfu_input), "sfu launch");
   };
   SfuCheck numerical = check_sfu(op, sample.p, o);
   if (!numerical.passed) throw Failure("native SFU one-step output differs from CPU double reference");
@@ -577,7 +605,10 @@ void experiment_sfu(Options o, const cudaDeviceProp& p, const Sink& out) {
      .f("throughput_ops_s", control ? 0.0 : double(slots) / tm.device_s).u("throughput_bytes_s", 0)
      .u("working_set_bytes", 0).u("requested_working_set_bytes", 0).u("allocated_bytes", allocated).u("seed", o.seed)
      .u("checksum", control ? sfu_checksum(ref_sink.p, o.sfu_lanes) : checksum)
-     .str("checksum_kind", "distributed_per_lane_register_fnv_hash_sample")
+     .str("checksum_kind", o.sfu_input == SFU_INPUT_UNIFORM_0P5_2 ? "distributed_per_lane_register_xor_sample"
+                                                                  : "distributed_per_lane_register_fnv_hash_sample")
+     .raw("sfu_thread_xor_checksum", o.sfu_input == SFU_INPUT_UNIFORM_0P5_2
+                                         ? std::to_string(xor_all(control ? ref_sink.p : sink.p, o.sfu_lanes)) : "null")
      .raw("kernel_resources", resources_json(control ? ca : ta, control ? cb : tb, o.threads, p, o.blocks))
      .raw("control_kernel_resources", resources_json(ca, cb, o.threads, p, o.blocks))
      .raw("numerical_validation", Obj().u("checked_values", control ? 0 : numerical.checked)
@@ -850,7 +881,10 @@ ReadCheck check_read_sums(const Options& o, const uint32_t* sink, uint64_t words
       for (uint64_t k = 0; k < steps; ++k) {
         uint32_t v = 0;
         for (uint64_t w = 0; w < unit; ++w)
-          v += random_word((offset_words + (l1 ? block * slice : 0) + pos * unit + w) ^ o.seed);
+        {
+          const uint64_t index = offset_words + (l1 ? block * slice : 0) + pos * unit + w;
+          v += o.fill == FILL_LCG ? lcg_word(index, o.seed) : random_word(index ^ o.seed);
+        }
         cycle += v;
         if (k < o.iterations % period) prefix += v;
         pos = (pos + advance) % region;
@@ -939,8 +973,9 @@ void experiment(Options o, const cudaDeviceProp& p, const Sink& out) {
   check(cudaMemset(ref_sink.p, 0, (context ? lanes : 1) * 4), "cudaMemset");
   check(cudaMemset(ref_blocks.p, 0, (context ? kSmSlots : 1) * 8), "cudaMemset");
   check(cudaMemset(tstatus.p, 0, sizeof(TensorStatus)), "cudaMemset");
-  if (memory) check(launch_fill_words(input.p, words + offset_words, o.seed, p.multiProcessorCount, 0), "fill");
-  if (memory && o.access != "read") check(launch_fill_words(output.p, words + offset_words, o.seed ^ 0x9e3779b9ULL, p.multiProcessorCount, 0), "fill");
+  if (memory) check(launch_fill_words(input.p, words + offset_words, o.seed, p.multiProcessorCount, 0, o.fill), "fill");
+  if (memory && o.access != "read")
+    check(launch_fill_words(output.p, words + offset_words, o.seed ^ 0x9e3779b9ULL, p.multiProcessorCount, 0, o.fill), "fill");
   check(launch_fill_halves(a.p, a_count, o.seed, o.tensor_uniform, p.multiProcessorCount, 0), "fill");
   check(launch_fill_halves(b.p, b_count, o.seed ^ 12345ULL, o.tensor_uniform, p.multiProcessorCount, 0), "fill");
   check(cudaDeviceSynchronize(), "fill kernels");
@@ -1146,6 +1181,7 @@ void experiment(Options o, const cudaDeviceProp& p, const Sink& out) {
    .raw("memory_word_bytes", memory ? "4" : "null").raw("stride_words", memory ? std::to_string(o.stride) : "null")
    .raw("lane_stride_bytes", memory ? std::to_string(o.stride * (vector ? 16 : 4)) : "null")
    .i("memory_vector_bytes", memory ? o.vector_bytes : 0).str("chase_granularity", o.chase_granularity)
+   .raw("memory_fill", memory ? (o.fill == FILL_LCG ? "\"uint32_lcg_1664525_1013904223_v1\"" : "\"random_word_xor_seed_v1\"") : "null")
    .i("tensor_accumulators", acc).i("tensor_tile_m", tensor ? kTmaM : 0).i("tensor_tile_n", tensor ? tensor_tile_n(acc) : 0)
    .i("gemm_m", o.gemm_m).i("gemm_n", o.gemm_n).i("gemm_k", o.gemm_k).u("seed", o.seed)
    .u("checksum", checksum).str("checksum_kind", checksum_kind)

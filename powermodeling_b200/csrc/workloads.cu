@@ -45,17 +45,22 @@ __device__ __forceinline__ uint64_t add_wrap(uint64_t a, uint64_t b, uint64_t n)
 }
 
 // ---------------------------------------------------------------------------
-__global__ void fill_words_kernel(uint32_t* data, uint64_t n, uint64_t seed) {
+__global__ void fill_words_kernel(uint32_t* data, uint64_t n, uint64_t seed, int fill) {
   const uint64_t quads = n / 4;
   const uint64_t step = uint64_t(gridDim.x) * blockDim.x;
   uint4* q = reinterpret_cast<uint4*>(data);
   for (uint64_t i = uint64_t(blockIdx.x) * blockDim.x + threadIdx.x; i < quads; i += step) {
     const uint64_t w = 4 * i;
-    q[i] = make_uint4(random_word(w ^ seed), random_word((w + 1) ^ seed), random_word((w + 2) ^ seed),
-                      random_word((w + 3) ^ seed));
+    if (fill == FILL_LCG) {
+      const uint32_t x0 = lcg_word(w, seed), x1 = 1664525U * x0 + 1013904223U, x2 = 1664525U * x1 + 1013904223U;
+      q[i] = make_uint4(x0, x1, x2, 1664525U * x2 + 1013904223U);
+    } else {
+      q[i] = make_uint4(random_word(w ^ seed), random_word((w + 1) ^ seed), random_word((w + 2) ^ seed),
+                        random_word((w + 3) ^ seed));
+    }
   }
   for (uint64_t w = 4 * quads + uint64_t(blockIdx.x) * blockDim.x + threadIdx.x; w < n; w += step)
-    data[w] = random_word(w ^ seed);
+    data[w] = fill == FILL_LCG ? lcg_word(w, seed) : random_word(w ^ seed);
 }
 
 // fp16 operands: the reference's [-0.25, 0.25) grid (gpu_bench.cu:287-290) or
@@ -236,12 +241,14 @@ __device__ __forceinline__ uint32_t sfu_step(float x) {
 }
 
 template <int Op, bool Control, int Chains>
-__global__ void sfu_kernel(uint32_t* sink, uint64_t lanes, uint64_t iterations, uint64_t seed) {
+__global__ void sfu_kernel(uint32_t* sink, uint64_t lanes, uint64_t iterations, uint64_t seed, int input) {
   const uint64_t step = uint64_t(gridDim.x) * blockDim.x;
   for (uint64_t lane = uint64_t(blockIdx.x) * blockDim.x + threadIdx.x; lane < lanes; lane += step) {
     float state[Chains];
 #pragma unroll
-    for (int c = 0; c < Chains; ++c) state[c] = __uint_as_float(sfu_initial_bits(lane, seed, c));
+    for (int c = 0; c < Chains; ++c)
+      state[c] = __uint_as_float(input == SFU_INPUT_UNIFORM_0P5_2 ? sfu_uniform_bits(lane, seed, c)
+                                                                  : sfu_initial_bits(lane, seed, c));
 #pragma unroll 1
     for (uint64_t it = 0; it < iterations; ++it) {
 #pragma unroll
@@ -250,20 +257,25 @@ __global__ void sfu_kernel(uint32_t* sink, uint64_t lanes, uint64_t iterations, 
         state[c] = __uint_as_float(((r ^ uint32_t(it)) & 0x007fffffU) | 0x3f000000U);
       }
     }
-    uint32_t h = 2166136261U;
+    uint32_t h = 2166136261U, x = 0;
 #pragma unroll
-    for (int c = 0; c < Chains; ++c) h = (h ^ __float_as_uint(state[c])) * 16777619U;
-    sink[lane] = h;
+    for (int c = 0; c < Chains; ++c) {
+      h = (h ^ __float_as_uint(state[c])) * 16777619U;
+      x ^= __float_as_uint(state[c]);
+    }
+    sink[lane] = input == SFU_INPUT_UNIFORM_0P5_2 ? x : h;
   }
 }
 
 // Eight one-step samples (x, MUFU(x)) for the CPU double-precision check (sfu.cuh:107-117).
 template <int Op>
-__global__ void sfu_check_kernel(uint32_t* sample, uint64_t lanes, uint64_t seed, int chains) {
+__global__ void sfu_check_kernel(uint32_t* sample, uint64_t lanes, uint64_t seed, int chains, int input) {
   const unsigned k = threadIdx.x;
   if (k >= 8) return;
   const uint64_t lane = uint64_t(k) * (lanes - 1) / 7;
-  const uint32_t bits = sfu_initial_bits(lane, seed, int(k % unsigned(chains)));
+  const int chain = int(k % unsigned(chains));
+  const uint32_t bits = input == SFU_INPUT_UNIFORM_0P5_2 ? sfu_uniform_bits(lane, seed, chain)
+                                                         : sfu_initial_bits(lane, seed, chain);
   sample[2 * k] = bits;
   sample[2 * k + 1] = sfu_step<Op, false>(__uint_as_float(bits));
 }
@@ -275,8 +287,8 @@ static int fill_grid(uint64_t n, int sms) {
   return int(want < 1 ? 1 : (want > cap ? cap : want));
 }
 
-cudaError_t launch_fill_words(uint32_t* data, uint64_t n, uint64_t seed, int sms, cudaStream_t s) {
-  fill_words_kernel<<<fill_grid(n, sms), 256, 0, s>>>(data, n, seed);
+cudaError_t launch_fill_words(uint32_t* data, uint64_t n, uint64_t seed, int sms, cudaStream_t s, int fill) {
+  fill_words_kernel<<<fill_grid(n, sms), 256, 0, s>>>(data, n, seed, fill);
   return cudaGetLastError();
 }
 
@@ -342,34 +354,38 @@ cudaError_t launch_chase_lines(const uint64_t* lines, uint64_t* terminal, uint64
 }
 
 template <int Op, bool Control>
-static void sfu_dispatch_chains(int chains, uint32_t* sink, uint64_t lanes, uint64_t it, uint64_t seed, int b, int t, cudaStream_t s) {
-  if (chains == 1) sfu_kernel<Op, Control, 1><<<b, t, 0, s>>>(sink, lanes, it, seed);
-  else if (chains == 4) sfu_kernel<Op, Control, 4><<<b, t, 0, s>>>(sink, lanes, it, seed);
-  else sfu_kernel<Op, Control, 8><<<b, t, 0, s>>>(sink, lanes, it, seed);
+static void sfu_dispatch_chains(int chains, uint32_t* sink, uint64_t lanes, uint64_t it, uint64_t seed, int b, int t,
+                                cudaStream_t s, int input) {
+  if (chains == 1) sfu_kernel<Op, Control, 1><<<b, t, 0, s>>>(sink, lanes, it, seed, input);
+  else if (chains == 4) sfu_kernel<Op, Control, 4><<<b, t, 0, s>>>(sink, lanes, it, seed, input);
+  else sfu_kernel<Op, Control, 8><<<b, t, 0, s>>>(sink, lanes, it, seed, input);
 }
 
 cudaError_t launch_sfu(int op, bool control, int chains, uint32_t* sink, uint64_t lanes, uint64_t iterations,
-                       uint64_t seed, int blocks, int threads, cudaStream_t s) {
-  if (control) { sfu_dispatch_chains<SFU_EX2, true>(chains, sink, lanes, iterations, seed, blocks, threads, s); return cudaGetLastError(); }
+                       uint64_t seed, int blocks, int threads, cudaStream_t s, int input) {
+#define PM_SFU(OP, CTRL) sfu_dispatch_chains<OP, CTRL>(chains, sink, lanes, iterations, seed, blocks, threads, s, input)
+  if (control) { PM_SFU(SFU_EX2, true); return cudaGetLastError(); }
   switch (op) {
-    case SFU_EX2: sfu_dispatch_chains<SFU_EX2, false>(chains, sink, lanes, iterations, seed, blocks, threads, s); break;
-    case SFU_TANH: sfu_dispatch_chains<SFU_TANH, false>(chains, sink, lanes, iterations, seed, blocks, threads, s); break;
-    case SFU_RSQRT: sfu_dispatch_chains<SFU_RSQRT, false>(chains, sink, lanes, iterations, seed, blocks, threads, s); break;
-    case SFU_RCP: sfu_dispatch_chains<SFU_RCP, false>(chains, sink, lanes, iterations, seed, blocks, threads, s); break;
-    case SFU_LG2: sfu_dispatch_chains<SFU_LG2, false>(chains, sink, lanes, iterations, seed, blocks, threads, s); break;
-    default: sfu_dispatch_chains<SFU_SQRT, false>(chains, sink, lanes, iterations, seed, blocks, threads, s); break;
+    case SFU_EX2: PM_SFU(SFU_EX2, false); break;
+    case SFU_TANH: PM_SFU(SFU_TANH, false); break;
+    case SFU_RSQRT: PM_SFU(SFU_RSQRT, false); break;
+    case SFU_RCP: PM_SFU(SFU_RCP, false); break;
+    case SFU_LG2: PM_SFU(SFU_LG2, false); break;
+    default: PM_SFU(SFU_SQRT, false); break;
   }
+#undef PM_SFU
   return cudaGetLastError();
 }
 
-cudaError_t launch_sfu_check(int op, uint32_t* sample, uint64_t lanes, uint64_t seed, int chains, cudaStream_t s) {
+cudaError_t launch_sfu_check(int op, uint32_t* sample, uint64_t lanes, uint64_t seed, int chains, cudaStream_t s,
+                             int input) {
   switch (op) {
-    case SFU_EX2: sfu_check_kernel<SFU_EX2><<<1, 32, 0, s>>>(sample, lanes, seed, chains); break;
-    case SFU_TANH: sfu_check_kernel<SFU_TANH><<<1, 32, 0, s>>>(sample, lanes, seed, chains); break;
-    case SFU_RSQRT: sfu_check_kernel<SFU_RSQRT><<<1, 32, 0, s>>>(sample, lanes, seed, chains); break;
-    case SFU_RCP: sfu_check_kernel<SFU_RCP><<<1, 32, 0, s>>>(sample, lanes, seed, chains); break;
-    case SFU_LG2: sfu_check_kernel<SFU_LG2><<<1, 32, 0, s>>>(sample, lanes, seed, chains); break;
-    default: sfu_check_kernel<SFU_SQRT><<<1, 32, 0, s>>>(sample, lanes, seed, chains); break;
+    case SFU_EX2: sfu_check_kernel<SFU_EX2><<<1, 32, 0, s>>>(sample, lanes, seed, chains, input); break;
+    case SFU_TANH: sfu_check_kernel<SFU_TANH><<<1, 32, 0, s>>>(sample, lanes, seed, chains, input); break;
+    case SFU_RSQRT: sfu_check_kernel<SFU_RSQRT><<<1, 32, 0, s>>>(sample, lanes, seed, chains, input); break;
+    case SFU_RCP: sfu_check_kernel<SFU_RCP><<<1, 32, 0, s>>>(sample, lanes, seed, chains, input); break;
+    case SFU_LG2: sfu_check_kernel<SFU_LG2><<<1, 32, 0, s>>>(sample, lanes, seed, chains, input); break;
+    default: sfu_check_kernel<SFU_SQRT><<<1, 32, 0, s>>>(sample, lanes, seed, chains, input); break;
   }
   return cudaGetLastError();
 }

@@ -7,6 +7,7 @@
 // indices compare bit for bit; the vector (16-byte) read/copy and the
 // line-granular chase are additional B200 modes with their own version tags.
 #pragma once
+#include <cstring>
 #include <cstdint>
 #include <cuda_runtime.h>
 
@@ -28,6 +29,36 @@ __host__ __device__ __forceinline__ uint32_t sfu_initial_bits(uint64_t lane, uin
   return (random_word(lane ^ seed ^ (uint64_t(chain + 1) * 0x9e3779b97f4a7c15ULL)) & 0x007fffffU) | 0x3f000000U;
 }
 
+// Seeded uint32 LCG fill (an extra mode beside random_word): x_0 = low 32 bits
+// of the seed, x_{i+1} = 1664525 x_i + 1013904223 (mod 2^32), word i = x_i.
+// Word i is reached in at most 64 squarings of the affine step (a, c):
+// composing (a1, c1) after (a2, c2) gives (a1 a2, a1 c2 + c1).
+__host__ __device__ __forceinline__ uint32_t lcg_word(uint64_t i, uint64_t seed) {
+  uint32_t a = 1664525U, c = 1013904223U, x = uint32_t(seed);
+  while (i) {
+    if (i & 1) x = a * x + c;
+    c = a * c + c;
+    a = a * a;
+    i >>= 1;
+  }
+  return x;
+}
+enum WordFill { FILL_RANDOM_WORD = 0, FILL_LCG = 1 };
+
+// The SFU arm's input in BASELINE mode (an extra mode beside the reference's
+// [0.5, 1) operand): uniform in [0.5, 2.0) from the thread-index hash,
+// 0.5 + 1.5 m / 2^24 for the top 24 bits m of the hash, in two separately
+// rounded float operations.
+__host__ __device__ __forceinline__ uint32_t sfu_uniform_bits(uint64_t lane, uint64_t seed, int chain) {
+  const uint32_t m = random_word(lane ^ seed ^ (uint64_t(chain + 1) * 0x9e3779b97f4a7c15ULL)) >> 8;
+  const float scaled = float(m) * (1.5f / 16777216.0f);
+  const float x = scaled + 0.5f;
+  uint32_t bits;
+  memcpy(&bits, &x, 4);
+  return bits;
+}
+enum SfuInput { SFU_INPUT_PARITY = 0, SFU_INPUT_UNIFORM_0P5_2 = 1 };
+
 // Cache policies of the read arms.
 enum ReadPolicy { RP_CA = 0, RP_CG = 1, RP_CS = 2 };
 enum SfuOp { SFU_EX2 = 0, SFU_TANH = 1, SFU_RSQRT = 2, SFU_RCP = 3, SFU_LG2 = 4, SFU_SQRT = 5 };
@@ -39,7 +70,7 @@ struct Admission {
 };
 
 // Host launchers (workloads.cu).  All return cudaGetLastError() of the launch.
-cudaError_t launch_fill_words(uint32_t* data, uint64_t n, uint64_t seed, int sms, cudaStream_t s);
+cudaError_t launch_fill_words(uint32_t* data, uint64_t n, uint64_t seed, int sms, cudaStream_t s, int fill = FILL_RANDOM_WORD);
 cudaError_t launch_fill_halves(void* data, uint64_t n, uint64_t seed, int uniform_pm1, int sms, cudaStream_t s);
 cudaError_t launch_read_scalar(int policy, bool l1, const uint32_t* in, uint32_t* sink, uint64_t words, uint64_t slice,
                                uint64_t stride, uint64_t iterations, int blocks, int threads, Admission adm, cudaStream_t s);
@@ -57,9 +88,12 @@ cudaError_t launch_chase_words(const uint32_t* links, uint32_t* sink, uint64_t w
 cudaError_t launch_chase_lines(const uint64_t* lines, uint64_t* terminal, uint64_t nodes, uint64_t iterations,
                                uint64_t nonce, int blocks, int threads, Admission adm, unsigned long long* cycles,
                                unsigned long long* loads, cudaStream_t s);
+// input: SFU_INPUT_PARITY (the reference's operands, FNV hash of the chains per lane) or
+// SFU_INPUT_UNIFORM_0P5_2 (uniform [0.5, 2.0) operands, XOR of the chains per lane).
 cudaError_t launch_sfu(int op, bool control, int chains, uint32_t* sink, uint64_t lanes, uint64_t iterations,
-                       uint64_t seed, int blocks, int threads, cudaStream_t s);
-cudaError_t launch_sfu_check(int op, uint32_t* sample, uint64_t lanes, uint64_t seed, int chains, cudaStream_t s);
+                       uint64_t seed, int blocks, int threads, cudaStream_t s, int input = SFU_INPUT_PARITY);
+cudaError_t launch_sfu_check(int op, uint32_t* sample, uint64_t lanes, uint64_t seed, int chains, cudaStream_t s,
+                             int input = SFU_INPUT_PARITY);
 cudaError_t sfu_attributes(int op, bool control, int chains, cudaFuncAttributes* attr);
 const void* kernel_symbol(const char* name, int a, int b, int c);
 

@@ -82,6 +82,39 @@ def test_hbm_scalar_and_vector_reads(gpu_ready, policy):
         assert ref["checksum"] == scalar["checksum"]
 
 
+@pytest.mark.parametrize("vector", [False, True])
+def test_lcg_fill_read_sums(gpu_ready, vector):
+    """The seeded uint32 LCG payload (an extra mode): per-thread read sums equal the oracle's over
+    the stepped recurrence, and the engine's own CPU check passes."""
+    words, blocks, threads, stride, iters = (1 << 20) // 4, 8, 64, 3, 33
+    args = ["--workload", "hbm", "--fill", "lcg", "--blocks", blocks, "--threads", threads, "--working-set-bytes", 1 << 20,
+            "--seed", "11", "--iterations", iters, "--stride-words", stride, "--offset-bytes", "32", *QUICK]
+    r = result_of(powerbench.run(args + (["--memory-vector-bytes", "16"] if vector else [])))
+    assert r["memory_fill"] == "uint32_lcg_1664525_1013904223_v1"
+    assert r["memory_read_validation"]["status"] == "pass"
+    sums = W.read_sums_of(W.lcg_words(words + 8, 11), words, 8, blocks, threads, stride, iters, unit=4 if vector else 1)
+    assert r["checksum"] == W.sink_hash(sums[:512])
+    plain = result_of(powerbench.run(args[:2] + args[4:]))
+    assert plain["memory_fill"] == "random_word_xor_seed_v1" and plain["checksum"] != r["checksum"]
+
+
+@pytest.mark.parametrize("workload", ["sfu_ex2", "sfu_rsqrt", "sfu_tanh"])
+def test_sfu_uniform_input_mode(gpu_ready, workload):
+    """Operands uniform in [0.5, 2) with a per-thread XOR checksum (an extra mode): the one-step
+    checks pass on the new operands, the XOR fold is deterministic, and the record names the mode."""
+    args = ["--workload", workload, "--threads", "256", "--sfu-lanes", "8192", "--sfu-chains", "4", "--iterations", "64",
+            "--seed", "5", "--sfu-input", "uniform_0p5_2", *QUICK]
+    r = result_of(powerbench.run(args))
+    assert r["sanity"]["numerical_validation_passed"] is True and r["numerical_validation"]["checked_values"] == 16
+    assert r["sfu_input_policy"] == "thread_hash_uniform_0p5_2_then_feedback_xor_iteration_mantissa_0p5_1_v1"
+    assert r["checksum_kind"] == "distributed_per_lane_register_xor_sample"
+    again = result_of(powerbench.run(args))
+    assert isinstance(r["sfu_thread_xor_checksum"], int) and r["sfu_thread_xor_checksum"] == again["sfu_thread_xor_checksum"]
+    assert again["checksum"] == r["checksum"]
+    parity = result_of(powerbench.run(args[:-2]))
+    assert parity["sfu_thread_xor_checksum"] is None and parity["checksum"] != r["checksum"]
+
+
 @pytest.mark.parametrize("access,vector", [("copy", False), ("write", False), ("copy", True)])
 def test_write_copy_sinks(gpu_ready, access, vector):
     blocks, threads, stride, iters = 4, 64, 3, 7

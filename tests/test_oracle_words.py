@@ -65,3 +65,33 @@ def test_sfu_initial_operands_are_half_open_unit_mantissas():
             bits = W.lib().oracle_sfu_initial_bits(lane, 1, chain)
             x = np.frombuffer(np.uint32(bits).tobytes(), dtype=np.float32)[0]
             assert 0.5 <= x < 1.0
+
+
+def test_lcg_fill_is_the_seeded_recurrence():
+    for seed in (0, 11, 2 ** 40 + 5):
+        words = W.lcg_words(1000, seed)
+        x = seed & 0xFFFFFFFF
+        for i in range(1000):
+            assert int(words[i]) == x
+            x = (1664525 * x + 1013904223) & 0xFFFFFFFF
+
+
+def test_read_sums_over_an_explicit_payload_equal_the_random_word_sums():
+    payload = np.array([W.lib().oracle_random_word(i ^ 11) for i in range(4096 + 8)], dtype=np.uint32)
+    for unit in (1, 4):
+        a = W.read_sums(4096, 8, 11, 4, 32, 3, 17, unit=unit)
+        b = W.read_sums_of(payload, 4096, 8, 4, 32, 3, 17, unit=unit)
+        assert np.array_equal(a, b)
+
+
+def test_sfu_uniform_operands_lie_in_half_to_two():
+    seen = []
+    for lane in range(0, 20000, 7):
+        for chain in range(4):
+            bits = W.sfu_uniform_bits(lane, 3, chain)
+            x = np.frombuffer(np.uint32(bits).tobytes(), dtype=np.float32)[0]
+            m = W.lib().oracle_random_word(lane ^ 3 ^ ((chain + 1) * 0x9E3779B97F4A7C15 & MASK64)) >> 8
+            assert x == np.float32(np.float32(m) * np.float32(1.5 / 16777216.0)) + np.float32(0.5)
+            assert 0.5 <= x < 2.0
+            seen.append(x)
+    assert min(seen) < 0.52 and max(seen) > 1.98 and 0.3 < np.mean(np.array(seen) < 1.0) < 0.37

@@ -32,7 +32,31 @@ def lib():
     L.oracle_chase_terminal.argtypes = [p, u64, u64, u64, u64]
     L.oracle_sfu_initial_bits.restype = C.c_uint32
     L.oracle_sfu_initial_bits.argtypes = [u64, u64, C.c_int]
+    L.oracle_sfu_uniform_bits.restype = C.c_uint32
+    L.oracle_sfu_uniform_bits.argtypes = [u64, u64, C.c_int]
+    L.oracle_lcg_words.argtypes = [u64, u64, p]
+    L.oracle_read_sums_of.argtypes = [p] + [u64] * 8 + [p, u64]
     return L
+
+
+def lcg_words(n: int, seed: int) -> np.ndarray:
+    out = np.zeros(n, dtype=np.uint32)
+    lib().oracle_lcg_words(n, seed, out.ctypes.data)
+    return out
+
+
+def read_sums_of(payload: np.ndarray, words, offset_words, blocks, threads, stride, iterations, slice_words=0, unit=1,
+                 count=None):
+    count = blocks * threads if count is None else count
+    buf = np.ascontiguousarray(payload, dtype=np.uint32)
+    out = np.zeros(count, dtype=np.uint32)
+    lib().oracle_read_sums_of(buf.ctypes.data, words, offset_words, blocks, threads, stride, iterations, slice_words,
+                              unit, out.ctypes.data, count)
+    return out
+
+
+def sfu_uniform_bits(lane: int, seed: int, chain: int) -> int:
+    return int(lib().oracle_sfu_uniform_bits(lane, seed, chain))
 
 
 def sink_hash(words: np.ndarray) -> int:
