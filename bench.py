@@ -454,6 +454,7 @@ def run_b200(args, rank: int, world: int) -> dict | None:
     if peer:
         px.check()
         px.close()
+    fleet = run_fleet_arms(local, world, rank) if world > 1 and not args.no_arms else None
     c_h2d = in_bytes + offsets.nbytes + rows.nbytes + h_seeds.nbytes
     c_d2h = sum(a.nbytes for a in h_out.values()) + h_groups.nbytes
     # summarize uploads the packed trials, then the metric and memory-rail rows with the group
@@ -495,6 +496,8 @@ def run_b200(args, rank: int, world: int) -> dict | None:
         line["exchange"] = "nvlink-peer" if peer else "nccl"
         if exchange_note:
             line["exchange_note"] = exchange_note
+    if fleet:
+        line["arms_per_gpu"] = fleet
     if world == 1 and not args.no_cpu_baseline:
         line["cpu_baseline"] = cpu_baseline(records, policy)
     if not args.no_arms and world == 1:
@@ -744,6 +747,41 @@ def run_arms(local: int, peaks: dict, energy: bool = True) -> dict:
     return summary, detail
 
 
+def run_fleet_arms(local: int, world: int, rank: int) -> dict | None:
+    """Every rank runs the same arm on its own GPU at the same time, each with its own NVML
+    sampler bound to its GPU's UUID (powermodeling_b200.fleet.gpu_arm): HBM read, tcgen05 MMA and
+    SFU EX2.  Rank 0 gets the per-GPU rates and their sum."""
+    import torch.distributed as dist
+    from powermodeling_b200.fleet import gpu_arm
+    sms = 148
+    arms = {
+        "hbm_read_16B_cs_4GiB": (["--workload", "hbm", "--memory-vector-bytes", 16, "--read-cache-policy", "cs",
+                                   "--blocks", sms * 8, "--threads", 256, "--working-set-bytes", 4 << 30,
+                                   "--iterations", 885, "--batch-launches", 8, "--fixed-batches", 6, *ARM_QUICK],
+                                  "throughput_bytes_s", 1e9, "GB/s"),
+        "tcgen05_mma_2acc": (["--workload", "tensor", "--blocks", sms, "--threads", 128, "--iterations", 8192,
+                              "--tensor-accumulators", 2, "--batch-launches", 4, "--seconds", 2, "--warmup-seconds", 0,
+                              "--idle-seconds", 0, "--warmup-batches", 2], "throughput_ops_s", 1e12, "TFLOP/s"),
+        "sfu_ex2_148x8": (["--workload", "sfu_ex2", "--grid-mode", "fixed", "--blocks", sms * 8, "--threads", 256,
+                           "--sfu-lanes", sms * 8 * 256, "--sfu-chains", 4, "--iterations", 65536, "--batch-launches", 1,
+                           "--fixed-batches", 4, *ARM_QUICK], "throughput_ops_s", 1e12, "Tops/s"),
+    }
+    out = {}
+    for name, (args, key, scale, unit) in arms.items():
+        dist.barrier()                                  # every GPU starts the arm together
+        row = gpu_arm(local, args)
+        rows: list = [None] * world
+        dist.all_gather_object(rows, {"device": row["device"], "uuid": row["uuid"], "rate": row.get(key),
+                                      "sm_mhz": row.get("sm_mhz"), "power_w": row.get("power_w"),
+                                      "reasons": row.get("clock_event_reasons")})
+        rates = [r["rate"] / scale for r in rows if r["rate"] is not None]
+        out[name] = {"unit": unit, "sum": _sig(sum(rates)), "per_gpu": [_sig(v) for v in rates],
+                     "gpus_active": len(rates), "sm_mhz": [r["sm_mhz"] for r in rows],
+                     "power_w": [_sig(r["power_w"], 4) if r["power_w"] else None for r in rows],
+                     "reasons": sorted({x for r in rows for x in (r["reasons"] or [])})}
+    return out if rank == 0 else None
+
+
 NONLINEAR_ELEMENTS = 1 << 28          # 1 GiB of fp32 input, 1 GiB of output: far above the 126 MB L2
 NONLINEAR_ROW_WIDTH = 1024            # the reference's default row width
 
@@ -780,9 +818,9 @@ def run_nonlinear_arms(sms: int, peaks: dict) -> dict:
 # DRAM bytes read + written.  The kernels are deterministic for the fixed
 # seeds, so the counts are the same on every launch; None where not captured.
 NCU_PER_LAUNCH = {
-    "analyze_kernel": {"inst": None, "dram": 5_149_184},
-    "bootstrap_prepare_kernel": {"inst": None, "dram": None},
-    "bootstrap_kernel<0>": {"inst": None, "dram": 183_040},
+    "analyze_kernel": {"inst": 22_774_000, "dram": 5_092_352},
+    "bootstrap_prepare_kernel": {"inst": 11_400_512, "dram": 52_736},
+    "bootstrap_kernel<0>": {"inst": 752_751, "dram": 188_672},
 }
 # Blackwell SM: four schedulers, each issuing one warp instruction per clock.
 ISSUE_PER_SM_CLOCK = 4

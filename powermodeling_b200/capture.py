@@ -72,10 +72,14 @@ def phase_records(events: list, samples: list) -> dict[str, dict[str, Any]]:
 
 
 def capture_trial(args: list, device: NvmlDevice, sample_interval_s: float = 0.01,
-                  config: dict | None = None) -> dict[str, Any]:
-    """Runs powerbench ``args`` in this process under the native sampler; returns the trial record."""
+                  config: dict | None = None, trial_id: str | None = None) -> dict[str, Any]:
+    """Runs powerbench ``args`` in this process under the native sampler; returns the trial record.
+
+    ``status`` is "complete" when the capture raised no runner error, as the
+    reference's runner marks a trial (runner.py:476); ``trial_id`` is the
+    plan's id for the trial (analysis reports a trial without one)."""
     record: dict[str, Any] = {
-        "schema_version": 1, "status": "failed", "config": dict(config or {}),
+        "schema_version": 1, "trial_id": trial_id, "status": "failed", "config": dict(config or {}),
         "benchmark": {}, "active_reference": {}, "treatment_protocol": {}, "phases": {}, "samples": [],
         "events": [], "device": {}, "cuda_device": {}, "telemetry": {},
         "quality": {"valid": False, "benchmark_exit_code": None, "runner_errors": [],
@@ -120,6 +124,6 @@ def capture_trial(args: list, device: NvmlDevice, sample_interval_s: float = 0.0
         if key in bench and key not in record["config"]:
             record["config"][key] = bench[key]
     record["workload"] = bench.get("workload")
-    record["status"] = "ok" if not quality["runner_errors"] else "failed"
+    record["status"] = "complete" if not quality["runner_errors"] else "failed"
     quality["valid"] = not quality["runner_errors"]
     return record

@@ -216,7 +216,8 @@ def energy_arm(args: list, seconds: float = 10.0, idle: float = 6.0, warmup: flo
     device = NvmlDevice(uuid=describe()["uuid"])
     try:
         record = capture_trial([*map(str, args), "--seconds", seconds, "--warmup-seconds", warmup,
-                                "--idle-seconds", idle], device, sample_interval_s=0.01)
+                                "--idle-seconds", idle], device, sample_interval_s=0.01,
+                               trial_id=f"energy-{args[1]}-{int(time.time() * 1e3)}")
     finally:
         device.close()
     trial = analyze_trial(record)
