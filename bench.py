@@ -122,54 +122,53 @@ class ClockSampler:
                 "interval_ms": self.interval_ms}
 
 
-class NvmlPoller:
-    """SM clock, power and clock-event reasons read through NVML while the timed steps run.
-
-    The steps are enqueued ahead, so the launching thread is free while the
-    GPUs work: it polls every ~0.2 ms until the last step's event completes,
-    giving many samples inside a region of a few milliseconds (nvidia-smi's
-    loop yields one every 20 ms)."""
+class GpuClockWatch:
+    """This rank's GPU: SM clock and clock-event reasons read every 0.1 ms by a native thread
+    (telemetry.ClockWatch) while the timed steps run, so a region of a few milliseconds has
+    many clock records (nvidia-smi's loop gives one every 20 ms)."""
     REASONS = {0x8: "hw_slowdown", 0x40: "hw_thermal_slowdown", 0x20: "sw_thermal_slowdown", 0x4: "sw_power_cap"}
 
-    def __init__(self, indices):
-        self.nv, self.handles, self.rows = None, [], []
+    def __init__(self, local: int):
+        self.device = self.watch = None
         try:
-            import pynvml as nv
-            nv.nvmlInit()
-            self.nv = nv
-            self.handles = [nv.nvmlDeviceGetHandleByIndex(i) for i in indices]
-        except Exception:                                  # no NVML: the nvidia-smi record stands alone
-            self.nv = None
+            from powermodeling_b200 import powerbench
+            from powermodeling_b200.telemetry import ClockWatch, NvmlDevice
+            uuid = next(r for r in powerbench.run(["--describe", "--device", str(local)]) if r["type"] == "device")["uuid"]
+            self.device = NvmlDevice(uuid=uuid)
+            self.watch = ClockWatch(self.device, interval_s=1e-4)
+        except Exception:                               # no NVML here: the nvidia-smi record stands alone
+            self.device = self.watch = None
 
-    def poll_until(self, done) -> None:
-        if self.nv is None:
-            return
-        nv = self.nv
-        while True:
-            finished = done()
-            for h in self.handles:
-                try:
-                    self.rows.append((nv.nvmlDeviceGetClockInfo(h, nv.NVML_CLOCK_SM),
-                                      nv.nvmlDeviceGetCurrentClocksEventReasons(h)))
-                except Exception:
-                    pass
-            if finished:
-                return
-            time.sleep(0.0002)
+    def start(self):
+        if self.watch:
+            self.watch.start()
 
-    def summary(self) -> dict | None:
-        if self.nv is None:
+    def stop(self) -> dict | None:
+        if not self.watch:
             return None
         try:
-            self.nv.nvmlShutdown()
-        except Exception:
-            pass
-        if not self.rows:
+            t, mhz, bits = self.watch.stop()
+        finally:
+            self.device.close()
+        if not len(t):
             return None
-        sm = [r[0] for r in self.rows]
-        reasons = sorted({name for _, bits in self.rows for bit, name in self.REASONS.items() if bits & bit})
-        return {"sm_mhz": statistics.median(sm), "sm_mhz_min": min(sm), "reasons": reasons, "samples": len(self.rows),
-                "source": "NVML, polled every ~0.2 ms during the timed steps"}
+        union = 0
+        for b in set(bits.tolist()):
+            union |= int(b)
+        return {"sm_mhz": float(statistics.median(mhz.tolist())), "sm_mhz_min": int(mhz.min()), "samples": int(len(t)),
+                "reasons": sorted(name for bit, name in self.REASONS.items() if union & bit)}
+
+
+def merge_clock_records(records: list) -> dict | None:
+    """One clock record for all ranks: the median of the ranks' medians, the lowest clock seen,
+    every reason seen, and the samples counted over all GPUs."""
+    records = [r for r in records if r]
+    if not records:
+        return None
+    return {"sm_mhz": statistics.median(r["sm_mhz"] for r in records), "sm_mhz_min": min(r["sm_mhz_min"] for r in records),
+            "samples": sum(r["samples"] for r in records), "gpus": len(records),
+            "reasons": sorted({x for r in records for x in r["reasons"]}),
+            "source": "native NVML clock watch, every 0.1 ms on each GPU during the timed steps"}
 
 
 # --------------------------------------------------------------------------- workload
@@ -367,21 +366,27 @@ def run_b200(args, rank: int, world: int) -> dict | None:
     if world > 1:
         dist.barrier()
     torch.cuda.synchronize()
-    poller = NvmlPoller(range(world)) if rank == 0 else None
+    watch = GpuClockWatch(local)
+    watch.start()
     if clocks:
         clocks.mark_begin()
     evs, side_evs = run_steps(args.steps)
-    if poller:
-        poller.poll_until(evs[-1][4].query)
     torch.cuda.synchronize()
     if clocks:
         clocks.mark_end()
+    watched = watch.stop()
+    if world > 1:
+        everyone: list = [None] * world
+        dist.all_gather_object(everyone, watched)
+        watched = merge_clock_records(everyone)
+    else:
+        watched = merge_clock_records([watched])
     clock_info = clocks.stop() if clocks else None
-    if poller and (polled := poller.summary()):
+    if rank == 0 and watched:
         clock_info = dict(clock_info or {}, nvidia_smi_samples=(clock_info or {}).get("samples"),
-                          sm_mhz=polled["sm_mhz"], sm_mhz_min=polled["sm_mhz_min"],
-                          reasons=sorted(set(polled["reasons"]) | set((clock_info or {}).get("reasons") or [])),
-                          samples=polled["samples"], source=polled["source"])
+                          sm_mhz=watched["sm_mhz"], sm_mhz_min=watched["sm_mhz_min"],
+                          reasons=sorted(set(watched["reasons"]) | set((clock_info or {}).get("reasons") or [])),
+                          samples=watched["samples"], source=watched["source"])
     parts_ms = {"analyze": [], "join": [], "finish": [], "gather_groups": []}
     prepare_ms, step_ms = [], []
     for ev, side_ev in zip(evs, side_evs):

@@ -204,6 +204,17 @@ int pm_sampler_status(pm_sampler* sampler, int* reason, uint64_t* where, int* ru
 /* Frees the sampler; PM_E_STATE while its thread runs. */
 int pm_sampler_destroy(pm_sampler* sampler);
 
+/* A clock watch: a native thread that reads only the SM clock (MHz) and the
+ * clock-event reason bits every interval_s (the reference samples them inside
+ * its full reads, telemetry.py:195-243; this is the fast form for short timed
+ * regions).  The device counts it as an attached sampler until it stops.
+ * stop joins the thread, copies up to `capacity` records (any output may be
+ * NULL; codes[k] is the driver code of record k, 0 = read) and frees it. */
+typedef struct pm_clock_watch pm_clock_watch;
+int pm_clock_watch_start(pm_nvml_device* device, double interval_s, pm_clock_watch** out);
+int pm_clock_watch_stop(pm_clock_watch* watch, uint32_t* sm_mhz, uint64_t* reasons, double* t_s, int32_t* codes,
+                        uint64_t capacity, uint64_t* count);
+
 #ifdef __cplusplus
 }
 #endif

@@ -805,6 +805,74 @@ int pm_sampler_status(pm_sampler* s, int* reason, uint64_t* where, int* running)
   return PM_OK;
 }
 
+// A light clock watch: a native thread reads only the SM clock and the clock-event reasons
+// (two driver calls of a few microseconds, no energy counter or process lists), so that a timed
+// region of a few milliseconds still gets many clock records.
+struct pm_clock_watch {
+  pm_nvml_device* dev = nullptr;
+  std::thread thread;
+  std::atomic<bool> stop{false};
+  std::chrono::nanoseconds interval{100000};
+  std::vector<uint32_t> mhz;
+  std::vector<uint64_t> reasons;
+  std::vector<double> t;
+  std::vector<int> code;
+};
+
+int pm_clock_watch_start(pm_nvml_device* d, double interval_s, pm_clock_watch** out) {
+  if (!d || !out || !(interval_s > 0) || interval_s > 10) return fail(PM_E_INVALID, "pm_clock_watch_start: bad argument");
+  auto* w = new pm_clock_watch();
+  w->dev = d;
+  w->interval = std::chrono::nanoseconds(int64_t(interval_s * 1e9));
+  w->mhz.reserve(1 << 16);
+  w->reasons.reserve(1 << 16);
+  w->t.reserve(1 << 16);
+  w->code.reserve(1 << 16);
+  d->active_samplers.fetch_add(1);
+  w->thread = std::thread([w] {
+    const pm_nvml_backend& be = w->dev->be;
+    auto next = std::chrono::steady_clock::now();
+    while (!w->stop.load(std::memory_order_relaxed) && w->t.size() < (size_t(1) << 20)) {
+      uint64_t mhz = 0, bits = 0;
+      int rc = 0;
+      {
+        std::unique_lock<std::timed_mutex> guard(w->dev->lock, std::defer_lock);
+        if (!guard.try_lock_for(kLockWait)) break;
+        rc = be.clock(be.ctx, w->dev->handle, 1, &mhz);
+        if (!rc) rc = be.throttle_reasons(be.ctx, w->dev->handle, &bits);
+      }
+      timespec ts;
+      clock_gettime(CLOCK_MONOTONIC, &ts);
+      w->mhz.push_back(uint32_t(mhz));
+      w->reasons.push_back(bits);
+      w->t.push_back(double(ts.tv_sec) + ts.tv_nsec * 1e-9);
+      w->code.push_back(rc);
+      next += w->interval;
+      std::this_thread::sleep_until(next);
+    }
+  });
+  *out = w;
+  return PM_OK;
+}
+
+int pm_clock_watch_stop(pm_clock_watch* w, uint32_t* sm_mhz, uint64_t* reasons, double* t_s, int32_t* codes,
+                        uint64_t capacity, uint64_t* count) {
+  if (!w || !count) return fail(PM_E_INVALID, "pm_clock_watch_stop: bad argument");
+  w->stop.store(true);
+  if (w->thread.joinable()) w->thread.join();
+  w->dev->active_samplers.fetch_sub(1);
+  const uint64_t n = std::min<uint64_t>(w->t.size(), capacity);
+  for (uint64_t k = 0; k < n; ++k) {
+    if (sm_mhz) sm_mhz[k] = w->mhz[k];
+    if (reasons) reasons[k] = w->reasons[k];
+    if (t_s) t_s[k] = w->t[k];
+    if (codes) codes[k] = w->code[k];
+  }
+  *count = n;
+  delete w;
+  return PM_OK;
+}
+
 int pm_sampler_destroy(pm_sampler* s) {
   if (!s) return PM_OK;
   {

@@ -118,6 +118,8 @@ def _lib():
         "pm_sampler_copy": (C.c_int, [_vp, C.c_uint64, C.c_uint64, P(Sample), P(Process), C.c_uint64]),
         "pm_sampler_status": (C.c_int, [_vp, P(C.c_int), P(C.c_uint64), P(C.c_int)]),
         "pm_sampler_destroy": (C.c_int, [_vp]),
+        "pm_clock_watch_start": (C.c_int, [_vp, C.c_double, P(_vp)]),
+        "pm_clock_watch_stop": (C.c_int, [_vp, _vp, _vp, _vp, _vp, C.c_uint64, P(C.c_uint64)]),
     }
     for name, (res, args) in sig.items():
         fn = getattr(lib, name)
@@ -815,3 +817,38 @@ class Sampler:
                 _lib().pm_sampler_destroy(ptr)
             except Exception:  # noqa: BLE001 - interpreter shutdown
                 pass
+
+
+class ClockWatch:
+    """The SM clock and clock-event reasons read by a native thread every ``interval_s``
+    (pm_clock_watch_*): many records even inside a timed region of milliseconds.
+
+    ``stop()`` returns (t_s, sm_mhz, reason_bits) arrays of the successful reads."""
+
+    def __init__(self, device: "NvmlDevice", interval_s: float = 1e-4):
+        self.device, self.interval_s, self._ptr = device, interval_s, None
+
+    def start(self) -> "ClockWatch":
+        ptr = _vp()
+        rc = _lib().pm_clock_watch_start(self.device._handle, self.interval_s, C.byref(ptr))
+        if rc:
+            raise TelemetryError(f"pm_clock_watch_start failed ({rc}): {_last_error()}")
+        self._ptr = ptr
+        return self
+
+    def stop(self):
+        import numpy as np
+        if self._ptr is None:
+            raise TelemetryError("clock watch not started")
+        cap = 1 << 20
+        mhz, bits = np.zeros(cap, np.uint32), np.zeros(cap, np.uint64)
+        t, codes = np.zeros(cap, np.float64), np.zeros(cap, np.int32)
+        count = C.c_uint64()
+        rc = _lib().pm_clock_watch_stop(self._ptr, mhz.ctypes.data, bits.ctypes.data, t.ctypes.data, codes.ctypes.data,
+                                        cap, C.byref(count))
+        self._ptr = None
+        if rc:
+            raise TelemetryError(f"pm_clock_watch_stop failed ({rc}): {_last_error()}")
+        n = count.value
+        ok = codes[:n] == 0
+        return t[:n][ok], mhz[:n][ok], bits[:n][ok]

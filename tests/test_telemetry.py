@@ -337,3 +337,22 @@ def test_capture_without_a_gpu_keeps_samples_and_reports_failure():
     assert q["benchmark_exit_code"] == 1 and any("powerbench failed" in e for e in q["runner_errors"])
     assert record["status"] == "failed" and len(record["samples"]) >= 2
     assert record["device"]["name"] == "NVIDIA B200" and record["telemetry"]["power_w"]["available"]
+
+
+def test_clock_watch_reads_the_sm_clock_and_reasons_on_its_own_thread():
+    import time
+    from powermodeling_b200.telemetry import ClockWatch
+    from nvml_fake import FakeDriver
+    with NvmlDevice(nvml_module=FakeDriver()) as device:
+        watch = ClockWatch(device, interval_s=0.001).start()
+        try:
+            attached = device._active_samplers
+            time.sleep(0.05)
+        finally:
+            t, mhz, bits = watch.stop()
+        assert attached == 1 and device._active_samplers == 0
+        ref = device.read_sample()
+    assert 10 <= len(t) <= 80
+    assert (t[1:] > t[:-1]).all()
+    assert set(mhz.tolist()) == {ref["sm_clock_mhz"]}
+    assert set(bits.tolist()) == {ref["throttle_reasons"]}
