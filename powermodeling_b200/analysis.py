@@ -879,12 +879,55 @@ def finish_groups(groups: list, trials: list, members: list, group_indices: list
         group["paired_reference_order_effect_power_w"] = arm["AB"] - arm["BA"] if None not in arm.values() else None
 
 
+NOTES = ["No fabricated measurement or architecture-specific idle wattage is supplied.",
+         "A device power limit is not measured consumption, and headline FLOP/s is not achieved throughput.",
+         "Idle subtraction cannot separate physical static leakage from refresh/clock/background power.",
+         "L1/L2/HBM logical bytes are not guaranteed physical traffic; numeric profiler evidence is recomputed for target verification.",
+         "Verified selections require exact matching work/power windows; old records retain explicitly qualified stationary-rate estimates.",
+         "Uncontrolled default-clock trials are comparative and excluded from controlled-frequency optimum searches.",
+         "Each GPU UUID has its own empirically selected optimum; 1110 MHz is a mandatory supported sweep point, not a preset optimum.",
+         "Near-optimum and uncertainty-overlap sets contain only measured support points; no continuous interval or unmeasured gap is claimed."]
+"""The summary's notes (analysis.py:1547-1554), reported as the reference reports them."""
+
+
 def summary_record(trials: list, groups: list, duplicates: list, throughput_fraction: float,
-                   hbm_bandwidth_fraction: float, min_repeats: int, resamples: int) -> dict[str, Any]:
+                   hbm_bandwidth_fraction: float, min_repeats: int, resamples: int,
+                   policy: AnalysisPolicy | None = None) -> dict[str, Any]:
+    """The summary: trials, groups, and the selection sections over the groups (analysis.py:1500-1556)."""
+    from . import selections as S
+    policy = policy or AnalysisPolicy()
+    f, n = throughput_fraction, min_repeats
+    optima = lambda across, single: S.energy_optima(  # noqa: E731
+        groups, f, n, policy.near_optimum_fraction, policy.min_geometries, across_memory_domains=across,
+        single_geometry_exploratory=single)
     return {"schema_version": 2, "trials": trials, "groups": groups, "duplicate_trial_ids_ignored": duplicates,
-            "selection_policy": {"throughput_fraction": throughput_fraction, "hbm_bandwidth_fraction": hbm_bandwidth_fraction,
-                                 "min_repeats": min_repeats, "resamples": resamples,
-                                 "ci_method": f"deterministic percentile bootstrap of repeat medians ({resamples} draws)"}}
+            "within_clock_best": S.best_conditions(groups, f, n, False),
+            "cross_clock_best": S.best_conditions(groups, f, n, True),
+            "within_clock_best_total_energy": S.best_conditions(groups, f, n, False, total_energy=True),
+            "cross_clock_best_total_energy": S.best_conditions(groups, f, n, True, total_energy=True),
+            "uncontrolled_clock_exploratory_best": S.best_conditions(groups, f, n, True, exploratory_only=True),
+            "pareto_frontiers": S.pareto_frontiers(groups, n, False) + S.pareto_frontiers(groups, n, True),
+            "active_control_associations": S.control_associations(groups, n),
+            "verified_target_within_clock_best": S.best_conditions(groups, f, n, False, True),
+            "verified_target_cross_clock_best": S.best_conditions(groups, f, n, True, True),
+            "verified_target_coverage": S.verification_coverage(groups, f, n, False) + S.verification_coverage(groups, f, n, True),
+            "empirical_gpu_energy_optima": optima(False, False),
+            "empirical_gpu_overall_energy_optima": optima(True, False),
+            "exploratory_single_geometry_energy_optima": optima(False, True),
+            "exploratory_single_geometry_overall_energy_optima": optima(True, True),
+            "metric_aliases": {"pj_per_op": "legacy operational idle increment per reported benchmark operation; tensor FLOP uses explicit operational_idle_increment_pj_per_flop",
+                               "pj_per_logical_byte": "legacy operational idle increment per logical byte; divide by 8 for logical-bit metric",
+                               "incremental_power_w": "operational_idle_increment_power_w; a baseline contrast, not physical switching power"},
+            "selection_policy": {"throughput_fraction": f, "hbm_bandwidth_fraction": hbm_bandwidth_fraction,
+                                 "hbm_throughput_constraint": "all conditions with median sustained logical bandwidth >= the configured fraction of clock-specific DDR theory; every valid repeat needs complete measured memory-clock and CUDA bus-width evidence; observed 95% and plateaus are diagnostic only",
+                                 "min_repeats": n, "min_geometries": policy.min_geometries,
+                                 "near_optimum_fraction": policy.near_optimum_fraction,
+                                 "geometry_requirement": "at least min_geometries distinct verified execution-resource geometries per frequency; throughput peak still uses all valid groups; repeat/seed/footprint-only variants do not qualify; count alone is not saturation proof",
+                                 "primary_energy_objective": "whole-device total energy per logical bit, FLOP or nonlinear output element",
+                                 "frequency_utilization_constraint": "HBM: clock-specific theoretical bandwidth gate; other workloads: own-frequency complete measured geometry peak, with global-near-peak optima reported separately",
+                                 "baseline_objectives": "separate matched operational idle increment and paired active-reference contrast; never automatically substituted for total energy",
+                                 "ci_method": f"deterministic percentile bootstrap of repeat medians ({resamples} draws); n=3 intervals are coarse"},
+            "notes": list(NOTES)}
 
 
 def check_summary_arguments(throughput_fraction: float, min_repeats: int, hbm_bandwidth_fraction: float) -> float:
@@ -922,7 +965,7 @@ def _summarize(records, throughput_fraction, policy, min_repeats, hbm_bandwidth_
     med, lo, hi = bootstrap_groups(rows, members, seeds, resamples) if groups else (None, None, None)
     finish_groups(groups, trials, members, group_indices, med, lo, hi, hbm_bandwidth_fraction)
     return summary_record(trials, groups, duplicates, throughput_fraction, hbm_bandwidth_fraction, min_repeats,
-                          resamples)
+                          resamples, policy)
 
 
 # trials.csv columns (analysis.py:1565-1573), in the reference's order.

@@ -120,4 +120,4 @@ def summarize_sharded(records: Iterable[Mapping[str, Any]], throughput_fraction:
     med, lo, hi = _all_gather_groups(len(groups), width, mine, outputs, world, group)
     A.finish_groups(groups, trials, members, group_indices, med, lo, hi, hbm_bandwidth_fraction)
     return A.summary_record(trials, groups, duplicates, throughput_fraction, hbm_bandwidth_fraction, min_repeats,
-                            resamples)
+                            resamples, policy)

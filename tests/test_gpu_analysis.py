@@ -198,3 +198,30 @@ def test_trials_csv_matches_reference(gpu_ready, tmp_path, label, shape, seed):
             a = float(mine[col]) if mine[col] else None
             b = float(ref[col]) if ref[col] else None
             assert close(a, b, rel=REL), (mine["trial_id"], col, a, b)
+
+
+SELECTION_SECTIONS = ("within_clock_best", "cross_clock_best", "within_clock_best_total_energy",
+                      "cross_clock_best_total_energy", "uncontrolled_clock_exploratory_best", "pareto_frontiers",
+                      "active_control_associations", "verified_target_within_clock_best",
+                      "verified_target_cross_clock_best", "verified_target_coverage", "empirical_gpu_energy_optima",
+                      "empirical_gpu_overall_energy_optima", "exploratory_single_geometry_energy_optima",
+                      "exploratory_single_geometry_overall_energy_optima", "metric_aliases", "notes")
+
+
+def test_summary_selection_sections_match_reference(gpu_ready):
+    """summarize's selection sections over the GPU's groups equal the reference's summarize on the
+    same records (the summary-file fixture: a trapezoid sweep and an energy-counter sweep)."""
+    import json
+    from powermodeling_b200.analysis import summarize
+    from powermodeling_b200.synthetic import ANALYSIS_POLICY, SweepShape, make_sweep
+    shapes = {"trapezoid": (SweepShape(points=2, repeats=4), 21),
+              "counter": (SweepShape(points=2, repeats=3, with_energy_counter=True), 22)}
+    for case in load_golden("summary_files.json.gz"):
+        want = json.loads(case["files"]["summary.json"])
+        shape, seed = shapes[case["label"]]
+        got = json.loads(json.dumps(summarize(make_sweep(shape, seed), policy=ANALYSIS_POLICY)))
+        assert want["within_clock_best"], case["label"]          # the fixture selects something
+        for key in SELECTION_SECTIONS:
+            assert got[key] == want[key], (case["label"], key)
+        for key, value in want["selection_policy"].items():
+            assert got["selection_policy"][key] == value, key
