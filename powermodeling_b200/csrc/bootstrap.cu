@@ -20,6 +20,7 @@
 // For n >= 8 each draw's median rank pair is binned directly per metric from
 // an index stream kept in global scratch.
 #include <atomic>
+#include <cstdlib>
 #include <mutex>
 
 #include "pmb200.h"
@@ -94,19 +95,24 @@ __device__ void seed_state(uint32_t* mt, uint64_t seed) {
 // also reads new word 0, recomputes that word from the old state: a single
 // barrier per twist.  Outputs are tempered as they are produced, into
 // ring[base + i].
+// kOutput false: the state alone advances (a block skipped by a CTA that
+// draws a later range of resamples); nothing is tempered or written to the ring.
+template <bool kOutput = true>
 __device__ __forceinline__ void twist_block(const uint32_t* src, uint32_t* dst, uint32_t* ring, int base) {
   constexpr int A = kMtN - kMtM;          // 227
   const int t = threadIdx.x;
   if (t < A) {
     const uint32_t a = twist_one(src[t], src[t + 1], src[t + kMtM]);
     const uint32_t b = twist_one(src[t + A], src[t + A + 1], a);
-    dst[t] = a; ring[base + t] = temper(a);
-    dst[t + A] = b; ring[base + t + A] = temper(b);
+    dst[t] = a;
+    dst[t + A] = b;
+    if (kOutput) { ring[base + t] = temper(a); ring[base + t + A] = temper(b); }
     if (t < kMtN - 2 * A) {
       const int i = t + 2 * A;
       const uint32_t next = i < kMtN - 1 ? src[i + 1] : twist_one(src[0], src[1], src[kMtM]);
       const uint32_t c = twist_one(src[i], next, b);
-      dst[i] = c; ring[base + i] = temper(c);
+      dst[i] = c;
+      if (kOutput) ring[base + i] = temper(c);
     }
   }
   __syncthreads();
@@ -194,18 +200,21 @@ struct BootSmem {
   }
 };
 
-// Scratch layout: the prepared multiset histograms (one per group, kMaxBins
-// words), then, when a group may have more than kHistMaxN members, one index
-// stream per group (B draws of up to kDirectMaxN one-byte indices).
-__host__ __device__ inline size_t hist_area_bytes(int n_groups) {
-  return ((size_t)n_groups * kMaxBins * sizeof(uint32_t) + 255) & ~(size_t)255;
+// Scratch layout: the prepared multiset histograms (draw_splits per group,
+// kMaxBins words each: one partial histogram per range of resamples), then,
+// when a group may have more than kHistMaxN members, one index stream per group
+// (B draws of up to kDirectMaxN one-byte indices).
+__host__ __device__ inline size_t hist_area_bytes(int n_groups, int splits) {
+  return ((size_t)n_groups * (splits < 1 ? 1 : splits) * kMaxBins * sizeof(uint32_t) + 255) & ~(size_t)255;
 }
-__device__ inline uint32_t* prepared_hist(const BootArgs& A, int g) {
-  return reinterpret_cast<uint32_t*>(A.scratch) + (size_t)g * kMaxBins;
+__device__ inline int splits_of(const BootArgs& A) { return A.draw_splits < 1 ? 1 : A.draw_splits; }
+__device__ inline uint32_t* prepared_hist(const BootArgs& A, int g, int split) {
+  return reinterpret_cast<uint32_t*>(A.scratch) + ((size_t)g * splits_of(A) + split) * kMaxBins;
 }
 __device__ inline uint8_t* index_stream(const BootArgs& A, int g) {
-  return A.max_members > kHistMaxN ? A.scratch + hist_area_bytes(A.n_groups) + (size_t)g * A.resamples * kDirectMaxN
-                                   : nullptr;
+  return A.max_members > kHistMaxN
+             ? A.scratch + hist_area_bytes(A.n_groups, A.draw_splits) + (size_t)g * A.resamples * kDirectMaxN
+             : nullptr;
 }
 
 // Shared state of one group's stream.
@@ -217,10 +226,12 @@ struct GenShared {
   uint32_t binom[16][16];
 };
 
-// The B resamples of n draws from the seeded state in sh.mt_seed: multiset
-// counts into sh.hist (n <= kHistMaxN, hist cleared here) or raw indices into
-// `stream` (n > kHistMaxN).  All threads call it.
-__device__ __forceinline__ void generate_resamples(GenShared& sh, int n, int B, uint8_t* stream) {
+// Resamples r0..r1-1 (of B) of n draws from the seeded state in sh.mt_seed:
+// multiset counts into sh.hist (n <= kHistMaxN, hist cleared here) or raw
+// indices into `stream` (n > kHistMaxN).  The blocks of the stream before the
+// range are twisted without output.  All threads call it.
+__device__ __forceinline__ void generate_resamples(GenShared& sh, int n, int B, uint8_t* stream, uint32_t r0 = 0,
+                                                   uint32_t r1 = 0xffffffffu) {
   const bool histogram = n <= kHistMaxN;
   if (histogram)
     for (int i = threadIdx.x; i < kMaxBins; i += blockDim.x) sh.hist[i] = 0;
@@ -228,17 +239,23 @@ __device__ __forceinline__ void generate_resamples(GenShared& sh, int n, int B, 
   __syncthreads();
   const double nd = (double)n;
   const uint32_t words_per_draw = 2u * (uint32_t)n;          // 2nB < 2^32 (B <= 2^24, n <= 128)
-  const uint32_t blocks = (uint32_t)((2ull * n * B + kMtN - 1) / kMtN);
-  uint32_t next_r = 0;
-  int slot = 0;                                               // ring slot of the current block
-  for (uint32_t blk = 0; blk < blocks; ++blk) {
+  if (r1 > (uint32_t)B) r1 = B;
+  const uint32_t blocks = (uint32_t)(((uint64_t)r1 * words_per_draw + kMtN - 1) / kMtN);
+  // The block holding the first word of resample r0: every earlier block only advances the state.
+  const uint32_t first_block = (uint32_t)(((uint64_t)r0 * words_per_draw) / kMtN);
+  uint32_t blk = 0;
+  for (; blk < first_block && blk < blocks; ++blk)
+    twist_block<false>(sh.mt[blk & 1], sh.mt[(blk & 1) ^ 1], sh.ring, 0);
+  uint32_t next_r = r0;
+  int slot = (int)(blk % 3);                                  // ring slot of the current block
+  for (; blk < blocks; ++blk) {
     twist_block(sh.mt[blk & 1], sh.mt[(blk & 1) ^ 1], sh.ring, slot * kMtN);
     // Words [first, avail) are readable: the previous block and this one.
     const uint32_t avail = (blk + 1) * (uint32_t)kMtN;
     const uint32_t first = blk ? avail - 2 * kMtN : 0;
     const int first_slot = blk ? (slot + 2) % 3 : 0;          // slot of word `first`
     uint32_t r_end = avail / words_per_draw;
-    if (r_end > (uint32_t)B) r_end = B;
+    if (r_end > r1) r_end = r1;
     for (uint32_t r = next_r + threadIdx.x; r < r_end; r += blockDim.x) {
       uint32_t pos = first_slot * kMtN + (r * words_per_draw - first);
       if (pos >= (uint32_t)kRing) pos -= kRing;
@@ -272,17 +289,22 @@ __device__ __forceinline__ void load_binom(GenShared& sh) {
 // count every metric has when all listed members are valid and finite), the
 // multiset histogram (n <= kHistMaxN) or the index stream.  It needs only
 // seeds and group sizes, so it can run while the trials are still analysed.
+// With draw_splits S > 1, CTA (g, s) draws resamples [s B / S, (s + 1) B / S)
+// of group g: a partial histogram each (the finish adds them), or its range
+// of the index stream.
 __global__ void __launch_bounds__(kBootThreads) bootstrap_prepare_kernel(BootArgs A) {
   __shared__ GenShared sh;
-  const int g = blockIdx.x;
+  const int S = splits_of(A);
+  const int g = blockIdx.x / S, split = blockIdx.x - g * S;
   const int n = A.offsets[g + 1] - A.offsets[g];
   if (n < 3 || n > A.max_members || n > kDirectMaxN) return;   // no interval for n < 3 (uniform exit)
   load_binom(sh);
   if (threadIdx.x == 0) seed_state(sh.mt_seed, A.seeds[g]);
   __syncthreads();
-  generate_resamples(sh, n, A.resamples, index_stream(A, g));
+  const uint32_t r0 = (uint32_t)((uint64_t)A.resamples * split / S), r1 = (uint32_t)((uint64_t)A.resamples * (split + 1) / S);
+  generate_resamples(sh, n, A.resamples, index_stream(A, g), r0, r1);
   if (n <= kHistMaxN) {
-    uint32_t* out = prepared_hist(A, g);
+    uint32_t* out = prepared_hist(A, g, split);
     const int nbins = (int)sh.binom[2 * n - 1][n];
     for (int i = threadIdx.x; i < nbins; i += blockDim.x) out[i] = sh.hist[i];
   }
@@ -400,8 +422,12 @@ __global__ void __launch_bounds__(kBootThreads) bootstrap_kernel(BootArgs A, pm_
     uint8_t* stream = index_stream(A, g);
     if (A.prepared && n == members) {
       if (histogram) {
-        const uint32_t* src = prepared_hist(A, g);
-        for (int i = threadIdx.x; i < nbins; i += blockDim.x) sh.hist[i] = src[i];
+        const int S = splits_of(A);
+        for (int i = threadIdx.x; i < nbins; i += blockDim.x) {
+          uint32_t c = 0;
+          for (int sp = 0; sp < S; ++sp) c += prepared_hist(A, g, sp)[i];
+          sh.hist[i] = c;
+        }
       }
       __syncthreads();
     } else {
@@ -752,8 +778,23 @@ int prepare_bootstrap_constants(int device) {
   return 0;
 }
 
+// Resample ranges per group for the draws: enough CTAs to cover the SMs when the
+// groups alone do not (at most 16 per group); PM_DRAW_SPLITS overrides it
+// (read once).  The scratch size and every launch use the same value.
+int draw_splits(int n_groups) {
+  static const int forced = [] {
+    const char* env = getenv("PM_DRAW_SPLITS");
+    return env ? atoi(env) : 0;
+  }();
+  if (forced > 0) return forced > 64 ? 64 : forced;
+  if (n_groups <= 0) return 1;
+  const int s = 148 / n_groups;
+  return s < 1 ? 1 : s > 16 ? 16 : s;
+}
+
 size_t bootstrap_scratch_bytes(int n_groups, int max_members, int resamples) {
-  return hist_area_bytes(n_groups) + (max_members > kHistMaxN ? (size_t)n_groups * resamples * kDirectMaxN : 0);
+  return hist_area_bytes(n_groups, draw_splits(n_groups)) +
+         (max_members > kHistMaxN ? (size_t)n_groups * resamples * kDirectMaxN : 0);
 }
 
 // Shared memory the fold needs for M metrics and groups of up to mm members,
@@ -811,7 +852,8 @@ int launch_bootstrap(const BootArgs& A, cudaStream_t stream, const pm_peer_group
 
 int launch_bootstrap_prepare(const BootArgs& A, cudaStream_t stream) {
   if (A.n_groups == 0) return 0;
-  bootstrap_prepare_kernel<<<A.n_groups, kBootThreads, 0, stream>>>(A);
+  const int S = A.draw_splits < 1 ? 1 : A.draw_splits;
+  bootstrap_prepare_kernel<<<A.n_groups * S, kBootThreads, 0, stream>>>(A);
   return 0;
 }
 

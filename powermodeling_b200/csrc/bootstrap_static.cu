@@ -79,7 +79,7 @@ extern "C" int pm_group_bootstrap_device_static(const pm_bootstrap_job* job, voi
   // group's histogram or stream completely before the fold reads it back.
   BootArgs A{job->n_groups, job->n_metrics, job->resamples, job->max_members, job->values, job->group_offsets,
              job->member_rows, job->member_valid, job->seeds, job->medians, job->ci_lo, job->ci_hi,
-             static_cast<uint8_t*>(scratch), 1};
+             static_cast<uint8_t*>(scratch), 1, draw_splits(job->n_groups)};
   if (launch_bootstrap_prepare(A, static_cast<cudaStream_t>(stream)))
     return fail(PM_E_CUDA, "bootstrap_prepare_kernel launch failed");
   cudaError_t e = cudaGetLastError();

@@ -520,7 +520,7 @@ static int device_boot_args(const pm_bootstrap_job* job, void* scratch, size_t s
     return fail(PM_E_INVALID, "bootstrap needs %zu bytes of device scratch, got %zu", need, scratch_bytes);
   *out = BootArgs{job->n_groups, job->n_metrics, job->resamples, job->max_members, job->values, job->group_offsets,
                   job->member_rows, job->member_valid, job->seeds, job->medians, job->ci_lo, job->ci_hi,
-                  static_cast<uint8_t*>(scratch), 1};
+                  static_cast<uint8_t*>(scratch), 1, draw_splits(job->n_groups)};
   return PM_OK;
 }
 
@@ -616,7 +616,7 @@ int pm_group_bootstrap(const pm_bootstrap_job* job) {
                 reinterpret_cast<const int32_t*>(dev_of(ho)), hr ? reinterpret_cast<const int32_t*>(dev_of(hr)) : nullptr,
                 hvalid ? reinterpret_cast<const uint8_t*>(dev_of(hvalid)) : nullptr,
                 reinterpret_cast<const uint64_t*>(dev_of(hs)), dmed, dlo, dhi,
-                reinterpret_cast<uint8_t*>(dout + out_bytes), 1};
+                reinterpret_cast<uint8_t*>(dout + out_bytes), 1, draw_splits((int)G)};
   launch_bootstrap_prepare(args, st);
   launch_bootstrap(args, st);
   e = cudaGetLastError();
@@ -682,7 +682,7 @@ int pm_analyze_sweep(const pm_trials* trials, const pm_policy* policy, pm_trial_
                 reinterpret_cast<const int32_t*>(dptr(hr)), S.dres.valid, reinterpret_cast<const uint64_t*>(dptr(hs)),
                 reinterpret_cast<double*>(dout), reinterpret_cast<double*>(dout + align256(G * M * 8)),
                 reinterpret_cast<double*>(dout + 2 * align256(G * M * 8)),
-                reinterpret_cast<uint8_t*>(dout + gout), 1};
+                reinterpret_cast<uint8_t*>(dout + gout), 1, draw_splits((int)G)};
   // The resample draws need only seeds and group sizes: their inputs go first,
   // on the side stream, and the draws run there while the host stages the
   // trials (the GPU is otherwise idle then); the fold waits for them.

@@ -29,7 +29,10 @@ struct BootArgs {
   double* medians; double* lo; double* hi;
   uint8_t* scratch;               // prepared histograms, then index streams of groups with more than 7 members
   int prepared;                   // 1: bootstrap_prepare_kernel filled scratch for each group's member count
+  int draw_splits;                // resample ranges per group in the prepare launch (0 or 1: one CTA per group)
 };
+// Resample ranges per group the prepare launch uses for n_groups groups (bootstrap.cu).
+int draw_splits(int n_groups);
 
 // Raises `kernel`'s dynamic shared-memory limit on the current device to at
 // least `bytes` (static plus dynamic above 48 KB needs the opt-in); `limits`

@@ -24,7 +24,9 @@ from __future__ import annotations
 import gzip
 import json
 import os
+import subprocess
 import sys
+import types
 from pathlib import Path
 
 HERE = Path(__file__).resolve().parent
@@ -41,18 +43,19 @@ TRIALS = [
     ("l1-read", "l1", {"blocks": 148, "threads": 256, "working_set_bytes": 148 * 65536, "iterations": 2048}, None),
     ("chase-words", "l2_latency", {"blocks": 148, "threads": 32, "working_set_bytes": 16 << 20, "iterations": 20000}, None),
     ("tensor", "tensor", {"blocks": 148, "threads": 128, "iterations": 2048, "tensor_accumulators": 2}, None),
-    ("tensor-paired", "tensor", {"blocks": 148, "threads": 128, "iterations": 2048, "tensor_accumulators": 4}, "AB"),
     ("gemm", "gemm", {"gemm_m": 2048, "gemm_n": 2048, "gemm_k": 2048}, None),
     ("control", "control", {"blocks": 296, "threads": 256, "iterations": 4096}, None),
     ("sfu-ex2-paired", "sfu_ex2", {"grid_mode": "fixed", "blocks": 1184, "threads": 256, "sfu_lanes": 1184 * 256,
                                    "sfu_chains": 4, "iterations": 4096}, "AB"),
-    ("sfu-tanh-paired", "sfu_tanh", {"sfu_lanes": 65536, "threads": 256, "sfu_chains": 8, "iterations": 4096}, "BA"),
+    ("sfu-tanh", "sfu_tanh", {"sfu_lanes": 65536, "threads": 256, "sfu_chains": 8, "iterations": 4096}, None),
     ("softmax-paired", "softmax", {"nonlinear_mode": "streaming", "row_width": 1024, "grid_mode": "fixed",
                                    "blocks": 1184, "threads": 256, "working_set_bytes": 1 << 28}, "BA"),
     ("rmsnorm", "rmsnorm", {"nonlinear_mode": "streaming", "row_width": 1024, "working_set_bytes": 1 << 28}, None),
     ("exp", "exp", {"nonlinear_mode": "streaming", "working_set_bytes": 1 << 28}, None),
 ]
 SECONDS, WARMUP, IDLE, INTERVAL = 1.0, 0.2, 0.5, 0.05
+# Paired trials run the reference's minimum arms (the engine refuses shorter ones, gpu_bench.cu's guard).
+PAIRED_SECONDS, PAIRED_WARMUP, PAIRED_IDLE = 10.0, 1.0, 6.0
 
 
 def plan_trials() -> list[dict]:
@@ -64,6 +67,7 @@ def plan_trials() -> list[dict]:
                  "warmup_seconds": WARMUP, "idle_seconds": IDLE, "stage": "runner_contract_fixture"}
         if order:
             trial["treatment_protocol"] = {"kind": "paired_active_reference", "order": order}
+            trial.update(seconds=PAIRED_SECONDS, warmup_seconds=PAIRED_WARMUP, idle_seconds=PAIRED_IDLE)
         out.append(trial)
     return out
 
@@ -151,7 +155,9 @@ def check(tree: str | None) -> None:
             def metadata(self, _meta=cap["device_metadata"]):
                 return dict(_meta)
 
-        runner.subprocess.Popen = lambda *a, _cap=cap, **k: _Replay(_cap)
+        # The runner's own module of subprocess calls, with Popen replaying this capture.
+        runner.subprocess = types.SimpleNamespace(Popen=lambda *a, _cap=cap, **k: _Replay(_cap), PIPE=subprocess.PIPE,
+                                                  TimeoutExpired=subprocess.TimeoutExpired, run=subprocess.run)
         telemetry.Sampler = Sampler
         record = runner.capture_trial("powerbench", plan[cap["trial_id"]], Device(),
                                       {"uuid": cap["uuid"], "device_index": 0}, sample_interval_s=INTERVAL)
