@@ -172,11 +172,17 @@ def merge_clock_records(records: list) -> dict | None:
 
 
 # --------------------------------------------------------------------------- workload
-def build_workload(rank: int):
-    """Records, packed arrays and analyzed trials of one rank's 64-point shard of the sweep."""
+def build_workload(rank: int, world: int = 1, strong: bool = False):
+    """Records, packed arrays and analyzed trials of one rank's share of the sweep: its own 64 points
+    (weak scaling), or its slice of one 64-point sweep, whole points only (strong scaling)."""
     from powermodeling_b200 import analysis as A
     from powermodeling_b200.synthetic import ANALYSIS_POLICY, SweepShape, make_sweep
-    records = make_sweep(SweepShape(points=POINTS, repeats=REPEATS), seed=rank, first_point=rank * POINTS)
+    if strong:
+        lo, hi = rank * POINTS // world, (rank + 1) * POINTS // world
+        records = [r for r in make_sweep(SweepShape(points=POINTS, repeats=REPEATS), seed=0)
+                   if lo <= r["config"]["point"] < hi]
+    else:
+        records = make_sweep(SweepShape(points=POINTS, repeats=REPEATS), seed=rank, first_point=rank * POINTS)
     policy = A.AnalysisPolicy(**ANALYSIS_POLICY)
     packed, _, _ = A.prepare(records)
     trials = A.analyze_trials(records, policy)              # one untimed pass for the group keys
@@ -221,7 +227,8 @@ def run_b200(args, rank: int, world: int) -> dict | None:
     local = int(os.environ.get("LOCAL_RANK", "0"))
     torch.cuda.set_device(local)
     lib = N.library()
-    records, policy, packed, host_trials_list = build_workload(rank)
+    strong = args.scaling == "strong"
+    records, policy, packed, host_trials_list = build_workload(rank, world, strong)
     members, seeds = local_groups(host_trials_list)
     n, M, G = packed.n_trials, len(METRICS), len(members)
     per_rank = G
@@ -402,6 +409,11 @@ def run_b200(args, rank: int, world: int) -> dict | None:
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
         total_ms = float(t.item())
     ms_per_step = total_ms / args.steps
+    n_total, g_total = n * world, G * world
+    if world > 1:
+        sizes = torch.tensor([n, G], dtype=torch.int64, device="cuda")
+        dist.all_reduce(sizes)
+        n_total, g_total = int(sizes[0].item()), int(sizes[1].item())
     value = resamples_per_step / (ms_per_step / 1e3)
     t_analyze, t_finish = parts_ms["analyze"], parts_ms["finish"]
 
@@ -474,10 +486,13 @@ def run_b200(args, rank: int, world: int) -> dict | None:
     roofline = roofline_entry(a_ms, p_ms, f_ms, in_bytes, out_bytes, G, M, packed, peaks,
                               (clock_info or {}).get("sm_mhz"))
     line = {"metric": METRIC, "value": value, "unit": "resamples/s", "n_gpus": world, "steps": args.steps,
-            "warmup": args.warmup, "ms_per_step": ms_per_step, "higher_is_better": True, "scaling": "weak",
+            "warmup": args.warmup, "ms_per_step": ms_per_step, "higher_is_better": True, "scaling": args.scaling,
             "vs_baseline": None, "dtype": "f64", "data": "synthetic",
-            "config": {"workload": WORKLOAD, "points": POINTS * world, "points_per_gpu": POINTS, "repeats": REPEATS,
-                       "trials": n * world, "groups": G * world,
+            "config": {"workload": WORKLOAD if not strong else
+                       "analysis: one 64-point sweep split over the GPUs by points, 4 paired repeats, 3 s arms / 1 s idles at 10 ms, B=10000",
+                       "points": POINTS if strong else POINTS * world,
+                       "points_per_gpu": POINTS // world if strong else POINTS, "repeats": REPEATS,
+                       "trials": n_total, "groups": g_total,
                        "resamples": RESAMPLES, "samples": packed.n_samples, "l2": "flushed (256 MiB write) between steps",
                        "parallelism": (f"sweep-partitioned x{world}: each rank analyses its points and bootstraps their "
                                        f"groups; group results gathered on rank 0 " +
@@ -936,6 +951,8 @@ def main():
     parser.add_argument("--exchange", choices=("peer", "nccl"), default="peer",
                         help="N>1: group results stored into rank 0 by the bootstrap kernel over NVLink, or all-gathered by NCCL")
     parser.add_argument("--no-cpu-baseline", action="store_true")
+    parser.add_argument("--scaling", choices=("weak", "strong"), default="weak",
+                        help="weak: 64 points per GPU; strong: one 64-point sweep split over the GPUs by points")
     parser.add_argument("--no-arms", action="store_true", help="skip the HBM/tensor/GEMM/SFU arm measurements")
     parser.add_argument("--no-energy", action="store_true", help="skip the captured 10 s energy trials of the arms")
     parser.add_argument("--arms-detail", help="also write every arm row to this JSON file")

@@ -6,17 +6,16 @@ throughput bar (the reference's summarize sections ``within_clock_best`` ...
 ``exploratory_single_geometry_overall_energy_optima``, analysis.py:1104-1376,
 with the eligibility rules of evaluation.py:67-103 and hbm_bandwidth.py:128-143).
 
-The design here: every group is read once into a ``View`` (its workload
-family, the rate and energy fields that apply to it, its eligibility flags and
-its stratum keys); each section is then a filter over views, a bucketing by
-a stratum key and a choice within each bucket.  Record keys, strings and
-ordering are the reference's, since summary.json carries them.
+The design here: a workload family maps to the rate and energy fields it is
+judged on (``rate_field``, ``energy_field``, ``selection_field``); a section
+is a filter of the groups by eligibility predicates, a bucketing by a stratum
+key (``clock_stratum``) and a choice within each bucket.  Record keys,
+strings and ordering are the reference's, since summary.json carries them.
 """
 from __future__ import annotations
 
 import json
 import math
-from dataclasses import dataclass, field
 from typing import Any, Mapping
 
 TENSOR = {"tensor", "fp16_tensor", "tensor_fp16", "gemm"}

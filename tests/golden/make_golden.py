@@ -1,7 +1,7 @@
 """Generate the golden analysis fixtures from the reference implementation.
 
 Run in a checkout where the reference package is importable (read-only):
-    python tests/golden/make_golden.py /root/reference
+    python tests/golden/make_golden.py <reference checkout>      (or PM_REFERENCE_TREE=<reference checkout>)
 It imports powermodeling.analysis from that tree, runs the reference's own
 analyze_trial / summarize / _median_ci on inputs rebuilt deterministically
 by tests/trial_builders.py and powermodeling_b200.synthetic, and writes their
@@ -18,6 +18,7 @@ import json
 import math
 import random
 import statistics
+import os
 import sys
 from pathlib import Path
 
@@ -126,4 +127,7 @@ def main(reference: str) -> None:
 
 
 if __name__ == "__main__":
-    main(sys.argv[1] if len(sys.argv) > 1 else "/root/reference")
+    tree = sys.argv[1] if len(sys.argv) > 1 else os.environ.get("PM_REFERENCE_TREE")
+    if not tree:
+        sys.exit(f"usage: {Path(__file__).name} <reference checkout>  (or set PM_REFERENCE_TREE)")
+    main(tree)

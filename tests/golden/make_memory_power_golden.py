@@ -1,6 +1,6 @@
 """Generate the golden memory-rail sensor fixtures from the reference implementation.
 
-    python tests/golden/make_memory_power_golden.py /root/reference
+    python tests/golden/make_memory_power_golden.py <reference checkout>      (or PM_REFERENCE_TREE=<reference checkout>)
 
 Runs the reference's analyze_trial on tests/trial_builders.memory_rail_scenarios()
 and its summarize on memory_rail_group(), keeping each trial's
@@ -12,6 +12,7 @@ from __future__ import annotations
 
 import gzip
 import json
+import os
 import sys
 from pathlib import Path
 
@@ -50,4 +51,7 @@ def main(reference: str) -> None:
 
 
 if __name__ == "__main__":
-    main(sys.argv[1] if len(sys.argv) > 1 else "/root/reference")
+    tree = sys.argv[1] if len(sys.argv) > 1 else os.environ.get("PM_REFERENCE_TREE")
+    if not tree:
+        sys.exit(f"usage: {Path(__file__).name} <reference checkout>  (or set PM_REFERENCE_TREE)")
+    main(tree)

@@ -1,6 +1,6 @@
 """Generate the nonlinear count-contract fixture from the reference implementation.
 
-    python tests/golden/make_nonlinear_golden.py /root/reference
+    python tests/golden/make_nonlinear_golden.py <reference checkout>      (or PM_REFERENCE_TREE=<reference checkout>)
 
 Runs the reference's powermodeling.nonlinear.count_issues (nonlinear.py:22-128)
 on every record of tests/nonlinear_cases.cases() and writes the issue lists,
@@ -11,6 +11,7 @@ from __future__ import annotations
 import gzip
 import hashlib
 import json
+import os
 import sys
 from pathlib import Path
 
@@ -35,4 +36,7 @@ def main(reference: str) -> None:
 
 
 if __name__ == "__main__":
-    main(sys.argv[1] if len(sys.argv) > 1 else "/root/reference")
+    tree = sys.argv[1] if len(sys.argv) > 1 else os.environ.get("PM_REFERENCE_TREE")
+    if not tree:
+        sys.exit(f"usage: {Path(__file__).name} <reference checkout>  (or set PM_REFERENCE_TREE)")
+    main(tree)

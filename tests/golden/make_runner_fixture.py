@@ -15,7 +15,9 @@ Three steps, each writing a committed fixture:
         (runner.py:331-480: one result, protocol and device per trial, UUID
         match, ordered phases, paired-protocol checks, exclusivity) with its
         subprocess and sampler replaced by the stored stdout and samples, and
-        runs sfu/memory/nonlinear.count_issues -> tests/golden/runner_checks.json.gz
+        runs sfu/memory/nonlinear.count_issues -> tests/golden/runner_checks.json.gz;
+        keeps the runner's records with the reference's analyze_trial of each
+        and its summarize over all of them -> tests/golden/runner_records.json.gz
 
 PM_REFERENCE_TREE may name the reference checkout instead of the argument.
 """
@@ -133,11 +135,11 @@ def check(tree: str | None) -> None:
     _reference(tree)
     import powermodeling.runner as runner
     import powermodeling.telemetry as telemetry
-    from powermodeling import memory, nonlinear, sfu
+    from powermodeling import analysis, memory, nonlinear, sfu
     plan = {e["trial"]["trial_id"]: e["trial"] for e in json.loads((HERE / "runner_plan.json").read_text())}
     with gzip.open(HERE / "runner_captures.json.gz", "rt") as f:
         captures = json.load(f)
-    results = []
+    results, records = [], []
     for cap in captures:
         class Sampler:
             def __init__(self, device, interval_s=0.05):
@@ -171,9 +173,16 @@ def check(tree: str | None) -> None:
                         "sfu_reference": sfu.count_issues(reference, workload, reference=True) if reference else [],
                         "memory": memory.count_issues(bench, workload),
                         "nonlinear": nonlinear.count_issues(bench, workload)})
+        records.append(json.loads(json.dumps(record)))
         print(cap["trial_id"], record["status"], record["quality"]["runner_errors"])
     with gzip.open(HERE / "runner_checks.json.gz", "wt") as f:
         json.dump(results, f, indent=0, sort_keys=True)
+    # JSON round trips: NaN and infinities travel as the json module writes them.
+    analysed = [json.loads(json.dumps(analysis.analyze_trial(r))) for r in records]
+    summary = json.loads(json.dumps(analysis.summarize(records)))
+    with gzip.open(HERE / "runner_records.json.gz", "wt") as f:
+        json.dump({"records": records, "trials": analysed, "groups": summary["groups"]}, f)
+    print(sum(t["valid"] for t in analysed), "of", len(analysed), "trials valid;", len(summary["groups"]), "groups")
 
 
 if __name__ == "__main__":

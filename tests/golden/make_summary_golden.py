@@ -1,6 +1,6 @@
 """Generate the summary-file fixture from the reference implementation.
 
-    python tests/golden/make_summary_golden.py /root/reference
+    python tests/golden/make_summary_golden.py <reference checkout>      (or PM_REFERENCE_TREE=<reference checkout>)
 
 Runs the reference's summarize on two small synthetic sweeps (its evaluation
 entry removed: the report files are out of scope), round-trips each summary
@@ -12,6 +12,7 @@ from __future__ import annotations
 
 import gzip
 import json
+import os
 import sys
 import tempfile
 from pathlib import Path
@@ -40,4 +41,7 @@ def main(reference: str) -> None:
 
 
 if __name__ == "__main__":
-    main(sys.argv[1] if len(sys.argv) > 1 else "/root/reference")
+    tree = sys.argv[1] if len(sys.argv) > 1 else os.environ.get("PM_REFERENCE_TREE")
+    if not tree:
+        sys.exit(f"usage: {Path(__file__).name} <reference checkout>  (or set PM_REFERENCE_TREE)")
+    main(tree)

@@ -1,6 +1,6 @@
 """Generate the golden telemetry fixtures from the reference implementation.
 
-    python tests/golden/make_telemetry_golden.py /root/reference
+    python tests/golden/make_telemetry_golden.py <reference checkout>      (or PM_REFERENCE_TREE=<reference checkout>)
 
 Runs the reference's NvmlDevice (powermodeling/telemetry.py) on every fake
 driver scenario of tests/nvml_fake.py — read_sample repeated as the scenario
@@ -14,6 +14,7 @@ from __future__ import annotations
 import gzip
 import json
 import math
+import os
 import sys
 from pathlib import Path
 
@@ -78,4 +79,7 @@ def main(reference: str) -> None:
 
 
 if __name__ == "__main__":
-    main(sys.argv[1] if len(sys.argv) > 1 else "/root/reference")
+    tree = sys.argv[1] if len(sys.argv) > 1 else os.environ.get("PM_REFERENCE_TREE")
+    if not tree:
+        sys.exit(f"usage: {Path(__file__).name} <reference checkout>  (or set PM_REFERENCE_TREE)")
+    main(tree)
