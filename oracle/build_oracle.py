@@ -18,7 +18,6 @@ from pathlib import Path
 
 HERE = Path(__file__).resolve().parent
 REF_OUT = HERE / "_ref"
-REFERENCE = Path(os.environ.get("PM_REFERENCE_TREE", "/root/reference"))
 
 
 def _run(cmd: list[str]) -> None:
@@ -41,13 +40,17 @@ def build_words() -> Path | None:
     return target
 
 
-def build_reference() -> Path | None:
-    source = REFERENCE / "cuda" / "gpu_bench.cu"
+def build_reference(tree: str | os.PathLike | None) -> Path | None:
+    """``tree``: the reference checkout (None: nothing to build)."""
+    if not tree:
+        return None
+    reference = Path(tree)
+    source = reference / "cuda" / "gpu_bench.cu"
     if not source.exists():
         return None
     REF_OUT.mkdir(exist_ok=True)
     target = REF_OUT / "powerbench_ref"
-    headers = [REFERENCE / "cuda" / h for h in ("sfu.cuh", "nonlinear.cuh", "memory_read_math.cuh")]
+    headers = [reference / "cuda" / h for h in ("sfu.cuh", "nonlinear.cuh", "memory_read_math.cuh")]
     if _stale(target, [source, *[h for h in headers if h.exists()]]):
         nvcc = shutil.which("nvcc") or "/usr/local/cuda/bin/nvcc"
         _run([nvcc, "-std=c++17", "-O3", "--expt-relaxed-constexpr", "-gencode", "arch=compute_100a,code=sm_100a",
@@ -55,11 +58,13 @@ def build_reference() -> Path | None:
     return target
 
 
-def build() -> None:
+def build(tree: str | os.PathLike | None = None) -> None:
+    """The word oracle always; the reference binary when ``tree`` (or PM_REFERENCE_TREE) names a checkout."""
     build_words()
-    build_reference()
+    build_reference(tree or os.environ.get("PM_REFERENCE_TREE"))
 
 
 if __name__ == "__main__":
-    build()
+    import sys
+    build(sys.argv[1] if len(sys.argv) > 1 else None)
     print("oracle built")

@@ -900,6 +900,11 @@ def summary_record(trials: list, groups: list, duplicates: list, throughput_frac
     optima = lambda across, single: S.energy_optima(  # noqa: E731
         groups, f, n, policy.near_optimum_fraction, policy.min_geometries, across_memory_domains=across,
         single_geometry_exploratory=single)
+    with S.stratum_memo():
+        return _summary_sections(S, trials, groups, duplicates, f, n, optima, hbm_bandwidth_fraction, policy, resamples)
+
+
+def _summary_sections(S, trials, groups, duplicates, f, n, optima, hbm_bandwidth_fraction, policy, resamples):
     return {"schema_version": 2, "trials": trials, "groups": groups, "duplicate_trial_ids_ignored": duplicates,
             "within_clock_best": S.best_conditions(groups, f, n, False),
             "cross_clock_best": S.best_conditions(groups, f, n, True),

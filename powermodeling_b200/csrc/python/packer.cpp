@@ -18,6 +18,7 @@
 // of the host code sees exactly what the Python packer produced.
 #define PY_SSIZE_T_CLEAN
 #include <Python.h>
+#include <sched.h>
 
 #include <algorithm>
 #include <atomic>
@@ -522,10 +523,15 @@ bool fill_slot(SlotPlan& plan, PyObject* pid, KeyCache& cache, const OutColumns&
 // Slots the last pack() call packed on the fast path (for tests and diagnostics).
 Py_ssize_t g_last_fast_slots = 0;
 
+// Worker threads: PM_PACK_THREADS, else the CPUs this process may run on (its
+// affinity mask, which a launcher that pins one process per GPU narrows), at most 8.
 int pack_threads() {
   static const int n = [] {
     const char* env = getenv("PM_PACK_THREADS");
-    int v = env ? atoi(env) : (int)std::min(8u, std::max(1u, std::thread::hardware_concurrency()));
+    cpu_set_t set;
+    int cpus = sched_getaffinity(0, sizeof(set), &set) == 0 ? CPU_COUNT(&set)
+                                                           : (int)std::thread::hardware_concurrency();
+    int v = env ? atoi(env) : std::min(8, std::max(1, cpus));
     return std::max(1, std::min(v, 64));
   }();
   return n;

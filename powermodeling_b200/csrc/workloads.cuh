@@ -45,7 +45,7 @@ __host__ __device__ __forceinline__ uint32_t lcg_word(uint64_t i, uint64_t seed)
 }
 enum WordFill { FILL_RANDOM_WORD = 0, FILL_LCG = 1 };
 
-// The SFU arm's input in BASELINE mode (an extra mode beside the reference's
+// The SFU arm's uniform input mode (an extra mode beside the reference's
 // [0.5, 1) operand): uniform in [0.5, 2.0) from the thread-index hash,
 // 0.5 + 1.5 m / 2^24 for the top 24 bits m of the hash, in two separately
 // rounded float operations.

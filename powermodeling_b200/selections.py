@@ -216,6 +216,37 @@ def _key(stratum: Mapping) -> str:
     return json.dumps(stratum, sort_keys=True)
 
 
+# Within ``stratum_memo()``, each group's stratum and key are computed once per
+# comparison scope (the summary evaluates a dozen sections over the same groups).
+_MEMO: dict | None = None
+
+
+class stratum_memo:
+    """Context in which stratum_of caches by group identity (the groups must outlive it)."""
+
+    def __enter__(self):
+        global _MEMO
+        self.outer, _MEMO = _MEMO, {}
+        return self
+
+    def __exit__(self, *exc):
+        global _MEMO
+        _MEMO = self.outer
+
+
+def stratum_of(group: Mapping, cross_clock: bool) -> tuple[str, dict]:
+    """(key string, stratum) of clock_stratum(group, cross_clock)."""
+    if _MEMO is None:
+        stratum = clock_stratum(group, cross_clock)
+        return _key(stratum), stratum
+    slot = (id(group), cross_clock)
+    hit = _MEMO.get(slot)
+    if hit is None:
+        stratum = clock_stratum(group, cross_clock)
+        hit = _MEMO[slot] = (_key(stratum), stratum)
+    return hit
+
+
 def _bucket(items, key_of) -> list[tuple[str, list]]:
     buckets: dict[str, list] = {}
     for item in items:
@@ -247,7 +278,7 @@ def best_conditions(groups: list, fraction: float, min_repeats: int, cross_clock
     valid sweep's, so an incomplete verified subset cannot lower the bar."""
     chosen = [g for g in groups if _selectable(g, min_repeats, verified_only, total_energy, exploratory_only)]
     out = []
-    for key, candidates in _bucket(chosen, lambda g: _key(clock_stratum(g, cross_clock))):
+    for key, candidates in _bucket(chosen, lambda g: stratum_of(g, cross_clock)[0]):
         first = candidates[0]
         metric, rate = selection_field(first["workload"], total_energy), rate_field(first["workload"])
         stratum = json.loads(key)
@@ -256,7 +287,7 @@ def best_conditions(groups: list, fraction: float, min_repeats: int, cross_clock
                       if g["workload"] == first["workload"] and peak_population_eligible(g)
                       and g["gpu_uuid"] == first["gpu_uuid"] and g["valid_repeats"] >= min_repeats
                       and g["clock_comparison_controlled"] == first["clock_comparison_controlled"]
-                      and clock_stratum(g, cross_clock) == stratum and g.get(rate) is not None]
+                      and stratum_of(g, cross_clock)[1] == stratum and g.get(rate) is not None]
         sweep_max = max(population) if population else candidate_max
         bar = sweep_max if verified_only else candidate_max
         passing = [g for g in candidates if meets_bar(g, rate, bar, fraction)]
@@ -288,7 +319,7 @@ def verification_coverage(groups: list, fraction: float, min_repeats: int, cross
     """Per stratum, how much of the valid sweep's peak the profiler-verified groups reach."""
     valid = [g for g in groups if _controlled_population(g, min_repeats) and (g.get(rate_field(g["workload"])) or 0) > 0]
     out = []
-    for key, candidates in _bucket(valid, lambda g: _key(clock_stratum(g, cross_clock))):
+    for key, candidates in _bucket(valid, lambda g: stratum_of(g, cross_clock)[0]):
         rate = rate_field(candidates[0]["workload"])
         peak = max(g[rate] for g in candidates)
         verified = [g for g in candidates if g["verified_selection_eligible"]]
@@ -316,7 +347,7 @@ def pareto_frontiers(groups: list, min_repeats: int, cross_clock: bool) -> list[
              and g["clock_comparison_controlled"] and g.get("board_power_w") is not None
              and g.get(rate_field(g["workload"])) is not None]
     out = []
-    for key, candidates in _bucket(valid, lambda g: _key(clock_stratum(g, cross_clock))):
+    for key, candidates in _bucket(valid, lambda g: stratum_of(g, cross_clock)[0]):
         rate = rate_field(candidates[0]["workload"])
 
         def dominated(g):
@@ -377,7 +408,7 @@ def energy_optima(groups: list, fraction: float, min_repeats: int, near_fraction
     (analysis.py:1181-1298).  Every support point is a measured group; nothing is interpolated."""
     population = [g for g in groups if g["workload"] in ENERGY and peak_population_eligible(g)
                   and g["valid_repeats"] >= min_repeats and g["clock_comparison_controlled"]]
-    own_clock = lambda g: _key(clock_stratum(g, False))  # noqa: E731
+    own_clock = lambda g: stratum_of(g, False)[0]  # noqa: E731
     peaks: dict[str, float] = {}
     shapes: dict[str, set] = {}
     verified_shapes: dict[str, set] = {}
@@ -412,7 +443,7 @@ def energy_optima(groups: list, fraction: float, min_repeats: int, near_fraction
             metric = energy_field(g["workload"], prefix)
             if _positive(g.get(metric)) is None:
                 continue
-            stratum = clock_stratum(g, True)
+            stratum = dict(stratum_of(g, True)[1])
             if not across_memory_domains:
                 stratum["memory_clock_mhz"] = g["config"].get("memory_clock_mhz")
             stratum["objective"] = objective
@@ -441,7 +472,7 @@ def _optimum(key, candidates, shapes, verified_shapes, population, fraction, nea
     evidence = "single_geometry_reference_only" if single else "multiple_resource_geometries_compared"
 
     def counts(g) -> dict[str, int]:
-        clock = _key(clock_stratum(g, False))
+        clock = stratum_of(g, False)[0]
         verified = len(verified_shapes.get(clock, set()))
         return {"own_clock_distinct_geometry_count": verified, "own_clock_verified_distinct_geometry_count": verified,
                 "own_clock_observed_distinct_geometry_count": len(shapes.get(clock, set()))}
@@ -468,7 +499,7 @@ def _optimum(key, candidates, shapes, verified_shapes, population, fraction, nea
                and c[0]["ci95"][metric][0] <= best_ci[1] and c[0]["ci95"][metric][1] >= best_ci[0]]
     stratum = json.loads(key)
     base = {k: v for k, v in stratum.items() if k not in ("objective", "memory_clock_mhz")}
-    comparable = [p for p in population if clock_stratum(p, True) == base
+    comparable = [p for p in population if stratum_of(p, True)[1] == base
                   and (across or p["config"].get("memory_clock_mhz") == stratum["memory_clock_mhz"])]
     observed = sorted({(p["config"].get("graphics_clock_mhz"), p["config"].get("memory_clock_mhz")) for p in comparable})
     eligible = sorted({(c[0]["config"].get("graphics_clock_mhz"), c[0]["config"].get("memory_clock_mhz")) for c in candidates})

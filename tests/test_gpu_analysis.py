@@ -13,7 +13,7 @@ from tests.golden.make_golden import TRIAL_KEYS, PHASE_KEYS, records_digest
 
 pytestmark = pytest.mark.gpu
 
-# Floating tolerance of the north star: 1e-6 relative for energies and pJ/op.
+# Floating tolerance: 1e-6 relative for energies and pJ/op.
 REL = 1e-6
 EXACT_KEYS = ("total_energy_j", "integrated_power_energy_j", "energy_counter_j", "board_power_w", "idle_power_w",
               "incremental_energy_j", "pj_per_op", "throughput_ops_s", "paired_active_reference_power_w")

@@ -31,9 +31,14 @@ def ours(groups: list) -> dict:
     return json.loads(json.dumps(out))
 
 
+@pytest.mark.parametrize("memo", [False, True], ids=["direct", "memo"])
 @pytest.mark.parametrize("case", CASES, ids=[str(c["seed"]) for c in CASES])
-def test_sections_match_reference(case):
-    got = ours(case["groups"])
+def test_sections_match_reference(case, memo):
+    if memo:                      # the summary evaluates its sections with strata cached per group
+        with S.stratum_memo():
+            got = ours(case["groups"])
+    else:
+        got = ours(case["groups"])
     assert got.keys() == case["sections"].keys()
     for key, want in case["sections"].items():
         assert got[key] == want, key
