@@ -140,10 +140,14 @@ class GpuClockWatch:
             self.device = self.watch = None
 
     def start(self):
+        """Started ahead of the timed steps: the thread's first reads of a newly opened device
+        take milliseconds, longer than a short timed region."""
         if self.watch:
             self.watch.start()
 
-    def stop(self) -> dict | None:
+    def stop(self, begin: float, end: float) -> dict | None:
+        """The records read between ``begin`` and ``end`` (time.monotonic(), the watch's clock);
+        the one nearest the region when none falls inside it."""
         if not self.watch:
             return None
         try:
@@ -152,6 +156,12 @@ class GpuClockWatch:
             self.device.close()
         if not len(t):
             return None
+        inside = (t >= begin) & (t <= end)
+        if inside.any():
+            t, mhz, bits = t[inside], mhz[inside], bits[inside]
+        else:
+            nearest = int(np.argmin(np.minimum(np.abs(t - begin), np.abs(t - end))))
+            t, mhz, bits = t[nearest:nearest + 1], mhz[nearest:nearest + 1], bits[nearest:nearest + 1]
         union = 0
         for b in set(bits.tolist()):
             union |= int(b)
@@ -370,18 +380,20 @@ def run_b200(args, rank: int, world: int) -> dict | None:
     clocks = ClockSampler(",".join(str(i) for i in range(world))) if rank == 0 else None
     if clocks:
         clocks.start()
+    watch = GpuClockWatch(local)
+    watch.start()
     if world > 1:
         dist.barrier()
     torch.cuda.synchronize()
-    watch = GpuClockWatch(local)
-    watch.start()
     if clocks:
         clocks.mark_begin()
+    begin = time.monotonic()
     evs, side_evs = run_steps(args.steps)
     torch.cuda.synchronize()
+    end = time.monotonic()
     if clocks:
         clocks.mark_end()
-    watched = watch.stop()
+    watched = watch.stop(begin, end)
     if world > 1:
         everyone: list = [None] * world
         dist.all_gather_object(everyone, watched)

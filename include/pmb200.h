@@ -219,8 +219,12 @@ typedef struct {
 } pm_bootstrap_job;
 
 int pm_group_bootstrap(const pm_bootstrap_job* job);
-/* Device scratch: one prepared multiset histogram per group, plus index
- * streams (resamples x 128 bytes per group) when max_members > 7. */
+/* Device scratch: one prepared multiset histogram per group (6864 bytes)
+ * plus every group's index stream (resamples x max_members bytes per group).
+ * The _device entry points also accept a scratch without the streams of
+ * groups of up to seven members (only the histograms, and the streams when
+ * max_members > 7): the prepare pass then consumes the draws as it generates
+ * them, which takes several times longer. */
 size_t pm_bootstrap_scratch_bytes(int32_t n_groups, int32_t max_members, int32_t resamples);
 /* Device buffers, stream-ordered: pm_bootstrap_prepare_device then
  * pm_bootstrap_finish_device, or both at once. */
@@ -281,12 +285,14 @@ int pm_gemm_probe(int m, int n, int k, int uniform, uint64_t seed, float* out, u
  * (a process whose own pool owns the whole device, a runtime that forbids
  * foreign allocations, a service that must fix the library's footprint in
  * advance).  No counterpart in the reference.  It calls no cudaMalloc,
- * cudaFree or allocating library routine: the index streams of groups with
- * more than seven members live in one fixed array inside this library, of
+ * cudaFree or allocating library routine: the prepared histograms and index
+ * streams live in one fixed array inside this library, of
  * pm_bootstrap_static_scratch_capacity() bytes (32 MiB), which every GPU that
- * loads the library holds until the process exits.  A job needing more
- * (n_groups x resamples x 128 bytes when max_members > 7) is rejected with
- * PM_E_LIMIT.  Inputs and outputs are the caller's device buffers, as for
+ * loads the library holds until the process exits.  Every group's stream is
+ * kept while they fit; beyond that, groups of up to seven members are drawn
+ * without one.  A job needing more than the array even then (n_groups x 6864
+ * bytes, plus n_groups x resamples x max_members bytes when max_members > 7)
+ * is rejected with PM_E_LIMIT.  Inputs and outputs are the caller's device buffers, as for
  * pm_group_bootstrap_device; job->max_members must bound every group.
  * The first call on a device looks up the array's device address and uploads
  * the generator constants; make that first call before any stream capture.

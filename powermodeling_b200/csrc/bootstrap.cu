@@ -32,6 +32,7 @@
 namespace pm {
 
 constexpr int kBootThreads = 256;
+constexpr int kPrepThreads = 320;       // the prepare pass: one thread per word pair of a block (312)
 constexpr int kMtN = 624, kMtM = 397;
 constexpr int kHistMaxN = 7;            // multiset histogram path
 constexpr int kMaxBins = 1716;          // C(13, 7)
@@ -94,10 +95,9 @@ __device__ void seed_state(uint32_t* mt, uint64_t seed) {
 // every new operand in its own registers, and the last word (623), which
 // also reads new word 0, recomputes that word from the old state: a single
 // barrier per twist.  Outputs are tempered as they are produced, into
-// ring[base + i].
-// kOutput false: the state alone advances (a block skipped by a CTA that
-// draws a later range of resamples); nothing is tempered or written to the ring.
-template <bool kOutput = true>
+// ring[base + i].  kBarrier false: the caller places the barrier (after work
+// of its own that reads neither `dst` nor ring[base, base + 624)).
+template <bool kBarrier = true>
 __device__ __forceinline__ void twist_block(const uint32_t* src, uint32_t* dst, uint32_t* ring, int base) {
   constexpr int A = kMtN - kMtM;          // 227
   const int t = threadIdx.x;
@@ -106,16 +106,17 @@ __device__ __forceinline__ void twist_block(const uint32_t* src, uint32_t* dst, 
     const uint32_t b = twist_one(src[t + A], src[t + A + 1], a);
     dst[t] = a;
     dst[t + A] = b;
-    if (kOutput) { ring[base + t] = temper(a); ring[base + t + A] = temper(b); }
+    ring[base + t] = temper(a);
+    ring[base + t + A] = temper(b);
     if (t < kMtN - 2 * A) {
       const int i = t + 2 * A;
       const uint32_t next = i < kMtN - 1 ? src[i + 1] : twist_one(src[0], src[1], src[kMtM]);
       const uint32_t c = twist_one(src[i], next, b);
       dst[i] = c;
-      if (kOutput) ring[base + i] = temper(c);
+      ring[base + i] = temper(c);
     }
   }
-  __syncthreads();
+  if (kBarrier) __syncthreads();
 }
 
 __device__ __forceinline__ int draw_index(uint32_t w0, uint32_t w1, double n) {
@@ -200,20 +201,20 @@ struct BootSmem {
   }
 };
 
-// Scratch layout: the prepared multiset histograms (draw_splits per group,
-// kMaxBins words each: one partial histogram per range of resamples), then,
-// when a group may have more than kHistMaxN members, one index stream per group
-// (B draws of up to kDirectMaxN one-byte indices).
-__host__ __device__ inline size_t hist_area_bytes(int n_groups, int splits) {
-  return ((size_t)n_groups * (splits < 1 ? 1 : splits) * kMaxBins * sizeof(uint32_t) + 255) & ~(size_t)255;
+// Scratch layout: one prepared multiset histogram per group (kMaxBins words),
+// then, when the prepare pass streams every group (A.streamed) or a group may
+// have more than kHistMaxN members, one index stream per group: B resamples
+// of up to max_members one-byte indices, resample r of a count-n draw at
+// [r n, r n + n).
+__host__ __device__ inline size_t hist_area_bytes(int n_groups) {
+  return ((size_t)n_groups * kMaxBins * sizeof(uint32_t) + 255) & ~(size_t)255;
 }
-__device__ inline int splits_of(const BootArgs& A) { return A.draw_splits < 1 ? 1 : A.draw_splits; }
-__device__ inline uint32_t* prepared_hist(const BootArgs& A, int g, int split) {
-  return reinterpret_cast<uint32_t*>(A.scratch) + ((size_t)g * splits_of(A) + split) * kMaxBins;
+__device__ inline uint32_t* prepared_hist(const BootArgs& A, int g) {
+  return reinterpret_cast<uint32_t*>(A.scratch) + (size_t)g * kMaxBins;
 }
 __device__ inline uint8_t* index_stream(const BootArgs& A, int g) {
-  return A.max_members > kHistMaxN
-             ? A.scratch + hist_area_bytes(A.n_groups, A.draw_splits) + (size_t)g * A.resamples * kDirectMaxN
+  return A.streamed || A.max_members > kHistMaxN
+             ? A.scratch + hist_area_bytes(A.n_groups) + (size_t)g * A.resamples * A.max_members
              : nullptr;
 }
 
@@ -226,12 +227,16 @@ struct GenShared {
   uint32_t binom[16][16];
 };
 
-// Resamples r0..r1-1 (of B) of n draws from the seeded state in sh.mt_seed:
-// multiset counts into sh.hist (n <= kHistMaxN, hist cleared here) or raw
-// indices into `stream` (n > kHistMaxN).  The blocks of the stream before the
-// range are twisted without output.  All threads call it.
-__device__ __forceinline__ void generate_resamples(GenShared& sh, int n, int B, uint8_t* stream, uint32_t r0 = 0,
-                                                   uint32_t r1 = 0xffffffffu) {
+__device__ __forceinline__ void load_binom(GenShared& sh) {
+  for (int i = threadIdx.x; i < 256; i += blockDim.x) sh.binom[i >> 4][i & 15] = c_binom[i >> 4][i & 15];
+}
+
+// B resamples of n draws from the seeded state in sh.mt_seed, generated and
+// consumed block by block in one CTA: multiset counts into sh.hist
+// (n <= kHistMaxN, hist cleared here) or raw indices into `stream`
+// (n > kHistMaxN).  The finish uses it for a count that was not prepared, and
+// the prepare pass when the scratch holds no streams.  All threads call it.
+__device__ __forceinline__ void generate_resamples(GenShared& sh, int n, int B, uint8_t* stream) {
   const bool histogram = n <= kHistMaxN;
   if (histogram)
     for (int i = threadIdx.x; i < kMaxBins; i += blockDim.x) sh.hist[i] = 0;
@@ -239,23 +244,17 @@ __device__ __forceinline__ void generate_resamples(GenShared& sh, int n, int B, 
   __syncthreads();
   const double nd = (double)n;
   const uint32_t words_per_draw = 2u * (uint32_t)n;          // 2nB < 2^32 (B <= 2^24, n <= 128)
-  if (r1 > (uint32_t)B) r1 = B;
-  const uint32_t blocks = (uint32_t)(((uint64_t)r1 * words_per_draw + kMtN - 1) / kMtN);
-  // The block holding the first word of resample r0: every earlier block only advances the state.
-  const uint32_t first_block = (uint32_t)(((uint64_t)r0 * words_per_draw) / kMtN);
-  uint32_t blk = 0;
-  for (; blk < first_block && blk < blocks; ++blk)
-    twist_block<false>(sh.mt[blk & 1], sh.mt[(blk & 1) ^ 1], sh.ring, 0);
-  uint32_t next_r = r0;
-  int slot = (int)(blk % 3);                                  // ring slot of the current block
-  for (; blk < blocks; ++blk) {
+  const uint32_t blocks = (uint32_t)(((uint64_t)B * words_per_draw + kMtN - 1) / kMtN);
+  uint32_t next_r = 0;
+  int slot = 0;                                               // ring slot of the current block
+  for (uint32_t blk = 0; blk < blocks; ++blk) {
     twist_block(sh.mt[blk & 1], sh.mt[(blk & 1) ^ 1], sh.ring, slot * kMtN);
     // Words [first, avail) are readable: the previous block and this one.
     const uint32_t avail = (blk + 1) * (uint32_t)kMtN;
     const uint32_t first = blk ? avail - 2 * kMtN : 0;
     const int first_slot = blk ? (slot + 2) % 3 : 0;          // slot of word `first`
     uint32_t r_end = avail / words_per_draw;
-    if (r_end > r1) r_end = r1;
+    if (r_end > (uint32_t)B) r_end = B;
     for (uint32_t r = next_r + threadIdx.x; r < r_end; r += blockDim.x) {
       uint32_t pos = first_slot * kMtN + (r * words_per_draw - first);
       if (pos >= (uint32_t)kRing) pos -= kRing;
@@ -281,30 +280,96 @@ __device__ __forceinline__ void generate_resamples(GenShared& sh, int n, int B, 
   __syncthreads();
 }
 
-__device__ __forceinline__ void load_binom(GenShared& sh) {
-  for (int i = threadIdx.x; i < 256; i += blockDim.x) sh.binom[i >> 4][i & 15] = c_binom[i >> 4][i & 15];
+// The group's whole index stream (B n draws, one byte each) from the seeded
+// state in sh.mt_seed, with nothing else in the generator's serial chain: each
+// pass twists block k into one half of the ring while the threads turn the
+// 312 word pairs of block k - 1 (the other half) into draw indices and store
+// them, then one barrier.  A draw never straddles two blocks (624 is even),
+// so draw d of the stream is pair d mod 312 of block d / 312.
+// Needs blockDim.x >= 312.  All threads call it.
+__device__ __forceinline__ void stream_draws(GenShared& sh, int n, int B, uint8_t* stream) {
+  constexpr int kPairs = kMtN / 2;
+  for (int i = threadIdx.x; i < kMtN; i += blockDim.x) sh.mt[0][i] = sh.mt_seed[i];
+  __syncthreads();
+  const double nd = (double)n;
+  const uint32_t draws = (uint32_t)B * (uint32_t)n;
+  const uint32_t blocks = (draws + kPairs - 1) / kPairs;
+  const int j = threadIdx.x;
+  for (uint32_t blk = 0; blk <= blocks; ++blk) {
+    if (blk < blocks) twist_block<false>(sh.mt[blk & 1], sh.mt[(blk & 1) ^ 1], sh.ring, (int)(blk & 1) * kMtN);
+    if (blk > 0 && j < kPairs) {
+      const uint32_t d = (blk - 1) * kPairs + j;
+      const uint32_t* words = sh.ring + ((blk - 1) & 1) * kMtN;
+      if (d < draws) stream[d] = (uint8_t)draw_index(words[2 * j], words[2 * j + 1], nd);
+    }
+    __syncthreads();
+  }
+}
+
+// Multiset counts of the B resamples of a count-N stream (N <= kHistMaxN)
+// into sh.hist: each thread sorts its resamples' indices in registers and
+// ranks the multiset; lanes of a warp holding the same rank add once together.
+template <int N>
+__device__ __forceinline__ void histogram_stream(GenShared& sh, int B, const uint8_t* stream) {
+  for (int r0 = 0; r0 < B; r0 += blockDim.x) {
+    const int r = r0 + threadIdx.x;
+    int rank = -1;
+    if (r < B) {
+      int t[N];
+#pragma unroll
+      for (int i = 0; i < N; ++i) t[i] = stream[(size_t)r * N + i];
+#pragma unroll
+      for (int i = 0; i < N; ++i)
+#pragma unroll
+        for (int k = 0; k < N - 1 - i; ++k) {
+          const int a = t[k], b = t[k + 1];
+          t[k] = min(a, b); t[k + 1] = max(a, b);
+        }
+      rank = 0;
+#pragma unroll
+      for (int i = 0; i < N; ++i) rank += (int)sh.binom[t[i] + i][i + 1];
+    }
+    const unsigned live = __ballot_sync(0xffffffffu, rank >= 0);
+    if (rank >= 0) {
+      const unsigned same = __match_any_sync(live, rank);
+      if ((int)(threadIdx.x & 31) == __ffs(same) - 1) atomicAdd(&sh.hist[rank], (uint32_t)__popc(same));
+    }
+  }
 }
 
 // Stream generation ahead of the fold: for each group's member count n (the
 // count every metric has when all listed members are valid and finite), the
-// multiset histogram (n <= kHistMaxN) or the index stream.  It needs only
-// seeds and group sizes, so it can run while the trials are still analysed.
-// With draw_splits S > 1, CTA (g, s) draws resamples [s B / S, (s + 1) B / S)
-// of group g: a partial histogram each (the finish adds them), or its range
-// of the index stream.
-__global__ void __launch_bounds__(kBootThreads) bootstrap_prepare_kernel(BootArgs A) {
+// multiset histogram (n <= kHistMaxN) and, where the scratch holds streams,
+// the index stream.  It needs only seeds and group sizes, so it runs while
+// the trials are still analysed.  A.streamed: the index stream first (the
+// generator's chain alone), then the histogram from it; otherwise the
+// resamples are consumed as the blocks are produced.
+__global__ void __launch_bounds__(kPrepThreads) bootstrap_prepare_kernel(BootArgs A) {
   __shared__ GenShared sh;
-  const int S = splits_of(A);
-  const int g = blockIdx.x / S, split = blockIdx.x - g * S;
+  const int g = blockIdx.x;
   const int n = A.offsets[g + 1] - A.offsets[g];
   if (n < 3 || n > A.max_members || n > kDirectMaxN) return;   // no interval for n < 3 (uniform exit)
   load_binom(sh);
   if (threadIdx.x == 0) seed_state(sh.mt_seed, A.seeds[g]);
+  for (int i = threadIdx.x; i < kMaxBins; i += blockDim.x) sh.hist[i] = 0;
   __syncthreads();
-  const uint32_t r0 = (uint32_t)((uint64_t)A.resamples * split / S), r1 = (uint32_t)((uint64_t)A.resamples * (split + 1) / S);
-  generate_resamples(sh, n, A.resamples, index_stream(A, g), r0, r1);
+  uint8_t* stream = index_stream(A, g);
+  if (A.streamed) {
+    stream_draws(sh, n, A.resamples, stream);
+    switch (n) {
+      case 3: histogram_stream<3>(sh, A.resamples, stream); break;
+      case 4: histogram_stream<4>(sh, A.resamples, stream); break;
+      case 5: histogram_stream<5>(sh, A.resamples, stream); break;
+      case 6: histogram_stream<6>(sh, A.resamples, stream); break;
+      case 7: histogram_stream<7>(sh, A.resamples, stream); break;
+      default: break;                                          // direct path: the stream is the product
+    }
+    __syncthreads();
+  } else {
+    generate_resamples(sh, n, A.resamples, stream);
+  }
   if (n <= kHistMaxN) {
-    uint32_t* out = prepared_hist(A, g, split);
+    uint32_t* out = prepared_hist(A, g);
     const int nbins = (int)sh.binom[2 * n - 1][n];
     for (int i = threadIdx.x; i < nbins; i += blockDim.x) out[i] = sh.hist[i];
   }
@@ -422,12 +487,8 @@ __global__ void __launch_bounds__(kBootThreads) bootstrap_kernel(BootArgs A, pm_
     uint8_t* stream = index_stream(A, g);
     if (A.prepared && n == members) {
       if (histogram) {
-        const int S = splits_of(A);
-        for (int i = threadIdx.x; i < nbins; i += blockDim.x) {
-          uint32_t c = 0;
-          for (int sp = 0; sp < S; ++sp) c += prepared_hist(A, g, sp)[i];
-          sh.hist[i] = c;
-        }
+        const uint32_t* prepared = prepared_hist(A, g);
+        for (int i = threadIdx.x; i < nbins; i += blockDim.x) sh.hist[i] = prepared[i];
       }
       __syncthreads();
     } else {
@@ -778,27 +839,9 @@ int prepare_bootstrap_constants(int device) {
   return 0;
 }
 
-// Resample ranges per group for the draws: the draws take at most half of the
-// 148 SMs (at most 16 CTAs per group), leaving the other half to the trial
-// analysis they overlap.  On B200 with 64 groups beside the 64-trial analysis,
-// one range per group gives the shortest step (0.159 ms; 2, 4, 8 ranges: 0.162,
-// 0.184, 0.225 ms), since each extra CTA re-twists the blocks before its range.
-// PM_DRAW_SPLITS overrides it (read once).  The scratch size and every launch
-// use the same value.
-int draw_splits(int n_groups) {
-  static const int forced = [] {
-    const char* env = getenv("PM_DRAW_SPLITS");
-    return env ? atoi(env) : 0;
-  }();
-  if (forced > 0) return forced > 64 ? 64 : forced;
-  if (n_groups <= 0) return 1;
-  const int s = 74 / n_groups;
-  return s < 1 ? 1 : s > 16 ? 16 : s;
-}
-
-size_t bootstrap_scratch_bytes(int n_groups, int max_members, int resamples) {
-  return hist_area_bytes(n_groups, draw_splits(n_groups)) +
-         (max_members > kHistMaxN ? (size_t)n_groups * resamples * kDirectMaxN : 0);
+size_t bootstrap_scratch_bytes(int n_groups, int max_members, int resamples, bool streamed) {
+  return hist_area_bytes(n_groups) +
+         (streamed || max_members > kHistMaxN ? (size_t)n_groups * resamples * max_members : 0);
 }
 
 // Shared memory the fold needs for M metrics and groups of up to mm members,
@@ -856,8 +899,7 @@ int launch_bootstrap(const BootArgs& A, cudaStream_t stream, const pm_peer_group
 
 int launch_bootstrap_prepare(const BootArgs& A, cudaStream_t stream) {
   if (A.n_groups == 0) return 0;
-  const int S = A.draw_splits < 1 ? 1 : A.draw_splits;
-  bootstrap_prepare_kernel<<<A.n_groups * S, kBootThreads, 0, stream>>>(A);
+  bootstrap_prepare_kernel<<<A.n_groups, kPrepThreads, 0, stream>>>(A);
   return 0;
 }
 

@@ -24,14 +24,14 @@ namespace pm {
 int launch_bootstrap(const BootArgs& A, cudaStream_t stream, const pm_peer_groups* groups = nullptr);
 int launch_bootstrap_prepare(const BootArgs& A, cudaStream_t stream);
 int prepare_bootstrap_constants(int device);
-size_t bootstrap_scratch_bytes(int n_groups, int max_members, int resamples);
 
 namespace {
 
-// Prepared multiset histograms (6.9 KB per group) and, when a group may have
-// more than seven members, index streams (resamples x 128 bytes per group):
-// 32 MiB covers, for example, 4800 groups of up to seven members, or 26 groups
-// of 8 or more members at 10 000 resamples.
+// Prepared multiset histograms (6.9 KB per group) and index streams
+// (resamples x max_members bytes per group; for groups of up to seven members
+// only while they fit, the faster prepare pass): 32 MiB covers, for example,
+// 4800 groups of up to seven members, or 200 groups of up to 16 members at
+// 10 000 resamples.
 constexpr size_t kStaticStreamBytes = size_t(32) << 20;
 static __device__ __align__(256) uint8_t g_static_streams[kStaticStreamBytes];
 
@@ -52,7 +52,10 @@ extern "C" int pm_group_bootstrap_device_static(const pm_bootstrap_job* job, voi
   // The checks of every other bootstrap entry point (sizes, limits, arrays).
   int rc = check_bootstrap(job);
   if (rc) return rc;
-  const size_t need = bootstrap_scratch_bytes(job->n_groups, job->max_members, job->resamples);
+  // Every group's index stream when the array holds them (the faster prepare
+  // pass), else only what the fused pass needs.
+  const bool streamed = bootstrap_scratch_bytes(job->n_groups, job->max_members, job->resamples) <= kStaticStreamBytes;
+  const size_t need = bootstrap_scratch_bytes(job->n_groups, job->max_members, job->resamples, streamed);
   if (need > kStaticStreamBytes)
     return fail(PM_E_LIMIT,
                 "pm_group_bootstrap_device_static: %d groups of up to %d members at %d resamples need %zu bytes of "
@@ -79,7 +82,7 @@ extern "C" int pm_group_bootstrap_device_static(const pm_bootstrap_job* job, voi
   // group's histogram or stream completely before the fold reads it back.
   BootArgs A{job->n_groups, job->n_metrics, job->resamples, job->max_members, job->values, job->group_offsets,
              job->member_rows, job->member_valid, job->seeds, job->medians, job->ci_lo, job->ci_hi,
-             static_cast<uint8_t*>(scratch), 1, draw_splits(job->n_groups)};
+             static_cast<uint8_t*>(scratch), 1, streamed ? 1 : 0};
   if (launch_bootstrap_prepare(A, static_cast<cudaStream_t>(stream)))
     return fail(PM_E_CUDA, "bootstrap_prepare_kernel launch failed");
   cudaError_t e = cudaGetLastError();

@@ -29,7 +29,6 @@ int launch_bootstrap(const BootArgs& A, cudaStream_t stream, const pm_peer_group
 int launch_bootstrap_prepare(const BootArgs& A, cudaStream_t stream);
 int launch_resample_indices(uint64_t seed, int n, int B, int32_t* out, cudaStream_t stream);
 int prepare_bootstrap_constants(int device);
-size_t bootstrap_scratch_bytes(int n_groups, int max_members, int resamples);
 
 static thread_local std::string t_error;
 
@@ -515,12 +514,16 @@ static int device_boot_args(const pm_bootstrap_job* job, void* scratch, size_t s
   if ((rc = current_device(&device))) return rc;
   if (prepare_bootstrap_constants(device)) return fail(PM_E_CUDA, "bootstrap constants upload failed");
   if ((rc = check_bootstrap_fits(job->n_metrics, job->max_members))) return rc;
-  const size_t need = bootstrap_scratch_bytes(job->n_groups, job->max_members, job->resamples);
+  // pm_bootstrap_scratch_bytes sizes the streamed layout; a scratch holding only
+  // the histograms (and the streams of groups above seven members) still works,
+  // with the draws consumed as they are generated.
+  const bool streamed = scratch && bootstrap_scratch_bytes(job->n_groups, job->max_members, job->resamples) <= scratch_bytes;
+  const size_t need = bootstrap_scratch_bytes(job->n_groups, job->max_members, job->resamples, streamed);
   if (need > scratch_bytes || (need && !scratch))
     return fail(PM_E_INVALID, "bootstrap needs %zu bytes of device scratch, got %zu", need, scratch_bytes);
   *out = BootArgs{job->n_groups, job->n_metrics, job->resamples, job->max_members, job->values, job->group_offsets,
                   job->member_rows, job->member_valid, job->seeds, job->medians, job->ci_lo, job->ci_hi,
-                  static_cast<uint8_t*>(scratch), 1, draw_splits(job->n_groups)};
+                  static_cast<uint8_t*>(scratch), 1, streamed ? 1 : 0};
   return PM_OK;
 }
 
@@ -616,7 +619,7 @@ int pm_group_bootstrap(const pm_bootstrap_job* job) {
                 reinterpret_cast<const int32_t*>(dev_of(ho)), hr ? reinterpret_cast<const int32_t*>(dev_of(hr)) : nullptr,
                 hvalid ? reinterpret_cast<const uint8_t*>(dev_of(hvalid)) : nullptr,
                 reinterpret_cast<const uint64_t*>(dev_of(hs)), dmed, dlo, dhi,
-                reinterpret_cast<uint8_t*>(dout + out_bytes), 1, draw_splits((int)G)};
+                reinterpret_cast<uint8_t*>(dout + out_bytes), 1, 1};
   launch_bootstrap_prepare(args, st);
   launch_bootstrap(args, st);
   e = cudaGetLastError();
@@ -682,7 +685,7 @@ int pm_analyze_sweep(const pm_trials* trials, const pm_policy* policy, pm_trial_
                 reinterpret_cast<const int32_t*>(dptr(hr)), S.dres.valid, reinterpret_cast<const uint64_t*>(dptr(hs)),
                 reinterpret_cast<double*>(dout), reinterpret_cast<double*>(dout + align256(G * M * 8)),
                 reinterpret_cast<double*>(dout + 2 * align256(G * M * 8)),
-                reinterpret_cast<uint8_t*>(dout + gout), 1, draw_splits((int)G)};
+                reinterpret_cast<uint8_t*>(dout + gout), 1, 1};
   // The resample draws need only seeds and group sizes: their inputs go first,
   // on the side stream, and the draws run there while the host stages the
   // trials (the GPU is otherwise idle then); the fold waits for them.

@@ -27,12 +27,13 @@ struct BootArgs {
   const uint8_t* member_valid;    // NULL: all rows count
   const uint64_t* seeds;
   double* medians; double* lo; double* hi;
-  uint8_t* scratch;               // prepared histograms, then index streams of groups with more than 7 members
+  uint8_t* scratch;               // prepared histograms, then index streams (all groups if streamed, else those above 7 members)
   int prepared;                   // 1: bootstrap_prepare_kernel filled scratch for each group's member count
-  int draw_splits;                // resample ranges per group in the prepare launch (0 or 1: one CTA per group)
+  int streamed;                   // 1: scratch holds every group's index stream (bootstrap_scratch_bytes(..., true))
 };
-// Resample ranges per group the prepare launch uses for n_groups groups (bootstrap.cu).
-int draw_splits(int n_groups);
+// Device scratch of a bootstrap: one histogram per group, plus index streams
+// for every group (streamed) or only when max_members > 7 (bootstrap.cu).
+size_t bootstrap_scratch_bytes(int n_groups, int max_members, int resamples, bool streamed = true);
 
 // Raises `kernel`'s dynamic shared-memory limit on the current device to at
 // least `bytes` (static plus dynamic above 48 KB needs the opt-in); `limits`

@@ -58,9 +58,12 @@ def test_static_bootstrap_matches_allocating_entry_point_twice():
     lib.pm_bootstrap_static_scratch_capacity.restype = C.c_size_t
     assert lib.pm_bootstrap_static_scratch_capacity() == 32 << 20
     rng = np.random.default_rng(20261201)
-    # Groups of more than seven members use the fixed array; smaller ones the shared-memory histogram.
-    for sizes, resamples in (((9, 12, 5, 20), 10000), ((8, 3, 16), 1000)):
-        values, members, seeds = _groups(rng, sizes, 47)
+    # Every group's index stream in the fixed array (the streamed prepare pass); the last job's streams
+    # do not fit, so its groups of up to seven members are drawn and counted in one pass instead.
+    many = tuple(3 + i % 5 for i in range(3000))
+    assert 3000 * 10000 * 7 > 32 << 20 > 3000 * 1716 * 4
+    for sizes, resamples, metrics in (((9, 12, 5, 20), 10000, 47), ((8, 3, 16), 1000, 47), (many, 10000, 3)):
+        values, members, seeds = _groups(rng, sizes, metrics)
         expected = bootstrap_groups(values, members, seeds, resamples)          # allocating host entry point
         got = _static_call(torch, lib, values, members, seeds, resamples)
         for e, g in zip(expected, got):
@@ -72,7 +75,9 @@ def test_static_bootstrap_rejects_jobs_beyond_its_array():
     lib = N.library()
     lib.pm_group_bootstrap_device_static.argtypes = [C.POINTER(N.BootstrapJob), C.c_void_p]
     dummy = C.c_double(0.0)
-    job = N.BootstrapJob(64, 1, 64 * 9, 64 * 9, 10000, 9, C.addressof(dummy), C.addressof(dummy), None, None,
+    # 64 groups of up to 64 members at 10 000 resamples: 41 MB of index streams, rejected before any launch.
+    assert 64 * 10000 * 64 > 32 << 20
+    job = N.BootstrapJob(64, 1, 64 * 64, 64 * 64, 10000, 64, C.addressof(dummy), C.addressof(dummy), None, None,
                          C.addressof(dummy), C.addressof(dummy), C.addressof(dummy), C.addressof(dummy))
     rc = lib.pm_group_bootstrap_device_static(job, None)
     assert rc == -4 and "fixed array holds" in N.last_error()
