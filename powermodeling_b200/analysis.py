@@ -945,8 +945,13 @@ def check_summary_arguments(throughput_fraction: float, min_repeats: int, hbm_ba
 def summarize(records: Iterable[Mapping[str, Any]], throughput_fraction: float = 0.95,
               policy: AnalysisPolicy | Mapping[str, Any] | None = None, min_repeats: int = 3,
               plan: Mapping[str, Any] | None = None, evaluation_policy=None,
-              hbm_bandwidth_fraction: float = 0.80, resamples: int = DEFAULT_RESAMPLES) -> dict[str, Any]:
-    """summarize's trial and group sections (analysis.py:1400-1519); ``resamples`` generalises the 1000 draws.
+              hbm_bandwidth_fraction: float = 0.80, resamples: int = DEFAULT_RESAMPLES,
+              plan_validator=None) -> dict[str, Any]:
+    """The reference's summary (analysis.py:1400-1556): trials, groups, selection sections and the
+    component evaluation; ``resamples`` generalises the 1000 draws.  ``plan`` and
+    ``evaluation_policy`` go to the evaluation (powermodeling_b200.evaluation.evaluate), whose
+    planner policy check is not restated: pass ``plan_validator`` (runner.validate_plan_execution)
+    to have its error recorded in the coverage.
 
     The cyclic garbage collector is paused for the call: the summary is built
     from tens of thousands of new dicts and lists, and a full collection in
@@ -955,7 +960,12 @@ def summarize(records: Iterable[Mapping[str, Any]], throughput_fraction: float =
     paused = gc.isenabled()
     gc.disable()
     try:
-        return _summarize(records, throughput_fraction, policy, min_repeats, hbm_bandwidth_fraction, resamples)
+        records = records if isinstance(records, list) else list(records)
+        summary = _summarize(records, throughput_fraction, policy, min_repeats, hbm_bandwidth_fraction, resamples)
+        from .evaluation import evaluate
+        summary["evaluation"] = evaluate(summary, plan=plan, policy=evaluation_policy, raw_records=records,
+                                         plan_validator=plan_validator)
+        return summary
     finally:
         if paused:
             gc.enable()
@@ -1000,8 +1010,9 @@ def write_summary(summary: Mapping[str, Any], output_dir) -> dict[str, str]:
     summary.json is the summary as indented JSON (non-finite numbers refused,
     as the reference refuses them); trials.csv holds one row per trial with
     the reference's columns, lists and dicts as JSON text and absent fields
-    empty.  The evaluation report files the reference adds for a summary with
-    an ``evaluation`` entry are not written."""
+    empty.  A summary with an ``evaluation`` entry also gets evaluation.json,
+    evaluation.csv and, with an HBM component, hbm-memory-power.csv
+    (evaluation.write_evaluation; the reference's HTML view is not written)."""
     import csv
     from pathlib import Path
     destination = Path(output_dir)
@@ -1015,5 +1026,9 @@ def write_summary(summary: Mapping[str, Any], output_dir) -> dict[str, str]:
         for trial in summary.get("trials", []):
             writer.writerow({f: json.dumps(trial[f]) if isinstance(trial.get(f), (list, dict)) else trial.get(f)
                              for f in TRIAL_CSV_FIELDS})
-    return {"summary_json": str(json_path), "trials_csv": str(csv_path)}
+    paths = {"summary_json": str(json_path), "trials_csv": str(csv_path)}
+    if summary.get("evaluation") is not None:
+        from .evaluation import write_evaluation
+        paths.update(write_evaluation(summary["evaluation"], destination))
+    return paths
 

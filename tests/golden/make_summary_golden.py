@@ -2,11 +2,11 @@
 
     python tests/golden/make_summary_golden.py <reference checkout>      (or PM_REFERENCE_TREE=<reference checkout>)
 
-Runs the reference's summarize on two small synthetic sweeps (its evaluation
-entry removed: the report files are out of scope), round-trips each summary
-through JSON, and runs the reference's write_summary on it; stores the text
-of summary.json and trials.csv (the summary is summary.json read back) in
-tests/golden/summary_files.json.gz.
+Runs the reference's summarize on two small synthetic sweeps, round-trips
+each summary through JSON, and runs the reference's write_summary on it;
+stores the text of summary.json, trials.csv, evaluation.json and
+evaluation.csv (the summary is summary.json read back; the HTML view is not
+kept) in tests/golden/summary_files.json.gz.
 """
 from __future__ import annotations
 
@@ -29,11 +29,11 @@ def main(reference: str) -> None:
     for label, shape, seed in (("trapezoid", SweepShape(points=2, repeats=4), 21),
                                ("counter", SweepShape(points=2, repeats=3, with_energy_counter=True), 22)):
         summary = ref.summarize(make_sweep(shape, seed), policy=ANALYSIS_POLICY)
-        summary["evaluation"] = None
         summary = json.loads(json.dumps(summary, allow_nan=False))
         with tempfile.TemporaryDirectory() as tmp:
             ref.write_summary(summary, tmp)
-            files = {name: (Path(tmp) / name).read_text() for name in ("summary.json", "trials.csv")}
+            files = {name: (Path(tmp) / name).read_text()
+                     for name in ("summary.json", "trials.csv", "evaluation.json", "evaluation.csv")}
         cases.append({"label": label, "files": files})   # the summary itself is json.loads(summary.json)
     with gzip.open(HERE / "summary_files.json.gz", "wt") as f:
         json.dump(cases, f)

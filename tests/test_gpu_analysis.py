@@ -209,8 +209,9 @@ SELECTION_SECTIONS = ("within_clock_best", "cross_clock_best", "within_clock_bes
 
 
 def test_summary_selection_sections_match_reference(gpu_ready):
-    """summarize's selection sections over the GPU's groups equal the reference's summarize on the
-    same records (the summary-file fixture: a trapezoid sweep and an energy-counter sweep)."""
+    """summarize's selection sections and evaluation over the GPU's groups equal the reference's
+    summarize on the same records (the summary-file fixture: a trapezoid sweep and an energy-counter
+    sweep)."""
     import json
     from powermodeling_b200.analysis import summarize
     from powermodeling_b200.synthetic import ANALYSIS_POLICY, SweepShape, make_sweep
@@ -225,3 +226,4 @@ def test_summary_selection_sections_match_reference(gpu_ready):
             assert got[key] == want[key], (case["label"], key)
         for key, value in want["selection_policy"].items():
             assert got["selection_policy"][key] == value, key
+        assert got["evaluation"] == want["evaluation"], case["label"]
