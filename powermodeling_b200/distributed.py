@@ -85,8 +85,9 @@ def _all_gather_groups(n_groups: int, width: int, mine: list[int], outputs, worl
 def summarize_sharded(records: Iterable[Mapping[str, Any]], throughput_fraction: float = 0.95,
                       policy: A.AnalysisPolicy | Mapping[str, Any] | None = None, min_repeats: int = 3,
                       hbm_bandwidth_fraction: float = 0.80, resamples: int = A.DEFAULT_RESAMPLES,
-                      group=None) -> dict[str, Any]:
-    """``summarize`` of all ranks' records (rank order); each rank passes its own and gets the whole summary."""
+                      group=None, plan=None, evaluation_policy=None, plan_validator=None) -> dict[str, Any]:
+    """``summarize`` of all ranks' records (rank order); each rank passes its own and gets the whole summary.
+    The evaluation's display traces are gathered as trace points, not whole records."""
     import torch.distributed as dist
     rank, world = dist.get_rank(group), dist.get_world_size(group)
     hbm_bandwidth_fraction = A.check_summary_arguments(throughput_fraction, min_repeats, hbm_bandwidth_fraction)
@@ -119,5 +120,12 @@ def summarize_sharded(records: Iterable[Mapping[str, Any]], throughput_fraction:
         outputs = tuple(np.zeros((0, width)) for _ in range(3))
     med, lo, hi = _all_gather_groups(len(groups), width, mine, outputs, world, group)
     A.finish_groups(groups, trials, members, group_indices, med, lo, hi, hbm_bandwidth_fraction)
-    return A.summary_record(trials, groups, duplicates, throughput_fraction, hbm_bandwidth_fraction, min_repeats,
-                            resamples, policy)
+    summary = A.summary_record(trials, groups, duplicates, throughput_fraction, hbm_bandwidth_fraction, min_repeats,
+                               resamples, policy)
+    from .evaluation import evaluate, trace_points
+    shards: list = [None] * world
+    dist.all_gather_object(shards, [(r.get("trial_id"), trace_points(r)) for r in records], group=group)
+    traces = {trial_id: points for shard in shards for trial_id, points in shard}   # the last record of an id wins
+    summary["evaluation"] = evaluate(summary, plan=plan, policy=evaluation_policy, plan_validator=plan_validator,
+                                     traces=traces)
+    return summary

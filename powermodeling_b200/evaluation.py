@@ -488,28 +488,48 @@ def _thinned(n: int) -> list[int]:
     return sorted({round(i * (n - 1) / min(95, n - 1)) for i in range(points)})
 
 
-def representative_trace(groups: list, analyzed: Mapping, raw: Mapping) -> dict | None:
-    """The median-energy valid repeat of the best-repeated group, its phases thinned for display."""
+def trace_points(record: Mapping) -> list | None:
+    """A record's display trace: at most 96 samples per phase (None when its phases are not a dict)."""
+    phases = record.get("phases") or {}
+    if not isinstance(phases, dict):
+        return None
+    points = []
+    for name, phase in phases.items():
+        samples = phase.get("samples", [])
+        points += [{"phase": name, **{k: _num(samples[i].get(k)) for k in _TRACE_FIELDS}}
+                   for i in _thinned(len(samples)) if isinstance(samples[i], dict)]
+    return points
+
+
+def representative_trace(groups: list, analyzed: Mapping, traces: Mapping) -> dict | None:
+    """The median-energy valid repeat of the best-repeated group with a trace (``traces``: trial id ->
+    trace_points of its record, None or absent when it has none)."""
     for group in sorted(groups, key=lambda g: (-g.get("valid_repeats", 0), g["group_id"])):
         valid = sorted((analyzed[i] for i in group["trial_ids"] if i in analyzed and analyzed[i].get("valid")),
                        key=lambda t: t.get("total_energy_j") or 0)
         if not valid:
             continue
         trial = valid[len(valid) // 2]
-        record = raw.get(trial["trial_id"])
-        if record is None:
+        points = traces.get(trial["trial_id"])
+        if points is None:
             continue
-        phases = record.get("phases") or {}
-        if not isinstance(phases, dict):
-            continue
-        points = []
-        for name, phase in phases.items():
-            samples = phase.get("samples", [])
-            points += [{"phase": name, **{k: _num(samples[i].get(k)) for k in _TRACE_FIELDS}}
-                       for i in _thinned(len(samples)) if isinstance(samples[i], dict)]
         return {"trial_id": trial["trial_id"], "group_id": group["group_id"], "points": points,
                 "note": "One valid repeat; at most 96 observed samples per phase for display only. Energy uses original samples and exact complete epochs."}
     return None
+
+
+class _LazyTraces(dict):
+    """trial id -> trace_points of the last record with that id, computed on first use."""
+
+    def __init__(self, records):
+        super().__init__()
+        self.records = {r.get("trial_id"): r for r in records}
+
+    def get(self, trial_id, default=None):
+        if trial_id not in self:
+            record = self.records.get(trial_id)
+            self[trial_id] = None if record is None else trace_points(record)
+        return dict.get(self, trial_id, default)
 
 
 # ---------------------------------------------------------------------------- one component
@@ -523,7 +543,7 @@ class _Context:
     plan: Any
     coverage: dict
     analyzed: dict
-    raw: dict
+    traces: Mapping
     input_curves: dict
 
 
@@ -820,7 +840,7 @@ def _component(key: str, groups: list, ctx: _Context) -> dict:
             "input_scaling": _input_scaling(groups, u, ctx),
             "profiler_evidence": evidence, "latency_points": latency,
             "correctness_scope": _correctness_scope(workload),
-            "measurement_example": representative_trace(groups, ctx.analyzed, ctx.raw),
+            "measurement_example": representative_trace(groups, ctx.analyzed, ctx.traces),
             "interpretation": _interpretation(workload)}
 
 
@@ -838,10 +858,12 @@ LIMITS = (
 )
 
 
-def evaluate(summary: Mapping, plan=None, policy=None, raw_records=(), plan_validator=None) -> dict[str, Any]:
+def evaluate(summary: Mapping, plan=None, policy=None, raw_records=(), plan_validator=None,
+             traces: Mapping | None = None) -> dict[str, Any]:
     """The evaluation of a summary (evaluation.py:436): components, plan coverage, limits.
 
-    ``raw_records`` are the runner's records (for the representative traces);
+    ``raw_records`` are the runner's records (for the representative traces), or ``traces`` their
+    trace_points by trial id (what a sharded caller gathers instead of whole records);
     ``plan_validator`` is the planner's execution policy check (see plan_coverage)."""
     policy = policy if isinstance(policy, EvaluationPolicy) else EvaluationPolicy(**(policy or {}))
     selection = summary["selection_policy"]
@@ -856,7 +878,7 @@ def evaluate(summary: Mapping, plan=None, policy=None, raw_records=(), plan_vali
     ctx = _Context(policy=policy, minimum_repeats=selection["min_repeats"], minimum_geometries=selection["min_geometries"],
                    fraction=selection["throughput_fraction"], near_fraction=selection.get("near_optimum_fraction", 0.05),
                    plan=plan, coverage=coverage, analyzed={t["trial_id"]: t for t in summary["trials"]},
-                   raw={r.get("trial_id"): r for r in raw_records}, input_curves=curves)
+                   traces=traces if traces is not None else _LazyTraces(raw_records), input_curves=curves)
     components = [_component(key, groups, ctx) for key, groups in sorted(strata.items())]
     return {"schema_version": 1,
             "policy": {**asdict(policy), "throughput_fraction": ctx.fraction,
