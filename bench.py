@@ -296,15 +296,17 @@ def run_b200(args, rank: int, world: int) -> dict | None:
 
     def step(ev, side_ev):
         # The resample draws need only seeds and group sizes: drawn on a side
-        # stream while this rank's trials are analysed.
+        # stream while this rank's trials are analysed.  The analysis is
+        # enqueued first, so its CTAs take their SMs before the draws' CTAs
+        # fill what is left.
         ev[0].record(stream)
         side.wait_event(ev[0])
+        N.check(lib.pm_analyze_trials_device(trials, native_policy, results, C.c_void_p(scratch.data_ptr()), a_scr, sptr),
+                "analyze")
         side_ev[0].record(side)
         if G:
             N.check(lib.pm_bootstrap_prepare_device(job, boot_scratch, b_scr, side_ptr), "prepare")
         side_ev[1].record(side)
-        N.check(lib.pm_analyze_trials_device(trials, native_policy, results, C.c_void_p(scratch.data_ptr()), a_scr, sptr),
-                "analyze")
         ev[1].record(stream)
         stream.wait_event(side_ev[1])
         ev[2].record(stream)
@@ -978,10 +980,16 @@ def main():
             print(json.dumps(run_reference(args)), flush=True)
         return
     if world > 1:
+        # The ranks share the host's cores: each rank's record packer and staging pool take
+        # their share instead of all of them (the variables are read once, at first use).
+        share = max(1, (len(os.sched_getaffinity(0)) or 1) // int(os.environ.get("LOCAL_WORLD_SIZE", world)))
+        os.environ.setdefault("PM_PACK_THREADS", str(min(8, share)))
+        os.environ.setdefault("PM_HOST_THREADS", str(max(1, min(3, share - 1))))
         import datetime
         import torch
         import torch.distributed as dist
         torch.cuda.set_device(int(os.environ.get("LOCAL_RANK", "0")))
+        torch.set_num_threads(min(torch.get_num_threads(), share))
         dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120))
     try:
         line = run_b200(args, rank, world)
