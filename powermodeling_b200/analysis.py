@@ -454,6 +454,7 @@ def analyze_trials(records: Iterable[Mapping[str, Any]], policy: AnalysisPolicy 
                    hbm_bandwidth_fraction: float = 0.80, _metrics_out: list | None = None) -> list[dict[str, Any]]:
     """analyze_trial over a batch, in one kernel launch."""
     from .hbm import trial_bandwidth, validate_fraction
+    from .trial_report import complete_trial
     hbm_bandwidth_fraction = validate_fraction(hbm_bandwidth_fraction)
     policy = _policy(policy)
     records = list(records)
@@ -655,6 +656,10 @@ def analyze_trials(records: Iterable[Mapping[str, Any]], policy: AnalysisPolicy 
                 for alias in ("memory_rail_power_w", "memory_rail_incremental_power_w"):
                     value = result[alias]
                     rows[i, METRICS.index(alias)] = math.nan if value is None else value
+        reported = [p for p, name in enumerate(N.PHASE_NAMES)
+                    if name in ("idle_pre", "measure", "idle_post") or (name == "active_control" and phases_rec.get(name))]
+        complete_trial(record, result, policy.trim_s, selected,
+                       {N.PHASE_NAMES[p]: _selected(packed, i, p, views) for p in reported})
         out.append(result)
     return out
 
@@ -844,9 +849,10 @@ def group_structure(trials: list, min_repeats: int) -> tuple[list, list, list, l
 
 
 def finish_groups(groups: list, trials: list, members: list, group_indices: list, med: np.ndarray, lo: np.ndarray,
-                  hi: np.ndarray, hbm_bandwidth_fraction: float) -> None:
+                  hi: np.ndarray, hbm_bandwidth_fraction: float, min_repeats: int = 3) -> None:
     """Group medians, intervals and the derived group records, from the bootstrap outputs (in place)."""
     from .hbm import group_bandwidth
+    from .trial_report import complete_group
     base = len(METRICS)
     for g, group in enumerate(groups):
         for m, metric in enumerate(METRICS):
@@ -877,6 +883,7 @@ def finish_groups(groups: list, trials: list, members: list, group_indices: list
             arm[order] = statistics.median(vals) if vals else None
         group["paired_reference_order_medians_power_w"] = arm
         group["paired_reference_order_effect_power_w"] = arm["AB"] - arm["BA"] if None not in arm.values() else None
+        complete_group(group, trials[group_indices[g][0]], vt, min_repeats)
 
 
 NOTES = ["No fabricated measurement or architecture-specific idle wattage is supplied.",
@@ -978,7 +985,7 @@ def _summarize(records, throughput_fraction, policy, min_repeats, hbm_bandwidth_
     trials, rows = analyze_rows(kept, policy, hbm_bandwidth_fraction)
     groups, members, seeds, group_indices = group_structure(trials, min_repeats)
     med, lo, hi = bootstrap_groups(rows, members, seeds, resamples) if groups else (None, None, None)
-    finish_groups(groups, trials, members, group_indices, med, lo, hi, hbm_bandwidth_fraction)
+    finish_groups(groups, trials, members, group_indices, med, lo, hi, hbm_bandwidth_fraction, min_repeats)
     return summary_record(trials, groups, duplicates, throughput_fraction, hbm_bandwidth_fraction, min_repeats,
                           resamples, policy)
 

@@ -119,7 +119,7 @@ def summarize_sharded(records: Iterable[Mapping[str, Any]], throughput_fraction:
     else:
         outputs = tuple(np.zeros((0, width)) for _ in range(3))
     med, lo, hi = _all_gather_groups(len(groups), width, mine, outputs, world, group)
-    A.finish_groups(groups, trials, members, group_indices, med, lo, hi, hbm_bandwidth_fraction)
+    A.finish_groups(groups, trials, members, group_indices, med, lo, hi, hbm_bandwidth_fraction, min_repeats)
     summary = A.summary_record(trials, groups, duplicates, throughput_fraction, hbm_bandwidth_fraction, min_repeats,
                                resamples, policy)
     from .evaluation import evaluate, trace_points

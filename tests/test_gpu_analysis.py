@@ -41,6 +41,18 @@ def test_trial_matches_reference(gpu_ready, golden_trials, name, record, policy)
             assert close(expected[key], got.get(key), rel=0.0), (key, expected[key], got.get(key))
 
 
+@pytest.mark.parametrize("name,record,policy", scenarios(), ids=[s[0] for s in scenarios()])
+def test_whole_trial_dict_matches_reference(gpu_ready, name, record, policy):
+    """Every field of the reference's analyze_trial result (tests/golden/trial_reports.json.gz)."""
+    import json
+    from powermodeling_b200.analysis import analyze_trial
+    case = next(c for c in load_golden("trial_reports.json.gz") if c["name"] == name)
+    assert case["digest"] == records_digest([record])
+    got = json.loads(json.dumps(analyze_trial(record, policy)))
+    problems = _differences(case["expected"], got)
+    assert not problems, problems[:8]
+
+
 def test_sweep_groups_match_reference(gpu_ready):
     from powermodeling_b200.analysis import group_key, summarize, METRICS
     from powermodeling_b200.synthetic import ANALYSIS_POLICY, SweepShape, make_sweep

@@ -63,20 +63,26 @@ def test_analysis_of_runner_records_matches_reference(gpu_ready, runner_records)
     """The reference runner's records of B200 telemetry, analysed here and by the reference."""
     from tests.golden.make_golden import PHASE_KEYS, TRIAL_KEYS
     from powermodeling_b200.analysis import analyze_trials
+    from test_gpu_analysis import _differences
     got = analyze_trials(runner_records["records"])
     for expected, trial in zip(runner_records["trials"], got):
         problems = diff(expected, trial, TRIAL_KEYS)
         for phase, stats in expected["phases"].items():
             problems += [f"{phase}.{p}" for p in diff(stats, trial["phases"].get(phase, {}), PHASE_KEYS)]
         assert not problems, (expected["trial_id"], problems)
+        # every field of the reference's trial dict, at the floating tolerance
+        assert not _differences(expected, json.loads(json.dumps(trial))), (expected["trial_id"], _differences(expected, json.loads(json.dumps(trial)))[:6])
     assert any(t["valid"] for t in got) and any(t.get("paired_active_reference_power_w") for t in got)
 
 
 @pytest.mark.gpu
 def test_summary_of_runner_records_matches_reference(gpu_ready, runner_records):
     from powermodeling_b200.analysis import METRICS, summarize
+    from test_gpu_analysis import _differences
     groups = summarize(runner_records["records"])["groups"]
     assert [g["group_id"] for g in groups] == [g["group_id"] for g in runner_records["groups"]]
+    for got, expected in zip(groups, runner_records["groups"]):
+        assert not _differences(expected, json.loads(json.dumps(got))), (expected["group_id"], _differences(expected, json.loads(json.dumps(got)))[:6])
     for got, expected in zip(groups, runner_records["groups"]):
         for metric in METRICS:
             assert close(expected.get(metric), got.get(metric)), (expected["group_id"], metric)
