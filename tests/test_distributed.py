@@ -40,7 +40,12 @@ def fake_analyze_rows(records, policy, hbm_bandwidth_fraction):
                  "baseline_valid": h % 5 != 0, "operational_idle_increment_eligible": True,
                  "paired_active_reference_eligible": True,
                  "paired_active_reference_protocol": {"order": "AB" if rec["repeat"] % 2 == 0 else "BA"},
-                 "paired_active_reference_power_w": 300.0 + h % 17, "hbm_memory_power": None}
+                 "paired_active_reference_power_w": 300.0 + h % 17, "hbm_memory_power": None,
+                 "target_verified": False, "verified_selection_eligible": False, "ncu_status": "unprofiled",
+                 "ncu_utilization_status": "inconclusive",
+                 "measurement_diagnostics": {"objectives": {"operational_idle_increment": {"power_w": 1.0 + h % 3},
+                                                            "paired_active_reference": {"power_w": 2.0}},
+                                             "scope_factors": {"total_over_idle_increment": 1.5 + h % 4}}}
         row = [float(_h(rec["trial_id"], k) % 100_000) / 97.0 for k in range(WIDTH)]
         for k in range(0, WIDTH, 11):
             if _h(rec["trial_id"], 1000 + k) % 4 == 0:
