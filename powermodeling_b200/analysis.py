@@ -658,10 +658,43 @@ def analyze_trials(records: Iterable[Mapping[str, Any]], policy: AnalysisPolicy 
                     rows[i, METRICS.index(alias)] = math.nan if value is None else value
         reported = [p for p, name in enumerate(N.PHASE_NAMES)
                     if name in ("idle_pre", "measure", "idle_post") or (name == "active_control" and phases_rec.get(name))]
-        complete_trial(record, result, policy.trim_s, selected,
-                       {N.PHASE_NAMES[p]: _selected(packed, i, p, views) for p in reported})
+        complete_trial(record, result, policy.trim_s, _binding(packed, i, views),
+                       _rail_sources(packed, i, reported, views))
         out.append(result)
     return out
+
+
+def _window(trial, phase, views):
+    slot = trial * N.PM_PHASES + phase
+    po = views.phase_out[slot * views.PO:(slot + 1) * views.PO]
+    lo, hi = po[N.layout("PM_PO_SEL_LO")], po[N.layout("PM_PO_SEL_HI")]
+    return slot, (None if math.isnan(lo) else (int(lo), int(hi)))
+
+
+def _binding(packed, trial, views):
+    """The measure window's clock bindings, built by the native packer."""
+    from .pack import _native_packer
+    slot, window = _window(trial, 1, views)
+    return _native_packer().binding_samples(packed.samples[slot], *window) if window else []
+
+
+def _rail_sources(packed, trial, phases, views):
+    """Memory-power sources of the selected windows; the packed flag words say first whether any
+    selected sample reports a memory power at all."""
+    from .trial_report import rail_sources_of
+    flags, offsets = packed.arrays["sample_flags"], packed.arrays["phase_offsets"]
+    windows = []
+    for p in phases:
+        slot, window = _window(trial, p, views)
+        if window:
+            windows.append((slot, window))
+    if packed.broadcast & dict(N.BROADCAST_COLUMNS)["sample_flags"]:        # one flag word for every sample
+        any_memory = bool(windows) and bool(int(flags[0]) & N.S_MEMORY_POWER_SET)
+    else:
+        any_memory = any((flags[offsets[slot] + a:offsets[slot] + b] & N.S_MEMORY_POWER_SET).any() for slot, (a, b) in windows)
+    if not any_memory:
+        return []
+    return rail_sources_of(packed.samples[slot][a:b] for slot, (a, b) in windows)
 
 
 def _selected(packed, trial, phase, views):

@@ -748,9 +748,89 @@ PyObject* pack(PyObject*, PyObject* args) {
 
 PyObject* last_fast_slots(PyObject*, PyObject*) { return PyLong_FromSsize_t(g_last_fast_slots); }
 
+// binding_samples(samples, lo, hi) -> [{"phase": "measure", "graphics_clock_mhz": s.get(...),
+// "memory_clock_mhz": s.get(...)} for s in samples[lo:hi]]: the clock binding of a trial's
+// selected measure samples (plain dicts read directly, anything else through its get()).
+// Runs of samples with equal clocks (same type and value) share one entry object.
+PyObject* binding_samples(PyObject*, PyObject* args) {
+  PyObject* samples;
+  Py_ssize_t lo, hi;
+  if (!PyArg_ParseTuple(args, "O!nn", &PyList_Type, &samples, &lo, &hi)) return nullptr;
+  const Py_ssize_t n = PyList_GET_SIZE(samples);
+  lo = lo < 0 ? 0 : lo > n ? n : lo;
+  hi = hi < lo ? lo : hi > n ? n : hi;
+  static PyObject* k_phase = PyUnicode_InternFromString("phase");
+  static PyObject* k_measure = PyUnicode_InternFromString("measure");
+  static PyObject* k_gfx = PyUnicode_InternFromString("graphics_clock_mhz");
+  static PyObject* k_mem = PyUnicode_InternFromString("memory_clock_mhz");
+  if (!k_phase || !k_measure || !k_gfx || !k_mem) return nullptr;
+  PyObject* out = PyList_New(hi - lo);
+  if (!out) return nullptr;
+  // Consecutive samples usually hold the same clocks: an entry whose two values equal the
+  // previous entry's (same type, equal value) is that entry's dict object again.
+  PyObject *last = nullptr, *last_gfx = nullptr, *last_mem = nullptr;
+  auto same = [](PyObject* a, PyObject* b) {
+    if (a == b) return 1;
+    if (!a || !b || Py_TYPE(a) != Py_TYPE(b) || !(PyLong_CheckExact(a) || PyFloat_CheckExact(a))) return 0;
+    return PyObject_RichCompareBool(a, b, Py_EQ);
+  };
+  for (Py_ssize_t i = lo; i < hi; ++i) {
+    PyObject* s = PyList_GET_ITEM(samples, i);
+    PyObject *gfx = nullptr, *mem = nullptr;
+    if (PyDict_CheckExact(s)) {              // borrowed values of a plain dict
+      gfx = PyDict_GetItemWithError(s, k_gfx);
+      if (gfx || !PyErr_Occurred()) mem = PyDict_GetItemWithError(s, k_mem);
+      Py_XINCREF(gfx);
+      Py_XINCREF(mem);
+      if (!gfx && !PyErr_Occurred()) gfx = Py_NewRef(Py_None);
+      if (!mem && !PyErr_Occurred()) mem = Py_NewRef(Py_None);
+    } else {                                 // anything else answers its own get()
+      gfx = PyObject_CallMethod(s, "get", "O", k_gfx);
+      if (gfx) mem = PyObject_CallMethod(s, "get", "O", k_mem);
+    }
+    if (!gfx || !mem) {
+      Py_XDECREF(gfx);
+      Py_XDECREF(mem);
+      Py_DECREF(out);
+      return nullptr;
+    }
+    if (last) {
+      const int eg = same(gfx, last_gfx), em = eg == 1 ? same(mem, last_mem) : 0;
+      if (eg < 0 || em < 0) {
+        Py_DECREF(gfx);
+        Py_DECREF(mem);
+        Py_DECREF(out);
+        return nullptr;
+      }
+      if (eg == 1 && em == 1) {
+        Py_DECREF(gfx);
+        Py_DECREF(mem);
+        PyList_SET_ITEM(out, i - lo, Py_NewRef(last));
+        continue;
+      }
+    }
+    PyObject* d = _PyDict_NewPresized(3);
+    const bool ok = d && PyDict_SetItem(d, k_phase, k_measure) == 0 && PyDict_SetItem(d, k_gfx, gfx) == 0 &&
+                    PyDict_SetItem(d, k_mem, mem) == 0;
+    Py_DECREF(gfx);
+    Py_DECREF(mem);
+    if (!ok) {
+      Py_XDECREF(d);
+      Py_DECREF(out);
+      return nullptr;
+    }
+    PyList_SET_ITEM(out, i - lo, d);
+    last = d;                                // borrowed: the list holds it
+    last_gfx = PyDict_GetItem(d, k_gfx);
+    last_mem = PyDict_GetItem(d, k_mem);
+  }
+  return out;
+}
+
 PyMethodDef kMethods[] = {
     {"pack", pack, METH_VARARGS, "pack(slots, pids, source_ids) -> (columns, counts, sorted, foreign)"},
     {"last_fast_slots", last_fast_slots, METH_NOARGS, "slots the last pack() call packed on its parallel fast path"},
+    {"binding_samples", binding_samples, METH_VARARGS, "binding_samples(samples, lo, hi) -> measure clock bindings"},
     {nullptr, nullptr, 0, nullptr}};
 
 PyModuleDef kModule = {PyModuleDef_HEAD_INIT, "_packnative",

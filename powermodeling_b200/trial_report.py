@@ -157,12 +157,17 @@ def kept_epochs(bench: Mapping, phase: Mapping | None, trim_s: float) -> list[di
     return [e for e in parsed if e["start_s"] >= start + trim_s - 1e-6 and e["end_s"] <= end - trim_s + 1e-6]
 
 
-def _validation_binding(record: Mapping, bench: Mapping, config: Mapping, selected: list) -> dict[str, Any]:
+def binding_samples(selected: list) -> list[dict]:
+    """The measure window's clock bindings (the native packer builds the same list faster)."""
+    return [{"phase": "measure", "graphics_clock_mhz": s.get("graphics_clock_mhz"),
+             "memory_clock_mhz": s.get("memory_clock_mhz")} for s in selected]
+
+
+def _validation_binding(record: Mapping, bench: Mapping, config: Mapping, binding: list) -> dict[str, Any]:
     return {"condition_id": record.get("condition_id"), "workload": record.get("workload"), "config": config,
             "provenance": record.get("provenance"),
             "benchmark": {k: v for k, v in bench.items() if k not in ("measure_epochs", "work_epochs")},
-            "samples": [{"phase": "measure", "graphics_clock_mhz": s.get("graphics_clock_mhz"),
-                         "memory_clock_mhz": s.get("memory_clock_mhz")} for s in selected]}
+            "samples": binding}
 
 
 def _sfu_diagnostics(record: Mapping, bench: Mapping, result: dict, count_ok: bool) -> None:
@@ -328,13 +333,19 @@ def measurement_diagnostics(result: Mapping, bench: Mapping, epochs: list) -> di
     }
 
 
+def rail_sources_of(phase_selected) -> list:
+    """Sorted memory-power sources of the samples that report a memory power."""
+    return sorted({s.get("memory_power_source") for samples in phase_selected
+                   for s in samples if s.get("memory_power_w") is not None and s.get("memory_power_source")})
+
+
 # ---------------------------------------------------------------------------- the whole trial
-def complete_trial(record: Mapping, result: dict, trim_s: float, selected_measure: list,
-                   phase_selected: Mapping[str, list]) -> dict:
+def complete_trial(record: Mapping, result: dict, trim_s: float, binding: list, rail_sources: list) -> dict:
     """Add the reporting fields to ``result`` (in place; also returned).
 
-    ``selected_measure``: the measure phase's selected samples (the aligned window);
-    ``phase_selected``: the selected samples of idle_pre, measure, idle_post and active_control."""
+    ``binding``: binding_samples of the measure phase's selected samples (the aligned window);
+    ``rail_sources``: the memory-power sources seen in the selected samples of idle_pre, measure,
+    idle_post and active_control (rail_sources_of)."""
     from .contracts import sfu_count_issues
     bench = record.get("benchmark") or record.get("result") or {}
     device = record.get("device") or {}
@@ -347,9 +358,8 @@ def complete_trial(record: Mapping, result: dict, trim_s: float, selected_measur
     result.update(_profiler_state(record, bench, config, result))
     result.update(_passthrough(record, bench, device))
     result.update(_statements(record, bench, result, epochs))
-    result["validation_binding"] = _validation_binding(record, bench, config, selected_measure)
-    result["memory_rail_sources"] = sorted({s.get("memory_power_source") for samples in phase_selected.values()
-                                            for s in samples if s.get("memory_power_w") is not None and s.get("memory_power_source")})
+    result["validation_binding"] = _validation_binding(record, bench, config, binding)
+    result["memory_rail_sources"] = rail_sources
     if workload == "l2_latency":
         result["latency_diagnostics"] = dict(bench)
     if phases_rec.get("active_control"):

@@ -8,6 +8,7 @@ dict is checked (tests/test_runner_contract.py)."""
 from __future__ import annotations
 
 import copy
+import json
 
 import pytest
 
@@ -53,7 +54,7 @@ CASES = _cases()
 def test_reporting_fields_match_reference(name, record, policy, expected):
     numeric = {k: copy.deepcopy(v) for k, v in expected.items() if k not in REPORT_KEYS + ON_GPU_ONLY}
     trim_s = AnalysisPolicy(**(policy or {})).trim_s
-    got = complete_trial(record, numeric, trim_s, [], {})
+    got = complete_trial(record, numeric, trim_s, [], [])
     for key in REPORT_KEYS:
         assert (key in got) == (key in expected), key
         if key in expected:
@@ -112,3 +113,26 @@ def test_group_reporting_fields_match_reference(label, trials, groups):
             if key in group:
                 assert close(group[key], got[key]), (label, group["workload"], key, group[key], got[key])
         assert close(group["ci95"], got["ci95"]), (label, "ci95")
+
+
+def test_native_binding_samples_equal_the_python_statement():
+    from powermodeling_b200 import _packnative
+    from powermodeling_b200.trial_report import binding_samples
+
+    class Sample(dict):
+        def get(self, key, default=None):
+            return "own"
+    samples = [{"graphics_clock_mhz": 1965, "memory_clock_mhz": 3996}, {"graphics_clock_mhz": 1965, "memory_clock_mhz": 3996},
+               {"graphics_clock_mhz": 1965.0, "memory_clock_mhz": 3996}, {"graphics_clock_mhz": True, "memory_clock_mhz": 3996},
+               {"graphics_clock_mhz": 1, "memory_clock_mhz": 3996}, {"graphics_clock_mhz": float("nan")},
+               {"graphics_clock_mhz": float("nan")}, {"graphics_clock_mhz": 1.5}, {}, {},
+               Sample(graphics_clock_mhz=1), {"memory_clock_mhz": None, "t_s": 2.0}]
+    n = len(samples)
+    for lo, hi in ((0, n), (1, 3), (4, 4), (-2, n + 4), (2, 7)):
+        want = binding_samples(samples[max(lo, 0):min(hi, n)])
+        got = _packnative.binding_samples(samples, lo, hi)
+        assert json.dumps(got) == json.dumps(want) and len(got) == len(want)
+    shared = _packnative.binding_samples(samples, 0, 2)
+    assert shared[0] is shared[1]                   # equal clocks: one entry object
+    with pytest.raises(AttributeError):
+        _packnative.binding_samples([3], 0, 1)
