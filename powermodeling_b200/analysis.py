@@ -221,11 +221,12 @@ def _host_treatment_issues(record, bench, config, device, epoch_status) -> list[
     if record.get("status") != "complete" or bench.get("error"):
         issues.append("benchmark_failed")
     sanity = bench.get("sanity") or {}
-    if isinstance(sanity, Mapping) and sanity.get("finite_output_sample") is False:
+    sanity_map = type(sanity) is dict or isinstance(sanity, Mapping)
+    if sanity_map and sanity.get("finite_output_sample") is False:
         issues.append("benchmark_output_sanity_failed")
     read_validation = bench.get("memory_read_validation") or {}
-    if ((isinstance(sanity, Mapping) and sanity.get("memory_read_sample_matches_reference") is False)
-            or (isinstance(read_validation, Mapping) and
+    if ((sanity_map and sanity.get("memory_read_sample_matches_reference") is False)
+            or ((type(read_validation) is dict or isinstance(read_validation, Mapping)) and
                 (read_validation.get("status") == "fail" or (finite(read_validation.get("mismatched_values")) or 0) > 0))):
         issues.append("memory_read_reference_mismatch")
     workload = record.get("workload")

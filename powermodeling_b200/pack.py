@@ -46,6 +46,8 @@ def finite(value) -> float | None:
 
 
 def nan_if_none(value) -> float:
+    if type(value) is float:               # the common case: no call into finite()
+        return value if math.isfinite(value) else NAN
     v = finite(value)
     return NAN if v is None else v
 
@@ -288,7 +290,7 @@ def pack_trials(records: list, host_flags: list, architectures: Mapping, native:
             slot = t * N.PM_PHASES + p
             phase = phases.get(name)
             raw = []
-            if phase and isinstance(phase, Mapping):
+            if phase and (type(phase) is dict or isinstance(phase, Mapping)):
                 present[slot] = 1
                 starts[slot] = nan_if_none(phase.get("start_s"))
                 ends[slot] = nan_if_none(phase.get("end_s"))
