@@ -296,17 +296,15 @@ def run_b200(args, rank: int, world: int) -> dict | None:
 
     def step(ev, side_ev):
         # The resample draws need only seeds and group sizes: drawn on a side
-        # stream while this rank's trials are analysed.  The analysis is
-        # enqueued first, so its CTAs take their SMs before the draws' CTAs
-        # fill what is left.
+        # stream while this rank's trials are analysed.
         ev[0].record(stream)
         side.wait_event(ev[0])
-        N.check(lib.pm_analyze_trials_device(trials, native_policy, results, C.c_void_p(scratch.data_ptr()), a_scr, sptr),
-                "analyze")
         side_ev[0].record(side)
         if G:
             N.check(lib.pm_bootstrap_prepare_device(job, boot_scratch, b_scr, side_ptr), "prepare")
         side_ev[1].record(side)
+        N.check(lib.pm_analyze_trials_device(trials, native_policy, results, C.c_void_p(scratch.data_ptr()), a_scr, sptr),
+                "analyze")
         ev[1].record(stream)
         stream.wait_event(side_ev[1])
         ev[2].record(stream)

@@ -32,7 +32,7 @@
 namespace pm {
 
 constexpr int kBootThreads = 256;
-constexpr int kPrepThreads = 576;       // the prepare pass: 256 twisting threads, then one per word pair of a block (312)
+constexpr int kPrepThreads = 320;       // the prepare pass: one thread per word pair of a block (312)
 constexpr int kMtN = 624, kMtM = 397;
 constexpr int kHistMaxN = 7;            // multiset histogram path
 constexpr int kMaxBins = 1716;          // C(13, 7)
@@ -280,33 +280,13 @@ __device__ __forceinline__ void generate_resamples(GenShared& sh, int n, int B, 
   __syncthreads();
 }
 
-// One twist of the state, words only (no tempering, no ring): the chain of
-// twist_block on threads t < 227, with no barrier.
-__device__ __forceinline__ void twist_words(const uint32_t* src, uint32_t* dst) {
-  constexpr int A = kMtN - kMtM;          // 227
-  const int t = threadIdx.x;
-  if (t < A) {
-    const uint32_t a = twist_one(src[t], src[t + 1], src[t + kMtM]);
-    const uint32_t b = twist_one(src[t + A], src[t + A + 1], a);
-    dst[t] = a;
-    dst[t + A] = b;
-    if (t < kMtN - 2 * A) {
-      const int i = t + 2 * A;
-      const uint32_t next = i < kMtN - 1 ? src[i + 1] : twist_one(src[0], src[1], src[kMtM]);
-      dst[i] = twist_one(src[i], next, b);
-    }
-  }
-}
-
 // The group's whole index stream (B n draws, one byte each) from the seeded
-// state in sh.mt_seed.  The generator's serial chain runs alone on the first
-// kTwisters threads: pass k twists state k - 1 into state k (the untempered
-// words of block k), while the next 312 threads each temper one word pair of
-// block k - 1 (the state that pass k reads, so it stays put until the barrier)
-// and store its draw index; then one barrier.  A draw never straddles two
-// blocks (624 is even), so draw d is pair d mod 312 of block d / 312.
-// Needs blockDim.x >= kTwisters + 312.  All threads call it.
-constexpr int kTwisters = 256;
+// state in sh.mt_seed, with nothing else in the generator's serial chain: each
+// pass twists block k into one half of the ring while the threads turn the
+// 312 word pairs of block k - 1 (the other half) into draw indices and store
+// them, then one barrier.  A draw never straddles two blocks (624 is even),
+// so draw d of the stream is pair d mod 312 of block d / 312.
+// Needs blockDim.x >= 312.  All threads call it.
 __device__ __forceinline__ void stream_draws(GenShared& sh, int n, int B, uint8_t* stream) {
   constexpr int kPairs = kMtN / 2;
   for (int i = threadIdx.x; i < kMtN; i += blockDim.x) sh.mt[0][i] = sh.mt_seed[i];
@@ -314,14 +294,13 @@ __device__ __forceinline__ void stream_draws(GenShared& sh, int n, int B, uint8_
   const double nd = (double)n;
   const uint32_t draws = (uint32_t)B * (uint32_t)n;
   const uint32_t blocks = (draws + kPairs - 1) / kPairs;
-  const int j = (int)threadIdx.x - kTwisters;                 // word pair of a drawing thread
+  const int j = threadIdx.x;
   for (uint32_t blk = 0; blk <= blocks; ++blk) {
-    const uint32_t* last = sh.mt[blk & 1];                    // state blk - 1: block blk - 1's words
-    if (j < 0) {
-      if (blk < blocks) twist_words(last, sh.mt[(blk & 1) ^ 1]);
-    } else if (blk > 0 && j < kPairs) {
-      const uint32_t d = (blk - 1) * kPairs + (uint32_t)j;
-      if (d < draws) stream[d] = (uint8_t)draw_index(temper(last[2 * j]), temper(last[2 * j + 1]), nd);
+    if (blk < blocks) twist_block<false>(sh.mt[blk & 1], sh.mt[(blk & 1) ^ 1], sh.ring, (int)(blk & 1) * kMtN);
+    if (blk > 0 && j < kPairs) {
+      const uint32_t d = (blk - 1) * kPairs + j;
+      const uint32_t* words = sh.ring + ((blk - 1) & 1) * kMtN;
+      if (d < draws) stream[d] = (uint8_t)draw_index(words[2 * j], words[2 * j + 1], nd);
     }
     __syncthreads();
   }
