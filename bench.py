@@ -851,7 +851,7 @@ def run_nonlinear_arms(sms: int, peaks: dict) -> dict:
 # seeds, so the counts are the same on every launch; None where not captured.
 NCU_PER_LAUNCH = {
     "analyze_kernel": {"inst": 22_774_000, "dram": 5_092_352},
-    "bootstrap_prepare_kernel": {"inst": 11_400_512, "dram": 52_736},
+    "bootstrap_prepare_kernel": {"inst": 10_013_759, "dram": 43_008},
     "bootstrap_kernel<0>": {"inst": 752_751, "dram": 188_672},
 }
 # Blackwell SM: four schedulers, each issuing one warp instruction per clock.
