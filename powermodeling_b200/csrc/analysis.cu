@@ -56,10 +56,20 @@ struct Shared {
   int32_t anchor_q;         // first covering sample flagged as energy anchor (INT32_MAX: none)
 };
 
+// A read of the trial batch, which no thread writes during the launch: through
+// the read-only path, so the compiler may issue it ahead of the shared-memory
+// stores around it instead of after them.
+template <class E>
+__device__ __forceinline__ E ro(const E* p) { return __ldg(p); }
+template <>
+__device__ __forceinline__ int64_t ro<int64_t>(const int64_t* p) {
+  return (int64_t)__ldg(reinterpret_cast<const long long*>(p));
+}
+
 // Sample i of a per-sample column; a broadcast column holds one element.
 template <class E>
 __device__ __forceinline__ E col_at(const E* col, uint32_t bit, const pm_trials& T, int64_t i) {
-  return (T.broadcast_columns & bit) ? col[0] : col[i];
+  return ro((T.broadcast_columns & bit) ? col : col + i);
 }
 
 // The PM_COL_* bit of a sample column (0: derived columns, never broadcast).
@@ -97,43 +107,43 @@ __device__ __noinline__ void measure_epochs(const pm_trials& T, const pm_policy&
                                EpochResult& r, int16_t* order) {
   r.n_inner = 0; r.issue = -1; r.start_s = r.end_s = dnan();
   r.ops = r.bytes = r.slots = dnan(); r.exact = 0;
-  const int status = T.epoch_status[trial * 2 + arm];
+  const int status = ro(T.epoch_status + (trial * 2 + arm));
   if (status == PM_EP_NONE || status == PM_EP_INVALID_LIST) return;
   if (none(phase_start) || none(phase_end)) { r.issue = 0; return; }
-  const int32_t b = T.epoch_offsets[trial * 2 + arm], e = T.epoch_offsets[trial * 2 + arm + 1];
+  const int32_t b = ro(T.epoch_offsets + (trial * 2 + arm)), e = ro(T.epoch_offsets + (trial * 2 + arm + 1));
   const int n = e - b;
   if (n < 0 || n > kMaxEpochs) { r.issue = 5; return; }   // the host entry points reject these lists first
   for (int k = 0; k < n; ++k) {
-    const double a = T.epoch_start_s[b + k], z = T.epoch_end_s[b + k];
+    const double a = ro(T.epoch_start_s + (b + k)), z = ro(T.epoch_end_s + (b + k));
     if (none(a) || none(z) || z <= a || a < phase_start - 1e-6 || z > phase_end + 1e-6) { r.issue = 1; return; }
-    const double ops = T.epoch_operations[b + k];
+    const double ops = ro(T.epoch_operations + (b + k));
     if (none(ops) || ops < 0) { r.issue = 2; return; }
-    const double bytes = T.epoch_logical_bytes[b + k];
+    const double bytes = ro(T.epoch_logical_bytes + (b + k));
     if (none(bytes) || bytes < 0) { r.issue = 3; return; }
   }
   if (status == PM_EP_NON_DICT_AFTER) { r.issue = 8; return; }
   // Stable insertion sort by start (Python's list.sort is stable).
   for (int k = 0; k < n; ++k) {
-    const double key = T.epoch_start_s[b + k];
+    const double key = ro(T.epoch_start_s + (b + k));
     int j = k - 1;
-    while (j >= 0 && T.epoch_start_s[b + order[j]] > key) { order[j + 1] = order[j]; --j; }
+    while (j >= 0 && ro(T.epoch_start_s + (b + order[j])) > key) { order[j + 1] = order[j]; --j; }
     order[j + 1] = (int16_t)k;
   }
   for (int k = 1; k < n; ++k)
-    if (T.epoch_start_s[b + order[k]] < T.epoch_end_s[b + order[k - 1]] - 1e-6) { r.issue = 4; return; }
+    if (ro(T.epoch_start_s + (b + order[k])) < ro(T.epoch_end_s + (b + order[k - 1])) - 1e-6) { r.issue = 4; return; }
   int first = -1, last = -1, kept = 0;
   for (int k = 0; k < n; ++k) {
     const int i = b + order[k];
-    if (T.epoch_start_s[i] >= phase_start + P.trim_s - 1e-6 && T.epoch_end_s[i] <= phase_end - P.trim_s + 1e-6) {
+    if (ro(T.epoch_start_s + (i)) >= phase_start + P.trim_s - 1e-6 && ro(T.epoch_end_s + (i)) <= phase_end - P.trim_s + 1e-6) {
       if (first < 0) first = k;
       last = k; ++kept;
     }
   }
-  if (kept == 0 || T.epoch_end_s[b + order[last]] - T.epoch_start_s[b + order[first]] < P.min_measure_s - 1e-6) {
+  if (kept == 0 || ro(T.epoch_end_s + (b + order[last])) - ro(T.epoch_start_s + (b + order[first])) < P.min_measure_s - 1e-6) {
     r.issue = 5; return;
   }
   NeumaierSum so, sb;
-  for (int k = 0; k < n; ++k) { so.add(T.epoch_operations[b + order[k]]); sb.add(T.epoch_logical_bytes[b + order[k]]); }
+  for (int k = 0; k < n; ++k) { so.add(ro(T.epoch_operations + (b + order[k]))); sb.add(ro(T.epoch_logical_bytes + (b + order[k]))); }
   const double counted_ops = so.result(), counted_bytes = sb.result();
   if (!none(whole_ops) && fabs(counted_ops - whole_ops) > fmax(fabs(whole_ops) * 1e-6, 1.0)) { r.issue = 6; return; }
   if (!none(whole_bytes) && fabs(counted_bytes - whole_bytes) > fmax(fabs(whole_bytes) * 1e-6, 1.0)) { r.issue = 7; return; }
@@ -144,13 +154,13 @@ __device__ __noinline__ void measure_epochs(const pm_trials& T, const pm_policy&
   int m = 0;
   for (int k = 0; k < n; ++k) {
     const int i = b + order[k];
-    if (!(T.epoch_start_s[i] >= phase_start + P.trim_s - 1e-6 && T.epoch_end_s[i] <= phase_end - P.trim_s + 1e-6)) continue;
-    if (m == 0) s0 = T.epoch_start_s[i];
-    s1 = T.epoch_end_s[i];
-    io.add(T.epoch_operations[i]); ib.add(T.epoch_logical_bytes[i]);
-    const double sl = T.epoch_loop_slots[i];
+    if (!(ro(T.epoch_start_s + (i)) >= phase_start + P.trim_s - 1e-6 && ro(T.epoch_end_s + (i)) <= phase_end - P.trim_s + 1e-6)) continue;
+    if (m == 0) s0 = ro(T.epoch_start_s + (i));
+    s1 = ro(T.epoch_end_s + (i));
+    io.add(ro(T.epoch_operations + (i))); ib.add(ro(T.epoch_logical_bytes + (i)));
+    const double sl = ro(T.epoch_loop_slots + (i));
     if (none(sl)) slots_ok = false; else is.add(sl);
-    exact = exact && T.epoch_counts_exact[i] != 0;
+    exact = exact && ro(T.epoch_counts_exact + (i)) != 0;
     order[m++] = order[k];   // compact kept indices in place (m <= k)
   }
   r.n_inner = m; r.start_s = s0; r.end_s = s1;
@@ -218,13 +228,21 @@ __device__ __noinline__ void phase_stats_impl(const pm_trials& T, const pm_polic
   const double inf = dinf();
   for (int q = threadIdx.x; q < SP; q += blockDim.x) {
     double* col = sortbuf;
-    col[C_GAP * SP + q] = (q < ncov - 1) ? t[cb + q + 1] - t[cb + q] : inf;
+    // every load of the sample first, then the stores
+    const bool gap = q < ncov - 1, selected = q < nsel;
+    const double ta = gap ? ro(t + cb + q) : 0.0, tb = gap ? ro(t + cb + q + 1) : 0.0;
+    double v[C_COUNT];
+#pragma unroll
+    for (int c = C_POWER; c < C_COUNT; ++c) {
+      v[c] = inf;
+      if (selected && !(T.broadcast_columns & column_bit(c))) v[c] = col_value(T, c, lo + q);
+    }
+    col[C_GAP * SP + q] = gap ? tb - ta : inf;
     col[C_CHANGE * SP + q] = inf;
+#pragma unroll
     for (int c = C_POWER; c < C_COUNT; ++c) {
       if (T.broadcast_columns & column_bit(c)) continue;   // one value for every sample: see the reductions
-      double v = inf;
-      if (q < nsel) { const double x = col_value(T, c, lo + q); if (!none(x)) v = x; }
-      col[c * SP + q] = v;
+      col[c * SP + q] = none(v[c]) ? inf : v[c];
     }
   }
   __syncthreads();
@@ -251,7 +269,7 @@ __device__ __noinline__ void phase_stats_impl(const pm_trials& T, const pm_polic
       if (change) {
         const int pos = before + __popc(ballot & ((1u << lane) - 1u));
         // store the change instant temporarily in the CHANGE column
-        sortbuf[C_CHANGE * SP + pos] = t[lo + q + 1];
+        sortbuf[C_CHANGE * SP + pos] = ro(t + lo + q + 1);
       }
       base += total;
       __syncthreads();
@@ -316,7 +334,8 @@ __device__ __noinline__ void phase_stats_impl(const pm_trials& T, const pm_polic
       const int64_t i = cb + q;
       const double pw = col_at(T.power_w, PM_COL_POWER_W, T, i);
       const uint16_t sf = col_at(T.sample_flags, PM_COL_SAMPLE_FLAGS, T, i);
-      st_t[q] = t[i]; st_p[q] = pw; st_m[q] = col_at(T.memory_power_w, PM_COL_MEMORY_POWER_W, T, i);
+      const double mp = col_at(T.memory_power_w, PM_COL_MEMORY_POWER_W, T, i);
+      st_t[q] = ro(t + i); st_p[q] = pw; st_m[q] = mp;
       if ((sf & PM_S_ENERGY_ANCHOR) && (uint32_t)q < anchor_q) anchor_q = (uint32_t)q;
       if (!none(pw) && pw < 0) neg_power = true;   // negative power is checked over the covering samples
       if (i < lo || i >= hi) continue;             // the rest concerns the selected samples
