@@ -410,21 +410,40 @@ def group_coalescing(valid: list) -> dict | None:
     return out
 
 
+def _median_of(numbers: list) -> float:
+    """statistics.median of a non-empty list of floats."""
+    numbers.sort()
+    n = len(numbers)
+    mid = n // 2
+    return numbers[mid] if n % 2 else (numbers[mid - 1] + numbers[mid]) / 2
+
+
 def _fold(values: list):
     """Repeat diagnostics as one: dicts key by key, lists as their distinct items, flags all-true,
     numbers by their median, anything else as the first present value."""
-    present = [v for v in values if v is not None]
-    first = present[0] if present else None
-    if isinstance(first, dict):
-        keys = dict.fromkeys(k for v in present if isinstance(v, dict) for k in v)
+    first = next((v for v in values if v is not None), None)
+    kind = type(first)
+    if kind is dict or isinstance(first, dict):
+        keys = dict.fromkeys(k for v in values if isinstance(v, dict) for k in v)
         return {k: _fold([v.get(k) if isinstance(v, dict) else None for v in values]) for k in keys}
-    if isinstance(first, list):
+    if kind is list or isinstance(first, list):
         import json
         return list({json.dumps(item, sort_keys=True): item for v in values if isinstance(v, list) for item in v}.values())
-    if isinstance(first, bool):
+    if kind is bool:
         return all(v is True for v in values)
-    numbers = [n for n in (finite(v) for v in values if isinstance(v, (int, float)) and not isinstance(v, bool)) if n is not None]
-    return _median(numbers) if numbers else first
+    if kind is str or first is None:
+        return first
+    numbers = []
+    for v in values:
+        t = type(v)
+        if t is float or t is int:
+            if math.isfinite(v):
+                numbers.append(float(v))
+        elif isinstance(v, (int, float)) and not isinstance(v, bool):
+            f = finite(v)
+            if f is not None:
+                numbers.append(f)
+    return _median_of(numbers) if numbers else first
 
 
 def group_diagnostics(valid: list, group: Mapping) -> dict:
