@@ -410,6 +410,24 @@ def _phase_dict(name: str, po: np.ndarray, flags: int, policy: AnalysisPolicy, p
     return out
 
 
+def _phase_index() -> tuple:
+    """Phase-row positions in the order _recordnative.phase_dicts takes them."""
+    L = _po_names()
+    scalars = ("START_S", "END_S", "DURATION_S", "MIDPOINT_S", "SAMPLES", "GAP_MEDIAN_S", "GAP_MAX_S", "ENERGY_J",
+               "INTEGRATED_POWER_W", "POWER_W", "MEMORY_ENERGY_J", "MEMORY_POWER_W", "COUNTER_J", "DISAGREEMENT",
+               "DISTINCT_POWER", "CHANGE_MEDIAN_S")
+    clocks = ("graphics_clock_mhz", "sm_clock_mhz", "memory_clock_mhz", "temperature_c")
+    return tuple(L[k] for k in scalars) + tuple(i for field in clocks for i in L[field])
+
+
+def _phase_dicts(views) -> list[dict]:
+    """_phase_dict of every (trial, phase) slot of a result batch, built natively in one call."""
+    from .trial_report import _record_native
+    missing, invalid, reset, issue_bits = _pf_bits()
+    return _record_native().phase_dicts(views.phase_out, views.phase_flags, views.PO, tuple(N.PHASE_NAMES),
+                                        _phase_index(), (missing, invalid, reset), issue_bits, _CADENCE_NOTE)
+
+
 def _gpu_uuid(record):
     config = dict(record.get("config") or {})
     device = record.get("device") or {}
@@ -470,7 +488,8 @@ def analyze_trials(records: Iterable[Mapping[str, Any]], policy: AnalysisPolicy 
     if _metrics_out is not None:
         _metrics_out.append((views.metrics.reshape(len(records), len(METRICS)).copy(), views.valid.copy()))
     TO = {name: N.layout("PM_TO_" + name) for name in _TO_NAMES}
-    po_rows, to_rows = _py_rows(views.phase_out, views.PO), _py_rows(views.trial_out, views.TO)
+    to_rows = _py_rows(views.trial_out, views.TO)
+    all_phases = _phase_dicts(views)
     policy_dict = asdict(policy)
     sel_lo, sel_hi = N.layout("PM_PO_SEL_LO"), N.layout("PM_PO_SEL_HI")
     out = []
@@ -487,11 +506,7 @@ def analyze_trials(records: Iterable[Mapping[str, Any]], policy: AnalysisPolicy 
         baseline_issues = _bits(ib[1], words[1])
         paired_issues = host_paired[i] + _bits(ib[2], words[2])
         warnings = _bits(ib[3], words[3])
-        phase_dicts = {}
-        for p, name in enumerate(N.PHASE_NAMES):
-            slot = i * N.PM_PHASES + p
-            po = views.phase_out[slot * views.PO:(slot + 1) * views.PO]
-            phase_dicts[name] = _phase_dict(name, po, int(views.phase_flags[slot]), policy, po_rows[slot])
+        phase_dicts = dict(zip(N.PHASE_NAMES, all_phases[i * N.PM_PHASES:(i + 1) * N.PM_PHASES]))
         other_pids = set()
         measure_slot = i * N.PM_PHASES + 1
         mpo = views.phase_out[measure_slot * views.PO:(measure_slot + 1) * views.PO]

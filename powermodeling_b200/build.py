@@ -43,6 +43,9 @@ MAIN = CSRC / "powerbench_main.cpp"
 # The record packer is a CPython extension (host C++, no CUDA).
 PACKER_SRC = CSRC / "python" / "packer.cpp"
 PACKER = PACKAGE / ("_packnative" + (sysconfig.get_config_var("EXT_SUFFIX") or ".so"))
+# The record assembly helpers: a second CPython extension (host C++).
+RECORDS_SRC = CSRC / "python" / "records.cpp"
+RECORDS = PACKAGE / ("_recordnative" + (sysconfig.get_config_var("EXT_SUFFIX") or ".so"))
 
 
 def _sources() -> list[Path]:
@@ -90,12 +93,13 @@ def build(verbose: bool = False, jobs: int | None = None) -> Path:
         if verbose:
             print(" ".join(exe), file=sys.stderr)
         _drain(subprocess.Popen(exe, stdout=subprocess.PIPE, stderr=subprocess.STDOUT, text=True))
-    if _stale(PACKER, PACKER_SRC, [INCLUDE / "pmb200.h"]):
-        ext = [shutil.which("g++") or "g++", "-std=c++17", "-O2", "-shared", "-fPIC", "-fvisibility=hidden",
-               "-I" + sysconfig.get_paths()["include"], "-I" + str(INCLUDE), str(PACKER_SRC), "-o", str(PACKER)]
-        if verbose:
-            print(" ".join(ext), file=sys.stderr)
-        _drain(subprocess.Popen(ext, stdout=subprocess.PIPE, stderr=subprocess.STDOUT, text=True))
+    for target, source in ((PACKER, PACKER_SRC), (RECORDS, RECORDS_SRC)):
+        if _stale(target, source, [INCLUDE / "pmb200.h"]):
+            ext = [shutil.which("g++") or "g++", "-std=c++17", "-O2", "-shared", "-fPIC", "-fvisibility=hidden",
+                   "-I" + sysconfig.get_paths()["include"], "-I" + str(INCLUDE), str(source), "-o", str(target)]
+            if verbose:
+                print(" ".join(ext), file=sys.stderr)
+            _drain(subprocess.Popen(ext, stdout=subprocess.PIPE, stderr=subprocess.STDOUT, text=True))
     return LIBRARY
 
 

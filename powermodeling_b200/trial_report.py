@@ -418,6 +418,15 @@ def _median_of(numbers: list) -> float:
     return numbers[mid] if n % 2 else (numbers[mid - 1] + numbers[mid]) / 2
 
 
+def _record_native():
+    try:
+        from . import _recordnative
+    except ImportError as exc:
+        from ._native import NativeError
+        raise NativeError("the record assembly extension (_recordnative) is not built; run powermodeling_b200.build") from exc
+    return _recordnative
+
+
 def _fold(values: list):
     """Repeat diagnostics as one: dicts key by key, lists as their distinct items, flags all-true,
     numbers by their median, anything else as the first present value."""
@@ -451,7 +460,7 @@ def group_diagnostics(valid: list, group: Mapping) -> dict:
     (analysis.py:567-595)."""
     if not valid:
         return {"schema_version": 1, "valid_repeats": 0, "aggregation": "no valid repeat diagnostics"}
-    folded = _fold([t["measurement_diagnostics"] for t in valid])
+    folded = _record_native().fold([t["measurement_diagnostics"] for t in valid], _fold)
     folded.update(schema_version=1, valid_repeats=len(valid),
                   aggregation="Each numeric diagnostic is the median of valid repeat diagnostics; reconstructed energy/work and scope factors are medians of per-repeat ratios, not ratios of separately aggregated powers/counts.")
     for objective, flag in (("operational_idle_increment", "idle_increment_eligible"),

@@ -1,0 +1,135 @@
+"""The native record assembly helpers (_recordnative) against their Python statements.
+
+fold: the group diagnostics' fold (trial_report._fold) on nested repeat diagnostics with
+every kind of leaf, missing keys, None repeats and values that take the Python path.
+phase_dicts: analysis._phase_dict over phase rows with random values, NaNs and flag words.
+"""
+from __future__ import annotations
+
+import json
+import math
+import random
+
+import numpy as np
+import pytest
+
+from powermodeling_b200 import _native as N
+from powermodeling_b200 import analysis as A
+from powermodeling_b200 import trial_report as TR
+
+
+def _same(a, b) -> bool:
+    """Equal values of equal types, key order included (NaN equals NaN)."""
+    if type(a) is not type(b):
+        return False
+    if isinstance(a, dict):
+        return list(a) == list(b) and all(_same(a[k], b[k]) for k in a)
+    if isinstance(a, list):
+        return len(a) == len(b) and all(_same(x, y) for x, y in zip(a, b))
+    if isinstance(a, float) and math.isnan(a) and math.isnan(b):
+        return True
+    return a == b
+
+
+class Weird(float):
+    """A float subclass: the fold hands such values to the Python statement."""
+
+
+def _leaf(rng: random.Random):
+    kind = rng.randrange(11)
+    if kind == 0:
+        return None
+    if kind == 1:
+        return rng.random() < 0.7
+    if kind == 2:
+        return rng.choice(["pass", "fail", "inconclusive"])
+    if kind == 3:
+        return rng.randrange(-5, 50)
+    if kind == 4:
+        return rng.choice([float("nan"), float("inf"), -0.0, 0.0])
+    if kind == 5:
+        return [rng.choice(["a", "b", "c", "d"]) for _ in range(rng.randrange(4))]
+    if kind == 6:
+        return [{"x": rng.randrange(3)}] if rng.random() < 0.5 else [1, "a"]
+    if kind == 7:
+        return Weird(rng.uniform(0, 10))
+    return rng.uniform(-1e3, 1e3)
+
+
+def _tree(rng: random.Random, depth: int, keys: list[str]):
+    if depth == 0 or rng.random() < 0.25:
+        return _leaf(rng)
+    return {k: _tree(rng, depth - 1, keys) for k in rng.sample(keys, rng.randrange(1, len(keys)))}
+
+
+def test_fold_equals_python_statement():
+    native = TR._record_native()
+    rng = random.Random(7)
+    keys = [f"k{i}" for i in range(7)]
+    for case in range(400):
+        repeats = rng.randrange(1, 6)
+        template = _tree(rng, 3, keys)
+        values = []
+        for _ in range(repeats):
+            if rng.random() < 0.1:
+                values.append(None)
+                continue
+            # repeats share their shape and mostly their kinds, as real diagnostics do
+            v = json.loads(json.dumps(template, default=float)) if isinstance(template, dict) else template
+            values.append(_tree(rng, 3, keys) if rng.random() < 0.3 else _perturb(rng, v))
+        assert _same(native.fold(values, TR._fold), TR._fold(values)), f"case {case}"
+
+
+def _perturb(rng, v):
+    if isinstance(v, dict):
+        out = {k: _perturb(rng, x) for k, x in v.items() if rng.random() > 0.1}
+        if rng.random() < 0.2:
+            out["extra"] = _leaf(rng)
+        return out
+    if isinstance(v, float):
+        return v * rng.uniform(0.5, 2.0) if math.isfinite(v) else v
+    if isinstance(v, bool) or v is None:
+        return v if rng.random() < 0.8 else _leaf(rng)
+    return v
+
+
+def test_fold_edge_cases():
+    native = TR._record_native()
+    cases = [[], [None], [None, None], [True, True], [True, None], [1, 2.5, None, True], [-0.0, 0.0],
+             [0.0, -0.0], [2 ** 80, 1], ["s", 1.0], [[], ["a"], ["a", "b"]], [{"a": 1}, None, {"b": [True]}],
+             [{"a": {"b": 1.0}}, {"a": None}], [float("nan"), float("inf")], [Weird(1.0), 2.0]]
+    for values in cases:
+        assert _same(native.fold(values, TR._fold), TR._fold(values)), values
+    with pytest.raises(OverflowError):
+        native.fold([10 ** 400, 1.0], TR._fold)
+
+
+def _phase_views(rng: np.random.Generator, n_trials: int):
+    views = A._Views(n_trials)
+    views.phase_out[:] = rng.uniform(-1e3, 1e3, views.phase_out.size)
+    views.phase_out[rng.random(views.phase_out.size) < 0.2] = np.nan
+    samples, distinct = A._po_names()["SAMPLES"], A._po_names()["DISTINCT_POWER"]
+    rows = views.phase_out.reshape(-1, views.PO)
+    rows[:, samples] = rng.integers(0, 400, len(rows))
+    rows[:, distinct] = rng.integers(0, 50, len(rows))
+    views.phase_flags[:] = rng.integers(0, 2 ** 31, views.phase_flags.size, dtype=np.int64).astype(np.uint32)
+    # mostly computed phases: clear the missing and invalid-window bits of most slots
+    missing, invalid, _, _ = A._pf_bits()
+    keep = rng.random(views.phase_flags.size) < 0.8
+    views.phase_flags[keep] &= np.uint32(~((1 << missing) | (1 << invalid)) & 0xFFFFFFFF)
+    return views
+
+
+def test_phase_dicts_equal_python_statement():
+    if not N.LIBRARY.exists():
+        pytest.skip("libpmb200 not built")
+    rng = np.random.default_rng(11)
+    views = _phase_views(rng, 40)
+    policy = A.AnalysisPolicy()
+    native = A._phase_dicts(views)
+    assert len(native) == 40 * N.PM_PHASES
+    for slot, got in enumerate(native):
+        name = N.PHASE_NAMES[slot % N.PM_PHASES]
+        po = views.phase_out[slot * views.PO:(slot + 1) * views.PO]
+        want = A._phase_dict(name, po, int(views.phase_flags[slot]), policy)
+        assert _same(got, want), (slot, got, want)
