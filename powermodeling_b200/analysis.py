@@ -691,7 +691,13 @@ def _binding(packed, trial, views):
     """The measure window's clock bindings, built by the native packer."""
     from .pack import _native_packer
     slot, window = _window(trial, 1, views)
-    return _native_packer().binding_samples(packed.samples[slot], *window) if window else []
+    if not window:
+        return []
+    if packed.clock_repeat is None:
+        return _native_packer().binding_samples(packed.samples[slot], *window)
+    offsets = packed.arrays["phase_offsets"]
+    repeat = memoryview(packed.clock_repeat)[int(offsets[slot]):int(offsets[slot + 1])]
+    return _native_packer().binding_samples(packed.samples[slot], *window, repeat)
 
 
 def _rail_sources(packed, trial, phases, views):

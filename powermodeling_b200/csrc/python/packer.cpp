@@ -340,7 +340,10 @@ struct OutColumns {
   int64_t *e_int, *throttle;
   uint16_t* flags;
   uint8_t* source;
+  uint8_t* clock_repeat;   // host only: 1 when a sample's clocks repeat the previous kept sample's
 };
+
+
 
 // Key of an exact str by content (-1: not one of ours, -2: not an exact str), with a pointer cache per worker.
 struct KeyCache {
@@ -370,6 +373,20 @@ bool compact_int(PyObject* v, int64_t* out) {
   if (!PyLong_CheckExact(v) || !PyUnstable_Long_IsCompact(reinterpret_cast<PyLongObject*>(v))) return false;
   *out = (int64_t)PyUnstable_Long_CompactValue(reinterpret_cast<PyLongObject*>(v));
   return true;
+}
+
+// Two telemetry values that read back as the same Python value: the same object, None and an
+// absent key, exact floats with the same bits, or exact compact ints of the same value.
+bool same_value(PyObject* a, PyObject* b) {
+  if (!a) a = Py_None;
+  if (!b) b = Py_None;
+  if (a == b) return true;
+  if (PyFloat_CheckExact(a) && PyFloat_CheckExact(b)) {
+    const double x = PyFloat_AS_DOUBLE(a), y = PyFloat_AS_DOUBLE(b);
+    return memcmp(&x, &y, sizeof x) == 0;
+  }
+  int64_t i, j;
+  return compact_int(a, &i) && compact_int(b, &j) && i == j;
 }
 
 // _finite on plain values: 1 finite (*out), 0 None/absent/bool/non-finite, -1 needs the object API.
@@ -452,6 +469,12 @@ bool fill_slot(SlotPlan& plan, PyObject* pid, KeyCache& cache, const OutColumns&
     const size_t row = (size_t)plan.base + k;
     PyObject** v = &plan.vals[(size_t)plan.order[k] * K_COUNT];
     c.t[row] = plan.t[k];
+    if (k == 0) {
+      c.clock_repeat[row] = 0;
+    } else {
+      PyObject** u = &plan.vals[(size_t)plan.order[k - 1] * K_COUNT];
+      c.clock_repeat[row] = same_value(v[K_GFX], u[K_GFX]) && same_value(v[K_MEM], u[K_MEM]) ? 1 : 0;
+    }
     for (int j = 0; j < 9; ++j) {
       double x;
       const int r = plain_finite(v[fields[j]], &x);
@@ -627,14 +650,14 @@ PyObject* pack(PyObject*, PyObject* args) {
     rows += m;
   }
   // The output columns, allocated once; pass two fills the fast slots' rows in parallel.
-  const char* names[15] = {"t_s", "power_w", "memory_power_w", "graphics_clock_mhz", "sm_clock_mhz", "memory_clock_mhz",
+  const char* names[16] = {"t_s", "power_w", "memory_power_w", "graphics_clock_mhz", "sm_clock_mhz", "memory_clock_mhz",
                            "temperature_c", "power_limit_w", "enforced_power_limit_w", "pstate", "energy_int",
-                           "energy_float", "throttle_reasons", "sample_flags", "memory_power_source"};
-  const size_t widths[15] = {8, 8, 8, 8, 8, 8, 8, 8, 8, 8, 8, 8, 8, 2, 1};
+                           "energy_float", "throttle_reasons", "sample_flags", "memory_power_source", "clock_repeat"};
+  const size_t widths[16] = {8, 8, 8, 8, 8, 8, 8, 8, 8, 8, 8, 8, 8, 2, 1, 1};
   PyObject* columns = PyDict_New();
   if (!columns) { release(); return nullptr; }
-  char* buf[15];
-  for (int j = 0; j < 15; ++j) {
+  char* buf[16];
+  for (int j = 0; j < 16; ++j) {
     PyObject* b = PyByteArray_FromStringAndSize(nullptr, (Py_ssize_t)(rows * widths[j]));
     if (!b || PyDict_SetItemString(columns, names[j], b) < 0) { Py_XDECREF(b); Py_DECREF(columns); release(); return nullptr; }
     Py_DECREF(b);
@@ -647,7 +670,7 @@ PyObject* pack(PyObject*, PyObject* args) {
                        reinterpret_cast<double*>(buf[8]), reinterpret_cast<double*>(buf[9]),
                        reinterpret_cast<double*>(buf[11]), reinterpret_cast<int64_t*>(buf[10]),
                        reinterpret_cast<int64_t*>(buf[12]), reinterpret_cast<uint16_t*>(buf[13]),
-                       reinterpret_cast<uint8_t*>(buf[14])};
+                       reinterpret_cast<uint8_t*>(buf[14]), reinterpret_cast<uint8_t*>(buf[15])};
   std::vector<Py_ssize_t> fast;
   for (Py_ssize_t i = 0; i < n; ++i)
     if (plans[(size_t)i].fast) fast.push_back(i);
@@ -690,6 +713,7 @@ PyObject* pack(PyObject*, PyObject* args) {
     put(out.mem, c.mem); put(out.temp, c.temp); put(out.plimit, c.plimit); put(out.enf, c.enf);
     put(out.pstate, c.pstate); put(out.e_float, c.e_float); put(out.e_int, c.e_int); put(out.throttle, c.throttle);
     put(out.flags, c.flags); put(out.source, c.source);
+    if (m) memset(out.clock_repeat + b, 0, m);    // these slots' bindings read every sample
   }
   g_last_fast_slots = (Py_ssize_t)std::count_if(plans.begin(), plans.end(), [](const SlotPlan& p) { return p.fast; });
   PyObject* counts = PyList_New(n);
@@ -755,10 +779,14 @@ PyObject* last_fast_slots(PyObject*, PyObject*) { return PyLong_FromSsize_t(g_la
 PyObject* binding_samples(PyObject*, PyObject* args) {
   PyObject* samples;
   Py_ssize_t lo, hi;
-  if (!PyArg_ParseTuple(args, "O!nn", &PyList_Type, &samples, &lo, &hi)) return nullptr;
+  Py_buffer repeat{};
+  if (!PyArg_ParseTuple(args, "O!nn|y*", &PyList_Type, &samples, &lo, &hi, &repeat)) return nullptr;
+  struct Release { Py_buffer* b; ~Release() { if (b->obj) PyBuffer_Release(b); } } release_repeat{&repeat};
   const Py_ssize_t n = PyList_GET_SIZE(samples);
   lo = lo < 0 ? 0 : lo > n ? n : lo;
   hi = hi < lo ? lo : hi > n ? n : hi;
+  // repeat[i] = 1: sample i's clocks read back as sample i-1's (the packer's clock_repeat column)
+  const uint8_t* rep = repeat.obj && repeat.len == n ? static_cast<const uint8_t*>(repeat.buf) : nullptr;
   static PyObject* k_phase = PyUnicode_InternFromString("phase");
   static PyObject* k_measure = PyUnicode_InternFromString("measure");
   static PyObject* k_gfx = PyUnicode_InternFromString("graphics_clock_mhz");
@@ -766,15 +794,14 @@ PyObject* binding_samples(PyObject*, PyObject* args) {
   if (!k_phase || !k_measure || !k_gfx || !k_mem) return nullptr;
   PyObject* out = PyList_New(hi - lo);
   if (!out) return nullptr;
-  // Consecutive samples usually hold the same clocks: an entry whose two values equal the
-  // previous entry's (same type, equal value) is that entry's dict object again.
+  // Consecutive samples usually hold the same clocks: an entry whose two values read back as
+  // the previous entry's (same_value) is that entry's dict object again.
   PyObject *last = nullptr, *last_gfx = nullptr, *last_mem = nullptr;
-  auto same = [](PyObject* a, PyObject* b) {
-    if (a == b) return 1;
-    if (!a || !b || Py_TYPE(a) != Py_TYPE(b) || !(PyLong_CheckExact(a) || PyFloat_CheckExact(a))) return 0;
-    return PyObject_RichCompareBool(a, b, Py_EQ);
-  };
   for (Py_ssize_t i = lo; i < hi; ++i) {
+    if (last && rep && rep[i]) {             // the previous entry's values, without reading the sample
+      PyList_SET_ITEM(out, i - lo, Py_NewRef(last));
+      continue;
+    }
     PyObject* s = PyList_GET_ITEM(samples, i);
     PyObject *gfx = nullptr, *mem = nullptr;
     if (PyDict_CheckExact(s)) {              // borrowed values of a plain dict
@@ -795,14 +822,7 @@ PyObject* binding_samples(PyObject*, PyObject* args) {
       return nullptr;
     }
     if (last) {
-      const int eg = same(gfx, last_gfx), em = eg == 1 ? same(mem, last_mem) : 0;
-      if (eg < 0 || em < 0) {
-        Py_DECREF(gfx);
-        Py_DECREF(mem);
-        Py_DECREF(out);
-        return nullptr;
-      }
-      if (eg == 1 && em == 1) {
+      if (same_value(gfx, last_gfx) && same_value(mem, last_mem)) {
         Py_DECREF(gfx);
         Py_DECREF(mem);
         PyList_SET_ITEM(out, i - lo, Py_NewRef(last));

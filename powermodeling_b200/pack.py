@@ -100,6 +100,7 @@ class Packed:
     samples: list = field(default_factory=list)       # per slot: sorted sample dicts (for host-side lists)
     foreign_pids: list = field(default_factory=list)  # per slot: list of (index, pids)
     broadcast: int = 0                                # PM_COL_* bits of the one-element columns
+    clock_repeat: bytes | bytearray | None = None    # per sample: 1 when its clocks read back as the previous sample's
 
 
 class _Columns:
@@ -264,6 +265,7 @@ def _pack_slots_native(slot_raw: list, slot_pid: list):
     columns, counts, slot_samples, slot_foreign = _native_packer().pack(slot_raw, slot_pid, _SOURCE_IDS)
     # views of the bytearrays the packer filled (no copy)
     arrays = {name: np.frombuffer(columns[name], dtype=dtype) for name, dtype in SAMPLE_COLUMNS}
+    arrays["clock_repeat"] = columns["clock_repeat"]
     return arrays, counts, slot_samples, slot_foreign
 
 
@@ -336,6 +338,7 @@ def pack_trials(records: list, host_flags: list, architectures: Mapping, native:
             flags |= N.T_ORDER_BA
         tflags[t] = flags
     sample_arrays, counts, slot_samples, slot_foreign = (_pack_slots_native if native else _pack_slots_python)(slot_raw, slot_pid)
+    clock_repeat = sample_arrays.pop("clock_repeat", None)   # host only (the Python packer leaves it out)
     np.cumsum(counts, out=offsets[1:])
     ns = int(offsets[-1])
     longest = max(counts, default=0)
@@ -352,7 +355,7 @@ def pack_trials(records: list, host_flags: list, architectures: Mapping, native:
         "trial_scalars": np.ascontiguousarray(scalars.reshape(-1)), "trial_flags": tflags,
     }
     broadcast = broadcast_constant_columns(arrays, ns)
-    return Packed(arrays, nt, ns, len(ep_rows), longest, slot_samples, slot_foreign, broadcast)
+    return Packed(arrays, nt, ns, len(ep_rows), longest, slot_samples, slot_foreign, broadcast, clock_repeat)
 
 
 def broadcast_constant_columns(arrays: dict, n_samples: int) -> int:

@@ -137,3 +137,47 @@ def test_fast_and_object_paths_number_sources_in_slot_order():
     from powermodeling_b200 import _packnative
     P.pack_trials(records, [0] * len(records), ARCHITECTURES, native=True)
     assert 0 < _packnative.last_fast_slots() < 5 * len(records)
+
+
+def _bits_equal(a, b) -> bool:
+    """Equal with types, float bits and key order (signed zeros and NaN payloads included)."""
+    import struct
+    if type(a) is not type(b):
+        return False
+    if isinstance(a, dict):
+        return list(a) == list(b) and all(_bits_equal(a[k], b[k]) for k in a)
+    if isinstance(a, list):
+        return len(a) == len(b) and all(_bits_equal(x, y) for x, y in zip(a, b))
+    if isinstance(a, float):
+        return struct.pack("<d", a) == struct.pack("<d", b)
+    return a == b
+
+
+def test_measure_bindings_from_the_clock_repeat_column():
+    """binding_samples with the packer's clock_repeat column equals the Python statement on clocks
+    that repeat, change kind (int 1 / float 1.0 / True), sign (0.0 / -0.0), go missing or None, or NaN."""
+    from powermodeling_b200.trial_report import binding_samples
+    rng = np.random.default_rng(5)
+    records = make_sweep(SweepShape(points=4, repeats=2), 9)
+    choices = [1410, 1410.0, 0.0, -0.0, None, "absent", float("nan"), True, 1, 1.0, 1980]
+    for record in records:
+        for phase in record["phases"].values():
+            run = None
+            for s in phase.get("samples", []):
+                if run is None or rng.random() < 0.15:
+                    run = (choices[rng.integers(len(choices))], choices[rng.integers(len(choices))])
+                for key, value in zip(("graphics_clock_mhz", "memory_clock_mhz"), run):
+                    if value == "absent":
+                        s.pop(key, None)
+                    else:
+                        s[key] = value
+    packed = P.pack_trials(records, [0] * len(records), ARCHITECTURES, native=True)
+    assert packed.clock_repeat is not None and len(packed.clock_repeat) == packed.n_samples
+    native = P._native_packer()
+    offsets = packed.arrays["phase_offsets"]
+    for slot, samples in enumerate(packed.samples):
+        repeat = memoryview(packed.clock_repeat)[int(offsets[slot]):int(offsets[slot + 1])]
+        for lo, hi in ((0, len(samples)), (3, len(samples) - 2), (len(samples) // 2, len(samples))):
+            got = native.binding_samples(samples, lo, hi, repeat)
+            assert _bits_equal(got, binding_samples(samples[lo:hi])), (slot, lo, hi)
+            assert _bits_equal(native.binding_samples(samples, lo, hi), got)
