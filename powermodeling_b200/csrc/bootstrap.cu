@@ -123,6 +123,10 @@ __device__ __forceinline__ int draw_index(uint32_t w0, uint32_t w1, double n) {
   const double r = ((double)(w0 >> 5) * 67108864.0 + (double)(w1 >> 6)) * (1.0 / 9007199254740992.0);
   return (int)floor(r * n);
 }
+// For n = 2^p (1 <= p <= 26) random() * n only rescales the 53-bit fraction, so
+// it is exact and floor(random() * n) is the top p bits of the first word:
+// w0 >> (32 - p).  pow2_shift(n) is that shift, or 0 when n is not such a power.
+__device__ __forceinline__ int pow2_shift(int n) { return n >= 2 && (n & (n - 1)) == 0 ? 33 - __ffs(n) : 0; }
 
 // Rank of a non-decreasing n-tuple over [0, n) among multisets (combinatorial
 // number system on b_i = a_i + i, strictly increasing in [0, 2n-1)).
@@ -292,6 +296,7 @@ __device__ __forceinline__ void stream_draws(GenShared& sh, int n, int B, uint8_
   for (int i = threadIdx.x; i < kMtN; i += blockDim.x) sh.mt[0][i] = sh.mt_seed[i];
   __syncthreads();
   const double nd = (double)n;
+  const int shift = pow2_shift(n);
   const uint32_t draws = (uint32_t)B * (uint32_t)n;
   const uint32_t blocks = (draws + kPairs - 1) / kPairs;
   const int j = threadIdx.x;
@@ -300,7 +305,8 @@ __device__ __forceinline__ void stream_draws(GenShared& sh, int n, int B, uint8_
     if (blk > 0 && j < kPairs) {
       const uint32_t d = (blk - 1) * kPairs + j;
       const uint32_t* words = sh.ring + ((blk - 1) & 1) * kMtN;
-      if (d < draws) stream[d] = (uint8_t)draw_index(words[2 * j], words[2 * j + 1], nd);
+      if (d < draws)
+        stream[d] = (uint8_t)(shift ? (int)(words[2 * j] >> shift) : draw_index(words[2 * j], words[2 * j + 1], nd));
     }
     __syncthreads();
   }
