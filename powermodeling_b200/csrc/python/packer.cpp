@@ -847,10 +847,159 @@ PyObject* binding_samples(PyObject*, PyObject* args) {
   return out;
 }
 
+// ---------------------------------------------------------------------------
+// epochs(arms, fallback) -> (status, counts, columns): the completion-epoch
+// lists of every (trial, arm) in one call, by the reference's parsing rules
+// (powermodeling/analysis.py:228-276 as powermodeling_b200/pack.py states
+// them in _epochs): the list under "measure_epochs" (else "work_epochs"),
+// None -> PM_EP_NONE, not a non-empty list -> PM_EP_INVALID_LIST, parsing
+// stops at the first item that is not a dict (PM_EP_NON_DICT_AFTER, the items
+// before it kept); start_s / end_s through _finite, else the host monotonic
+// (else plain) nanosecond stamps / 1e9; operations, logical_bytes and
+// reference_loop_slots NaN when not finite; counts_exact only when True.
+// An arm that is not an exact dict, or whose list or items are not exact
+// lists and dicts, is parsed by `fallback` (the Python statement), which
+// returns (status, [tuples]).
+namespace {
+
+PyObject* g_epoch_keys[11];
+enum { E_MEASURE, E_WORK, E_START_S, E_END_S, E_HOST_START, E_START_NS, E_HOST_END, E_END_NS, E_OPS, E_BYTES, E_SLOTS };
+
+// dict.get(key) of an exact dict, borrowed (NULL: absent); -1 on error.
+int dget(PyObject* d, int key, PyObject** out) {
+  *out = PyDict_GetItemWithError(d, g_epoch_keys[key]);
+  return (!*out && PyErr_Occurred()) ? -1 : 0;
+}
+
+// d.get(a, d.get(b)) as the reference writes it: the value under `a` when the key is present.
+int dget_or(PyObject* d, int a, int b, PyObject** out) {
+  if (dget(d, a, out) < 0) return -1;
+  if (*out) return 0;
+  return dget(d, b, out);
+}
+
+// One epoch time: _finite(seconds), else _finite(stamp) / 1e9, else NaN.
+int epoch_time(PyObject* epoch, int seconds, int host_ns, int plain_ns, double* out) {
+  PyObject* v;
+  double x;
+  if (dget(epoch, seconds, &v) < 0) return -1;
+  int r = finite(v, &x);
+  if (r < 0) return -1;
+  if (r) { *out = x; return 0; }
+  if (dget_or(epoch, host_ns, plain_ns, &v) < 0) return -1;
+  r = finite(v, &x);
+  if (r < 0) return -1;
+  *out = r ? x / 1e9 : kNaN;
+  return 0;
+}
+
+int epoch_value(PyObject* epoch, int key, double* out) {
+  PyObject* v;
+  double x;
+  if (dget(epoch, key, &v) < 0) return -1;
+  const int r = finite(v, &x);
+  if (r < 0) return -1;
+  *out = r ? x : kNaN;
+  return 0;
+}
+
+}  // namespace
+
+PyObject* epochs(PyObject*, PyObject* args) {
+  PyObject *arms, *fallback;
+  if (!PyArg_ParseTuple(args, "O!O", &PyList_Type, &arms, &fallback)) return nullptr;
+  static PyObject* k_exact = PyUnicode_InternFromString("counts_exact");
+  if (!k_exact) return nullptr;
+  if (!g_epoch_keys[0]) {
+    const char* names[11] = {"measure_epochs", "work_epochs", "start_s", "end_s", "host_monotonic_start_ns", "start_ns",
+                             "host_monotonic_end_ns", "end_ns", "operations", "logical_bytes", "reference_loop_slots"};
+    for (int i = 0; i < 11; ++i)
+      if (!(g_epoch_keys[i] = PyUnicode_InternFromString(names[i]))) return nullptr;
+  }
+  const Py_ssize_t n = PyList_GET_SIZE(arms);
+  std::vector<int32_t> status((size_t)n), counts((size_t)n);
+  std::vector<double> cols[5];
+  std::vector<uint8_t> exact;
+  auto push = [&](double a, double b, double ops, double bytes, double slots, bool ex) {
+    cols[0].push_back(a); cols[1].push_back(b); cols[2].push_back(ops); cols[3].push_back(bytes); cols[4].push_back(slots);
+    exact.push_back(ex ? 1 : 0);
+  };
+  for (Py_ssize_t i = 0; i < n; ++i) {
+    PyObject* bench = PyList_GET_ITEM(arms, i);
+    const size_t before = exact.size();
+    bool plain = PyDict_CheckExact(bench);
+    PyObject* source = nullptr;
+    if (plain && dget_or(bench, E_MEASURE, E_WORK, &source) < 0) return nullptr;
+    if (plain && source && source != Py_None && PyList_Check(source)) {
+      if (!PyList_CheckExact(source)) plain = false;
+      for (Py_ssize_t k = 0; plain && k < PyList_GET_SIZE(source); ++k) {
+        PyObject* e = PyList_GET_ITEM(source, k);
+        if (PyDict_Check(e) && !PyDict_CheckExact(e)) plain = false;
+        if (!PyDict_Check(e)) break;              // parsing stops here either way
+      }
+    }
+    if (!plain) {                                  // the Python statement for this arm
+      PyObject* r = PyObject_CallOneArg(fallback, bench);
+      if (!r) return nullptr;
+      PyObject *st = nullptr, *items = nullptr;
+      if (!PyArg_ParseTuple(r, "OO", &st, &items) || !PyList_Check(items)) {
+        Py_DECREF(r);
+        if (!PyErr_Occurred()) PyErr_SetString(PyExc_TypeError, "epoch fallback must return (status, list)");
+        return nullptr;
+      }
+      status[(size_t)i] = (int32_t)PyLong_AsLong(st);
+      for (Py_ssize_t k = 0; k < PyList_GET_SIZE(items); ++k) {
+        double v[5];
+        int ex = 0;
+        PyObject* t = PyList_GET_ITEM(items, k);
+        if (!PyArg_ParseTuple(t, "dddddp", &v[0], &v[1], &v[2], &v[3], &v[4], &ex)) { Py_DECREF(r); return nullptr; }
+        push(v[0], v[1], v[2], v[3], v[4], ex != 0);
+      }
+      Py_DECREF(r);
+      if (PyErr_Occurred()) return nullptr;
+      counts[(size_t)i] = (int32_t)(exact.size() - before);
+      continue;
+    }
+    if (!source || source == Py_None) { status[(size_t)i] = PM_EP_NONE; counts[(size_t)i] = 0; continue; }
+    if (!PyList_Check(source) || PyList_GET_SIZE(source) == 0) {
+      status[(size_t)i] = PM_EP_INVALID_LIST; counts[(size_t)i] = 0; continue;
+    }
+    int32_t st = PM_EP_OK;
+    for (Py_ssize_t k = 0; k < PyList_GET_SIZE(source); ++k) {
+      PyObject* e = PyList_GET_ITEM(source, k);
+      if (!PyDict_Check(e)) { st = PM_EP_NON_DICT_AFTER; break; }
+      double a, b, ops, bytes, slots;
+      if (epoch_time(e, E_START_S, E_HOST_START, E_START_NS, &a) < 0 ||
+          epoch_time(e, E_END_S, E_HOST_END, E_END_NS, &b) < 0 || epoch_value(e, E_OPS, &ops) < 0 ||
+          epoch_value(e, E_BYTES, &bytes) < 0 || epoch_value(e, E_SLOTS, &slots) < 0)
+        return nullptr;
+      PyObject* ex = PyDict_GetItemWithError(e, k_exact);
+      if (!ex && PyErr_Occurred()) return nullptr;
+      push(a, b, ops, bytes, slots, ex == Py_True);
+    }
+    status[(size_t)i] = st;
+    counts[(size_t)i] = (int32_t)(exact.size() - before);
+  }
+  auto bytes_of = [](const void* p, size_t nbytes) { return PyByteArray_FromStringAndSize(static_cast<const char*>(p), (Py_ssize_t)nbytes); };
+  PyObject* columns = PyTuple_New(6);
+  if (!columns) return nullptr;
+  for (int c = 0; c < 5; ++c) {
+    PyObject* b = bytes_of(cols[c].data(), cols[c].size() * sizeof(double));
+    if (!b) { Py_DECREF(columns); return nullptr; }
+    PyTuple_SET_ITEM(columns, c, b);
+  }
+  PyObject* b = bytes_of(exact.data(), exact.size());
+  if (!b) { Py_DECREF(columns); return nullptr; }
+  PyTuple_SET_ITEM(columns, 5, b);
+  return Py_BuildValue("(NNN)", bytes_of(status.data(), status.size() * 4), bytes_of(counts.data(), counts.size() * 4),
+                       columns);
+}
+
 PyMethodDef kMethods[] = {
     {"pack", pack, METH_VARARGS, "pack(slots, pids, source_ids) -> (columns, counts, sorted, foreign)"},
     {"last_fast_slots", last_fast_slots, METH_NOARGS, "slots the last pack() call packed on its parallel fast path"},
     {"binding_samples", binding_samples, METH_VARARGS, "binding_samples(samples, lo, hi) -> measure clock bindings"},
+    {"epochs", epochs, METH_VARARGS, "epochs(arms, fallback) -> (status, counts, columns) of every arm's epoch list"},
     {nullptr, nullptr, 0, nullptr}};
 
 PyModuleDef kModule = {PyModuleDef_HEAD_INIT, "_packnative",

@@ -206,6 +206,25 @@ def _epochs(bench: Mapping):
     return N.EP_OK, out
 
 
+def _epoch_columns_python(arms: list):
+    """(status per arm, epoch count per arm, the six epoch columns) by _epochs (the native parser's statement)."""
+    status, counts, rows = [], [], []
+    for source in arms:
+        st, r = _epochs(source)
+        status.append(st)
+        counts.append(len(r))
+        rows.extend(r)
+    columns = tuple(np.asarray([r[k] for r in rows], dtype=np.float64) for k in range(5))
+    columns += (np.asarray([r[5] for r in rows], dtype=np.uint8),)
+    return np.asarray(status, dtype=np.int32), np.asarray(counts, dtype=np.int32), columns
+
+
+def _epoch_columns_native(arms: list):
+    status, counts, columns = _native_packer().epochs(arms, _epochs)
+    cols = tuple(np.frombuffer(c, dtype=np.float64) for c in columns[:5]) + (np.frombuffer(columns[5], dtype=np.uint8),)
+    return np.frombuffer(status, dtype=np.int32), np.frombuffer(counts, dtype=np.int32), cols
+
+
 def tensor_flops_per_clock(record: Mapping, architectures: Mapping) -> float | None:
     """dense FLOP/SM/clock x SM count, or None when the reference's lookup would raise."""
     device = record.get("cuda_device") or record.get("device") or {}
@@ -281,10 +300,10 @@ def pack_trials(records: list, host_flags: list, architectures: Mapping, native:
     present = np.zeros(nt * N.PM_PHASES, dtype=np.uint8)
     ep_off = np.zeros(nt * 2 + 1, dtype=np.int32)
     ep_status = np.zeros(nt * 2, dtype=np.int32)
-    ep_rows = []
     scalars = np.full((nt, N.TS_COUNT), NAN)
     tflags = np.zeros(nt, dtype=np.uint32)
     slot_raw, slot_pid = [], []
+    arms = []                                        # per (trial, arm): the mapping holding its epoch list
     for t, record in enumerate(records):
         phases = phase_records(record)
         pid = (record.get("quality") or {}).get("measurement_pid")
@@ -301,11 +320,8 @@ def pack_trials(records: list, host_flags: list, architectures: Mapping, native:
             slot_pid.append(pid)
         bench = record.get("benchmark") or record.get("result") or {}
         reference = record.get("active_reference") or {}
-        for arm, source in enumerate((bench, reference)):
-            status, rows = _epochs(source)
-            ep_status[t * 2 + arm] = status
-            ep_rows.extend(rows)
-            ep_off[t * 2 + arm + 1] = len(ep_rows)
+        arms.append(bench)
+        arms.append(reference)
         config = dict(record.get("config") or {})
         device = record.get("device") or {}
         sc = scalars[t]
@@ -337,6 +353,9 @@ def pack_trials(records: list, host_flags: list, architectures: Mapping, native:
         elif protocol.get("order") == "BA":
             flags |= N.T_ORDER_BA
         tflags[t] = flags
+    epochs = _epoch_columns_native(arms) if native else _epoch_columns_python(arms)
+    ep_status[:] = epochs[0]
+    np.cumsum(epochs[1], out=ep_off[1:])
     sample_arrays, counts, slot_samples, slot_foreign = (_pack_slots_native if native else _pack_slots_python)(slot_raw, slot_pid)
     clock_repeat = sample_arrays.pop("clock_repeat", None)   # host only (the Python packer leaves it out)
     np.cumsum(counts, out=offsets[1:])
@@ -346,16 +365,12 @@ def pack_trials(records: list, host_flags: list, architectures: Mapping, native:
         "phase_offsets": offsets, "phase_start_s": starts, "phase_end_s": ends, "phase_present": present,
         **sample_arrays,
         "epoch_offsets": ep_off, "epoch_status": ep_status,
-        "epoch_start_s": np.asarray([r[0] for r in ep_rows], dtype=np.float64),
-        "epoch_end_s": np.asarray([r[1] for r in ep_rows], dtype=np.float64),
-        "epoch_operations": np.asarray([r[2] for r in ep_rows], dtype=np.float64),
-        "epoch_logical_bytes": np.asarray([r[3] for r in ep_rows], dtype=np.float64),
-        "epoch_loop_slots": np.asarray([r[4] for r in ep_rows], dtype=np.float64),
-        "epoch_counts_exact": np.asarray([r[5] for r in ep_rows], dtype=np.uint8),
+        "epoch_start_s": epochs[2][0], "epoch_end_s": epochs[2][1], "epoch_operations": epochs[2][2],
+        "epoch_logical_bytes": epochs[2][3], "epoch_loop_slots": epochs[2][4], "epoch_counts_exact": epochs[2][5],
         "trial_scalars": np.ascontiguousarray(scalars.reshape(-1)), "trial_flags": tflags,
     }
     broadcast = broadcast_constant_columns(arrays, ns)
-    return Packed(arrays, nt, ns, len(ep_rows), longest, slot_samples, slot_foreign, broadcast, clock_repeat)
+    return Packed(arrays, nt, ns, int(ep_off[-1]), longest, slot_samples, slot_foreign, broadcast, clock_repeat)
 
 
 def broadcast_constant_columns(arrays: dict, n_samples: int) -> int:

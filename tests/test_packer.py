@@ -181,3 +181,32 @@ def test_measure_bindings_from_the_clock_repeat_column():
             got = native.binding_samples(samples, lo, hi, repeat)
             assert _bits_equal(got, binding_samples(samples[lo:hi])), (slot, lo, hi)
             assert _bits_equal(native.binding_samples(samples, lo, hi), got)
+
+
+class EpochDict(dict):
+    pass
+
+
+def test_epoch_lists_native_equal_python_statement():
+    """Every arm shape the reference's epoch parsing distinguishes: absent, None, empty, not a list,
+    measure_epochs over work_epochs (a present None included), nanosecond stamps, non-finite and
+    non-numeric values, a non-dict item that stops parsing, and subclasses (the Python path)."""
+    ep = lambda **kw: dict({"start_s": 1.0, "end_s": 2.0, "operations": 10, "logical_bytes": 4.5,
+                            "reference_loop_slots": None, "counts_exact": True}, **kw)
+    arms = [
+        {}, {"measure_epochs": None}, {"measure_epochs": []}, {"measure_epochs": (ep(),)}, {"measure_epochs": "x"},
+        {"work_epochs": [ep(), ep(start_s=3.0)]}, {"measure_epochs": None, "work_epochs": [ep()]},
+        {"measure_epochs": [ep(start_s=None, host_monotonic_start_ns=5e9, end_s="bad", end_ns=7_000_000_000)]},
+        {"measure_epochs": [ep(start_s=float("nan"), start_ns=True, end_s=float("inf"), host_monotonic_end_ns=None)]},
+        {"measure_epochs": [ep(operations="12", logical_bytes=float("inf"), counts_exact=1)]},
+        {"measure_epochs": [ep(), 3, ep()]}, {"measure_epochs": [ep(counts_exact=False), ep(reference_loop_slots=2 ** 70)]},
+        {"measure_epochs": [EpochDict(ep()), ep()]}, EpochDict({"measure_epochs": [ep()]}),
+        {"measure_epochs": [ep(start_s=True, end_s=False)]},
+    ]
+    a = P._epoch_columns_native(arms)
+    b = P._epoch_columns_python(arms)
+    assert np.array_equal(a[0], b[0]) and np.array_equal(a[1], b[1])
+    for x, y in zip(a[2], b[2]):
+        assert x.dtype == y.dtype and np.array_equal(x.view(np.uint8), y.view(np.uint8))
+    with pytest.raises(OverflowError):
+        P._epoch_columns_native([{"measure_epochs": [ep(operations=10 ** 400)]}])
