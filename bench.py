@@ -286,55 +286,73 @@ def run_b200(args, rank: int, world: int) -> dict | None:
                          d_seeds.data_ptr(), group_out[0].data_ptr(), group_out[1].data_ptr(), group_out[2].data_ptr())
     a_scr = lib.pm_analyze_scratch_bytes(n, packed.max_phase_samples)
     b_scr = lib.pm_bootstrap_scratch_bytes(max(1, G), max_members, RESAMPLES)
-    scratch = torch.empty(max(1, a_scr + b_scr), dtype=torch.uint8, device="cuda")
+    sweep_scr = lib.pm_analyze_sweep_scratch_bytes(n, packed.max_phase_samples, G, max_members, RESAMPLES)
+    scratch = torch.empty(max(1, a_scr + b_scr, sweep_scr), dtype=torch.uint8, device="cuda")
     flush = torch.empty(256 * 1024 * 1024 // 4, dtype=torch.float32, device="cuda")
     stream = torch.cuda.current_stream()
     side = torch.cuda.Stream()
     sptr, side_ptr = C.c_void_p(stream.cuda_stream), C.c_void_p(side.cuda_stream)
     boot_scratch = C.c_void_p(scratch.data_ptr() + a_scr)
     native_policy = policy.native()
+    scratch_ptr, scratch_bytes = C.c_void_p(scratch.data_ptr()), scratch.numel()
 
-    def step(ev, side_ev):
-        # The resample draws need only seeds and group sizes: drawn on a side
-        # stream while this rank's trials are analysed.
+    def step(ev):
+        # One call per step: the library forks the draws onto its side stream
+        # beside the analysis, joins them and runs the finish (with the group
+        # gather's peer stores when it is on); rank 0 then waits for every
+        # rank's arrival flag of the step, or the ranks all-gather over NCCL.
         ev[0].record(stream)
-        side.wait_event(ev[0])
-        side_ev[0].record(side)
-        if G:
-            N.check(lib.pm_bootstrap_prepare_device(job, boot_scratch, b_scr, side_ptr), "prepare")
-        side_ev[1].record(side)
-        N.check(lib.pm_analyze_trials_device(trials, native_policy, results, C.c_void_p(scratch.data_ptr()), a_scr, sptr),
-                "analyze")
-        ev[1].record(stream)
-        stream.wait_event(side_ev[1])
-        ev[2].record(stream)
         if peer:
             px.next_epoch()
-            N.check(lib.pm_bootstrap_finish_device_exchange(job, boot_scratch, b_scr, C.byref(px.groups), sptr),
-                    "finish + group gather")
-        elif G:
-            N.check(lib.pm_bootstrap_finish_device(job, boot_scratch, b_scr, sptr), "finish")
-        ev[3].record(stream)
+        N.check(lib.pm_analyze_sweep_device(trials, native_policy, results, job, scratch_ptr, scratch_bytes,
+                                            C.byref(px.groups) if peer else None, sptr), "pm_analyze_sweep_device")
         if peer:
             if rank == 0:
                 px.wait_groups(stream.cuda_stream)
         elif world > 1:
             dist.all_gather_into_tensor(all_group_out, group_out)
-        ev[4].record(stream)
-
-    def new_events(k):
-        return ([[torch.cuda.Event(enable_timing=True) for _ in range(5)] for _ in range(k)],
-                [[torch.cuda.Event(enable_timing=True) for _ in range(2)] for _ in range(k)])
+        ev[1].record(stream)
 
     def run_steps(k):
         """k steps enqueued back to back (L2 flushed before each, outside its events); no host wait between them."""
-        evs, side_evs = new_events(k)
+        evs = [[torch.cuda.Event(enable_timing=True) for _ in range(2)] for _ in range(k)]
         if peer:
             px.gate(stream.cuda_stream)                 # every rank's GPU starts the steps together
         for i in range(k):
             flush.zero_()
-            step(evs[i], side_evs[i])
-        return evs, side_evs
+            step(evs[i])
+        return evs
+
+    def breakdown(k):
+        """Per-kernel times of k further steps through the separate entry points, each step
+        enqueued whole before the GPU reaches it (a synchronize, then the L2 flush, ahead of it):
+        the analysis, the draws on the side stream beside it, the join and the finish."""
+        parts = {"analyze": [], "prepare": [], "join": [], "finish": []}
+        for _ in range(k):
+            torch.cuda.synchronize()
+            flush.zero_()
+            ev = [torch.cuda.Event(enable_timing=True) for _ in range(4)]
+            sev = [torch.cuda.Event(enable_timing=True) for _ in range(2)]
+            ev[0].record(stream)
+            side.wait_event(ev[0])
+            sev[0].record(side)
+            if G:
+                N.check(lib.pm_bootstrap_prepare_device(job, boot_scratch, b_scr, side_ptr), "prepare")
+            sev[1].record(side)
+            N.check(lib.pm_analyze_trials_device(trials, native_policy, results, C.c_void_p(scratch.data_ptr()), a_scr,
+                                                 sptr), "analyze")
+            ev[1].record(stream)
+            stream.wait_event(sev[1])
+            ev[2].record(stream)
+            if G:
+                N.check(lib.pm_bootstrap_finish_device(job, boot_scratch, b_scr, sptr), "finish")
+            ev[3].record(stream)
+            torch.cuda.synchronize()
+            parts["analyze"].append(ev[0].elapsed_time(ev[1]))
+            parts["prepare"].append(sev[0].elapsed_time(sev[1]))
+            parts["join"].append(ev[1].elapsed_time(ev[2]))
+            parts["finish"].append(ev[2].elapsed_time(ev[3]))
+        return {k: statistics.median(v) for k, v in parts.items()}
 
     if world > 1:
         torch.cuda.synchronize()
@@ -388,7 +406,7 @@ def run_b200(args, rank: int, world: int) -> dict | None:
     if clocks:
         clocks.mark_begin()
     begin = time.monotonic()
-    evs, side_evs = run_steps(args.steps)
+    evs = run_steps(args.steps)
     torch.cuda.synchronize()
     end = time.monotonic()
     if clocks:
@@ -406,13 +424,8 @@ def run_b200(args, rank: int, world: int) -> dict | None:
                           sm_mhz=watched["sm_mhz"], sm_mhz_min=watched["sm_mhz_min"],
                           reasons=sorted(set(watched["reasons"]) | set((clock_info or {}).get("reasons") or [])),
                           samples=watched["samples"], source=watched["source"])
-    parts_ms = {"analyze": [], "join": [], "finish": [], "gather_groups": []}
-    prepare_ms, step_ms = [], []
-    for ev, side_ev in zip(evs, side_evs):
-        for k, name in enumerate(parts_ms):
-            parts_ms[name].append(ev[k].elapsed_time(ev[k + 1]))
-        prepare_ms.append(side_ev[0].elapsed_time(side_ev[1]))
-        step_ms.append(ev[0].elapsed_time(ev[4]))
+    step_ms = [ev[0].elapsed_time(ev[1]) for ev in evs]
+    parts = breakdown(50)                               # untimed: the kernels of the step one by one
     if world > 1:
         dist.barrier()
     total_ms = sum(step_ms)
@@ -427,7 +440,6 @@ def run_b200(args, rank: int, world: int) -> dict | None:
         dist.all_reduce(sizes)
         n_total, g_total = int(sizes[0].item()), int(sizes[1].item())
     value = resamples_per_step / (ms_per_step / 1e3)
-    t_analyze, t_finish = parts_ms["analyze"], parts_ms["finish"]
 
     # ---- end to end ------------------------------------------------------------------------------
     # e2e: the drop-in call itself, summarize(records) (analysis.py:1400), on the runner's record
@@ -494,7 +506,7 @@ def run_b200(args, rank: int, world: int) -> dict | None:
     if rank != 0:
         return None
     peaks = measured_peaks()
-    a_ms, f_ms, p_ms = statistics.mean(t_analyze), statistics.mean(t_finish), statistics.mean(prepare_ms)
+    a_ms, f_ms, p_ms = parts["analyze"], parts["finish"], parts["prepare"]
     roofline = roofline_entry(a_ms, p_ms, f_ms, in_bytes, out_bytes, G, M, packed, peaks,
                               (clock_info or {}).get("sm_mhz"))
     line = {"metric": METRIC, "value": value, "unit": "resamples/s", "n_gpus": world, "steps": args.steps,
@@ -516,13 +528,13 @@ def run_b200(args, rank: int, world: int) -> dict | None:
             "e2e_c_abi": {"value": resamples_per_step / c_abi_s, "unit": "resamples/s", "h2d_bytes_per_step": int(c_h2d),
                           "d2h_bytes_per_step": int(c_d2h), "ms_per_step": c_abi_s * 1e3,
                           "call": "pm_analyze_sweep on packed host arrays"},
-            # per step: analyze, the draws and the finish, plus rank 0's arrival wait of the peer gather
-            "gpu_launches": 3 * args.steps + (args.steps if peer else 0),
-            "kernels": {"analyze_kernel_ms": a_ms,
-                        "bootstrap_prepare_kernel_ms (side stream, overlaps analyze)": p_ms,
-                        "join_wait_ms": statistics.mean(parts_ms["join"]),
-                        "bootstrap_finish_kernel_ms": f_ms,
-                        "gather_groups_ms (rank 0)": statistics.mean(parts_ms["gather_groups"])},
+            # per step: the draws, the analysis and the finish, plus rank 0's arrival wait of the peer
+            # gather (and the start gate once)
+            "gpu_launches": 3 * args.steps + ((args.steps if rank == 0 else 0) + 1 if peer else 0),
+            "kernels": {"source": "50 further steps, each enqueued whole before it runs (medians)",
+                        "analyze_kernel_ms": a_ms,
+                        "bootstrap_prepare_kernel_ms (side stream, overlaps the analysis)": p_ms,
+                        "join_wait_ms": parts["join"], "bootstrap_finish_kernel_ms": f_ms},
             "roofline": roofline, "clocks": clock_info}
     if world > 1:
         line["exchange"] = "nvlink-peer" if peer else "nccl"

@@ -184,7 +184,9 @@ int32_t pm_device_count(void);
  * Staging and device workspaces are owned by the library (grow-only, per device). */
 int pm_analyze_trials(const pm_trials* trials, const pm_policy* policy, pm_trial_results* out);
 /* Bytes of device scratch pm_analyze_trials_device needs for phases longer
- * than the shared-memory tile (2047 samples); 0 when none is needed. */
+ * than the shared-memory tile (1023 samples); 0 when none is needed.  Device
+ * scratch passed to the analysis and bootstrap entry points is 16-byte
+ * aligned (the sweep's, pm_analyze_sweep_device, 256-byte aligned). */
 size_t pm_analyze_scratch_bytes(int32_t n_trials, int32_t max_phase_samples);
 /* Same as pm_analyze_trials with every pointer in device memory, enqueued on
  * `stream`; trials->max_phase_samples must bound every segment. */
@@ -248,6 +250,27 @@ int pm_bootstrap_finish_device(const pm_bootstrap_job* job, void* scratch, size_
  */
 int pm_analyze_sweep(const pm_trials* trials, const pm_policy* policy, pm_trial_results* out,
                      pm_bootstrap_job* groups);
+
+/*
+ * The same sweep on device buffers, stream-ordered on `stream`: the groups'
+ * draws on the library's own side stream (forked from and joined back to
+ * `stream`), beside the trial analysis, then the groups' medians and
+ * intervals.  The job's values and member_valid are normally out->metrics and
+ * out->valid (the groups read the analysis's rows; the finish is ordered after
+ * it).  `exchange` (NULL: none; pmb200_peer.h) also stores every group's
+ * result into the receiving ranks' gathered tables, as
+ * pm_bootstrap_finish_device_exchange does.  One call instead of the
+ * analysis, prepare and finish calls: no counterpart in the reference (its
+ * summarize is one host call, analysis.py:1400-1470).  Scratch: at least
+ * pm_analyze_sweep_scratch_bytes (the analysis's, then the bootstrap's at the
+ * next 256-byte boundary).
+ */
+struct pm_peer_groups;
+size_t pm_analyze_sweep_scratch_bytes(int32_t n_trials, int32_t max_phase_samples, int32_t n_groups,
+                                      int32_t max_members, int32_t resamples);
+int pm_analyze_sweep_device(const pm_trials* trials, const pm_policy* policy, pm_trial_results* out,
+                            const pm_bootstrap_job* groups, void* scratch, size_t scratch_bytes,
+                            const struct pm_peer_groups* exchange, void* stream);
 
 /*
  * The measured-workload engine behind the powerbench command line

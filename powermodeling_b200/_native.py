@@ -162,6 +162,10 @@ def library() -> C.CDLL:
             lib.pm_bootstrap_scratch_bytes.argtypes = [C.c_int32, C.c_int32, C.c_int32]
             lib.pm_analyze_sweep.argtypes = [C.POINTER(Trials), C.POINTER(Policy), C.POINTER(TrialResults),
                                              C.POINTER(BootstrapJob)]
+            lib.pm_analyze_sweep_scratch_bytes.restype = C.c_size_t
+            lib.pm_analyze_sweep_scratch_bytes.argtypes = [C.c_int32] * 5
+            lib.pm_analyze_sweep_device.argtypes = [C.POINTER(Trials), C.POINTER(Policy), C.POINTER(TrialResults),
+                                                    C.POINTER(BootstrapJob), _p, C.c_size_t, _p, _p]
             lib.pm_resample_indices.argtypes = [C.c_uint64, C.c_int32, C.c_int32, C.POINTER(C.c_int32)]
             lib.pm_peer_alloc.argtypes = [C.c_size_t, C.POINTER(_p), C.POINTER(PeerHandle)]
             lib.pm_peer_free.argtypes = [_p]

@@ -280,6 +280,8 @@ int pm_analyze_trials_device(const pm_trials* trials, const pm_policy* policy, p
   const size_t need = analyze_scratch_bytes(trials->n_trials, trials->max_phase_samples);
   if (need > scratch_bytes || (need && !scratch))
     return fail(PM_E_INVALID, "analysis needs %zu bytes of device scratch, got %zu", need, scratch_bytes);
+  if (need && reinterpret_cast<uintptr_t>(scratch) % 16)
+    return fail(PM_E_INVALID, "the analysis's device scratch must be 16-byte aligned");
   launch_analyze(*trials, *policy, *out, trials->max_phase_samples, need ? (double*)scratch : nullptr, (cudaStream_t)stream, nullptr);
   cudaError_t e = cudaGetLastError();
   if (e != cudaSuccess) return cuda_fail(e, "analyze_kernel launch");
@@ -302,6 +304,8 @@ int pm_analyze_trials_device_exchange(const pm_trials* trials, const pm_policy* 
   const size_t need = analyze_scratch_bytes(trials->n_trials, trials->max_phase_samples);
   if (need > scratch_bytes || (need && !scratch))
     return fail(PM_E_INVALID, "analysis needs %zu bytes of device scratch, got %zu", need, scratch_bytes);
+  if (need && reinterpret_cast<uintptr_t>(scratch) % 16)
+    return fail(PM_E_INVALID, "the analysis's device scratch must be 16-byte aligned");
   launch_analyze(*trials, *policy, *out, trials->max_phase_samples, need ? (double*)scratch : nullptr, (cudaStream_t)stream,
                  nullptr, rows);
   cudaError_t e = cudaGetLastError();
@@ -510,6 +514,8 @@ size_t pm_bootstrap_scratch_bytes(int32_t n_groups, int32_t max_members, int32_t
 static int device_boot_args(const pm_bootstrap_job* job, void* scratch, size_t scratch_bytes, BootArgs* out) {
   int rc = check_bootstrap(job);
   if (rc) return rc;
+  if (reinterpret_cast<uintptr_t>(scratch) % 16)
+    return fail(PM_E_INVALID, "the bootstrap's device scratch must be 16-byte aligned");
   int device = 0;
   if ((rc = current_device(&device))) return rc;
   if (prepare_bootstrap_constants(device)) return fail(PM_E_CUDA, "bootstrap constants upload failed");
@@ -563,6 +569,86 @@ int pm_bootstrap_finish_device_exchange(const pm_bootstrap_job* job, void* scrat
   if (groups->per_rank < A.n_groups) return fail(PM_E_INVALID, "per_rank below this rank's group count");
   launch_bootstrap(A, (cudaStream_t)stream, groups);
   cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) return cuda_fail(e, "bootstrap_kernel launch");
+  return PM_OK;
+}
+
+// The device sweep's own side stream and fork/join events, one set per device
+// (created on first use with that device current); the mutex keeps one call's
+// record/wait pairs together when several host threads call at once.
+struct SweepFork {
+  cudaStream_t side = nullptr;
+  cudaEvent_t fork = nullptr, join = nullptr;
+  std::mutex lock;
+};
+static SweepFork g_sweep_fork[kMaxDevices];
+
+size_t pm_analyze_sweep_scratch_bytes(int32_t n_trials, int32_t max_phase_samples, int32_t n_groups,
+                                      int32_t max_members, int32_t resamples) {
+  if (n_trials < 0 || max_phase_samples < 0 || n_groups < 0 || max_members < 0 || resamples < 0) return 0;
+  return align256(analyze_scratch_bytes(n_trials, max_phase_samples)) +
+         bootstrap_scratch_bytes(n_groups, max_members, resamples);
+}
+
+int pm_analyze_sweep_device(const pm_trials* trials, const pm_policy* policy, pm_trial_results* out,
+                            const pm_bootstrap_job* groups, void* scratch, size_t scratch_bytes,
+                            const pm_peer_groups* exchange, void* stream) {
+  if (!trials || !policy || !out || !groups) return fail(PM_E_INVALID, "NULL argument");
+  if (trials->n_trials < 0 || trials->max_phase_samples < 0) return fail(PM_E_INVALID, "negative size");
+  if (trials->broadcast_columns & ~uint32_t(PM_COL_ALL)) return fail(PM_E_INVALID, "broadcast_columns has unknown bits");
+  if (trials->max_phase_samples > kMaxPhaseSamples) return fail(PM_E_LIMIT, "max_phase_samples beyond %d", kMaxPhaseSamples);
+  if (policy->min_samples < 2) return fail(PM_E_INVALID, "min_samples must be >= 2");
+  if (exchange) {
+    if (exchange->n_ranks < 1 || exchange->n_ranks > PM_MAX_RANKS || exchange->rank < 0 || exchange->rank >= exchange->n_ranks)
+      return fail(PM_E_INVALID, "bad rank geometry");
+    if (exchange->root < -1 || exchange->root >= exchange->n_ranks) return fail(PM_E_INVALID, "root must be -1 or a rank");
+    if (exchange->epoch == 0 || !exchange->done) return fail(PM_E_INVALID, "bad epoch or counter");
+    for (int r = 0; r < exchange->n_ranks; ++r)
+      if ((exchange->root < 0 || r == exchange->root) && (!exchange->out[r] || !exchange->flags[r]))
+        return fail(PM_E_INVALID, "a receiving rank's buffer is NULL");
+    if (exchange->per_rank < groups->n_groups) return fail(PM_E_INVALID, "per_rank below this rank's group count");
+  }
+  const size_t a_need = analyze_scratch_bytes(trials->n_trials, trials->max_phase_samples);
+  const size_t b_off = align256(a_need);
+  const size_t b_need = bootstrap_scratch_bytes(groups->n_groups, groups->max_members, groups->resamples);
+  if (b_off + b_need > scratch_bytes || !scratch)
+    return fail(PM_E_INVALID, "the sweep needs %zu bytes of device scratch (pm_analyze_sweep_scratch_bytes), got %zu",
+                b_off + b_need, scratch_bytes);
+  if (reinterpret_cast<uintptr_t>(scratch) % 256)
+    return fail(PM_E_INVALID, "the sweep's device scratch must be 256-byte aligned");
+  BootArgs A;
+  int rc = device_boot_args(groups, static_cast<uint8_t*>(scratch) + b_off, scratch_bytes - b_off, &A);
+  if (rc) return rc;
+  int device = 0;
+  if ((rc = current_device(&device))) return rc;
+  SweepFork& F = g_sweep_fork[device];
+  std::lock_guard<std::mutex> guard(F.lock);
+  if (!F.side) {
+    cudaError_t e = cudaStreamCreateWithFlags(&F.side, cudaStreamNonBlocking);
+    if (e == cudaSuccess) e = cudaEventCreateWithFlags(&F.fork, cudaEventDisableTiming);
+    if (e == cudaSuccess) e = cudaEventCreateWithFlags(&F.join, cudaEventDisableTiming);
+    if (e != cudaSuccess) { F.side = nullptr; return cuda_fail(e, "sweep side stream / events"); }
+  }
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  // The draws need only the seeds and group sizes: on the side stream, beside
+  // the analysis on the caller's stream (one CTA per trial), joined before the
+  // finish.
+  cudaError_t e = cudaEventRecord(F.fork, s);
+  if (e == cudaSuccess) e = cudaStreamWaitEvent(F.side, F.fork, 0);
+  if (e != cudaSuccess) return cuda_fail(e, "sweep fork");
+  launch_bootstrap_prepare(A, F.side);
+  e = cudaGetLastError();
+  if (e != cudaSuccess) return cuda_fail(e, "bootstrap_prepare_kernel launch");
+  e = cudaEventRecord(F.join, F.side);
+  if (e != cudaSuccess) return cuda_fail(e, "sweep join record");
+  launch_analyze(*trials, *policy, *out, trials->max_phase_samples, a_need ? static_cast<double*>(scratch) : nullptr, s,
+                 nullptr);
+  e = cudaGetLastError();
+  if (e != cudaSuccess) return cuda_fail(e, "analysis launch");
+  e = cudaStreamWaitEvent(s, F.join, 0);
+  if (e != cudaSuccess) return cuda_fail(e, "sweep join");
+  launch_bootstrap(A, s, exchange);
+  e = cudaGetLastError();
   if (e != cudaSuccess) return cuda_fail(e, "bootstrap_kernel launch");
   return PM_OK;
 }
