@@ -62,15 +62,22 @@ __device__ __forceinline__ uint32_t twist_one(uint32_t cur, uint32_t next, uint3
 // algorithm's loops are unwound into straight index runs (the wrap of i at
 // 624 and the alternation of j become explicit), so each step is the
 // dependent multiply-xor-add on `prev` and nothing else.
-__device__ void seed_state(uint32_t* mt, uint64_t seed) {
+// `init` reads init_genrand(19650218): the constant table (ConstInit) or a
+// shared-memory copy of it (the draw pass stages one: the 2.5 KB table does
+// not stay in the constant cache across the chain).
+struct ConstInit {
+  __device__ __forceinline__ uint32_t operator[](int i) const { return c_mt_init[i]; }
+};
+template <class Init>
+__device__ void seed_state(uint32_t* mt, uint64_t seed, Init init) {
   const bool two = (seed >> 32) != 0;
   const uint32_t add0 = (uint32_t)seed;                           // key[0] + 0
   const uint32_t add1 = two ? (uint32_t)(seed >> 32) + 1u : add0;  // key[1] + 1, or key[0] again
-  uint32_t prev = c_mt_init[0];
+  uint32_t prev = init[0];
   // Loop 1 (624 steps): i = 1..623, then i wraps (mt[0] = mt[623]) and i = 1 once more.
 #pragma unroll 8
   for (int t = 0; t < kMtN - 1; ++t) {
-    prev = (c_mt_init[1 + t] ^ ((prev ^ (prev >> 30)) * 1664525u)) + ((t & 1) ? add1 : add0);
+    prev = (init[1 + t] ^ ((prev ^ (prev >> 30)) * 1664525u)) + ((t & 1) ? add1 : add0);
     mt[1 + t] = prev;
   }
   mt[0] = prev;
@@ -315,30 +322,40 @@ __device__ __forceinline__ void stream_draws(GenShared& sh, int n, int B, uint8_
 // Multiset counts of the B resamples of a count-N stream (N <= kHistMaxN)
 // into sh.hist: each thread sorts its resamples' indices in registers and
 // ranks the multiset; lanes of a warp holding the same rank add once together.
+// The stream was written by this CTA and sits in L2: each thread reads the
+// indices of kBatch resamples before ranking any of them.
 template <int N>
 __device__ __forceinline__ void histogram_stream(GenShared& sh, int B, const uint8_t* stream) {
-  for (int r0 = 0; r0 < B; r0 += blockDim.x) {
-    const int r = r0 + threadIdx.x;
-    int rank = -1;
-    if (r < B) {
-      int t[N];
+  constexpr int kBatch = 4;
+  for (int r0 = 0; r0 < B; r0 += blockDim.x * kBatch) {
+    int t[kBatch][N];
 #pragma unroll
-      for (int i = 0; i < N; ++i) t[i] = stream[(size_t)r * N + i];
+    for (int u = 0; u < kBatch; ++u) {
+      const int r = r0 + u * blockDim.x + threadIdx.x;
 #pragma unroll
-      for (int i = 0; i < N; ++i)
-#pragma unroll
-        for (int k = 0; k < N - 1 - i; ++k) {
-          const int a = t[k], b = t[k + 1];
-          t[k] = min(a, b); t[k + 1] = max(a, b);
-        }
-      rank = 0;
-#pragma unroll
-      for (int i = 0; i < N; ++i) rank += (int)sh.binom[t[i] + i][i + 1];
+      for (int i = 0; i < N; ++i) t[u][i] = r < B ? stream[(size_t)r * N + i] : 0;
     }
-    const unsigned live = __ballot_sync(0xffffffffu, rank >= 0);
-    if (rank >= 0) {
-      const unsigned same = __match_any_sync(live, rank);
-      if ((int)(threadIdx.x & 31) == __ffs(same) - 1) atomicAdd(&sh.hist[rank], (uint32_t)__popc(same));
+#pragma unroll
+    for (int u = 0; u < kBatch; ++u) {
+      const int r = r0 + u * blockDim.x + threadIdx.x;
+      int rank = -1;
+      if (r < B) {
+#pragma unroll
+        for (int i = 0; i < N; ++i)
+#pragma unroll
+          for (int k = 0; k < N - 1 - i; ++k) {
+            const int a = t[u][k], b = t[u][k + 1];
+            t[u][k] = min(a, b); t[u][k + 1] = max(a, b);
+          }
+        rank = 0;
+#pragma unroll
+        for (int i = 0; i < N; ++i) rank += (int)sh.binom[t[u][i] + i][i + 1];
+      }
+      const unsigned live = __ballot_sync(0xffffffffu, rank >= 0);
+      if (rank >= 0) {
+        const unsigned same = __match_any_sync(live, rank);
+        if ((int)(threadIdx.x & 31) == __ffs(same) - 1) atomicAdd(&sh.hist[rank], (uint32_t)__popc(same));
+      }
     }
   }
 }
@@ -356,7 +373,10 @@ __global__ void __launch_bounds__(kPrepThreads) bootstrap_prepare_kernel(BootArg
   const int n = A.offsets[g + 1] - A.offsets[g];
   if (n < 3 || n > A.max_members || n > kDirectMaxN) return;   // no interval for n < 3 (uniform exit)
   load_binom(sh);
-  if (threadIdx.x == 0) seed_state(sh.mt_seed, A.seeds[g]);
+  // The seeding table in shared memory (sh.mt[1] is free until the first twist).
+  for (int i = threadIdx.x; i < kMtN; i += blockDim.x) sh.mt[1][i] = c_mt_init[i];
+  __syncthreads();
+  if (threadIdx.x == 0) seed_state(sh.mt_seed, A.seeds[g], static_cast<const uint32_t*>(sh.mt[1]));
   for (int i = threadIdx.x; i < kMaxBins; i += blockDim.x) sh.hist[i] = 0;
   __syncthreads();
   uint8_t* stream = index_stream(A, g);
@@ -410,7 +430,7 @@ __global__ void __launch_bounds__(kBootThreads) bootstrap_kernel(BootArgs A, pm_
   // Without a prepare pass, one thread of the last warp seeds the generator
   // while the others gather the metric values (every metric's _median_ci
   // starts random.Random(seed) afresh, so one seeded state serves them all).
-  if (!A.prepared && threadIdx.x == blockDim.x - 32) seed_state(sh.mt_seed, A.seeds[g]);
+  if (!A.prepared && threadIdx.x == blockDim.x - 32) seed_state(sh.mt_seed, A.seeds[g], ConstInit{});
   const BootSmem L(M, A.max_members, A.max_members > kHistMaxN);
   double* vals = reinterpret_cast<double*>(dsm + L.vals);
   int* cnt = reinterpret_cast<int*>(dsm + L.cnt);
@@ -499,7 +519,7 @@ __global__ void __launch_bounds__(kBootThreads) bootstrap_kernel(BootArgs A, pm_
       __syncthreads();
     } else {
       if (!seeded) {
-        if (threadIdx.x == 0) seed_state(sh.mt_seed, A.seeds[g]);
+        if (threadIdx.x == 0) seed_state(sh.mt_seed, A.seeds[g], ConstInit{});
         seeded = true;
       }
       __syncthreads();
@@ -793,7 +813,7 @@ __global__ void signal_groups_kernel(pm_peer_groups X) {
 __global__ void resample_indices_kernel(uint64_t seed, int n, int B, int32_t* out) {
   __shared__ uint32_t mt[2][kMtN];
   __shared__ uint32_t ring[kRing];
-  if (threadIdx.x == 0) seed_state(mt[0], seed);
+  if (threadIdx.x == 0) seed_state(mt[0], seed, ConstInit{});
   __syncthreads();
   const uint32_t words_per_draw = 2u * (uint32_t)n;
   const uint32_t blocks = (uint32_t)((2ull * n * B + kMtN - 1) / kMtN);
