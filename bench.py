@@ -862,9 +862,9 @@ def run_nonlinear_arms(sms: int, peaks: dict) -> dict:
 # DRAM bytes read + written.  The kernels are deterministic for the fixed
 # seeds, so the counts are the same on every launch; None where not captured.
 NCU_PER_LAUNCH = {
-    "analyze_kernel": {"inst": 22_774_000, "dram": 5_092_352},
-    "bootstrap_prepare_kernel": {"inst": 10_013_759, "dram": 43_008},
-    "bootstrap_kernel<0>": {"inst": 752_751, "dram": 188_672},
+    "analyze_kernel": {"inst": 24_437_880, "dram": 5_000_576},
+    "bootstrap_prepare_kernel": {"inst": 9_640_767, "dram": 70_528},
+    "bootstrap_kernel<0>": {"inst": 744_303, "dram": 185_344},
 }
 # Blackwell SM: four schedulers, each issuing one warp instruction per clock.
 ISSUE_PER_SM_CLOCK = 4
