@@ -322,6 +322,7 @@ class _Views:
         self.issue_bits = np.empty(n * 4, dtype=np.uint64)
         self.metrics = np.empty(n * len(METRICS))
         self.valid = np.empty(n, dtype=np.uint8)
+        self.windows = None          # per slot (lo, hi) or None, read from phase_out once it is filled
 
     def struct(self) -> N.TrialResults:
         r = N.TrialResults()
@@ -489,6 +490,9 @@ def analyze_trials(records: Iterable[Mapping[str, Any]], policy: AnalysisPolicy 
         _metrics_out.append((views.metrics.reshape(len(records), len(METRICS)).copy(), views.valid.copy()))
     TO = {name: N.layout("PM_TO_" + name) for name in _TO_NAMES}
     to_rows = _py_rows(views.trial_out, views.TO)
+    # the same rows as plain floats (NaN kept: flags are read with bool()), and the issue words as ints
+    to_raw = views.trial_out.reshape(-1, views.TO).tolist()
+    issue_rows = views.issue_bits.reshape(-1, 4).tolist()
     all_phases = _phase_dicts(views)
     policy_dict = asdict(policy)
     sel_lo, sel_hi = N.layout("PM_PO_SEL_LO"), N.layout("PM_PO_SEL_HI")
@@ -498,10 +502,10 @@ def analyze_trials(records: Iterable[Mapping[str, Any]], policy: AnalysisPolicy 
         config = dict(record.get("config") or {})
         device = record.get("device") or {}
         phases_rec = phase_records(record)
-        to = views.trial_out[i * views.TO:(i + 1) * views.TO]
+        to = to_raw[i]
         to_py = to_rows[i]
         g = lambda name: to_py[TO[name]]  # noqa: E731
-        ib = [int(x) for x in views.issue_bits[i * 4:(i + 1) * 4]]
+        ib = issue_rows[i]
         issues = host_issues[i] + _bits(ib[0], words[0])
         baseline_issues = _bits(ib[1], words[1])
         paired_issues = host_paired[i] + _bits(ib[2], words[2])
@@ -680,11 +684,19 @@ def analyze_trials(records: Iterable[Mapping[str, Any]], policy: AnalysisPolicy 
     return out
 
 
+def _windows(views) -> list:
+    """Every slot's selected window (lo, hi) relative to its segment, or None: read from the
+    phase rows at once."""
+    rows = views.phase_out.reshape(-1, views.PO)
+    pairs = rows[:, [N.layout("PM_PO_SEL_LO"), N.layout("PM_PO_SEL_HI")]].tolist()
+    return [None if math.isnan(lo) else (int(lo), int(hi)) for lo, hi in pairs]
+
+
 def _window(trial, phase, views):
     slot = trial * N.PM_PHASES + phase
-    po = views.phase_out[slot * views.PO:(slot + 1) * views.PO]
-    lo, hi = po[N.layout("PM_PO_SEL_LO")], po[N.layout("PM_PO_SEL_HI")]
-    return slot, (None if math.isnan(lo) else (int(lo), int(hi)))
+    if views.windows is None:
+        views.windows = _windows(views)
+    return slot, views.windows[slot]
 
 
 def _binding(packed, trial, views):
@@ -720,12 +732,8 @@ def _rail_sources(packed, trial, phases, views):
 
 
 def _selected(packed, trial, phase, views):
-    slot = trial * N.PM_PHASES + phase
-    po = views.phase_out[slot * views.PO:(slot + 1) * views.PO]
-    lo, hi = po[N.layout("PM_PO_SEL_LO")], po[N.layout("PM_PO_SEL_HI")]
-    if math.isnan(lo):
-        return []
-    return packed.samples[slot][int(lo):int(hi)]
+    slot, window = _window(trial, phase, views)
+    return packed.samples[slot][window[0]:window[1]] if window else []
 
 
 _TO_NAMES = ("DURATION_S", "BENCH_MEASURED_DURATION_S", "BENCH_DEVICE_DURATION_S", "IDLE_POWER_W", "IDLE_MEMORY_POWER_W",
@@ -909,16 +917,23 @@ def finish_groups(groups: list, trials: list, members: list, group_indices: list
     from .hbm import group_bandwidth
     from .trial_report import complete_group
     base = len(METRICS)
+    if not groups:
+        return
+    # the bootstrap outputs as rows of Python floats, None for NaN, converted at once
+    width = med.shape[1]
+    med_rows, lo_rows, hi_rows = (_py_rows(np.ascontiguousarray(x).reshape(-1), width) for x in (med, lo, hi))
     for g, group in enumerate(groups):
+        mr, lr, hr = med_rows[g], lo_rows[g], hi_rows[g]
+        ci = group["ci95"]
         for m, metric in enumerate(METRICS):
-            group[metric] = _none(med[g, m])
-            a, b = _none(lo[g, m]), _none(hi[g, m])
-            group["ci95"][metric] = [a, b] if a is not None else None
+            group[metric] = mr[m]
+            a = lr[m]
+            ci[metric] = [a, hr[m]] if a is not None else None
         vt = [trials[i] for i in members[g]]
         group["hbm_bandwidth"] = group_bandwidth(vt, group["workload"], hbm_bandwidth_fraction)
-        sensor_medians = [_none(med[g, base + k]) for k in range(len(SENSOR_FIELDS))]
-        sensor_intervals = [[_none(lo[g, base + k]), _none(hi[g, base + k])] if _none(lo[g, base + k]) is not None
-                            else None for k in range(len(SENSOR_FIELDS))]
+        sensor_medians = mr[base:base + len(SENSOR_FIELDS)]
+        sensor_intervals = [[lr[base + k], hr[base + k]] if lr[base + k] is not None else None
+                            for k in range(len(SENSOR_FIELDS))]
         group["hbm_memory_power"] = group_sensor(vt, group["workload"], [trials[i] for i in group_indices[g]],
                                                  sensor_medians, sensor_intervals)
         if group["hbm_memory_power"] is not None:
