@@ -2,7 +2,8 @@
 
 Two GPUs: rows and group results stored into every rank by the analysis and
 bootstrap kernels equal, bit for bit, an NCCL all-gather of the same local
-outputs, over several epochs.  One GPU: the arrival wait ends on its own
+outputs, over several epochs, with the groups split evenly over the ranks
+and with one rank owning a group fewer (its last slot is never written).  One GPU: the arrival wait ends on its own
 limit when a flag is never raised, reports it, and leaves the context usable.
 """
 from __future__ import annotations
@@ -21,7 +22,7 @@ pytestmark = pytest.mark.gpu
 POINTS, REPEATS, STEPS = 4, 4, 3
 
 
-def _worker(rank, world, port, out_path):
+def _worker(rank, world, port, out_path, uneven=False):
     import datetime
     import numpy as np
     import torch
@@ -53,7 +54,7 @@ def _worker(rank, world, port, out_path):
                                                                 "metrics", "valid")))
         policy = A.AnalysisPolicy(**ANALYSIS_POLICY).native()
         # groups: every point's repeats (global rows), owned round robin
-        G = world * POINTS
+        G = world * POINTS - (1 if uneven else 0)
         members = [[(g // POINTS) * n + (g % POINTS) * REPEATS + k for k in range(REPEATS)] for g in range(G)]
         mine = [g for g in range(G) if g % world == rank]
         per_rank = -(-G // world)
@@ -90,9 +91,13 @@ def _worker(rank, world, port, out_path):
         dist.all_gather_into_tensor(want_groups, group_out)
         torch.cuda.synchronize()
         got_rows, got_valid, got_groups = px.view("metrics"), px.view("valid"), px.view("groups")
+        # each rank's owned slots (a rank with fewer groups leaves its last slot unwritten)
+        owned = [len([g for g in range(G) if g % world == r]) for r in range(world)]
+        same_groups = all(torch.equal(got_groups[r, :, :owned[r]].reshape(-1).view(torch.int64),
+                                      want_groups[r, :, :owned[r]].reshape(-1).view(torch.int64)) for r in range(world))
         result = {"rows": bool(torch.equal(got_rows.reshape(-1).view(torch.int64), want_rows.view(torch.int64))),
                   "valid": bool(torch.equal(got_valid, want_valid)),
-                  "groups": bool(torch.equal(got_groups.reshape(-1).view(torch.int64), want_groups.reshape(-1).view(torch.int64))),
+                  "groups": bool(same_groups),
                   "groups_finite": int(torch.isfinite(want_groups[:, 1]).sum().item()),
                   "epoch": int(px.rows.epoch)}
         px.close()
@@ -102,7 +107,8 @@ def _worker(rank, world, port, out_path):
         dist.destroy_process_group()
 
 
-def test_two_gpu_peer_exchange_equals_all_gather(gpu_ready):
+@pytest.mark.parametrize("uneven", [False, True], ids=["even", "one-group-fewer"])
+def test_two_gpu_peer_exchange_equals_all_gather(gpu_ready, uneven):
     import torch
     if torch.cuda.device_count() < 2:
         pytest.skip("needs two GPUs")
@@ -115,7 +121,7 @@ def test_two_gpu_peer_exchange_equals_all_gather(gpu_ready):
     os.environ.update(env)
     with tempfile.TemporaryDirectory() as tmp:
         out = os.path.join(tmp, "peer")
-        procs = [ctx.Process(target=_worker, args=(r, world, port, out)) for r in range(world)]
+        procs = [ctx.Process(target=_worker, args=(r, world, port, out, uneven)) for r in range(world)]
         for p in procs:
             p.start()
         for p in procs:
