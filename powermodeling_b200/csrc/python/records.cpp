@@ -17,11 +17,18 @@
 // are not strings, numbers of other types) is handed to `fallback`, the
 // Python statement of the same rule, with the node's values as a list, so
 // both paths return the same objects.
+//
+// phase_dicts and measurement_diagnostics (below) build the trial records'
+// phase dicts and measurement diagnostics; their Python statements in
+// powermodeling_b200/analysis.py and trial_report.py are the specification.
 #define PY_SSIZE_T_CLEAN
 #include <Python.h>
 
 #include <algorithm>
 #include <cmath>
+#include <cstring>
+#include <string>
+#include <unordered_map>
 #include <vector>
 
 namespace {
@@ -347,8 +354,448 @@ PyObject* phase_dicts(PyObject*, PyObject* args) {
   return out;
 }
 
+// ---------------------------------------------------------------------------
+// measurement_diagnostics: a trial's measurement diagnostics (the rules of
+// powermodeling/analysis.py:530-566 as powermodeling_b200/trial_report.py
+// states them in measurement_diagnostics, which stays the specification):
+// each objective's reported pJ beside its reconstruction from energy and
+// count (or power and rate), scope factors, power shares, telemetry and
+// throughput cross-checks, execution facts and timing, keys in that
+// function's order.  Values read from the records are the records' own
+// objects; sums of epoch durations go through Python's sum().
+
+// _finite: 1 and *out when finite, 0 for None, a bool or a value float()
+// rejects, -1 with an exception set (float()'s other errors).
+int py_finite(PyObject* v, double* out) {
+  if (!v || v == Py_None || PyBool_Check(v)) return 0;
+  double d;
+  if (PyFloat_CheckExact(v)) {
+    d = PyFloat_AS_DOUBLE(v);
+  } else if (PyLong_CheckExact(v)) {
+    d = PyLong_AsDouble(v);
+    if (d == -1.0 && PyErr_Occurred()) return -1;
+  } else {
+    PyObject* f = PyNumber_Float(v);
+    if (!f) {
+      if (PyErr_ExceptionMatches(PyExc_TypeError) || PyErr_ExceptionMatches(PyExc_ValueError)) {
+        PyErr_Clear();
+        return 0;
+      }
+      return -1;
+    }
+    d = PyFloat_AS_DOUBLE(f);
+    Py_DECREF(f);
+  }
+  if (!std::isfinite(d)) return 0;
+  *out = d;
+  return 1;
+}
+
+// An optional float of the diagnostics.
+struct Opt {
+  bool has = false;
+  double v = 0.0;
+  PyObject* py() const { return has ? PyFloat_FromDouble(v) : Py_NewRef(Py_None); }
+};
+inline Opt some(double v) { return Opt{true, v}; }
+
+// An interned key per string literal (cached by the literal's address).
+PyObject* key_of(const char* text) {
+  static std::unordered_map<const char*, PyObject*> cache;
+  auto it = cache.find(text);
+  if (it != cache.end()) return it->second;
+  PyObject* k = PyUnicode_InternFromString(text);
+  if (k) cache.emplace(text, k);
+  return k;
+}
+
+// m.get(key[, default]) as a new reference: exact dicts directly, anything else through its get().
+PyObject* get_new(PyObject* m, const char* key, PyObject* dflt = Py_None) {
+  PyObject* k = key_of(key);
+  if (!k) return nullptr;
+  if (PyDict_CheckExact(m)) {
+    PyObject* v = PyDict_GetItemWithError(m, k);
+    if (!v) return PyErr_Occurred() ? nullptr : Py_NewRef(dflt);
+    return Py_NewRef(v);
+  }
+  return PyObject_CallMethodObjArgs(m, key_of("get"), k, dflt, nullptr);
+}
+
+// m.get(key) for a key built at run time (not cached), as a new reference.
+PyObject* get_dynamic(PyObject* m, const std::string& key) {
+  PyObject* k = PyUnicode_FromStringAndSize(key.data(), (Py_ssize_t)key.size());
+  if (!k) return nullptr;
+  PyObject* v;
+  if (PyDict_CheckExact(m)) {
+    v = PyDict_GetItemWithError(m, k);
+    v = v ? Py_NewRef(v) : (PyErr_Occurred() ? nullptr : Py_NewRef(Py_None));
+  } else {
+    v = PyObject_CallMethodObjArgs(m, key_of("get"), k, nullptr);
+  }
+  Py_DECREF(k);
+  return v;
+}
+
+// _finite(m.get(key)) into *out; -1 with an exception set.
+int finite_of(PyObject* m, const char* key, Opt* out) {
+  PyObject* v = get_new(m, key);
+  if (!v) return -1;
+  double d;
+  const int r = py_finite(v, &d);
+  Py_DECREF(v);
+  if (r < 0) return -1;
+  *out = r ? some(d) : Opt{};
+  return 0;
+}
+
+// m.get(key) is True
+int is_true(PyObject* m, const char* key, bool* out) {
+  PyObject* v = get_new(m, key);
+  if (!v) return -1;
+  *out = v == Py_True;
+  Py_DECREF(v);
+  return 0;
+}
+
+inline Opt ratio(Opt a, Opt b) { return a.has && b.has && b.v > 0 ? some(a.v / b.v) : Opt{}; }
+
+// A dict built in key order; any failure leaves `ok` false and the exception set.
+struct DictBuilder {
+  PyObject* d;
+  bool ok;
+  DictBuilder() : d(PyDict_New()), ok(d != nullptr) {}
+  ~DictBuilder() { Py_XDECREF(d); }
+  DictBuilder& set(const char* key, PyObject* value) {          // steals `value`
+    if (!ok || !value) { ok = false; Py_XDECREF(value); return *this; }
+    PyObject* k = key_of(key);
+    ok = k && PyDict_SetItem(d, k, value) == 0;
+    Py_DECREF(value);
+    return *this;
+  }
+  DictBuilder& ref(const char* key, PyObject* value) { return set(key, Py_NewRef(value ? value : Py_None)); }
+  DictBuilder& from(const char* key, PyObject* m, const char* field) { return set(key, ok ? get_new(m, field) : nullptr); }
+  DictBuilder& str(const char* key, const char* text) { return set(key, text ? PyUnicode_FromString(text) : Py_NewRef(Py_None)); }
+  DictBuilder& num(const char* key, Opt v) { return set(key, v.py()); }
+  DictBuilder& flag(const char* key, bool v) { return set(key, PyBool_FromLong(v)); }
+  PyObject* take() { if (!ok) return nullptr; PyObject* r = d; d = nullptr; return r; }
+};
+
+// The workload classes the diagnostics distinguish (the caller's sets).
+struct Classes {
+  PyObject *memory, *tensor, *sfu, *nonlinear;
+};
+
+int member(PyObject* set, PyObject* workload, bool* out) {
+  const int r = PySet_Contains(set, workload);
+  if (r < 0) return -1;
+  *out = r == 1;
+  return 0;
+}
+
+// The work denominator: unit, energy-metric suffix, rate per second, selected count.
+struct Denominator {
+  const char *unit = nullptr, *suffix = nullptr;
+  Opt rate, count;
+};
+
+int denominator(PyObject* result, PyObject* workload, const Classes& C, Denominator* d) {
+  bool memory, sfu, tensor, nonlinear;
+  if (member(C.memory, workload, &memory) < 0) return -1;
+  if (memory) {
+    Opt rate, count;
+    if (finite_of(result, "throughput_bytes_s", &rate) < 0 || finite_of(result, "counted_measure_logical_bytes", &count) < 0)
+      return -1;
+    d->unit = "logical bit";
+    d->suffix = "pj_per_logical_bit";
+    d->rate = rate.has ? some(rate.v * 8) : Opt{};
+    d->count = count.has ? some(count.v * 8) : Opt{};
+    return 0;
+  }
+  if (member(C.sfu, workload, &sfu) < 0 || member(C.tensor, workload, &tensor) < 0 ||
+      member(C.nonlinear, workload, &nonlinear) < 0)
+    return -1;
+  if (sfu || tensor || nonlinear) {
+    d->unit = sfu ? "scalar SFU instruction" : tensor ? "FLOP" : "element";
+    d->suffix = sfu ? "pj_per_instruction" : tensor ? "pj_per_flop" : "pj_per_element";
+    if (finite_of(result, "throughput_ops_s", &d->rate) < 0 || finite_of(result, "counted_measure_operations", &d->count) < 0)
+      return -1;
+  }
+  return 0;
+}
+
+PyObject* objective(PyObject* result, const char* name, const char* prefix, const char* power_field,
+                    const char* energy_field, const Denominator& D, bool exact) {
+  const bool total = strcmp(name, "total") == 0;
+  bool eligible;
+  if (total) {
+    bool valid;
+    if (is_true(result, "valid", &valid) < 0) return nullptr;
+    eligible = valid && exact;
+  } else {
+    PyObject* v = get_dynamic(result, std::string(name) + "_eligible");
+    if (!v) return nullptr;
+    eligible = v == Py_True;
+    Py_DECREF(v);
+  }
+  Opt power, energy, reported;
+  if (finite_of(result, power_field, &power) < 0 || finite_of(result, energy_field, &energy) < 0) return nullptr;
+  std::string metric = D.suffix ? std::string(prefix) + D.suffix : std::string();
+  if (D.suffix) {
+    PyObject* v = get_dynamic(result, metric);
+    if (!v) return nullptr;
+    double x;
+    const int r = py_finite(v, &x);
+    Py_DECREF(v);
+    if (r < 0) return nullptr;
+    reported = r ? some(x) : Opt{};
+  }
+  Opt rebuilt = exact ? ratio(energy, D.count) : ratio(power, D.rate);
+  if (rebuilt.has) rebuilt.v = rebuilt.v * 1e12;
+  DictBuilder b;
+  b.set("metric", D.suffix ? PyUnicode_FromString(metric.c_str()) : Py_NewRef(Py_None));
+  b.set("unit", D.unit ? PyUnicode_FromFormat("pJ/%s", D.unit) : Py_NewRef(Py_None));
+  b.num("reported_value", reported).num("reconstructed_value", rebuilt);
+  b.num("reconstruction_difference", reported.has && rebuilt.has ? some(reported.v - rebuilt.v) : Opt{});
+  b.num("power_w", power).num("energy_j", energy).flag("eligible", eligible);
+  b.str("scope", total ? "whole-device total"
+                       : "whole-device operational contrast; physical component energy is not isolated");
+  return b.take();
+}
+
+PyObject* alias_entry(const char* canonical, PyObject* multiplier, PyObject* unit) {   // steals both
+  DictBuilder b;
+  b.str("canonical_metric", canonical).set("value_multiplier", multiplier).set("unit", unit);
+  return b.take();
+}
+
+PyObject* aliases(PyObject* result, PyObject* bench, PyObject* workload, const Classes& C, const Denominator& D) {
+  bool memory, tensor, nonlinear;
+  if (member(C.memory, workload, &memory) < 0) return nullptr;
+  DictBuilder b;
+  if (memory) {
+    Opt ops, nbytes;
+    if (finite_of(result, "counted_measure_operations", &ops) < 0 ||
+        finite_of(result, "counted_measure_logical_bytes", &nbytes) < 0)
+      return nullptr;
+    const Opt per_op = ratio(nbytes.has ? some(nbytes.v * 8) : Opt{}, ops);
+    PyObject* dflt = PyUnicode_FromString("pJ/reported memory operation");
+    PyObject* unit = dflt ? get_new(bench, "operation_unit", dflt) : nullptr;
+    Py_XDECREF(dflt);
+    b.set("pj_per_logical_byte", alias_entry("operational_idle_increment_pj_per_logical_bit", PyLong_FromLong(8),
+                                             PyUnicode_FromString("pJ/logical byte")));
+    b.set("total_pj_per_logical_byte", alias_entry("total_pj_per_logical_bit", PyLong_FromLong(8),
+                                                   PyUnicode_FromString("pJ/logical byte")));
+    b.set("pj_per_op", unit ? alias_entry("operational_idle_increment_pj_per_logical_bit", per_op.py(), unit) : nullptr);
+    return b.take();
+  }
+  if (member(C.tensor, workload, &tensor) < 0 || member(C.nonlinear, workload, &nonlinear) < 0) return nullptr;
+  if (tensor || nonlinear) {
+    b.set("pj_per_op", alias_entry(("operational_idle_increment_" + std::string(D.suffix)).c_str(), PyLong_FromLong(1),
+                                   PyUnicode_FromFormat("pJ/%s", D.unit)));
+    b.set("total_pj_per_op", alias_entry(("total_" + std::string(D.suffix)).c_str(), PyLong_FromLong(1),
+                                         PyUnicode_FromFormat("pJ/%s", D.unit)));
+  }
+  return b.take();
+}
+
+// e[key] (any mapping), new reference.
+PyObject* item(PyObject* e, const char* key) {
+  PyObject* k = key_of(key);
+  return k ? PyObject_GetItem(e, k) : nullptr;
+}
+
+// The epoch timing figures: durations' sum, span, summed readback seconds (None: absent).
+struct EpochTiming {
+  PyObject *span = nullptr, *summed = nullptr, *gap = nullptr;   // new references or NULL for None
+  Opt readback_s;
+  ~EpochTiming() { Py_XDECREF(span); Py_XDECREF(summed); Py_XDECREF(gap); }
+};
+
+int epoch_timing(PyObject* epochs, PyObject* sum_fn, EpochTiming* T) {
+  const Py_ssize_t n = PyList_GET_SIZE(epochs);
+  if (n == 0) return 0;
+  PyObject* durations = PyList_New(n);
+  PyObject* readbacks = PyList_New(n);
+  if (!durations || !readbacks) { Py_XDECREF(durations); Py_XDECREF(readbacks); return -1; }
+  bool all_ok = true;
+  for (Py_ssize_t i = 0; i < n; ++i) {
+    PyObject* e = PyList_GET_ITEM(epochs, i);
+    PyObject* a = item(e, "start_s");
+    PyObject* b = a ? item(e, "end_s") : nullptr;
+    PyObject* d = b ? PyNumber_Subtract(b, a) : nullptr;
+    Py_XDECREF(a);
+    Py_XDECREF(b);
+    if (!d) { Py_DECREF(durations); Py_DECREF(readbacks); return -1; }
+    PyList_SET_ITEM(durations, i, d);
+    Opt r;
+    if (finite_of(e, "counter_readback_ns", &r) < 0) { Py_DECREF(durations); Py_DECREF(readbacks); return -1; }
+    if (!r.has || !(r.v >= 0)) all_ok = false;
+    PyList_SET_ITEM(readbacks, i, r.py());
+  }
+  PyObject* first = PyList_GET_ITEM(epochs, 0);
+  PyObject* last = PyList_GET_ITEM(epochs, n - 1);
+  PyObject* end = item(last, "end_s");
+  PyObject* start = end ? item(first, "start_s") : nullptr;
+  T->span = start ? PyNumber_Subtract(end, start) : nullptr;
+  Py_XDECREF(end);
+  Py_XDECREF(start);
+  T->summed = T->span ? PyObject_CallOneArg(sum_fn, durations) : nullptr;
+  PyObject* rs = nullptr;
+  if (T->summed && all_ok) {
+    rs = PyObject_CallOneArg(sum_fn, readbacks);
+    if (rs) {
+      const double x = PyFloat_AsDouble(rs);
+      if (!(x == -1.0 && PyErr_Occurred())) T->readback_s = some(x / 1e9);
+    }
+  }
+  Py_DECREF(durations);
+  Py_DECREF(readbacks);
+  if (!T->summed || (all_ok && !rs) || PyErr_Occurred()) { Py_XDECREF(rs); return -1; }
+  Py_XDECREF(rs);
+  // max(0.0, span - summed)
+  PyObject* diff = PyNumber_Subtract(T->span, T->summed);
+  if (!diff) return -1;
+  PyObject* zero = PyFloat_FromDouble(0.0);
+  const int greater = zero ? PyObject_RichCompareBool(diff, zero, Py_GT) : -1;
+  if (greater < 0) { Py_DECREF(diff); Py_XDECREF(zero); return -1; }
+  T->gap = greater ? diff : zero;
+  Py_DECREF(greater ? zero : diff);
+  return 0;
+}
+
+PyObject* measurement_diagnostics(PyObject*, PyObject* args) {
+  PyObject *result, *bench, *epochs, *sum_fn;
+  Classes C;
+  if (!PyArg_ParseTuple(args, "OOO!OOOOO", &result, &bench, &PyList_Type, &epochs, &C.memory, &C.tensor, &C.sfu,
+                        &C.nonlinear, &sum_fn))
+    return nullptr;
+  PyObject* workload = get_new(result, "workload");
+  if (!workload) return nullptr;
+  bool memory = false, tensor = false;
+  Denominator D;
+  if (member(C.memory, workload, &memory) < 0 || member(C.tensor, workload, &tensor) < 0 ||
+      denominator(result, workload, C, &D) < 0) {
+    Py_DECREF(workload);
+    return nullptr;
+  }
+  Opt duration, board, idle, reference, paired, incremental, integral, counter, ops, nbytes;
+  bool exact = false;
+  if (finite_of(result, "duration_s", &duration) < 0 || is_true(result, "count_energy_time_alignment_exact", &exact) < 0 ||
+      finite_of(result, "board_power_w", &board) < 0 || finite_of(result, "idle_power_w", &idle) < 0 ||
+      finite_of(result, "active_reference_power_w", &reference) < 0 ||
+      finite_of(result, "paired_active_reference_power_w", &paired) < 0 ||
+      finite_of(result, "operational_idle_increment_power_w", &incremental) < 0 ||
+      finite_of(result, "integrated_power_energy_j", &integral) < 0 || finite_of(result, "energy_counter_j", &counter) < 0 ||
+      finite_of(result, "counted_measure_operations", &ops) < 0 ||
+      finite_of(result, "counted_measure_logical_bytes", &nbytes) < 0) {
+    Py_DECREF(workload);
+    return nullptr;
+  }
+  EpochTiming T;
+  if (epoch_timing(epochs, sum_fn, &T) < 0) { Py_DECREF(workload); return nullptr; }
+  bool idle_eligible, paired_eligible, target_verified, valid, baseline_valid;
+  if (is_true(result, "operational_idle_increment_eligible", &idle_eligible) < 0 ||
+      is_true(result, "paired_active_reference_eligible", &paired_eligible) < 0 ||
+      is_true(result, "target_verified", &target_verified) < 0 || is_true(result, "valid", &valid) < 0 ||
+      is_true(result, "baseline_valid", &baseline_valid) < 0) {
+    Py_DECREF(workload);
+    return nullptr;
+  }
+
+  DictBuilder den;
+  den.str("unit", D.unit).num("measured_count", exact ? D.count : Opt{}).num("selected_epoch_count", D.count)
+      .num("rate_per_s", D.rate).num("aligned_window_s", duration).flag("exact_matching_window", exact)
+      .str("kind", exact ? "same-window counted work"
+                         : "stationary whole-run throughput estimate; no exact energy-window work count");
+  static const char* kObjectives[3][4] = {
+      {"total", "total_", "board_power_w", "total_energy_j"},
+      {"operational_idle_increment", "operational_idle_increment_", "operational_idle_increment_power_w",
+       "operational_idle_increment_energy_j"},
+      {"paired_active_reference", "paired_active_reference_", "paired_active_reference_power_w",
+       "paired_active_reference_energy_j"}};
+  DictBuilder obj;
+  for (auto& o : kObjectives) obj.set(o[0], obj.ok ? objective(result, o[0], o[1], o[2], o[3], D, exact) : nullptr);
+  DictBuilder units;
+  units.set("bits_per_byte", memory ? PyLong_FromLong(8) : Py_NewRef(Py_None))
+      .set("flops_per_fma", tensor ? PyLong_FromLong(2) : Py_NewRef(Py_None))
+      .from("flop_convention", result, "flop_count_convention").from("reported_operation_unit", bench, "operation_unit")
+      .num("logical_bits_per_reported_memory_operation", memory ? ratio(nbytes.has ? some(nbytes.v * 8) : Opt{}, ops) : Opt{})
+      .str("logical_byte_scope", memory ? "requested read payload plus requested write payload for copy; not physical "
+                                          "cache-sector or DRAM traffic" : nullptr)
+      .set("aliases", units.ok ? aliases(result, bench, workload, C, D) : nullptr);
+  DictBuilder scope;
+  scope.num("total_over_idle_increment", ratio(board, incremental)).num("total_over_paired_reference", ratio(board, paired))
+      .flag("idle_increment_eligible", idle_eligible).flag("paired_reference_eligible", paired_eligible)
+      .str("interpretation", "Numerical operational scope ratios only; ineligible contrasts and component literature "
+                             "must not be silently substituted.");
+  DictBuilder power;
+  power.num("total_w", board).num("idle_w", idle).num("idle_fraction", ratio(idle, board)).num("paired_reference_w", reference)
+      .num("paired_reference_fraction", ratio(reference, board)).num("idle_increment_w", incremental)
+      .num("paired_contrast_w", paired);
+  DictBuilder tele;
+  tele.from("energy_source", result, "energy_source").num("counter_energy_j", counter).num("integrated_power_energy_j", integral)
+      .num("counter_over_integrated", ratio(counter, integral))
+      .num("disagreement_fraction", counter.has && integral.has && integral.v > 0
+                                        ? some(std::fabs(counter.v - integral.v) / integral.v) : Opt{});
+  DictBuilder thr;
+  thr.set("unit", D.unit ? PyUnicode_FromFormat("%s/s", D.unit) : Py_NewRef(Py_None)).num("sustained_rate_per_s", D.rate)
+      .ref("profiler_replay_rate_per_s", nullptr).ref("profiler_replay_count", nullptr)
+      .ref("profiler_replay_summed_kernel_duration_s", nullptr).ref("profiler_over_sustained_rate", nullptr)
+      .flag("profiler_target_verified", target_verified).flag("same_energy_run", false)
+      .str("note", "Profiler replay uses a different run and summed kernel duration. Rate disagreement can motivate "
+                   "timing/traffic review but does not prove host overhead, permit energy rescaling or supply "
+                   "same-window physical traffic.");
+  DictBuilder exe;
+  exe.from("kernel_resources", bench, "kernel_resources").from("sfu_contract", result, "sfu_contract")
+      .from("sfu_reference_delta", result, "sfu_reference_delta_diagnostics")
+      .from("auxiliary_work", bench, "auxiliary_work").from("execution_diagnostics", bench, "execution_diagnostics")
+      .from("implementation_version", bench, "kernel_implementation_version");
+  for (const char* k : {"memory_accesses_per_thread_iteration", "memory_read_checksum_scope", "memory_read_validation",
+                        "grid_mode", "input_elements", "block_completion_count_source", "active_sm_ids",
+                        "active_sm_distribution_status", "sm_distribution_scope"})
+    exe.from(k, bench, k);
+  exe.str("saturation_status", "CUDA occupancy bounds and grid size do not establish achieved utilization or hardware "
+                               "saturation");
+  Opt host_duration, event_duration, mean_batch;
+  if (finite_of(bench, "host_duration_s", &host_duration) < 0 || finite_of(bench, "duration_s", &event_duration) < 0 ||
+      finite_of(bench, "mean_batch_duration_s", &mean_batch) < 0) {
+    Py_DECREF(workload);
+    return nullptr;
+  }
+  PyObject* scope_default = PyUnicode_FromString("CUDA experiment window; summed kernel busy time is not established");
+  DictBuilder tim;
+  tim.num("host_duration_s", host_duration).num("event_duration_s", event_duration)
+      .set("event_duration_scope", scope_default ? get_new(bench, "duration_scope", scope_default) : nullptr)
+      .num("mean_batch_experiment_duration_s", mean_batch)
+      .set("complete_epochs", PyLong_FromSsize_t(PyList_GET_SIZE(epochs))).ref("complete_epoch_span_s", T.span)
+      .ref("summed_epoch_duration_s", T.summed).ref("inter_epoch_gap_s", T.gap).num("counter_readback_s", T.readback_s)
+      .num("counter_readback_fraction", ratio(T.readback_s, duration)).ref("kernel_busy_time_s", nullptr)
+      .str("note", "Host synchronization, launch and readback gaps remain in sustained experiment energy and "
+                   "throughput. CUDA event-window rate is not a kernel-busy rate; NCU replay is a separate run.");
+  Py_XDECREF(scope_default);
+  PyObject* empty_issues = PyList_New(0);
+  PyObject* empty_baseline = PyList_New(0);
+  DictBuilder qual;
+  qual.flag("valid", valid).set("issues", empty_issues ? get_new(result, "issues", empty_issues) : nullptr)
+      .flag("baseline_valid", baseline_valid)
+      .set("baseline_issues", empty_baseline ? get_new(result, "baseline_issues", empty_baseline) : nullptr)
+      .flag("target_verified", target_verified);
+  Py_XDECREF(empty_issues);
+  Py_XDECREF(empty_baseline);
+  Py_DECREF(workload);
+
+  DictBuilder out;
+  out.set("schema_version", PyLong_FromLong(1)).set("denominator", den.take()).set("objectives", obj.take())
+      .set("unit_conventions", units.take()).set("scope_factors", scope.take()).set("power_contributions", power.take())
+      .set("telemetry_crosscheck", tele.take()).set("throughput_crosscheck", thr.take()).set("execution", exe.take())
+      .set("timing", tim.take()).set("quality", qual.take());
+  return out.take();
+}
+
 PyMethodDef kMethods[] = {
     {"fold", fold, METH_VARARGS, "fold(values, fallback) -> the repeats' diagnostics folded into one"},
+    {"measurement_diagnostics", measurement_diagnostics, METH_VARARGS,
+     "measurement_diagnostics(result, bench, epochs, memory, tensor, sfu, nonlinear, sum) -> a trial's diagnostics"},
     {"phase_dicts", phase_dicts, METH_VARARGS,
      "phase_dicts(phase_out, phase_flags, width, names, index, bits, issue_bits, note) -> a phase dict per slot"},
     {nullptr, nullptr, 0, nullptr}};

@@ -372,7 +372,8 @@ def complete_trial(record: Mapping, result: dict, trim_s: float, binding: list, 
         if phases_rec.get("active_reference"):
             _sfu_diagnostics(record, bench, result, not sfu_count_issues(bench, workload))
     result["energy_peak_population_eligible"] = peak_population_eligible(result)
-    diagnostics = measurement_diagnostics(result, bench, epochs)
+    diagnostics = _record_native().measurement_diagnostics(result, bench, epochs, MEMORY_WORKLOADS, TENSOR_WORKLOADS,
+                                                           SFU_WORKLOADS, NONLINEAR_WORKLOADS, sum)
     diagnostics["memory_access_geometry"] = result["memory_access_geometry"]
     diagnostics["memory_coalescing"] = result["memory_coalescing"]
     result["measurement_diagnostics"] = diagnostics

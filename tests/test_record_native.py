@@ -3,6 +3,9 @@
 fold: the group diagnostics' fold (trial_report._fold) on nested repeat diagnostics with
 every kind of leaf, missing keys, None repeats and values that take the Python path.
 phase_dicts: analysis._phase_dict over phase rows with random values, NaNs and flag words.
+measurement_diagnostics: trial_report.measurement_diagnostics over randomized trial results of
+every workload class, odd value types, epochs with and without counter readbacks, and a bench
+that is not a dict.
 """
 from __future__ import annotations
 
@@ -133,3 +136,62 @@ def test_phase_dicts_equal_python_statement():
         po = views.phase_out[slot * views.PO:(slot + 1) * views.PO]
         want = A._phase_dict(name, po, int(views.phase_flags[slot]), policy)
         assert _same(got, want), (slot, got, want)
+
+
+def _diagnostic_case(rng: random.Random):
+    from types import MappingProxyType
+    workloads = ["hbm", "l1", "tensor", "gemm", "sfu_ex2", "softmax", "exp", "control", None]
+    numeric = lambda: rng.choice([None, rng.uniform(-5, 500), rng.randrange(0, 10 ** 6), float("nan"), float("inf"),
+                                  True, "12.5", "x", 0.0, -0.0])
+    result = {"workload": rng.choice(workloads)}
+    for key in ("throughput_bytes_s", "counted_measure_logical_bytes", "throughput_ops_s", "counted_measure_operations",
+                "duration_s", "board_power_w", "idle_power_w", "active_reference_power_w",
+                "paired_active_reference_power_w", "operational_idle_increment_power_w", "integrated_power_energy_j",
+                "energy_counter_j", "total_energy_j", "operational_idle_increment_energy_j",
+                "paired_active_reference_energy_j", "total_pj_per_logical_bit", "total_pj_per_flop",
+                "operational_idle_increment_pj_per_instruction", "paired_active_reference_pj_per_element"):
+        if rng.random() < 0.85:
+            result[key] = numeric()
+    for key in ("count_energy_time_alignment_exact", "valid", "operational_idle_increment_eligible",
+                "paired_active_reference_eligible", "target_verified", "baseline_valid"):
+        if rng.random() < 0.9:
+            result[key] = rng.choice([True, False, 1, None])
+    for key in ("flop_count_convention", "energy_source", "sfu_contract", "sfu_reference_delta_diagnostics"):
+        if rng.random() < 0.7:
+            result[key] = rng.choice(["text", None, {"a": 1}])
+    if rng.random() < 0.7:
+        result["issues"] = ["a", "b"][:rng.randrange(3)]
+    if rng.random() < 0.7:
+        result["baseline_issues"] = []
+    bench = {k: rng.choice(["u", 3, None, {"k": [1]}]) for k in (
+        "operation_unit", "kernel_resources", "auxiliary_work", "execution_diagnostics", "kernel_implementation_version",
+        "memory_accesses_per_thread_iteration", "grid_mode", "active_sm_ids", "duration_scope") if rng.random() < 0.6}
+    for key in ("host_duration_s", "duration_s", "mean_batch_duration_s"):
+        if rng.random() < 0.7:
+            bench[key] = numeric()
+    if rng.random() < 0.2:
+        bench = MappingProxyType(bench)
+    epochs = []
+    t = rng.uniform(0, 5)
+    for _ in range(rng.randrange(0, 6)):
+        start = t + rng.uniform(0, 0.01)
+        t = start + rng.uniform(0.001, 0.2)
+        epoch = {"start_s": start, "end_s": t}
+        if rng.random() < 0.8:
+            epoch["counter_readback_ns"] = rng.choice([rng.randrange(0, 50000), -5, None, 12.5, float("nan")])
+        epochs.append(epoch)
+    return result, bench, epochs
+
+
+def test_measurement_diagnostics_equal_python_statement():
+    from powermodeling_b200.pack import MEMORY_WORKLOADS, NONLINEAR_WORKLOADS, SFU_WORKLOADS, TENSOR_WORKLOADS
+    native = TR._record_native()
+    rng = random.Random(3)
+    for case in range(600):
+        result, bench, epochs = _diagnostic_case(rng)
+        want = TR.measurement_diagnostics(result, bench, epochs)
+        got = native.measurement_diagnostics(result, bench, epochs, MEMORY_WORKLOADS, TENSOR_WORKLOADS, SFU_WORKLOADS,
+                                             NONLINEAR_WORKLOADS, sum)
+        assert _same(got, want), (case, result, bench, epochs)
+        # values read from the records are the records' own objects
+        assert got["quality"]["issues"] is result.get("issues", got["quality"]["issues"])
