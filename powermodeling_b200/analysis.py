@@ -789,7 +789,9 @@ def group_key(trial: Mapping[str, Any]) -> str:
     config = {k: v for k, v in trial.get("config", {}).items() if k not in REPEAT_KEYS}
     achieved = None if trial.get("clock_comparison_controlled") else {
         f: trial.get(f) for f in ("graphics_clock_mhz", "memory_clock_mhz")}
-    return json.dumps({"gpu_uuid": trial.get("gpu_uuid"), "workload": trial.get("workload"),
+    from .trial_report import _record_native
+    # json.dumps(..., sort_keys=True, separators=(",", ":")), written natively
+    return _record_native().sorted_json({"gpu_uuid": trial.get("gpu_uuid"), "workload": trial.get("workload"),
                        "experiment_role": trial.get("experiment_role", "legacy_unspecified"),
                        "config": config, "uncontrolled_achieved_clocks": achieved,
                        "benchmark_sha256": trial.get("benchmark_sha256"),
@@ -798,7 +800,7 @@ def group_key(trial: Mapping[str, Any]) -> str:
                        "nonlinear_contract": trial.get("nonlinear_contract"),
                        "sfu_contract": trial.get("sfu_contract"),
                        "treatment_design_stratum": trial.get("treatment_design_stratum"),
-                       "resource_geometry": trial.get("resource_geometry")}, sort_keys=True, separators=(",", ":"))
+                       "resource_geometry": trial.get("resource_geometry")})
 
 
 def group_seed(key: str) -> int:

@@ -21,6 +21,7 @@
 // phase_dicts and measurement_diagnostics (below) build the trial records'
 // phase dicts and measurement diagnostics; their Python statements in
 // powermodeling_b200/analysis.py and trial_report.py are the specification.
+// sorted_json writes the group key's JSON text (json.dumps with sorted keys).
 #define PY_SSIZE_T_CLEAN
 #include <Python.h>
 
@@ -792,7 +793,130 @@ PyObject* measurement_diagnostics(PyObject*, PyObject* args) {
   return out.take();
 }
 
+// ---------------------------------------------------------------------------
+// sorted_json(obj): json.dumps(obj, sort_keys=True, separators=(",", ":"))
+// (the group key's text, whose sha256 seeds the group's resampling): None,
+// true/false, ints and floats by their reprs (NaN, Infinity, -Infinity),
+// strings with every character outside printable ASCII escaped (\uXXXX,
+// surrogate pairs above U+FFFF), lists and tuples, dicts with their items
+// sorted and non-string keys written as their JSON text after sorting.
+// Anything else raises TypeError, as json does without a default.
+
+void json_string(std::string& out, PyObject* s) {
+  const Py_ssize_t n = PyUnicode_GET_LENGTH(s);
+  const int kind = PyUnicode_KIND(s);
+  const void* data = PyUnicode_DATA(s);
+  static const char hex[] = "0123456789abcdef";
+  out.push_back('"');
+  auto unit = [&](unsigned u) {
+    out += "\\u";
+    out.push_back(hex[(u >> 12) & 15]); out.push_back(hex[(u >> 8) & 15]);
+    out.push_back(hex[(u >> 4) & 15]); out.push_back(hex[u & 15]);
+  };
+  for (Py_ssize_t i = 0; i < n; ++i) {
+    const Py_UCS4 c = PyUnicode_READ(kind, data, i);
+    if (c >= ' ' && c <= '~' && c != '\\' && c != '"') { out.push_back((char)c); continue; }
+    switch (c) {
+      case '\\': out += "\\\\"; break;
+      case '"': out += "\\\""; break;
+      case '\b': out += "\\b"; break;
+      case '\f': out += "\\f"; break;
+      case '\n': out += "\\n"; break;
+      case '\r': out += "\\r"; break;
+      case '\t': out += "\\t"; break;
+      default:
+        if (c >= 0x10000) {
+          const Py_UCS4 v = c - 0x10000;
+          unit(0xd800 | ((v >> 10) & 0x3ff));
+          unit(0xdc00 | (v & 0x3ff));
+        } else {
+          unit(c);
+        }
+    }
+  }
+  out.push_back('"');
+}
+
+// The repr of an int or float as json writes it (NaN and infinities by name).
+int json_number(std::string& out, PyObject* v) {
+  PyObject* r;
+  if (PyFloat_Check(v)) {
+    const double d = PyFloat_AS_DOUBLE(v);
+    if (std::isnan(d)) { out += "NaN"; return 0; }
+    if (std::isinf(d)) { out += d > 0 ? "Infinity" : "-Infinity"; return 0; }
+    r = PyFloat_Type.tp_repr(v);
+  } else {
+    r = PyLong_Type.tp_repr(v);
+  }
+  if (!r) return -1;
+  Py_ssize_t len;
+  const char* text = PyUnicode_AsUTF8AndSize(r, &len);
+  if (!text) { Py_DECREF(r); return -1; }
+  out.append(text, (size_t)len);
+  Py_DECREF(r);
+  return 0;
+}
+
+int json_value(std::string& out, PyObject* v, int depth) {
+  if (depth > 1000) { PyErr_SetString(PyExc_RecursionError, "maximum recursion depth exceeded in sorted_json"); return -1; }
+  if (v == Py_None) { out += "null"; return 0; }
+  if (v == Py_True) { out += "true"; return 0; }
+  if (v == Py_False) { out += "false"; return 0; }
+  if (PyUnicode_Check(v)) { json_string(out, v); return 0; }
+  if (PyLong_Check(v) || PyFloat_Check(v)) return json_number(out, v);
+  if (PyList_Check(v) || PyTuple_Check(v)) {
+    PyObject* seq = PySequence_Fast(v, "sequence");
+    if (!seq) return -1;
+    out.push_back('[');
+    for (Py_ssize_t i = 0; i < PySequence_Fast_GET_SIZE(seq); ++i) {
+      if (i) out.push_back(',');
+      if (json_value(out, PySequence_Fast_GET_ITEM(seq, i), depth + 1) < 0) { Py_DECREF(seq); return -1; }
+    }
+    out.push_back(']');
+    Py_DECREF(seq);
+    return 0;
+  }
+  if (PyDict_Check(v)) {
+    PyObject* items = PyMapping_Items(v);
+    if (!items || PyList_Sort(items) < 0) { Py_XDECREF(items); return -1; }
+    out.push_back('{');
+    for (Py_ssize_t i = 0; i < PyList_GET_SIZE(items); ++i) {
+      PyObject* kv = PyList_GET_ITEM(items, i);
+      PyObject* k = PyTuple_GET_ITEM(kv, 0);
+      if (i) out.push_back(',');
+      if (PyUnicode_Check(k)) {
+        json_string(out, k);
+      } else if (PyFloat_Check(k) || (PyLong_Check(k) && !PyBool_Check(k))) {
+        std::string text;
+        if (json_number(text, k) < 0) { Py_DECREF(items); return -1; }
+        out.push_back('"'); out += text; out.push_back('"');
+      } else if (k == Py_True || k == Py_False || k == Py_None) {
+        out += k == Py_True ? "\"true\"" : k == Py_False ? "\"false\"" : "\"null\"";
+      } else {
+        PyErr_Format(PyExc_TypeError, "keys must be str, int, float, bool or None, not %.100s", Py_TYPE(k)->tp_name);
+        Py_DECREF(items);
+        return -1;
+      }
+      out.push_back(':');
+      if (json_value(out, PyTuple_GET_ITEM(kv, 1), depth + 1) < 0) { Py_DECREF(items); return -1; }
+    }
+    out.push_back('}');
+    Py_DECREF(items);
+    return 0;
+  }
+  PyErr_Format(PyExc_TypeError, "Object of type %.100s is not JSON serializable", Py_TYPE(v)->tp_name);
+  return -1;
+}
+
+PyObject* sorted_json(PyObject*, PyObject* obj) {
+  std::string out;
+  out.reserve(1024);
+  if (json_value(out, obj, 0) < 0) return nullptr;
+  return PyUnicode_FromStringAndSize(out.data(), (Py_ssize_t)out.size());
+}
+
 PyMethodDef kMethods[] = {
+    {"sorted_json", sorted_json, METH_O, "sorted_json(obj) -> json.dumps(obj, sort_keys=True, separators=(',', ':'))"},
     {"fold", fold, METH_VARARGS, "fold(values, fallback) -> the repeats' diagnostics folded into one"},
     {"measurement_diagnostics", measurement_diagnostics, METH_VARARGS,
      "measurement_diagnostics(result, bench, epochs, memory, tensor, sfu, nonlinear, sum) -> a trial's diagnostics"},

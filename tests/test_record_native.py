@@ -6,6 +6,7 @@ phase_dicts: analysis._phase_dict over phase rows with random values, NaNs and f
 measurement_diagnostics: trial_report.measurement_diagnostics over randomized trial results of
 every workload class, odd value types, epochs with and without counter readbacks, and a bench
 that is not a dict.
+sorted_json: json.dumps(sort_keys=True, separators=(",", ":")) on randomized nested values.
 """
 from __future__ import annotations
 
@@ -195,3 +196,52 @@ def test_measurement_diagnostics_equal_python_statement():
         assert _same(got, want), (case, result, bench, epochs)
         # values read from the records are the records' own objects
         assert got["quality"]["issues"] is result.get("issues", got["quality"]["issues"])
+
+
+class Flag(int):
+    pass
+
+
+def _json_value(rng: random.Random, depth: int):
+    kind = rng.randrange(12 if depth < 4 else 8)
+    if kind == 0:
+        return None
+    if kind == 1:
+        return rng.random() < 0.5
+    if kind == 2:
+        return rng.randrange(-10 ** 30, 10 ** 30)
+    if kind == 3:
+        return rng.choice([rng.uniform(-1e6, 1e6), 1e-320, -0.0, float("nan"), float("inf"), -float("inf"), 0.1])
+    if kind == 4:
+        return "".join(rng.choice(["a", "Z", " ", '"', "\\", "\n", "\t", "\x01", "\x7f", "é", "☃", "\U0001F600", "/"])
+                       for _ in range(rng.randrange(8)))
+    if kind == 5:
+        return Flag(rng.randrange(5))
+    if kind == 6:
+        return rng.choice(["gpu", "hbm", ""])
+    if kind == 7:
+        return rng.uniform(0, 1)
+    if kind in (8, 9):
+        return [_json_value(rng, depth + 1) for _ in range(rng.randrange(4))] if kind == 8 else \
+            tuple(_json_value(rng, depth + 1) for _ in range(rng.randrange(3)))
+    keys = rng.choice([["b", "a", "c", "aa", "B"], [3, 1, 2], [1.5, -2.0, 0.25], [True, None]])
+    return {k: _json_value(rng, depth + 1) for k in rng.sample(keys, rng.randrange(len(keys) + 1))}
+
+
+def test_sorted_json_equals_json_dumps():
+    native = TR._record_native()
+    rng = random.Random(19)
+    for case in range(2000):
+        value = _json_value(rng, 0)
+        try:
+            want = json.dumps(value, sort_keys=True, separators=(",", ":"))
+        except TypeError:                    # keys that do not sort together: both refuse
+            with pytest.raises(TypeError):
+                native.sorted_json(value)
+            continue
+        assert native.sorted_json(value) == want, case
+    for bad in ({1: 1, "a": 2}, {(1,): 2}, {"a": object()}, [{1, 2}], {"a": b"x"}):
+        with pytest.raises(TypeError):
+            json.dumps(bad, sort_keys=True, separators=(",", ":"))
+        with pytest.raises(TypeError):
+            native.sorted_json(bad)
