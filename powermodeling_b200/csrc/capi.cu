@@ -611,7 +611,7 @@ int pm_analyze_sweep_device(const pm_trials* trials, const pm_policy* policy, pm
   const size_t a_need = analyze_scratch_bytes(trials->n_trials, trials->max_phase_samples);
   const size_t b_off = align256(a_need);
   const size_t b_need = bootstrap_scratch_bytes(groups->n_groups, groups->max_members, groups->resamples);
-  if (b_off + b_need > scratch_bytes || !scratch)
+  if (b_off + b_need > scratch_bytes || (b_off + b_need > 0 && !scratch))
     return fail(PM_E_INVALID, "the sweep needs %zu bytes of device scratch (pm_analyze_sweep_scratch_bytes), got %zu",
                 b_off + b_need, scratch_bytes);
   if (reinterpret_cast<uintptr_t>(scratch) % 256)
