@@ -993,7 +993,7 @@ def main():
         # The ranks share the host's cores: each rank's record packer and staging pool take
         # their share instead of all of them (the variables are read once, at first use).
         share = max(1, (len(os.sched_getaffinity(0)) or 1) // int(os.environ.get("LOCAL_WORLD_SIZE", world)))
-        os.environ.setdefault("PM_PACK_THREADS", str(min(8, share)))
+        os.environ.setdefault("PM_PACK_THREADS", str(min(16, share)))
         os.environ.setdefault("PM_HOST_THREADS", str(max(1, min(3, share - 1))))
         import datetime
         import torch
