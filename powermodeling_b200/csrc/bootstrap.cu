@@ -135,6 +135,36 @@ __device__ __forceinline__ int draw_index(uint32_t w0, uint32_t w1, double n) {
 // w0 >> (32 - p).  pow2_shift(n) is that shift, or 0 when n is not such a power.
 __device__ __forceinline__ int pow2_shift(int n) { return n >= 2 && (n & (n - 1)) == 0 ? 33 - __ffs(n) : 0; }
 
+// twist_block for n = 2^p: a draw reads the first (even) word of its pair
+// alone, so each even word's index goes straight from the twist into the
+// stream (draw d0 + i / 2 for word i, kept while below `draws`); odd words
+// are neither tempered nor kept, and no ring or conversion pass is needed.
+__device__ __forceinline__ void twist_block_emit(const uint32_t* src, uint32_t* dst, uint8_t* stream, uint32_t d0,
+                                                 uint32_t draws, int shift) {
+  constexpr int A = kMtN - kMtM;          // 227
+  const int t = threadIdx.x;
+  if (t < A) {
+    auto emit = [&](int i, uint32_t w) {
+      const uint32_t d = d0 + (uint32_t)(i >> 1);
+      if (!(i & 1) && d < draws) stream[d] = (uint8_t)(temper(w) >> shift);
+    };
+    const uint32_t a = twist_one(src[t], src[t + 1], src[t + kMtM]);
+    const uint32_t b = twist_one(src[t + A], src[t + A + 1], a);
+    dst[t] = a;
+    dst[t + A] = b;
+    emit(t, a);
+    emit(t + A, b);
+    if (t < kMtN - 2 * A) {
+      const int i = t + 2 * A;
+      const uint32_t next = i < kMtN - 1 ? src[i + 1] : twist_one(src[0], src[1], src[kMtM]);
+      const uint32_t c = twist_one(src[i], next, b);
+      dst[i] = c;
+      emit(i, c);
+    }
+  }
+  __syncthreads();
+}
+
 // Rank of a non-decreasing n-tuple over [0, n) among multisets (combinatorial
 // number system on b_i = a_i + i, strictly increasing in [0, 2n-1)).
 // `binom` is a shared-memory copy of c_binom: lookups here are thread-divergent.
@@ -296,7 +326,9 @@ __device__ __forceinline__ void generate_resamples(GenShared& sh, int n, int B, 
 // pass twists block k into one half of the ring while the threads turn the
 // 312 word pairs of block k - 1 (the other half) into draw indices and store
 // them, then one barrier.  A draw never straddles two blocks (624 is even),
-// so draw d of the stream is pair d mod 312 of block d / 312.
+// so draw d of the stream is pair d mod 312 of block d / 312.  For n = 2^p
+// the twist stores the indices itself (twist_block_emit): one barrier per
+// block and nothing else in the loop.
 // Needs blockDim.x >= 312.  All threads call it.
 __device__ __forceinline__ void stream_draws(GenShared& sh, int n, int B, uint8_t* stream) {
   constexpr int kPairs = kMtN / 2;
@@ -306,6 +338,11 @@ __device__ __forceinline__ void stream_draws(GenShared& sh, int n, int B, uint8_
   const int shift = pow2_shift(n);
   const uint32_t draws = (uint32_t)B * (uint32_t)n;
   const uint32_t blocks = (draws + kPairs - 1) / kPairs;
+  if (shift) {
+    for (uint32_t blk = 0; blk < blocks; ++blk)
+      twist_block_emit(sh.mt[blk & 1], sh.mt[(blk & 1) ^ 1], stream, blk * kPairs, draws, shift);
+    return;
+  }
   const int j = threadIdx.x;
   for (uint32_t blk = 0; blk <= blocks; ++blk) {
     if (blk < blocks) twist_block<false>(sh.mt[blk & 1], sh.mt[(blk & 1) ^ 1], sh.ring, (int)(blk & 1) * kMtN);
