@@ -40,6 +40,8 @@ CANDIDATE_PLATEAUS = ("observed_plateau", "observed_problem_size_plateau", "obse
 
 
 def _num(value) -> float | None:
+    if type(value) is float:                 # the common case: float() of an exact float is the float itself
+        return value if value - value == 0.0 else None
     ok = isinstance(value, (int, float)) and not isinstance(value, bool) and math.isfinite(value)
     return float(value) if ok else None
 
