@@ -862,9 +862,9 @@ def run_nonlinear_arms(sms: int, peaks: dict) -> dict:
 # DRAM bytes read + written.  The kernels are deterministic for the fixed
 # seeds, so the counts are the same on every launch; None where not captured.
 NCU_PER_LAUNCH = {
-    "analyze_kernel": {"inst": 24_438_325, "dram": 4_916_608},
-    "bootstrap_prepare_kernel": {"inst": 9_173_759, "dram": 86_912},
-    "bootstrap_kernel<0>": {"inst": 744_303, "dram": 185_984},
+    "analyze_kernel": {"inst": 24_438_012, "dram": 5_002_240},
+    "bootstrap_prepare_kernel": {"inst": 7_448_191, "dram": 70_272},
+    "bootstrap_kernel<0>": {"inst": 744_303, "dram": 184_320},
 }
 # Blackwell SM: four schedulers, each issuing one warp instruction per clock.
 ISSUE_PER_SM_CLOCK = 4

@@ -137,30 +137,47 @@ __device__ __forceinline__ int pow2_shift(int n) { return n >= 2 && (n & (n - 1)
 
 // twist_block for n = 2^p: a draw reads the first (even) word of its pair
 // alone, so each even word's index goes straight from the twist into the
-// stream (draw d0 + i / 2 for word i, kept while below `draws`); odd words
-// are neither tempered nor kept, and no ring or conversion pass is needed.
+// stream (draw d0 + i / 2 for word i, kept while below `draws`); odd words are
+// neither tempered nor kept, and no ring or conversion pass is needed.  The
+// chain t, t + 227, t + 454 alternates parity (227 is odd), so threads 0-127
+// take the even t and threads 128-255 the odd t: every warp tempers the same
+// words of its chains.  The state sits even words first (word i at
+// emit_slot(i)), so a warp's loads and stores of one parity are consecutive.
+__device__ __forceinline__ int emit_slot(int i) { return (i & 1) * (kMtN / 2) + (i >> 1); }
+
+template <int kParity>
+__device__ __forceinline__ void twist_chain_emit(const uint32_t* src, uint32_t* dst, uint8_t* stream, uint32_t d0,
+                                                 uint32_t draws, int shift, int k) {
+  constexpr int A = kMtN - kMtM;          // 227
+  const int t = 2 * k + kParity;
+  auto emit = [&](int i, uint32_t w) {    // i even
+    const uint32_t d = d0 + (uint32_t)(i >> 1);
+    if (d < draws) stream[d] = (uint8_t)(temper(w) >> shift);
+  };
+  const uint32_t a = twist_one(src[emit_slot(t)], src[emit_slot(t + 1)], src[emit_slot(t + kMtM)]);
+  const uint32_t b = twist_one(src[emit_slot(t + A)], src[emit_slot(t + A + 1)], a);
+  dst[emit_slot(t)] = a;
+  dst[emit_slot(t + A)] = b;
+  if (kParity == 0) emit(t, a); else emit(t + A, b);
+  if (t < kMtN - 2 * A) {
+    const int i = t + 2 * A;
+    const uint32_t next = i < kMtN - 1 ? src[emit_slot(i + 1)]
+                                       : twist_one(src[emit_slot(0)], src[emit_slot(1)], src[emit_slot(kMtM)]);
+    const uint32_t c = twist_one(src[emit_slot(i)], next, b);
+    dst[emit_slot(i)] = c;
+    if (kParity == 0) emit(i, c);
+  }
+}
+
+// Needs blockDim.x >= 256; src and dst in the emit_slot layout.
 __device__ __forceinline__ void twist_block_emit(const uint32_t* src, uint32_t* dst, uint8_t* stream, uint32_t d0,
                                                  uint32_t draws, int shift) {
-  constexpr int A = kMtN - kMtM;          // 227
-  const int t = threadIdx.x;
-  if (t < A) {
-    auto emit = [&](int i, uint32_t w) {
-      const uint32_t d = d0 + (uint32_t)(i >> 1);
-      if (!(i & 1) && d < draws) stream[d] = (uint8_t)(temper(w) >> shift);
-    };
-    const uint32_t a = twist_one(src[t], src[t + 1], src[t + kMtM]);
-    const uint32_t b = twist_one(src[t + A], src[t + A + 1], a);
-    dst[t] = a;
-    dst[t + A] = b;
-    emit(t, a);
-    emit(t + A, b);
-    if (t < kMtN - 2 * A) {
-      const int i = t + 2 * A;
-      const uint32_t next = i < kMtN - 1 ? src[i + 1] : twist_one(src[0], src[1], src[kMtM]);
-      const uint32_t c = twist_one(src[i], next, b);
-      dst[i] = c;
-      emit(i, c);
-    }
+  constexpr int A = kMtN - kMtM;
+  const int r = threadIdx.x;
+  if (r < 128) {
+    if (2 * r < A) twist_chain_emit<0>(src, dst, stream, d0, draws, shift, r);
+  } else if (r < 256) {
+    if (2 * (r - 128) + 1 < A) twist_chain_emit<1>(src, dst, stream, d0, draws, shift, r - 128);
   }
   __syncthreads();
 }
@@ -327,15 +344,15 @@ __device__ __forceinline__ void generate_resamples(GenShared& sh, int n, int B, 
 // 312 word pairs of block k - 1 (the other half) into draw indices and store
 // them, then one barrier.  A draw never straddles two blocks (624 is even),
 // so draw d of the stream is pair d mod 312 of block d / 312.  For n = 2^p
-// the twist stores the indices itself (twist_block_emit): one barrier per
-// block and nothing else in the loop.
+// the twist stores the indices itself (twist_block_emit, state in the
+// emit_slot layout): one barrier per block and nothing else in the loop.
 // Needs blockDim.x >= 312.  All threads call it.
 __device__ __forceinline__ void stream_draws(GenShared& sh, int n, int B, uint8_t* stream) {
   constexpr int kPairs = kMtN / 2;
-  for (int i = threadIdx.x; i < kMtN; i += blockDim.x) sh.mt[0][i] = sh.mt_seed[i];
+  const int shift = pow2_shift(n);
+  for (int i = threadIdx.x; i < kMtN; i += blockDim.x) sh.mt[0][shift ? emit_slot(i) : i] = sh.mt_seed[i];
   __syncthreads();
   const double nd = (double)n;
-  const int shift = pow2_shift(n);
   const uint32_t draws = (uint32_t)B * (uint32_t)n;
   const uint32_t blocks = (draws + kPairs - 1) / kPairs;
   if (shift) {
