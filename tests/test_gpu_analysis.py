@@ -145,9 +145,12 @@ def test_long_phases_match_oracle(gpu_ready, arm_s):
         assert not problems, problems
 
 
-@pytest.mark.parametrize("members", [5, 9, 16, 24])
+@pytest.mark.parametrize("members", [4, 5, 8, 9, 16, 24, 32])
 def test_bootstrap_mixed_member_counts_match_oracle(gpu_ready, members):
-    """Metrics that lose members to NaN: the prepared draws serve count == members, fresh draws the rest."""
+    """Metrics that lose members to NaN: the prepared draws serve count == members, fresh draws the rest.
+
+    Power-of-two groups (4, 8, 16, 32) take the draw pass whose twist stores the indices itself; the
+    others convert word pairs."""
     import hashlib
     import statistics
     from powermodeling_b200.analysis import bootstrap_groups
